@@ -1,0 +1,363 @@
+#!/usr/bin/env python
+"""bench.py -- decode tok/s of the 12B-shape Q4 model on B200.
+
+One "step" = one greedy decode token through all 48 layers + the Q8 LM head +
+top-64 (the reference's gpuDispatchForwardToken, src/gpu/model_dispatch.zig:344).
+Workload: seeded synthetic weights (seed 3), a 512-token prompt of uniform ids
+prefilled with the batched path, then greedy decode at clocks 512.. (config 4
+decodes 256 tokens; warmup + steps default to 8 + 248 = 256).  Per-token weight
+stream is 7.2 GB (> 126 MB L2), so no L2 flush is needed between steps.
+
+  value : device-resident loop (ch_decode_run: ring lists pre-planned in HBM, the
+          greedy token fed back on the device), CUDA events on the library stream.
+  e2e   : the reference-facing call ch_forward_token per token with host buffers
+          (x from the host bf16 table, host ring lists, top-64 read back).
+  --impl reference : the reference CPU path = the oracle restatement (Zig cannot
+          be built here), all host threads, one bounded sample per step.
+
+Multi-GPU (torchrun): replicas -- each rank decodes its own stream on its own GPU
+(weak scaling); row-sharded tensor parallel decode is not in this build yet.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+SEED = 3
+PROMPT = 512
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=248)
+    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--layers", type=int, default=48)
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    return ap.parse_args()
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks + throttle reasons sampled during the timed region."""
+
+    def __init__(self, index: int):
+        self.index = index
+        self.samples = []
+        self.proc = None
+
+    def __enter__(self):
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={q}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except FileNotFoundError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.samples.append([s.strip() for s in line.split(",")])
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(s[1]) for s in self.samples if len(s) > 8 and s[1].replace(".", "").isdigit()]
+        smax = [float(s[2]) for s in self.samples if len(s) > 8 and s[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for s in self.samples if len(s) > 8 for i in range(4) if s[5 + i] == "Active"})
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": max(smax) if smax else None,
+                "reasons": reasons, "samples": len(self.samples)}
+
+
+# ----------------------------------------------------------------------------------------
+def cpu_sample(steps: int, warmup: int, threads_note: bool = True):
+    """Reference CPU path (the oracle restatement, all host threads) on a bounded sample
+    of the config-4 decode step: 2 of the 48 layers and 1/16 of the LM head rows, timed
+    per token and scaled to the full model (x24 layers, x16 head)."""
+    from channel_b200.engine import config_12b
+    from oracle import oracle as o
+
+    full = config_12b()
+    cfg2 = config_12b(layers=2)
+    cfg2.vocab_size = full.vocab_size // 16
+    cfg2.layer_types = [False, False]
+    w = o.SyntheticWeights(cfg2, SEED)
+    m = o.Model(cfg2, w)
+    rng = np.random.default_rng(SEED)
+    x = (rng.standard_normal(cfg2.hidden_size) * 0.5).astype(np.float32)
+    clock = PROMPT
+    act = np.arange(clock + 1, dtype=np.uint32)
+    sli = np.arange(max(0, clock + 1 - 1024), clock + 1, dtype=np.uint32)
+    times_layers, times_head = [], []
+    lm = w.lm_head
+    for i in range(warmup + steps):
+        t0 = time.perf_counter()
+        m.forward_token(x, clock, clock, act, sli)
+        t1 = time.perf_counter()
+        o.gemv_q8(lm, x, cfg2.vocab_size, cfg2.hidden_size)
+        t2 = time.perf_counter()
+        if i >= warmup:
+            times_layers.append(t1 - t0)
+            times_head.append(t2 - t1)
+    t_layers = float(np.median(times_layers)) - float(np.median(times_head))  # forward includes one head slice
+    t_tok = t_layers * (full.num_hidden_layers / 2) + float(np.median(times_head)) * 16
+    return {"value": 1.0 / t_tok, "unit": "tok/s", "cores": o.nthreads(), "kind": "port",
+            "sample": "oracle decode of 2/48 layers + 1/16 of the Q8 LM head per token at clock 512, "
+                      "median of {} tokens, scaled x24 layers / x16 head".format(steps),
+            "sec_per_token": t_tok}
+
+
+def reference_arm(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    steps = max(1, min(args.steps, 8))
+    warm = max(0, min(args.warmup, 2))
+    r = cpu_sample(steps, warm)
+    line = {"metric": "decode tok/s (12B-shape Q4) at 1/2/4/8 GPU; Q4 GEMV HBM GB/s vs peak",
+            "impl": "reference", "value": r["value"], "unit": "tok/s", "n_gpus": args.gpus, "steps": steps,
+            "warmup": warm, "ms_per_step": 1000.0 / r["value"], "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "config4: 12B-shape Q4 decode, 48 layers, H 3840, I 15360, 16q/8kv, D 256, "
+                                   "V 262144, greedy decode after a 512-token prompt", "parallelism": "cpu"},
+            "cpu_baseline": {k: r[k] for k in ("value", "unit", "cores", "kind", "sample")},
+            "e2e": {"value": r["value"], "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ----------------------------------------------------------------------------------------
+def ours(args):
+    import torch
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
+
+    from channel_b200 import DynamicRingBuffer, GpuContext, GpuModelContext, config_12b, gpu_dispatch_prefill_batch
+    from channel_b200 import _lib as L
+    from channel_b200.engine import gpu_dispatch_forward_token
+
+    assert args.warmup >= 3, "at least 3 warm-up steps"
+    cfg = config_12b(layers=args.layers)
+    ctx = GpuContext.init(local)
+    t0 = time.time()
+    gm = GpuModelContext.synthetic(ctx, cfg, SEED)
+    build_s = time.time() - t0
+    stream = torch.cuda.ExternalStream(ctx.stream)
+
+    rng = np.random.default_rng(SEED + rank)
+    prompt = rng.integers(0, cfg.vocab_size, PROMPT).astype(np.uint32)
+    n_total = args.warmup + args.steps
+
+    def fresh_prefill():
+        gm.zero_state()
+        ring = DynamicRingBuffer(cfg.num_hidden_layers, 0)
+        ring.setNumAnchors(min(PROMPT, 512))  # stream_handler.zig:67
+        prev = ring.getPrefillPrevSlots(0, 0, PROMPT)
+        slots = np.concatenate([prev, [ring.getSlotIndex(c) for c in range(PROMPT)]]).astype(np.uint32)
+        for c in range(PROMPT):
+            for l in range(cfg.num_hidden_layers):
+                ring.activateSlot(l, c)
+        torch.cuda.synchronize()
+        t = time.time()
+        cands = gpu_dispatch_prefill_batch(gm, prompt, None, slots, 0, len(prev))
+        return ring, int(cands[0].id), time.time() - t
+
+    def step_lists(ring, clock):
+        ring.activateSlot(0, clock)
+        slot = ring.getSlotIndex(clock)
+        return slot, ring.getActiveSlotsLayer(0, clock, False, cfg.sliding_window), \
+            ring.getActiveSlotsLayer(0, clock, True, cfg.sliding_window)
+
+    # ---- value: device-resident loop -------------------------------------------------
+    ring, first, prefill_s = fresh_prefill()
+    plan = []
+    for i in range(n_total):
+        clock = PROMPT + i
+        slot, act, sli = step_lists(ring, clock)
+        plan.append((clock, slot, act, sli))
+    gm.decode_plan(plan)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    gm.decode_run(first, args.warmup)
+    ctx.synchronize()
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        ev0.record(stream)
+        gm.decode_continue(args.steps)
+        ev1.record(stream)
+        ev1.synchronize()
+    ms = ev0.elapsed_time(ev1)
+    torch.cuda.synchronize()
+    tokens = gm.decode_tokens(n_total)
+    if dist:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+        dist.barrier()
+    ms_per_step = ms / args.steps
+    value = world * args.steps / (ms / 1000.0)
+
+    # ---- roofline: dominant kernel (fused gate/up GEMV), timed alone over rotating layers
+    lib = L.load()
+    H, I = cfg.hidden_size, cfg.intermediate_size
+    xbuf = torch.randn(H, device="cuda", dtype=torch.float32)
+    ybuf = torch.empty(I, device="cuda", dtype=torch.float32)
+    tiles = [gm.weight_tiles(l, 2)[0] for l in range(cfg.num_hidden_layers)]
+    torch.cuda.synchronize()
+    for l in range(min(4, len(tiles))):
+        L.check(lib.ch_fused_mlp_q4(ctx.handle, tiles[l], I, H, xbuf.data_ptr(), ybuf.data_ptr()))
+    reps = 3 * len(tiles)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ctx.synchronize()
+    e0.record(stream)
+    for i in range(reps):
+        L.check(lib.ch_fused_mlp_q4(ctx.handle, tiles[i % len(tiles)], I, H, xbuf.data_ptr(), ybuf.data_ptr()))
+    e1.record(stream)
+    e1.synchronize()
+    k_ms = e0.elapsed_time(e1) / reps
+    gateup_bytes = 2 * I * H * 18 // 32 + H * 4 + I * 4
+    peak, peak_kind = peaks()
+    achieved = gateup_bytes / (k_ms / 1000.0) / 1e9
+    traffic = None
+    tp = ROOT / "profiles" / "gemv_gateup_traffic.json"
+    if tp.exists():
+        traffic = json.loads(tp.read_text()).get("bytes_per_launch")
+    step_bytes = (cfg.num_hidden_layers * ((cfg.q_dim + 2 * cfg.kv_dim) * H + H * cfg.q_dim + 3 * I * H) * 18 // 32
+                  + cfg.vocab_size * H * 36 // 32)
+    kv_bytes = cfg.num_hidden_layers * 2 * 2 * cfg.kv_dim * (PROMPT + args.warmup + args.steps / 2)
+    step_gbs = (step_bytes + kv_bytes) / (ms_per_step / 1000.0) / 1e9
+
+    # ---- e2e: reference-facing call with host buffers ---------------------------------
+    e2e = None
+    if not args.no_e2e:
+        emb_dev = torch.empty(cfg.vocab_size * H, dtype=torch.int16, device="cuda")
+        L.check(lib.ch_gen_bf16(ctx.handle, emb_dev.data_ptr(), emb_dev.numel(),
+                                lib.ch_tensor_seed(SEED, 0, 20), 0.0, 0.02))
+        ctx.synchronize()
+        table = emb_dev.cpu().numpy().view(np.uint16).reshape(cfg.vocab_size, H)
+        del emb_dev
+        scale = np.float32(math.sqrt(H))
+
+        def embed(tok):
+            return (table[tok].astype(np.uint32) << 16).view(np.float32) * scale
+
+        ring, tok, _ = fresh_prefill()
+        h2d = d2h = 0
+        e_tokens = []
+        for i in range(n_total):
+            if i == args.warmup:
+                ctx.synchronize()
+                if dist:
+                    dist.barrier()
+                h2d = d2h = 0
+                es0, es1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                es0.record(stream)
+                tw = time.perf_counter()
+            clock = PROMPT + i
+            slot, act, sli = step_lists(ring, clock)
+            x = embed(tok)
+            tok, cands = gpu_dispatch_forward_token(gm, x, clock, slot, act, sli)
+            e_tokens.append(tok)
+            h2d += x.nbytes + 32 + 4 * (len(act) + len(sli))
+            d2h += 64 * 8
+        es1.record(stream)
+        es1.synchronize()
+        e_ms = es0.elapsed_time(es1)
+        wall_ms = (time.perf_counter() - tw) * 1000
+        e_ms = max(e_ms, wall_ms)
+        if dist:
+            t = torch.tensor([e_ms], device="cuda")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            e_ms = float(t.item())
+        e2e = {"value": world * args.steps / (e_ms / 1000.0), "unit": "tok/s",
+               "h2d_bytes_per_step": h2d // args.steps, "d2h_bytes_per_step": d2h // args.steps,
+               "ms_per_step": e_ms / args.steps,
+               "tokens_match_device_loop": bool(list(e_tokens) == [int(t) for t in tokens])}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        cpu = cpu_sample(steps=3, warmup=1)
+        cpu = {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")}
+
+    launches_per_step = 1 + 5 * cfg.num_hidden_layers + 2
+    if rank == 0:
+        line = {
+            "metric": "decode tok/s (12B-shape Q4) at 1/2/4/8 GPU; Q4 GEMV HBM GB/s vs peak",
+            "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "q4/f16-mma/f32-acc", "data": "synthetic",
+            "config": {"workload": "config4: 12B-shape Q4 greedy decode ({} layers, H 3840, I 15360, 16q/8kv heads, "
+                                   "D 256, V 262144 Q8 head) after a 512-token prefill, seed 3".format(cfg.num_hidden_layers),
+                       "global_batch": world, "seq_len": PROMPT + n_total,
+                       "parallelism": "replicas" if world > 1 else "single",
+                       "l2": "per-step weight stream 7.2 GB > 126 MB L2 (no flush needed)"},
+            "roofline": {"bound": "hbm", "kernel": "gemv_kernel<Q4, GELU_MUL, ADD_RMSNORM> (fused gate/up)",
+                         "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                         "traffic": traffic, "bytes_per_launch": gateup_bytes, "us_per_launch": k_ms * 1000,
+                         "peak_kind": peak_kind + " (hbm_gbs, kernel timed alone over 48 rotating layers)"},
+            "step_roofline": {"bytes_per_step": step_bytes + kv_bytes, "achieved_gbs": step_gbs,
+                              "frac": step_gbs / peak},
+            "cpu_baseline": cpu,
+            "e2e": e2e,
+            "gpu_launches": launches_per_step * args.steps,
+            "clocks": clk.summary(),
+            "setup_s": {"model_build": build_s, "prefill_512": prefill_s},
+            "tokens_head": [int(t) for t in tokens[:8]],
+        }
+        print(json.dumps(line), flush=True)
+    gm.deinit()
+    ctx.deinit()
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    a = parse()
+    if a.impl == "reference":
+        reference_arm(a)
+    else:
+        ours(a)

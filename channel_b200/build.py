@@ -1,0 +1,77 @@
+"""Build libchannel_b200.so (sm_100a CUDA kernels + C-ABI) in-tree with nvcc.
+
+The shared library lands next to this file so it travels with the source tree;
+nothing is installed into site-packages.  Usage: ``python -m channel_b200.build``.
+"""
+from __future__ import annotations
+
+import os
+import shutil
+import subprocess
+import sys
+from pathlib import Path
+
+PKG = Path(__file__).resolve().parent
+ROOT = PKG.parent
+CSRC = PKG / "csrc"
+OUT = PKG / "libchannel_b200.so"
+OBJ = PKG / "_build"
+
+NVCC_FLAGS = [
+    "-gencode", "arch=compute_100a,code=sm_100a",
+    "-O3", "-lineinfo", "-std=c++17",
+    "-Xcompiler", "-fPIC",
+    "--expt-relaxed-constexpr",
+    "-I", str(ROOT / "include"),
+]
+
+
+def _nvcc() -> str:
+    for cand in (os.environ.get("NVCC"), shutil.which("nvcc"), "/usr/local/cuda/bin/nvcc"):
+        if cand and Path(cand).exists():
+            return cand
+    raise RuntimeError("nvcc not found")
+
+
+def sources() -> list[Path]:
+    return sorted(list(CSRC.glob("*.cu")) + list(CSRC.glob("*.cpp")))
+
+
+def build(verbose: bool = False, force: bool = False) -> Path:
+    nvcc = _nvcc()
+    OBJ.mkdir(exist_ok=True)
+    headers = list(CSRC.glob("*.cuh")) + [ROOT / "include" / "channel_cuda.h"]
+    newest_hdr = max(h.stat().st_mtime for h in headers)
+    objs = []
+    for src in sources():
+        obj = OBJ / (src.name + ".o")
+        objs.append(obj)
+        if not force and obj.exists() and obj.stat().st_mtime >= max(src.stat().st_mtime, newest_hdr):
+            continue
+        cmd = [nvcc, *NVCC_FLAGS, "-c", str(src), "-o", str(obj)]
+        if src.suffix == ".cpp":
+            cmd = [nvcc, "-x", "cu", *cmd[1:]]
+        if verbose:
+            print(" ".join(cmd), flush=True)
+        subprocess.run(cmd, check=True)
+    if force or not OUT.exists() or OUT.stat().st_mtime < max(o.stat().st_mtime for o in objs):
+        cmd = [nvcc, "-shared", "-gencode", "arch=compute_100a,code=sm_100a", *map(str, objs), "-o", str(OUT),
+               "-lcudart"]
+        if verbose:
+            print(" ".join(cmd), flush=True)
+        subprocess.run(cmd, check=True)
+    return OUT
+
+
+def build_oracle(verbose: bool = False) -> Path:
+    """Compile the CPU oracle (test infrastructure) with its Makefile."""
+    oracle = ROOT / "oracle"
+    subprocess.run(["make", "-s", "-C", str(oracle)], check=True,
+                   stdout=None if verbose else subprocess.DEVNULL)
+    return oracle / "liboracle.so"
+
+
+if __name__ == "__main__":
+    v = "-v" in sys.argv
+    print(build(verbose=v, force="--force" in sys.argv))
+    print(build_oracle(verbose=v))

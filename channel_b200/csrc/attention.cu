@@ -1,0 +1,318 @@
+// attention.cu -- decode attention over the 4,096-slot ring-buffer KV cache.
+//
+// Restates, in one kernel, the reference's two decode passes:
+//   qkv_rope.wgsl:25-180   per-head RMSNorm * q_norm / k_norm, half-split RoPE at
+//                          `clock`, V unit-RMSNorm, K/V written to cache[slot]
+//   decode_attn.wgsl:24-218 scores = q.k * scale over the slot list, softmax
+//                          (max seeded at -1e9, 1/(sum + 1e-9)), weighted V; GQA
+//                          kv_head = q_head / ratio
+// B200 design: split-K over the slot list (flash-decode).  Grid = kv_heads x
+// splits; each CTA owns every q head of its kv head (GQA packing), recomputes
+// the tiny norm + RoPE of q/k/v for that head itself (so no separate launch),
+// streams its slice of the gathered f16 K/V rows with 16-byte loads, keeps
+// per-chunk max / sum / weighted V, and the last CTA of each kv head combines
+// the chunk partials in fixed order (deterministic).  The fresh K/V of the
+// current slot are used from shared memory, so no CTA reads a cache row that
+// another CTA of the same launch is writing.  RoPE angles: inv_freq comes from
+// the host table, cos/sin are evaluated in double and rounded once.
+#include "common.cuh"
+#include "kernels.cuh"
+
+namespace ch {
+
+namespace {
+constexpr int kAttnThreads = 256;
+constexpr int kAttnWarps = kAttnThreads / 32;
+constexpr int kMaxRatio = 8;
+}  // namespace
+
+int attn_default_splits(uint32_t nkv) {
+  int target = 2 * num_sms();
+  int s = (int)((target + nkv - 1) / nkv);
+  if (s < 1) s = 1;
+  if (s > 64) s = 64;
+  return s;
+}
+size_t attn_partial_floats(uint32_t nkv, uint32_t ratio, uint32_t D, int splits) {
+  return (size_t)nkv * splits * ratio * (D + 2);
+}
+
+// normalize one head with a warp: out = rope(rmsnorm(in) * w) (w == nullptr -> unit norm, no rope)
+CH_DEV void head_norm_rope(const float *in, const float *w, float *out, uint32_t D, uint32_t rot, const float *inv_freq,
+                           uint32_t clock, float eps, bool rope, int lane) {
+  float ss = 0.f;
+  for (uint32_t d = lane; d < D; d += 32) ss = __fmaf_rn(in[d], in[d], ss);
+  ss = warp_sum(ss);
+  const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)D), eps)));
+  if (!rope) {
+    for (uint32_t d = lane; d < D; d += 32) out[d] = __fmul_rn(in[d], inv);
+    return;
+  }
+  const uint32_t half = rot / 2;
+  for (uint32_t d = lane; d < half; d += 32) {
+    const float v0 = __fmul_rn(__fmul_rn(in[d], inv), w[d]);
+    const float v1 = __fmul_rn(__fmul_rn(in[d + half], inv), w[d + half]);
+    const float ang = __fmul_rn((float)clock, inv_freq[d]);
+    double sd, cd;
+    sincos((double)ang, &sd, &cd);
+    const float c = (float)cd, s = (float)sd;
+    out[d] = __fsub_rn(__fmul_rn(v0, c), __fmul_rn(v1, s));
+    out[d + half] = __fadd_rn(__fmul_rn(v0, s), __fmul_rn(v1, c));
+  }
+  for (uint32_t d = rot + lane; d < D; d += 32) out[d] = __fmul_rn(__fmul_rn(in[d], inv), w[d]);
+}
+
+template <int R>
+__global__ void __launch_bounds__(kAttnThreads) decode_attn_kernel(const AttnArgs a, int splits, int chunk_cap) {
+  constexpr int D = 256, EPL = D / 32;  // elements per lane
+  extern __shared__ __align__(16) float sm[];
+  float *q_s = sm;                       // [R][D]
+  float *k_new = q_s + R * D;            // [D]
+  float *v_new = k_new + D;              // [D]
+  float *o_s = v_new + D;                // [warps][R][D]
+  float *sc = o_s + kAttnWarps * R * D;  // [R][chunk_cap]
+  __shared__ float red[kAttnWarps];
+  __shared__ float stat[2 * kMaxRatio];
+  __shared__ uint32_t last_flag;
+
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const uint32_t kvh = blockIdx.x, split = blockIdx.y;
+  const size_t kv_dim = (size_t)a.nkv * D;
+
+  // step state was written before the previous kernel started (see model.cu)
+  const StepParams sp = *a.sp;
+  const uint32_t S = a.is_sliding ? sp.n_sliding : sp.n_active;
+  const uint32_t *list = a.is_sliding ? sp.sliding : sp.active;
+  const uint32_t c0 = (uint32_t)(((uint64_t)S * split) / splits), c1 = (uint32_t)(((uint64_t)S * (split + 1)) / splits);
+  const uint32_t n = c1 - c0;
+
+  // warm L2 with this CTA's K/V rows while the projections finish
+  for (uint32_t i = c0 + tid; i < c1; i += kAttnThreads) {
+    const uint32_t phys = list[i];
+    if (phys < a.cache_slots) {
+      const __half *kr = a.k_cache + (size_t)phys * kv_dim + (size_t)kvh * D;
+      const __half *vr = a.v_cache + (size_t)phys * kv_dim + (size_t)kvh * D;
+      asm volatile("prefetch.global.L2 [%0];" ::"l"(kr));
+      asm volatile("prefetch.global.L2 [%0];" ::"l"(kr + 128));
+      asm volatile("prefetch.global.L2 [%0];" ::"l"(vr));
+      asm volatile("prefetch.global.L2 [%0];" ::"l"(vr + 128));
+    }
+  }
+  grid_dep_wait();
+
+  // ---- q/k/v norm + rope for this kv head (qkv_rope.wgsl) ----
+  const float *qraw = a.qkv;
+  const float *kraw = a.qkv + (size_t)a.nq * D;
+  const float *vraw = kraw + kv_dim;
+  for (int h = warp; h < R + 2; h += kAttnWarps) {
+    if (h < R) {
+      head_norm_rope(qraw + (size_t)(kvh * R + h) * D, a.q_norm_w, q_s + h * D, D, a.rot, a.inv_freq, sp.clock, a.eps,
+                     true, lane);
+    } else if (h == R) {
+      head_norm_rope(kraw + (size_t)kvh * D, a.k_norm_w, k_new, D, a.rot, a.inv_freq, sp.clock, a.eps, true, lane);
+      for (uint32_t d = lane; d < D; d += 32) {
+        __half hk = __float2half_rn(k_new[d]);
+        k_new[d] = __half2float(hk);
+        if (split == 0 && sp.slot < a.cache_slots) a.k_cache[(size_t)sp.slot * kv_dim + (size_t)kvh * D + d] = hk;
+      }
+    } else {
+      head_norm_rope(vraw + (size_t)kvh * D, nullptr, v_new, D, a.rot, nullptr, 0, a.eps, false, lane);
+      for (uint32_t d = lane; d < D; d += 32) {
+        __half hv = __float2half_rn(v_new[d]);
+        v_new[d] = __half2float(hv);
+        if (split == 0 && sp.slot < a.cache_slots) a.v_cache[(size_t)sp.slot * kv_dim + (size_t)kvh * D + d] = hv;
+      }
+    }
+  }
+  if (split == 0 && sp.slot >= a.cache_slots && tid == 0) atomicOr(a.err, DEV_ERR_BAD_SLOT);
+  __syncthreads();
+  grid_dep_launch();
+
+  // ---- scores: one slot per warp iteration, lane owns dims [lane*8, lane*8+8) ----
+  float qr[R][EPL];
+#pragma unroll
+  for (int h = 0; h < R; h++)
+#pragma unroll
+    for (int e = 0; e < EPL; e++) qr[h][e] = q_s[h * D + lane * EPL + e];
+
+  for (uint32_t i = warp; i < n; i += kAttnWarps) {
+    const uint32_t phys = list[c0 + i];
+    float kv[EPL];
+    bool valid = true;
+    if (phys == sp.slot) {
+#pragma unroll
+      for (int e = 0; e < EPL; e++) kv[e] = k_new[lane * EPL + e];
+    } else if (phys < a.cache_slots) {
+      const uint4 raw = *reinterpret_cast<const uint4 *>(a.k_cache + (size_t)phys * kv_dim + (size_t)kvh * D + lane * EPL);
+      const __half2 *hp = reinterpret_cast<const __half2 *>(&raw);
+#pragma unroll
+      for (int e = 0; e < EPL / 2; e++) {
+        float2 f = __half22float2(hp[e]);
+        kv[2 * e] = f.x;
+        kv[2 * e + 1] = f.y;
+      }
+    } else {
+      valid = false;
+#pragma unroll
+      for (int e = 0; e < EPL; e++) kv[e] = 0.f;
+    }
+#pragma unroll
+    for (int h = 0; h < R; h++) {
+      float dot = 0.f;
+#pragma unroll
+      for (int e = 0; e < EPL; e++) dot = __fmaf_rn(qr[h][e], kv[e], dot);
+      dot = warp_sum(dot);
+      if (lane == 0) sc[h * chunk_cap + i] = valid ? __fmul_rn(dot, a.scale) : -INFINITY;
+    }
+    if (!valid && lane == 0) atomicOr(a.err, DEV_ERR_BAD_LIST);
+  }
+  __syncthreads();
+
+  // ---- chunk max / exp / sum per q head ----
+  for (int h = 0; h < R; h++) {
+    float m = -1e9f;
+    for (uint32_t i = tid; i < n; i += kAttnThreads) m = fmaxf(m, sc[h * chunk_cap + i]);
+    m = warp_max(m);
+    if (lane == 0) red[warp] = m;
+    __syncthreads();
+    if (tid == 0) {
+      float mm = red[0];
+      for (int w = 1; w < kAttnWarps; w++) mm = fmaxf(mm, red[w]);
+      stat[2 * h] = mm;
+    }
+    __syncthreads();
+    const float mh = stat[2 * h];
+    float l = 0.f;
+    for (uint32_t i = tid; i < n; i += kAttnThreads) {
+      float e = expf(__fsub_rn(sc[h * chunk_cap + i], mh));
+      sc[h * chunk_cap + i] = e;
+      l = __fadd_rn(l, e);
+    }
+    l = warp_sum(l);
+    __syncthreads();
+    if (lane == 0) red[warp] = l;
+    __syncthreads();
+    if (tid == 0) {
+      float ll = 0.f;
+      for (int w = 0; w < kAttnWarps; w++) ll = __fadd_rn(ll, red[w]);
+      stat[2 * h + 1] = ll;
+    }
+    __syncthreads();
+  }
+
+  // ---- weighted V ----
+  float acc[R][EPL];
+#pragma unroll
+  for (int h = 0; h < R; h++)
+#pragma unroll
+    for (int e = 0; e < EPL; e++) acc[h][e] = 0.f;
+  for (uint32_t i = warp; i < n; i += kAttnWarps) {
+    const uint32_t phys = list[c0 + i];
+    float vv[EPL];
+    if (phys == sp.slot) {
+#pragma unroll
+      for (int e = 0; e < EPL; e++) vv[e] = v_new[lane * EPL + e];
+    } else if (phys < a.cache_slots) {
+      const uint4 raw = *reinterpret_cast<const uint4 *>(a.v_cache + (size_t)phys * kv_dim + (size_t)kvh * D + lane * EPL);
+      const __half2 *hp = reinterpret_cast<const __half2 *>(&raw);
+#pragma unroll
+      for (int e = 0; e < EPL / 2; e++) {
+        float2 f = __half22float2(hp[e]);
+        vv[2 * e] = f.x;
+        vv[2 * e + 1] = f.y;
+      }
+    } else {
+#pragma unroll
+      for (int e = 0; e < EPL; e++) vv[e] = 0.f;
+    }
+#pragma unroll
+    for (int h = 0; h < R; h++) {
+      const float p = sc[h * chunk_cap + i];
+#pragma unroll
+      for (int e = 0; e < EPL; e++) acc[h][e] = __fmaf_rn(p, vv[e], acc[h][e]);
+    }
+  }
+#pragma unroll
+  for (int h = 0; h < R; h++)
+#pragma unroll
+    for (int e = 0; e < EPL; e++) o_s[(warp * R + h) * D + lane * EPL + e] = acc[h][e];
+  __syncthreads();
+
+  // ---- partial out: [kvh][split][h] = {o[D], m, l} ----
+  float *part = a.partial + ((size_t)(kvh * splits + split) * R) * (D + 2);
+  for (int idx = tid; idx < R * D; idx += kAttnThreads) {
+    const int h = idx / D, d = idx % D;
+    float s = 0.f;
+    for (int w = 0; w < kAttnWarps; w++) s = __fadd_rn(s, o_s[(w * R + h) * D + d]);
+    part[h * (D + 2) + d] = s;
+  }
+  if (tid < R) {
+    part[tid * (D + 2) + D] = stat[2 * tid];
+    part[tid * (D + 2) + D + 1] = stat[2 * tid + 1];
+  }
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) {
+    const uint32_t old = atomicAdd(&a.counters[kvh], 1u);
+    last_flag = (old == (uint32_t)splits - 1) ? 1u : 0u;
+  }
+  __syncthreads();
+  if (!last_flag) return;
+  __threadfence();
+
+  // ---- combine (fixed split order) ----
+  const float *base = a.partial + ((size_t)kvh * splits * R) * (D + 2);
+  for (int idx = tid; idx < R * D; idx += kAttnThreads) {
+    const int h = idx / D, d = idx % D;
+    float M = -INFINITY;
+    for (int sp_i = 0; sp_i < splits; sp_i++) M = fmaxf(M, __ldcg(&base[((size_t)sp_i * R + h) * (D + 2) + D]));
+    float L = 0.f, O = 0.f;
+    for (int sp_i = 0; sp_i < splits; sp_i++) {
+      const float *p = base + ((size_t)sp_i * R + h) * (D + 2);
+      const float f = expf(__fsub_rn(__ldcg(&p[D]), M));
+      L = __fmaf_rn(__ldcg(&p[D + 1]), f, L);
+      O = __fmaf_rn(__ldcg(&p[d]), f, O);
+    }
+    const float inv = __fdiv_rn(1.0f, __fadd_rn(L, 1e-9f));
+    a.out[(size_t)(kvh * R + h) * D + d] = __fmul_rn(O, inv);
+  }
+  if (tid == 0) a.counters[kvh] = 0u;
+}
+
+template <int R>
+static cudaError_t launch_attn_t(const AttnArgs &a, int splits, cudaStream_t s, bool pdl) {
+  const int chunk_cap = (int)((a.cache_slots + splits - 1) / splits) + 1;
+  const size_t smem = sizeof(float) * ((size_t)R * 256 + 2 * 256 + (size_t)kAttnWarps * R * 256 + (size_t)R * chunk_cap);
+  static bool attr_done = false;
+  if (!attr_done) {
+    cudaError_t e = cudaFuncSetAttribute(decode_attn_kernel<R>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    if (e != cudaSuccess) return e;
+    attr_done = true;
+  }
+  if (smem > 227 * 1024) return cudaErrorInvalidValue;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(a.nkv, splits);
+  cfg.blockDim = dim3(kAttnThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, decode_attn_kernel<R>, a, splits, chunk_cap);
+}
+
+cudaError_t launch_decode_attn(const AttnArgs &a, int splits, cudaStream_t s, bool pdl) {
+  if (a.D != 256 || a.nkv == 0 || a.nq % a.nkv != 0) return cudaErrorInvalidValue;
+  const uint32_t R = a.nq / a.nkv;
+  switch (R) {
+    case 1: return launch_attn_t<1>(a, splits, s, pdl);
+    case 2: return launch_attn_t<2>(a, splits, s, pdl);
+    case 4: return launch_attn_t<4>(a, splits, s, pdl);
+    case 8: return launch_attn_t<8>(a, splits, s, pdl);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+}  // namespace ch

@@ -1,0 +1,575 @@
+// gemv.cu -- HBM-bound decode matvecs over repacked Q4 / Q8 weight tiles.
+//
+// Semantics restated from the reference shaders:
+//   gemv_q4.wgsl:28-93      y[r] = sum_b d_rb * sum_i (q_i - 8) * x_{32b+i}      (the f16 `min` is ignored)
+//   fused_qkv_q4.wgsl       q|k|v rows are one concatenated matrix here
+//   fused_mlp_q4.wgsl:33-128 act[r] = gelu_tanh(Wg x)[r] * (Wu x)[r]             (gate/up rows interleaved per tile)
+//   gemv_q8.wgsl            logits[r] = sum_b s_rb * sum_i q_i x_i               (int8, f32 scale)
+//
+// B200 design: each warp streams a contiguous range of 576-byte tiles with
+// 1-D bulk copies (cp.async.bulk, mbarrier completion, SPW stages per warp) --
+// the ranges are an even "stream-K" split of all tiles over every warp of a
+// persistent grid, so any matrix shape keeps every SM streaming.  Dequant is
+// in registers (LOP3/PRMT magic-number tricks giving exact q-8 / q in f16) and
+// the 16x16 weight fragments feed mma.sync as the A operand against x split
+// into f16 hi + lo columns (B), so each 32-weight block dot product is fp32
+// accurate; the block scale is applied in f32 exactly like the shader.
+// Partial row tiles at warp-range boundaries are combined deterministically
+// (fixed order) by the last-arriving warp.  The input prologue fuses the
+// reference's rmsnorm / add_rmsnorm passes (add_rmsnorm.wgsl:15-51) so no
+// separate norm kernel runs on the decode path.
+#include "common.cuh"
+#include "kernels.cuh"
+
+namespace ch {
+
+namespace {
+constexpr int NW = 8;    // consumer warps per CTA (each self-feeds its own stages)
+constexpr int SPW = 4;   // stages per warp
+constexpr int CT = 8;    // tiles per stage (4608 B per bulk copy)
+constexpr int kStageBytes = CT * kTileBytes;
+}  // namespace
+
+int num_sms() {
+  static int n = 0;
+  if (n == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (n <= 0) n = 148;
+  }
+  return n;
+}
+int gemv_default_grid() { return num_sms(); }
+size_t gemv_partial_floats(int grid) { return (size_t)grid * NW * 2 * 16; }
+
+// first tile of warp w's range
+CH_DEV uint64_t range_begin(uint64_t T, uint64_t w, uint64_t GW) { return (T * w) / GW; }
+// warp whose range contains tile t (T > 0)
+CH_DEV uint64_t warp_of(uint64_t t, uint64_t T, uint64_t GW) {
+  uint64_t w = ((t + 1) * GW + T - 1) / T - 1;
+  return w;
+}
+
+CH_DEV float gelu_tanh(float x) {
+  // src/kernels.zig:7-10 / fused_mlp_q4.wgsl:15-18 (explicit rounding, no contraction)
+  float x3 = __fmul_rn(__fmul_rn(__fmul_rn(0.044715f, x), x), x);
+  float inner = __fmul_rn(0.7978845608f, __fadd_rn(x, x3));
+  return __fmul_rn(__fmul_rn(0.5f, x), __fadd_rn(1.0f, tanhf(inner)));
+}
+
+template <int EPI>
+CH_DEV void epilogue(float *y, uint32_t rt, int g, float v0, float v1) {
+  if (EPI == EPI_STORE) {
+    y[rt * 16 + g] = v0;
+    y[rt * 16 + g + 8] = v1;
+  } else {
+    y[rt * 8 + g] = __fmul_rn(gelu_tanh(v0), v1);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// prologue: build the f16 hi/lo B fragments of the (optionally normed) input.
+// xf layout: [chunk of 16 k][t 0..3][hi|lo] uint2 {b0, b1}.
+CH_DEV void to_fragments(const float *v, uint2 *xf, uint32_t K) {
+  uint32_t n = (K / 16) * 4;
+  for (uint32_t idx = threadIdx.x; idx < n; idx += blockDim.x) {
+    uint32_t c = idx >> 2, t = idx & 3, base = c * 16 + 2 * t;
+    float v0 = v[base], v1 = v[base + 1], v2 = v[base + 8], v3 = v[base + 9];
+    __half h0 = __float2half_rn(v0), h1 = __float2half_rn(v1), h2 = __float2half_rn(v2), h3 = __float2half_rn(v3);
+    __half l0 = __float2half_rn(__fsub_rn(v0, __half2float(h0)));
+    __half l1 = __float2half_rn(__fsub_rn(v1, __half2float(h1)));
+    __half l2 = __float2half_rn(__fsub_rn(v2, __half2float(h2)));
+    __half l3 = __float2half_rn(__fsub_rn(v3, __half2float(h3)));
+    xf[c * 8 + t * 2 + 0] = make_uint2(pack_half2(h0, h1), pack_half2(h2, h3));
+    xf[c * 8 + t * 2 + 1] = make_uint2(pack_half2(l0, l1), pack_half2(l2, l3));
+  }
+}
+
+template <int PRO>
+CH_DEV void prologue(const GemvArgs &a, float *vec, uint2 *xf, float *red) {
+  const uint32_t K = a.K;
+  if (PRO == PRO_NONE) {
+    to_fragments(a.x, xf, K);
+    return;
+  }
+  const bool writer = (blockIdx.x == 0);
+  if (PRO == PRO_RMSNORM) {
+    float ss = 0.0f;
+    for (uint32_t i = threadIdx.x; i < K; i += blockDim.x) {
+      float v = a.x[i];
+      vec[i] = v;
+      ss = __fmaf_rn(v, v, ss);
+    }
+    ss = block_sum(ss, red);
+    float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)K), a.eps)));
+    for (uint32_t i = threadIdx.x; i < K; i += blockDim.x) {
+      float v = __fmul_rn(__fmul_rn(vec[i], inv), a.norm_w[i]);
+      vec[i] = v;
+      if (writer && a.normed_out) a.normed_out[i] = v;
+    }
+  } else {  // PRO_ADD_RMSNORM: r' = post_w ? rmsnorm(r) : r ; x = (x_in + r') * scalar ; y = rmsnorm(x) * w
+    if (a.post_w) {
+      float ss = 0.0f;
+      for (uint32_t i = threadIdx.x; i < K; i += blockDim.x) {
+        float v = a.r[i];
+        vec[i] = v;
+        ss = __fmaf_rn(v, v, ss);
+      }
+      ss = block_sum(ss, red);
+      float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)K), a.eps)));
+      for (uint32_t i = threadIdx.x; i < K; i += blockDim.x) vec[i] = __fmul_rn(__fmul_rn(vec[i], inv), a.post_w[i]);
+    } else {
+      for (uint32_t i = threadIdx.x; i < K; i += blockDim.x) vec[i] = a.r[i];
+    }
+    float ss = 0.0f;
+    for (uint32_t i = threadIdx.x; i < K; i += blockDim.x) {
+      float v = __fmul_rn(__fadd_rn(a.x[i], vec[i]), a.scalar);
+      vec[i] = v;
+      if (writer && a.x_out) a.x_out[i] = v;
+      ss = __fmaf_rn(v, v, ss);
+    }
+    ss = block_sum(ss, red);
+    float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)K), a.eps)));
+    for (uint32_t i = threadIdx.x; i < K; i += blockDim.x) {
+      float v = __fmul_rn(__fmul_rn(vec[i], inv), a.norm_w[i]);
+      vec[i] = v;
+      if (writer && a.normed_out) a.normed_out[i] = v;
+    }
+  }
+  __syncthreads();
+  to_fragments(vec, xf, K);
+}
+
+// one 576-byte tile: 16 rows; lanes with t == 0 accumulate rows g and g+8
+template <int FMT>
+CH_DEV void tile_mma(const uint8_t *tile, uint32_t kt, const uint2 *xf, int lane, float &acc0, float &acc1) {
+  const int g = lane >> 2, t = lane & 3;
+  const uint4 w = *reinterpret_cast<const uint4 *>(tile + lane * 16);
+  if (FMT == FMT_Q4) {
+    const uint2 sc = *reinterpret_cast<const uint2 *>(tile + 512 + g * 8);
+    const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+    for (int blk = 0; blk < 2; blk++) {
+      float d[4] = {0.f, 0.f, 0.f, 0.f};
+      uint32_t af[4];
+#pragma unroll
+      for (int ch = 0; ch < 2; ch++) {
+        const uint32_t c = kt * 4 + blk * 2 + ch;
+        const uint2 b = (g < 2) ? xf[c * 8 + t * 2 + g] : make_uint2(0u, 0u);
+        dequant_q4_word(ws[blk * 2 + ch], af);
+        mma_16816(d, af, b.x, b.y);
+      }
+      const float s0 = __half2float(__ushort_as_half((unsigned short)((blk ? sc.x >> 16 : sc.x) & 0xFFFFu)));
+      const float s1 = __half2float(__ushort_as_half((unsigned short)((blk ? sc.y >> 16 : sc.y) & 0xFFFFu)));
+      acc0 = __fmaf_rn(s0, __fadd_rn(d[0], d[1]), acc0);
+      acc1 = __fmaf_rn(s1, __fadd_rn(d[2], d[3]), acc1);
+    }
+  } else {
+    const float2 sc = *reinterpret_cast<const float2 *>(tile + 512 + g * 8);
+    float d[4] = {0.f, 0.f, 0.f, 0.f};
+    uint32_t af[4];
+#pragma unroll
+    for (int ch = 0; ch < 2; ch++) {
+      const uint32_t c = kt * 2 + ch;
+      const uint2 b = (g < 2) ? xf[c * 8 + t * 2 + g] : make_uint2(0u, 0u);
+      dequant_q8_words(ch ? w.z : w.x, ch ? w.w : w.y, af);
+      mma_16816(d, af, b.x, b.y);
+    }
+    acc0 = __fmaf_rn(sc.x, __fadd_rn(d[0], d[1]), acc0);
+    acc1 = __fmaf_rn(sc.y, __fadd_rn(d[2], d[3]), acc1);
+  }
+}
+
+template <int FMT, int EPI, int PRO>
+__global__ void __launch_bounds__(NW * 32, 1) gemv_kernel(const GemvArgs a) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint8_t *stages = smem;
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + NW * SPW * kStageBytes);
+  uint2 *xf = reinterpret_cast<uint2 *>(smem + NW * SPW * kStageBytes + NW * SPW * 8);
+  float *vec = reinterpret_cast<float *>(reinterpret_cast<uint8_t *>(xf) + (a.K / 16) * 64);
+  __shared__ float red[32];
+
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int g = lane >> 2, t = lane & 3;
+  const uint64_t GW = (uint64_t)gridDim.x * NW;
+  const uint64_t gw = (uint64_t)blockIdx.x * NW + warp;
+  const uint64_t KT = a.k_tiles;
+  const uint64_t T = (uint64_t)a.row_tiles * KT;
+  const uint64_t tb = range_begin(T, gw, GW), te = range_begin(T, gw + 1, GW);
+  const uint32_t nchunks = (uint32_t)((te - tb + CT - 1) / CT);
+  uint8_t *my_stages = stages + (size_t)warp * SPW * kStageBytes;
+  uint64_t *my_bars = bars + warp * SPW;
+
+  // weights do not depend on the previous kernel: start streaming before the dependency wait
+  if (lane == 0) {
+    for (int s = 0; s < SPW; s++) mbar_init(&my_bars[s], 1);
+    fence_mbar_init();
+    for (uint32_t j = 0; j < (uint32_t)SPW && j < nchunks; j++) {
+      uint64_t t0 = tb + (uint64_t)j * CT;
+      uint32_t bytes = (uint32_t)(min((uint64_t)CT, te - t0) * kTileBytes);
+      mbar_arrive_expect_tx(&my_bars[j], bytes);
+      bulk_g2s(my_stages + (size_t)j * kStageBytes, a.tiles + t0 * kTileBytes, bytes, &my_bars[j]);
+    }
+  }
+  __syncwarp();
+
+  grid_dep_wait();
+  prologue<PRO>(a, vec, xf, red);
+  __syncthreads();
+  grid_dep_launch();
+
+  uint64_t cur_rt = ~0ull;
+  uint32_t kt_begin = 0, kt = 0;
+  uint64_t rt = 0;
+  float acc0 = 0.f, acc1 = 0.f;
+  bool first_seg = true;
+  bool ok = true;
+  if (nchunks > 0) {
+    rt = tb / KT;
+    kt = (uint32_t)(tb - rt * KT);
+  }
+
+  auto flush = [&](uint64_t frt, uint32_t kb, uint32_t ke) {
+    const bool full = (kb == 0 && ke == (uint32_t)KT);
+    if (full) {
+      if (t == 0) epilogue<EPI>(a.y, (uint32_t)frt, g, acc0, acc1);
+    } else {
+      const int slot = first_seg ? 0 : 1;
+      if (t == 0) {
+        a.partial[(gw * 2 + slot) * 16 + g] = acc0;
+        a.partial[(gw * 2 + slot) * 16 + g + 8] = acc1;
+      }
+      __threadfence();
+      __syncwarp();
+      uint32_t old = 0;
+      if (lane == 0) old = atomicAdd(&a.counters[frt], 1u);
+      old = __shfl_sync(0xffffffffu, old, 0);
+      const uint64_t w_first = warp_of(frt * KT, T, GW), w_last = warp_of((frt + 1) * KT - 1, T, GW);
+      uint32_t ncontrib = 0;
+      for (uint64_t w = w_first; w <= w_last; w++)
+        if (range_begin(T, w + 1, GW) > range_begin(T, w, GW)) ncontrib++;
+      if (old == ncontrib - 1) {
+        __threadfence();
+        float v0 = 0.f, v1 = 0.f;
+        for (uint64_t w = w_first; w <= w_last; w++) {
+          uint64_t b = range_begin(T, w, GW);
+          if (range_begin(T, w + 1, GW) == b) continue;
+          const int sl = (b / KT == frt) ? 0 : 1;
+          v0 = __fadd_rn(v0, __ldcg(&a.partial[(w * 2 + sl) * 16 + g]));
+          v1 = __fadd_rn(v1, __ldcg(&a.partial[(w * 2 + sl) * 16 + g + 8]));
+        }
+        if (t == 0) epilogue<EPI>(a.y, (uint32_t)frt, g, v0, v1);
+        if (lane == 0) a.counters[frt] = 0u;
+      }
+    }
+    first_seg = false;
+  };
+
+  uint32_t failed_at = 0;
+  for (uint32_t j = 0; j < nchunks && ok; j++) {
+    const int s = j % SPW;
+    if (!mbar_wait_bounded(&my_bars[s], (j / SPW) & 1, a.err)) {
+      ok = false;
+      failed_at = j;
+      break;
+    }
+    const uint8_t *st = my_stages + (size_t)s * kStageBytes;
+    const uint64_t t0 = tb + (uint64_t)j * CT;
+    const uint32_t nt = (uint32_t)min((uint64_t)CT, te - t0);
+    for (uint32_t i = 0; i < nt; i++) {
+      if (rt != cur_rt) {
+        if (cur_rt != ~0ull) flush(cur_rt, kt_begin, (uint32_t)KT);
+        cur_rt = rt;
+        kt_begin = kt;
+        acc0 = acc1 = 0.f;
+      }
+      tile_mma<FMT>(st + (size_t)i * kTileBytes, kt, xf, lane, acc0, acc1);
+      if (++kt == (uint32_t)KT) {
+        kt = 0;
+        rt++;
+      }
+    }
+    __syncwarp();
+    if (lane == 0 && j + SPW < nchunks) {
+      fence_proxy_async();
+      const uint64_t tn = tb + (uint64_t)(j + SPW) * CT;
+      const uint32_t bytes = (uint32_t)(min((uint64_t)CT, te - tn) * kTileBytes);
+      mbar_arrive_expect_tx(&my_bars[s], bytes);
+      bulk_g2s(my_stages + (size_t)s * kStageBytes, a.tiles + tn * kTileBytes, bytes, &my_bars[s]);
+    }
+  }
+  if (!ok) {
+    // drain the copies this warp still has in flight (chunks failed_at .. +SPW-1), bounded
+    for (uint32_t j = failed_at + 1; j < nchunks && j < failed_at + SPW; j++)
+      mbar_wait_bounded(&my_bars[j % SPW], (j / SPW) & 1, nullptr, 100000000ull);
+    return;
+  }
+  if (cur_rt != ~0ull) {
+    const uint32_t ke = (uint32_t)(te - cur_rt * KT);
+    flush(cur_rt, kt_begin, ke);
+  }
+}
+
+template <int FMT, int EPI, int PRO>
+static cudaError_t launch_gemv_t(const GemvArgs &a, int grid, cudaStream_t s, bool pdl) {
+  size_t smem = (size_t)NW * SPW * kStageBytes + NW * SPW * 8 + (size_t)(a.K / 16) * 64;
+  if (PRO != PRO_NONE) smem += (size_t)a.K * 4;
+  static bool attr_done = false;
+  if (!attr_done) {
+    cudaError_t e = cudaFuncSetAttribute(gemv_kernel<FMT, EPI, PRO>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         227 * 1024);
+    if (e != cudaSuccess) return e;
+    attr_done = true;
+  }
+  if (smem > 227 * 1024) return cudaErrorInvalidValue;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(NW * 32);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, gemv_kernel<FMT, EPI, PRO>, a);
+}
+
+cudaError_t launch_gemv(const GemvPlan &p, const GemvArgs &a, cudaStream_t s, bool pdl) {
+  if (a.K % 64 != 0 && p.fmt == FMT_Q4) return cudaErrorInvalidValue;
+  if (a.K % 32 != 0) return cudaErrorInvalidValue;
+  int grid = p.grid > 0 ? p.grid : gemv_default_grid();
+#define CH_GEMV_CASE(F, E, P) \
+  if (p.fmt == F && p.epi == E && p.pro == P) return launch_gemv_t<F, E, P>(a, grid, s, pdl);
+  CH_GEMV_CASE(FMT_Q4, EPI_STORE, PRO_NONE)
+  CH_GEMV_CASE(FMT_Q4, EPI_STORE, PRO_RMSNORM)
+  CH_GEMV_CASE(FMT_Q4, EPI_STORE, PRO_ADD_RMSNORM)
+  CH_GEMV_CASE(FMT_Q4, EPI_GELU_MUL, PRO_NONE)
+  CH_GEMV_CASE(FMT_Q4, EPI_GELU_MUL, PRO_RMSNORM)
+  CH_GEMV_CASE(FMT_Q4, EPI_GELU_MUL, PRO_ADD_RMSNORM)
+  CH_GEMV_CASE(FMT_Q8, EPI_STORE, PRO_NONE)
+  CH_GEMV_CASE(FMT_Q8, EPI_STORE, PRO_RMSNORM)
+  CH_GEMV_CASE(FMT_Q8, EPI_STORE, PRO_ADD_RMSNORM)
+#undef CH_GEMV_CASE
+  return cudaErrorInvalidValue;
+}
+
+// ---------------------------------------------------------------------------
+// repack: quant.zig blocks (5 words / 32 weights, src/quant.zig:54-98) -> tiles.
+// One thread per (tile, lane).  rowmap MAP_GATEUP interleaves two matrices:
+// tile rows 0..7 come from `src` rows rt*8.., rows 8..15 from `src_b`.
+CH_DEV uint32_t q4_nib(const uint32_t *src, uint32_t nb, uint32_t row, uint32_t k) {
+  uint32_t b = k >> 5, n = k & 31;
+  return (src[((size_t)row * nb + b) * 5 + 1 + (n >> 3)] >> (4 * (n & 7))) & 0xFu;
+}
+__global__ void repack_q4_kernel(const uint32_t *src, const uint32_t *src_b, uint32_t rows_out, uint32_t cols, int rowmap,
+                                 uint8_t *dst) {
+  const uint32_t KT = cols / kQ4TileK, nb = cols / 32;
+  const uint64_t total = (uint64_t)(rows_out / 16) * KT * 32;
+  for (uint64_t idx = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; idx < total;
+       idx += (uint64_t)gridDim.x * blockDim.x) {
+    const uint32_t lane = idx & 31;
+    const uint64_t tile = idx >> 5;
+    const uint32_t rt = (uint32_t)(tile / KT), kt = (uint32_t)(tile % KT);
+    const uint32_t g = lane >> 2, t = lane & 3;
+    const uint32_t *sa, *sb;
+    uint32_t ra, rb;
+    if (rowmap == MAP_GATEUP) {
+      sa = src;
+      sb = src_b;
+      ra = rt * 8 + g;
+      rb = rt * 8 + g;
+    } else {
+      sa = src;
+      sb = src;
+      ra = rt * 16 + g;
+      rb = rt * 16 + g + 8;
+    }
+    uint32_t out[4];
+#pragma unroll
+    for (int blk = 0; blk < 2; blk++)
+#pragma unroll
+      for (int ch = 0; ch < 2; ch++) {
+        const uint32_t kb = kt * 64 + blk * 32 + ch * 16;
+        uint32_t w = 0;
+        w |= q4_nib(sa, nb, ra, kb + 2 * t) << 0;
+        w |= q4_nib(sa, nb, ra, kb + 2 * t + 1) << 16;
+        w |= q4_nib(sb, nb, rb, kb + 2 * t) << 4;
+        w |= q4_nib(sb, nb, rb, kb + 2 * t + 1) << 20;
+        w |= q4_nib(sa, nb, ra, kb + 2 * t + 8) << 8;
+        w |= q4_nib(sa, nb, ra, kb + 2 * t + 9) << 24;
+        w |= q4_nib(sb, nb, rb, kb + 2 * t + 8) << 12;
+        w |= q4_nib(sb, nb, rb, kb + 2 * t + 9) << 28;
+        out[blk * 2 + ch] = w;
+      }
+    uint8_t *tp = dst + tile * kTileBytes;
+    *reinterpret_cast<uint4 *>(tp + lane * 16) = make_uint4(out[0], out[1], out[2], out[3]);
+    if (t == 0) {
+      const uint32_t b0 = kt * 2, b1 = kt * 2 + 1;
+      uint32_t sa0 = sa[((size_t)ra * nb + b0) * 5] & 0xFFFFu, sa1 = sa[((size_t)ra * nb + b1) * 5] & 0xFFFFu;
+      uint32_t sb0 = sb[((size_t)rb * nb + b0) * 5] & 0xFFFFu, sb1 = sb[((size_t)rb * nb + b1) * 5] & 0xFFFFu;
+      *reinterpret_cast<uint2 *>(tp + 512 + g * 8) = make_uint2(sa0 | (sa1 << 16), sb0 | (sb1 << 16));
+    }
+  }
+}
+// Q8_0 blocks (9 words / 32, src/quant.zig:19-52) -> tiles; bytes stored as q ^ 0x80
+CH_DEV uint32_t q8_byte(const uint32_t *src, uint32_t nb, uint32_t row, uint32_t k) {
+  uint32_t b = k >> 5, n = k & 31;
+  return ((src[((size_t)row * nb + b) * 9 + 1 + (n >> 2)] >> (8 * (n & 3))) & 0xFFu) ^ 0x80u;
+}
+__global__ void repack_q8_kernel(const uint32_t *src, uint32_t rows, uint32_t cols, uint8_t *dst) {
+  const uint32_t KT = cols / kQ8TileK, nb = cols / 32;
+  const uint64_t total = (uint64_t)(rows / 16) * KT * 32;
+  for (uint64_t idx = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; idx < total;
+       idx += (uint64_t)gridDim.x * blockDim.x) {
+    const uint32_t lane = idx & 31;
+    const uint64_t tile = idx >> 5;
+    const uint32_t rt = (uint32_t)(tile / KT), kt = (uint32_t)(tile % KT);
+    const uint32_t g = lane >> 2, t = lane & 3;
+    const uint32_t ra = rt * 16 + g, rb = ra + 8;
+    uint32_t out[4];
+#pragma unroll
+    for (int ch = 0; ch < 2; ch++) {
+      const uint32_t kb = kt * 32 + ch * 16;
+      out[ch * 2 + 0] = q8_byte(src, nb, ra, kb + 2 * t) | (q8_byte(src, nb, ra, kb + 2 * t + 1) << 8) |
+                        (q8_byte(src, nb, rb, kb + 2 * t) << 16) | (q8_byte(src, nb, rb, kb + 2 * t + 1) << 24);
+      out[ch * 2 + 1] = q8_byte(src, nb, ra, kb + 2 * t + 8) | (q8_byte(src, nb, ra, kb + 2 * t + 9) << 8) |
+                        (q8_byte(src, nb, rb, kb + 2 * t + 8) << 16) | (q8_byte(src, nb, rb, kb + 2 * t + 9) << 24);
+    }
+    uint8_t *tp = dst + tile * kTileBytes;
+    *reinterpret_cast<uint4 *>(tp + lane * 16) = make_uint4(out[0], out[1], out[2], out[3]);
+    if (t == 0) {
+      uint32_t da = src[((size_t)ra * nb + kt) * 9], db = src[((size_t)rb * nb + kt) * 9];
+      *reinterpret_cast<uint2 *>(tp + 512 + g * 8) = make_uint2(da, db);
+    }
+  }
+}
+
+static int grid_for(uint64_t n, int block) {
+  uint64_t g = (n + block - 1) / block;
+  uint64_t cap = (uint64_t)num_sms() * 16;
+  return (int)(g < cap ? (g > 0 ? g : 1) : cap);
+}
+
+cudaError_t launch_repack_q4(const uint32_t *src, const uint32_t *src_b, uint32_t rows_out, uint32_t cols, int rowmap,
+                             uint8_t *dst, cudaStream_t s) {
+  if (rows_out % 16 || cols % 64) return cudaErrorInvalidValue;
+  uint64_t n = (uint64_t)(rows_out / 16) * (cols / 64) * 32;
+  repack_q4_kernel<<<grid_for(n, 256), 256, 0, s>>>(src, src_b ? src_b : src, rows_out, cols, rowmap, dst);
+  return cudaGetLastError();
+}
+cudaError_t launch_repack_q8(const uint32_t *src, uint32_t rows, uint32_t cols, uint8_t *dst, cudaStream_t s) {
+  if (rows % 16 || cols % 32) return cudaErrorInvalidValue;
+  uint64_t n = (uint64_t)(rows / 16) * (cols / 32) * 32;
+  repack_q8_kernel<<<grid_for(n, 256), 256, 0, s>>>(src, rows, cols, dst);
+  return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
+// seeded synthetic tensors (same spec as the oracle's or_gen_*)
+__global__ void gen_q4_kernel(uint32_t *dst, uint64_t nblocks, uint64_t tseed, float scale_std) {
+  for (uint64_t blk = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; blk < nblocks;
+       blk += (uint64_t)gridDim.x * blockDim.x) {
+    uint64_t ha = hash3(tseed, 0, blk * 2), hb = hash3(tseed, 0, blk * 2 + 1);
+    float z = gen_normal(tseed, 1, blk);
+    float d = __fmul_rn(fabsf(z), scale_std);
+    __half d16 = __float2half_rn(d);
+    __half m16 = __float2half_rn(__fmul_rn(-8.0f, __half2float(d16)));
+    uint32_t *o = dst + blk * 5;
+    o[0] = (uint32_t)__half_as_ushort(d16) | ((uint32_t)__half_as_ushort(m16) << 16);
+    o[1] = (uint32_t)ha;
+    o[2] = (uint32_t)(ha >> 32);
+    o[3] = (uint32_t)hb;
+    o[4] = (uint32_t)(hb >> 32);
+  }
+}
+__global__ void gen_bf16_kernel(uint16_t *dst, uint64_t n, uint64_t tseed, float mean, float std) {
+  for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n; i += (uint64_t)gridDim.x * blockDim.x) {
+    float z = gen_normal(tseed, 2, i);
+    dst[i] = bf16_rne(__fadd_rn(mean, __fmul_rn(z, std)));
+  }
+}
+__global__ void gen_f32_kernel(float *dst, uint64_t n, uint64_t tseed, float mean, float std) {
+  for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n; i += (uint64_t)gridDim.x * blockDim.x) {
+    float z = gen_normal(tseed, 3, i);
+    dst[i] = __fadd_rn(mean, __fmul_rn(z, std));
+  }
+}
+__global__ void bf16_to_f32_kernel(const uint16_t *src, float *dst, uint64_t n) {
+  for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n; i += (uint64_t)gridDim.x * blockDim.x)
+    dst[i] = bf16_to_f32(src[i]);
+}
+// quantizeRowQ8_0 (src/quant.zig:21-52), one warp per 32-element block
+__global__ void quantize_q8_kernel(const uint16_t *src, uint64_t nblocks, uint32_t *dst) {
+  const int lane = threadIdx.x & 31;
+  for (uint64_t blk = (blockIdx.x * (uint64_t)blockDim.x + threadIdx.x) >> 5; blk < nblocks;
+       blk += ((uint64_t)gridDim.x * blockDim.x) >> 5) {
+    float v = bf16_to_f32(src[blk * 32 + lane]);
+    float amax = warp_max(fabsf(v));
+    float d = __fdiv_rn(amax, 127.0f);
+    float id = amax > 0.0f ? __fdiv_rn(127.0f, amax) : 0.0f;
+    int q = (int)roundf(__fmul_rn(v, id));
+    q = max(-128, min(127, q));
+    uint32_t byte = (uint32_t)(q & 0xFF) << (8 * (lane & 3));
+    byte |= __shfl_xor_sync(0xffffffffu, byte, 1);
+    byte |= __shfl_xor_sync(0xffffffffu, byte, 2);
+    uint32_t *o = dst + blk * 9;
+    if (lane == 0) o[0] = __float_as_uint(d);
+    if ((lane & 3) == 0) o[1 + (lane >> 2)] = byte;
+  }
+}
+// quantizeRowQ4_0 (src/quant.zig:58-98), one warp per block
+__global__ void quantize_q4_kernel(const uint16_t *src, uint64_t nblocks, uint32_t *dst) {
+  const int lane = threadIdx.x & 31;
+  for (uint64_t blk = (blockIdx.x * (uint64_t)blockDim.x + threadIdx.x) >> 5; blk < nblocks;
+       blk += ((uint64_t)gridDim.x * blockDim.x) >> 5) {
+    float v = bf16_to_f32(src[blk * 32 + lane]);
+    float amax = warp_max(fabsf(v));
+    float d = __fdiv_rn(amax, 8.0f);
+    float id = d > 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+    int q = (int)roundf(__fadd_rn(__fmul_rn(v, id), 8.0f));
+    q = max(0, min(15, q));
+    uint32_t nib = (uint32_t)q << (4 * (lane & 7));
+    nib |= __shfl_xor_sync(0xffffffffu, nib, 1);
+    nib |= __shfl_xor_sync(0xffffffffu, nib, 2);
+    nib |= __shfl_xor_sync(0xffffffffu, nib, 4);
+    uint32_t *o = dst + blk * 5;
+    if (lane == 0) {
+      __half s = __float2half_rn(d), m = __float2half_rn(__fmul_rn(-8.0f, d));
+      o[0] = (uint32_t)__half_as_ushort(s) | ((uint32_t)__half_as_ushort(m) << 16);
+    }
+    if ((lane & 7) == 0) o[1 + (lane >> 3)] = nib;
+  }
+}
+
+cudaError_t launch_gen_q4_blocks(uint32_t *dst, uint32_t rows, uint32_t cols, uint64_t tseed, float scale_std,
+                                 cudaStream_t s) {
+  uint64_t nb = (uint64_t)rows * (cols / 32);
+  gen_q4_kernel<<<grid_for(nb, 256), 256, 0, s>>>(dst, nb, tseed, scale_std);
+  return cudaGetLastError();
+}
+cudaError_t launch_gen_bf16(uint16_t *dst, size_t n, uint64_t tseed, float mean, float std, cudaStream_t s) {
+  gen_bf16_kernel<<<grid_for(n, 256), 256, 0, s>>>(dst, n, tseed, mean, std);
+  return cudaGetLastError();
+}
+cudaError_t launch_gen_f32(float *dst, size_t n, uint64_t tseed, float mean, float std, cudaStream_t s) {
+  gen_f32_kernel<<<grid_for(n, 256), 256, 0, s>>>(dst, n, tseed, mean, std);
+  return cudaGetLastError();
+}
+cudaError_t launch_bf16_to_f32(const uint16_t *src, float *dst, size_t n, cudaStream_t s) {
+  bf16_to_f32_kernel<<<grid_for(n, 256), 256, 0, s>>>(src, dst, n);
+  return cudaGetLastError();
+}
+cudaError_t launch_quantize_q8_rows(const uint16_t *src, uint32_t rows, uint32_t cols, uint32_t *dst, cudaStream_t s) {
+  uint64_t nb = (uint64_t)rows * (cols / 32);
+  quantize_q8_kernel<<<grid_for(nb * 32, 256), 256, 0, s>>>(src, nb, dst);
+  return cudaGetLastError();
+}
+cudaError_t launch_quantize_q4_rows(const uint16_t *src, uint32_t rows, uint32_t cols, uint32_t *dst, cudaStream_t s) {
+  uint64_t nb = (uint64_t)rows * (cols / 32);
+  quantize_q4_kernel<<<grid_for(nb * 32, 256), 256, 0, s>>>(src, nb, dst);
+  return cudaGetLastError();
+}
+
+}  // namespace ch

@@ -1,0 +1,169 @@
+// kernels.cuh -- host-side launch interface of the device kernels (internal to
+// libchannel_b200; the public boundary is include/channel_cuda.h).
+#pragma once
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace ch {
+
+// ---------------------------------------------------------------------------
+// repacked weight tiles: 16 rows x 64 k (Q4) or 16 rows x 32 k (Q8), 576 bytes:
+// 512 bytes of mma A-fragments (lane-major, 16 B per lane) + 64 bytes of scales.
+constexpr int kTileBytes = 576;
+constexpr int kTileRows = 16;
+constexpr int kQ4TileK = 64;
+constexpr int kQ8TileK = 32;
+
+enum WFmt { FMT_Q4 = 0, FMT_Q8 = 1 };
+enum Epi { EPI_STORE = 0, EPI_GELU_MUL = 1 };
+enum Pro { PRO_NONE = 0, PRO_RMSNORM = 1, PRO_ADD_RMSNORM = 2 };
+enum RowMap { MAP_PLAIN = 0, MAP_GATEUP = 1 };
+
+inline size_t q4_tile_bytes(uint32_t rows, uint32_t cols) {
+  return (size_t)(rows / kTileRows) * (cols / kQ4TileK) * kTileBytes;
+}
+inline size_t q8_tile_bytes(uint32_t rows, uint32_t cols) {
+  return (size_t)(rows / kTileRows) * (cols / kQ8TileK) * kTileBytes;
+}
+
+struct GemvArgs {
+  const uint8_t *tiles = nullptr;
+  uint32_t row_tiles = 0, k_tiles = 0, K = 0;
+  const float *x = nullptr;       // input (PRO_NONE), or x / x_in for the norm prologues
+  const float *r = nullptr;       // PRO_ADD_RMSNORM: branch output added to x_in
+  const float *post_w = nullptr;  // PRO_ADD_RMSNORM: optional rmsnorm weight applied to r first
+  const float *norm_w = nullptr;  // norm weight of the prologue
+  float scalar = 1.0f, eps = 1e-6f;
+  float *x_out = nullptr;       // PRO_ADD_RMSNORM: updated residual (written by CTA 0)
+  float *normed_out = nullptr;  // optional copy of the normed input (written by CTA 0)
+  float *y = nullptr;
+  float *partial = nullptr;     // stream-K partials [grid*warps][2][16]
+  uint32_t *counters = nullptr; // per row tile, zero between launches
+  uint32_t *err = nullptr;
+};
+
+struct GemvPlan {
+  int fmt = FMT_Q4, epi = EPI_STORE, pro = PRO_NONE;
+  int grid = 0;
+};
+
+int num_sms();
+// scratch sizes needed by gemv for a given grid
+size_t gemv_partial_floats(int grid);
+int gemv_default_grid();
+cudaError_t launch_gemv(const GemvPlan &plan, const GemvArgs &a, cudaStream_t s, bool pdl);
+
+// repack / generate
+cudaError_t launch_repack_q4(const uint32_t *src_blocks, const uint32_t *src_blocks_b, uint32_t rows_out, uint32_t cols,
+                             int rowmap, uint8_t *dst, cudaStream_t s);
+cudaError_t launch_repack_q8(const uint32_t *src_blocks, uint32_t rows, uint32_t cols, uint8_t *dst, cudaStream_t s);
+cudaError_t launch_gen_q4_blocks(uint32_t *dst, uint32_t rows, uint32_t cols, uint64_t tseed, float scale_std,
+                                 cudaStream_t s);
+cudaError_t launch_gen_bf16(uint16_t *dst, size_t n, uint64_t tseed, float mean, float std, cudaStream_t s);
+cudaError_t launch_gen_f32(float *dst, size_t n, uint64_t tseed, float mean, float std, cudaStream_t s);
+cudaError_t launch_bf16_to_f32(const uint16_t *src, float *dst, size_t n, cudaStream_t s);
+cudaError_t launch_quantize_q8_rows(const uint16_t *src_bf16, uint32_t rows, uint32_t cols, uint32_t *dst,
+                                    cudaStream_t s);
+cudaError_t launch_quantize_q4_rows(const uint16_t *src_bf16, uint32_t rows, uint32_t cols, uint32_t *dst,
+                                    cudaStream_t s);
+
+// ---------------------------------------------------------------------------
+// decode step state read by the kernels (updated by H2D copy or by step_begin)
+struct StepParams {
+  uint32_t clock, slot, n_active, n_sliding;
+  const uint32_t *active;   // device list of physical slots (full-attention layers)
+  const uint32_t *sliding;  // device list (sliding layers)
+  uint32_t step, pad;
+};
+
+struct AttnArgs {
+  const float *qkv;      // q [nq*D] | k [nkv*D] | v [nkv*D] (raw projections)
+  const float *q_norm_w, *k_norm_w;
+  const float *inv_freq;  // [rot/2]
+  __half *k_cache, *v_cache;  // [4096][nkv*D]
+  const StepParams *sp;
+  int is_sliding;
+  uint32_t nq, nkv, D, rot;
+  float eps, scale;
+  float *out;           // [nq*D]
+  float *partial;       // [nkv][splits][ratio][D+2]
+  uint32_t *counters;   // [nkv]
+  uint32_t *err;
+  uint32_t cache_slots; // 4096
+};
+int attn_default_splits(uint32_t nkv);
+size_t attn_partial_floats(uint32_t nkv, uint32_t ratio, uint32_t D, int splits);
+cudaError_t launch_decode_attn(const AttnArgs &a, int splits, cudaStream_t s, bool pdl);
+
+struct TopkArgs {
+  const float *logits;
+  uint32_t V;
+  uint64_t *cand;      // [blocks][64] composite keys
+  uint32_t *counter;   // 1 word, zero between launches
+  uint32_t *ids;       // [64]
+  float *vals;         // [64]
+  uint32_t *token_out;          // optional: ids[0]
+  uint32_t *token_hist;         // optional: token history [hist_cap], indexed by sp->step
+  uint32_t hist_cap;
+  StepParams *sp;               // optional: step counter advanced by the last CTA
+  uint32_t *err;
+};
+int topk_blocks(uint32_t V);
+cudaError_t launch_topk64(const TopkArgs &a, cudaStream_t s, bool pdl);
+
+// embedding + step advance for the device-resident decode loop
+struct StepBeginArgs {
+  const uint16_t *embed;  // bf16 [V][H]
+  uint32_t H;
+  float embed_scale;
+  const uint32_t *token;  // current token id
+  float *x;               // f32 [H]
+  StepParams *sp;
+  const StepParams *plan; // [n_plan]
+  uint32_t n_plan;
+  uint32_t *err;
+};
+cudaError_t launch_step_begin(const StepBeginArgs &a, cudaStream_t s, bool pdl);
+
+// standalone ops (tests and prefill)
+cudaError_t launch_rmsnorm_rows(const float *x, const float *w, float *y, uint32_t N, uint32_t H, float eps,
+                                cudaStream_t s);
+cudaError_t launch_add_rmsnorm_rows(float *x, const float *r, const float *w, float *y, uint32_t N, uint32_t H,
+                                    float eps, float scalar, cudaStream_t s);
+cudaError_t launch_embed_rows(const uint16_t *embed, const uint32_t *tokens, uint32_t N, uint32_t H, float scale,
+                              float *x, cudaStream_t s);
+
+// batched prefill
+struct BatchQkvRopeArgs {
+  const float *q, *k, *v;  // token t at q + t*q_stride, k/v + t*kv_stride
+  uint32_t q_stride, kv_stride;
+  const float *q_norm_w, *k_norm_w, *inv_freq;
+  float *q_out;
+  __half *k_cache, *v_cache;
+  const uint32_t *slots;  // device
+  uint32_t slot_offset, start_clock, N, nq, nkv, D, rot;
+  float eps;
+  int k_eq_v;
+};
+cudaError_t launch_batch_qkv_rope(const BatchQkvRopeArgs &a, cudaStream_t s);
+struct BatchAttnArgs {
+  const float *q;  // [N][nq*D] (normed + roped)
+  const __half *k_cache, *v_cache;
+  const uint32_t *slots;
+  uint32_t N, num_prev, nq, nkv, D;
+  float scale;
+  int is_sliding;
+  float *out;  // [N][nq*D]
+};
+cudaError_t launch_batch_causal_attn(const BatchAttnArgs &a, cudaStream_t s);
+struct BatchGemmArgs {
+  const uint8_t *tiles;  // Q4 tiles
+  uint32_t M, K, N;      // rows, cols, tokens
+  const float *X;        // [N][K]
+  float *Y;              // EPI_STORE: [N][M]; EPI_GELU_MUL: [N][M/2]
+  int epi;
+};
+cudaError_t launch_batch_gemm_q4(const BatchGemmArgs &a, cudaStream_t s);
+
+}  // namespace ch

@@ -1,0 +1,1224 @@
+// model.cu -- the C-ABI (include/channel_cuda.h): context, model upload and
+// repack, the decode step (captured once into a CUDA graph with programmatic
+// dependent launches), batched prefill, state access, the device-resident
+// greedy loop and the op-level entry points.
+//
+// Reference interfaces replaced (Sullux/channel):
+//   GpuContext.init/deinit            src/gpu/context.zig:17-109
+//   GpuModelContext.init/deinit       src/gpu/model_gpu.zig:68-216
+//   recordForwardGraph / gpuDispatchForwardToken  src/gpu/model_dispatch.zig:226-369
+//   gpuDispatchPrefillBatch           src/gpu/batch_dispatch.zig:27-172
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/channel_cuda.h"
+#include "common.cuh"
+#include "kernels.cuh"
+
+using namespace ch;
+
+// ---------------------------------------------------------------------------
+// error plumbing
+static thread_local std::string g_err;
+static int fail(int code, const std::string &msg) {
+  g_err = msg;
+  return code;
+}
+#define CH_CUDA(call)                                                                          \
+  do {                                                                                         \
+    cudaError_t _e = (call);                                                                   \
+    if (_e != cudaSuccess)                                                                     \
+      return fail(CH_ECUDA, std::string(#call) + ": " + cudaGetErrorString(_e) + " @" + \
+                                std::to_string(__LINE__));                                     \
+  } while (0)
+
+extern "C" const char *ch_last_error(void) { return g_err.c_str(); }
+extern "C" int ch_api_version(void) { return CH_API_VERSION; }
+
+// ---------------------------------------------------------------------------
+// context
+struct ch_ctx {
+  int device = 0;
+  cudaStream_t stream = nullptr;
+  uint32_t *err = nullptr;  // device status word
+  // op-level scratch (lazily sized)
+  float *gemv_partial = nullptr;
+  uint32_t *gemv_counters = nullptr;
+  size_t gemv_counters_n = 0;
+  float *attn_partial = nullptr;
+  size_t attn_partial_n = 0;
+  uint32_t *attn_counters = nullptr;
+  size_t attn_counters_n = 0;
+  uint64_t *topk_cand = nullptr;
+  uint32_t *topk_counter = nullptr;
+  float *attn_inv_freq = nullptr;
+  size_t attn_inv_freq_n = 0;
+  StepParams *op_sp = nullptr;
+};
+
+static int ctx_ensure_gemv(ch_ctx *c, uint32_t row_tiles) {
+  if (!c->gemv_partial) CH_CUDA(cudaMalloc(&c->gemv_partial, gemv_partial_floats(gemv_default_grid()) * sizeof(float)));
+  if (c->gemv_counters_n < row_tiles) {
+    if (c->gemv_counters) CH_CUDA(cudaFree(c->gemv_counters));
+    c->gemv_counters_n = row_tiles;
+    CH_CUDA(cudaMalloc(&c->gemv_counters, row_tiles * sizeof(uint32_t)));
+    CH_CUDA(cudaMemsetAsync(c->gemv_counters, 0, row_tiles * sizeof(uint32_t), c->stream));
+  }
+  return CH_OK;
+}
+
+extern "C" int ch_ctx_create(int device, ch_ctx **out) {
+  if (!out) return fail(CH_EINVAL, "out is NULL");
+  int n = 0;
+  CH_CUDA(cudaGetDeviceCount(&n));
+  if (device < 0 || device >= n) return fail(CH_EINVAL, "device index out of range");
+  CH_CUDA(cudaSetDevice(device));
+  ch_ctx *c = new ch_ctx();
+  c->device = device;
+  CH_CUDA(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking));
+  CH_CUDA(cudaMalloc(&c->err, sizeof(uint32_t)));
+  CH_CUDA(cudaMemsetAsync(c->err, 0, sizeof(uint32_t), c->stream));
+  CH_CUDA(cudaMalloc(&c->topk_cand, (size_t)8192 * sizeof(uint64_t)));
+  CH_CUDA(cudaMalloc(&c->topk_counter, sizeof(uint32_t)));
+  CH_CUDA(cudaMemsetAsync(c->topk_counter, 0, sizeof(uint32_t), c->stream));
+  CH_CUDA(cudaMalloc(&c->op_sp, sizeof(StepParams)));
+  CH_CUDA(cudaStreamSynchronize(c->stream));
+  *out = c;
+  return CH_OK;
+}
+extern "C" void ch_ctx_destroy(ch_ctx *c) {
+  if (!c) return;
+  cudaSetDevice(c->device);
+  cudaStreamSynchronize(c->stream);
+  cudaFree(c->err);
+  cudaFree(c->gemv_partial);
+  cudaFree(c->gemv_counters);
+  cudaFree(c->attn_partial);
+  cudaFree(c->attn_counters);
+  cudaFree(c->topk_cand);
+  cudaFree(c->topk_counter);
+  cudaFree(c->attn_inv_freq);
+  cudaFree(c->op_sp);
+  cudaStreamDestroy(c->stream);
+  delete c;
+}
+extern "C" int ch_ctx_synchronize(ch_ctx *c) {
+  if (!c) return fail(CH_EINVAL, "ctx is NULL");
+  CH_CUDA(cudaStreamSynchronize(c->stream));
+  return CH_OK;
+}
+extern "C" void *ch_ctx_stream(ch_ctx *c) { return c ? (void *)c->stream : nullptr; }
+extern "C" int ch_ctx_device_status(ch_ctx *c, uint32_t *flags) {
+  if (!c || !flags) return fail(CH_EINVAL, "NULL argument");
+  CH_CUDA(cudaMemcpyAsync(flags, c->err, sizeof(uint32_t), cudaMemcpyDeviceToHost, c->stream));
+  CH_CUDA(cudaMemsetAsync(c->err, 0, sizeof(uint32_t), c->stream));
+  CH_CUDA(cudaStreamSynchronize(c->stream));
+  return CH_OK;
+}
+static int status_from_flags(uint32_t f) {
+  if (f & (DEV_ERR_TMA_TIMEOUT | DEV_ERR_PEER_TIMEOUT)) return fail(CH_ETIMEOUT, "a bounded device wait gave up");
+  if (f & (DEV_ERR_BAD_SLOT | DEV_ERR_BAD_LIST)) return fail(CH_EDEVICE, "kernel saw a slot index >= 4096");
+  return CH_OK;
+}
+
+// ---------------------------------------------------------------------------
+// model
+namespace {
+struct DevLayer {
+  uint8_t *qkv = nullptr, *o = nullptr, *gateup = nullptr, *down = nullptr;
+  float *input_norm = nullptr, *q_norm = nullptr, *k_norm = nullptr, *post_attn = nullptr, *pre_ffn = nullptr,
+        *post_ffn = nullptr;
+  float scalar = 1.0f;
+  __half *kc = nullptr, *vc = nullptr;
+  bool full = false;
+};
+constexpr uint32_t kSlots = 4096;
+}  // namespace
+
+struct ch_model {
+  ch_ctx *ctx = nullptr;
+  ch_model_config cfg{};
+  uint32_t H = 0, I = 0, V = 0, D = 0, nq = 0, nkv = 0, qd = 0, kvd = 0, L = 0;
+  std::vector<DevLayer> layers;
+  uint8_t *lm = nullptr;
+  float *final_norm = nullptr;
+  uint16_t *embed = nullptr;
+  float *inv_freq_s = nullptr, *inv_freq_f = nullptr;
+  // decode buffers
+  float *X[2] = {nullptr, nullptr};
+  float *normed = nullptr, *qkv = nullptr, *attn = nullptr, *o_out = nullptr, *act = nullptr, *down_out = nullptr,
+        *logits = nullptr, *vals = nullptr;
+  uint32_t *ids = nullptr, *token = nullptr, *token_hist = nullptr;
+  StepParams *sp = nullptr;
+  uint32_t *active = nullptr, *sliding = nullptr;
+  // scratch
+  float *gemv_partial = nullptr;
+  uint32_t *gemv_counters = nullptr;
+  float *attn_partial = nullptr;
+  uint32_t *attn_counters = nullptr;
+  uint64_t *topk_cand = nullptr;
+  uint32_t *topk_counter = nullptr;
+  int attn_splits = 0;
+  // host staging (pinned)
+  float *h_x = nullptr;
+  StepParams *h_sp = nullptr;
+  uint32_t *h_lists = nullptr;  // [2][4096]
+  uint32_t *h_ids = nullptr;
+  float *h_vals = nullptr;
+  uint32_t *h_run = nullptr;  // [2] staging for ch_decode_run
+  // graphs
+  cudaGraphExec_t g_host_logits = nullptr, g_host_nologits = nullptr, g_loop = nullptr;
+  bool pdl = true;
+  // device loop plan
+  StepParams *plan = nullptr;
+  uint32_t *plan_lists = nullptr;
+  uint32_t plan_steps = 0, hist_cap = 0, loop_pos = 0;
+  // prefill buffers
+  uint32_t pf_cap = 0;
+  float *pX = nullptr, *pNX = nullptr, *pQKV = nullptr, *pQO = nullptr, *pA = nullptr, *pMO = nullptr, *pACT = nullptr;
+  uint32_t *pSlots = nullptr, *pTok = nullptr;
+};
+
+static void free_model(ch_model *m) {
+  if (!m) return;
+  cudaSetDevice(m->ctx->device);
+  cudaStreamSynchronize(m->ctx->stream);
+  for (auto &l : m->layers) {
+    cudaFree(l.qkv);
+    cudaFree(l.o);
+    cudaFree(l.gateup);
+    cudaFree(l.down);
+    cudaFree(l.input_norm);
+    cudaFree(l.q_norm);
+    cudaFree(l.k_norm);
+    cudaFree(l.post_attn);
+    cudaFree(l.pre_ffn);
+    cudaFree(l.post_ffn);
+    cudaFree(l.kc);
+    cudaFree(l.vc);
+  }
+  void *dev[] = {m->lm, m->final_norm, m->embed, m->inv_freq_s, m->inv_freq_f, m->X[0], m->X[1], m->normed, m->qkv,
+                 m->attn, m->o_out, m->act, m->down_out, m->logits, m->vals, m->ids, m->token, m->token_hist, m->sp,
+                 m->active, m->sliding, m->gemv_partial, m->gemv_counters, m->attn_partial, m->attn_counters,
+                 m->topk_cand, m->topk_counter, m->plan, m->plan_lists, m->pX, m->pNX, m->pQKV, m->pQO, m->pA, m->pMO,
+                 m->pACT, m->pSlots, m->pTok};
+  for (void *p : dev) cudaFree(p);
+  void *host[] = {m->h_x, m->h_sp, m->h_lists, m->h_ids, m->h_vals, m->h_run};
+  for (void *p : host) cudaFreeHost(p);
+  if (m->g_host_logits) cudaGraphExecDestroy(m->g_host_logits);
+  if (m->g_host_nologits) cudaGraphExecDestroy(m->g_host_nologits);
+  if (m->g_loop) cudaGraphExecDestroy(m->g_loop);
+  delete m;
+}
+
+static int check_cfg(const ch_model_config *c) {
+  if (!c) return fail(CH_EINVAL, "cfg is NULL");
+  if (c->num_hidden_layers == 0 || c->num_hidden_layers > 64) return fail(CH_EINVAL, "num_hidden_layers must be 1..64");
+  if (c->head_dim != 256) return fail(CH_EINVAL, "head_dim must be 256");
+  if (c->rotary_dim == 0 || c->rotary_dim > c->head_dim || (c->rotary_dim & 1))
+    return fail(CH_EINVAL, "rotary_dim must be even and <= head_dim");
+  if (c->num_key_value_heads == 0 || c->num_attention_heads % c->num_key_value_heads)
+    return fail(CH_EINVAL, "num_attention_heads must be a multiple of num_key_value_heads");
+  uint32_t r = c->num_attention_heads / c->num_key_value_heads;
+  if (r != 1 && r != 2 && r != 4 && r != 8) return fail(CH_EINVAL, "GQA ratio must be 1, 2, 4 or 8");
+  if (c->hidden_size % 64 || c->intermediate_size % 64) return fail(CH_EINVAL, "hidden/intermediate must be % 64");
+  if (c->vocab_size % 16 || c->vocab_size > 262144) return fail(CH_EINVAL, "vocab must be % 16 and <= 262144");
+  if (c->hidden_size % 32) return fail(CH_EINVAL, "hidden % 32");
+  return CH_OK;
+}
+
+template <typename T>
+static int dmalloc(T **p, size_t n) {
+  cudaError_t e = cudaMalloc((void **)p, n * sizeof(T) > 0 ? n * sizeof(T) : 16);
+  if (e != cudaSuccess) return fail(CH_ENOMEM, std::string("cudaMalloc: ") + cudaGetErrorString(e));
+  return CH_OK;
+}
+#define CH_TRY(x)          \
+  do {                     \
+    int _r = (x);          \
+    if (_r != CH_OK) return _r; \
+  } while (0)
+
+static int alloc_model_buffers(ch_model *m) {
+  const ch_model_config &c = m->cfg;
+  m->H = c.hidden_size;
+  m->I = c.intermediate_size;
+  m->V = c.vocab_size;
+  m->D = c.head_dim;
+  m->nq = c.num_attention_heads;
+  m->nkv = c.num_key_value_heads;
+  m->qd = m->nq * m->D;
+  m->kvd = m->nkv * m->D;
+  m->L = c.num_hidden_layers;
+  m->layers.resize(m->L);
+  for (uint32_t l = 0; l < m->L; l++) {
+    DevLayer &dl = m->layers[l];
+    dl.full = c.layer_types[l] != 0;
+    CH_TRY(dmalloc(&dl.qkv, q4_tile_bytes(m->qd + 2 * m->kvd, m->H)));
+    CH_TRY(dmalloc(&dl.o, q4_tile_bytes(m->H, m->qd)));
+    CH_TRY(dmalloc(&dl.gateup, q4_tile_bytes(2 * m->I, m->H)));
+    CH_TRY(dmalloc(&dl.down, q4_tile_bytes(m->H, m->I)));
+    CH_TRY(dmalloc(&dl.input_norm, m->H));
+    CH_TRY(dmalloc(&dl.q_norm, m->D));
+    CH_TRY(dmalloc(&dl.k_norm, m->D));
+    CH_TRY(dmalloc(&dl.pre_ffn, m->H));
+    CH_TRY(dmalloc(&dl.kc, (size_t)kSlots * m->kvd));
+    CH_TRY(dmalloc(&dl.vc, (size_t)kSlots * m->kvd));
+    CH_CUDA(cudaMemsetAsync(dl.kc, 0, (size_t)kSlots * m->kvd * 2, m->ctx->stream));
+    CH_CUDA(cudaMemsetAsync(dl.vc, 0, (size_t)kSlots * m->kvd * 2, m->ctx->stream));
+  }
+  CH_TRY(dmalloc(&m->lm, q8_tile_bytes(m->V, m->H)));
+  CH_TRY(dmalloc(&m->final_norm, m->H));
+  CH_TRY(dmalloc(&m->inv_freq_s, c.rotary_dim / 2));
+  CH_TRY(dmalloc(&m->inv_freq_f, c.rotary_dim / 2));
+  CH_TRY(dmalloc(&m->X[0], m->H));
+  CH_TRY(dmalloc(&m->X[1], m->H));
+  CH_TRY(dmalloc(&m->normed, m->H));
+  CH_TRY(dmalloc(&m->qkv, m->qd + 2 * m->kvd));
+  CH_TRY(dmalloc(&m->attn, m->qd));
+  CH_TRY(dmalloc(&m->o_out, m->H));
+  CH_TRY(dmalloc(&m->act, m->I));
+  CH_TRY(dmalloc(&m->down_out, m->H));
+  CH_TRY(dmalloc(&m->logits, m->V));
+  CH_TRY(dmalloc(&m->vals, 64));
+  CH_TRY(dmalloc(&m->ids, 64));
+  CH_TRY(dmalloc(&m->token, 1));
+  CH_TRY(dmalloc(&m->sp, 1));
+  CH_TRY(dmalloc(&m->active, kSlots));
+  CH_TRY(dmalloc(&m->sliding, kSlots));
+  CH_CUDA(cudaMemsetAsync(m->X[0], 0, m->H * 4, m->ctx->stream));
+  CH_CUDA(cudaMemsetAsync(m->X[1], 0, m->H * 4, m->ctx->stream));
+  CH_CUDA(cudaMemsetAsync(m->sp, 0, sizeof(StepParams), m->ctx->stream));
+  CH_CUDA(cudaMemsetAsync(m->token, 0, 4, m->ctx->stream));
+  // scratch
+  const int grid = gemv_default_grid();
+  CH_TRY(dmalloc(&m->gemv_partial, gemv_partial_floats(grid)));
+  const uint32_t max_rt = std::max({(m->qd + 2 * m->kvd) / 16, m->H / 16, 2 * m->I / 16, m->V / 16});
+  CH_TRY(dmalloc(&m->gemv_counters, max_rt));
+  CH_CUDA(cudaMemsetAsync(m->gemv_counters, 0, max_rt * 4, m->ctx->stream));
+  m->attn_splits = attn_default_splits(m->nkv);
+  CH_TRY(dmalloc(&m->attn_partial, attn_partial_floats(m->nkv, m->nq / m->nkv, m->D, m->attn_splits)));
+  CH_TRY(dmalloc(&m->attn_counters, m->nkv));
+  CH_CUDA(cudaMemsetAsync(m->attn_counters, 0, m->nkv * 4, m->ctx->stream));
+  CH_TRY(dmalloc(&m->topk_cand, (size_t)topk_blocks(m->V) * 64));
+  CH_TRY(dmalloc(&m->topk_counter, 1));
+  CH_CUDA(cudaMemsetAsync(m->topk_counter, 0, 4, m->ctx->stream));
+  // pinned staging
+  CH_CUDA(cudaMallocHost(&m->h_x, m->H * sizeof(float)));
+  CH_CUDA(cudaMallocHost(&m->h_sp, sizeof(StepParams)));
+  CH_CUDA(cudaMallocHost(&m->h_lists, 2 * kSlots * sizeof(uint32_t)));
+  CH_CUDA(cudaMallocHost(&m->h_ids, 64 * sizeof(uint32_t)));
+  CH_CUDA(cudaMallocHost(&m->h_vals, 64 * sizeof(float)));
+  CH_CUDA(cudaMallocHost(&m->h_run, 2 * sizeof(uint32_t)));
+  // RoPE inverse frequencies: same formula as the oracle (double pow, one rounding)
+  std::vector<float> fs(c.rotary_dim / 2), ff(c.rotary_dim / 2);
+  for (uint32_t i = 0; i < c.rotary_dim / 2; i++) {
+    float e = (2.0f * (float)i) / (float)c.rotary_dim;
+    fs[i] = (float)(1.0 / pow((double)c.rope_theta, (double)e));
+    ff[i] = (float)(1.0 / pow((double)c.rope_theta_full, (double)e));
+  }
+  CH_CUDA(cudaMemcpy(m->inv_freq_s, fs.data(), fs.size() * 4, cudaMemcpyHostToDevice));
+  CH_CUDA(cudaMemcpy(m->inv_freq_f, ff.data(), ff.size() * 4, cudaMemcpyHostToDevice));
+  return CH_OK;
+}
+
+// upload quant.zig Q4 blocks of one matrix into a temp device buffer
+static int upload_blocks(ch_model *m, const uint32_t *host, uint32_t rows, uint32_t cols, uint32_t *tmp) {
+  if (!host) return fail(CH_EINVAL, "NULL weight pointer");
+  CH_CUDA(cudaMemcpyAsync(tmp, host, (size_t)rows * (cols / 32) * 5 * 4, cudaMemcpyHostToDevice, m->ctx->stream));
+  return CH_OK;
+}
+
+extern "C" int ch_model_create(ch_ctx *ctx, const ch_model_config *cfg, const ch_layer_weights *lw,
+                               const uint32_t *lm_head_q8, const float *final_norm, const uint16_t *embed_bf16,
+                               ch_model **out) {
+  if (!ctx || !out || !lw || !lm_head_q8 || !final_norm) return fail(CH_EINVAL, "NULL argument");
+  CH_TRY(check_cfg(cfg));
+  CH_CUDA(cudaSetDevice(ctx->device));
+  ch_model *m = new ch_model();
+  m->ctx = ctx;
+  m->cfg = *cfg;
+  int r = alloc_model_buffers(m);
+  if (r != CH_OK) {
+    free_model(m);
+    return r;
+  }
+  cudaStream_t s = ctx->stream;
+  // temp block buffers sized for the largest matrix
+  size_t max_words = std::max({(size_t)(m->qd + 2 * m->kvd) * (m->H / 32) * 5, (size_t)m->H * (m->qd / 32) * 5,
+                               (size_t)m->I * (m->H / 32) * 5, (size_t)m->H * (m->I / 32) * 5});
+  uint32_t *tA = nullptr, *tB = nullptr;
+  auto bail = [&](int code) {
+    cudaFree(tA);
+    cudaFree(tB);
+    free_model(m);
+    return code;
+  };
+  if (dmalloc(&tA, max_words) != CH_OK || dmalloc(&tB, max_words) != CH_OK) return bail(CH_ENOMEM);
+  const size_t qw = (size_t)m->qd * (m->H / 32) * 5, kw = (size_t)m->kvd * (m->H / 32) * 5;
+  for (uint32_t l = 0; l < m->L; l++) {
+    const ch_layer_weights &w = lw[l];
+    DevLayer &dl = m->layers[l];
+    if (!w.q_proj || !w.k_proj || !w.v_proj || !w.o_proj || !w.gate_proj || !w.up_proj || !w.down_proj ||
+        !w.input_norm || !w.q_norm || !w.k_norm || !w.pre_ffn_norm)
+      return bail(fail(CH_EINVAL, "layer " + std::to_string(l) + ": NULL weight"));
+    // q|k|v concatenated rows
+    if (upload_blocks(m, w.q_proj, m->qd, m->H, tA) || upload_blocks(m, w.k_proj, m->kvd, m->H, tA + qw) ||
+        upload_blocks(m, w.v_proj, m->kvd, m->H, tA + qw + kw))
+      return bail(CH_ECUDA);
+    if (launch_repack_q4(tA, nullptr, m->qd + 2 * m->kvd, m->H, MAP_PLAIN, dl.qkv, s) != cudaSuccess)
+      return bail(fail(CH_ECUDA, "repack qkv"));
+    if (upload_blocks(m, w.o_proj, m->H, m->qd, tB)) return bail(CH_ECUDA);
+    if (launch_repack_q4(tB, nullptr, m->H, m->qd, MAP_PLAIN, dl.o, s) != cudaSuccess)
+      return bail(fail(CH_ECUDA, "repack o"));
+    cudaStreamSynchronize(s);
+    if (upload_blocks(m, w.gate_proj, m->I, m->H, tA) || upload_blocks(m, w.up_proj, m->I, m->H, tB))
+      return bail(CH_ECUDA);
+    if (launch_repack_q4(tA, tB, 2 * m->I, m->H, MAP_GATEUP, dl.gateup, s) != cudaSuccess)
+      return bail(fail(CH_ECUDA, "repack gate/up"));
+    cudaStreamSynchronize(s);
+    if (upload_blocks(m, w.down_proj, m->H, m->I, tA)) return bail(CH_ECUDA);
+    if (launch_repack_q4(tA, nullptr, m->H, m->I, MAP_PLAIN, dl.down, s) != cudaSuccess)
+      return bail(fail(CH_ECUDA, "repack down"));
+    auto up = [&](float **dst, const float *src, uint32_t n, bool optional) -> int {
+      if (!src) {
+        if (optional) return CH_OK;
+        return fail(CH_EINVAL, "NULL norm");
+      }
+      if (!*dst && dmalloc(dst, n) != CH_OK) return CH_ENOMEM;
+      CH_CUDA(cudaMemcpyAsync(*dst, src, n * 4, cudaMemcpyHostToDevice, s));
+      return CH_OK;
+    };
+    if (up(&dl.input_norm, w.input_norm, m->H, false) || up(&dl.q_norm, w.q_norm, m->D, false) ||
+        up(&dl.k_norm, w.k_norm, m->D, false) || up(&dl.pre_ffn, w.pre_ffn_norm, m->H, false) ||
+        up(&dl.post_attn, w.post_attn_norm, m->H, true) || up(&dl.post_ffn, w.post_ffn_norm, m->H, true))
+      return bail(CH_ECUDA);
+    dl.scalar = w.layer_scalar;
+    cudaStreamSynchronize(s);
+  }
+  cudaFree(tA);
+  cudaFree(tB);
+  tA = tB = nullptr;
+  // LM head Q8_0 blocks: upload in row chunks, repack per chunk
+  {
+    const uint32_t chunk_rows = 16384;
+    uint32_t *tq = nullptr;
+    if (dmalloc(&tq, (size_t)chunk_rows * (m->H / 32) * 9) != CH_OK) return bail(CH_ENOMEM);
+    for (uint32_t r0 = 0; r0 < m->V; r0 += chunk_rows) {
+      uint32_t nr = std::min(chunk_rows, m->V - r0);
+      cudaMemcpyAsync(tq, lm_head_q8 + (size_t)r0 * (m->H / 32) * 9, (size_t)nr * (m->H / 32) * 9 * 4,
+                      cudaMemcpyHostToDevice, s);
+      launch_repack_q8(tq, nr, m->H, m->lm + q8_tile_bytes(r0, m->H), s);
+      cudaStreamSynchronize(s);
+    }
+    cudaFree(tq);
+  }
+  if (cudaMemcpyAsync(m->final_norm, final_norm, m->H * 4, cudaMemcpyHostToDevice, s) != cudaSuccess)
+    return bail(fail(CH_ECUDA, "final norm upload"));
+  if (embed_bf16) {
+    if (dmalloc(&m->embed, (size_t)m->V * m->H) != CH_OK) return bail(CH_ENOMEM);
+    if (cudaMemcpyAsync(m->embed, embed_bf16, (size_t)m->V * m->H * 2, cudaMemcpyHostToDevice, s) != cudaSuccess)
+      return bail(fail(CH_ECUDA, "embed upload"));
+  }
+  cudaError_t e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess) return bail(fail(CH_ECUDA, std::string("model upload: ") + cudaGetErrorString(e)));
+  *out = m;
+  return CH_OK;
+}
+
+// tensor ids of the synthetic generator (shared with tests/ and the oracle driver)
+enum : uint32_t {
+  T_Q = 0, T_K = 1, T_V = 2, T_O = 3, T_GATE = 4, T_UP = 5, T_DOWN = 6,
+  T_IN_NORM = 10, T_Q_NORM = 11, T_K_NORM = 12, T_POST_ATTN = 13, T_PRE_FFN = 14, T_POST_FFN = 15,
+  T_EMBED = 20, T_FINAL_NORM = 21,
+};
+
+static uint64_t host_mix64(uint64_t z) {
+  z += 0x9E3779B97F4A7C15ull;
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  return z ^ (z >> 31);
+}
+extern "C" uint64_t ch_tensor_seed(uint64_t seed, uint32_t layer, uint32_t tensor_id) {
+  return host_mix64(host_mix64(seed) ^ (((uint64_t)layer << 16) | tensor_id));
+}
+
+static int gen_norm(ch_model *m, float **dst, uint32_t n, uint64_t tseed, uint16_t *tmp) {
+  if (!*dst) CH_TRY(dmalloc(dst, n));
+  if (launch_gen_bf16(tmp, n, tseed, 1.0f, 0.02f, m->ctx->stream) != cudaSuccess) return fail(CH_ECUDA, "gen norm");
+  if (launch_bf16_to_f32(tmp, *dst, n, m->ctx->stream) != cudaSuccess) return fail(CH_ECUDA, "norm convert");
+  return CH_OK;
+}
+
+extern "C" int ch_model_create_synthetic(ch_ctx *ctx, const ch_model_config *cfg, uint64_t seed, ch_model **out) {
+  if (!ctx || !out) return fail(CH_EINVAL, "NULL argument");
+  CH_TRY(check_cfg(cfg));
+  CH_CUDA(cudaSetDevice(ctx->device));
+  ch_model *m = new ch_model();
+  m->ctx = ctx;
+  m->cfg = *cfg;
+  int r = alloc_model_buffers(m);
+  if (r != CH_OK) {
+    free_model(m);
+    return r;
+  }
+  cudaStream_t s = ctx->stream;
+  size_t max_words = std::max({(size_t)(m->qd + 2 * m->kvd) * (m->H / 32) * 5, (size_t)m->H * (m->qd / 32) * 5,
+                               (size_t)m->I * (m->H / 32) * 5, (size_t)m->H * (m->I / 32) * 5});
+  uint32_t *tA = nullptr, *tB = nullptr;
+  uint16_t *tn = nullptr;
+  auto bail = [&](int code) {
+    cudaFree(tA);
+    cudaFree(tB);
+    cudaFree(tn);
+    free_model(m);
+    return code;
+  };
+  if (dmalloc(&tA, max_words) != CH_OK || dmalloc(&tB, max_words) != CH_OK || dmalloc(&tn, std::max(m->H, m->D)) != CH_OK)
+    return bail(CH_ENOMEM);
+  const float wstd = 0.02f;
+  const size_t qw = (size_t)m->qd * (m->H / 32) * 5, kw = (size_t)m->kvd * (m->H / 32) * 5;
+  for (uint32_t l = 0; l < m->L; l++) {
+    DevLayer &dl = m->layers[l];
+    bool ok = launch_gen_q4_blocks(tA, m->qd, m->H, ch_tensor_seed(seed, l, T_Q), wstd, s) == cudaSuccess &&
+              launch_gen_q4_blocks(tA + qw, m->kvd, m->H, ch_tensor_seed(seed, l, T_K), wstd, s) == cudaSuccess &&
+              launch_gen_q4_blocks(tA + qw + kw, m->kvd, m->H, ch_tensor_seed(seed, l, T_V), wstd, s) == cudaSuccess &&
+              launch_repack_q4(tA, nullptr, m->qd + 2 * m->kvd, m->H, MAP_PLAIN, dl.qkv, s) == cudaSuccess &&
+              launch_gen_q4_blocks(tB, m->H, m->qd, ch_tensor_seed(seed, l, T_O), wstd, s) == cudaSuccess &&
+              launch_repack_q4(tB, nullptr, m->H, m->qd, MAP_PLAIN, dl.o, s) == cudaSuccess &&
+              launch_gen_q4_blocks(tA, m->I, m->H, ch_tensor_seed(seed, l, T_GATE), wstd, s) == cudaSuccess &&
+              launch_gen_q4_blocks(tB, m->I, m->H, ch_tensor_seed(seed, l, T_UP), wstd, s) == cudaSuccess &&
+              launch_repack_q4(tA, tB, 2 * m->I, m->H, MAP_GATEUP, dl.gateup, s) == cudaSuccess &&
+              launch_gen_q4_blocks(tA, m->H, m->I, ch_tensor_seed(seed, l, T_DOWN), wstd, s) == cudaSuccess &&
+              launch_repack_q4(tA, nullptr, m->H, m->I, MAP_PLAIN, dl.down, s) == cudaSuccess;
+    if (!ok) return bail(fail(CH_ECUDA, "synthetic layer generation"));
+    if (gen_norm(m, &dl.input_norm, m->H, ch_tensor_seed(seed, l, T_IN_NORM), tn) ||
+        gen_norm(m, &dl.q_norm, m->D, ch_tensor_seed(seed, l, T_Q_NORM), tn) ||
+        gen_norm(m, &dl.k_norm, m->D, ch_tensor_seed(seed, l, T_K_NORM), tn) ||
+        gen_norm(m, &dl.post_attn, m->H, ch_tensor_seed(seed, l, T_POST_ATTN), tn) ||
+        gen_norm(m, &dl.pre_ffn, m->H, ch_tensor_seed(seed, l, T_PRE_FFN), tn) ||
+        gen_norm(m, &dl.post_ffn, m->H, ch_tensor_seed(seed, l, T_POST_FFN), tn))
+      return bail(CH_ECUDA);
+    dl.scalar = 1.0f;
+  }
+  if (gen_norm(m, &m->final_norm, m->H, ch_tensor_seed(seed, 0, T_FINAL_NORM), tn)) return bail(CH_ECUDA);
+  cudaFree(tA);
+  cudaFree(tB);
+  tA = tB = nullptr;
+  // tied embedding bf16 N(0, 0.02), LM head = quantizeRowQ8_0 of it
+  if (dmalloc(&m->embed, (size_t)m->V * m->H) != CH_OK) return bail(CH_ENOMEM);
+  if (launch_gen_bf16(m->embed, (size_t)m->V * m->H, ch_tensor_seed(seed, 0, T_EMBED), 0.0f, 0.02f, s) != cudaSuccess)
+    return bail(fail(CH_ECUDA, "gen embed"));
+  {
+    const uint32_t chunk_rows = 16384;
+    uint32_t *tq = nullptr;
+    if (dmalloc(&tq, (size_t)chunk_rows * (m->H / 32) * 9) != CH_OK) return bail(CH_ENOMEM);
+    for (uint32_t r0 = 0; r0 < m->V; r0 += chunk_rows) {
+      uint32_t nr = std::min(chunk_rows, m->V - r0);
+      launch_quantize_q8_rows(m->embed + (size_t)r0 * m->H, nr, m->H, tq, s);
+      launch_repack_q8(tq, nr, m->H, m->lm + q8_tile_bytes(r0, m->H), s);
+    }
+    cudaStreamSynchronize(s);
+    cudaFree(tq);
+  }
+  cudaError_t e = cudaStreamSynchronize(s);
+  cudaFree(tn);
+  tn = nullptr;
+  if (e != cudaSuccess) return bail(fail(CH_ECUDA, std::string("synthetic model: ") + cudaGetErrorString(e)));
+  *out = m;
+  return CH_OK;
+}
+
+extern "C" void ch_model_destroy(ch_model *m) { free_model(m); }
+
+extern "C" int ch_model_weight_tiles(ch_model *m, uint32_t layer, int which, void **tiles, uint32_t *rows,
+                                     uint32_t *cols) {
+  if (!m || !tiles || !rows || !cols || layer >= m->L) return fail(CH_EINVAL, "bad argument");
+  const DevLayer &l = m->layers[layer];
+  switch (which) {
+    case 0: *tiles = l.qkv, *rows = m->qd + 2 * m->kvd, *cols = m->H; break;
+    case 1: *tiles = l.o, *rows = m->H, *cols = m->qd; break;
+    case 2: *tiles = l.gateup, *rows = 2 * m->I, *cols = m->H; break;
+    case 3: *tiles = l.down, *rows = m->H, *cols = m->I; break;
+    case 4: *tiles = m->lm, *rows = m->V, *cols = m->H; break;
+    default: return fail(CH_EINVAL, "which must be 0..4");
+  }
+  return CH_OK;
+}
+
+extern "C" int ch_model_zero_state(ch_model *m) {
+  if (!m) return fail(CH_EINVAL, "model is NULL");
+  cudaStream_t s = m->ctx->stream;
+  for (auto &l : m->layers) {
+    CH_CUDA(cudaMemsetAsync(l.kc, 0, (size_t)kSlots * m->kvd * 2, s));
+    CH_CUDA(cudaMemsetAsync(l.vc, 0, (size_t)kSlots * m->kvd * 2, s));
+  }
+  CH_CUDA(cudaMemsetAsync(m->X[0], 0, m->H * 4, s));
+  CH_CUDA(cudaMemsetAsync(m->X[1], 0, m->H * 4, s));
+  CH_CUDA(cudaMemsetAsync(m->normed, 0, m->H * 4, s));
+  CH_CUDA(cudaStreamSynchronize(s));
+  return CH_OK;
+}
+
+// ---------------------------------------------------------------------------
+// the decode step (model_dispatch.zig:226-342 order; norms fused into GEMV prologues)
+static cudaError_t enqueue_decode(ch_model *m, cudaStream_t s, bool logits, bool device_loop) {
+  cudaError_t e;
+  const bool pdl = m->pdl;
+  GemvArgs base;
+  base.partial = m->gemv_partial;
+  base.counters = m->gemv_counters;
+  base.err = m->ctx->err;
+  base.eps = m->cfg.rms_norm_eps;
+  if (device_loop) {
+    StepBeginArgs sb{m->embed, m->H, sqrtf((float)m->H), m->token, m->X[0], m->sp, m->plan, m->plan_steps,
+                     m->ctx->err};
+    if ((e = launch_step_begin(sb, s, pdl)) != cudaSuccess) return e;
+  }
+  for (uint32_t l = 0; l < m->L; l++) {
+    DevLayer &dl = m->layers[l];
+    // q|k|v projections; prologue = layer-0 input norm, or the previous layer's
+    // post-FFN norm + residual add + this layer's input norm (model_gpu.zig:160-163)
+    {
+      GemvArgs a = base;
+      GemvPlan p;
+      a.tiles = dl.qkv;
+      a.row_tiles = (m->qd + 2 * m->kvd) / 16;
+      a.k_tiles = m->H / 64;
+      a.K = m->H;
+      a.norm_w = dl.input_norm;
+      a.normed_out = m->normed;
+      a.y = m->qkv;
+      if (l == 0) {
+        p.pro = PRO_RMSNORM;
+        a.x = m->X[0];
+      } else {
+        const DevLayer &pl = m->layers[l - 1];
+        p.pro = PRO_ADD_RMSNORM;
+        a.x = m->X[1];
+        a.r = m->down_out;
+        a.post_w = pl.post_ffn;
+        a.scalar = pl.scalar;
+        a.x_out = m->X[0];
+      }
+      if ((e = launch_gemv(p, a, s, pdl)) != cudaSuccess) return e;
+    }
+    {
+      AttnArgs a{};
+      a.qkv = m->qkv;
+      a.q_norm_w = dl.q_norm;
+      a.k_norm_w = dl.k_norm;
+      a.inv_freq = dl.full ? m->inv_freq_f : m->inv_freq_s;
+      a.k_cache = dl.kc;
+      a.v_cache = dl.vc;
+      a.sp = m->sp;
+      a.is_sliding = dl.full ? 0 : 1;
+      a.nq = m->nq;
+      a.nkv = m->nkv;
+      a.D = m->D;
+      a.rot = m->cfg.rotary_dim;
+      a.eps = m->cfg.rms_norm_eps;
+      a.scale = 1.0f;  // Gemma-style: q/k norms replace 1/sqrt(d) (forward.zig:85)
+      a.out = m->attn;
+      a.partial = m->attn_partial;
+      a.counters = m->attn_counters;
+      a.err = m->ctx->err;
+      a.cache_slots = kSlots;
+      if ((e = launch_decode_attn(a, m->attn_splits, s, pdl)) != cudaSuccess) return e;
+    }
+    {
+      GemvArgs a = base;
+      GemvPlan p;
+      a.tiles = dl.o;
+      a.row_tiles = m->H / 16;
+      a.k_tiles = m->qd / 64;
+      a.K = m->qd;
+      a.x = m->attn;
+      a.y = m->o_out;
+      if ((e = launch_gemv(p, a, s, pdl)) != cudaSuccess) return e;
+    }
+    {
+      GemvArgs a = base;
+      GemvPlan p;
+      p.epi = EPI_GELU_MUL;
+      p.pro = PRO_ADD_RMSNORM;
+      a.tiles = dl.gateup;
+      a.row_tiles = 2 * m->I / 16;
+      a.k_tiles = m->H / 64;
+      a.K = m->H;
+      a.x = m->X[0];
+      a.r = m->o_out;
+      a.post_w = dl.post_attn;
+      a.scalar = 1.0f;
+      a.norm_w = dl.pre_ffn;
+      a.x_out = m->X[1];
+      a.normed_out = m->normed;
+      a.y = m->act;
+      if ((e = launch_gemv(p, a, s, pdl)) != cudaSuccess) return e;
+    }
+    {
+      GemvArgs a = base;
+      GemvPlan p;
+      a.tiles = dl.down;
+      a.row_tiles = m->H / 16;
+      a.k_tiles = m->I / 64;
+      a.K = m->I;
+      a.x = m->act;
+      a.y = m->down_out;
+      if ((e = launch_gemv(p, a, s, pdl)) != cudaSuccess) return e;
+    }
+  }
+  const DevLayer &last = m->layers[m->L - 1];
+  if (logits) {
+    GemvArgs a = base;
+    GemvPlan p;
+    p.fmt = FMT_Q8;
+    p.pro = PRO_ADD_RMSNORM;
+    a.tiles = m->lm;
+    a.row_tiles = m->V / 16;
+    a.k_tiles = m->H / 32;
+    a.K = m->H;
+    a.x = m->X[1];
+    a.r = m->down_out;
+    a.post_w = last.post_ffn;
+    a.scalar = last.scalar;
+    a.norm_w = m->final_norm;
+    a.x_out = m->X[0];
+    a.normed_out = m->normed;
+    a.y = m->logits;
+    if ((e = launch_gemv(p, a, s, pdl)) != cudaSuccess) return e;
+    TopkArgs t{};
+    t.logits = m->logits;
+    t.V = m->V;
+    t.cand = m->topk_cand;
+    t.counter = m->topk_counter;
+    t.ids = m->ids;
+    t.vals = m->vals;
+    t.token_out = m->token;
+    t.token_hist = device_loop ? m->token_hist : nullptr;
+    t.hist_cap = m->hist_cap;
+    t.sp = device_loop ? m->sp : nullptr;
+    t.err = m->ctx->err;
+    if ((e = launch_topk64(t, s, pdl)) != cudaSuccess) return e;
+  } else {
+    // no-logits variant: still fold the last residual add so read_x matches the logits path
+    if (last.post_ffn &&
+        (e = launch_rmsnorm_rows(m->down_out, last.post_ffn, m->down_out, 1, m->H, m->cfg.rms_norm_eps, s)) !=
+            cudaSuccess)
+      return e;
+    if ((e = launch_add_rmsnorm_rows(m->X[1], m->down_out, m->final_norm, m->normed, 1, m->H, m->cfg.rms_norm_eps,
+                                     last.scalar, s)) != cudaSuccess)
+      return e;
+    if ((e = cudaMemcpyAsync(m->X[0], m->X[1], m->H * 4, cudaMemcpyDeviceToDevice, s)) != cudaSuccess) return e;
+  }
+  return cudaSuccess;
+}
+
+static int capture(ch_model *m, bool logits, bool device_loop, cudaGraphExec_t *out) {
+  cudaStream_t s = m->ctx->stream;
+  for (int attempt = 0; attempt < 2; attempt++) {
+    cudaGraph_t g = nullptr;
+    CH_CUDA(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
+    cudaError_t e = enqueue_decode(m, s, logits, device_loop);
+    cudaError_t e2 = cudaStreamEndCapture(s, &g);
+    if (e == cudaSuccess && e2 == cudaSuccess) {
+      cudaError_t e3 = cudaGraphInstantiate(out, g, 0);
+      cudaGraphDestroy(g);
+      if (e3 == cudaSuccess) return CH_OK;
+      e = e3;
+    }
+    if (g) cudaGraphDestroy(g);
+    cudaGetLastError();
+    if (!m->pdl) return fail(CH_ECUDA, std::string("graph capture: ") + cudaGetErrorString(e != cudaSuccess ? e : e2));
+    m->pdl = false;  // retry without programmatic dependent launch
+  }
+  return fail(CH_ECUDA, "graph capture failed");
+}
+
+static int check_lists(const uint32_t *l, uint32_t n) {
+  if (n > kSlots) return fail(CH_EINVAL, "slot list longer than 4096");
+  if (n && !l) return fail(CH_EINVAL, "NULL slot list");
+  for (uint32_t i = 0; i < n; i++)
+    if (l[i] >= kSlots) return fail(CH_EINVAL, "slot list entry >= 4096");
+  return CH_OK;
+}
+
+extern "C" int ch_forward_token(ch_model *m, const float *x, uint32_t clock, uint32_t slot, const uint32_t *active,
+                                uint32_t n_active, const uint32_t *sliding, uint32_t n_sliding, ch_topk *topk_out,
+                                uint32_t *token_out) {
+  if (!m || !x) return fail(CH_EINVAL, "NULL argument");
+  if (slot >= kSlots) return fail(CH_EINVAL, "slot >= 4096");
+  CH_TRY(check_lists(active, n_active));
+  CH_TRY(check_lists(sliding, n_sliding));
+  CH_CUDA(cudaSetDevice(m->ctx->device));
+  const bool logits = topk_out || token_out;
+  cudaGraphExec_t *g = logits ? &m->g_host_logits : &m->g_host_nologits;
+  if (!*g) CH_TRY(capture(m, logits, false, g));
+  cudaStream_t s = m->ctx->stream;
+  memcpy(m->h_x, x, m->H * 4);
+  m->h_sp->clock = clock;
+  m->h_sp->slot = slot;
+  m->h_sp->n_active = n_active;
+  m->h_sp->n_sliding = n_sliding;
+  m->h_sp->active = m->active;
+  m->h_sp->sliding = m->sliding;
+  m->h_sp->step = 0;
+  if (n_active) memcpy(m->h_lists, active, n_active * 4);
+  if (n_sliding) memcpy(m->h_lists + kSlots, sliding, n_sliding * 4);
+  CH_CUDA(cudaMemcpyAsync(m->X[0], m->h_x, m->H * 4, cudaMemcpyHostToDevice, s));
+  CH_CUDA(cudaMemcpyAsync(m->sp, m->h_sp, sizeof(StepParams), cudaMemcpyHostToDevice, s));
+  if (n_active) CH_CUDA(cudaMemcpyAsync(m->active, m->h_lists, n_active * 4, cudaMemcpyHostToDevice, s));
+  if (n_sliding) CH_CUDA(cudaMemcpyAsync(m->sliding, m->h_lists + kSlots, n_sliding * 4, cudaMemcpyHostToDevice, s));
+  CH_CUDA(cudaGraphLaunch(*g, s));
+  if (logits) {
+    CH_CUDA(cudaMemcpyAsync(m->h_ids, m->ids, 64 * 4, cudaMemcpyDeviceToHost, s));
+    CH_CUDA(cudaMemcpyAsync(m->h_vals, m->vals, 64 * 4, cudaMemcpyDeviceToHost, s));
+  }
+  CH_CUDA(cudaStreamSynchronize(s));
+  if (topk_out)
+    for (int i = 0; i < 64; i++) topk_out[i] = ch_topk{m->h_ids[i], m->h_vals[i]};
+  if (token_out) *token_out = m->h_ids[0];
+  return CH_OK;
+}
+
+// ---------------------------------------------------------------------------
+// device-resident greedy loop
+extern "C" int ch_decode_plan(ch_model *m, const ch_step_desc *steps, uint32_t n_steps) {
+  if (!m || (!steps && n_steps)) return fail(CH_EINVAL, "NULL argument");
+  if (!m->embed) return fail(CH_ESTATE, "device decode loop needs the device embedding table");
+  size_t total = 0;
+  for (uint32_t i = 0; i < n_steps; i++) {
+    if (steps[i].slot >= kSlots) return fail(CH_EINVAL, "slot >= 4096");
+    CH_TRY(check_lists(steps[i].active, steps[i].n_active));
+    CH_TRY(check_lists(steps[i].sliding, steps[i].n_sliding));
+    total += steps[i].n_active + steps[i].n_sliding;
+  }
+  CH_CUDA(cudaSetDevice(m->ctx->device));
+  CH_CUDA(cudaStreamSynchronize(m->ctx->stream));
+  cudaFree(m->plan);
+  cudaFree(m->plan_lists);
+  m->plan = nullptr;
+  m->plan_lists = nullptr;
+  CH_TRY(dmalloc(&m->plan, std::max<uint32_t>(n_steps, 1)));
+  CH_TRY(dmalloc(&m->plan_lists, std::max<size_t>(total, 1)));
+  std::vector<StepParams> hp(n_steps);
+  std::vector<uint32_t> hl(total);
+  size_t off = 0;
+  for (uint32_t i = 0; i < n_steps; i++) {
+    hp[i].clock = steps[i].clock;
+    hp[i].slot = steps[i].slot;
+    hp[i].n_active = steps[i].n_active;
+    hp[i].n_sliding = steps[i].n_sliding;
+    if (steps[i].n_active) memcpy(&hl[off], steps[i].active, steps[i].n_active * 4);
+    hp[i].active = m->plan_lists + off;
+    off += steps[i].n_active;
+    if (steps[i].n_sliding) memcpy(&hl[off], steps[i].sliding, steps[i].n_sliding * 4);
+    hp[i].sliding = m->plan_lists + off;
+    off += steps[i].n_sliding;
+    hp[i].step = i;
+    hp[i].pad = 0;
+  }
+  if (n_steps) CH_CUDA(cudaMemcpy(m->plan, hp.data(), n_steps * sizeof(StepParams), cudaMemcpyHostToDevice));
+  if (total) CH_CUDA(cudaMemcpy(m->plan_lists, hl.data(), total * 4, cudaMemcpyHostToDevice));
+  if (m->hist_cap < n_steps) {
+    cudaFree(m->token_hist);
+    m->token_hist = nullptr;
+    CH_TRY(dmalloc(&m->token_hist, n_steps));
+    m->hist_cap = n_steps;
+  }
+  if (n_steps == 0) return fail(CH_EINVAL, "empty plan");
+  m->plan_steps = n_steps;
+  // the loop graph bakes in plan / token_hist pointers and the plan length: recapture
+  if (m->g_loop) {
+    cudaGraphExecDestroy(m->g_loop);
+    m->g_loop = nullptr;
+  }
+  CH_TRY(capture(m, true, true, &m->g_loop));
+  return CH_OK;
+}
+
+extern "C" int ch_decode_run(ch_model *m, uint32_t first_token, uint32_t n_steps) {
+  if (!m) return fail(CH_EINVAL, "model is NULL");
+  if (!m->g_loop || n_steps > m->plan_steps) return fail(CH_ESTATE, "ch_decode_plan must cover n_steps first");
+  if (first_token >= m->V) return fail(CH_EINVAL, "first_token >= vocab");
+  CH_CUDA(cudaSetDevice(m->ctx->device));
+  cudaStream_t s = m->ctx->stream;
+  CH_CUDA(cudaStreamSynchronize(s));  // previous run may still read the staging words
+  m->h_run[0] = 0;
+  m->h_run[1] = first_token;
+  CH_CUDA(cudaMemcpyAsync(&m->sp->step, &m->h_run[0], 4, cudaMemcpyHostToDevice, s));
+  CH_CUDA(cudaMemcpyAsync(m->token, &m->h_run[1], 4, cudaMemcpyHostToDevice, s));
+  for (uint32_t i = 0; i < n_steps; i++) CH_CUDA(cudaGraphLaunch(m->g_loop, s));
+  m->loop_pos = n_steps;
+  return CH_OK;
+}
+
+extern "C" int ch_decode_continue(ch_model *m, uint32_t n_steps) {
+  if (!m) return fail(CH_EINVAL, "model is NULL");
+  if (!m->g_loop) return fail(CH_ESTATE, "ch_decode_plan and ch_decode_run come first");
+  if ((uint64_t)m->loop_pos + n_steps > m->plan_steps) return fail(CH_EINVAL, "more steps than planned");
+  CH_CUDA(cudaSetDevice(m->ctx->device));
+  for (uint32_t i = 0; i < n_steps; i++) CH_CUDA(cudaGraphLaunch(m->g_loop, m->ctx->stream));
+  m->loop_pos += n_steps;
+  return CH_OK;
+}
+
+extern "C" int ch_decode_tokens(ch_model *m, uint32_t *tokens, uint32_t n) {
+  if (!m || (!tokens && n)) return fail(CH_EINVAL, "NULL argument");
+  if (n > m->hist_cap) return fail(CH_EINVAL, "more tokens than planned steps");
+  CH_CUDA(cudaStreamSynchronize(m->ctx->stream));
+  if (n) CH_CUDA(cudaMemcpy(tokens, m->token_hist, n * 4, cudaMemcpyDeviceToHost));
+  uint32_t f = 0;
+  CH_TRY(ch_ctx_device_status(m->ctx, &f));
+  return status_from_flags(f);
+}
+
+// ---------------------------------------------------------------------------
+// state access
+extern "C" int ch_read_x(ch_model *m, float *x) {
+  if (!m || !x) return fail(CH_EINVAL, "NULL argument");
+  CH_CUDA(cudaStreamSynchronize(m->ctx->stream));
+  CH_CUDA(cudaMemcpy(x, m->X[0], m->H * 4, cudaMemcpyDeviceToHost));
+  return CH_OK;
+}
+extern "C" int ch_read_normed_x(ch_model *m, float *x) {
+  if (!m || !x) return fail(CH_EINVAL, "NULL argument");
+  CH_CUDA(cudaStreamSynchronize(m->ctx->stream));
+  CH_CUDA(cudaMemcpy(x, m->normed, m->H * 4, cudaMemcpyDeviceToHost));
+  return CH_OK;
+}
+extern "C" int ch_kv_read(ch_model *m, uint32_t layer, uint32_t slot, float *k, float *v) {
+  if (!m || layer >= m->L || slot >= kSlots) return fail(CH_EINVAL, "bad layer / slot");
+  CH_CUDA(cudaStreamSynchronize(m->ctx->stream));
+  std::vector<__half> hk(m->kvd), hv(m->kvd);
+  CH_CUDA(cudaMemcpy(hk.data(), m->layers[layer].kc + (size_t)slot * m->kvd, m->kvd * 2, cudaMemcpyDeviceToHost));
+  CH_CUDA(cudaMemcpy(hv.data(), m->layers[layer].vc + (size_t)slot * m->kvd, m->kvd * 2, cudaMemcpyDeviceToHost));
+  for (uint32_t i = 0; i < m->kvd; i++) {
+    if (k) k[i] = __half2float(hk[i]);
+    if (v) v[i] = __half2float(hv[i]);
+  }
+  return CH_OK;
+}
+extern "C" int ch_kv_write(ch_model *m, uint32_t layer, uint32_t slot, const float *k, const float *v) {
+  if (!m || layer >= m->L || slot >= kSlots || !k || !v) return fail(CH_EINVAL, "bad argument");
+  std::vector<__half> hk(m->kvd), hv(m->kvd);
+  for (uint32_t i = 0; i < m->kvd; i++) {
+    hk[i] = __float2half_rn(k[i]);
+    hv[i] = __float2half_rn(v[i]);
+  }
+  CH_CUDA(cudaStreamSynchronize(m->ctx->stream));
+  CH_CUDA(cudaMemcpy(m->layers[layer].kc + (size_t)slot * m->kvd, hk.data(), m->kvd * 2, cudaMemcpyHostToDevice));
+  CH_CUDA(cudaMemcpy(m->layers[layer].vc + (size_t)slot * m->kvd, hv.data(), m->kvd * 2, cudaMemcpyHostToDevice));
+  return CH_OK;
+}
+
+// ---------------------------------------------------------------------------
+// batched prefill (batch_dispatch.zig:55-151 order)
+static int ensure_prefill(ch_model *m) {
+  const uint32_t N = m->cfg.max_prefill_tokens ? m->cfg.max_prefill_tokens : 1024;
+  if (m->pf_cap >= N) return CH_OK;
+  CH_TRY(dmalloc(&m->pX, (size_t)N * m->H));
+  CH_TRY(dmalloc(&m->pNX, (size_t)N * m->H));
+  CH_TRY(dmalloc(&m->pQKV, (size_t)N * (m->qd + 2 * m->kvd)));
+  CH_TRY(dmalloc(&m->pQO, (size_t)N * m->qd));
+  CH_TRY(dmalloc(&m->pA, (size_t)N * m->qd));
+  CH_TRY(dmalloc(&m->pMO, (size_t)N * m->H));
+  CH_TRY(dmalloc(&m->pACT, (size_t)N * m->I));
+  CH_TRY(dmalloc(&m->pSlots, (size_t)N + kSlots));
+  CH_TRY(dmalloc(&m->pTok, (size_t)N));
+  m->pf_cap = N;
+  return CH_OK;
+}
+
+extern "C" int ch_prefill(ch_model *m, const uint32_t *tokens, uint32_t n, const uint16_t *embed_bf16,
+                          const uint32_t *slots, uint32_t start_clock, uint32_t num_prev, ch_topk *topk_out,
+                          ch_progress_fn progress_fn, void *progress_ctx) {
+  if (!m || !tokens || !slots) return fail(CH_EINVAL, "NULL argument");
+  const uint32_t cap = m->cfg.max_prefill_tokens ? m->cfg.max_prefill_tokens : 1024;
+  if (n == 0 || n > cap) return fail(CH_EBATCH, "BatchTooLarge: n_tokens must be 1..max_prefill_tokens");
+  if (num_prev + n > kSlots) return fail(CH_EINVAL, "num_prev_slots + n_tokens > 4096");
+  CH_TRY(check_lists(slots, num_prev + n));
+  for (uint32_t i = 0; i < n; i++)
+    if (tokens[i] >= m->V) return fail(CH_EINVAL, "token id >= vocab");
+  if (!embed_bf16 && !m->embed) return fail(CH_ESTATE, "no embedding table (host or device)");
+  CH_CUDA(cudaSetDevice(m->ctx->device));
+  CH_TRY(ensure_prefill(m));
+  cudaStream_t s = m->ctx->stream;
+  const float scale = sqrtf((float)m->H);
+  if (embed_bf16) {
+    // host expand like expandEmbeddings (batch_dispatch.zig:14-23)
+    std::vector<float> hx((size_t)n * m->H);
+    for (uint32_t t = 0; t < n; t++) {
+      const uint16_t *row = embed_bf16 + (size_t)tokens[t] * m->H;
+      for (uint32_t i = 0; i < m->H; i++) {
+        uint32_t u = (uint32_t)row[i] << 16;
+        float f;
+        memcpy(&f, &u, 4);
+        hx[(size_t)t * m->H + i] = f * scale;
+      }
+    }
+    CH_CUDA(cudaMemcpyAsync(m->pX, hx.data(), hx.size() * 4, cudaMemcpyHostToDevice, s));
+    CH_CUDA(cudaStreamSynchronize(s));
+  } else {
+    CH_CUDA(cudaMemcpyAsync(m->pTok, tokens, n * 4, cudaMemcpyHostToDevice, s));
+    CH_CUDA(launch_embed_rows(m->embed, m->pTok, n, m->H, scale, m->pX, s));
+  }
+  CH_CUDA(cudaMemcpyAsync(m->pSlots, slots, (num_prev + n) * 4, cudaMemcpyHostToDevice, s));
+  const float eps = m->cfg.rms_norm_eps;
+  const uint32_t qkvd = m->qd + 2 * m->kvd;
+  for (uint32_t l = 0; l < m->L; l++) {
+    DevLayer &dl = m->layers[l];
+    if (l == 0) CH_CUDA(launch_rmsnorm_rows(m->pX, dl.input_norm, m->pNX, n, m->H, eps, s));
+    CH_CUDA(launch_batch_gemm_q4(BatchGemmArgs{dl.qkv, qkvd, m->H, n, m->pNX, m->pQKV, EPI_STORE}, s));
+    BatchQkvRopeArgs r{};
+    r.q = m->pQKV;
+    r.k = m->pQKV + m->qd;
+    r.v = m->pQKV + m->qd + m->kvd;
+    r.q_stride = qkvd;
+    r.kv_stride = qkvd;
+    r.q_norm_w = dl.q_norm;
+    r.k_norm_w = dl.k_norm;
+    r.inv_freq = dl.full ? m->inv_freq_f : m->inv_freq_s;
+    r.q_out = m->pQO;
+    r.k_cache = dl.kc;
+    r.v_cache = dl.vc;
+    r.slots = m->pSlots;
+    r.slot_offset = num_prev;
+    r.start_clock = start_clock;
+    r.N = n;
+    r.nq = m->nq;
+    r.nkv = m->nkv;
+    r.D = m->D;
+    r.rot = m->cfg.rotary_dim;
+    r.eps = eps;
+    r.k_eq_v = 0;
+    CH_CUDA(launch_batch_qkv_rope(r, s));
+    BatchAttnArgs at{m->pQO, dl.kc, dl.vc, m->pSlots, n, num_prev, m->nq, m->nkv, m->D, 1.0f, dl.full ? 0 : 1, m->pA};
+    CH_CUDA(launch_batch_causal_attn(at, s));
+    CH_CUDA(launch_batch_gemm_q4(BatchGemmArgs{dl.o, m->H, m->qd, n, m->pA, m->pMO, EPI_STORE}, s));
+    if (dl.post_attn) CH_CUDA(launch_rmsnorm_rows(m->pMO, dl.post_attn, m->pMO, n, m->H, eps, s));
+    CH_CUDA(launch_add_rmsnorm_rows(m->pX, m->pMO, dl.pre_ffn, m->pNX, n, m->H, eps, 1.0f, s));
+    CH_CUDA(launch_batch_gemm_q4(BatchGemmArgs{dl.gateup, 2 * m->I, m->H, n, m->pNX, m->pACT, EPI_GELU_MUL}, s));
+    CH_CUDA(launch_batch_gemm_q4(BatchGemmArgs{dl.down, m->H, m->I, n, m->pACT, m->pMO, EPI_STORE}, s));
+    if (dl.post_ffn) CH_CUDA(launch_rmsnorm_rows(m->pMO, dl.post_ffn, m->pMO, n, m->H, eps, s));
+    const float *next = (l + 1 < m->L) ? m->layers[l + 1].input_norm : m->final_norm;
+    CH_CUDA(launch_add_rmsnorm_rows(m->pX, m->pMO, next, m->pNX, n, m->H, eps, dl.scalar, s));
+    if (progress_fn && ((l + 1) % 4 == 0 || l + 1 == m->L)) {
+      CH_CUDA(cudaStreamSynchronize(s));
+      progress_fn(l + 1, m->L, progress_ctx);
+    }
+  }
+  // decode-visible state = last token's residual / normed hidden
+  CH_CUDA(cudaMemcpyAsync(m->X[0], m->pX + (size_t)(n - 1) * m->H, m->H * 4, cudaMemcpyDeviceToDevice, s));
+  CH_CUDA(cudaMemcpyAsync(m->normed, m->pNX + (size_t)(n - 1) * m->H, m->H * 4, cudaMemcpyDeviceToDevice, s));
+  if (topk_out) {
+    GemvArgs a;
+    GemvPlan p;
+    p.fmt = FMT_Q8;
+    a.tiles = m->lm;
+    a.row_tiles = m->V / 16;
+    a.k_tiles = m->H / 32;
+    a.K = m->H;
+    a.x = m->normed;
+    a.y = m->logits;
+    a.partial = m->gemv_partial;
+    a.counters = m->gemv_counters;
+    a.err = m->ctx->err;
+    CH_CUDA(launch_gemv(p, a, s, false));
+    TopkArgs t{};
+    t.logits = m->logits;
+    t.V = m->V;
+    t.cand = m->topk_cand;
+    t.counter = m->topk_counter;
+    t.ids = m->ids;
+    t.vals = m->vals;
+    t.token_out = m->token;
+    t.err = m->ctx->err;
+    CH_CUDA(launch_topk64(t, s, false));
+    CH_CUDA(cudaMemcpyAsync(m->h_ids, m->ids, 256, cudaMemcpyDeviceToHost, s));
+    CH_CUDA(cudaMemcpyAsync(m->h_vals, m->vals, 256, cudaMemcpyDeviceToHost, s));
+  }
+  CH_CUDA(cudaStreamSynchronize(s));
+  if (topk_out)
+    for (int i = 0; i < 64; i++) topk_out[i] = ch_topk{m->h_ids[i], m->h_vals[i]};
+  uint32_t f = 0;
+  CH_TRY(ch_ctx_device_status(m->ctx, &f));
+  return status_from_flags(f);
+}
+
+// ---------------------------------------------------------------------------
+// op-level entry points
+extern "C" size_t ch_q4_tile_bytes(uint32_t rows, uint32_t cols) { return q4_tile_bytes(rows, cols); }
+extern "C" size_t ch_q8_tile_bytes(uint32_t rows, uint32_t cols) { return q8_tile_bytes(rows, cols); }
+extern "C" int ch_q4_pack(ch_ctx *c, const uint32_t *blocks, uint32_t rows, uint32_t cols, void *tiles) {
+  if (!c || !blocks || !tiles || rows % 16 || cols % 64) return fail(CH_EINVAL, "q4_pack: rows % 16, cols % 64");
+  CH_CUDA(launch_repack_q4(blocks, nullptr, rows, cols, MAP_PLAIN, (uint8_t *)tiles, c->stream));
+  return CH_OK;
+}
+extern "C" int ch_q4_pack_gateup(ch_ctx *c, const uint32_t *gate, const uint32_t *up, uint32_t rows, uint32_t cols,
+                                 void *tiles) {
+  if (!c || !gate || !up || !tiles || rows % 8 || cols % 64) return fail(CH_EINVAL, "q4_pack_gateup: rows % 8, cols % 64");
+  CH_CUDA(launch_repack_q4(gate, up, 2 * rows, cols, MAP_GATEUP, (uint8_t *)tiles, c->stream));
+  return CH_OK;
+}
+extern "C" int ch_q8_pack(ch_ctx *c, const uint32_t *blocks, uint32_t rows, uint32_t cols, void *tiles) {
+  if (!c || !blocks || !tiles || rows % 16 || cols % 32) return fail(CH_EINVAL, "q8_pack: rows % 16, cols % 32");
+  CH_CUDA(launch_repack_q8(blocks, rows, cols, (uint8_t *)tiles, c->stream));
+  return CH_OK;
+}
+static int op_gemv(ch_ctx *c, int fmt, int epi, const void *tiles, uint32_t rows_tiles16, uint32_t cols,
+                   const float *x, float *y) {
+  CH_TRY(ctx_ensure_gemv(c, rows_tiles16));
+  GemvArgs a;
+  GemvPlan p;
+  p.fmt = fmt;
+  p.epi = epi;
+  a.tiles = (const uint8_t *)tiles;
+  a.row_tiles = rows_tiles16;
+  a.k_tiles = fmt == FMT_Q4 ? cols / 64 : cols / 32;
+  a.K = cols;
+  a.x = x;
+  a.y = y;
+  a.partial = c->gemv_partial;
+  a.counters = c->gemv_counters;
+  a.err = c->err;
+  CH_CUDA(launch_gemv(p, a, c->stream, false));
+  return CH_OK;
+}
+extern "C" int ch_gemv_q4(ch_ctx *c, const void *tiles, uint32_t rows, uint32_t cols, const float *x, float *y) {
+  if (!c || !tiles || !x || !y || rows % 16 || cols % 64 || rows == 0) return fail(CH_EINVAL, "gemv_q4 arguments");
+  return op_gemv(c, FMT_Q4, EPI_STORE, tiles, rows / 16, cols, x, y);
+}
+extern "C" int ch_fused_mlp_q4(ch_ctx *c, const void *tiles, uint32_t rows, uint32_t cols, const float *x, float *act) {
+  if (!c || !tiles || !x || !act || rows % 8 || cols % 64 || rows == 0) return fail(CH_EINVAL, "fused_mlp_q4 arguments");
+  return op_gemv(c, FMT_Q4, EPI_GELU_MUL, tiles, 2 * rows / 16, cols, x, act);
+}
+extern "C" int ch_gemv_q8(ch_ctx *c, const void *tiles, uint32_t rows, uint32_t cols, const float *x, float *y) {
+  if (!c || !tiles || !x || !y || rows % 16 || cols % 32 || rows == 0) return fail(CH_EINVAL, "gemv_q8 arguments");
+  return op_gemv(c, FMT_Q8, EPI_STORE, tiles, rows / 16, cols, x, y);
+}
+extern "C" int ch_rmsnorm(ch_ctx *c, const float *x, const float *w, float *y, uint32_t n, uint32_t h, float eps) {
+  if (!c || !x || !w || !y) return fail(CH_EINVAL, "NULL argument");
+  CH_CUDA(launch_rmsnorm_rows(x, w, y, n, h, eps, c->stream));
+  return CH_OK;
+}
+extern "C" int ch_add_rmsnorm(ch_ctx *c, float *x, const float *r, const float *w, float *y, uint32_t n, uint32_t h,
+                              float eps, float scalar) {
+  if (!c || !x || !r || !w || !y) return fail(CH_EINVAL, "NULL argument");
+  CH_CUDA(launch_add_rmsnorm_rows(x, r, w, y, n, h, eps, scalar, c->stream));
+  return CH_OK;
+}
+extern "C" int ch_decode_attention(ch_ctx *c, const float *qkv, const float *q_norm, const float *k_norm, void *k_cache,
+                                   void *v_cache, const uint32_t *slots_dev, uint32_t n_slots, uint32_t clock,
+                                   uint32_t slot, uint32_t nq, uint32_t nkv, uint32_t head_dim, uint32_t rot, float theta,
+                                   float eps, float scale, float *out) {
+  if (!c || !qkv || !q_norm || !k_norm || !k_cache || !v_cache || !out || (n_slots && !slots_dev))
+    return fail(CH_EINVAL, "NULL argument");
+  if (head_dim != 256 || nkv == 0 || nq % nkv || n_slots > kSlots || slot >= kSlots || rot > head_dim || (rot & 1))
+    return fail(CH_EINVAL, "decode_attention shape");
+  const uint32_t R = nq / nkv;
+  if (R != 1 && R != 2 && R != 4 && R != 8) return fail(CH_EINVAL, "GQA ratio must be 1, 2, 4 or 8");
+  const int splits = attn_default_splits(nkv);
+  const size_t need = attn_partial_floats(nkv, R, head_dim, splits);
+  if (c->attn_partial_n < need) {
+    cudaFree(c->attn_partial);
+    c->attn_partial = nullptr;
+    CH_TRY(dmalloc(&c->attn_partial, need));
+    c->attn_partial_n = need;
+  }
+  if (c->attn_counters_n < nkv) {
+    cudaFree(c->attn_counters);
+    c->attn_counters = nullptr;
+    CH_TRY(dmalloc(&c->attn_counters, nkv));
+    c->attn_counters_n = nkv;
+    CH_CUDA(cudaMemsetAsync(c->attn_counters, 0, nkv * 4, c->stream));
+  }
+  if (c->attn_inv_freq_n < rot / 2) {
+    cudaFree(c->attn_inv_freq);
+    c->attn_inv_freq = nullptr;
+    CH_TRY(dmalloc(&c->attn_inv_freq, 128));
+    c->attn_inv_freq_n = 128;
+  }
+  std::vector<float> f(rot / 2);
+  for (uint32_t i = 0; i < rot / 2; i++) {
+    float e = (2.0f * (float)i) / (float)rot;
+    f[i] = (float)(1.0 / pow((double)theta, (double)e));
+  }
+  StepParams sp{clock, slot, n_slots, n_slots, slots_dev, slots_dev, 0, 0};
+  CH_CUDA(cudaMemcpyAsync(c->attn_inv_freq, f.data(), f.size() * 4, cudaMemcpyHostToDevice, c->stream));
+  CH_CUDA(cudaMemcpyAsync(c->op_sp, &sp, sizeof(sp), cudaMemcpyHostToDevice, c->stream));
+  AttnArgs a{};
+  a.qkv = qkv;
+  a.q_norm_w = q_norm;
+  a.k_norm_w = k_norm;
+  a.inv_freq = c->attn_inv_freq;
+  a.k_cache = (__half *)k_cache;
+  a.v_cache = (__half *)v_cache;
+  a.sp = c->op_sp;
+  a.is_sliding = 0;
+  a.nq = nq;
+  a.nkv = nkv;
+  a.D = head_dim;
+  a.rot = rot;
+  a.eps = eps;
+  a.scale = scale;
+  a.out = out;
+  a.partial = c->attn_partial;
+  a.counters = c->attn_counters;
+  a.err = c->err;
+  a.cache_slots = kSlots;
+  CH_CUDA(launch_decode_attn(a, splits, c->stream, false));
+  // host staging above is synchronous-by-contract: wait so the stack copies stay valid
+  CH_CUDA(cudaStreamSynchronize(c->stream));
+  return CH_OK;
+}
+extern "C" int ch_topk64(ch_ctx *c, const float *logits, uint32_t V, uint32_t *ids, float *vals) {
+  if (!c || !logits || !ids || !vals || V == 0 || V > 262144) return fail(CH_EINVAL, "topk64 arguments");
+  TopkArgs t{};
+  t.logits = logits;
+  t.V = V;
+  t.cand = c->topk_cand;
+  t.counter = c->topk_counter;
+  t.ids = ids;
+  t.vals = vals;
+  t.err = c->err;
+  CH_CUDA(launch_topk64(t, c->stream, false));
+  return CH_OK;
+}
+extern "C" int ch_batch_gemm_q4(ch_ctx *c, const void *tiles, uint32_t rows, uint32_t cols, const float *x, uint32_t n,
+                                float *y) {
+  if (!c || !tiles || !x || !y || rows % 16 || cols % 64) return fail(CH_EINVAL, "batch_gemm_q4 arguments");
+  CH_CUDA(launch_batch_gemm_q4(BatchGemmArgs{(const uint8_t *)tiles, rows, cols, n, x, y, EPI_STORE}, c->stream));
+  return CH_OK;
+}
+extern "C" int ch_batch_fused_mlp_q4(ch_ctx *c, const void *tiles, uint32_t rows, uint32_t cols, const float *x,
+                                     uint32_t n, float *act) {
+  if (!c || !tiles || !x || !act || rows % 8 || cols % 64) return fail(CH_EINVAL, "batch_fused_mlp_q4 arguments");
+  CH_CUDA(launch_batch_gemm_q4(BatchGemmArgs{(const uint8_t *)tiles, 2 * rows, cols, n, x, act, EPI_GELU_MUL}, c->stream));
+  return CH_OK;
+}
+extern "C" int ch_gen_q4_blocks(ch_ctx *c, uint32_t *dst, uint32_t rows, uint32_t cols, uint64_t tseed, float sstd) {
+  if (!c || !dst || cols % 32) return fail(CH_EINVAL, "gen_q4_blocks arguments");
+  CH_CUDA(launch_gen_q4_blocks(dst, rows, cols, tseed, sstd, c->stream));
+  return CH_OK;
+}
+extern "C" int ch_gen_bf16(ch_ctx *c, uint16_t *dst, size_t n, uint64_t tseed, float mean, float std) {
+  if (!c || !dst) return fail(CH_EINVAL, "gen_bf16 arguments");
+  CH_CUDA(launch_gen_bf16(dst, n, tseed, mean, std, c->stream));
+  return CH_OK;
+}
+extern "C" int ch_quantize_q8_rows(ch_ctx *c, const uint16_t *src, uint32_t rows, uint32_t cols, uint32_t *dst) {
+  if (!c || !src || !dst || cols % 32) return fail(CH_EINVAL, "quantize_q8_rows arguments");
+  CH_CUDA(launch_quantize_q8_rows(src, rows, cols, dst, c->stream));
+  return CH_OK;
+}
+extern "C" int ch_quantize_q4_rows(ch_ctx *c, const uint16_t *src, uint32_t rows, uint32_t cols, uint32_t *dst) {
+  if (!c || !src || !dst || cols % 32) return fail(CH_EINVAL, "quantize_q4_rows arguments");
+  CH_CUDA(launch_quantize_q4_rows(src, rows, cols, dst, c->stream));
+  return CH_OK;
+}

@@ -1,0 +1,321 @@
+// prefill.cu -- batched prefill kernels (one chunk of N <= 1024 prompt tokens).
+//
+// Restated reference shaders:
+//   batch_gemm_q4.wgsl:26-160       Y[t*M + r] = sum_b d_rb sum_i (q-8) X[t][32b+i]
+//   batch_fused_mlp_q4.wgsl:33-196  Y[t*M + r] = gelu_tanh(g) * u
+//   batch_qkv_rope.wgsl:29-176      token t: clock = start + t, slot = Slots[offset + t]
+//   batch_causal_attn.wgsl:25-223   token t attends Slots[start .. num_prev+t+1), sliding: last 1024
+//   batch_rmsnorm.wgsl / batch_add_rmsnorm.wgsl
+// The GEMM here runs on the decode tile layout with mma.sync: weights are
+// exact (q-8) f16 A fragments, activations are split into f16 hi + lo B
+// fragments and the per-block f16 scale is applied in f32 -- fp32-faithful.
+#include "common.cuh"
+#include "kernels.cuh"
+
+namespace ch {
+
+// ---------------------------------------------------------------------------
+// norms: one CTA per row
+__global__ void rmsnorm_rows_kernel(const float *x, const float *w, float *y, uint32_t H, float eps) {
+  __shared__ float red[32];
+  const float *xr = x + (size_t)blockIdx.x * H;
+  float *yr = y + (size_t)blockIdx.x * H;
+  float ss = 0.f;
+  for (uint32_t i = threadIdx.x; i < H; i += blockDim.x) ss = __fmaf_rn(xr[i], xr[i], ss);
+  ss = block_sum(ss, red);
+  const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)H), eps)));
+  for (uint32_t i = threadIdx.x; i < H; i += blockDim.x) yr[i] = __fmul_rn(__fmul_rn(xr[i], inv), w[i]);
+}
+__global__ void add_rmsnorm_rows_kernel(float *x, const float *r, const float *w, float *y, uint32_t H, float eps,
+                                        float scalar) {
+  __shared__ float red[32];
+  float *xr = x + (size_t)blockIdx.x * H;
+  const float *rr = r + (size_t)blockIdx.x * H;
+  float *yr = y + (size_t)blockIdx.x * H;
+  float ss = 0.f;
+  for (uint32_t i = threadIdx.x; i < H; i += blockDim.x) {
+    const float v = __fmul_rn(__fadd_rn(xr[i], rr[i]), scalar);
+    xr[i] = v;
+    ss = __fmaf_rn(v, v, ss);
+  }
+  ss = block_sum(ss, red);
+  const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)H), eps)));
+  for (uint32_t i = threadIdx.x; i < H; i += blockDim.x) yr[i] = __fmul_rn(__fmul_rn(xr[i], inv), w[i]);
+}
+cudaError_t launch_rmsnorm_rows(const float *x, const float *w, float *y, uint32_t N, uint32_t H, float eps,
+                                cudaStream_t s) {
+  if (N == 0) return cudaSuccess;
+  rmsnorm_rows_kernel<<<N, 256, 0, s>>>(x, w, y, H, eps);
+  return cudaGetLastError();
+}
+cudaError_t launch_add_rmsnorm_rows(float *x, const float *r, const float *w, float *y, uint32_t N, uint32_t H,
+                                    float eps, float scalar, cudaStream_t s) {
+  if (N == 0) return cudaSuccess;
+  add_rmsnorm_rows_kernel<<<N, 256, 0, s>>>(x, r, w, y, H, eps, scalar);
+  return cudaGetLastError();
+}
+__global__ void embed_rows_kernel(const uint16_t *embed, const uint32_t *tokens, uint32_t H, float scale, float *x) {
+  const uint16_t *row = embed + (size_t)tokens[blockIdx.x] * H;
+  float *xr = x + (size_t)blockIdx.x * H;
+  for (uint32_t i = threadIdx.x; i < H; i += blockDim.x) xr[i] = __fmul_rn(bf16_to_f32(row[i]), scale);
+}
+cudaError_t launch_embed_rows(const uint16_t *embed, const uint32_t *tokens, uint32_t N, uint32_t H, float scale,
+                              float *x, cudaStream_t s) {
+  if (N == 0) return cudaSuccess;
+  embed_rows_kernel<<<N, 256, 0, s>>>(embed, tokens, H, scale, x);
+  return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
+// batch qkv_rope: one warp per (head, token)
+CH_DEV void warp_norm_rope(const float *in, const float *w, float *out, uint32_t D, uint32_t rot, const float *inv_freq,
+                           uint32_t clock, float eps, bool rope, int lane) {
+  float ss = 0.f;
+  for (uint32_t d = lane; d < D; d += 32) ss = __fmaf_rn(in[d], in[d], ss);
+  ss = warp_sum(ss);
+  const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)D), eps)));
+  if (!rope) {
+    for (uint32_t d = lane; d < D; d += 32) out[d] = __fmul_rn(in[d], inv);
+    return;
+  }
+  const uint32_t half = rot / 2;
+  for (uint32_t d = lane; d < half; d += 32) {
+    const float v0 = __fmul_rn(__fmul_rn(in[d], inv), w[d]);
+    const float v1 = __fmul_rn(__fmul_rn(in[d + half], inv), w[d + half]);
+    const float ang = __fmul_rn((float)clock, inv_freq[d]);
+    double sd, cd;
+    sincos((double)ang, &sd, &cd);
+    const float c = (float)cd, s = (float)sd;
+    out[d] = __fsub_rn(__fmul_rn(v0, c), __fmul_rn(v1, s));
+    out[d + half] = __fadd_rn(__fmul_rn(v0, s), __fmul_rn(v1, c));
+  }
+  for (uint32_t d = rot + lane; d < D; d += 32) out[d] = __fmul_rn(__fmul_rn(in[d], inv), w[d]);
+}
+__global__ void batch_qkv_rope_kernel(const BatchQkvRopeArgs a) {
+  __shared__ float tmp[8][512];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const uint32_t heads = a.nq + a.nkv;
+  const uint64_t item = (uint64_t)blockIdx.x * 8 + warp;
+  if (item >= (uint64_t)heads * a.N) return;
+  const uint32_t t = (uint32_t)(item / heads), h = (uint32_t)(item % heads);
+  const uint32_t D = a.D, clock = a.start_clock + t;
+  const size_t qd = (size_t)a.nq * D, kvd = (size_t)a.nkv * D;
+  if (h < a.nq) {
+    warp_norm_rope(a.q + (size_t)t * a.q_stride + (size_t)h * D, a.q_norm_w, a.q_out + t * qd + (size_t)h * D, D, a.rot, a.inv_freq,
+                   clock, a.eps, true, lane);
+    return;
+  }
+  const uint32_t kh = h - a.nq;
+  const uint32_t slot = a.slots[a.slot_offset + t];
+  float *o = tmp[warp];
+  warp_norm_rope(a.k + (size_t)t * a.kv_stride + (size_t)kh * D, a.k_norm_w, o, D, a.rot, a.inv_freq, clock, a.eps, true, lane);
+  __syncwarp();
+  for (uint32_t d = lane; d < D; d += 32) a.k_cache[(size_t)slot * kvd + (size_t)kh * D + d] = __float2half_rn(o[d]);
+  __syncwarp();
+  warp_norm_rope((a.k_eq_v ? a.k : a.v) + (size_t)t * a.kv_stride + (size_t)kh * D, nullptr, o, D, a.rot, nullptr, 0, a.eps, false, lane);
+  __syncwarp();
+  for (uint32_t d = lane; d < D; d += 32) a.v_cache[(size_t)slot * kvd + (size_t)kh * D + d] = __float2half_rn(o[d]);
+}
+cudaError_t launch_batch_qkv_rope(const BatchQkvRopeArgs &a, cudaStream_t s) {
+  if (a.D > 512 || a.N == 0) return a.N == 0 ? cudaSuccess : cudaErrorInvalidValue;
+  const uint64_t items = (uint64_t)(a.nq + a.nkv) * a.N;
+  batch_qkv_rope_kernel<<<(unsigned)((items + 7) / 8), 256, 0, s>>>(a);
+  return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
+// batch causal attention: one warp per (q head, token), online softmax over the
+// gathered slots (K/V rows shared through L1/L2 by the 8 tokens of a CTA).
+__global__ void __launch_bounds__(256) batch_causal_attn_kernel(const BatchAttnArgs a) {
+  constexpr int D = 256, EPL = 8;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const uint32_t h = blockIdx.y;
+  const uint32_t t = blockIdx.x * 8 + warp;
+  if (t >= a.N) return;
+  const uint32_t ratio = a.nq / a.nkv, kvh = h / ratio;
+  const size_t qd = (size_t)a.nq * D, kvd = (size_t)a.nkv * D;
+  const float *qp = a.q + t * qd + (size_t)h * D + lane * EPL;
+  float q[EPL];
+#pragma unroll
+  for (int e = 0; e < EPL; e++) q[e] = qp[e];
+  const uint32_t S = a.num_prev + t + 1;
+  const uint32_t start = (a.is_sliding && S > 1024) ? S - 1024 : 0;
+  float m = -1e9f, l = 0.f, acc[EPL];
+#pragma unroll
+  for (int e = 0; e < EPL; e++) acc[e] = 0.f;
+  for (uint32_t i = start; i < S; i++) {
+    const uint32_t phys = a.slots[i];
+    const uint4 kr = *reinterpret_cast<const uint4 *>(a.k_cache + (size_t)phys * kvd + (size_t)kvh * D + lane * EPL);
+    const uint4 vr = *reinterpret_cast<const uint4 *>(a.v_cache + (size_t)phys * kvd + (size_t)kvh * D + lane * EPL);
+    const __half2 *kh = reinterpret_cast<const __half2 *>(&kr);
+    const __half2 *vh = reinterpret_cast<const __half2 *>(&vr);
+    float dot = 0.f;
+#pragma unroll
+    for (int e = 0; e < EPL / 2; e++) {
+      const float2 f = __half22float2(kh[e]);
+      dot = __fmaf_rn(q[2 * e], f.x, dot);
+      dot = __fmaf_rn(q[2 * e + 1], f.y, dot);
+    }
+    dot = __fmul_rn(warp_sum(dot), a.scale);
+    const float mn = fmaxf(m, dot);
+    const float corr = expf(__fsub_rn(m, mn));
+    const float p = expf(__fsub_rn(dot, mn));
+    l = __fmaf_rn(l, corr, p);
+#pragma unroll
+    for (int e = 0; e < EPL / 2; e++) {
+      const float2 f = __half22float2(vh[e]);
+      acc[2 * e] = __fmaf_rn(acc[2 * e], corr, __fmul_rn(p, f.x));
+      acc[2 * e + 1] = __fmaf_rn(acc[2 * e + 1], corr, __fmul_rn(p, f.y));
+    }
+    m = mn;
+  }
+  const float inv = __fdiv_rn(1.0f, __fadd_rn(l, 1e-9f));
+  float *op = a.out + t * qd + (size_t)h * D + lane * EPL;
+#pragma unroll
+  for (int e = 0; e < EPL; e++) op[e] = __fmul_rn(acc[e], inv);
+}
+cudaError_t launch_batch_causal_attn(const BatchAttnArgs &a, cudaStream_t s) {
+  if (a.D != 256 || a.N == 0) return a.N == 0 ? cudaSuccess : cudaErrorInvalidValue;
+  dim3 grid((a.N + 7) / 8, a.nq);
+  batch_causal_attn_kernel<<<grid, 256, 0, s>>>(a);
+  return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
+// batch GEMM on Q4 tiles: CTA = 8 warps = 128 weight rows x 64 tokens.
+// X tile [64 tokens][64 k] staged in shared memory as f16 hi and lo planes.
+namespace {
+constexpr int kBgTok = 64;
+constexpr int kBgStride = 72;  // halves per token row (64 + 8 pad -> conflict-free fragment loads)
+}  // namespace
+
+template <int EPI>
+__global__ void __launch_bounds__(256) batch_gemm_q4_kernel(const BatchGemmArgs a) {
+  __shared__ __align__(16) __half xh[2][kBgTok * kBgStride];
+  __shared__ __align__(16) __half xl[2][kBgTok * kBgStride];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int g = lane >> 2, t = lane & 3;
+  const uint32_t KT = a.K / 64, row_tiles = a.M / 16;
+  const uint32_t rt = blockIdx.x * 8 + warp;
+  const uint32_t tok0 = blockIdx.y * kBgTok;
+  const bool active = rt < row_tiles;
+
+  float acc[8][4];
+#pragma unroll
+  for (int j = 0; j < 8; j++)
+#pragma unroll
+    for (int e = 0; e < 4; e++) acc[j][e] = 0.f;
+
+  auto load_x = [&](uint32_t kt, int buf) {
+    // 256 threads: token = tid / 4, 16 consecutive k each
+    const uint32_t tk = tid >> 2, kseg = (tid & 3) * 16;
+    const uint32_t tok = tok0 + tk;
+    __half *hr = xh[buf] + tk * kBgStride + kseg;
+    __half *lr = xl[buf] + tk * kBgStride + kseg;
+    if (tok < a.N) {
+      const float4 *src = reinterpret_cast<const float4 *>(a.X + (size_t)tok * a.K + kt * 64 + kseg);
+#pragma unroll
+      for (int q = 0; q < 4; q++) {
+        const float4 v = src[q];
+        const float vv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+          const __half hh = __float2half_rn(vv[e]);
+          hr[q * 4 + e] = hh;
+          lr[q * 4 + e] = __float2half_rn(__fsub_rn(vv[e], __half2float(hh)));
+        }
+      }
+    } else {
+#pragma unroll
+      for (int e = 0; e < 16; e++) {
+        hr[e] = __float2half_rn(0.f);
+        lr[e] = __float2half_rn(0.f);
+      }
+    }
+  };
+
+  load_x(0, 0);
+  __syncthreads();
+  for (uint32_t kt = 0; kt < KT; kt++) {
+    const int buf = kt & 1;
+    if (kt + 1 < KT) load_x(kt + 1, buf ^ 1);
+    if (active) {
+      const uint8_t *tile = a.tiles + ((size_t)rt * KT + kt) * kTileBytes;
+      const uint4 w = __ldg(reinterpret_cast<const uint4 *>(tile + lane * 16));
+      const uint2 sc = __ldg(reinterpret_cast<const uint2 *>(tile + 512 + g * 8));
+      const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+      for (int blk = 0; blk < 2; blk++) {
+        uint32_t af[2][4];
+        dequant_q4_word(ws[blk * 2 + 0], af[0]);
+        dequant_q4_word(ws[blk * 2 + 1], af[1]);
+        const float s0 = __half2float(__ushort_as_half((unsigned short)((blk ? sc.x >> 16 : sc.x) & 0xFFFFu)));
+        const float s1 = __half2float(__ushort_as_half((unsigned short)((blk ? sc.y >> 16 : sc.y) & 0xFFFFu)));
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+          float d[4] = {0.f, 0.f, 0.f, 0.f};
+          const int row = j * 8 + g;
+#pragma unroll
+          for (int ch = 0; ch < 2; ch++) {
+            const int kk = blk * 32 + ch * 16 + 2 * t;
+            const uint32_t bh0 = *reinterpret_cast<const uint32_t *>(&xh[buf][row * kBgStride + kk]);
+            const uint32_t bh1 = *reinterpret_cast<const uint32_t *>(&xh[buf][row * kBgStride + kk + 8]);
+            const uint32_t bl0 = *reinterpret_cast<const uint32_t *>(&xl[buf][row * kBgStride + kk]);
+            const uint32_t bl1 = *reinterpret_cast<const uint32_t *>(&xl[buf][row * kBgStride + kk + 8]);
+            mma_16816(d, af[ch], bh0, bh1);
+            mma_16816(d, af[ch], bl0, bl1);
+          }
+          acc[j][0] = __fmaf_rn(s0, d[0], acc[j][0]);
+          acc[j][1] = __fmaf_rn(s0, d[1], acc[j][1]);
+          acc[j][2] = __fmaf_rn(s1, d[2], acc[j][2]);
+          acc[j][3] = __fmaf_rn(s1, d[3], acc[j][3]);
+        }
+      }
+    }
+    __syncthreads();
+  }
+  if (!active) return;
+  // D layout: d0 = (row g, token 2t), d1 = (row g, token 2t+1), d2/d3 = row g+8
+#pragma unroll
+  for (int j = 0; j < 8; j++) {
+    const uint32_t ta = tok0 + j * 8 + 2 * t, tb = ta + 1;
+    if (EPI == EPI_STORE) {
+      const uint32_t r0 = rt * 16 + g, r1 = r0 + 8;
+      if (ta < a.N) {
+        a.Y[(size_t)ta * a.M + r0] = acc[j][0];
+        a.Y[(size_t)ta * a.M + r1] = acc[j][2];
+      }
+      if (tb < a.N) {
+        a.Y[(size_t)tb * a.M + r0] = acc[j][1];
+        a.Y[(size_t)tb * a.M + r1] = acc[j][3];
+      }
+    } else {
+      const uint32_t Mo = a.M / 2, r = rt * 8 + g;
+      float x3, inner;
+      if (ta < a.N) {
+        const float x = acc[j][0];
+        x3 = __fmul_rn(__fmul_rn(__fmul_rn(0.044715f, x), x), x);
+        inner = __fmul_rn(0.7978845608f, __fadd_rn(x, x3));
+        a.Y[(size_t)ta * Mo + r] = __fmul_rn(__fmul_rn(__fmul_rn(0.5f, x), __fadd_rn(1.0f, tanhf(inner))), acc[j][2]);
+      }
+      if (tb < a.N) {
+        const float x = acc[j][1];
+        x3 = __fmul_rn(__fmul_rn(__fmul_rn(0.044715f, x), x), x);
+        inner = __fmul_rn(0.7978845608f, __fadd_rn(x, x3));
+        a.Y[(size_t)tb * Mo + r] = __fmul_rn(__fmul_rn(__fmul_rn(0.5f, x), __fadd_rn(1.0f, tanhf(inner))), acc[j][3]);
+      }
+    }
+  }
+}
+
+cudaError_t launch_batch_gemm_q4(const BatchGemmArgs &a, cudaStream_t s) {
+  if (a.M % 16 || a.K % 64 || a.N == 0) return a.N == 0 ? cudaSuccess : cudaErrorInvalidValue;
+  dim3 grid((a.M / 16 + 7) / 8, (a.N + kBgTok - 1) / kBgTok);
+  if (a.epi == EPI_STORE)
+    batch_gemm_q4_kernel<EPI_STORE><<<grid, 256, 0, s>>>(a);
+  else
+    batch_gemm_q4_kernel<EPI_GELU_MUL><<<grid, 256, 0, s>>>(a);
+  return cudaGetLastError();
+}
+
+}  // namespace ch

@@ -1,0 +1,233 @@
+// topk.cu -- logit softcap + top-64 (+ greedy token) over the vocabulary.
+//
+// Restates topk_pass1.wgsl:17-19 (softcap 30*tanh(v/30)), topk_pass1/2 (top-64
+// sorted descending) and sampler greedy = candidates[0] (src/sampler.zig:213).
+// The reference's bitonic merges leave tie order unspecified; here every value
+// carries a unique 64-bit key (sortable softcap bits << 32 | ~index), so the
+// order is value descending then lowest index first -- deterministic, and the
+// same rule the oracle uses.
+// B200 design: one pass of radix-select per CTA over 2,048 logits (8 rounds of
+// 8-bit histograms in shared memory), 64 candidates per CTA, and the last CTA
+// to finish repeats the select over all candidates.  Two launches collapse
+// into one; no global sort.
+#include "common.cuh"
+#include "kernels.cuh"
+
+namespace ch {
+
+namespace {
+constexpr int kTkThreads = 256;
+constexpr int kTkPer = 8;  // logits per thread in pass 1
+constexpr int kTkChunk = kTkThreads * kTkPer;
+constexpr int kFinalPer = 32;  // candidates per thread in the final pass (up to 8192 candidates)
+}  // namespace
+
+int topk_blocks(uint32_t V) { return (int)((V + kTkChunk - 1) / kTkChunk); }
+
+CH_DEV uint32_t sortable(float f) {
+  uint32_t u = __float_as_uint(f);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+CH_DEV float unsortable(uint32_t s) {
+  uint32_t u = (s & 0x80000000u) ? (s ^ 0x80000000u) : ~s;
+  return __uint_as_float(u);
+}
+CH_DEV float softcap(float v) {
+  // shaders/topk_pass1.wgsl:17-19
+  return __fmul_rn(30.0f, tanhf(__fmul_rn(v, 1.0f / 30.0f)));
+}
+
+// K-th largest 64-bit key held E-per-thread across the block (keys unique except 0 padding)
+template <int E>
+CH_DEV uint64_t block_kth_largest(const uint64_t (&k)[E], int K, uint32_t *hist, uint32_t *sh) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  uint64_t prefix = 0, mask = 0;
+  int need = K;
+  for (int shift = 56; shift >= 0; shift -= 8) {
+    for (int i = tid; i < 256; i += blockDim.x) hist[i] = 0;
+    __syncthreads();
+#pragma unroll
+    for (int e = 0; e < E; e++)
+      if ((k[e] & mask) == prefix) atomicAdd(&hist[(uint32_t)(k[e] >> shift) & 0xFFu], 1u);
+    __syncthreads();
+    if (warp == 0) {
+      uint32_t cnt = 0;
+#pragma unroll
+      for (int b = 0; b < 8; b++) cnt += hist[lane * 8 + b];
+      uint32_t suf = cnt;  // inclusive suffix sum over lanes >= lane
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        uint32_t v = __shfl_down_sync(0xffffffffu, suf, o);
+        if (lane + o < 32) suf += v;
+      }
+      uint32_t above = __shfl_down_sync(0xffffffffu, suf, 1);
+      if (lane == 31) above = 0;
+      if (suf >= (uint32_t)need && above < (uint32_t)need) {
+        uint32_t run = above;
+        for (int b = 7; b >= 0; b--) {
+          uint32_t h = hist[lane * 8 + b];
+          if (run + h >= (uint32_t)need) {
+            sh[0] = (uint32_t)(lane * 8 + b);
+            sh[1] = (uint32_t)need - run;
+            break;
+          }
+          run += h;
+        }
+      }
+    }
+    __syncthreads();
+    const uint32_t sel = sh[0];
+    need = (int)sh[1];
+    prefix |= (uint64_t)sel << shift;
+    mask |= 0xFFull << shift;
+    __syncthreads();
+  }
+  return prefix;
+}
+
+// keys >= thr collected into out[64] sorted descending (rank by comparison; pads are 0)
+template <int E>
+CH_DEV void collect_sorted64(const uint64_t (&k)[E], uint64_t thr, uint64_t *buf, uint32_t *cnt, uint64_t *out) {
+  const int tid = threadIdx.x;
+  if (tid == 0) *cnt = 0;
+  if (tid < 64) buf[tid] = 0;
+  __syncthreads();
+#pragma unroll
+  for (int e = 0; e < E; e++)
+    if (k[e] >= thr && k[e] != 0) {
+      uint32_t p = atomicAdd(cnt, 1u);
+      if (p < 64) buf[p] = k[e];
+    }
+  __syncthreads();
+  if (tid < 64) {
+    const uint64_t me = buf[tid];
+    int rank = 0;
+    for (int j = 0; j < 64; j++) {
+      const uint64_t o = buf[j];
+      rank += (o > me) || (o == me && j < tid);
+    }
+    out[rank] = me;
+  }
+  __syncthreads();
+}
+
+__global__ void __launch_bounds__(kTkThreads) topk64_kernel(const TopkArgs a) {
+  __shared__ uint32_t hist[256];
+  __shared__ uint32_t sh[4];
+  __shared__ uint64_t buf[64];
+  __shared__ uint64_t sorted[64];
+  __shared__ uint32_t cnt;
+  __shared__ uint32_t last_flag;
+  const int tid = threadIdx.x;
+  grid_dep_wait();
+  grid_dep_launch();
+
+  {
+    uint64_t k[kTkPer];
+    const uint32_t base = blockIdx.x * kTkChunk;
+#pragma unroll
+    for (int e = 0; e < kTkPer; e++) {
+      const uint32_t idx = base + e * kTkThreads + tid;
+      if (idx < a.V) {
+        const float v = softcap(a.logits[idx]);
+        k[e] = ((uint64_t)sortable(v) << 32) | (uint64_t)(0xFFFFFFFFu - idx);
+      } else {
+        k[e] = 0;
+      }
+    }
+    const uint64_t thr = block_kth_largest<kTkPer>(k, 64, hist, sh);
+    collect_sorted64<kTkPer>(k, thr, buf, &cnt, sorted);
+    if (tid < 64) a.cand[(size_t)blockIdx.x * 64 + tid] = sorted[tid];
+  }
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) last_flag = (atomicAdd(a.counter, 1u) == gridDim.x - 1) ? 1u : 0u;
+  __syncthreads();
+  if (!last_flag) return;
+  __threadfence();
+
+  uint64_t k[kFinalPer];
+  const uint32_t ncand = gridDim.x * 64;
+#pragma unroll
+  for (int e = 0; e < kFinalPer; e++) {
+    const uint32_t i = e * kTkThreads + tid;
+    k[e] = i < ncand ? __ldcg(&a.cand[i]) : 0ull;
+  }
+  const uint64_t thr = block_kth_largest<kFinalPer>(k, 64, hist, sh);
+  collect_sorted64<kFinalPer>(k, thr, buf, &cnt, sorted);
+  if (tid < 64) {
+    const uint64_t key = sorted[tid];
+    uint32_t id = 0;
+    float val = -1e30f;
+    if (key != 0) {
+      id = 0xFFFFFFFFu - (uint32_t)(key & 0xFFFFFFFFu);
+      val = unsortable((uint32_t)(key >> 32));
+    }
+    a.ids[tid] = id;
+    a.vals[tid] = val;
+    if (tid == 0) {
+      if (a.token_out) *a.token_out = id;
+      if (a.sp) {
+        const uint32_t step = a.sp->step;
+        if (a.token_hist && step < a.hist_cap) a.token_hist[step] = id;
+        a.sp->step = step + 1;
+      }
+    }
+  }
+  if (tid == 0) *a.counter = 0u;
+}
+
+cudaError_t launch_topk64(const TopkArgs &a, cudaStream_t s, bool pdl) {
+  const int blocks = topk_blocks(a.V);
+  if (blocks * 64 > kTkThreads * kFinalPer) return cudaErrorInvalidValue;  // V <= 262,144 with these sizes
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(blocks);
+  cfg.blockDim = dim3(kTkThreads);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, topk64_kernel, a);
+}
+
+// ---------------------------------------------------------------------------
+// step_begin: advance the device-resident decode loop -- copy plan[step] into
+// the live StepParams and expand the embedding of the current token
+// (src/model/forward.zig:33-37: x = bf16(embed[token]) * sqrt(H)).
+__global__ void step_begin_kernel(const StepBeginArgs a) {
+  grid_dep_wait();
+  __shared__ StepParams cur;
+  if (threadIdx.x == 0) {
+    uint32_t step = a.sp->step;
+    if (step >= a.n_plan) {  // replayed past the uploaded plan: keep the last entry, flag it
+      atomicOr(a.err, DEV_ERR_BAD_LIST);
+      step = a.n_plan - 1;
+    }
+    cur = a.plan[step];
+    cur.step = step;
+  }
+  __syncthreads();
+  if (blockIdx.x == 0 && threadIdx.x == 0) *a.sp = cur;
+  const uint32_t tok = *a.token;
+  const uint16_t *row = a.embed + (size_t)tok * a.H;
+  for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < a.H; i += gridDim.x * blockDim.x)
+    a.x[i] = __fmul_rn(bf16_to_f32(row[i]), a.embed_scale);
+  grid_dep_launch();
+}
+cudaError_t launch_step_begin(const StepBeginArgs &a, cudaStream_t s, bool pdl) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(1);
+  cfg.blockDim = dim3(512);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, step_begin_kernel, a);
+}
+
+}  // namespace ch

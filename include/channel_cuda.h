@@ -1,0 +1,221 @@
+/*
+ * channel_cuda.h -- C-ABI of libchannel_b200.so, the B200 (sm_100a) replacement
+ * for the Vulkan GPU backend of Sullux/channel (src/gpu.zig, src/gpu/*.zig).
+ *
+ * Plain C types only: pointers, sizes, fixed-width integers.  Every call
+ * returns an int status (CH_OK = 0, negative on error) unless noted; the
+ * message of the last failure on the calling thread is ch_last_error().
+ * Calls on one ch_model are not thread-safe (the reference drives its GPU
+ * context from the single server thread, src/server.zig:259-281).
+ *
+ * Host pointers are ordinary (pageable) host memory unless the name says
+ * `_dev`, in which case it is a CUDA device pointer on the context's device
+ * and the call is asynchronous on the context stream (ch_ctx_stream).
+ */
+#ifndef CHANNEL_CUDA_H
+#define CHANNEL_CUDA_H
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define CH_API_VERSION 1
+
+typedef enum {
+  CH_OK = 0,
+  CH_EINVAL = -1,   /* bad argument (shape, pointer, size)                         */
+  CH_ENOMEM = -2,   /* device or host allocation failed                            */
+  CH_ECUDA = -3,    /* CUDA runtime error                                          */
+  CH_ETIMEOUT = -4, /* a bounded device wait gave up (status word set by a kernel) */
+  CH_EBATCH = -5,   /* BatchTooLarge (src/gpu/batch_dispatch.zig:42)               */
+  CH_ESTATE = -6,   /* call not valid in the current state                         */
+  CH_EDEVICE = -7,  /* a kernel reported a bad slot / list entry                   */
+  CH_ECOMM = -8     /* multi-GPU communicator error                                */
+} ch_status;
+
+typedef struct ch_ctx ch_ctx;
+typedef struct ch_model ch_model;
+typedef struct ch_ring ch_ring;
+
+/* TopKCandidate (src/model/types.zig:282-285) */
+typedef struct {
+  uint32_t id;
+  float val;
+} ch_topk;
+
+const char *ch_last_error(void);
+int ch_api_version(void);
+
+/* ------------------------------------------------------------------------
+ * Context -- replaces GpuContext.init / deinit (src/gpu/context.zig:17-107,109)
+ * ---------------------------------------------------------------------- */
+int ch_ctx_create(int device, ch_ctx **out);
+void ch_ctx_destroy(ch_ctx *ctx);
+int ch_ctx_synchronize(ch_ctx *ctx);
+void *ch_ctx_stream(ch_ctx *ctx); /* cudaStream_t */
+/* Reads and clears the device status word (bit 0 bulk-copy wait timeout,
+ * bit 1 bad slot, bit 2 bad slot-list entry, bit 3 peer wait timeout). */
+int ch_ctx_device_status(ch_ctx *ctx, uint32_t *flags);
+
+/* ------------------------------------------------------------------------
+ * Model -- replaces GpuModelContext.init / deinit (src/gpu/model_gpu.zig:68-216)
+ * ---------------------------------------------------------------------- */
+/* ModelConfig subset (src/model/types.zig:210-229) */
+typedef struct {
+  uint32_t vocab_size, hidden_size, intermediate_size, num_hidden_layers;
+  uint32_t num_attention_heads, num_key_value_heads, head_dim, rotary_dim;
+  float rms_norm_eps, rope_theta, rope_theta_full;
+  uint32_t sliding_window;     /* decode sliding list length used by the caller's ring */
+  uint32_t max_prefill_tokens; /* BatchPrefillContext max_tokens (model_gpu.zig:178): 1024 */
+  uint8_t layer_types[64];     /* 0 = sliding_attention, 1 = full_attention (types.zig:174,228) */
+} ch_model_config;
+
+/* LayerWeights (src/model/types.zig:180-208): projections already quantized by
+ * quantizeRowQ4_0 (src/quant.zig:58-98, 5 words per 32 weights), norms as f32
+ * (createNormBuffer, model_gpu.zig:57-66).  post_* may be NULL. */
+typedef struct {
+  const uint32_t *q_proj, *k_proj, *v_proj, *o_proj, *gate_proj, *up_proj, *down_proj;
+  const float *input_norm, *q_norm, *k_norm, *post_attn_norm, *pre_ffn_norm, *post_ffn_norm;
+  float layer_scalar;
+} ch_layer_weights;
+
+/* Uploads and repacks every projection, the Q8_0 LM head (quantizeRowQ8_0 of
+ * the tied embedding, model_gpu.zig:157) and the norms; allocates the 4,096-slot
+ * f16 KV cache per layer.  embed_bf16 (vocab x hidden) is optional and enables
+ * device-side embedding lookup. */
+int ch_model_create(ch_ctx *ctx, const ch_model_config *cfg, const ch_layer_weights *layers, const uint32_t *lm_head_q8,
+                    const float *final_norm, const uint16_t *embed_bf16, ch_model **out);
+/* Same model with seeded synthetic weights generated on the device (Q4 codes
+ * uniform in [-8,7], scales |N(0,0.02)| as f16, embedding bf16 N(0,0.02), LM head
+ * = Q8_0 of the embedding, norms 1+N(0,0.02)); generator shared with the oracle. */
+int ch_model_create_synthetic(ch_ctx *ctx, const ch_model_config *cfg, uint64_t seed, ch_model **out);
+void ch_model_destroy(ch_model *m);
+/* Zero KV caches and decode state (src/server.zig:76-82). */
+int ch_model_zero_state(ch_model *m);
+/* Device pointer and logical shape of one repacked weight (which: 0 q|k|v,
+ * 1 o_proj, 2 gate|up interleaved (rows = 2*intermediate), 3 down_proj,
+ * 4 LM head Q8) -- for single-kernel measurement through the op-level calls. */
+int ch_model_weight_tiles(ch_model *m, uint32_t layer, int which, void **tiles_dev, uint32_t *rows, uint32_t *cols);
+
+/* ------------------------------------------------------------------------
+ * Decode -- replaces gpuDispatchForwardToken (src/gpu/model_dispatch.zig:344-369)
+ * x: f32[hidden] (embedding row * sqrt(hidden), forward.zig:33-37).
+ * active / sliding: physical slot lists from DynamicRingBuffer.getActiveSlotsLayer
+ * (layer 0, used by every layer, forward.zig:42-45).  topk_out: 64 entries or
+ * NULL; token_out: greedy token (topk[0].id) or NULL.  When both are NULL the
+ * logits tail is skipped (the reference's no-logits command buffer).
+ * ---------------------------------------------------------------------- */
+int ch_forward_token(ch_model *m, const float *x, uint32_t clock, uint32_t slot, const uint32_t *active, uint32_t n_active,
+                     const uint32_t *sliding, uint32_t n_sliding, ch_topk *topk_out, uint32_t *token_out);
+
+/* ------------------------------------------------------------------------
+ * Prefill -- replaces gpuDispatchPrefillBatch (src/gpu/batch_dispatch.zig:27-172)
+ * tokens: n_tokens ids (1..max_prefill_tokens, else CH_EBATCH); embed_bf16: host
+ * table (NULL -> device table from model creation); slots: num_prev_slots
+ * previous slots followed by the n_tokens new slots; topk_out: 64 or NULL.
+ * progress_fn is called after every 4 layers like the reference.
+ * ---------------------------------------------------------------------- */
+typedef void (*ch_progress_fn)(size_t layer_idx, size_t total_layers, void *ctx);
+int ch_prefill(ch_model *m, const uint32_t *tokens, uint32_t n_tokens, const uint16_t *embed_bf16, const uint32_t *slots,
+               uint32_t start_clock, uint32_t num_prev_slots, ch_topk *topk_out, ch_progress_fn progress_fn,
+               void *progress_ctx);
+
+/* ------------------------------------------------------------------------
+ * State access -- replaces the mapped UMA buffers the reference reads/writes
+ * directly (buf_x: decode.zig:13; KV: memory.zig:106-107, snapshot.zig:97-98)
+ * ---------------------------------------------------------------------- */
+int ch_read_x(ch_model *m, float *x);               /* residual after the last step */
+int ch_read_normed_x(ch_model *m, float *normed_x); /* final-normed hidden state    */
+int ch_kv_read(ch_model *m, uint32_t layer, uint32_t slot, float *k, float *v);
+int ch_kv_write(ch_model *m, uint32_t layer, uint32_t slot, const float *k, const float *v);
+
+/* ------------------------------------------------------------------------
+ * Device-resident greedy decode loop (no host round trip per token): the
+ * per-step ring lists are uploaded once, then each step embeds the previous
+ * token on the device and feeds its greedy token to the next step.
+ * ---------------------------------------------------------------------- */
+typedef struct {
+  uint32_t clock, slot, n_active, n_sliding;
+  const uint32_t *active, *sliding; /* host lists */
+} ch_step_desc;
+int ch_decode_plan(ch_model *m, const ch_step_desc *steps, uint32_t n_steps); /* requires the device embedding */
+int ch_decode_run(ch_model *m, uint32_t first_token, uint32_t n_steps);     /* async; restarts at plan step 0 */
+int ch_decode_continue(ch_model *m, uint32_t n_steps);                      /* async; next planned steps   */
+int ch_decode_tokens(ch_model *m, uint32_t *tokens, uint32_t n);            /* syncs, copies step tokens */
+
+/* ------------------------------------------------------------------------
+ * Op-level entry points (device pointers, async on the context stream).
+ * Weight tiles: 16 rows x 64 k (Q4) / 16 x 32 (Q8), 576 bytes each.
+ * ---------------------------------------------------------------------- */
+size_t ch_q4_tile_bytes(uint32_t rows, uint32_t cols);
+size_t ch_q8_tile_bytes(uint32_t rows, uint32_t cols);
+/* quant.zig Q4 blocks (rows x cols/32 x 5 words) -> tiles; rows % 16, cols % 64 */
+int ch_q4_pack(ch_ctx *ctx, const uint32_t *blocks_dev, uint32_t rows, uint32_t cols, void *tiles_dev);
+/* gate/up pair (rows each) -> interleaved tiles for ch_fused_mlp_q4 (2*rows rows) */
+int ch_q4_pack_gateup(ch_ctx *ctx, const uint32_t *gate_dev, const uint32_t *up_dev, uint32_t rows, uint32_t cols,
+                      void *tiles_dev);
+/* Q8_0 blocks (rows x cols/32 x 9 words) -> tiles */
+int ch_q8_pack(ch_ctx *ctx, const uint32_t *blocks_dev, uint32_t rows, uint32_t cols, void *tiles_dev);
+/* gemv_q4.wgsl: y[rows] = W x */
+int ch_gemv_q4(ch_ctx *ctx, const void *tiles_dev, uint32_t rows, uint32_t cols, const float *x_dev, float *y_dev);
+/* fused_mlp_q4.wgsl: act[rows] = gelu_tanh(Wg x) * (Wu x) */
+int ch_fused_mlp_q4(ch_ctx *ctx, const void *gateup_tiles_dev, uint32_t rows, uint32_t cols, const float *x_dev,
+                    float *act_dev);
+/* gemv_q8.wgsl */
+int ch_gemv_q8(ch_ctx *ctx, const void *tiles_dev, uint32_t rows, uint32_t cols, const float *x_dev, float *y_dev);
+/* rmsnorm.wgsl / add_rmsnorm.wgsl over n_rows rows of h */
+int ch_rmsnorm(ch_ctx *ctx, const float *x_dev, const float *w_dev, float *y_dev, uint32_t n_rows, uint32_t h, float eps);
+int ch_add_rmsnorm(ch_ctx *ctx, float *x_dev, const float *r_dev, const float *w_dev, float *y_dev, uint32_t n_rows,
+                   uint32_t h, float eps, float scalar);
+/* qkv_rope.wgsl + decode_attn.wgsl for one layer: qkv_dev = q|k|v raw
+ * projections; K/V caches f16 [4096][nkv*head_dim]; the new K/V go to `slot`. */
+int ch_decode_attention(ch_ctx *ctx, const float *qkv_dev, const float *q_norm_dev, const float *k_norm_dev,
+                        void *k_cache_dev, void *v_cache_dev, const uint32_t *slots_dev, uint32_t n_slots, uint32_t clock,
+                        uint32_t slot, uint32_t nq, uint32_t nkv, uint32_t head_dim, uint32_t rotary_dim, float theta,
+                        float eps, float scale, float *out_dev);
+/* topk_pass1/2.wgsl: softcap + top-64, value desc then lowest index */
+int ch_topk64(ch_ctx *ctx, const float *logits_dev, uint32_t vocab, uint32_t *ids_dev, float *vals_dev);
+/* batch_gemm_q4.wgsl (Y[t*rows + r]) and batch_fused_mlp_q4.wgsl on tiles */
+int ch_batch_gemm_q4(ch_ctx *ctx, const void *tiles_dev, uint32_t rows, uint32_t cols, const float *x_dev,
+                     uint32_t n_tokens, float *y_dev);
+int ch_batch_fused_mlp_q4(ch_ctx *ctx, const void *gateup_tiles_dev, uint32_t rows, uint32_t cols, const float *x_dev,
+                          uint32_t n_tokens, float *act_dev);
+/* seeded generators (same spec as the oracle) */
+int ch_gen_q4_blocks(ch_ctx *ctx, uint32_t *blocks_dev, uint32_t rows, uint32_t cols, uint64_t tensor_seed,
+                     float scale_std);
+int ch_gen_bf16(ch_ctx *ctx, uint16_t *dst_dev, size_t n, uint64_t tensor_seed, float mean, float std);
+int ch_quantize_q8_rows(ch_ctx *ctx, const uint16_t *src_bf16_dev, uint32_t rows, uint32_t cols, uint32_t *dst_dev);
+int ch_quantize_q4_rows(ch_ctx *ctx, const uint16_t *src_bf16_dev, uint32_t rows, uint32_t cols, uint32_t *dst_dev);
+uint64_t ch_tensor_seed(uint64_t seed, uint32_t layer, uint32_t tensor_id);
+
+/* ------------------------------------------------------------------------
+ * Ring buffer slot math -- DynamicRingBuffer (src/ring_buffer.zig:21-391),
+ * metadata only (the K/V rows live in the model's device cache).
+ * ---------------------------------------------------------------------- */
+ch_ring *ch_ring_create(uint32_t num_layers, uint32_t num_anchors);
+void ch_ring_destroy(ch_ring *r);
+void ch_ring_reset(ch_ring *r);
+void ch_ring_set_num_anchors(ch_ring *r, size_t n);
+size_t ch_ring_num_anchors(const ch_ring *r);
+size_t ch_ring_total_ingested(const ch_ring *r);
+size_t ch_ring_window_size(const ch_ring *r, size_t layer);
+size_t ch_ring_get_slot_index(const ch_ring *r, size_t layer, size_t clock);
+size_t ch_ring_activate_slot(ch_ring *r, size_t layer, size_t clock);
+void ch_ring_deactivate_slot(ch_ring *r, size_t layer, size_t clock);
+void ch_ring_rollback_clock(ch_ring *r, size_t target_clock);
+void ch_ring_write_kv_meta(ch_ring *r, size_t layer, size_t clock);
+void ch_ring_write_recall_meta(ch_ring *r, size_t layer, size_t rank, size_t clock);
+void ch_ring_clear_recall(ch_ring *r);
+void ch_ring_mark_boundary(ch_ring *r, size_t clock, int span_type, float salience);
+int ch_ring_is_active(const ch_ring *r, size_t layer, size_t slot);
+size_t ch_ring_slot_clock(const ch_ring *r, size_t layer, size_t slot);
+size_t ch_ring_active_slots(const ch_ring *r, size_t layer, size_t clock, int is_sliding, size_t sliding_window,
+                            uint32_t *out);
+size_t ch_ring_prefill_prev_slots(const ch_ring *r, size_t layer, size_t start_clock, size_t chunk_len, uint32_t *out);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* CHANNEL_CUDA_H */
