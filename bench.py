@@ -48,6 +48,8 @@ def parse():
     ap.add_argument("--layers", type=int, default=48)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--kernel-only", action="store_true",
+                    help="only time the dominant kernel (fused gate/up GEMV) over rotating layers; for ncu captures")
     return ap.parse_args()
 
 
@@ -161,6 +163,42 @@ def reference_arm(args):
 
 
 # ----------------------------------------------------------------------------------------
+def gateup_roofline(ctx, gm, cfg, stream, reps=3):
+    """Dominant decode kernel (fused gate/up Q4 GEMV + GELU*up, 53% of the weight bytes)
+    timed alone through ch_fused_mlp_q4 with CUDA events on the library stream, rotating
+    over every layer's weights so no launch finds its 66 MB in L2."""
+    import torch
+    from channel_b200 import _lib as L
+    lib = L.load()
+    H, I = cfg.hidden_size, cfg.intermediate_size
+    xbuf = torch.randn(H, device="cuda", dtype=torch.float32)
+    ybuf = torch.empty(I, device="cuda", dtype=torch.float32)
+    tiles = [gm.weight_tiles(l, 2)[0] for l in range(cfg.num_hidden_layers)]
+    torch.cuda.synchronize()
+    for l in range(len(tiles)):
+        L.check(lib.ch_fused_mlp_q4(ctx.handle, tiles[l], I, H, xbuf.data_ptr(), ybuf.data_ptr()))
+    n = reps * len(tiles)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ctx.synchronize()
+    e0.record(stream)
+    for i in range(n):
+        L.check(lib.ch_fused_mlp_q4(ctx.handle, tiles[i % len(tiles)], I, H, xbuf.data_ptr(), ybuf.data_ptr()))
+    e1.record(stream)
+    e1.synchronize()
+    k_ms = e0.elapsed_time(e1) / n
+    nbytes = 2 * I * H * 18 // 32 + H * 4 + I * 4
+    peak, peak_kind = peaks()
+    achieved = nbytes / (k_ms / 1000.0) / 1e9
+    traffic = None
+    tp = ROOT / "profiles" / "gemv_gateup_traffic.json"
+    if tp.exists():
+        traffic = json.loads(tp.read_text()).get("bytes_per_launch")
+    return {"bound": "hbm", "kernel": "gemv_kernel<Q4, GELU_MUL> (fused gate/up, 2x15360x3840)",
+            "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak, "traffic": traffic,
+            "bytes_per_launch": nbytes, "us_per_launch": k_ms * 1000, "launches_timed": n,
+            "peak_kind": peak_kind + " hbm_gbs (burst; kernel timed alone over {} rotating layers)".format(len(tiles))}
+
+
 def ours(args):
     import torch
 
@@ -210,6 +248,13 @@ def ours(args):
         return slot, ring.getActiveSlotsLayer(0, clock, False, cfg.sliding_window), \
             ring.getActiveSlotsLayer(0, clock, True, cfg.sliding_window)
 
+    if args.kernel_only:
+        r = gateup_roofline(ctx, gm, cfg, stream, reps=3)
+        print(json.dumps({"kernel": "fused gate/up GEMV", **r}), flush=True)
+        gm.deinit()
+        ctx.deinit()
+        return
+
     # ---- value: device-resident loop -------------------------------------------------
     ring, first, prefill_s = fresh_prefill()
     plan = []
@@ -243,28 +288,8 @@ def ours(args):
     # ---- roofline: dominant kernel (fused gate/up GEMV), timed alone over rotating layers
     lib = L.load()
     H, I = cfg.hidden_size, cfg.intermediate_size
-    xbuf = torch.randn(H, device="cuda", dtype=torch.float32)
-    ybuf = torch.empty(I, device="cuda", dtype=torch.float32)
-    tiles = [gm.weight_tiles(l, 2)[0] for l in range(cfg.num_hidden_layers)]
-    torch.cuda.synchronize()
-    for l in range(min(4, len(tiles))):
-        L.check(lib.ch_fused_mlp_q4(ctx.handle, tiles[l], I, H, xbuf.data_ptr(), ybuf.data_ptr()))
-    reps = 3 * len(tiles)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    ctx.synchronize()
-    e0.record(stream)
-    for i in range(reps):
-        L.check(lib.ch_fused_mlp_q4(ctx.handle, tiles[i % len(tiles)], I, H, xbuf.data_ptr(), ybuf.data_ptr()))
-    e1.record(stream)
-    e1.synchronize()
-    k_ms = e0.elapsed_time(e1) / reps
-    gateup_bytes = 2 * I * H * 18 // 32 + H * 4 + I * 4
-    peak, peak_kind = peaks()
-    achieved = gateup_bytes / (k_ms / 1000.0) / 1e9
-    traffic = None
-    tp = ROOT / "profiles" / "gemv_gateup_traffic.json"
-    if tp.exists():
-        traffic = json.loads(tp.read_text()).get("bytes_per_launch")
+    rl = gateup_roofline(ctx, gm, cfg, stream, reps=3)
+    peak = rl["peak"]
     step_bytes = (cfg.num_hidden_layers * ((cfg.q_dim + 2 * cfg.kv_dim) * H + H * cfg.q_dim + 3 * I * H) * 18 // 32
                   + cfg.vocab_size * H * 36 // 32)
     kv_bytes = cfg.num_hidden_layers * 2 * 2 * cfg.kv_dim * (PROMPT + args.warmup + args.steps / 2)
@@ -334,10 +359,7 @@ def ours(args):
                        "global_batch": world, "seq_len": PROMPT + n_total,
                        "parallelism": "replicas" if world > 1 else "single",
                        "l2": "per-step weight stream 7.2 GB > 126 MB L2 (no flush needed)"},
-            "roofline": {"bound": "hbm", "kernel": "gemv_kernel<Q4, GELU_MUL, ADD_RMSNORM> (fused gate/up)",
-                         "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                         "traffic": traffic, "bytes_per_launch": gateup_bytes, "us_per_launch": k_ms * 1000,
-                         "peak_kind": peak_kind + " (hbm_gbs, kernel timed alone over 48 rotating layers)"},
+            "roofline": rl,
             "step_roofline": {"bytes_per_step": step_bytes + kv_bytes, "achieved_gbs": step_gbs,
                               "frac": step_gbs / peak},
             "cpu_baseline": cpu,

@@ -11,10 +11,13 @@
 // the tiny norm + RoPE of q/k/v for that head itself (so no separate launch),
 // streams its slice of the gathered f16 K/V rows with 16-byte loads, keeps
 // per-chunk max / sum / weighted V, and the last CTA of each kv head combines
-// the chunk partials in fixed order (deterministic).  The fresh K/V of the
-// current slot are used from shared memory, so no CTA reads a cache row that
-// another CTA of the same launch is writing.  RoPE angles: inv_freq comes from
-// the host table, cos/sin are evaluated in double and rounded once.
+// the chunk partials in fixed order (deterministic).  The split count adapts to
+// the list length (>= 64 slots per CTA).  The fresh K/V of the current slot are
+// used from shared memory, so no CTA reads a cache row that another CTA of the
+// same launch is writing.  RoPE (cos, sin) for the step's clock come from a
+// table computed once per step (double precision, rounded once).
+#include <algorithm>
+
 #include "common.cuh"
 #include "kernels.cuh"
 
@@ -37,9 +40,14 @@ size_t attn_partial_floats(uint32_t nkv, uint32_t ratio, uint32_t D, int splits)
   return (size_t)nkv * splits * ratio * (D + 2);
 }
 
-// normalize one head with a warp: out = rope(rmsnorm(in) * w) (w == nullptr -> unit norm, no rope)
-CH_DEV void head_norm_rope(const float *in, const float *w, float *out, uint32_t D, uint32_t rot, const float *inv_freq,
-                           uint32_t clock, float eps, bool rope, int lane) {
+namespace {
+constexpr uint32_t kMinChunk = 64;  // slots per CTA before splitting further stops paying
+}
+
+// One warp normalizes one head held in shared memory (in -> out, may alias):
+// rope: out = rope(rmsnorm(in) * w) with the (cos, sin) table; else unit rmsnorm.
+CH_DEV void head_norm_rope_s(const float *in, const float *w, float *out, uint32_t D, uint32_t rot, const float2 *cs,
+                             float eps, bool rope, int lane) {
   float ss = 0.f;
   for (uint32_t d = lane; d < D; d += 32) ss = __fmaf_rn(in[d], in[d], ss);
   ss = warp_sum(ss);
@@ -52,26 +60,24 @@ CH_DEV void head_norm_rope(const float *in, const float *w, float *out, uint32_t
   for (uint32_t d = lane; d < half; d += 32) {
     const float v0 = __fmul_rn(__fmul_rn(in[d], inv), w[d]);
     const float v1 = __fmul_rn(__fmul_rn(in[d + half], inv), w[d + half]);
-    const float ang = __fmul_rn((float)clock, inv_freq[d]);
-    double sd, cd;
-    sincos((double)ang, &sd, &cd);
-    const float c = (float)cd, s = (float)sd;
-    out[d] = __fsub_rn(__fmul_rn(v0, c), __fmul_rn(v1, s));
-    out[d + half] = __fadd_rn(__fmul_rn(v0, s), __fmul_rn(v1, c));
+    const float2 c = cs[d];
+    out[d] = __fsub_rn(__fmul_rn(v0, c.x), __fmul_rn(v1, c.y));
+    out[d + half] = __fadd_rn(__fmul_rn(v0, c.y), __fmul_rn(v1, c.x));
   }
   for (uint32_t d = rot + lane; d < D; d += 32) out[d] = __fmul_rn(__fmul_rn(in[d], inv), w[d]);
 }
 
 template <int R>
-__global__ void __launch_bounds__(kAttnThreads) decode_attn_kernel(const AttnArgs a, int splits, int chunk_cap) {
+__global__ void __launch_bounds__(kAttnThreads) decode_attn_kernel(const AttnArgs a, int max_splits, int chunk_cap) {
   constexpr int D = 256, EPL = D / 32;  // elements per lane
   extern __shared__ __align__(16) float sm[];
-  float *q_s = sm;                       // [R][D]
-  float *k_new = q_s + R * D;            // [D]
-  float *v_new = k_new + D;              // [D]
-  float *o_s = v_new + D;                // [warps][R][D]
-  float *sc = o_s + kAttnWarps * R * D;  // [R][chunk_cap]
-  __shared__ float red[kAttnWarps];
+  float *raw = sm;                        // [R+2][D] staged raw q heads | k | v
+  float *q_s = raw;                       // normalized in place: [R][D]
+  float *k_new = raw + R * D;             // [D]
+  float *v_new = k_new + D;               // [D]
+  float *o_s = v_new + D;                 // [warps][R][D]
+  float *sc = o_s + kAttnWarps * R * D;   // [R][chunk_cap]
+  float *cmb = sc + R * chunk_cap;        // [R][max_splits] combine factors
   __shared__ float stat[2 * kMaxRatio];
   __shared__ uint32_t last_flag;
 
@@ -83,8 +89,12 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attn_kernel(const AttnArg
   const StepParams sp = *a.sp;
   const uint32_t S = a.is_sliding ? sp.n_sliding : sp.n_active;
   const uint32_t *list = a.is_sliding ? sp.sliding : sp.active;
-  const uint32_t c0 = (uint32_t)(((uint64_t)S * split) / splits), c1 = (uint32_t)(((uint64_t)S * (split + 1)) / splits);
-  const uint32_t n = c1 - c0;
+  // adaptive split: at least kMinChunk slots per CTA, at most max_splits CTAs per kv head
+  const uint32_t chunk = max(kMinChunk, (S + max_splits - 1) / (uint32_t)max_splits);
+  const uint32_t nsplit = S == 0 ? 1u : (S + chunk - 1) / chunk;
+  if (split >= nsplit) return;  // idle CTA (exits count as the PDL trigger)
+  const uint32_t c0 = split * chunk, c1 = min(S, c0 + chunk);
+  const uint32_t n = c1 > c0 ? c1 - c0 : 0;
 
   // warm L2 with this CTA's K/V rows while the projections finish
   for (uint32_t i = c0 + tid; i < c1; i += kAttnThreads) {
@@ -100,27 +110,28 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attn_kernel(const AttnArg
   }
   grid_dep_wait();
 
-  // ---- q/k/v norm + rope for this kv head (qkv_rope.wgsl) ----
-  const float *qraw = a.qkv;
+  // ---- stage q heads | k | v of this kv head (one round trip), then norm + rope ----
   const float *kraw = a.qkv + (size_t)a.nq * D;
-  const float *vraw = kraw + kv_dim;
+  for (int idx = tid; idx < (R + 2) * (D / 4); idx += kAttnThreads) {
+    const int h = idx / (D / 4), f = idx % (D / 4);
+    const float *src = h < R ? a.qkv + (size_t)(kvh * R + h) * D : (h == R ? kraw : kraw + kv_dim) + (size_t)kvh * D;
+    reinterpret_cast<float4 *>(raw + h * D)[f] = reinterpret_cast<const float4 *>(src)[f];
+  }
+  __syncthreads();
   for (int h = warp; h < R + 2; h += kAttnWarps) {
-    if (h < R) {
-      head_norm_rope(qraw + (size_t)(kvh * R + h) * D, a.q_norm_w, q_s + h * D, D, a.rot, a.inv_freq, sp.clock, a.eps,
-                     true, lane);
-    } else if (h == R) {
-      head_norm_rope(kraw + (size_t)kvh * D, a.k_norm_w, k_new, D, a.rot, a.inv_freq, sp.clock, a.eps, true, lane);
-      for (uint32_t d = lane; d < D; d += 32) {
-        __half hk = __float2half_rn(k_new[d]);
-        k_new[d] = __half2float(hk);
-        if (split == 0 && sp.slot < a.cache_slots) a.k_cache[(size_t)sp.slot * kv_dim + (size_t)kvh * D + d] = hk;
-      }
+    float *hd = raw + h * D;
+    if (h <= R) {
+      head_norm_rope_s(hd, h < R ? a.q_norm_w : a.k_norm_w, hd, D, a.rot, a.rope_cs, a.eps, true, lane);
     } else {
-      head_norm_rope(vraw + (size_t)kvh * D, nullptr, v_new, D, a.rot, nullptr, 0, a.eps, false, lane);
+      head_norm_rope_s(hd, nullptr, hd, D, a.rot, nullptr, a.eps, false, lane);
+    }
+    __syncwarp();
+    if (h >= R) {  // round the new K / V to the cache's f16 and write them (split 0 only)
+      __half *dst = (h == R ? a.k_cache : a.v_cache) + (size_t)sp.slot * kv_dim + (size_t)kvh * D;
       for (uint32_t d = lane; d < D; d += 32) {
-        __half hv = __float2half_rn(v_new[d]);
-        v_new[d] = __half2float(hv);
-        if (split == 0 && sp.slot < a.cache_slots) a.v_cache[(size_t)sp.slot * kv_dim + (size_t)kvh * D + d] = hv;
+        const __half hv = __float2half_rn(hd[d]);
+        hd[d] = __half2float(hv);
+        if (split == 0 && sp.slot < a.cache_slots) dst[d] = hv;
       }
     }
   }
@@ -143,8 +154,8 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attn_kernel(const AttnArg
 #pragma unroll
       for (int e = 0; e < EPL; e++) kv[e] = k_new[lane * EPL + e];
     } else if (phys < a.cache_slots) {
-      const uint4 raw = *reinterpret_cast<const uint4 *>(a.k_cache + (size_t)phys * kv_dim + (size_t)kvh * D + lane * EPL);
-      const __half2 *hp = reinterpret_cast<const __half2 *>(&raw);
+      const uint4 rw = *reinterpret_cast<const uint4 *>(a.k_cache + (size_t)phys * kv_dim + (size_t)kvh * D + lane * EPL);
+      const __half2 *hp = reinterpret_cast<const __half2 *>(&rw);
 #pragma unroll
       for (int e = 0; e < EPL / 2; e++) {
         float2 f = __half22float2(hp[e]);
@@ -168,37 +179,24 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attn_kernel(const AttnArg
   }
   __syncthreads();
 
-  // ---- chunk max / exp / sum per q head ----
-  for (int h = 0; h < R; h++) {
-    float m = -1e9f;
-    for (uint32_t i = tid; i < n; i += kAttnThreads) m = fmaxf(m, sc[h * chunk_cap + i]);
+  // ---- chunk max / exp / sum per q head (warp h handles head h) ----
+  for (int h = warp; h < R; h += kAttnWarps) {
+    float m = -1e9f;  // decode_attn.wgsl:261
+    for (uint32_t i = lane; i < n; i += 32) m = fmaxf(m, sc[h * chunk_cap + i]);
     m = warp_max(m);
-    if (lane == 0) red[warp] = m;
-    __syncthreads();
-    if (tid == 0) {
-      float mm = red[0];
-      for (int w = 1; w < kAttnWarps; w++) mm = fmaxf(mm, red[w]);
-      stat[2 * h] = mm;
-    }
-    __syncthreads();
-    const float mh = stat[2 * h];
     float l = 0.f;
-    for (uint32_t i = tid; i < n; i += kAttnThreads) {
-      float e = expf(__fsub_rn(sc[h * chunk_cap + i], mh));
+    for (uint32_t i = lane; i < n; i += 32) {
+      const float e = expf(__fsub_rn(sc[h * chunk_cap + i], m));
       sc[h * chunk_cap + i] = e;
       l = __fadd_rn(l, e);
     }
     l = warp_sum(l);
-    __syncthreads();
-    if (lane == 0) red[warp] = l;
-    __syncthreads();
-    if (tid == 0) {
-      float ll = 0.f;
-      for (int w = 0; w < kAttnWarps; w++) ll = __fadd_rn(ll, red[w]);
-      stat[2 * h + 1] = ll;
+    if (lane == 0) {
+      stat[2 * h] = m;
+      stat[2 * h + 1] = l;
     }
-    __syncthreads();
   }
+  __syncthreads();
 
   // ---- weighted V ----
   float acc[R][EPL];
@@ -213,8 +211,8 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attn_kernel(const AttnArg
 #pragma unroll
       for (int e = 0; e < EPL; e++) vv[e] = v_new[lane * EPL + e];
     } else if (phys < a.cache_slots) {
-      const uint4 raw = *reinterpret_cast<const uint4 *>(a.v_cache + (size_t)phys * kv_dim + (size_t)kvh * D + lane * EPL);
-      const __half2 *hp = reinterpret_cast<const __half2 *>(&raw);
+      const uint4 rw = *reinterpret_cast<const uint4 *>(a.v_cache + (size_t)phys * kv_dim + (size_t)kvh * D + lane * EPL);
+      const __half2 *hp = reinterpret_cast<const __half2 *>(&rw);
 #pragma unroll
       for (int e = 0; e < EPL / 2; e++) {
         float2 f = __half22float2(hp[e]);
@@ -239,10 +237,11 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attn_kernel(const AttnArg
   __syncthreads();
 
   // ---- partial out: [kvh][split][h] = {o[D], m, l} ----
-  float *part = a.partial + ((size_t)(kvh * splits + split) * R) * (D + 2);
+  float *part = a.partial + ((size_t)(kvh * max_splits + split) * R) * (D + 2);
   for (int idx = tid; idx < R * D; idx += kAttnThreads) {
     const int h = idx / D, d = idx % D;
     float s = 0.f;
+#pragma unroll
     for (int w = 0; w < kAttnWarps; w++) s = __fadd_rn(s, o_s[(w * R + h) * D + d]);
     part[h * (D + 2) + d] = s;
   }
@@ -254,42 +253,61 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attn_kernel(const AttnArg
   __syncthreads();
   if (tid == 0) {
     const uint32_t old = atomicAdd(&a.counters[kvh], 1u);
-    last_flag = (old == (uint32_t)splits - 1) ? 1u : 0u;
+    last_flag = (old == nsplit - 1) ? 1u : 0u;
   }
   __syncthreads();
   if (!last_flag) return;
   __threadfence();
 
-  // ---- combine (fixed split order) ----
-  const float *base = a.partial + ((size_t)kvh * splits * R) * (D + 2);
+  // ---- combine (fixed split order): factors first, then one pipelined pass ----
+  const float *base = a.partial + ((size_t)kvh * max_splits * R) * (D + 2);
+  for (int idx = tid; idx < R * (int)nsplit; idx += kAttnThreads) {
+    const int h = idx / nsplit, j = idx % nsplit;
+    cmb[h * max_splits + j] = __ldcg(&base[((size_t)j * R + h) * (D + 2) + D]);
+  }
+  __syncthreads();
+  if (tid < R) {
+    float M = -INFINITY, L = 0.f;
+    for (uint32_t j = 0; j < nsplit; j++) M = fmaxf(M, cmb[tid * max_splits + j]);
+    for (uint32_t j = 0; j < nsplit; j++) {
+      const float f = expf(__fsub_rn(cmb[tid * max_splits + j], M));
+      L = __fmaf_rn(__ldcg(&base[((size_t)j * R + tid) * (D + 2) + D + 1]), f, L);
+      cmb[tid * max_splits + j] = f;
+    }
+    stat[2 * tid] = __fdiv_rn(1.0f, __fadd_rn(L, 1e-9f));
+  }
+  __syncthreads();
   for (int idx = tid; idx < R * D; idx += kAttnThreads) {
     const int h = idx / D, d = idx % D;
-    float M = -INFINITY;
-    for (int sp_i = 0; sp_i < splits; sp_i++) M = fmaxf(M, __ldcg(&base[((size_t)sp_i * R + h) * (D + 2) + D]));
-    float L = 0.f, O = 0.f;
-    for (int sp_i = 0; sp_i < splits; sp_i++) {
-      const float *p = base + ((size_t)sp_i * R + h) * (D + 2);
-      const float f = expf(__fsub_rn(__ldcg(&p[D]), M));
-      L = __fmaf_rn(__ldcg(&p[D + 1]), f, L);
-      O = __fmaf_rn(__ldcg(&p[d]), f, O);
+    float O = 0.f;
+    uint32_t j = 0;
+    for (; j + 4 <= nsplit; j += 4) {
+      const float p0 = __ldcg(&base[((size_t)(j + 0) * R + h) * (D + 2) + d]);
+      const float p1 = __ldcg(&base[((size_t)(j + 1) * R + h) * (D + 2) + d]);
+      const float p2 = __ldcg(&base[((size_t)(j + 2) * R + h) * (D + 2) + d]);
+      const float p3 = __ldcg(&base[((size_t)(j + 3) * R + h) * (D + 2) + d]);
+      O = __fmaf_rn(p0, cmb[h * max_splits + j], O);
+      O = __fmaf_rn(p1, cmb[h * max_splits + j + 1], O);
+      O = __fmaf_rn(p2, cmb[h * max_splits + j + 2], O);
+      O = __fmaf_rn(p3, cmb[h * max_splits + j + 3], O);
     }
-    const float inv = __fdiv_rn(1.0f, __fadd_rn(L, 1e-9f));
-    a.out[(size_t)(kvh * R + h) * D + d] = __fmul_rn(O, inv);
+    for (; j < nsplit; j++) O = __fmaf_rn(__ldcg(&base[((size_t)j * R + h) * (D + 2) + d]), cmb[h * max_splits + j], O);
+    a.out[(size_t)(kvh * R + h) * D + d] = __fmul_rn(O, stat[2 * h]);
   }
   if (tid == 0) a.counters[kvh] = 0u;
 }
 
 template <int R>
 static cudaError_t launch_attn_t(const AttnArgs &a, int splits, cudaStream_t s, bool pdl) {
-  const int chunk_cap = (int)((a.cache_slots + splits - 1) / splits) + 1;
-  const size_t smem = sizeof(float) * ((size_t)R * 256 + 2 * 256 + (size_t)kAttnWarps * R * 256 + (size_t)R * chunk_cap);
-  static bool attr_done = false;
-  if (!attr_done) {
-    cudaError_t e = cudaFuncSetAttribute(decode_attn_kernel<R>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+  const int chunk_cap = (int)std::max<uint32_t>(kMinChunk, (a.cache_slots + splits - 1) / splits);
+  const size_t smem = sizeof(float) * ((size_t)(R + 2) * 256 + (size_t)kAttnWarps * R * 256 + (size_t)R * chunk_cap +
+                                       (size_t)R * splits);
+  static size_t attr_bytes = 0;  // dynamic smem opt-in granted so far
+  if (smem > 48 * 1024 && smem > attr_bytes) {
+    cudaError_t e = cudaFuncSetAttribute(decode_attn_kernel<R>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
-    attr_done = true;
+    attr_bytes = smem;
   }
-  if (smem > 227 * 1024) return cudaErrorInvalidValue;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(a.nkv, splits);
   cfg.blockDim = dim3(kAttnThreads);

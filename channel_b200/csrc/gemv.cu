@@ -24,8 +24,8 @@
 namespace ch {
 
 namespace {
-constexpr int NW = 8;    // consumer warps per CTA (each self-feeds its own stages)
-constexpr int SPW = 4;   // stages per warp
+constexpr int NW = 16;   // consumer warps per CTA (each self-feeds its own stages)
+constexpr int SPW = 2;   // stages per warp
 constexpr int CT = 8;    // tiles per stage (4608 B per bulk copy)
 constexpr int kStageBytes = CT * kTileBytes;
 }  // namespace
@@ -70,112 +70,141 @@ CH_DEV void epilogue(float *y, uint32_t rt, int g, float v0, float v1) {
 
 // ---------------------------------------------------------------------------
 // prologue: build the f16 hi/lo B fragments of the (optionally normed) input.
-// xf layout: [chunk of 16 k][t 0..3][hi|lo] uint2 {b0, b1}.
-CH_DEV void to_fragments(const float *v, uint2 *xf, uint32_t K) {
-  uint32_t n = (K / 16) * 4;
-  for (uint32_t idx = threadIdx.x; idx < n; idx += blockDim.x) {
-    uint32_t c = idx >> 2, t = idx & 3, base = c * 16 + 2 * t;
-    float v0 = v[base], v1 = v[base + 1], v2 = v[base + 8], v3 = v[base + 9];
-    __half h0 = __float2half_rn(v0), h1 = __float2half_rn(v1), h2 = __float2half_rn(v2), h3 = __float2half_rn(v3);
-    __half l0 = __float2half_rn(__fsub_rn(v0, __half2float(h0)));
-    __half l1 = __float2half_rn(__fsub_rn(v1, __half2float(h1)));
-    __half l2 = __float2half_rn(__fsub_rn(v2, __half2float(h2)));
-    __half l3 = __float2half_rn(__fsub_rn(v3, __half2float(h3)));
-    xf[c * 8 + t * 2 + 0] = make_uint2(pack_half2(h0, h1), pack_half2(h2, h3));
-    xf[c * 8 + t * 2 + 1] = make_uint2(pack_half2(l0, l1), pack_half2(l2, l3));
+// xf layout: [32-k block][t 0..3][g 0 = hi | 1 = lo] uint4 {c0.b0, c0.b1, c1.b0, c1.b1}
+// (c0 / c1 = the block's two k16 chunks).  One thread per block; every load of a
+// phase is issued before any is used, so a phase costs one L2 round trip.
+CH_DEV void block_to_fragments(const float (&v)[32], uint4 *xf_blk) {
+  float lo[32];
+#pragma unroll
+  for (int e = 0; e < 32; e++) lo[e] = __fsub_rn(v[e], __half2float(__float2half_rn(v[e])));
+#pragma unroll
+  for (int t = 0; t < 4; t++) {
+    uint32_t hw[4], lw[4];
+#pragma unroll
+    for (int c = 0; c < 2; c++) {
+      const int k0 = c * 16 + 2 * t;
+      hw[c * 2 + 0] = pack_half2(__float2half_rn(v[k0]), __float2half_rn(v[k0 + 1]));
+      hw[c * 2 + 1] = pack_half2(__float2half_rn(v[k0 + 8]), __float2half_rn(v[k0 + 9]));
+      lw[c * 2 + 0] = pack_half2(__float2half_rn(lo[k0]), __float2half_rn(lo[k0 + 1]));
+      lw[c * 2 + 1] = pack_half2(__float2half_rn(lo[k0 + 8]), __float2half_rn(lo[k0 + 9]));
+    }
+    xf_blk[t * 2 + 0] = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+    xf_blk[t * 2 + 1] = make_uint4(lw[0], lw[1], lw[2], lw[3]);
   }
+}
+CH_DEV void load32(const float *p, float (&v)[32]) {
+  const float4 *q = reinterpret_cast<const float4 *>(p);
+#pragma unroll
+  for (int i = 0; i < 8; i++) {
+    const float4 f = q[i];
+    v[4 * i] = f.x, v[4 * i + 1] = f.y, v[4 * i + 2] = f.z, v[4 * i + 3] = f.w;
+  }
+}
+CH_DEV void store32(float *p, const float (&v)[32]) {
+  float4 *q = reinterpret_cast<float4 *>(p);
+#pragma unroll
+  for (int i = 0; i < 8; i++) q[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
 }
 
 template <int PRO>
-CH_DEV void prologue(const GemvArgs &a, float *vec, uint2 *xf, float *red) {
-  const uint32_t K = a.K;
+CH_DEV void prologue(const GemvArgs &a, float *vec, uint4 *xf, float *red) {
+  const uint32_t K = a.K, nb = K / 32;
   if (PRO == PRO_NONE) {
-    to_fragments(a.x, xf, K);
+    for (uint32_t b = threadIdx.x; b < nb; b += blockDim.x) {
+      float v[32];
+      load32(a.x + b * 32, v);
+      block_to_fragments(v, xf + b * 8);
+    }
     return;
   }
   const bool writer = (blockIdx.x == 0);
+  float ss = 0.0f;
   if (PRO == PRO_RMSNORM) {
-    float ss = 0.0f;
-    for (uint32_t i = threadIdx.x; i < K; i += blockDim.x) {
-      float v = a.x[i];
-      vec[i] = v;
-      ss = __fmaf_rn(v, v, ss);
+    for (uint32_t b = threadIdx.x; b < nb; b += blockDim.x) {
+      float v[32];
+      load32(a.x + b * 32, v);
+#pragma unroll
+      for (int e = 0; e < 32; e++) ss = __fmaf_rn(v[e], v[e], ss);
+      store32(vec + b * 32, v);
     }
-    ss = block_sum(ss, red);
-    float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)K), a.eps)));
-    for (uint32_t i = threadIdx.x; i < K; i += blockDim.x) {
-      float v = __fmul_rn(__fmul_rn(vec[i], inv), a.norm_w[i]);
-      vec[i] = v;
-      if (writer && a.normed_out) a.normed_out[i] = v;
-    }
-  } else {  // PRO_ADD_RMSNORM: r' = post_w ? rmsnorm(r) : r ; x = (x_in + r') * scalar ; y = rmsnorm(x) * w
+  } else {  // PRO_ADD_RMSNORM: r' = post_w ? rmsnorm(r) * post_w : r ; x = (x_in + r') * scalar
+    float inv_r = 1.0f;
     if (a.post_w) {
-      float ss = 0.0f;
-      for (uint32_t i = threadIdx.x; i < K; i += blockDim.x) {
-        float v = a.r[i];
-        vec[i] = v;
-        ss = __fmaf_rn(v, v, ss);
+      float sr = 0.0f;
+      for (uint32_t b = threadIdx.x; b < nb; b += blockDim.x) {
+        float v[32];
+        load32(a.r + b * 32, v);
+#pragma unroll
+        for (int e = 0; e < 32; e++) sr = __fmaf_rn(v[e], v[e], sr);
       }
-      ss = block_sum(ss, red);
-      float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)K), a.eps)));
-      for (uint32_t i = threadIdx.x; i < K; i += blockDim.x) vec[i] = __fmul_rn(__fmul_rn(vec[i], inv), a.post_w[i]);
-    } else {
-      for (uint32_t i = threadIdx.x; i < K; i += blockDim.x) vec[i] = a.r[i];
+      sr = block_sum(sr, red);
+      inv_r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sr, (float)K), a.eps)));
     }
-    float ss = 0.0f;
-    for (uint32_t i = threadIdx.x; i < K; i += blockDim.x) {
-      float v = __fmul_rn(__fadd_rn(a.x[i], vec[i]), a.scalar);
-      vec[i] = v;
-      if (writer && a.x_out) a.x_out[i] = v;
-      ss = __fmaf_rn(v, v, ss);
-    }
-    ss = block_sum(ss, red);
-    float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)K), a.eps)));
-    for (uint32_t i = threadIdx.x; i < K; i += blockDim.x) {
-      float v = __fmul_rn(__fmul_rn(vec[i], inv), a.norm_w[i]);
-      vec[i] = v;
-      if (writer && a.normed_out) a.normed_out[i] = v;
+    for (uint32_t b = threadIdx.x; b < nb; b += blockDim.x) {
+      float r[32], x[32], w[32];
+      load32(a.r + b * 32, r);
+      load32(a.x + b * 32, x);
+      if (a.post_w) load32(a.post_w + b * 32, w);
+#pragma unroll
+      for (int e = 0; e < 32; e++) {
+        const float rr = a.post_w ? __fmul_rn(__fmul_rn(r[e], inv_r), w[e]) : r[e];
+        x[e] = __fmul_rn(__fadd_rn(x[e], rr), a.scalar);
+        ss = __fmaf_rn(x[e], x[e], ss);
+      }
+      store32(vec + b * 32, x);
+      if (writer && a.x_out) store32(a.x_out + b * 32, x);
     }
   }
-  __syncthreads();
-  to_fragments(vec, xf, K);
+  ss = block_sum(ss, red);
+  const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)K), a.eps)));
+  for (uint32_t b = threadIdx.x; b < nb; b += blockDim.x) {
+    float v[32], w[32];
+    load32(vec + b * 32, v);
+    load32(a.norm_w + b * 32, w);
+#pragma unroll
+    for (int e = 0; e < 32; e++) v[e] = __fmul_rn(__fmul_rn(v[e], inv), w[e]);
+    if (writer && a.normed_out) store32(a.normed_out + b * 32, v);
+    block_to_fragments(v, xf + b * 8);
+  }
 }
 
-// one 576-byte tile: 16 rows; lanes with t == 0 accumulate rows g and g+8
+// one 576-byte tile: 16 rows; lanes with t == 0 accumulate rows g and g+8.
+// xb: this lane's x-fragment base (hi for g == 0, lo for g == 1, a zero page for
+// g >= 2) and xs its block stride (8 or 0 uint4).
 template <int FMT>
-CH_DEV void tile_mma(const uint8_t *tile, uint32_t kt, const uint2 *xf, int lane, float &acc0, float &acc1) {
-  const int g = lane >> 2, t = lane & 3;
+CH_DEV void tile_mma(const uint8_t *tile, uint32_t kt, const uint4 *xb, uint32_t xs, int lane, float &acc0,
+                     float &acc1) {
+  const int g = lane >> 2;
   const uint4 w = *reinterpret_cast<const uint4 *>(tile + lane * 16);
   if (FMT == FMT_Q4) {
     const uint2 sc = *reinterpret_cast<const uint2 *>(tile + 512 + g * 8);
-    const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-    for (int blk = 0; blk < 2; blk++) {
-      float d[4] = {0.f, 0.f, 0.f, 0.f};
-      uint32_t af[4];
-#pragma unroll
-      for (int ch = 0; ch < 2; ch++) {
-        const uint32_t c = kt * 4 + blk * 2 + ch;
-        const uint2 b = (g < 2) ? xf[c * 8 + t * 2 + g] : make_uint2(0u, 0u);
-        dequant_q4_word(ws[blk * 2 + ch], af);
-        mma_16816(d, af, b.x, b.y);
-      }
-      const float s0 = __half2float(__ushort_as_half((unsigned short)((blk ? sc.x >> 16 : sc.x) & 0xFFFFu)));
-      const float s1 = __half2float(__ushort_as_half((unsigned short)((blk ? sc.y >> 16 : sc.y) & 0xFFFFu)));
-      acc0 = __fmaf_rn(s0, __fadd_rn(d[0], d[1]), acc0);
-      acc1 = __fmaf_rn(s1, __fadd_rn(d[2], d[3]), acc1);
-    }
+    const uint4 b0 = xb[(kt * 2 + 0) * xs], b1 = xb[(kt * 2 + 1) * xs];
+    float d0[4] = {0.f, 0.f, 0.f, 0.f}, d1[4] = {0.f, 0.f, 0.f, 0.f};
+    uint32_t af[4];
+    dequant_q4_word(w.x, af);
+    mma_16816(d0, af, b0.x, b0.y);
+    dequant_q4_word(w.z, af);
+    mma_16816(d1, af, b1.x, b1.y);
+    dequant_q4_word(w.y, af);
+    mma_16816(d0, af, b0.z, b0.w);
+    dequant_q4_word(w.w, af);
+    mma_16816(d1, af, b1.z, b1.w);
+    const __half2 s_lo = *reinterpret_cast<const __half2 *>(&sc.x);  // (row g: blk0, blk1)
+    const __half2 s_hi = *reinterpret_cast<const __half2 *>(&sc.y);  // (row g+8: blk0, blk1)
+    const float2 fg = __half22float2(s_lo), fg8 = __half22float2(s_hi);
+    acc0 = __fmaf_rn(fg.x, __fadd_rn(d0[0], d0[1]), acc0);
+    acc1 = __fmaf_rn(fg8.x, __fadd_rn(d0[2], d0[3]), acc1);
+    acc0 = __fmaf_rn(fg.y, __fadd_rn(d1[0], d1[1]), acc0);
+    acc1 = __fmaf_rn(fg8.y, __fadd_rn(d1[2], d1[3]), acc1);
   } else {
     const float2 sc = *reinterpret_cast<const float2 *>(tile + 512 + g * 8);
+    const uint4 b = xb[kt * xs];
     float d[4] = {0.f, 0.f, 0.f, 0.f};
     uint32_t af[4];
-#pragma unroll
-    for (int ch = 0; ch < 2; ch++) {
-      const uint32_t c = kt * 2 + ch;
-      const uint2 b = (g < 2) ? xf[c * 8 + t * 2 + g] : make_uint2(0u, 0u);
-      dequant_q8_words(ch ? w.z : w.x, ch ? w.w : w.y, af);
-      mma_16816(d, af, b.x, b.y);
-    }
+    dequant_q8_words(w.x, w.y, af);
+    mma_16816(d, af, b.x, b.y);
+    dequant_q8_words(w.z, w.w, af);
+    mma_16816(d, af, b.z, b.w);
     acc0 = __fmaf_rn(sc.x, __fadd_rn(d[0], d[1]), acc0);
     acc1 = __fmaf_rn(sc.y, __fadd_rn(d[2], d[3]), acc1);
   }
@@ -186,8 +215,9 @@ __global__ void __launch_bounds__(NW * 32, 1) gemv_kernel(const GemvArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
   uint8_t *stages = smem;
   uint64_t *bars = reinterpret_cast<uint64_t *>(smem + NW * SPW * kStageBytes);
-  uint2 *xf = reinterpret_cast<uint2 *>(smem + NW * SPW * kStageBytes + NW * SPW * 8);
-  float *vec = reinterpret_cast<float *>(reinterpret_cast<uint8_t *>(xf) + (a.K / 16) * 64);
+  uint4 *xzero = reinterpret_cast<uint4 *>(smem + NW * SPW * kStageBytes + NW * SPW * 8);
+  uint4 *xf = xzero + 1;
+  float *vec = reinterpret_cast<float *>(xf + (a.K / 32) * 8);
   __shared__ float red[32];
 
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -212,6 +242,7 @@ __global__ void __launch_bounds__(NW * 32, 1) gemv_kernel(const GemvArgs a) {
       bulk_g2s(my_stages + (size_t)j * kStageBytes, a.tiles + t0 * kTileBytes, bytes, &my_bars[j]);
     }
   }
+  if (threadIdx.x == 0) *xzero = make_uint4(0u, 0u, 0u, 0u);
   __syncwarp();
 
   grid_dep_wait();
@@ -219,18 +250,19 @@ __global__ void __launch_bounds__(NW * 32, 1) gemv_kernel(const GemvArgs a) {
   __syncthreads();
   grid_dep_launch();
 
-  uint64_t cur_rt = ~0ull;
+  const uint4 *xb = (g < 2) ? xf + t * 2 + g : xzero;
+  const uint32_t xs = (g < 2) ? 8u : 0u;
+  uint64_t cur_rt = ~0ull, rt = 0;
   uint32_t kt_begin = 0, kt = 0;
-  uint64_t rt = 0;
-  float acc0 = 0.f, acc1 = 0.f;
+  float a0 = 0.f, a1 = 0.f, b0 = 0.f, b1 = 0.f;  // two accumulator chains (even / odd tiles)
   bool first_seg = true;
-  bool ok = true;
   if (nchunks > 0) {
     rt = tb / KT;
     kt = (uint32_t)(tb - rt * KT);
   }
 
   auto flush = [&](uint64_t frt, uint32_t kb, uint32_t ke) {
+    const float acc0 = __fadd_rn(a0, b0), acc1 = __fadd_rn(a1, b1);
     const bool full = (kb == 0 && ke == (uint32_t)KT);
     if (full) {
       if (t == 0) epilogue<EPI>(a.y, (uint32_t)frt, g, acc0, acc1);
@@ -267,7 +299,8 @@ __global__ void __launch_bounds__(NW * 32, 1) gemv_kernel(const GemvArgs a) {
   };
 
   uint32_t failed_at = 0;
-  for (uint32_t j = 0; j < nchunks && ok; j++) {
+  bool ok = true;
+  for (uint32_t j = 0; j < nchunks; j++) {
     const int s = j % SPW;
     if (!mbar_wait_bounded(&my_bars[s], (j / SPW) & 1, a.err)) {
       ok = false;
@@ -277,15 +310,38 @@ __global__ void __launch_bounds__(NW * 32, 1) gemv_kernel(const GemvArgs a) {
     const uint8_t *st = my_stages + (size_t)s * kStageBytes;
     const uint64_t t0 = tb + (uint64_t)j * CT;
     const uint32_t nt = (uint32_t)min((uint64_t)CT, te - t0);
-    for (uint32_t i = 0; i < nt; i++) {
+    uint32_t i = 0;
+    while (i < nt) {
       if (rt != cur_rt) {
         if (cur_rt != ~0ull) flush(cur_rt, kt_begin, (uint32_t)KT);
         cur_rt = rt;
         kt_begin = kt;
-        acc0 = acc1 = 0.f;
+        a0 = a1 = b0 = b1 = 0.f;
       }
-      tile_mma<FMT>(st + (size_t)i * kTileBytes, kt, xf, lane, acc0, acc1);
-      if (++kt == (uint32_t)KT) {
+      // a run of tiles inside one row tile: no per-tile boundary checks
+      const uint32_t run = min(nt - i, (uint32_t)KT - kt);
+      const uint8_t *p = st + (size_t)i * kTileBytes;
+      uint32_t r = 0;
+      if (run == CT) {
+#pragma unroll
+        for (int q = 0; q < CT; q += 2) {
+          tile_mma<FMT>(p + q * kTileBytes, kt + q, xb, xs, lane, a0, a1);
+          tile_mma<FMT>(p + (q + 1) * kTileBytes, kt + q + 1, xb, xs, lane, b0, b1);
+        }
+        r = CT;
+      } else {
+        for (; r + 2 <= run; r += 2) {
+          tile_mma<FMT>(p + r * kTileBytes, kt + r, xb, xs, lane, a0, a1);
+          tile_mma<FMT>(p + (r + 1) * kTileBytes, kt + r + 1, xb, xs, lane, b0, b1);
+        }
+        if (r < run) {
+          tile_mma<FMT>(p + r * kTileBytes, kt + r, xb, xs, lane, a0, a1);
+          r++;
+        }
+      }
+      i += run;
+      kt += run;
+      if (kt == (uint32_t)KT) {
         kt = 0;
         rt++;
       }
@@ -313,16 +369,15 @@ __global__ void __launch_bounds__(NW * 32, 1) gemv_kernel(const GemvArgs a) {
 
 template <int FMT, int EPI, int PRO>
 static cudaError_t launch_gemv_t(const GemvArgs &a, int grid, cudaStream_t s, bool pdl) {
-  size_t smem = (size_t)NW * SPW * kStageBytes + NW * SPW * 8 + (size_t)(a.K / 16) * 64;
+  size_t smem = (size_t)NW * SPW * kStageBytes + NW * SPW * 8 + 16 + (size_t)(a.K / 32) * 128;
   if (PRO != PRO_NONE) smem += (size_t)a.K * 4;
-  static bool attr_done = false;
-  if (!attr_done) {
-    cudaError_t e = cudaFuncSetAttribute(gemv_kernel<FMT, EPI, PRO>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         227 * 1024);
+  static size_t attr_bytes = 0;  // dynamic smem opt-in granted so far (static smem counts against 227 KB)
+  if (smem > 48 * 1024 && smem > attr_bytes) {
+    cudaError_t e =
+        cudaFuncSetAttribute(gemv_kernel<FMT, EPI, PRO>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
-    attr_done = true;
+    attr_bytes = smem;
   }
-  if (smem > 227 * 1024) return cudaErrorInvalidValue;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(NW * 32);

@@ -80,7 +80,7 @@ struct StepParams {
 struct AttnArgs {
   const float *qkv;      // q [nq*D] | k [nkv*D] | v [nkv*D] (raw projections)
   const float *q_norm_w, *k_norm_w;
-  const float *inv_freq;  // [rot/2]
+  const float2 *rope_cs;  // [rot/2] (cos, sin) of clock * inv_freq for this layer's theta
   __half *k_cache, *v_cache;  // [4096][nkv*D]
   const StepParams *sp;
   int is_sliding;
@@ -123,6 +123,9 @@ struct StepBeginArgs {
   const StepParams *plan; // [n_plan]
   uint32_t n_plan;
   uint32_t *err;
+  const float *inv_freq_s, *inv_freq_f;  // [rot/2] each
+  float2 *rope_cs;                       // out: [2][rot/2] (sliding theta, full theta)
+  uint32_t rot_half;
 };
 cudaError_t launch_step_begin(const StepBeginArgs &a, cudaStream_t s, bool pdl);
 

@@ -56,8 +56,8 @@ struct ch_ctx {
   size_t attn_counters_n = 0;
   uint64_t *topk_cand = nullptr;
   uint32_t *topk_counter = nullptr;
-  float *attn_inv_freq = nullptr;
-  size_t attn_inv_freq_n = 0;
+  float2 *attn_rope = nullptr;
+  size_t attn_rope_n = 0;
   StepParams *op_sp = nullptr;
 };
 
@@ -102,7 +102,7 @@ extern "C" void ch_ctx_destroy(ch_ctx *c) {
   cudaFree(c->attn_counters);
   cudaFree(c->topk_cand);
   cudaFree(c->topk_counter);
-  cudaFree(c->attn_inv_freq);
+  cudaFree(c->attn_rope);
   cudaFree(c->op_sp);
   cudaStreamDestroy(c->stream);
   delete c;
@@ -149,6 +149,9 @@ struct ch_model {
   float *final_norm = nullptr;
   uint16_t *embed = nullptr;
   float *inv_freq_s = nullptr, *inv_freq_f = nullptr;
+  std::vector<float> h_inv_s, h_inv_f;  // same tables on the host (per-step RoPE on the host path)
+  float2 *rope_cs = nullptr;            // [2][rot/2] (cos, sin) of the current clock
+  float2 *h_rope = nullptr;             // pinned staging
   // decode buffers
   float *X[2] = {nullptr, nullptr};
   float *normed = nullptr, *qkv = nullptr, *attn = nullptr, *o_out = nullptr, *act = nullptr, *down_out = nullptr,
@@ -202,13 +205,13 @@ static void free_model(ch_model *m) {
     cudaFree(l.kc);
     cudaFree(l.vc);
   }
-  void *dev[] = {m->lm, m->final_norm, m->embed, m->inv_freq_s, m->inv_freq_f, m->X[0], m->X[1], m->normed, m->qkv,
+  void *dev[] = {m->lm, m->final_norm, m->embed, m->inv_freq_s, m->inv_freq_f, m->rope_cs, m->X[0], m->X[1], m->normed, m->qkv,
                  m->attn, m->o_out, m->act, m->down_out, m->logits, m->vals, m->ids, m->token, m->token_hist, m->sp,
                  m->active, m->sliding, m->gemv_partial, m->gemv_counters, m->attn_partial, m->attn_counters,
                  m->topk_cand, m->topk_counter, m->plan, m->plan_lists, m->pX, m->pNX, m->pQKV, m->pQO, m->pA, m->pMO,
                  m->pACT, m->pSlots, m->pTok};
   for (void *p : dev) cudaFree(p);
-  void *host[] = {m->h_x, m->h_sp, m->h_lists, m->h_ids, m->h_vals, m->h_run};
+  void *host[] = {m->h_x, m->h_sp, m->h_lists, m->h_ids, m->h_vals, m->h_run, m->h_rope};
   for (void *p : host) cudaFreeHost(p);
   if (m->g_host_logits) cudaGraphExecDestroy(m->g_host_logits);
   if (m->g_host_nologits) cudaGraphExecDestroy(m->g_host_nologits);
@@ -324,6 +327,10 @@ static int alloc_model_buffers(ch_model *m) {
   }
   CH_CUDA(cudaMemcpy(m->inv_freq_s, fs.data(), fs.size() * 4, cudaMemcpyHostToDevice));
   CH_CUDA(cudaMemcpy(m->inv_freq_f, ff.data(), ff.size() * 4, cudaMemcpyHostToDevice));
+  m->h_inv_s = fs;
+  m->h_inv_f = ff;
+  CH_TRY(dmalloc(&m->rope_cs, c.rotary_dim));
+  CH_CUDA(cudaMallocHost(&m->h_rope, c.rotary_dim * sizeof(float2)));
   return CH_OK;
 }
 
@@ -576,8 +583,9 @@ static cudaError_t enqueue_decode(ch_model *m, cudaStream_t s, bool logits, bool
   base.err = m->ctx->err;
   base.eps = m->cfg.rms_norm_eps;
   if (device_loop) {
-    StepBeginArgs sb{m->embed, m->H, sqrtf((float)m->H), m->token, m->X[0], m->sp, m->plan, m->plan_steps,
-                     m->ctx->err};
+    StepBeginArgs sb{m->embed,      m->H,         sqrtf((float)m->H), m->token,      m->X[0],
+                     m->sp,         m->plan,      m->plan_steps,      m->ctx->err,   m->inv_freq_s,
+                     m->inv_freq_f, m->rope_cs,   m->cfg.rotary_dim / 2};
     if ((e = launch_step_begin(sb, s, pdl)) != cudaSuccess) return e;
   }
   for (uint32_t l = 0; l < m->L; l++) {
@@ -613,7 +621,7 @@ static cudaError_t enqueue_decode(ch_model *m, cudaStream_t s, bool logits, bool
       a.qkv = m->qkv;
       a.q_norm_w = dl.q_norm;
       a.k_norm_w = dl.k_norm;
-      a.inv_freq = dl.full ? m->inv_freq_f : m->inv_freq_s;
+      a.rope_cs = m->rope_cs + (dl.full ? m->cfg.rotary_dim / 2 : 0);
       a.k_cache = dl.kc;
       a.v_cache = dl.vc;
       a.sp = m->sp;
@@ -740,6 +748,15 @@ static int capture(ch_model *m, bool logits, bool device_loop, cudaGraphExec_t *
   return fail(CH_ECUDA, "graph capture failed");
 }
 
+// (cos, sin) of clock * inv_freq[i] for the RoPE of one step: angle in f32 as the
+// shaders form it (qkv_rope.wgsl:74-78), cos/sin in double rounded once
+static void rope_table(const std::vector<float> &inv, uint32_t clock, float2 *out) {
+  for (size_t i = 0; i < inv.size(); i++) {
+    const float ang = (float)clock * inv[i];
+    out[i] = make_float2((float)cos((double)ang), (float)sin((double)ang));
+  }
+}
+
 static int check_lists(const uint32_t *l, uint32_t n) {
   if (n > kSlots) return fail(CH_EINVAL, "slot list longer than 4096");
   if (n && !l) return fail(CH_EINVAL, "NULL slot list");
@@ -770,8 +787,12 @@ extern "C" int ch_forward_token(ch_model *m, const float *x, uint32_t clock, uin
   m->h_sp->step = 0;
   if (n_active) memcpy(m->h_lists, active, n_active * 4);
   if (n_sliding) memcpy(m->h_lists + kSlots, sliding, n_sliding * 4);
+  const uint32_t rh = m->cfg.rotary_dim / 2;
+  rope_table(m->h_inv_s, clock, m->h_rope);
+  rope_table(m->h_inv_f, clock, m->h_rope + rh);
   CH_CUDA(cudaMemcpyAsync(m->X[0], m->h_x, m->H * 4, cudaMemcpyHostToDevice, s));
   CH_CUDA(cudaMemcpyAsync(m->sp, m->h_sp, sizeof(StepParams), cudaMemcpyHostToDevice, s));
+  CH_CUDA(cudaMemcpyAsync(m->rope_cs, m->h_rope, 2 * rh * sizeof(float2), cudaMemcpyHostToDevice, s));
   if (n_active) CH_CUDA(cudaMemcpyAsync(m->active, m->h_lists, n_active * 4, cudaMemcpyHostToDevice, s));
   if (n_sliding) CH_CUDA(cudaMemcpyAsync(m->sliding, m->h_lists + kSlots, n_sliding * 4, cudaMemcpyHostToDevice, s));
   CH_CUDA(cudaGraphLaunch(*g, s));
@@ -1138,25 +1159,27 @@ extern "C" int ch_decode_attention(ch_ctx *c, const float *qkv, const float *q_n
     c->attn_counters_n = nkv;
     CH_CUDA(cudaMemsetAsync(c->attn_counters, 0, nkv * 4, c->stream));
   }
-  if (c->attn_inv_freq_n < rot / 2) {
-    cudaFree(c->attn_inv_freq);
-    c->attn_inv_freq = nullptr;
-    CH_TRY(dmalloc(&c->attn_inv_freq, 128));
-    c->attn_inv_freq_n = 128;
+  if (c->attn_rope_n < rot / 2) {
+    cudaFree(c->attn_rope);
+    c->attn_rope = nullptr;
+    CH_TRY(dmalloc(&c->attn_rope, 128));
+    c->attn_rope_n = 128;
   }
   std::vector<float> f(rot / 2);
   for (uint32_t i = 0; i < rot / 2; i++) {
     float e = (2.0f * (float)i) / (float)rot;
     f[i] = (float)(1.0 / pow((double)theta, (double)e));
   }
+  std::vector<float2> cs(rot / 2);
+  rope_table(f, clock, cs.data());
   StepParams sp{clock, slot, n_slots, n_slots, slots_dev, slots_dev, 0, 0};
-  CH_CUDA(cudaMemcpyAsync(c->attn_inv_freq, f.data(), f.size() * 4, cudaMemcpyHostToDevice, c->stream));
+  CH_CUDA(cudaMemcpyAsync(c->attn_rope, cs.data(), cs.size() * sizeof(float2), cudaMemcpyHostToDevice, c->stream));
   CH_CUDA(cudaMemcpyAsync(c->op_sp, &sp, sizeof(sp), cudaMemcpyHostToDevice, c->stream));
   AttnArgs a{};
   a.qkv = qkv;
   a.q_norm_w = q_norm;
   a.k_norm_w = k_norm;
-  a.inv_freq = c->attn_inv_freq;
+  a.rope_cs = c->attn_rope;
   a.k_cache = (__half *)k_cache;
   a.v_cache = (__half *)v_cache;
   a.sp = c->op_sp;

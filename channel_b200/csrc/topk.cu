@@ -211,6 +211,15 @@ __global__ void step_begin_kernel(const StepBeginArgs a) {
   }
   __syncthreads();
   if (blockIdx.x == 0 && threadIdx.x == 0) *a.sp = cur;
+  // RoPE (cos, sin) of this step's clock for both thetas, evaluated once per step
+  // in double and rounded once (same values as the host path and the oracle)
+  for (uint32_t i = threadIdx.x; i < 2 * a.rot_half; i += blockDim.x) {
+    const float f = i < a.rot_half ? a.inv_freq_s[i] : a.inv_freq_f[i - a.rot_half];
+    const float ang = __fmul_rn((float)cur.clock, f);
+    double sd, cd;
+    sincos((double)ang, &sd, &cd);
+    a.rope_cs[i] = make_float2((float)cd, (float)sd);
+  }
   const uint32_t tok = *a.token;
   const uint16_t *row = a.embed + (size_t)tok * a.H;
   for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < a.H; i += gridDim.x * blockDim.x)

@@ -31,7 +31,8 @@ def run_case(ctx, oracle, nq, nkv, slots, clock, slot, theta=1e4, scale=1 / 16, 
     qkv = dev(np.concatenate([q, k, v]))
     out = empty(nq * D)
     sd = dev(slots) if slots.size else empty(1, torch.int32)
-    call(lib.ch_decode_attention, ctx.handle, qkv.data_ptr(), dev(qn).data_ptr(), dev(kn).data_ptr(), kcd.data_ptr(),
+    qnd, knd = dev(qn), dev(kn)
+    call(lib.ch_decode_attention, ctx.handle, qkv.data_ptr(), qnd.data_ptr(), knd.data_ptr(), kcd.data_ptr(),
          vcd.data_ptr(), sd.data_ptr(), slots.size, clock, slot, nq, nkv, D, rot, theta, 1e-6, scale, out.data_ptr())
     ctx.synchronize()
     got_k = host(kcd, np.uint16).reshape(4096, -1)

@@ -38,7 +38,8 @@ def test_device_quantizer_matches_oracle(ctx, oracle, mode):
     ref = oracle.quantize_matrix(src, rows, cols, mode)
     d = empty(ref.size, torch.int32)
     fn = lib.ch_quantize_q8_rows if mode == 8 else lib.ch_quantize_q4_rows
-    call(fn, ctx.handle, dev(src).data_ptr(), rows, cols, d.data_ptr())
+    srcd = dev(src)
+    call(fn, ctx.handle, srcd.data_ptr(), rows, cols, d.data_ptr())
     ctx.synchronize()
     assert np.array_equal(host(d, np.uint32).reshape(ref.shape), ref)
 
@@ -54,8 +55,8 @@ def test_gemv_q4_parity(ctx, oracle, M, K):
     x = oracle.gen_f32(K, oracle.tensor_seed(0, 0, 100))
     ref = oracle.gemv_q4(W, x, M, K)
     tiles = empty(lib.ch_q4_tile_bytes(M, K), torch.uint8)
-    xd, yd = dev(x), empty(M)
-    call(lib.ch_q4_pack, ctx.handle, dev(W).data_ptr(), M, K, tiles.data_ptr())
+    xd, yd, Wd = dev(x), empty(M), dev(W)
+    call(lib.ch_q4_pack, ctx.handle, Wd.data_ptr(), M, K, tiles.data_ptr())
     for _ in range(2):  # second launch checks the stream-K counters were reset
         yd.fill_(float("nan"))
         call(lib.ch_gemv_q4, ctx.handle, tiles.data_ptr(), M, K, xd.data_ptr(), yd.data_ptr())
@@ -73,9 +74,9 @@ def test_fused_mlp_q4_parity(ctx, oracle, M, K):
     x = oracle.gen_f32(K, 5)
     ref = oracle.fused_mlp_q4(Wg, Wu, x, M, K)
     tiles = empty(lib.ch_q4_tile_bytes(2 * M, K), torch.uint8)
-    yd = empty(M)
-    call(lib.ch_q4_pack_gateup, ctx.handle, dev(Wg).data_ptr(), dev(Wu).data_ptr(), M, K, tiles.data_ptr())
-    call(lib.ch_fused_mlp_q4, ctx.handle, tiles.data_ptr(), M, K, dev(x).data_ptr(), yd.data_ptr())
+    yd, Wgd, Wud, xd = empty(M), dev(Wg), dev(Wu), dev(x)
+    call(lib.ch_q4_pack_gateup, ctx.handle, Wgd.data_ptr(), Wud.data_ptr(), M, K, tiles.data_ptr())
+    call(lib.ch_fused_mlp_q4, ctx.handle, tiles.data_ptr(), M, K, xd.data_ptr(), yd.data_ptr())
     ctx.synchronize()
     assert_close(host(yd), ref, what="fused_mlp_q4")
 
@@ -88,9 +89,9 @@ def test_gemv_q8_parity(ctx, oracle, M, K):
     x = oracle.gen_f32(K, 6)
     ref = oracle.gemv_q8(W, x, M, K)
     tiles = empty(lib.ch_q8_tile_bytes(M, K), torch.uint8)
-    yd = empty(M)
-    call(lib.ch_q8_pack, ctx.handle, dev(W).data_ptr(), M, K, tiles.data_ptr())
-    call(lib.ch_gemv_q8, ctx.handle, tiles.data_ptr(), M, K, dev(x).data_ptr(), yd.data_ptr())
+    yd, Wd, xd = empty(M), dev(W), dev(x)
+    call(lib.ch_q8_pack, ctx.handle, Wd.data_ptr(), M, K, tiles.data_ptr())
+    call(lib.ch_gemv_q8, ctx.handle, tiles.data_ptr(), M, K, xd.data_ptr(), yd.data_ptr())
     ctx.synchronize()
     assert_close(host(yd), ref, what="gemv_q8")
 

@@ -12,8 +12,8 @@ pytestmark = pytest.mark.gpu
 
 def run(ctx, oracle, logits):
     lib = L.load()
-    ids, vals = empty(64, torch.int32), empty(64)
-    call(lib.ch_topk64, ctx.handle, dev(logits).data_ptr(), logits.size, ids.data_ptr(), vals.data_ptr())
+    ids, vals, lg = empty(64, torch.int32), empty(64), dev(logits)
+    call(lib.ch_topk64, ctx.handle, lg.data_ptr(), logits.size, ids.data_ptr(), vals.data_ptr())
     ctx.synchronize()
     rid, rvals = oracle.topk64(logits)
     return host(ids, np.uint32), host(vals), rid, rvals
