@@ -19,6 +19,7 @@
 #include <algorithm>
 
 #include "common.cuh"
+#include "core.cuh"
 #include "kernels.cuh"
 
 namespace ch {
@@ -42,29 +43,6 @@ size_t attn_partial_floats(uint32_t nkv, uint32_t ratio, uint32_t D, int splits)
 
 namespace {
 constexpr uint32_t kMinChunk = 64;  // slots per CTA before splitting further stops paying
-}
-
-// One warp normalizes one head held in shared memory (in -> out, may alias):
-// rope: out = rope(rmsnorm(in) * w) with the (cos, sin) table; else unit rmsnorm.
-CH_DEV void head_norm_rope_s(const float *in, const float *w, float *out, uint32_t D, uint32_t rot, const float2 *cs,
-                             float eps, bool rope, int lane) {
-  float ss = 0.f;
-  for (uint32_t d = lane; d < D; d += 32) ss = __fmaf_rn(in[d], in[d], ss);
-  ss = warp_sum(ss);
-  const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)D), eps)));
-  if (!rope) {
-    for (uint32_t d = lane; d < D; d += 32) out[d] = __fmul_rn(in[d], inv);
-    return;
-  }
-  const uint32_t half = rot / 2;
-  for (uint32_t d = lane; d < half; d += 32) {
-    const float v0 = __fmul_rn(__fmul_rn(in[d], inv), w[d]);
-    const float v1 = __fmul_rn(__fmul_rn(in[d + half], inv), w[d + half]);
-    const float2 c = cs[d];
-    out[d] = __fsub_rn(__fmul_rn(v0, c.x), __fmul_rn(v1, c.y));
-    out[d + half] = __fadd_rn(__fmul_rn(v0, c.y), __fmul_rn(v1, c.x));
-  }
-  for (uint32_t d = rot + lane; d < D; d += 32) out[d] = __fmul_rn(__fmul_rn(in[d], inv), w[d]);
 }
 
 template <int R>

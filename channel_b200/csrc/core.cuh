@@ -1,0 +1,207 @@
+// core.cuh -- device building blocks shared by the per-op kernels and the
+// persistent decode-step kernel: tile dequant + mma, input fragments, head
+// norm/RoPE, GELU, and the radix top-64 select.
+#pragma once
+#include "common.cuh"
+#include "kernels.cuh"
+
+namespace ch {
+
+CH_DEV float gelu_tanh(float x) {
+  // src/kernels.zig:7-10 / fused_mlp_q4.wgsl:15-18 (explicit rounding, no contraction)
+  float x3 = __fmul_rn(__fmul_rn(__fmul_rn(0.044715f, x), x), x);
+  float inner = __fmul_rn(0.7978845608f, __fadd_rn(x, x3));
+  return __fmul_rn(__fmul_rn(0.5f, x), __fadd_rn(1.0f, tanhf(inner)));
+}
+
+// ---------------------------------------------------------------------------
+// prologue: build the f16 hi/lo B fragments of the (optionally normed) input.
+// xf layout: [32-k block][t 0..3][g 0 = hi | 1 = lo] uint4 {c0.b0, c0.b1, c1.b0, c1.b1}
+// (c0 / c1 = the block's two k16 chunks).  One thread per block; every load of a
+// phase is issued before any is used, so a phase costs one L2 round trip.
+CH_DEV void block_to_fragments(const float (&v)[32], uint4 *xf_blk) {
+  float lo[32];
+#pragma unroll
+  for (int e = 0; e < 32; e++) lo[e] = __fsub_rn(v[e], __half2float(__float2half_rn(v[e])));
+#pragma unroll
+  for (int t = 0; t < 4; t++) {
+    uint32_t hw[4], lw[4];
+#pragma unroll
+    for (int c = 0; c < 2; c++) {
+      const int k0 = c * 16 + 2 * t;
+      hw[c * 2 + 0] = pack_half2(__float2half_rn(v[k0]), __float2half_rn(v[k0 + 1]));
+      hw[c * 2 + 1] = pack_half2(__float2half_rn(v[k0 + 8]), __float2half_rn(v[k0 + 9]));
+      lw[c * 2 + 0] = pack_half2(__float2half_rn(lo[k0]), __float2half_rn(lo[k0 + 1]));
+      lw[c * 2 + 1] = pack_half2(__float2half_rn(lo[k0 + 8]), __float2half_rn(lo[k0 + 9]));
+    }
+    xf_blk[t * 2 + 0] = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+    xf_blk[t * 2 + 1] = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+  }
+}
+CH_DEV void load32(const float *p, float (&v)[32]) {
+  const float4 *q = reinterpret_cast<const float4 *>(p);
+#pragma unroll
+  for (int i = 0; i < 8; i++) {
+    const float4 f = q[i];
+    v[4 * i] = f.x, v[4 * i + 1] = f.y, v[4 * i + 2] = f.z, v[4 * i + 3] = f.w;
+  }
+}
+CH_DEV void store32(float *p, const float (&v)[32]) {
+  float4 *q = reinterpret_cast<float4 *>(p);
+#pragma unroll
+  for (int i = 0; i < 8; i++) q[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+}
+
+// one 576-byte tile: 16 rows; lanes with t == 0 accumulate rows g and g+8.
+// xb: this lane's x-fragment base (hi for g == 0, lo for g == 1, a zero page for
+// g >= 2) and xs its block stride (8 or 0 uint4).
+template <int FMT>
+CH_DEV void tile_mma(const uint8_t *tile, uint32_t kt, const uint4 *xb, uint32_t xs, int lane, float &acc0,
+                     float &acc1) {
+  const int g = lane >> 2;
+  const uint4 w = *reinterpret_cast<const uint4 *>(tile + lane * 16);
+  if (FMT == FMT_Q4) {
+    const uint2 sc = *reinterpret_cast<const uint2 *>(tile + 512 + g * 8);
+    const uint4 b0 = xb[(kt * 2 + 0) * xs], b1 = xb[(kt * 2 + 1) * xs];
+    float d0[4] = {0.f, 0.f, 0.f, 0.f}, d1[4] = {0.f, 0.f, 0.f, 0.f};
+    uint32_t af[4];
+    dequant_q4_word(w.x, af);
+    mma_16816(d0, af, b0.x, b0.y);
+    dequant_q4_word(w.z, af);
+    mma_16816(d1, af, b1.x, b1.y);
+    dequant_q4_word(w.y, af);
+    mma_16816(d0, af, b0.z, b0.w);
+    dequant_q4_word(w.w, af);
+    mma_16816(d1, af, b1.z, b1.w);
+    const __half2 s_lo = *reinterpret_cast<const __half2 *>(&sc.x);  // (row g: blk0, blk1)
+    const __half2 s_hi = *reinterpret_cast<const __half2 *>(&sc.y);  // (row g+8: blk0, blk1)
+    const float2 fg = __half22float2(s_lo), fg8 = __half22float2(s_hi);
+    acc0 = __fmaf_rn(fg.x, __fadd_rn(d0[0], d0[1]), acc0);
+    acc1 = __fmaf_rn(fg8.x, __fadd_rn(d0[2], d0[3]), acc1);
+    acc0 = __fmaf_rn(fg.y, __fadd_rn(d1[0], d1[1]), acc0);
+    acc1 = __fmaf_rn(fg8.y, __fadd_rn(d1[2], d1[3]), acc1);
+  } else {
+    const float2 sc = *reinterpret_cast<const float2 *>(tile + 512 + g * 8);
+    const uint4 b = xb[kt * xs];
+    float d[4] = {0.f, 0.f, 0.f, 0.f};
+    uint32_t af[4];
+    dequant_q8_words(w.x, w.y, af);
+    mma_16816(d, af, b.x, b.y);
+    dequant_q8_words(w.z, w.w, af);
+    mma_16816(d, af, b.z, b.w);
+    acc0 = __fmaf_rn(sc.x, __fadd_rn(d[0], d[1]), acc0);
+    acc1 = __fmaf_rn(sc.y, __fadd_rn(d[2], d[3]), acc1);
+  }
+}
+
+// One warp normalizes one head held in shared memory (in -> out, may alias):
+// rope: out = rope(rmsnorm(in) * w) with the (cos, sin) table; else unit rmsnorm.
+CH_DEV void head_norm_rope_s(const float *in, const float *w, float *out, uint32_t D, uint32_t rot, const float2 *cs,
+                             float eps, bool rope, int lane) {
+  float ss = 0.f;
+  for (uint32_t d = lane; d < D; d += 32) ss = __fmaf_rn(in[d], in[d], ss);
+  ss = warp_sum(ss);
+  const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)D), eps)));
+  if (!rope) {
+    for (uint32_t d = lane; d < D; d += 32) out[d] = __fmul_rn(in[d], inv);
+    return;
+  }
+  const uint32_t half = rot / 2;
+  for (uint32_t d = lane; d < half; d += 32) {
+    const float v0 = __fmul_rn(__fmul_rn(in[d], inv), w[d]);
+    const float v1 = __fmul_rn(__fmul_rn(in[d + half], inv), w[d + half]);
+    const float2 c = cs[d];
+    out[d] = __fsub_rn(__fmul_rn(v0, c.x), __fmul_rn(v1, c.y));
+    out[d + half] = __fadd_rn(__fmul_rn(v0, c.y), __fmul_rn(v1, c.x));
+  }
+  for (uint32_t d = rot + lane; d < D; d += 32) out[d] = __fmul_rn(__fmul_rn(in[d], inv), w[d]);
+}
+
+CH_DEV uint32_t sortable(float f) {
+  uint32_t u = __float_as_uint(f);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+CH_DEV float unsortable(uint32_t s) {
+  uint32_t u = (s & 0x80000000u) ? (s ^ 0x80000000u) : ~s;
+  return __uint_as_float(u);
+}
+CH_DEV float softcap(float v) {
+  // shaders/topk_pass1.wgsl:17-19
+  return __fmul_rn(30.0f, tanhf(__fmul_rn(v, 1.0f / 30.0f)));
+}
+
+// K-th largest 64-bit key held E-per-thread across the block (keys unique except 0 padding)
+template <int E>
+CH_DEV uint64_t block_kth_largest(const uint64_t (&k)[E], int K, uint32_t *hist, uint32_t *sh) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  uint64_t prefix = 0, mask = 0;
+  int need = K;
+  for (int shift = 56; shift >= 0; shift -= 8) {
+    for (int i = tid; i < 256; i += blockDim.x) hist[i] = 0;
+    __syncthreads();
+#pragma unroll
+    for (int e = 0; e < E; e++)
+      if ((k[e] & mask) == prefix) atomicAdd(&hist[(uint32_t)(k[e] >> shift) & 0xFFu], 1u);
+    __syncthreads();
+    if (warp == 0) {
+      uint32_t cnt = 0;
+#pragma unroll
+      for (int b = 0; b < 8; b++) cnt += hist[lane * 8 + b];
+      uint32_t suf = cnt;  // inclusive suffix sum over lanes >= lane
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        uint32_t v = __shfl_down_sync(0xffffffffu, suf, o);
+        if (lane + o < 32) suf += v;
+      }
+      uint32_t above = __shfl_down_sync(0xffffffffu, suf, 1);
+      if (lane == 31) above = 0;
+      if (suf >= (uint32_t)need && above < (uint32_t)need) {
+        uint32_t run = above;
+        for (int b = 7; b >= 0; b--) {
+          uint32_t h = hist[lane * 8 + b];
+          if (run + h >= (uint32_t)need) {
+            sh[0] = (uint32_t)(lane * 8 + b);
+            sh[1] = (uint32_t)need - run;
+            break;
+          }
+          run += h;
+        }
+      }
+    }
+    __syncthreads();
+    const uint32_t sel = sh[0];
+    need = (int)sh[1];
+    prefix |= (uint64_t)sel << shift;
+    mask |= 0xFFull << shift;
+    __syncthreads();
+  }
+  return prefix;
+}
+
+// keys >= thr collected into out[64] sorted descending (rank by comparison; pads are 0)
+template <int E>
+CH_DEV void collect_sorted64(const uint64_t (&k)[E], uint64_t thr, uint64_t *buf, uint32_t *cnt, uint64_t *out) {
+  const int tid = threadIdx.x;
+  if (tid == 0) *cnt = 0;
+  if (tid < 64) buf[tid] = 0;
+  __syncthreads();
+#pragma unroll
+  for (int e = 0; e < E; e++)
+    if (k[e] >= thr && k[e] != 0) {
+      uint32_t p = atomicAdd(cnt, 1u);
+      if (p < 64) buf[p] = k[e];
+    }
+  __syncthreads();
+  if (tid < 64) {
+    const uint64_t me = buf[tid];
+    int rank = 0;
+    for (int j = 0; j < 64; j++) {
+      const uint64_t o = buf[j];
+      rank += (o > me) || (o == me && j < tid);
+    }
+    out[rank] = me;
+  }
+  __syncthreads();
+}
+
+}  // namespace ch

@@ -19,6 +19,7 @@
 // reference's rmsnorm / add_rmsnorm passes (add_rmsnorm.wgsl:15-51) so no
 // separate norm kernel runs on the decode path.
 #include "common.cuh"
+#include "core.cuh"
 #include "kernels.cuh"
 
 namespace ch {
@@ -51,13 +52,6 @@ CH_DEV uint64_t warp_of(uint64_t t, uint64_t T, uint64_t GW) {
   return w;
 }
 
-CH_DEV float gelu_tanh(float x) {
-  // src/kernels.zig:7-10 / fused_mlp_q4.wgsl:15-18 (explicit rounding, no contraction)
-  float x3 = __fmul_rn(__fmul_rn(__fmul_rn(0.044715f, x), x), x);
-  float inner = __fmul_rn(0.7978845608f, __fadd_rn(x, x3));
-  return __fmul_rn(__fmul_rn(0.5f, x), __fadd_rn(1.0f, tanhf(inner)));
-}
-
 template <int EPI>
 CH_DEV void epilogue(float *y, uint32_t rt, int g, float v0, float v1) {
   if (EPI == EPI_STORE) {
@@ -66,44 +60,6 @@ CH_DEV void epilogue(float *y, uint32_t rt, int g, float v0, float v1) {
   } else {
     y[rt * 8 + g] = __fmul_rn(gelu_tanh(v0), v1);
   }
-}
-
-// ---------------------------------------------------------------------------
-// prologue: build the f16 hi/lo B fragments of the (optionally normed) input.
-// xf layout: [32-k block][t 0..3][g 0 = hi | 1 = lo] uint4 {c0.b0, c0.b1, c1.b0, c1.b1}
-// (c0 / c1 = the block's two k16 chunks).  One thread per block; every load of a
-// phase is issued before any is used, so a phase costs one L2 round trip.
-CH_DEV void block_to_fragments(const float (&v)[32], uint4 *xf_blk) {
-  float lo[32];
-#pragma unroll
-  for (int e = 0; e < 32; e++) lo[e] = __fsub_rn(v[e], __half2float(__float2half_rn(v[e])));
-#pragma unroll
-  for (int t = 0; t < 4; t++) {
-    uint32_t hw[4], lw[4];
-#pragma unroll
-    for (int c = 0; c < 2; c++) {
-      const int k0 = c * 16 + 2 * t;
-      hw[c * 2 + 0] = pack_half2(__float2half_rn(v[k0]), __float2half_rn(v[k0 + 1]));
-      hw[c * 2 + 1] = pack_half2(__float2half_rn(v[k0 + 8]), __float2half_rn(v[k0 + 9]));
-      lw[c * 2 + 0] = pack_half2(__float2half_rn(lo[k0]), __float2half_rn(lo[k0 + 1]));
-      lw[c * 2 + 1] = pack_half2(__float2half_rn(lo[k0 + 8]), __float2half_rn(lo[k0 + 9]));
-    }
-    xf_blk[t * 2 + 0] = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-    xf_blk[t * 2 + 1] = make_uint4(lw[0], lw[1], lw[2], lw[3]);
-  }
-}
-CH_DEV void load32(const float *p, float (&v)[32]) {
-  const float4 *q = reinterpret_cast<const float4 *>(p);
-#pragma unroll
-  for (int i = 0; i < 8; i++) {
-    const float4 f = q[i];
-    v[4 * i] = f.x, v[4 * i + 1] = f.y, v[4 * i + 2] = f.z, v[4 * i + 3] = f.w;
-  }
-}
-CH_DEV void store32(float *p, const float (&v)[32]) {
-  float4 *q = reinterpret_cast<float4 *>(p);
-#pragma unroll
-  for (int i = 0; i < 8; i++) q[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
 }
 
 template <int PRO>
@@ -165,48 +121,6 @@ CH_DEV void prologue(const GemvArgs &a, float *vec, uint4 *xf, float *red) {
     for (int e = 0; e < 32; e++) v[e] = __fmul_rn(__fmul_rn(v[e], inv), w[e]);
     if (writer && a.normed_out) store32(a.normed_out + b * 32, v);
     block_to_fragments(v, xf + b * 8);
-  }
-}
-
-// one 576-byte tile: 16 rows; lanes with t == 0 accumulate rows g and g+8.
-// xb: this lane's x-fragment base (hi for g == 0, lo for g == 1, a zero page for
-// g >= 2) and xs its block stride (8 or 0 uint4).
-template <int FMT>
-CH_DEV void tile_mma(const uint8_t *tile, uint32_t kt, const uint4 *xb, uint32_t xs, int lane, float &acc0,
-                     float &acc1) {
-  const int g = lane >> 2;
-  const uint4 w = *reinterpret_cast<const uint4 *>(tile + lane * 16);
-  if (FMT == FMT_Q4) {
-    const uint2 sc = *reinterpret_cast<const uint2 *>(tile + 512 + g * 8);
-    const uint4 b0 = xb[(kt * 2 + 0) * xs], b1 = xb[(kt * 2 + 1) * xs];
-    float d0[4] = {0.f, 0.f, 0.f, 0.f}, d1[4] = {0.f, 0.f, 0.f, 0.f};
-    uint32_t af[4];
-    dequant_q4_word(w.x, af);
-    mma_16816(d0, af, b0.x, b0.y);
-    dequant_q4_word(w.z, af);
-    mma_16816(d1, af, b1.x, b1.y);
-    dequant_q4_word(w.y, af);
-    mma_16816(d0, af, b0.z, b0.w);
-    dequant_q4_word(w.w, af);
-    mma_16816(d1, af, b1.z, b1.w);
-    const __half2 s_lo = *reinterpret_cast<const __half2 *>(&sc.x);  // (row g: blk0, blk1)
-    const __half2 s_hi = *reinterpret_cast<const __half2 *>(&sc.y);  // (row g+8: blk0, blk1)
-    const float2 fg = __half22float2(s_lo), fg8 = __half22float2(s_hi);
-    acc0 = __fmaf_rn(fg.x, __fadd_rn(d0[0], d0[1]), acc0);
-    acc1 = __fmaf_rn(fg8.x, __fadd_rn(d0[2], d0[3]), acc1);
-    acc0 = __fmaf_rn(fg.y, __fadd_rn(d1[0], d1[1]), acc0);
-    acc1 = __fmaf_rn(fg8.y, __fadd_rn(d1[2], d1[3]), acc1);
-  } else {
-    const float2 sc = *reinterpret_cast<const float2 *>(tile + 512 + g * 8);
-    const uint4 b = xb[kt * xs];
-    float d[4] = {0.f, 0.f, 0.f, 0.f};
-    uint32_t af[4];
-    dequant_q8_words(w.x, w.y, af);
-    mma_16816(d, af, b.x, b.y);
-    dequant_q8_words(w.z, w.w, af);
-    mma_16816(d, af, b.z, b.w);
-    acc0 = __fmaf_rn(sc.x, __fadd_rn(d[0], d[1]), acc0);
-    acc1 = __fmaf_rn(sc.y, __fadd_rn(d[2], d[3]), acc1);
   }
 }
 

@@ -18,6 +18,7 @@
 
 #include "../../include/channel_cuda.h"
 #include "common.cuh"
+#include "decode_step.cuh"
 #include "kernels.cuh"
 
 using namespace ch;
@@ -181,6 +182,18 @@ struct ch_model {
   StepParams *plan = nullptr;
   uint32_t *plan_lists = nullptr;
   uint32_t plan_steps = 0, hist_cap = 0, loop_pos = 0;
+  bool loop_ready = false;
+  // persistent decode-step kernel: phase tables, per-GEMV outputs, barrier counters
+  Phase *d_phases = nullptr, *d_phases_nl = nullptr;
+  uint32_t n_phases = 0, n_phases_nl = 0;
+  float *gdir[5] = {nullptr, nullptr, nullptr, nullptr, nullptr};
+  float *gpart[5] = {nullptr, nullptr, nullptr, nullptr, nullptr};
+  unsigned long long *mk_arrive = nullptr;
+  uint32_t *mk_epoch = nullptr;
+  uint32_t *gcnt[5] = {nullptr, nullptr, nullptr, nullptr, nullptr};
+  size_t mk_smem = 0;
+  int mk_grid = 0;
+  bool use_ops = false;  // kernel-per-op decode (CH_DECODE_OPS=1), kept for A/B measurement
   // prefill buffers
   uint32_t pf_cap = 0;
   float *pX = nullptr, *pNX = nullptr, *pQKV = nullptr, *pQO = nullptr, *pA = nullptr, *pMO = nullptr, *pACT = nullptr;
@@ -211,6 +224,15 @@ static void free_model(ch_model *m) {
                  m->topk_cand, m->topk_counter, m->plan, m->plan_lists, m->pX, m->pNX, m->pQKV, m->pQO, m->pA, m->pMO,
                  m->pACT, m->pSlots, m->pTok};
   for (void *p : dev) cudaFree(p);
+  for (int k = 0; k < 5; k++) {
+    cudaFree(m->gdir[k]);
+    cudaFree(m->gpart[k]);
+  }
+  cudaFree(m->d_phases);
+  cudaFree(m->d_phases_nl);
+  cudaFree(m->mk_arrive);
+  cudaFree(m->mk_epoch);
+  for (int k = 0; k < 5; k++) cudaFree(m->gcnt[k]);
   void *host[] = {m->h_x, m->h_sp, m->h_lists, m->h_ids, m->h_vals, m->h_run, m->h_rope};
   for (void *p : host) cudaFreeHost(p);
   if (m->g_host_logits) cudaGraphExecDestroy(m->g_host_logits);
@@ -308,7 +330,7 @@ static int alloc_model_buffers(ch_model *m) {
   CH_TRY(dmalloc(&m->attn_partial, attn_partial_floats(m->nkv, m->nq / m->nkv, m->D, m->attn_splits)));
   CH_TRY(dmalloc(&m->attn_counters, m->nkv));
   CH_CUDA(cudaMemsetAsync(m->attn_counters, 0, m->nkv * 4, m->ctx->stream));
-  CH_TRY(dmalloc(&m->topk_cand, (size_t)topk_blocks(m->V) * 64));
+  CH_TRY(dmalloc(&m->topk_cand, (size_t)std::max(topk_blocks(m->V), num_sms()) * 64));
   CH_TRY(dmalloc(&m->topk_counter, 1));
   CH_CUDA(cudaMemsetAsync(m->topk_counter, 0, 4, m->ctx->stream));
   // pinned staging
@@ -332,6 +354,170 @@ static int alloc_model_buffers(ch_model *m) {
   CH_TRY(dmalloc(&m->rope_cs, c.rotary_dim));
   CH_CUDA(cudaMallocHost(&m->h_rope, c.rotary_dim * sizeof(float2)));
   return CH_OK;
+}
+
+// ---------------------------------------------------------------------------
+// phase table of the persistent decode-step kernel (decode_step.cu)
+enum GemvKind { GK_QKV = 0, GK_O = 1, GK_GU = 2, GK_DOWN = 3, GK_LM = 4 };
+
+static int build_phases(ch_model *m, bool with_logits, Phase **d_out, uint32_t *n_out) {
+  const uint32_t GW = (uint32_t)m->mk_grid * mk_warps();
+  const uint32_t rows[5] = {m->qd + 2 * m->kvd, m->H, 2 * m->I, m->H, m->V};
+  const uint32_t KT[5] = {m->H / 64, m->qd / 64, m->H / 64, m->I / 64, m->H / 32};
+  GemvOut outs[5];
+  for (int k = 0; k < 5; k++) {
+    const uint64_t T = (uint64_t)(rows[k] / 16) * KT[k];
+    outs[k] = GemvOut{m->gdir[k], m->gpart[k], m->gcnt[k], KT[k], (uint32_t)(T / GW), (uint32_t)(T % GW),
+                      k == GK_GU ? 1u : 0u};
+  }
+  auto gemv = [&](int kind, const uint8_t *tiles, int fmt, uint32_t K) {
+    Phase p{};
+    p.kind = PH_GEMV;
+    p.fmt = fmt;
+    p.tiles = tiles;
+    p.row_tiles = rows[kind] / 16;
+    p.k_tiles = KT[kind];
+    p.K = K;
+    p.q = outs[kind].q;
+    p.rem = outs[kind].rem;
+    p.out = outs[kind];
+    p.scalar = 1.0f;
+    return p;
+  };
+  std::vector<Phase> ph;
+  const uint32_t rh = m->cfg.rotary_dim / 2;
+  for (uint32_t l = 0; l < m->L; l++) {
+    const DevLayer &dl = m->layers[l];
+    Phase q = gemv(GK_QKV, dl.qkv, FMT_Q4, m->H);
+    q.norm_w = dl.input_norm;
+    q.normed_out = m->normed;
+    if (l == 0) {
+      q.pm = PM_NORM;
+      q.x_in = m->X[0];
+    } else {
+      const DevLayer &pl = m->layers[l - 1];
+      q.pm = PM_ADD_NORM;
+      q.x_in = m->X[1];
+      q.r_in = outs[GK_DOWN];
+      q.post_w = pl.post_ffn;
+      q.scalar = pl.scalar;
+      q.x_out = m->X[0];
+    }
+    ph.push_back(q);
+    Phase at{};
+    at.kind = PH_ATTN;
+    at.r_in = outs[GK_QKV];
+    at.q_norm_w = dl.q_norm;
+    at.k_norm_w = dl.k_norm;
+    at.rope_cs = m->rope_cs + (dl.full ? rh : 0);
+    at.k_cache = dl.kc;
+    at.v_cache = dl.vc;
+    at.is_sliding = dl.full ? 0 : 1;
+    at.attn_scale = 1.0f;  // Gemma-style: q/k norms replace 1/sqrt(d) (forward.zig:85)
+    at.attn_out = m->attn;
+    ph.push_back(at);
+    Phase o = gemv(GK_O, dl.o, FMT_Q4, m->qd);
+    o.pm = PM_DIRECT;
+    o.x_in = m->attn;
+    ph.push_back(o);
+    Phase gu = gemv(GK_GU, dl.gateup, FMT_Q4, m->H);
+    gu.pm = PM_ADD_NORM;
+    gu.x_in = m->X[0];
+    gu.r_in = outs[GK_O];
+    gu.post_w = dl.post_attn;
+    gu.norm_w = dl.pre_ffn;
+    gu.x_out = m->X[1];
+    gu.normed_out = m->normed;
+    ph.push_back(gu);
+    Phase dn = gemv(GK_DOWN, dl.down, FMT_Q4, m->I);
+    dn.pm = PM_GELU;
+    dn.r_in = outs[GK_GU];
+    ph.push_back(dn);
+  }
+  const DevLayer &last = m->layers[m->L - 1];
+  Phase lm = gemv(GK_LM, m->lm, FMT_Q8, m->H);
+  lm.pm = PM_ADD_NORM;
+  lm.x_in = m->X[1];
+  lm.r_in = outs[GK_DOWN];
+  lm.post_w = last.post_ffn;
+  lm.scalar = last.scalar;
+  lm.norm_w = m->final_norm;
+  lm.x_out = m->X[0];
+  lm.normed_out = m->normed;
+  if (!with_logits) {  // prologue only: fold the last residual add + final norm
+    lm.row_tiles = 0;
+    lm.q = lm.rem = 0;
+  }
+  ph.push_back(lm);
+  if (with_logits) {
+    Phase tk{};
+    tk.kind = PH_TOPK;
+    tk.r_in = outs[GK_LM];
+    tk.vocab = m->V;
+    ph.push_back(tk);
+  }
+  CH_TRY(dmalloc(d_out, ph.size()));
+  CH_CUDA(cudaMemcpy(*d_out, ph.data(), ph.size() * sizeof(Phase), cudaMemcpyHostToDevice));
+  *n_out = (uint32_t)ph.size();
+  return CH_OK;
+}
+
+static int init_decode_step(ch_model *m) {
+  m->mk_grid = num_sms();
+  if (m->H > 4096) return fail(CH_EINVAL, "decode-step kernel stages at most 4096 hidden rows");
+  if ((m->V + m->mk_grid - 1) / m->mk_grid > 4096) return fail(CH_EINVAL, "vocab slice per SM exceeds 4096");
+  const size_t part = (size_t)m->mk_grid * mk_warps() * 2 * 16;
+  const uint32_t rows[5] = {m->qd + 2 * m->kvd, m->H, 2 * m->I, m->H, m->V};
+  for (int k = 0; k < 5; k++) {
+    CH_TRY(dmalloc(&m->gdir[k], rows[k]));
+    CH_TRY(dmalloc(&m->gpart[k], part));
+    CH_TRY(dmalloc(&m->gcnt[k], rows[k] / 16));
+    CH_CUDA(cudaMemset(m->gcnt[k], 0, rows[k] / 16 * 4));
+  }
+  CH_TRY(dmalloc(&m->mk_arrive, 1));
+  CH_TRY(dmalloc(&m->mk_epoch, 1));
+  CH_CUDA(cudaMemset(m->mk_arrive, 0, 8));
+  CH_CUDA(cudaMemset(m->mk_epoch, 0, 4));
+  CH_TRY(build_phases(m, true, &m->d_phases, &m->n_phases));
+  CH_TRY(build_phases(m, false, &m->d_phases_nl, &m->n_phases_nl));
+  const uint32_t max_k = std::max({m->H, m->qd, m->I});
+  m->mk_smem = mk_smem_bytes(max_k, m->H, m->nq / m->nkv,
+                             (uint32_t)std::min(m->mk_grid / (int)m->nkv, m->attn_splits), kSlots);
+  if (m->mk_smem > 227 * 1024) return fail(CH_EINVAL, "decode-step kernel needs more than 227 KB of shared memory");
+  int co = 0;
+  CH_CUDA(cudaDeviceGetAttribute(&co, cudaDevAttrCooperativeLaunch, m->ctx->device));
+  if (!co) return fail(CH_ECUDA, "device lacks cooperative launch");
+  const char *env = getenv("CH_DECODE_OPS");
+  m->use_ops = env && env[0] == '1';
+  return CH_OK;
+}
+
+static MegaArgs mega_args(ch_model *m, bool logits, bool device_loop) {
+  MegaArgs a{};
+  a.phases = logits ? m->d_phases : m->d_phases_nl;
+  a.nphases = logits ? m->n_phases : m->n_phases_nl;
+  a.grid = (uint32_t)m->mk_grid;
+  a.arrive = m->mk_arrive;
+  a.epoch = m->mk_epoch;
+  a.err = m->ctx->err;
+  a.sp = m->sp;
+  a.sp_rw = device_loop ? m->sp : nullptr;
+  a.nq = m->nq;
+  a.nkv = m->nkv;
+  a.rot = m->cfg.rotary_dim;
+  a.attn_max_splits = (uint32_t)std::min(m->mk_grid / (int)m->nkv, m->attn_splits);
+  a.cache_slots = kSlots;
+  a.eps = m->cfg.rms_norm_eps;
+  a.attn_partial = m->attn_partial;
+  a.attn_counters = m->attn_counters;
+  a.topk_cand = m->topk_cand;
+  a.topk_counter = m->topk_counter;
+  a.ids = m->ids;
+  a.vals = m->vals;
+  a.token_out = m->token;
+  a.token_hist = device_loop ? m->token_hist : nullptr;
+  a.hist_cap = m->hist_cap;
+  return a;
 }
 
 // upload quant.zig Q4 blocks of one matrix into a temp device buffer
@@ -434,6 +620,7 @@ extern "C" int ch_model_create(ch_ctx *ctx, const ch_model_config *cfg, const ch
   }
   cudaError_t e = cudaStreamSynchronize(s);
   if (e != cudaSuccess) return bail(fail(CH_ECUDA, std::string("model upload: ") + cudaGetErrorString(e)));
+  if (int r2 = init_decode_step(m)) return bail(r2);
   *out = m;
   return CH_OK;
 }
@@ -537,6 +724,7 @@ extern "C" int ch_model_create_synthetic(ch_ctx *ctx, const ch_model_config *cfg
   cudaFree(tn);
   tn = nullptr;
   if (e != cudaSuccess) return bail(fail(CH_ECUDA, std::string("synthetic model: ") + cudaGetErrorString(e)));
+  if (int r2 = init_decode_step(m)) return bail(r2);
   *out = m;
   return CH_OK;
 }
@@ -568,6 +756,12 @@ extern "C" int ch_model_zero_state(ch_model *m) {
   CH_CUDA(cudaMemsetAsync(m->X[0], 0, m->H * 4, s));
   CH_CUDA(cudaMemsetAsync(m->X[1], 0, m->H * 4, s));
   CH_CUDA(cudaMemsetAsync(m->normed, 0, m->H * 4, s));
+  CH_CUDA(cudaMemsetAsync(m->mk_arrive, 0, 8, s));
+  for (int k = 0; k < 5; k++) {
+    const uint32_t rows[5] = {m->qd + 2 * m->kvd, m->H, 2 * m->I, m->H, m->V};
+    CH_CUDA(cudaMemsetAsync(m->gcnt[k], 0, rows[k] / 16 * 4, s));
+  }
+  CH_CUDA(cudaMemsetAsync(m->mk_epoch, 0, 4, s));
   CH_CUDA(cudaStreamSynchronize(s));
   return CH_OK;
 }
@@ -775,7 +969,7 @@ extern "C" int ch_forward_token(ch_model *m, const float *x, uint32_t clock, uin
   CH_CUDA(cudaSetDevice(m->ctx->device));
   const bool logits = topk_out || token_out;
   cudaGraphExec_t *g = logits ? &m->g_host_logits : &m->g_host_nologits;
-  if (!*g) CH_TRY(capture(m, logits, false, g));
+  if (m->use_ops && !*g) CH_TRY(capture(m, logits, false, g));
   cudaStream_t s = m->ctx->stream;
   memcpy(m->h_x, x, m->H * 4);
   m->h_sp->clock = clock;
@@ -795,7 +989,10 @@ extern "C" int ch_forward_token(ch_model *m, const float *x, uint32_t clock, uin
   CH_CUDA(cudaMemcpyAsync(m->rope_cs, m->h_rope, 2 * rh * sizeof(float2), cudaMemcpyHostToDevice, s));
   if (n_active) CH_CUDA(cudaMemcpyAsync(m->active, m->h_lists, n_active * 4, cudaMemcpyHostToDevice, s));
   if (n_sliding) CH_CUDA(cudaMemcpyAsync(m->sliding, m->h_lists + kSlots, n_sliding * 4, cudaMemcpyHostToDevice, s));
-  CH_CUDA(cudaGraphLaunch(*g, s));
+  if (m->use_ops)
+    CH_CUDA(cudaGraphLaunch(*g, s));
+  else
+    CH_CUDA(launch_decode_step(mega_args(m, logits, false), m->mk_smem, s));
   if (logits) {
     CH_CUDA(cudaMemcpyAsync(m->h_ids, m->ids, 64 * 4, cudaMemcpyDeviceToHost, s));
     CH_CUDA(cudaMemcpyAsync(m->h_vals, m->vals, 64 * 4, cudaMemcpyDeviceToHost, s));
@@ -859,13 +1056,31 @@ extern "C" int ch_decode_plan(ch_model *m, const ch_step_desc *steps, uint32_t n
     cudaGraphExecDestroy(m->g_loop);
     m->g_loop = nullptr;
   }
-  CH_TRY(capture(m, true, true, &m->g_loop));
+  if (m->use_ops) CH_TRY(capture(m, true, true, &m->g_loop));
+  m->loop_ready = true;
+  return CH_OK;
+}
+
+static int launch_loop_steps(ch_model *m, uint32_t n_steps) {
+  cudaStream_t s = m->ctx->stream;
+  if (m->use_ops) {
+    for (uint32_t i = 0; i < n_steps; i++) CH_CUDA(cudaGraphLaunch(m->g_loop, s));
+    return CH_OK;
+  }
+  StepBeginArgs sb{m->embed,      m->H,       sqrtf((float)m->H), m->token,    m->X[0],
+                   m->sp,         m->plan,    m->plan_steps,      m->ctx->err, m->inv_freq_s,
+                   m->inv_freq_f, m->rope_cs, m->cfg.rotary_dim / 2};
+  const MegaArgs a = mega_args(m, true, true);
+  for (uint32_t i = 0; i < n_steps; i++) {
+    CH_CUDA(launch_step_begin(sb, s, false));
+    CH_CUDA(launch_decode_step(a, m->mk_smem, s));
+  }
   return CH_OK;
 }
 
 extern "C" int ch_decode_run(ch_model *m, uint32_t first_token, uint32_t n_steps) {
   if (!m) return fail(CH_EINVAL, "model is NULL");
-  if (!m->g_loop || n_steps > m->plan_steps) return fail(CH_ESTATE, "ch_decode_plan must cover n_steps first");
+  if (!m->loop_ready || n_steps > m->plan_steps) return fail(CH_ESTATE, "ch_decode_plan must cover n_steps first");
   if (first_token >= m->V) return fail(CH_EINVAL, "first_token >= vocab");
   CH_CUDA(cudaSetDevice(m->ctx->device));
   cudaStream_t s = m->ctx->stream;
@@ -874,17 +1089,17 @@ extern "C" int ch_decode_run(ch_model *m, uint32_t first_token, uint32_t n_steps
   m->h_run[1] = first_token;
   CH_CUDA(cudaMemcpyAsync(&m->sp->step, &m->h_run[0], 4, cudaMemcpyHostToDevice, s));
   CH_CUDA(cudaMemcpyAsync(m->token, &m->h_run[1], 4, cudaMemcpyHostToDevice, s));
-  for (uint32_t i = 0; i < n_steps; i++) CH_CUDA(cudaGraphLaunch(m->g_loop, s));
+  CH_TRY(launch_loop_steps(m, n_steps));
   m->loop_pos = n_steps;
   return CH_OK;
 }
 
 extern "C" int ch_decode_continue(ch_model *m, uint32_t n_steps) {
   if (!m) return fail(CH_EINVAL, "model is NULL");
-  if (!m->g_loop) return fail(CH_ESTATE, "ch_decode_plan and ch_decode_run come first");
+  if (!m->loop_ready) return fail(CH_ESTATE, "ch_decode_plan and ch_decode_run come first");
   if ((uint64_t)m->loop_pos + n_steps > m->plan_steps) return fail(CH_EINVAL, "more steps than planned");
   CH_CUDA(cudaSetDevice(m->ctx->device));
-  for (uint32_t i = 0; i < n_steps; i++) CH_CUDA(cudaGraphLaunch(m->g_loop, m->ctx->stream));
+  CH_TRY(launch_loop_steps(m, n_steps));
   m->loop_pos += n_steps;
   return CH_OK;
 }

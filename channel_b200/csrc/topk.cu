@@ -11,6 +11,7 @@
 // to finish repeats the select over all candidates.  Two launches collapse
 // into one; no global sort.
 #include "common.cuh"
+#include "core.cuh"
 #include "kernels.cuh"
 
 namespace ch {
@@ -23,93 +24,6 @@ constexpr int kFinalPer = 32;  // candidates per thread in the final pass (up to
 }  // namespace
 
 int topk_blocks(uint32_t V) { return (int)((V + kTkChunk - 1) / kTkChunk); }
-
-CH_DEV uint32_t sortable(float f) {
-  uint32_t u = __float_as_uint(f);
-  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
-}
-CH_DEV float unsortable(uint32_t s) {
-  uint32_t u = (s & 0x80000000u) ? (s ^ 0x80000000u) : ~s;
-  return __uint_as_float(u);
-}
-CH_DEV float softcap(float v) {
-  // shaders/topk_pass1.wgsl:17-19
-  return __fmul_rn(30.0f, tanhf(__fmul_rn(v, 1.0f / 30.0f)));
-}
-
-// K-th largest 64-bit key held E-per-thread across the block (keys unique except 0 padding)
-template <int E>
-CH_DEV uint64_t block_kth_largest(const uint64_t (&k)[E], int K, uint32_t *hist, uint32_t *sh) {
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  uint64_t prefix = 0, mask = 0;
-  int need = K;
-  for (int shift = 56; shift >= 0; shift -= 8) {
-    for (int i = tid; i < 256; i += blockDim.x) hist[i] = 0;
-    __syncthreads();
-#pragma unroll
-    for (int e = 0; e < E; e++)
-      if ((k[e] & mask) == prefix) atomicAdd(&hist[(uint32_t)(k[e] >> shift) & 0xFFu], 1u);
-    __syncthreads();
-    if (warp == 0) {
-      uint32_t cnt = 0;
-#pragma unroll
-      for (int b = 0; b < 8; b++) cnt += hist[lane * 8 + b];
-      uint32_t suf = cnt;  // inclusive suffix sum over lanes >= lane
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        uint32_t v = __shfl_down_sync(0xffffffffu, suf, o);
-        if (lane + o < 32) suf += v;
-      }
-      uint32_t above = __shfl_down_sync(0xffffffffu, suf, 1);
-      if (lane == 31) above = 0;
-      if (suf >= (uint32_t)need && above < (uint32_t)need) {
-        uint32_t run = above;
-        for (int b = 7; b >= 0; b--) {
-          uint32_t h = hist[lane * 8 + b];
-          if (run + h >= (uint32_t)need) {
-            sh[0] = (uint32_t)(lane * 8 + b);
-            sh[1] = (uint32_t)need - run;
-            break;
-          }
-          run += h;
-        }
-      }
-    }
-    __syncthreads();
-    const uint32_t sel = sh[0];
-    need = (int)sh[1];
-    prefix |= (uint64_t)sel << shift;
-    mask |= 0xFFull << shift;
-    __syncthreads();
-  }
-  return prefix;
-}
-
-// keys >= thr collected into out[64] sorted descending (rank by comparison; pads are 0)
-template <int E>
-CH_DEV void collect_sorted64(const uint64_t (&k)[E], uint64_t thr, uint64_t *buf, uint32_t *cnt, uint64_t *out) {
-  const int tid = threadIdx.x;
-  if (tid == 0) *cnt = 0;
-  if (tid < 64) buf[tid] = 0;
-  __syncthreads();
-#pragma unroll
-  for (int e = 0; e < E; e++)
-    if (k[e] >= thr && k[e] != 0) {
-      uint32_t p = atomicAdd(cnt, 1u);
-      if (p < 64) buf[p] = k[e];
-    }
-  __syncthreads();
-  if (tid < 64) {
-    const uint64_t me = buf[tid];
-    int rank = 0;
-    for (int j = 0; j < 64; j++) {
-      const uint64_t o = buf[j];
-      rank += (o > me) || (o == me && j < tid);
-    }
-    out[rank] = me;
-  }
-  __syncthreads();
-}
 
 __global__ void __launch_bounds__(kTkThreads) topk64_kernel(const TopkArgs a) {
   __shared__ uint32_t hist[256];
