@@ -77,6 +77,7 @@ SIGNATURES = {
     "ch_q4_pack_gateup": (i32, [vp, vp, vp, u32, u32, vp]),
     "ch_q8_pack": (i32, [vp, vp, u32, u32, vp]),
     "ch_gemv_q4": (i32, [vp, vp, u32, u32, vp, vp]),
+    "ch_gemv_q4_noalloc": (i32, [vp, u32, u32, vp, vp, vp, vp]),
     "ch_fused_mlp_q4": (i32, [vp, vp, u32, u32, vp, vp]),
     "ch_gemv_q8": (i32, [vp, vp, u32, u32, vp, vp]),
     "ch_rmsnorm": (i32, [vp, vp, vp, vp, u32, u32, f32]),

@@ -38,6 +38,11 @@ static int fail(int code, const std::string &msg) {
                                 std::to_string(__LINE__));                                     \
   } while (0)
 
+namespace ch {
+// lets other translation units of the C-ABI set the calling thread's message
+int set_last_error(int code, const std::string &msg) { return fail(code, msg); }
+}  // namespace ch
+
 extern "C" const char *ch_last_error(void) { return g_err.c_str(); }
 extern "C" int ch_api_version(void) { return CH_API_VERSION; }
 

@@ -165,6 +165,25 @@ int ch_fused_mlp_q4(ch_ctx *ctx, const void *gateup_tiles_dev, uint32_t rows, ui
                     float *act_dev);
 /* gemv_q8.wgsl */
 int ch_gemv_q8(ch_ctx *ctx, const void *tiles_dev, uint32_t rows, uint32_t cols, const float *x_dev, float *y_dev);
+/* No counterpart in the reference.  ch_gemv_q4 without a context and without
+ * allocating: for callers that may not allocate device memory -- a host
+ * runtime whose pool allocator owns the device's memory, a serving loop that
+ * bans cudaFree (it synchronizes the device) once it is running, or a binding
+ * that may only use the buffers its caller hands over.  The stream-K scratch
+ * lives in one static device array of about 300 KB that every GPU loading the
+ * library holds until exit.  Limits: rows <= 32768, cols <= 16384 (CH_EINVAL
+ * beyond).  Runs on the current device, asynchronously on `stream` (a
+ * cudaStream_t; NULL = default stream).  The first call on a device resolves
+ * the array's device address (and may load the library's CUDA module), so
+ * make it once during set-up, before any stream capture.  All calls on a
+ * device share the array: calls that overlap on the GPU (other streams, other
+ * threads) race and must be serialized by the caller.  The call clears the
+ * per-row-tile counters it uses before the kernel runs.  status_dev, if not
+ * NULL, is a device word into which the kernel ORs bit 0 when a weight copy
+ * stalls (the bits of ch_ctx_device_status; y is then incomplete); NULL
+ * discards them. */
+int ch_gemv_q4_noalloc(const void *tiles_dev, uint32_t rows, uint32_t cols, const float *x_dev, float *y_dev,
+                       uint32_t *status_dev, void *stream);
 /* rmsnorm.wgsl / add_rmsnorm.wgsl over n_rows rows of h */
 int ch_rmsnorm(ch_ctx *ctx, const float *x_dev, const float *w_dev, float *y_dev, uint32_t n_rows, uint32_t h, float eps);
 int ch_add_rmsnorm(ch_ctx *ctx, float *x_dev, const float *r_dev, const float *w_dev, float *y_dev, uint32_t n_rows,
