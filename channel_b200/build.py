@@ -37,30 +37,36 @@ def sources() -> list[Path]:
     return sorted(list(CSRC.glob("*.cu")) + list(CSRC.glob("*.cpp")))
 
 
-def build(verbose: bool = False, force: bool = False) -> Path:
+def build(verbose: bool = False, force: bool = False, trace: bool = False) -> Path:
+    """Compile every source and link the library.  trace=True builds the
+    instrumented variant (-DCH_PHASE_TRACE: per-phase timeline of the decode-step
+    kernel) as libchannel_b200_trace.so, in its own object folder."""
     nvcc = _nvcc()
-    OBJ.mkdir(exist_ok=True)
+    obj_dir = OBJ.with_name(OBJ.name + "_trace") if trace else OBJ
+    out = OUT.with_name("libchannel_b200_trace.so") if trace else OUT
+    extra = ["-DCH_PHASE_TRACE"] if trace else []
+    obj_dir.mkdir(exist_ok=True)
     headers = list(CSRC.glob("*.cuh")) + [ROOT / "include" / "channel_cuda.h"]
     newest_hdr = max(h.stat().st_mtime for h in headers)
     objs = []
     for src in sources():
-        obj = OBJ / (src.name + ".o")
+        obj = obj_dir / (src.name + ".o")
         objs.append(obj)
         if not force and obj.exists() and obj.stat().st_mtime >= max(src.stat().st_mtime, newest_hdr):
             continue
-        cmd = [nvcc, *NVCC_FLAGS, "-c", str(src), "-o", str(obj)]
+        cmd = [nvcc, *NVCC_FLAGS, *extra, "-c", str(src), "-o", str(obj)]
         if src.suffix == ".cpp":
             cmd = [nvcc, "-x", "cu", *cmd[1:]]
         if verbose:
             print(" ".join(cmd), flush=True)
         subprocess.run(cmd, check=True)
-    if force or not OUT.exists() or OUT.stat().st_mtime < max(o.stat().st_mtime for o in objs):
-        cmd = [nvcc, "-shared", "-gencode", "arch=compute_100a,code=sm_100a", *map(str, objs), "-o", str(OUT),
+    if force or not out.exists() or out.stat().st_mtime < max(o.stat().st_mtime for o in objs):
+        cmd = [nvcc, "-shared", "-gencode", "arch=compute_100a,code=sm_100a", *map(str, objs), "-o", str(out),
                "-lcudart"]
         if verbose:
             print(" ".join(cmd), flush=True)
         subprocess.run(cmd, check=True)
-    return OUT
+    return out
 
 
 def build_oracle(verbose: bool = False) -> Path:
@@ -73,5 +79,5 @@ def build_oracle(verbose: bool = False) -> Path:
 
 if __name__ == "__main__":
     v = "-v" in sys.argv
-    print(build(verbose=v, force="--force" in sys.argv))
+    print(build(verbose=v, force="--force" in sys.argv, trace="--trace" in sys.argv))
     print(build_oracle(verbose=v))

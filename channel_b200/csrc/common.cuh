@@ -32,6 +32,16 @@ CH_DEV void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" 
 CH_DEV void mbar_arrive_expect_tx(uint64_t *bar, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
 }
+// add expected transaction bytes to the current phase without arriving
+CH_DEV void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
+  asm volatile("mbarrier.expect_tx.relaxed.cta.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+CH_DEV void mbar_arrive(uint64_t *bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+// order this thread's earlier generic-proxy view of global memory (data other CTAs
+// wrote and published through a barrier) before its later bulk-copy reads
+CH_DEV void fence_proxy_async_global() { asm volatile("fence.proxy.async.global;" ::: "memory"); }
 CH_DEV bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
@@ -67,6 +77,28 @@ CH_DEV void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) 
       "l"(src), "r"(bytes), "r"(smem_u32(bar))
       : "memory");
 }
+
+// L2 policy for data read exactly once (the weight stream): evict it first, so
+// the small activations, norm weights and KV rows that phases re-read stay in L2.
+CH_DEV uint64_t l2_evict_first_policy() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+// bulk_g2s with an L2 cache policy
+CH_DEV void bulk_g2s_hint(void *dst, const void *src, uint32_t bytes, uint64_t *bar, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
+          smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
+}
+
+// 16-byte asynchronous global -> shared copy through L2 (no registers held)
+CH_DEV void cp_async16(void *dst, const void *src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+CH_DEV void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
 // programmatic dependent launch
 CH_DEV void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }

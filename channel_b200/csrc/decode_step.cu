@@ -10,34 +10,70 @@
 //   tail:       GEMV Q8 LM head  ->  TOPK
 //
 // B200 design.  A decode token is an HBM weight stream (7.2 GB for the 12B
-// shape) with tiny activations in between.  Every warp owns a balanced share of
-// the tiles of every GEMV phase and streams its shares of ALL phases back to
-// back through its own bulk-copy (cp.async.bulk) stages, so the weight stream
-// never drains at phase boundaries: weights do not depend on activations.  Only
-// the compute waits, on a grid-wide barrier per phase.  GEMV outputs are left as
-// per-warp partial row sums (no atomics, no fences in the GEMV) and the consumer
-// phase sums them in a fixed order while building its input (norms, GELU*up,
-// attention heads) -- deterministic, and the reduction rides on the L2 reads
-// the consumer needs anyway.
+// shape) with tiny activations in between, so the time that is not weight
+// streaming is latency: the dependent steps between two GEMVs.  The kernel is
+// built to keep that chain short:
+//
+//  * Weights never wait for activations.  Every warp owns a balanced share of
+//    the tiles of every GEMV phase and streams its shares of ALL phases back to
+//    back through its own ring of bulk-copy stages (cp.async.bulk, mbarrier
+//    completion, L2 evict-first), so the stream runs on through prologues,
+//    attention and barriers.
+//  * One grid barrier per phase (a monotonic arrival counter).  A GEMV leaves a
+//    row tile that straddles two CTAs as one partial sum per CTA; the consumer
+//    adds them up, so producers need no fences or atomics beyond the barrier.
+//  * Every activation a phase reads comes into shared memory by bulk copies
+//    (the same engine as the weights, so thousands of small loads per SM do not
+//    queue behind the weight stream): the inputs that do not depend on the
+//    previous phase (residual, norm weights, the attention window's K/V rows,
+//    RoPE table) are issued BEFORE the grid barrier, the previous phase's
+//    output and its straddle partials right after it -- one copy wait each.
 #include <algorithm>
 
 #include "common.cuh"
 #include "core.cuh"
 #include "decode_step.cuh"
 
+// build-time tuning: stages per warp, tiles per stage
+#ifndef CH_MK_SPW
+#define CH_MK_SPW 2
+#endif
+#ifndef CH_MK_CT
+#define CH_MK_CT 6
+#endif
+
 namespace ch {
 
 namespace {
-constexpr int MK_NW = 16;  // warps per CTA (all stream + compute)
-constexpr int MK_SPW = 2;  // bulk-copy stages per warp
-constexpr int MK_CT = 6;   // tiles per stage
+constexpr int MK_NW = 16;          // warps per CTA (all stream + compute)
+constexpr int MK_SPW = CH_MK_SPW;  // bulk-copy stages per warp
+constexpr int MK_CT = CH_MK_CT;    // tiles per stage
 constexpr int MK_STAGE = MK_CT * kTileBytes;
 constexpr int MK_THREADS = MK_NW * 32;
 constexpr uint32_t kMinChunk = 64;
-constexpr uint32_t kVecRows = 4096;  // rows staged per gather in the GEMV prologues
+constexpr uint32_t kWinSlots = 64;  // attention slots per work item staged in shared memory before the barrier
+constexpr uint32_t kNoStraddle = 0xFFFFFFFFu;
+constexpr int kHeadDim = 256;
+constexpr uint32_t kMaxGrid = 255;  // straddle-list entries hold CTA ids in 8 bits
 }  // namespace
 
 int mk_warps() { return MK_NW; }
+
+// Optional per-phase timeline (build with -DCH_PHASE_TRACE, see channel_b200/phase_trace.py):
+// thread 0 of every CTA records %globaltimer at six points of each phase.
+#ifdef CH_PHASE_TRACE
+constexpr int kTraceCtas = 256, kTracePhases = 512, kTraceMarks = 6;
+__device__ unsigned long long g_phase_trace[kTraceCtas * kTracePhases * kTraceMarks];
+#define PHASE_MARK(pi, k)                                                                               \
+  do {                                                                                                  \
+    if (threadIdx.x == 0 && blockIdx.x < kTraceCtas && (pi) < kTracePhases)                             \
+      g_phase_trace[((size_t)blockIdx.x * kTracePhases + (pi)) * kTraceMarks + (k)] = globaltimer_ns(); \
+  } while (0)
+#else
+#define PHASE_MARK(pi, k) \
+  do {                    \
+  } while (0)
+#endif
 
 // ---------------------------------------------------------------------------
 // balanced partition of T tiles over GW warps: warp w owns [w*q + min(w,rem), ...)
@@ -46,23 +82,57 @@ CH_DEV uint32_t part_warp_of(uint32_t t, uint32_t q, uint32_t rem) {
   const uint32_t big = rem * (q + 1);
   return t < big ? t / (q + 1) : rem + (t - big) / q;
 }
-
 // CTA-level view of the same partition: CTA c owns tiles [cta_begin(c), cta_begin(c+1))
 CH_DEV uint32_t cta_begin(const GemvOut &o, uint32_t c) { return part_begin(c * MK_NW, o.q, o.rem); }
-CH_DEV uint32_t cta_of(const GemvOut &o, uint32_t t) { return part_warp_of(t, o.q, o.rem) / MK_NW; }
 
-// Finished rows [r0, r1) of a GEMV output (act mode: finished acts) into shared
-// memory: every row is final in `direct` after the phase barrier.
-CH_DEV void gather_rows(const GemvOut &o, uint32_t r0, uint32_t r1, float *dst) {
-  const uint32_t n = r1 - r0;
-  for (uint32_t i = threadIdx.x * 4; i < n; i += blockDim.x * 4) {
-    if (i + 4 <= n && ((r0 + i) & 3) == 0) {
-      *reinterpret_cast<float4 *>(dst + i) = __ldcg(reinterpret_cast<const float4 *>(o.direct + r0 + i));
-    } else {
-      for (uint32_t e = i; e < min(n, i + 4); e++) dst[e] = __ldcg(&o.direct[r0 + e]);
+// ---------------------------------------------------------------------------
+// Straddle list of a GEMV output: entry c-1 describes the CTA boundary in front of
+// CTA c.  When that boundary is the first one inside a row tile rt, the row tile
+// is the sum of the partial slots of CTAs c-1 .. c1 and the entry holds
+// rt | (c-1) << 16 | (c1-c+1) << 24; otherwise kNoStraddle.  One thread per entry.
+CH_DEV void build_slist(const GemvOut &o, uint32_t *slist) {
+  const uint32_t G = gridDim.x, KT = o.KT;
+  for (uint32_t c = 1 + threadIdx.x; c < G; c += blockDim.x) {
+    const uint32_t B = cta_begin(o, c);  // first tile of CTA c
+    const uint32_t rt = B / KT;
+    uint32_t e = kNoStraddle;
+    if (B != rt * KT && cta_begin(o, c - 1) <= rt * KT) {
+      const uint32_t t_hi = rt * KT + KT - 1;
+      uint32_t c1 = c;
+      while (c1 + 1 < G && cta_begin(o, c1 + 1) <= t_hi) c1++;
+      e = rt | ((c - 1) << 16) | ((c1 - (c - 1)) << 24);
     }
+    slist[c - 1] = e;
   }
-  __syncthreads();
+}
+// value of row `row` (0..15) of straddling row tile (rt, c0..c1) from the staged
+// CTA partials P[grid][2][16]: the CTAs' sums in CTA order
+CH_DEV float straddle_value(const GemvOut &o, const float *P, uint32_t e, uint32_t row) {
+  const uint32_t rt = e & 0xFFFFu, c0 = (e >> 16) & 0xFFu, c1 = c0 + (e >> 24);
+  const uint32_t t_lo = rt * o.KT;
+  float v = 0.f;
+  for (uint32_t cc = c0; cc <= c1; cc++) {
+    const uint32_t b = cta_begin(o, cc);
+    if (b == cta_begin(o, cc + 1)) continue;  // CTA without tiles
+    v = __fadd_rn(v, P[(cc * 2 + (b < t_lo ? 1u : 0u)) * 16 + row]);
+  }
+  return v;
+}
+// Patch the straddling rows of staged output rows [r0, r1) (dst[i] = row r0 + i);
+// act mode: act values [r0, r1) = gelu(gate) * up of the interleaved row tiles.
+CH_DEV void patch_staged(const GemvOut &o, const uint32_t *slist, const float *P, uint32_t r0, uint32_t r1,
+                         float *dst) {
+  const uint32_t per = o.act ? 8u : 16u, n = (gridDim.x - 1) * per;
+  for (uint32_t idx = threadIdx.x; idx < n; idx += blockDim.x) {
+    const uint32_t e = slist[idx / per];
+    if (e == kNoStraddle) continue;
+    const uint32_t row = idx % per, r = (e & 0xFFFFu) * per + row;
+    if (r < r0 || r >= r1) continue;
+    if (o.act)
+      dst[r - r0] = __fmul_rn(gelu_tanh(straddle_value(o, P, e, row)), straddle_value(o, P, e, row + 8));
+    else
+      dst[r - r0] = straddle_value(o, P, e, row);
+  }
 }
 
 // grid barrier on a monotonically increasing arrival counter (bounded wait)
@@ -70,13 +140,13 @@ CH_DEV void grid_barrier(unsigned long long *arrive, unsigned long long target, 
   __syncthreads();
   if (threadIdx.x == 0) {
     __threadfence();
-    atomicAdd(arrive, 1ull);
+    asm volatile("red.relaxed.gpu.global.add.u64 [%0], 1;" ::"l"(arrive) : "memory");
     unsigned long long v;
-    asm volatile("ld.acquire.gpu.u64 %0, [%1];" : "=l"(v) : "l"(arrive) : "memory");
+    asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(arrive) : "memory");
     if (v < target) {
       const uint64_t t0 = globaltimer_ns();
       for (;;) {
-        asm volatile("ld.acquire.gpu.u64 %0, [%1];" : "=l"(v) : "l"(arrive) : "memory");
+        asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(arrive) : "memory");
         if (v >= target) break;
         if (globaltimer_ns() - t0 > 2000000000ull) {
           atomicOr(err, DEV_ERR_PEER_TIMEOUT);
@@ -84,120 +154,196 @@ CH_DEV void grid_barrier(unsigned long long *arrive, unsigned long long target, 
         }
       }
     }
-    __threadfence();
   }
   __syncthreads();
 }
 
 // ---------------------------------------------------------------------------
-// per-warp weight stream over the GEMV phases
-struct Stream {
-  uint32_t ph, ck;  // next chunk to issue: phase index, chunk index within the warp's share
-};
-
-CH_DEV uint32_t warp_chunks(const Phase &p, uint32_t gw) {
-  const uint32_t tb = part_begin(gw, p.q, p.rem), te = part_begin(gw + 1, p.q, p.rem);
-  return (te - tb + MK_CT - 1) / MK_CT;
-}
-
-// advance `s` to the next (phase, chunk) to issue; false when the step's stream is done
-CH_DEV bool stream_next(const MegaArgs &a, uint32_t gw, Stream &s) {
-  while (s.ph < a.nphases) {
-    const Phase &p = a.phases[s.ph];
-    if (p.kind == PH_GEMV && s.ck < warp_chunks(p, gw)) return true;
-    s.ph++;
-    s.ck = 0;
+// input pairs: pair p = (32-block b = p/4, t = p%4) holds the 8 values at
+// k = 32b + 2t + {0,1, 8,9, 16,17, 24,25} -- exactly one lane's B fragments
+CH_DEV void ld_pair(const float *src, uint32_t p, float (&v)[8]) {
+  const float *q = src + (p >> 2) * 32 + (p & 3u) * 2;
+#pragma unroll
+  for (int i = 0; i < 4; i++) {
+    const float2 f = *reinterpret_cast<const float2 *>(q + 8 * i);
+    v[2 * i] = f.x, v[2 * i + 1] = f.y;
   }
-  return false;
 }
-
-CH_DEV void stream_issue(const MegaArgs &a, uint32_t gw, Stream &s, uint8_t *stage, uint64_t *bar) {
-  const Phase &p = a.phases[s.ph];
-  const uint32_t tb = part_begin(gw, p.q, p.rem), te = part_begin(gw + 1, p.q, p.rem);
-  const uint32_t t0 = tb + s.ck * MK_CT;
-  const uint32_t bytes = min((uint32_t)MK_CT, te - t0) * kTileBytes;
-  mbar_arrive_expect_tx(bar, bytes);
-  bulk_g2s(stage, p.tiles + (size_t)t0 * kTileBytes, bytes, bar);
-  s.ck++;
+CH_DEV void st_pair(float *dst, uint32_t p, const float (&v)[8]) {
+  float *q = dst + (p >> 2) * 32 + (p & 3u) * 2;
+#pragma unroll
+  for (int i = 0; i < 4; i++) *reinterpret_cast<float2 *>(q + 8 * i) = make_float2(v[2 * i], v[2 * i + 1]);
+}
+// f16 hi/lo B fragments of a pair: xf[p*2] = hi, xf[p*2+1] = lo (layout of block_to_fragments).
+// xf[p*2 .. p*2+1] occupies the bytes of floats [8p, 8p+8) of the same 32-block, so a
+// staged vector can be converted in place once every pair of the block has been read.
+CH_DEV void pair_to_fragments(const float (&v)[8], uint4 *xf_pair) {
+  __half h[8], l[8];
+#pragma unroll
+  for (int e = 0; e < 8; e++) {
+    h[e] = __float2half_rn(v[e]);
+    l[e] = __float2half_rn(__fsub_rn(v[e], __half2float(h[e])));
+  }
+  xf_pair[0] = make_uint4(pack_half2(h[0], h[1]), pack_half2(h[2], h[3]), pack_half2(h[4], h[5]), pack_half2(h[6], h[7]));
+  xf_pair[1] = make_uint4(pack_half2(l[0], l[1]), pack_half2(l[2], l[3]), pack_half2(l[4], l[5]), pack_half2(l[6], l[7]));
 }
 
 // ---------------------------------------------------------------------------
-// GEMV phase: input prologue (all threads) then each warp's share of tiles
+// Per-warp weight stream over the GEMV phases, driven by lane 0.  The descriptor
+// of the phase after the current one is loaded one transition ahead, so moving
+// on to the next phase never waits for memory.
+struct Stream {
+  uint32_t g, ck, nck, tb, te;  // GEMV stream index, next chunk, chunks of this warp's share, its tiles
+  const uint8_t *tiles;
+  uint4 nxt;                    // raw StreamDesc of stream g + 1
+};
+CH_DEV uint4 load_desc(const MegaArgs &a, uint32_t g) {
+  return g < a.nstreams ? __ldg(reinterpret_cast<const uint4 *>(a.streams + g)) : make_uint4(0u, 0u, 0u, 0u);
+}
+CH_DEV void stream_enter(uint32_t gw, Stream &s, const uint4 &d) {
+  s.tiles = reinterpret_cast<const uint8_t *>((uint64_t)d.x | ((uint64_t)d.y << 32));
+  s.tb = part_begin(gw, d.z, d.w);
+  s.te = part_begin(gw + 1, d.z, d.w);
+  s.nck = (s.te - s.tb + MK_CT - 1) / MK_CT;
+  s.ck = 0;
+}
+CH_DEV void stream_init(const MegaArgs &a, uint32_t gw, Stream &s) {
+  s.g = 0;
+  stream_enter(gw, s, load_desc(a, 0));
+  s.nxt = load_desc(a, 1);
+}
+// advance to the next chunk to issue; false when the step's stream is done
+CH_DEV bool stream_next(const MegaArgs &a, uint32_t gw, Stream &s) {
+  while (s.ck >= s.nck) {
+    if (s.g + 1 >= a.nstreams) return false;
+    s.g++;
+    stream_enter(gw, s, s.nxt);
+    s.nxt = load_desc(a, s.g + 1);
+  }
+  return true;
+}
+CH_DEV void stream_issue(Stream &s, uint8_t *stage, uint64_t *bar, uint64_t pol) {
+  const uint32_t t0 = s.tb + s.ck * MK_CT;
+  const uint32_t bytes = min((uint32_t)MK_CT, s.te - t0) * kTileBytes;
+  mbar_arrive_expect_tx(bar, bytes);
+  bulk_g2s_hint(stage, s.tiles + (size_t)t0 * kTileBytes, bytes, bar, pol);
+  s.ck++;
+}
+
+// phase struct -> shared memory with asynchronous 16-byte copies (threads 0..)
+CH_DEV void copy_phase(const Phase *src, Phase *dst) {
+  constexpr uint32_t n = sizeof(Phase) / 16;
+  static_assert(sizeof(Phase) % 16 == 0, "Phase is copied in 16-byte pieces");
+  if (threadIdx.x < n)
+    cp_async16(reinterpret_cast<uint8_t *>(dst) + threadIdx.x * 16,
+               reinterpret_cast<const uint8_t *>(src) + threadIdx.x * 16);
+}
+
+// ---------------------------------------------------------------------------
 struct SmemLayout {
   uint8_t *stages;
   uint64_t *bars;
+  uint64_t *vbar;   // staged activations: two arrivals per phase (before and after the grid barrier)
   uint4 *xzero;
-  float *wpart;  // [warps][2][16] partial segments of the current GEMV phase
-  uint8_t *u;    // union region
+  float *wpart;     // [warps][2][16] partial segments of the current GEMV phase
+  uint32_t *slist;  // [kMaxGrid] straddle list of the current phase's input
+  uint32_t *wphys;  // [2][kWinSlots] attention window slot ids (full, sliding lists)
+  uint8_t *u;       // union region (GEMV staging / attention / top-k)
+};
+// stage `bytes` from global into shared memory on vbar (any thread)
+CH_DEV void stage_copy(const SmemLayout &L, void *dst, const void *src, uint32_t bytes) {
+  mbar_expect_tx(L.vbar, bytes);
+  bulk_g2s(dst, src, bytes, L.vbar);
+}
+
+// GEMV staging in the union region (K floats each): S0 = previous output (then the
+// B fragments, in place); for the norm prologues S1 = residual, S2 = post-norm
+// weight, S3 = norm weight; then the straddle partials of the previous GEMV.
+CH_DEV uint32_t gemv_stage_vectors(uint32_t pm) { return (pm == PM_NORM || pm == PM_ADD_NORM) ? 4u : 1u; }
+struct GemvStage {
+  float *s0, *s1, *s2, *s3, *part;
+  __device__ GemvStage(uint8_t *u, uint32_t K, uint32_t pm) {
+    s0 = reinterpret_cast<float *>(u);
+    s1 = s0 + K;
+    s2 = s1 + K;
+    s3 = s2 + K;
+    part = s0 + gemv_stage_vectors(pm) * K;
+  }
 };
 
-CH_DEV void gemv_prologue(const Phase &p, const MegaArgs &a, uint4 *xf, float *vec, float *red) {
-  const uint32_t K = p.K, nb = K / 32;
+// GEMV input: B fragments of the phase's input vector, in place over S0
+CH_DEV void gemv_prologue(const Phase &p, const MegaArgs &a, const SmemLayout &L, float *red) {
+  const uint32_t K = p.K, npairs = K / 8, tid = threadIdx.x;
+  GemvStage S(L.u, K, p.pm);
+  uint4 *xf = reinterpret_cast<uint4 *>(S.s0);
   const bool writer = (blockIdx.x == 0);
-  if (p.pm == PM_DIRECT) {
-    for (uint32_t b = threadIdx.x; b < nb; b += blockDim.x) {
-      float v[32];
-      load32(p.x_in + b * 32, v);
-      block_to_fragments(v, xf + b * 8);
+  if (p.pm == PM_DIRECT || p.pm == PM_GELU) {  // S0 holds the input (act already = gelu(gate) * up)
+    if (p.pm == PM_GELU) {
+      patch_staged(p.r_in, L.slist, S.part, 0, K, S.s0);
+      __syncthreads();
     }
-    return;
-  }
-  if (p.pm == PM_GELU) {  // act vector finished by the gate|up phase
-    for (uint32_t b = threadIdx.x; b < nb; b += blockDim.x) {
-      float v[32];
-      const float4 *q = reinterpret_cast<const float4 *>(p.r_in.direct + b * 32);
+    constexpr int U = 2;
+    for (uint32_t q0 = 0; q0 < npairs; q0 += U * MK_THREADS) {
+      float v[U][8];
 #pragma unroll
-      for (int i = 0; i < 8; i++) {
-        const float4 f = __ldcg(q + i);
-        v[4 * i] = f.x, v[4 * i + 1] = f.y, v[4 * i + 2] = f.z, v[4 * i + 3] = f.w;
+      for (int u = 0; u < U; u++) {
+        const uint32_t q = q0 + u * MK_THREADS + tid;
+        if (q < npairs) ld_pair(S.s0, q, v[u]);
       }
-      block_to_fragments(v, xf + b * 8);
+      __syncthreads();  // every pair of these blocks read before the in-place writes
+#pragma unroll
+      for (int u = 0; u < U; u++) {
+        const uint32_t q = q0 + u * MK_THREADS + tid;
+        if (q < npairs) pair_to_fragments(v[u], xf + q * 2);
+      }
     }
     return;
   }
-  float ss = 0.f;
-  if (p.pm == PM_NORM) {
-    for (uint32_t b = threadIdx.x; b < nb; b += blockDim.x) {
-      float v[32];
-      load32(p.x_in + b * 32, v);
+  // PM_NORM / PM_ADD_NORM: one pair per thread (K <= 8 * threads)
+  const bool on = tid < npairs;
+  float x[8], w[8];
 #pragma unroll
-      for (int e = 0; e < 32; e++) ss = __fmaf_rn(v[e], v[e], ss);
-      store32(vec + b * 32, v);
+  for (int e = 0; e < 8; e++) x[e] = 0.f, w[e] = 0.f;
+  if (p.pm == PM_ADD_NORM) {  // x = (x_in + [rmsnorm(r) * post_w]) * scalar     (add_rmsnorm.wgsl:15-51)
+    patch_staged(p.r_in, L.slist, S.part, 0, K, S.s0);
+    __syncthreads();
+    float r[8];
+#pragma unroll
+    for (int e = 0; e < 8; e++) r[e] = 0.f;
+    if (on) {
+      ld_pair(S.s0, tid, r);
+      ld_pair(S.s1, tid, x);
+      if (p.post_w) ld_pair(S.s2, tid, w);
     }
-  } else {  // PM_ADD_NORM: r' = post_w ? rmsnorm(r) * post_w : r ; x = (x_in + r') * scalar
-    gather_rows(p.r_in, 0, K, vec);
     float inv_r = 1.0f;
     if (p.post_w) {
       float sr = 0.f;
-      for (uint32_t i = threadIdx.x; i < K; i += blockDim.x) sr = __fmaf_rn(vec[i], vec[i], sr);
+#pragma unroll
+      for (int e = 0; e < 8; e++) sr = __fmaf_rn(r[e], r[e], sr);
       sr = block_sum(sr, red);
       inv_r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sr, (float)K), a.eps)));
     }
-    for (uint32_t b = threadIdx.x; b < nb; b += blockDim.x) {
-      float r[32], x[32], w[32];
-      load32(vec + b * 32, r);
-      load32(p.x_in + b * 32, x);
-      if (p.post_w) load32(p.post_w + b * 32, w);
 #pragma unroll
-      for (int e = 0; e < 32; e++) {
-        const float rr = p.post_w ? __fmul_rn(__fmul_rn(r[e], inv_r), w[e]) : r[e];
-        x[e] = __fmul_rn(__fadd_rn(x[e], rr), p.scalar);
-        ss = __fmaf_rn(x[e], x[e], ss);
-      }
-      store32(vec + b * 32, x);
-      if (writer && p.x_out) store32(p.x_out + b * 32, x);
+    for (int e = 0; e < 8; e++) {
+      const float rr = p.post_w ? __fmul_rn(__fmul_rn(r[e], inv_r), w[e]) : r[e];
+      x[e] = __fmul_rn(__fadd_rn(x[e], rr), p.scalar);
     }
+    if (writer && p.x_out && on) st_pair(p.x_out, tid, x);
+  } else if (on) {
+    ld_pair(S.s1, tid, x);
   }
-  ss = block_sum(ss, red);
-  const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)K), a.eps)));
-  for (uint32_t b = threadIdx.x; b < nb; b += blockDim.x) {
-    float v[32], w[32];
-    load32(vec + b * 32, v);
-    load32(p.norm_w + b * 32, w);
+  float ss = 0.f;
 #pragma unroll
-    for (int e = 0; e < 32; e++) v[e] = __fmul_rn(__fmul_rn(v[e], inv), w[e]);
-    if (writer && p.normed_out) store32(p.normed_out + b * 32, v);
-    block_to_fragments(v, xf + b * 8);
+  for (int e = 0; e < 8; e++) ss = __fmaf_rn(x[e], x[e], ss);
+  ss = block_sum(ss, red);  // also orders every read of S0 before the in-place fragment writes
+  const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)K), a.eps)));
+  if (on) {
+    float nw[8], v[8];
+    ld_pair(S.s3, tid, nw);
+#pragma unroll
+    for (int e = 0; e < 8; e++) v[e] = __fmul_rn(__fmul_rn(x[e], inv), nw[e]);
+    if (writer && p.normed_out) st_pair(p.normed_out, tid, v);
+    pair_to_fragments(v, xf + tid * 2);
   }
 }
 
@@ -228,39 +374,15 @@ CH_DEV void cta_combine(const Phase &p, const float *wpart) {
       } else if (lane < 16) {
         p.out.direct[rt * 16 + lane] = sum;
       }
-    } else {
-      // straddling row tile: publish this CTA's sum; the last CTA to arrive finishes it
-      const uint32_t slot = cb < t_lo ? 1u : 0u;
-      if (lane < 16) p.out.partial[((size_t)c * 2 + slot) * 16 + lane] = sum;
-      __threadfence();
-      __syncwarp();
-      uint32_t old = 0;
-      if (lane == 0) old = atomicAdd(&p.out.counters[rt], 1u);
-      old = __shfl_sync(0xffffffffu, old, 0);
-      const uint32_t c0 = cta_of(p.out, t_lo), c1 = cta_of(p.out, t_hi);
-      if (old == c1 - c0) {
-        __threadfence();
-        float tot = 0.f;
-        if (lane < 16)
-          for (uint32_t cc = c0; cc <= c1; cc++) {
-            const uint32_t sl = cta_begin(p.out, cc) < t_lo ? 1u : 0u;
-            tot = __fadd_rn(tot, __ldcg(&p.out.partial[((size_t)cc * 2 + sl) * 16 + lane]));
-          }
-        const float tup = __shfl_down_sync(0xffffffffu, tot, 8);
-        if (p.out.act) {
-          if (lane < 8) p.out.direct[rt * 8 + lane] = __fmul_rn(gelu_tanh(tot), tup);
-        } else if (lane < 16) {
-          p.out.direct[rt * 16 + lane] = tot;
-        }
-        if (lane == 0) p.out.counters[rt] = 0u;
-      }
+    } else if (lane < 16) {  // straddling row tile: this CTA's share, added up by the consumer
+      p.out.partial[((size_t)c * 2 + (cb < t_lo ? 1u : 0u)) * 16 + lane] = sum;
     }
   }
 }
 
 template <int FMT>
 CH_DEV void gemv_tiles(const Phase &p, const MegaArgs &a, uint32_t gw, const SmemLayout &L, const uint4 *xf,
-                       uint32_t &cidx, Stream &st, bool &ok) {
+                       uint32_t &cidx, Stream &st, bool &ok, uint64_t pol) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int g = lane >> 2, t = lane & 3;
   uint8_t *my_stages = L.stages + (size_t)warp * MK_SPW * MK_STAGE;
@@ -333,7 +455,7 @@ CH_DEV void gemv_tiles(const Phase &p, const MegaArgs &a, uint32_t gw, const Sme
     cidx++;
     if (lane == 0 && stream_next(a, gw, st)) {
       fence_proxy_async();
-      stream_issue(a, gw, st, my_stages + (size_t)s * MK_STAGE, &my_bars[s]);
+      stream_issue(st, my_stages + (size_t)s * MK_STAGE, &my_bars[s], pol);
     }
     __syncwarp();
   }
@@ -342,237 +464,422 @@ CH_DEV void gemv_tiles(const Phase &p, const MegaArgs &a, uint32_t gw, const Sme
 
 // ---------------------------------------------------------------------------
 // ATTN phase: work item (kv head, slot chunk) per CTA; qkv_rope.wgsl + decode_attn.wgsl
-template <int R>
-CH_DEV void attn_phase(const Phase &p, const MegaArgs &a, uint8_t *u, float *red) {
-  constexpr int D = 256, EPL = 8;
-  constexpr int PVW = (R <= 2) ? MK_NW : (MK_NW * 2 / R);  // warps accumulating P*V (bounds smem)
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const StepParams sp = *a.sp;
-  const uint32_t S = p.is_sliding ? sp.n_sliding : sp.n_active;
-  const uint32_t *list = p.is_sliding ? sp.sliding : sp.active;
-  const uint32_t max_splits = a.attn_max_splits;
-  const uint32_t chunk = max(kMinChunk, (S + max_splits - 1) / max_splits);
-  const uint32_t nsplit = S == 0 ? 1u : (S + chunk - 1) / chunk;
+struct AttnItem {
+  uint32_t S, nsplit, chunk, kvh, split, c0, n;
+  const uint32_t *list;
+  bool active;
+};
+CH_DEV AttnItem attn_item(const MegaArgs &a, const StepParams &sp, uint32_t is_sliding) {
+  AttnItem it;
+  it.S = is_sliding ? sp.n_sliding : sp.n_active;
+  it.list = is_sliding ? sp.sliding : sp.active;
+  it.chunk = max(kMinChunk, (it.S + a.attn_max_splits - 1) / a.attn_max_splits);
+  it.nsplit = it.S == 0 ? 1u : (it.S + it.chunk - 1) / it.chunk;
   const uint32_t item = blockIdx.x;
-  if (item >= a.nkv * nsplit) return;
-  const uint32_t kvh = item / nsplit, split = item % nsplit;
-  const uint32_t c0 = split * chunk, c1 = min(S, c0 + chunk), n = c1 > c0 ? c1 - c0 : 0;
+  it.active = item < a.nkv * it.nsplit;
+  it.kvh = item / it.nsplit;
+  it.split = item % it.nsplit;
+  it.c0 = it.split * it.chunk;
+  const uint32_t c1 = min(it.S, it.c0 + it.chunk);
+  it.n = c1 > it.c0 ? c1 - it.c0 : 0;
+  return it;
+}
+
+// Shared-memory layout of the ATTN phase (inside the union region).
+template <int R>
+struct AttnSmem {
+  static constexpr int D = kHeadDim;
+  float *q_s;      // [R][D] q heads (staged raw, normed + roped in place)
+  float *k_new;    // [D]   this step's K row (staged raw, then f16-rounded)
+  float *v_new;    // [D]
+  float *qn_w;     // [D]   q_norm weight      (staged before the barrier)
+  float *kn_w;     // [D]   k_norm weight      (staged before the barrier)
+  float2 *cs;      // [D/2] RoPE (cos, sin)    (staged before the barrier)
+  __half *kv;      // [2][kWinSlots][D] K then V rows of the window (staged before the barrier)
+  float *o_s;      // [MK_NW][R][D] per-warp P*V (overlays kv once scores and P*V are done)
+  float *sc;       // [R][chunk_cap]
+  float *cmb;      // [R][max_splits] split maxima, then weights
+  float *cml;      // [R][max_splits] split sums
+  float *stat;     // [2R]
+  float *part;     // [grid][2][16] straddle partials of the q|k|v GEMV
+  __device__ AttnSmem(uint8_t *u, uint32_t chunk_cap, uint32_t max_splits) {
+    q_s = reinterpret_cast<float *>(u);
+    k_new = q_s + R * D;
+    v_new = k_new + D;
+    qn_w = v_new + D;
+    kn_w = qn_w + D;
+    cs = reinterpret_cast<float2 *>(kn_w + D);
+    kv = reinterpret_cast<__half *>(cs + D / 2);
+    o_s = reinterpret_cast<float *>(kv);
+    const size_t kv_bytes = (size_t)2 * kWinSlots * D * 2, os_bytes = (size_t)MK_NW * R * D * 4;
+    sc = reinterpret_cast<float *>(reinterpret_cast<uint8_t *>(kv) + (kv_bytes > os_bytes ? kv_bytes : os_bytes));
+    cmb = sc + R * chunk_cap;
+    cml = cmb + R * max_splits;
+    stat = cml + R * max_splits;
+    part = reinterpret_cast<float *>((reinterpret_cast<uintptr_t>(stat + 2 * R) + 15) & ~(uintptr_t)15);
+  }
+};
+CH_DEV uint32_t attn_chunk_cap(const MegaArgs &a) {
+  return max(kMinChunk, (a.cache_slots + a.attn_max_splits - 1) / a.attn_max_splits);
+}
+
+// Once per step: the window's slot ids of this CTA's work item for the full and the
+// sliding lists (the lists do not change within a step).
+CH_DEV void attn_lists_init(const MegaArgs &a, const StepParams &sp, uint32_t *wphys) {
+  for (uint32_t v = 0; v < 2; v++) {
+    const AttnItem it = attn_item(a, sp, v);
+    for (uint32_t i = threadIdx.x; i < kWinSlots; i += MK_THREADS)
+      wphys[v * kWinSlots + i] = (it.active && i < it.n) ? __ldcg(it.list + it.c0 + i) : 0xFFFFFFFFu;
+  }
+}
+
+// before the barrier: bulk copies of the window's K/V rows, the head norm weights
+// and the RoPE table into shared memory; the rest of the chunk toward L2
+template <int R>
+CH_DEV void attn_pre(const Phase &p, const MegaArgs &a, const StepParams &sp, const SmemLayout &L) {
+  constexpr int D = kHeadDim;
+  const AttnItem it = attn_item(a, sp, p.is_sliding);
+  if (!it.active) return;
+  AttnSmem<R> sm(L.u, attn_chunk_cap(a), a.attn_max_splits);
   const size_t kv_dim = (size_t)a.nkv * D;
-  const uint32_t chunk_cap = max(kMinChunk, (a.cache_slots + max_splits - 1) / max_splits);
-
-  float *raw = reinterpret_cast<float *>(u);   // [R+2][D]
-  float *q_s = raw, *k_new = raw + R * D, *v_new = k_new + D;
-  float *o_s = v_new + D;                      // [PVW][R][D]
-  float *sc = o_s + PVW * R * D;               // [R][chunk_cap]
-  float *cmb = sc + R * chunk_cap;             // [R][max_splits]
-  float *stat = cmb + R * max_splits;          // [2R]
-
-  // prefetch this CTA's K/V rows toward L2 while the heads are assembled
-  for (uint32_t i = c0 + tid; i < c1; i += MK_THREADS) {
-    const uint32_t phys = list[i];
+  const uint32_t *wp = L.wphys + p.is_sliding * kWinSlots;
+  const uint32_t t = threadIdx.x;
+  if (t < 2 * kWinSlots) {  // one 512-byte row per thread: K rows, then V rows
+    const uint32_t i = t % kWinSlots, which = t / kWinSlots;
+    const uint32_t phys = i < it.n ? wp[i] : 0xFFFFFFFFu;
+    if (phys < a.cache_slots && phys != sp.slot) {
+      const __half *src = (which ? p.v_cache : p.k_cache) + (size_t)phys * kv_dim + (size_t)it.kvh * D;
+      stage_copy(L, sm.kv + (size_t)(which * kWinSlots + i) * D, src, D * 2);
+    }
+  } else if (t == 2 * kWinSlots) {
+    stage_copy(L, sm.qn_w, p.q_norm_w, D * 4);
+    stage_copy(L, sm.kn_w, p.k_norm_w, D * 4);
+    stage_copy(L, sm.cs, p.rope_cs, a.rot * 4);  // rot/2 (cos, sin) pairs
+  }
+  for (uint32_t i = kWinSlots + threadIdx.x; i < it.n; i += MK_THREADS) {
+    const uint32_t phys = __ldcg(it.list + it.c0 + i);
     if (phys < a.cache_slots) {
-      const __half *kr = p.k_cache + (size_t)phys * kv_dim + (size_t)kvh * D;
-      const __half *vr = p.v_cache + (size_t)phys * kv_dim + (size_t)kvh * D;
-      asm volatile("prefetch.global.L2 [%0];" ::"l"(kr));
-      asm volatile("prefetch.global.L2 [%0];" ::"l"(kr + 128));
-      asm volatile("prefetch.global.L2 [%0];" ::"l"(vr));
-      asm volatile("prefetch.global.L2 [%0];" ::"l"(vr + 128));
+      const size_t off = (size_t)phys * kv_dim + (size_t)it.kvh * D;
+      asm volatile("prefetch.global.L2 [%0];" ::"l"(p.k_cache + off));
+      asm volatile("prefetch.global.L2 [%0];" ::"l"(p.k_cache + off + 128));
+      asm volatile("prefetch.global.L2 [%0];" ::"l"(p.v_cache + off));
+      asm volatile("prefetch.global.L2 [%0];" ::"l"(p.v_cache + off + 128));
     }
   }
-  // raw q heads | k | v rows of this kv head from the q|k|v GEMV output
-  gather_rows(p.r_in, kvh * R * D, (kvh + 1) * R * D, raw);
-  gather_rows(p.r_in, a.nq * D + kvh * D, a.nq * D + (kvh + 1) * D, k_new);
-  gather_rows(p.r_in, a.nq * D + (uint32_t)kv_dim + kvh * D, a.nq * D + (uint32_t)kv_dim + (kvh + 1) * D, v_new);
-  for (int h = warp; h < R + 2; h += MK_NW) {
-    float *hd = raw + h * D;
-    if (h <= R)
-      head_norm_rope_s(hd, h < R ? p.q_norm_w : p.k_norm_w, hd, D, a.rot, p.rope_cs, a.eps, true, lane);
-    else
-      head_norm_rope_s(hd, nullptr, hd, D, a.rot, nullptr, a.eps, false, lane);
-    __syncwarp();
-    if (h >= R) {  // f16 cache row of the new K / V, written by split 0
-      __half *dst = (h == R ? p.k_cache : p.v_cache) + (size_t)sp.slot * kv_dim + (size_t)kvh * D;
-      for (uint32_t d = lane; d < D; d += 32) {
-        const __half hv = __float2half_rn(hd[d]);
-        hd[d] = __half2float(hv);
-        if (split == 0 && sp.slot < a.cache_slots) dst[d] = hv;
+}
+// right after the barrier (thread 0): this kv head's q | k | v rows and the q|k|v partials
+template <int R>
+CH_DEV void attn_post_copies(const Phase &p, const MegaArgs &a, const StepParams &sp, const SmemLayout &L) {
+  constexpr int D = kHeadDim;
+  const AttnItem it = attn_item(a, sp, p.is_sliding);
+  if (!it.active) return;
+  AttnSmem<R> sm(L.u, attn_chunk_cap(a), a.attn_max_splits);
+  const uint32_t kvh = it.kvh, kv_dim = a.nkv * D;
+  stage_copy(L, sm.q_s, p.r_in.direct + kvh * R * D, R * D * 4);
+  stage_copy(L, sm.k_new, p.r_in.direct + a.nq * D + kvh * D, D * 4);
+  stage_copy(L, sm.v_new, p.r_in.direct + a.nq * D + kv_dim + kvh * D, D * 4);
+  stage_copy(L, sm.part, p.r_in.partial, gridDim.x * 32 * 4);
+}
+
+template <int R>
+CH_DEV void attn_phase(const Phase &p, const MegaArgs &a, const StepParams &sp, const SmemLayout &L) {
+  constexpr int D = kHeadDim, EPL = 8;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const AttnItem it = attn_item(a, sp, p.is_sliding);
+  if (!it.active) return;
+  const uint32_t max_splits = a.attn_max_splits, n = it.n, kvh = it.kvh;
+  const size_t kv_dim = (size_t)a.nkv * D;
+  const uint32_t chunk_cap = attn_chunk_cap(a);
+  AttnSmem<R> sm(L.u, chunk_cap, max_splits);
+  const uint32_t *wp = L.wphys + p.is_sliding * kWinSlots;
+
+  // 0. straddling rows of the staged heads
+  patch_staged(p.r_in, L.slist, sm.part, kvh * R * D, (kvh + 1) * R * D, sm.q_s);
+  patch_staged(p.r_in, L.slist, sm.part, a.nq * D + kvh * D, a.nq * D + (kvh + 1) * D, sm.k_new);
+  patch_staged(p.r_in, L.slist, sm.part, a.nq * D + (uint32_t)kv_dim + kvh * D,
+               a.nq * D + (uint32_t)kv_dim + (kvh + 1) * D, sm.v_new);
+  __syncthreads();
+  // 1. q heads | k | v of this kv head: warp h norms and ropes head h in registers, in place
+  if (warp < R + 2) {
+    float *hd = warp < R ? sm.q_s + warp * D : (warp == R ? sm.k_new : sm.v_new);
+    float v[8];
+#pragma unroll
+    for (int e = 0; e < 8; e++) v[e] = hd[lane * 8 + e];
+    float ss = 0.f;
+#pragma unroll
+    for (int e = 0; e < 8; e++) ss = __fmaf_rn(v[e], v[e], ss);
+    ss = warp_sum(ss);
+    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)D), a.eps)));
+    float out[8];
+    if (warp <= R) {  // rmsnorm * w, then RoPE half-split at `clock` (qkv_rope.wgsl; kernels.zig:101-119)
+      const float *w = warp < R ? sm.qn_w : sm.kn_w;
+      float y[8], part[8];
+#pragma unroll
+      for (int e = 0; e < 8; e++) y[e] = __fmul_rn(__fmul_rn(v[e], inv), w[lane * 8 + e]);
+      const uint32_t half = a.rot / 2, lh = half / 8;
+      const int src = (uint32_t)lane < lh ? lane + (int)lh : lane - (int)lh;
+#pragma unroll
+      for (int e = 0; e < 8; e++) part[e] = __shfl_sync(0xffffffffu, y[e], src);
+#pragma unroll
+      for (int e = 0; e < 8; e++) {
+        const uint32_t d = lane * 8 + e;
+        if (d < half) {
+          const float2 c = sm.cs[d];
+          out[e] = __fsub_rn(__fmul_rn(y[e], c.x), __fmul_rn(part[e], c.y));
+        } else if (d < a.rot) {
+          const float2 c = sm.cs[d - half];
+          out[e] = __fadd_rn(__fmul_rn(part[e], c.y), __fmul_rn(y[e], c.x));
+        } else {
+          out[e] = y[e];
+        }
+      }
+    } else {  // v: unit rmsnorm
+#pragma unroll
+      for (int e = 0; e < 8; e++) out[e] = __fmul_rn(v[e], inv);
+    }
+    if (warp >= R) {  // f16 cache row of the new K / V (written by split 0); scores use the rounded values
+      __half hv[8];
+#pragma unroll
+      for (int e = 0; e < 8; e++) {
+        hv[e] = __float2half_rn(out[e]);
+        out[e] = __half2float(hv[e]);
+      }
+      if (it.split == 0 && sp.slot < a.cache_slots) {
+        __half *dst = (warp == R ? p.k_cache : p.v_cache) + (size_t)sp.slot * kv_dim + (size_t)kvh * D + lane * 8;
+        *reinterpret_cast<uint4 *>(dst) = make_uint4(pack_half2(hv[0], hv[1]), pack_half2(hv[2], hv[3]),
+                                                     pack_half2(hv[4], hv[5]), pack_half2(hv[6], hv[7]));
       }
     }
+    __syncwarp();
+    *reinterpret_cast<float4 *>(hd + lane * 8) = make_float4(out[0], out[1], out[2], out[3]);
+    *reinterpret_cast<float4 *>(hd + lane * 8 + 4) = make_float4(out[4], out[5], out[6], out[7]);
   }
-  if (split == 0 && sp.slot >= a.cache_slots && tid == 0) atomicOr(a.err, DEV_ERR_BAD_SLOT);
+  if (it.split == 0 && sp.slot >= a.cache_slots && tid == 0) atomicOr(a.err, DEV_ERR_BAD_SLOT);
   __syncthreads();
 
-  // scores
+  // 2. scores: warp w takes slots w, w+16, ...; lane holds d = lane*8 .. +7
   float qr[R][EPL];
 #pragma unroll
   for (int h = 0; h < R; h++)
 #pragma unroll
-    for (int e = 0; e < EPL; e++) qr[h][e] = q_s[h * D + lane * EPL + e];
-  for (uint32_t i = warp; i < n; i += MK_NW) {
-    const uint32_t phys = list[c0 + i];
-    float kv[EPL];
-    bool valid = true;
-    if (phys == sp.slot) {
+    for (int e = 0; e < EPL; e++) qr[h][e] = sm.q_s[h * D + lane * EPL + e];
+  auto unpack = [&](const uint4 &rw, float (&f)[EPL]) {
+    const __half2 *hp = reinterpret_cast<const __half2 *>(&rw);
 #pragma unroll
-      for (int e = 0; e < EPL; e++) kv[e] = k_new[lane * EPL + e];
-    } else if (phys < a.cache_slots) {
-      const uint4 rw = *reinterpret_cast<const uint4 *>(p.k_cache + (size_t)phys * kv_dim + (size_t)kvh * D + lane * EPL);
-      const __half2 *hp = reinterpret_cast<const __half2 *>(&rw);
-#pragma unroll
-      for (int e = 0; e < EPL / 2; e++) {
-        const float2 f = __half22float2(hp[e]);
-        kv[2 * e] = f.x;
-        kv[2 * e + 1] = f.y;
-      }
-    } else {
-      valid = false;
-#pragma unroll
-      for (int e = 0; e < EPL; e++) kv[e] = 0.f;
+    for (int e = 0; e < EPL / 2; e++) {
+      const float2 x = __half22float2(hp[e]);
+      f[2 * e] = x.x;
+      f[2 * e + 1] = x.y;
     }
+  };
+  // row of slot i (window slots from shared memory, the rest from global / L2)
+  auto row = [&](uint32_t i, uint32_t which, float (&f)[EPL], uint32_t &phys) {
+    phys = i < kWinSlots ? wp[i] : __ldcg(it.list + it.c0 + i);
+    if (phys == sp.slot) {
+      const float *src = which ? sm.v_new : sm.k_new;
+#pragma unroll
+      for (int e = 0; e < EPL; e++) f[e] = src[lane * EPL + e];
+    } else if (phys < a.cache_slots) {
+      if (i < kWinSlots)
+        unpack(*reinterpret_cast<const uint4 *>(sm.kv + (size_t)(which * kWinSlots + i) * D + lane * EPL), f);
+      else
+        unpack(__ldcg(reinterpret_cast<const uint4 *>((which ? p.v_cache : p.k_cache) + (size_t)phys * kv_dim +
+                                                       (size_t)kvh * D + lane * EPL)),
+               f);
+    } else {
+#pragma unroll
+      for (int e = 0; e < EPL; e++) f[e] = 0.f;
+    }
+  };
+  for (uint32_t i = warp; i < n; i += MK_NW) {
+    float kv[EPL];
+    uint32_t phys;
+    row(i, 0, kv, phys);
+    const bool valid = phys < a.cache_slots;
 #pragma unroll
     for (int h = 0; h < R; h++) {
       float dot = 0.f;
 #pragma unroll
       for (int e = 0; e < EPL; e++) dot = __fmaf_rn(qr[h][e], kv[e], dot);
       dot = warp_sum(dot);
-      if (lane == 0) sc[h * chunk_cap + i] = valid ? __fmul_rn(dot, p.attn_scale) : -INFINITY;
+      if (lane == 0) sm.sc[h * chunk_cap + i] = valid ? __fmul_rn(dot, p.attn_scale) : -INFINITY;
     }
     if (!valid && lane == 0) atomicOr(a.err, DEV_ERR_BAD_LIST);
   }
   __syncthreads();
+  // 3. softmax statistics per head over this chunk (max seeded at -1e9, decode_attn.wgsl:261)
   for (int h = warp; h < R; h += MK_NW) {
-    float m = -1e9f;  // decode_attn.wgsl:261
-    for (uint32_t i = lane; i < n; i += 32) m = fmaxf(m, sc[h * chunk_cap + i]);
+    float m = -1e9f;
+    for (uint32_t i = lane; i < n; i += 32) m = fmaxf(m, sm.sc[h * chunk_cap + i]);
     m = warp_max(m);
     float l = 0.f;
     for (uint32_t i = lane; i < n; i += 32) {
-      const float e = expf(__fsub_rn(sc[h * chunk_cap + i], m));
-      sc[h * chunk_cap + i] = e;
+      const float e = expf(__fsub_rn(sm.sc[h * chunk_cap + i], m));
+      sm.sc[h * chunk_cap + i] = e;
       l = __fadd_rn(l, e);
     }
     l = warp_sum(l);
     if (lane == 0) {
-      stat[2 * h] = m;
-      stat[2 * h + 1] = l;
+      sm.stat[2 * h] = m;
+      sm.stat[2 * h + 1] = l;
     }
   }
   __syncthreads();
-  // weighted V (PVW warps)
-  if (warp < PVW) {
+  // 4. weighted V: every warp over its slots, then a fixed-order sum over warps
+  {
     float acc[R][EPL];
 #pragma unroll
     for (int h = 0; h < R; h++)
 #pragma unroll
       for (int e = 0; e < EPL; e++) acc[h][e] = 0.f;
-    for (uint32_t i = warp; i < n; i += PVW) {
-      const uint32_t phys = list[c0 + i];
+    for (uint32_t i = warp; i < n; i += MK_NW) {
       float vv[EPL];
-      if (phys == sp.slot) {
-#pragma unroll
-        for (int e = 0; e < EPL; e++) vv[e] = v_new[lane * EPL + e];
-      } else if (phys < a.cache_slots) {
-        const uint4 rw =
-            *reinterpret_cast<const uint4 *>(p.v_cache + (size_t)phys * kv_dim + (size_t)kvh * D + lane * EPL);
-        const __half2 *hp = reinterpret_cast<const __half2 *>(&rw);
-#pragma unroll
-        for (int e = 0; e < EPL / 2; e++) {
-          const float2 f = __half22float2(hp[e]);
-          vv[2 * e] = f.x;
-          vv[2 * e + 1] = f.y;
-        }
-      } else {
-#pragma unroll
-        for (int e = 0; e < EPL; e++) vv[e] = 0.f;
-      }
+      uint32_t phys;
+      row(i, 1, vv, phys);
 #pragma unroll
       for (int h = 0; h < R; h++) {
-        const float pr = sc[h * chunk_cap + i];
+        const float pr_ = sm.sc[h * chunk_cap + i];
 #pragma unroll
-        for (int e = 0; e < EPL; e++) acc[h][e] = __fmaf_rn(pr, vv[e], acc[h][e]);
+        for (int e = 0; e < EPL; e++) acc[h][e] = __fmaf_rn(pr_, vv[e], acc[h][e]);
       }
     }
+    __syncthreads();  // o_s overlays the K/V window
 #pragma unroll
-    for (int h = 0; h < R; h++)
-#pragma unroll
-      for (int e = 0; e < EPL; e++) o_s[(warp * R + h) * D + lane * EPL + e] = acc[h][e];
+    for (int h = 0; h < R; h++) {
+      float *dst = sm.o_s + (warp * R + h) * D + lane * EPL;
+      *reinterpret_cast<float4 *>(dst) = make_float4(acc[h][0], acc[h][1], acc[h][2], acc[h][3]);
+      *reinterpret_cast<float4 *>(dst + 4) = make_float4(acc[h][4], acc[h][5], acc[h][6], acc[h][7]);
+    }
   }
   __syncthreads();
-  float *part = a.attn_partial + ((size_t)(kvh * max_splits + split) * R) * (D + 2);
+  if (it.nsplit == 1) {  // whole list in this CTA: normalize and write (same arithmetic as a 1-split combine)
+    for (int idx = tid; idx < R * D; idx += MK_THREADS) {
+      const int h = idx / D, d = idx % D;
+      float s = 0.f;
+#pragma unroll
+      for (int w = 0; w < MK_NW; w++) s = __fadd_rn(s, sm.o_s[(w * R + h) * D + d]);
+      const float Lsum = __fmaf_rn(sm.stat[2 * h + 1], 1.0f, 0.f);
+      p.attn_out[(size_t)(kvh * R + h) * D + d] =
+          __fmul_rn(__fmaf_rn(s, 1.0f, 0.f), __fdiv_rn(1.0f, __fadd_rn(Lsum, 1e-9f)));
+    }
+    return;
+  }
+  float *part = a.attn_partial + ((size_t)(kvh * max_splits + it.split) * R) * (D + 2);
   for (int idx = tid; idx < R * D; idx += MK_THREADS) {
     const int h = idx / D, d = idx % D;
     float s = 0.f;
 #pragma unroll
-    for (int w = 0; w < PVW; w++) s = __fadd_rn(s, o_s[(w * R + h) * D + d]);
+    for (int w = 0; w < MK_NW; w++) s = __fadd_rn(s, sm.o_s[(w * R + h) * D + d]);
     part[h * (D + 2) + d] = s;
   }
   if (tid < R) {
-    part[tid * (D + 2) + D] = stat[2 * tid];
-    part[tid * (D + 2) + D + 1] = stat[2 * tid + 1];
+    part[tid * (D + 2) + D] = sm.stat[2 * tid];
+    part[tid * (D + 2) + D + 1] = sm.stat[2 * tid + 1];
   }
   __threadfence();
   __syncthreads();
   __shared__ uint32_t last_flag;
-  if (tid == 0) last_flag = (atomicAdd(&a.attn_counters[kvh], 1u) == nsplit - 1) ? 1u : 0u;
+  if (tid == 0) last_flag = (atomicAdd(&a.attn_counters[kvh], 1u) == it.nsplit - 1) ? 1u : 0u;
   __syncthreads();
   if (!last_flag) return;
   __threadfence();
+  // 5. last CTA of this kv head: log-sum-exp combine of the splits, all loads in flight at once
   const float *base = a.attn_partial + ((size_t)kvh * max_splits * R) * (D + 2);
-  for (int idx = tid; idx < R * (int)nsplit; idx += MK_THREADS) {
-    const int h = idx / nsplit, j = idx % nsplit;
-    cmb[h * max_splits + j] = __ldcg(&base[((size_t)j * R + h) * (D + 2) + D]);
-  }
-  __syncthreads();
-  if (tid < R) {
-    float M = -INFINITY, Lsum = 0.f;
-    for (uint32_t j = 0; j < nsplit; j++) M = fmaxf(M, cmb[tid * max_splits + j]);
-    for (uint32_t j = 0; j < nsplit; j++) {
-      const float f = expf(__fsub_rn(cmb[tid * max_splits + j], M));
-      Lsum = __fmaf_rn(__ldcg(&base[((size_t)j * R + tid) * (D + 2) + D + 1]), f, Lsum);
-      cmb[tid * max_splits + j] = f;
-    }
-    stat[2 * tid] = __fdiv_rn(1.0f, __fadd_rn(Lsum, 1e-9f));
-  }
-  __syncthreads();
-  for (int idx = tid; idx < R * D; idx += MK_THREADS) {
+  const uint32_t nsplit = it.nsplit;
+  for (int idx0 = 0; idx0 < R * D; idx0 += MK_THREADS) {
+    const int idx = idx0 + tid;
     const int h = idx / D, d = idx % D;
-    float O = 0.f;
-    for (uint32_t j = 0; j < nsplit; j++)
-      O = __fmaf_rn(__ldcg(&base[((size_t)j * R + h) * (D + 2) + d]), cmb[h * max_splits + j], O);
-    p.attn_out[(size_t)(kvh * R + h) * D + d] = __fmul_rn(O, stat[2 * h]);
+    float pv[kMkMaxSplits];
+#pragma unroll
+    for (uint32_t j = 0; j < kMkMaxSplits; j++)
+      pv[j] = (j < nsplit && idx < R * D) ? __ldcg(&base[((size_t)j * R + h) * (D + 2) + d]) : 0.f;
+    if (idx0 == 0) {
+      for (int s = tid; s < R * (int)nsplit; s += MK_THREADS) {
+        const int hh = s / nsplit, j = s % nsplit;
+        const float2 ml = __ldcg(reinterpret_cast<const float2 *>(&base[((size_t)j * R + hh) * (D + 2) + D]));
+        sm.cmb[hh * max_splits + j] = ml.x;
+        sm.cml[hh * max_splits + j] = ml.y;
+      }
+      __syncthreads();
+      if (tid < R) {
+        float M = -INFINITY, Lsum = 0.f;
+        for (uint32_t j = 0; j < nsplit; j++) M = fmaxf(M, sm.cmb[tid * max_splits + j]);
+        for (uint32_t j = 0; j < nsplit; j++) {
+          const float f = expf(__fsub_rn(sm.cmb[tid * max_splits + j], M));
+          Lsum = __fmaf_rn(sm.cml[tid * max_splits + j], f, Lsum);
+          sm.cmb[tid * max_splits + j] = f;
+        }
+        sm.stat[2 * tid] = __fdiv_rn(1.0f, __fadd_rn(Lsum, 1e-9f));
+      }
+      __syncthreads();
+    }
+    if (idx < R * D) {
+      float O = 0.f;
+#pragma unroll
+      for (uint32_t j = 0; j < kMkMaxSplits; j++)
+        if (j < nsplit) O = __fmaf_rn(pv[j], sm.cmb[h * max_splits + j], O);
+      p.attn_out[(size_t)(kvh * R + h) * D + d] = __fmul_rn(O, sm.stat[2 * h]);
+    }
   }
   if (tid == 0) a.attn_counters[kvh] = 0u;
 }
 
 // ---------------------------------------------------------------------------
 // TOPK phase: each CTA selects the top 64 of its vocab slice, last CTA merges
-CH_DEV void topk_phase(const Phase &p, const MegaArgs &a, uint8_t *u) {
+struct TopkSmem {
+  uint32_t *hist, *sh, *cnt;
+  uint64_t *buf, *sorted;
+  float *lg;    // staged logits [lo4, hi4) of this CTA's slice (4-aligned)
+  float *part;  // [grid][2][16] straddle partials of the LM head
+  __device__ TopkSmem(uint8_t *u) {
+    hist = reinterpret_cast<uint32_t *>(u);
+    sh = hist + 256;
+    cnt = sh + 4;
+    buf = reinterpret_cast<uint64_t *>(cnt + 4);
+    sorted = buf + 64;
+    lg = reinterpret_cast<float *>(sorted + 64);
+    part = lg + 4096 + 8;
+  }
+};
+CH_DEV void topk_slice(const Phase &p, uint32_t &lo, uint32_t &hi) {
+  const uint32_t G = gridDim.x, V = p.vocab;
+  lo = (uint32_t)(((uint64_t)V * blockIdx.x) / G);
+  hi = (uint32_t)(((uint64_t)V * (blockIdx.x + 1)) / G);
+}
+CH_DEV void topk_post_copies(const Phase &p, const SmemLayout &L) {
+  TopkSmem sm(L.u);
+  uint32_t lo, hi;
+  topk_slice(p, lo, hi);
+  const uint32_t lo4 = lo & ~3u, hi4 = (hi + 3u) & ~3u;
+  if (hi4 > lo4) stage_copy(L, sm.lg, p.r_in.direct + lo4, (hi4 - lo4) * 4);
+  stage_copy(L, sm.part, p.r_in.partial, gridDim.x * 32 * 4);
+}
+CH_DEV void topk_phase(const Phase &p, const MegaArgs &a, const SmemLayout &L) {
   constexpr int E1 = 8, E2 = 20;  // per-thread keys: slice <= 4096, candidates <= 10240
-  uint32_t *hist = reinterpret_cast<uint32_t *>(u);
-  uint32_t *sh = hist + 256;
-  uint32_t *cnt = sh + 4;
-  uint64_t *buf = reinterpret_cast<uint64_t *>(cnt + 4);
-  uint64_t *sorted = buf + 64;
-  float *lg = reinterpret_cast<float *>(sorted + 64);  // this CTA's slice of the logits
+  TopkSmem sm(L.u);
   __shared__ uint32_t last_flag;
   const int tid = threadIdx.x;
-  const uint32_t G = gridDim.x, V = p.vocab;
-  const uint32_t lo = (uint32_t)(((uint64_t)V * blockIdx.x) / G), hi = (uint32_t)(((uint64_t)V * (blockIdx.x + 1)) / G);
-  gather_rows(p.r_in, lo, hi, lg);
+  const uint32_t G = gridDim.x;
+  uint32_t lo, hi;
+  topk_slice(p, lo, hi);
+  const uint32_t lo4 = lo & ~3u;
+  patch_staged(p.r_in, L.slist, sm.part, lo4, (hi + 3u) & ~3u, sm.lg);
+  __syncthreads();
   {
     uint64_t k[E1];
 #pragma unroll
     for (int e = 0; e < E1; e++) {
       const uint32_t idx = lo + e * MK_THREADS + tid;
       if (idx < hi) {
-        const float v = softcap(lg[idx - lo]);
+        const float v = softcap(sm.lg[idx - lo4]);
         k[e] = ((uint64_t)sortable(v) << 32) | (uint64_t)(0xFFFFFFFFu - idx);
       } else {
         k[e] = 0;
       }
     }
-    const uint64_t thr = block_kth_largest<E1>(k, 64, hist, sh);
-    collect_sorted64<E1>(k, thr, buf, cnt, sorted);
-    if (tid < 64) a.topk_cand[(size_t)blockIdx.x * 64 + tid] = sorted[tid];
+    const uint64_t thr = block_kth_largest<E1>(k, 64, sm.hist, sm.sh);
+    collect_sorted64<E1>(k, thr, sm.buf, sm.cnt, sm.sorted);
+    if (tid < 64) a.topk_cand[(size_t)blockIdx.x * 64 + tid] = sm.sorted[tid];
   }
   __threadfence();
   __syncthreads();
@@ -587,10 +894,10 @@ CH_DEV void topk_phase(const Phase &p, const MegaArgs &a, uint8_t *u) {
     const uint32_t i = e * MK_THREADS + tid;
     k[e] = i < ncand ? __ldcg(&a.topk_cand[i]) : 0ull;
   }
-  const uint64_t thr = block_kth_largest<E2>(k, 64, hist, sh);
-  collect_sorted64<E2>(k, thr, buf, cnt, sorted);
+  const uint64_t thr = block_kth_largest<E2>(k, 64, sm.hist, sm.sh);
+  collect_sorted64<E2>(k, thr, sm.buf, sm.cnt, sm.sorted);
   if (tid < 64) {
-    const uint64_t key = sorted[tid];
+    const uint64_t key = sm.sorted[tid];
     uint32_t id = 0;
     float val = -1e30f;
     if (key != 0) {
@@ -612,80 +919,161 @@ CH_DEV void topk_phase(const Phase &p, const MegaArgs &a, uint8_t *u) {
 }
 
 // ---------------------------------------------------------------------------
+// Before the grid barrier: everything the next phase can do without the previous
+// phase's result -- its input's straddle list and the bulk copies of inputs that
+// already exist -- then this thread-0 arrival on vbar (the first of two).
+template <int R>
+CH_DEV void pre_phase(const Phase &p, const MegaArgs &a, const StepParams &sp, const SmemLayout &L) {
+  cp_async_wait_all();  // this phase's struct (copied two phases ago)
+  fence_proxy_async();  // this thread's generic shared-memory writes before the bulk copies that reuse it
+  __syncthreads();
+  if (p.kind == PH_GEMV) {
+    if (p.pm == PM_ADD_NORM || p.pm == PM_GELU) build_slist(p.r_in, L.slist);
+    if ((p.pm == PM_NORM || p.pm == PM_ADD_NORM) && threadIdx.x == 0) {
+      GemvStage S(L.u, p.K, p.pm);
+      stage_copy(L, S.s1, p.x_in, p.K * 4);  // residual: written at least one barrier ago
+      stage_copy(L, S.s3, p.norm_w, p.K * 4);
+      if (p.post_w) stage_copy(L, S.s2, p.post_w, p.K * 4);
+    }
+  } else if (p.kind == PH_ATTN) {
+    build_slist(p.r_in, L.slist);
+    attn_pre<R>(p, a, sp, L);
+  } else {
+    build_slist(p.r_in, L.slist);
+  }
+  __syncthreads();  // every expect_tx of this phase precedes the arrival
+  if (threadIdx.x == 0) mbar_arrive(L.vbar);
+}
+// Right after the grid barrier (thread 0): bulk copies of the previous phase's
+// output (and its straddle partials), then the second arrival on vbar.
+template <int R>
+CH_DEV void post_copies(const Phase &p, const MegaArgs &a, const StepParams &sp, const SmemLayout &L) {
+  if (threadIdx.x != 0) return;
+  fence_proxy_async_global();  // the other CTAs' generic writes, acquired by the barrier, before bulk reads
+  if (p.kind == PH_GEMV) {
+    GemvStage S(L.u, p.K, p.pm);
+    if (p.pm == PM_DIRECT) stage_copy(L, S.s0, p.x_in, p.K * 4);
+    if (p.pm == PM_ADD_NORM || p.pm == PM_GELU) {
+      stage_copy(L, S.s0, p.r_in.direct, p.K * 4);  // act mode: K act values
+      stage_copy(L, S.part, p.r_in.partial, gridDim.x * 32 * 4);
+    }
+  } else if (p.kind == PH_ATTN) {
+    attn_post_copies<R>(p, a, sp, L);
+  } else {
+    topk_post_copies(p, L);
+  }
+  mbar_arrive(L.vbar);
+}
+
+// R = q heads per kv head
+template <int R>
 __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(const MegaArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
   SmemLayout L;
   L.stages = smem;
   L.bars = reinterpret_cast<uint64_t *>(smem + MK_NW * MK_SPW * MK_STAGE);
-  L.xzero = reinterpret_cast<uint4 *>(smem + MK_NW * MK_SPW * MK_STAGE + MK_NW * MK_SPW * 8);
+  L.vbar = L.bars + MK_NW * MK_SPW;
+  L.xzero = reinterpret_cast<uint4 *>(L.vbar + 2);
   L.wpart = reinterpret_cast<float *>(L.xzero + 1);
-  L.u = reinterpret_cast<uint8_t *>(L.wpart + MK_NW * 2 * 16);
+  L.slist = reinterpret_cast<uint32_t *>(L.wpart + MK_NW * 2 * 16);
+  L.wphys = L.slist + kMaxGrid + 1;
+  L.u = reinterpret_cast<uint8_t *>(L.wphys + 2 * kWinSlots);
   __shared__ float red[32];
+  __shared__ Phase ph_s[3];  // phases pi, pi+1 and pi+2 (copied ahead with cp.async)
+  __shared__ StepParams sp_s;
 
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const uint32_t gw = blockIdx.x * MK_NW + warp;
   uint8_t *my_stages = L.stages + (size_t)warp * MK_SPW * MK_STAGE;
   uint64_t *my_bars = L.bars + warp * MK_SPW;
-  Stream st{0, 0};
+  const uint64_t pol = l2_evict_first_policy();
+  Stream st;
   if (lane == 0) {
     for (int s = 0; s < MK_SPW; s++) mbar_init(&my_bars[s], 1);
+    if (warp == 0) mbar_init(L.vbar, 2);
     fence_mbar_init();
+    stream_init(a, gw, st);
     for (int s = 0; s < MK_SPW; s++)
-      if (stream_next(a, gw, st)) stream_issue(a, gw, st, my_stages + (size_t)s * MK_STAGE, &my_bars[s]);
+      if (stream_next(a, gw, st)) stream_issue(st, my_stages + (size_t)s * MK_STAGE, &my_bars[s], pol);
   }
-  if (threadIdx.x == 0) *L.xzero = make_uint4(0u, 0u, 0u, 0u);
-  // every lane keeps the stream cursor (lane 0's copy drives the issues)
-  st.ph = __shfl_sync(0xffffffffu, st.ph, 0);
-  st.ck = __shfl_sync(0xffffffffu, st.ck, 0);
+  if (threadIdx.x == 0) {
+    *L.xzero = make_uint4(0u, 0u, 0u, 0u);
+    sp_s = *a.sp;
+  }
+  for (uint32_t i = 0; i < 2 && i < a.nphases; i++) copy_phase(a.phases + i, &ph_s[i]);
+  cp_async_wait_all();
   __syncthreads();
+  attn_lists_init(a, sp_s, L.wphys);
+  pre_phase<R>(ph_s[0], a, sp_s, L);
 
   const unsigned long long epoch = *a.epoch;
   const unsigned long long base = epoch * (unsigned long long)(a.nphases - 1) * gridDim.x;
-  uint32_t cidx = 0;
+  uint32_t cidx = 0, vpar = 0;
   bool ok = true;
   for (uint32_t pi = 0; pi < a.nphases; pi++) {
-    const Phase &p = a.phases[pi];
+    const Phase &p = ph_s[pi % 3];
+    PHASE_MARK(pi, 0);
+    if (pi + 2 < a.nphases) copy_phase(a.phases + pi + 2, &ph_s[(pi + 2) % 3]);
+    post_copies<R>(p, a, sp_s, L);
+    if (!mbar_wait_bounded(L.vbar, vpar, a.err)) ok = false;
+    vpar ^= 1u;
     if (p.kind == PH_GEMV) {
-      uint4 *xf = reinterpret_cast<uint4 *>(L.u);
-      float *vec = reinterpret_cast<float *>(xf + (p.K / 32) * 8);
-      gemv_prologue(p, a, xf, vec, red);
+      gemv_prologue(p, a, L, red);
       __syncthreads();
+      PHASE_MARK(pi, 1);
+      const uint4 *xf = reinterpret_cast<const uint4 *>(L.u);
       if (p.fmt == FMT_Q4)
-        gemv_tiles<FMT_Q4>(p, a, gw, L, xf, cidx, st, ok);
+        gemv_tiles<FMT_Q4>(p, a, gw, L, xf, cidx, st, ok, pol);
       else
-        gemv_tiles<FMT_Q8>(p, a, gw, L, xf, cidx, st, ok);
+        gemv_tiles<FMT_Q8>(p, a, gw, L, xf, cidx, st, ok, pol);
       __syncthreads();
+      PHASE_MARK(pi, 2);
       cta_combine(p, L.wpart);
     } else if (p.kind == PH_ATTN) {
-      switch (a.nq / a.nkv) {
-        case 1: attn_phase<1>(p, a, L.u, red); break;
-        case 2: attn_phase<2>(p, a, L.u, red); break;
-        default: attn_phase<4>(p, a, L.u, red); break;
-      }
+      attn_phase<R>(p, a, sp_s, L);
     } else {
-      topk_phase(p, a, L.u);
+      topk_phase(p, a, L);
     }
-    if (pi + 1 < a.nphases) grid_barrier(a.arrive, base + (unsigned long long)(pi + 1) * gridDim.x, a.err);
+#ifdef CH_PHASE_TRACE
+    __syncthreads();
+#endif
+    PHASE_MARK(pi, 3);
+    if (pi + 1 < a.nphases) {
+      pre_phase<R>(ph_s[(pi + 1) % 3], a, sp_s, L);
+      PHASE_MARK(pi, 4);
+      grid_barrier(a.arrive, base + (unsigned long long)(pi + 1) * gridDim.x, a.err);
+      PHASE_MARK(pi, 5);
+    }
+  }
+  if (!ok && lane == 0) {
+    // a copy wait gave up: the last MK_SPW chunks' waits were skipped, so wait
+    // (bounded) for those copies before the CTA exits
+    for (uint32_t j = cidx >= MK_SPW ? cidx - MK_SPW : 0; j < cidx; j++)
+      mbar_wait_bounded(&my_bars[j % MK_SPW], (j / MK_SPW) & 1, nullptr, 100000000ull);
   }
   if (blockIdx.x == 0 && threadIdx.x == 0) *a.epoch = (uint32_t)(epoch + 1);
 }
 
-size_t mk_smem_bytes(uint32_t max_k, uint32_t hidden, uint32_t ratio, uint32_t max_splits, uint32_t cache_slots) {
-  const size_t fixed = (size_t)MK_NW * MK_SPW * MK_STAGE + MK_NW * MK_SPW * 8 + 16 + MK_NW * 2 * 16 * 4;
-  // xf (K*4 bytes) + vec (kVecRows floats; the norm prologues need hidden <= kVecRows)
-  const size_t gemv = (size_t)max_k * 4 + (size_t)std::max(hidden, kVecRows) * 4;
-  const uint32_t pvw = ratio <= 2 ? MK_NW : MK_NW * 2 / ratio;
+size_t mk_smem_bytes(uint32_t max_k, uint32_t hidden, uint32_t ratio, uint32_t max_splits, uint32_t cache_slots,
+                     uint32_t grid) {
+  const size_t fixed = (size_t)MK_NW * MK_SPW * MK_STAGE + (MK_NW * MK_SPW + 2) * 8 + 16 + MK_NW * 2 * 16 * 4 +
+                      (kMaxGrid + 1) * 4 + 2 * kWinSlots * 4;
+  const size_t part = (size_t)grid * 32 * 4;  // straddle partials of the previous GEMV
+  // GEMV staging: 4 vectors of `hidden` for the norm prologues, one of max_k otherwise
+  const size_t gemv = std::max((size_t)4 * hidden * 4, (size_t)max_k * 4) + part;
   const uint32_t chunk_cap = std::max(kMinChunk, (cache_slots + max_splits - 1) / max_splits);
-  const size_t attn = 4 * ((size_t)(ratio + 2) * 256 + (size_t)pvw * ratio * 256 + (size_t)ratio * chunk_cap +
-                           (size_t)ratio * max_splits + 2 * ratio);
-  const size_t topk = 256 * 4 + 32 + 128 * 8 + 4096 * 4;
+  const size_t kv = (size_t)2 * kWinSlots * kHeadDim * 2, os = (size_t)MK_NW * ratio * kHeadDim * 4;
+  const size_t attn = 4 * ((size_t)(ratio + 2) * kHeadDim + 2 * kHeadDim + kHeadDim) + std::max(kv, os) +
+                      4 * ((size_t)ratio * chunk_cap + 2 * (size_t)ratio * max_splits + 2 * ratio) + 16 + part;
+  const size_t topk = 256 * 4 + 32 + 128 * 8 + (4096 + 8) * 4 + part;
   return fixed + std::max({gemv, attn, topk});
 }
 
-cudaError_t launch_decode_step(const MegaArgs &a, size_t smem, cudaStream_t s) {
+template <int R>
+static cudaError_t launch_decode_step_t(const MegaArgs &a, size_t smem, cudaStream_t s) {
   static size_t attr = 0;
   if (smem > attr) {
-    cudaError_t e = cudaFuncSetAttribute(decode_step_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaError_t e = cudaFuncSetAttribute(decode_step_kernel<R>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
     attr = smem;
   }
@@ -699,7 +1087,25 @@ cudaError_t launch_decode_step(const MegaArgs &a, size_t smem, cudaStream_t s) {
   attr_c[0].val.cooperative = 1;
   cfg.attrs = attr_c;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, decode_step_kernel, a);
+  return cudaLaunchKernelEx(&cfg, decode_step_kernel<R>, a);
+}
+
+cudaError_t launch_decode_step(const MegaArgs &a, size_t smem, cudaStream_t s) {
+  if (a.grid > kMaxGrid) return cudaErrorInvalidValue;
+  switch (a.nq / a.nkv) {
+    case 1: return launch_decode_step_t<1>(a, smem, s);
+    case 2: return launch_decode_step_t<2>(a, smem, s);
+    case 4: return launch_decode_step_t<4>(a, smem, s);
+    default: return cudaErrorInvalidValue;
+  }
 }
 
 }  // namespace ch
+
+#ifdef CH_PHASE_TRACE
+// copies the timeline [cta][phase][mark] (u64 ns) of the last traced launch to host memory
+extern "C" int ch_phase_trace_copy(unsigned long long *host, size_t count) {
+  if (count > sizeof(ch::g_phase_trace) / 8) count = sizeof(ch::g_phase_trace) / 8;
+  return cudaMemcpyFromSymbol(host, ch::g_phase_trace, count * 8) == cudaSuccess ? 0 : -3;
+}
+#endif

@@ -15,18 +15,19 @@ enum PrologueMode : uint32_t {
   PM_GELU = 3,      // gelu_tanh(gate) * up from an interleaved gate|up GEMV output
 };
 
-// finished rows of a GEMV phase.  Row tiles whose k tiles straddle CTAs are
-// finished by the last straddling CTA to arrive (per-row-tile counter).
+// Output of a GEMV phase.  A row tile whose k tiles all fall in one CTA's share
+// is finished by that CTA in `direct`; a row tile that straddles CTAs is left as
+// one partial sum per CTA (slot 0: the CTA's first row tile, slot 1: its last)
+// and the consumer phase adds them up while it loads its input.
 struct GemvOut {
   float *direct;       // [rows]; act mode: [rows/2] = gelu(gate) * up
   float *partial;      // [grid][2][16] CTA partial sums of straddling row tiles
-  uint32_t *counters;  // [row tiles], zero between phases
   uint32_t KT;         // k tiles of the producing GEMV
   uint32_t q, rem;     // balanced partition of its rows/16*KT tiles over grid*warps
   uint32_t act;        // 1: interleaved gate|up GEMV; direct holds gelu(gate)*up
 };
 
-struct Phase {
+struct alignas(16) Phase {
   uint32_t kind, fmt, pm, is_sliding;
   // GEMV
   const uint8_t *tiles;
@@ -45,8 +46,16 @@ struct Phase {
   float *attn_out;
 };
 
+// the weight stream of one GEMV phase (phases in order, GEMV phases only)
+struct alignas(16) StreamDesc {
+  const uint8_t *tiles;
+  uint32_t q, rem;  // balanced partition of the phase's tiles over grid * warps
+};
+
 struct MegaArgs {
   const Phase *phases;
+  const StreamDesc *streams;
+  uint32_t nstreams;
   uint32_t nphases, grid;
   unsigned long long *arrive;  // grid-barrier arrivals (monotonic across launches)
   uint32_t *epoch;    // completed launches
@@ -66,7 +75,9 @@ struct MegaArgs {
 };
 
 int mk_warps();
-size_t mk_smem_bytes(uint32_t max_k, uint32_t hidden, uint32_t ratio, uint32_t max_splits, uint32_t cache_slots);
+constexpr uint32_t kMkMaxSplits = 24;  // attention splits per kv head held in registers by the combine
+size_t mk_smem_bytes(uint32_t max_k, uint32_t hidden, uint32_t ratio, uint32_t max_splits, uint32_t cache_slots,
+                     uint32_t grid);
 cudaError_t launch_decode_step(const MegaArgs &a, size_t smem, cudaStream_t s);
 
 }  // namespace ch

@@ -191,11 +191,12 @@ struct ch_model {
   // persistent decode-step kernel: phase tables, per-GEMV outputs, barrier counters
   Phase *d_phases = nullptr, *d_phases_nl = nullptr;
   uint32_t n_phases = 0, n_phases_nl = 0;
+  StreamDesc *d_streams = nullptr, *d_streams_nl = nullptr;  // weight streams of the GEMV phases
+  uint32_t n_streams = 0, n_streams_nl = 0;
   float *gdir[5] = {nullptr, nullptr, nullptr, nullptr, nullptr};
   float *gpart[5] = {nullptr, nullptr, nullptr, nullptr, nullptr};
   unsigned long long *mk_arrive = nullptr;
   uint32_t *mk_epoch = nullptr;
-  uint32_t *gcnt[5] = {nullptr, nullptr, nullptr, nullptr, nullptr};
   size_t mk_smem = 0;
   int mk_grid = 0;
   bool use_ops = false;  // kernel-per-op decode (CH_DECODE_OPS=1), kept for A/B measurement
@@ -235,9 +236,10 @@ static void free_model(ch_model *m) {
   }
   cudaFree(m->d_phases);
   cudaFree(m->d_phases_nl);
+  cudaFree(m->d_streams);
+  cudaFree(m->d_streams_nl);
   cudaFree(m->mk_arrive);
   cudaFree(m->mk_epoch);
-  for (int k = 0; k < 5; k++) cudaFree(m->gcnt[k]);
   void *host[] = {m->h_x, m->h_sp, m->h_lists, m->h_ids, m->h_vals, m->h_run, m->h_rope};
   for (void *p : host) cudaFreeHost(p);
   if (m->g_host_logits) cudaGraphExecDestroy(m->g_host_logits);
@@ -365,15 +367,15 @@ static int alloc_model_buffers(ch_model *m) {
 // phase table of the persistent decode-step kernel (decode_step.cu)
 enum GemvKind { GK_QKV = 0, GK_O = 1, GK_GU = 2, GK_DOWN = 3, GK_LM = 4 };
 
-static int build_phases(ch_model *m, bool with_logits, Phase **d_out, uint32_t *n_out) {
+static int build_phases(ch_model *m, bool with_logits, Phase **d_out, uint32_t *n_out, StreamDesc **d_str,
+                        uint32_t *n_str) {
   const uint32_t GW = (uint32_t)m->mk_grid * mk_warps();
   const uint32_t rows[5] = {m->qd + 2 * m->kvd, m->H, 2 * m->I, m->H, m->V};
   const uint32_t KT[5] = {m->H / 64, m->qd / 64, m->H / 64, m->I / 64, m->H / 32};
   GemvOut outs[5];
   for (int k = 0; k < 5; k++) {
     const uint64_t T = (uint64_t)(rows[k] / 16) * KT[k];
-    outs[k] = GemvOut{m->gdir[k], m->gpart[k], m->gcnt[k], KT[k], (uint32_t)(T / GW), (uint32_t)(T % GW),
-                      k == GK_GU ? 1u : 0u};
+    outs[k] = GemvOut{m->gdir[k], m->gpart[k], KT[k], (uint32_t)(T / GW), (uint32_t)(T % GW), k == GK_GU ? 1u : 0u};
   }
   auto gemv = [&](int kind, const uint8_t *tiles, int fmt, uint32_t K) {
     Phase p{};
@@ -464,36 +466,49 @@ static int build_phases(ch_model *m, bool with_logits, Phase **d_out, uint32_t *
   CH_TRY(dmalloc(d_out, ph.size()));
   CH_CUDA(cudaMemcpy(*d_out, ph.data(), ph.size() * sizeof(Phase), cudaMemcpyHostToDevice));
   *n_out = (uint32_t)ph.size();
+  std::vector<StreamDesc> st;
+  for (const Phase &p : ph)
+    if (p.kind == PH_GEMV) st.push_back(StreamDesc{p.tiles, p.q, p.rem});
+  CH_TRY(dmalloc(d_str, st.size()));
+  CH_CUDA(cudaMemcpy(*d_str, st.data(), st.size() * sizeof(StreamDesc), cudaMemcpyHostToDevice));
+  *n_str = (uint32_t)st.size();
   return CH_OK;
 }
 
+// attention splits per kv head in the decode-step kernel: at most one CTA per
+// (kv head, split) and no more than its combine keeps in registers
+static uint32_t mk_attn_splits(const ch_model *m) {
+  return (uint32_t)std::min({m->mk_grid / (int)m->nkv, m->attn_splits, (int)kMkMaxSplits});
+}
+
+// The decode step runs as one persistent kernel (decode_step.cu) when the shape
+// fits it; otherwise -- or with CH_DECODE_OPS=1, for A/B measurement -- as the
+// captured graph of per-op kernels.  Both are GPU paths with the same results.
 static int init_decode_step(ch_model *m) {
-  m->mk_grid = num_sms();
-  if (m->H > 4096) return fail(CH_EINVAL, "decode-step kernel stages at most 4096 hidden rows");
-  if ((m->V + m->mk_grid - 1) / m->mk_grid > 4096) return fail(CH_EINVAL, "vocab slice per SM exceeds 4096");
+  m->mk_grid = std::min(num_sms(), 255);  // straddle lists hold CTA ids in 8 bits
+  const char *env = getenv("CH_DECODE_OPS");
+  m->use_ops = env && env[0] == '1';
+  const uint32_t ratio = m->nq / m->nkv;
+  const uint32_t max_k = std::max({m->H, m->qd, m->I});
+  m->mk_smem = mk_smem_bytes(max_k, m->H, ratio, mk_attn_splits(m), kSlots, (uint32_t)m->mk_grid);
+  int co = 0;
+  CH_CUDA(cudaDeviceGetAttribute(&co, cudaDevAttrCooperativeLaunch, m->ctx->device));
+  const bool fits = co && m->H <= 4096 && m->D == 256 && (ratio == 1 || ratio == 2 || ratio == 4) &&
+                    (m->V + m->mk_grid - 1) / m->mk_grid <= 4096 && m->mk_smem <= 226 * 1024;
+  if (!fits) m->use_ops = true;
+  if (m->use_ops) return CH_OK;
   const size_t part = (size_t)m->mk_grid * mk_warps() * 2 * 16;
   const uint32_t rows[5] = {m->qd + 2 * m->kvd, m->H, 2 * m->I, m->H, m->V};
   for (int k = 0; k < 5; k++) {
     CH_TRY(dmalloc(&m->gdir[k], rows[k]));
     CH_TRY(dmalloc(&m->gpart[k], part));
-    CH_TRY(dmalloc(&m->gcnt[k], rows[k] / 16));
-    CH_CUDA(cudaMemset(m->gcnt[k], 0, rows[k] / 16 * 4));
   }
   CH_TRY(dmalloc(&m->mk_arrive, 1));
   CH_TRY(dmalloc(&m->mk_epoch, 1));
   CH_CUDA(cudaMemset(m->mk_arrive, 0, 8));
   CH_CUDA(cudaMemset(m->mk_epoch, 0, 4));
-  CH_TRY(build_phases(m, true, &m->d_phases, &m->n_phases));
-  CH_TRY(build_phases(m, false, &m->d_phases_nl, &m->n_phases_nl));
-  const uint32_t max_k = std::max({m->H, m->qd, m->I});
-  m->mk_smem = mk_smem_bytes(max_k, m->H, m->nq / m->nkv,
-                             (uint32_t)std::min(m->mk_grid / (int)m->nkv, m->attn_splits), kSlots);
-  if (m->mk_smem > 227 * 1024) return fail(CH_EINVAL, "decode-step kernel needs more than 227 KB of shared memory");
-  int co = 0;
-  CH_CUDA(cudaDeviceGetAttribute(&co, cudaDevAttrCooperativeLaunch, m->ctx->device));
-  if (!co) return fail(CH_ECUDA, "device lacks cooperative launch");
-  const char *env = getenv("CH_DECODE_OPS");
-  m->use_ops = env && env[0] == '1';
+  CH_TRY(build_phases(m, true, &m->d_phases, &m->n_phases, &m->d_streams, &m->n_streams));
+  CH_TRY(build_phases(m, false, &m->d_phases_nl, &m->n_phases_nl, &m->d_streams_nl, &m->n_streams_nl));
   return CH_OK;
 }
 
@@ -501,6 +516,8 @@ static MegaArgs mega_args(ch_model *m, bool logits, bool device_loop) {
   MegaArgs a{};
   a.phases = logits ? m->d_phases : m->d_phases_nl;
   a.nphases = logits ? m->n_phases : m->n_phases_nl;
+  a.streams = logits ? m->d_streams : m->d_streams_nl;
+  a.nstreams = logits ? m->n_streams : m->n_streams_nl;
   a.grid = (uint32_t)m->mk_grid;
   a.arrive = m->mk_arrive;
   a.epoch = m->mk_epoch;
@@ -510,7 +527,7 @@ static MegaArgs mega_args(ch_model *m, bool logits, bool device_loop) {
   a.nq = m->nq;
   a.nkv = m->nkv;
   a.rot = m->cfg.rotary_dim;
-  a.attn_max_splits = (uint32_t)std::min(m->mk_grid / (int)m->nkv, m->attn_splits);
+  a.attn_max_splits = mk_attn_splits(m);
   a.cache_slots = kSlots;
   a.eps = m->cfg.rms_norm_eps;
   a.attn_partial = m->attn_partial;
@@ -761,12 +778,8 @@ extern "C" int ch_model_zero_state(ch_model *m) {
   CH_CUDA(cudaMemsetAsync(m->X[0], 0, m->H * 4, s));
   CH_CUDA(cudaMemsetAsync(m->X[1], 0, m->H * 4, s));
   CH_CUDA(cudaMemsetAsync(m->normed, 0, m->H * 4, s));
-  CH_CUDA(cudaMemsetAsync(m->mk_arrive, 0, 8, s));
-  for (int k = 0; k < 5; k++) {
-    const uint32_t rows[5] = {m->qd + 2 * m->kvd, m->H, 2 * m->I, m->H, m->V};
-    CH_CUDA(cudaMemsetAsync(m->gcnt[k], 0, rows[k] / 16 * 4, s));
-  }
-  CH_CUDA(cudaMemsetAsync(m->mk_epoch, 0, 4, s));
+  if (m->mk_arrive) CH_CUDA(cudaMemsetAsync(m->mk_arrive, 0, 8, s));
+  if (m->mk_epoch) CH_CUDA(cudaMemsetAsync(m->mk_epoch, 0, 4, s));
   CH_CUDA(cudaStreamSynchronize(s));
   return CH_OK;
 }
