@@ -60,9 +60,9 @@ constexpr uint32_t kMaxGrid = 255;  // straddle-list entries hold CTA ids in 8 b
 int mk_warps() { return MK_NW; }
 
 // Optional per-phase timeline (build with -DCH_PHASE_TRACE, see channel_b200/phase_trace.py):
-// thread 0 of every CTA records %globaltimer at six points of each phase.
+// thread 0 of every CTA records %globaltimer at seven points of each phase.
 #ifdef CH_PHASE_TRACE
-constexpr int kTraceCtas = 256, kTracePhases = 512, kTraceMarks = 6;
+constexpr int kTraceCtas = 256, kTracePhases = 512, kTraceMarks = 8;
 __device__ unsigned long long g_phase_trace[kTraceCtas * kTracePhases * kTraceMarks];
 #define PHASE_MARK(pi, k)                                                                               \
   do {                                                                                                  \
@@ -86,61 +86,69 @@ CH_DEV uint32_t part_warp_of(uint32_t t, uint32_t q, uint32_t rem) {
 CH_DEV uint32_t cta_begin(const GemvOut &o, uint32_t c) { return part_begin(c * MK_NW, o.q, o.rem); }
 
 // ---------------------------------------------------------------------------
-// Straddle list of a GEMV output: entry c-1 describes the CTA boundary in front of
-// CTA c.  When that boundary is the first one inside a row tile rt, the row tile
-// is the sum of the partial slots of CTAs c-1 .. c1 and the entry holds
-// rt | (c-1) << 16 | (c1-c+1) << 24; otherwise kNoStraddle.  One thread per entry.
-CH_DEV void build_slist(const GemvOut &o, uint32_t *slist) {
+// Straddle list of a GEMV output: entry k = c-1 describes the CTA boundary in front
+// of CTA c.  When that boundary is the first one inside a row tile rt, the row
+// tile is the sum of the partial slots of CTAs c-1 .. c1: slist[k] = rt and
+// soff[k] = the two slot offsets (in floats, into the [grid][2][16] partials)
+// when c1 == c (the common case), else kNoStraddle (the general sum walks the
+// CTAs).  slist[k] = kNoStraddle for boundaries between row tiles.  One thread
+// per entry.
+CH_DEV void build_slist(const GemvOut &o, uint32_t *slist, uint32_t *soff) {
   const uint32_t G = gridDim.x, KT = o.KT;
   for (uint32_t c = 1 + threadIdx.x; c < G; c += blockDim.x) {
     const uint32_t B = cta_begin(o, c);  // first tile of CTA c
     const uint32_t rt = B / KT;
-    uint32_t e = kNoStraddle;
-    if (B != rt * KT && cta_begin(o, c - 1) <= rt * KT) {
+    uint32_t e = kNoStraddle, off = kNoStraddle;
+    const uint32_t b0 = cta_begin(o, c - 1);
+    if (B != rt * KT && b0 <= rt * KT) {
       const uint32_t t_hi = rt * KT + KT - 1;
-      uint32_t c1 = c;
-      while (c1 + 1 < G && cta_begin(o, c1 + 1) <= t_hi) c1++;
-      e = rt | ((c - 1) << 16) | ((c1 - (c - 1)) << 24);
+      if (c + 1 >= G || cta_begin(o, c + 1) > t_hi)  // exactly CTAs c-1 and c
+        off = ((c - 1) * 2 + (b0 < rt * KT ? 1u : 0u)) * 16 | ((c * 2) * 16) << 16;
+      e = rt;
     }
     slist[c - 1] = e;
+    soff[c - 1] = off;
   }
 }
-// value of row `row` (0..15) of straddling row tile (rt, c0..c1) from the staged
+// value of row `row` (0..15) of the straddling row tile of entry k from the staged
 // CTA partials P[grid][2][16]: the CTAs' sums in CTA order
-CH_DEV float straddle_value(const GemvOut &o, const float *P, uint32_t e, uint32_t row) {
-  const uint32_t rt = e & 0xFFFFu, c0 = (e >> 16) & 0xFFu, c1 = c0 + (e >> 24);
-  const uint32_t t_lo = rt * o.KT;
+CH_DEV float straddle_value(const GemvOut &o, const uint32_t *slist, const uint32_t *soff, const float *P,
+                            uint32_t k, uint32_t row) {
+  const uint32_t off = soff[k];
+  if (off != kNoStraddle) return __fadd_rn(__fadd_rn(0.f, P[(off & 0xFFFFu) + row]), P[(off >> 16) + row]);
+  const uint32_t t_lo = slist[k] * o.KT, t_hi = t_lo + o.KT - 1;
   float v = 0.f;
-  for (uint32_t cc = c0; cc <= c1; cc++) {
+  for (uint32_t cc = k; cc < gridDim.x && cta_begin(o, cc) <= t_hi; cc++) {
     const uint32_t b = cta_begin(o, cc);
     if (b == cta_begin(o, cc + 1)) continue;  // CTA without tiles
     v = __fadd_rn(v, P[(cc * 2 + (b < t_lo ? 1u : 0u)) * 16 + row]);
   }
   return v;
 }
-// Patch the straddling rows of staged output rows [r0, r1) (dst[i] = row r0 + i);
-// act mode: act values [r0, r1) = gelu(gate) * up of the interleaved row tiles.
-CH_DEV void patch_staged(const GemvOut &o, const uint32_t *slist, const float *P, uint32_t r0, uint32_t r1,
-                         float *dst) {
-  const uint32_t per = o.act ? 8u : 16u, n = (gridDim.x - 1) * per;
+// Patch the straddling rows of staged (non-act) output rows [r0, r1), dst[i] = row r0 + i
+CH_DEV void patch_staged(const GemvOut &o, const uint32_t *slist, const uint32_t *soff, const float *P, uint32_t r0,
+                         uint32_t r1, float *dst) {
+  const uint32_t n = (gridDim.x - 1) * 16;
   for (uint32_t idx = threadIdx.x; idx < n; idx += blockDim.x) {
-    const uint32_t e = slist[idx / per];
-    if (e == kNoStraddle) continue;
-    const uint32_t row = idx % per, r = (e & 0xFFFFu) * per + row;
-    if (r < r0 || r >= r1) continue;
-    if (o.act)
-      dst[r - r0] = __fmul_rn(gelu_tanh(straddle_value(o, P, e, row)), straddle_value(o, P, e, row + 8));
-    else
-      dst[r - r0] = straddle_value(o, P, e, row);
+    const uint32_t k = idx >> 4, rt = slist[k];
+    if (rt == kNoStraddle) continue;
+    const uint32_t row = idx & 15u, r = rt * 16 + row;
+    if (r >= r0 && r < r1) dst[r - r0] = straddle_value(o, slist, soff, P, k, row);
   }
 }
 
-// grid barrier on a monotonically increasing arrival counter (bounded wait)
-CH_DEV void grid_barrier(unsigned long long *arrive, unsigned long long target, uint32_t *err) {
+// Grid barrier on a monotonically increasing arrival counter, in two halves so a
+// CTA can do work that does not depend on the other CTAs between its arrival
+// and its wait.  The wait is bounded.
+CH_DEV void grid_arrive(unsigned long long *arrive) {
   __syncthreads();
   if (threadIdx.x == 0) {
     __threadfence();
     asm volatile("red.relaxed.gpu.global.add.u64 [%0], 1;" ::"l"(arrive) : "memory");
+  }
+}
+CH_DEV void grid_wait(unsigned long long *arrive, unsigned long long target, uint32_t *err) {
+  if (threadIdx.x == 0) {
     unsigned long long v;
     asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(arrive) : "memory");
     if (v < target) {
@@ -186,6 +194,59 @@ CH_DEV void pair_to_fragments(const float (&v)[8], uint4 *xf_pair) {
   }
   xf_pair[0] = make_uint4(pack_half2(h[0], h[1]), pack_half2(h[2], h[3]), pack_half2(h[4], h[5]), pack_half2(h[6], h[7]));
   xf_pair[1] = make_uint4(pack_half2(l[0], l[1]), pack_half2(l[2], l[3]), pack_half2(l[4], l[5]), pack_half2(l[6], l[7]));
+}
+
+// u32 word of a B-fragment array (layout of pair_to_fragments) that holds
+// elements (j, j+1), j even, of the K-vector: hi half (hl = 0) or lo half (hl = 1)
+CH_DEV uint32_t frag_word(uint32_t j, uint32_t hl) {
+  const uint32_t b = j >> 5, k = j & 31u;
+  return ((b * 4 + ((k & 7u) >> 1)) * 2 + hl) * 4 + (k >> 3);
+}
+// f16 hi/lo split of elements (j, j+1) into a B-fragment array (shared or global)
+CH_DEV void store_frag_pair(uint32_t *frag, uint32_t j, float v0, float v1) {
+  const __half h0 = __float2half_rn(v0), h1 = __float2half_rn(v1);
+  const __half l0 = __float2half_rn(__fsub_rn(v0, __half2float(h0)));
+  const __half l1 = __float2half_rn(__fsub_rn(v1, __half2float(h1)));
+  frag[frag_word(j, 0)] = pack_half2(h0, h1);
+  frag[frag_word(j, 1)] = pack_half2(l0, l1);
+}
+// Patch the act values of straddling gate|up row tiles (8 per row tile, act index
+// rt*8 + i = gelu(gate row i) * up row i+8) into a staged B-fragment array
+CH_DEV void patch_act_frag(const GemvOut &o, const uint32_t *slist, const uint32_t *soff, const float *P, uint32_t K,
+                           uint32_t *frag) {
+  const uint32_t n = (gridDim.x - 1) * 4;
+  for (uint32_t idx = threadIdx.x; idx < n; idx += blockDim.x) {
+    const uint32_t k = idx >> 2, rt = slist[k];
+    if (rt == kNoStraddle) continue;
+    const uint32_t i = (idx & 3u) * 2, j = rt * 8 + i;
+    if (j >= K) continue;
+    const float g0 = straddle_value(o, slist, soff, P, k, i), g1 = straddle_value(o, slist, soff, P, k, i + 1);
+    const float u0 = straddle_value(o, slist, soff, P, k, i + 8), u1 = straddle_value(o, slist, soff, P, k, i + 9);
+    store_frag_pair(frag, j, __fmul_rn(gelu_tanh(g0), u0), __fmul_rn(gelu_tanh(g1), u1));
+  }
+}
+// ld_pair without shared-memory bank conflicts: the pairs of one half-warp cover
+// four 32-blocks whose same-offset words share banks, so each thread starts its
+// four float2 loads at a different group (rotation by b % 4) and rotates back.
+CH_DEV void ld_pair_rot(const float *src, uint32_t p, float (&v)[8]) {
+  const float *q = src + (p >> 2) * 32 + (p & 3u) * 2;
+  const uint32_t r = (p >> 2) & 3u;
+  float2 f[4];
+#pragma unroll
+  for (int i = 0; i < 4; i++) f[i] = *reinterpret_cast<const float2 *>(q + 8 * ((i + r) & 3u));
+  // f[i] holds group (i + r) & 3; group g is f[(g - r) & 3]
+  if (r & 1u) {
+    const float2 t = f[3];
+    f[3] = f[2], f[2] = f[1], f[1] = f[0], f[0] = t;
+  }
+  if (r & 2u) {
+    float2 t = f[0];
+    f[0] = f[2], f[2] = t;
+    t = f[1];
+    f[1] = f[3], f[3] = t;
+  }
+#pragma unroll
+  for (int g = 0; g < 4; g++) v[2 * g] = f[g].x, v[2 * g + 1] = f[g].y;
 }
 
 // ---------------------------------------------------------------------------
@@ -247,6 +308,7 @@ struct SmemLayout {
   uint4 *xzero;
   float *wpart;     // [warps][2][16] partial segments of the current GEMV phase
   uint32_t *slist;  // [kMaxGrid] straddle list of the current phase's input
+  uint32_t *soff;   // [kMaxGrid] its partial-slot offsets
   uint32_t *wphys;  // [2][kWinSlots] attention window slot ids (full, sliding lists)
   uint8_t *u;       // union region (GEMV staging / attention / top-k)
 };
@@ -277,26 +339,9 @@ CH_DEV void gemv_prologue(const Phase &p, const MegaArgs &a, const SmemLayout &L
   GemvStage S(L.u, K, p.pm);
   uint4 *xf = reinterpret_cast<uint4 *>(S.s0);
   const bool writer = (blockIdx.x == 0);
-  if (p.pm == PM_DIRECT || p.pm == PM_GELU) {  // S0 holds the input (act already = gelu(gate) * up)
-    if (p.pm == PM_GELU) {
-      patch_staged(p.r_in, L.slist, S.part, 0, K, S.s0);
-      __syncthreads();
-    }
-    constexpr int U = 2;
-    for (uint32_t q0 = 0; q0 < npairs; q0 += U * MK_THREADS) {
-      float v[U][8];
-#pragma unroll
-      for (int u = 0; u < U; u++) {
-        const uint32_t q = q0 + u * MK_THREADS + tid;
-        if (q < npairs) ld_pair(S.s0, q, v[u]);
-      }
-      __syncthreads();  // every pair of these blocks read before the in-place writes
-#pragma unroll
-      for (int u = 0; u < U; u++) {
-        const uint32_t q = q0 + u * MK_THREADS + tid;
-        if (q < npairs) pair_to_fragments(v[u], xf + q * 2);
-      }
-    }
+  if (p.pm == PM_DIRECT) return;  // S0 holds the producer's B fragments
+  if (p.pm == PM_GELU) {           // S0 holds the B fragments of gelu(gate) * up; add the straddling ones
+    patch_act_frag(p.r_in, L.slist, L.soff, S.part, K, reinterpret_cast<uint32_t *>(S.s0));
     return;
   }
   // PM_NORM / PM_ADD_NORM: one pair per thread (K <= 8 * threads)
@@ -305,15 +350,15 @@ CH_DEV void gemv_prologue(const Phase &p, const MegaArgs &a, const SmemLayout &L
 #pragma unroll
   for (int e = 0; e < 8; e++) x[e] = 0.f, w[e] = 0.f;
   if (p.pm == PM_ADD_NORM) {  // x = (x_in + [rmsnorm(r) * post_w]) * scalar     (add_rmsnorm.wgsl:15-51)
-    patch_staged(p.r_in, L.slist, S.part, 0, K, S.s0);
+    patch_staged(p.r_in, L.slist, L.soff, S.part, 0, K, S.s0);
     __syncthreads();
     float r[8];
 #pragma unroll
     for (int e = 0; e < 8; e++) r[e] = 0.f;
     if (on) {
-      ld_pair(S.s0, tid, r);
-      ld_pair(S.s1, tid, x);
-      if (p.post_w) ld_pair(S.s2, tid, w);
+      ld_pair_rot(S.s0, tid, r);
+      ld_pair_rot(S.s1, tid, x);
+      if (p.post_w) ld_pair_rot(S.s2, tid, w);
     }
     float inv_r = 1.0f;
     if (p.post_w) {
@@ -330,7 +375,7 @@ CH_DEV void gemv_prologue(const Phase &p, const MegaArgs &a, const SmemLayout &L
     }
     if (writer && p.x_out && on) st_pair(p.x_out, tid, x);
   } else if (on) {
-    ld_pair(S.s1, tid, x);
+    ld_pair_rot(S.s1, tid, x);
   }
   float ss = 0.f;
 #pragma unroll
@@ -339,7 +384,7 @@ CH_DEV void gemv_prologue(const Phase &p, const MegaArgs &a, const SmemLayout &L
   const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)K), a.eps)));
   if (on) {
     float nw[8], v[8];
-    ld_pair(S.s3, tid, nw);
+    ld_pair_rot(S.s3, tid, nw);
 #pragma unroll
     for (int e = 0; e < 8; e++) v[e] = __fmul_rn(__fmul_rn(x[e], inv), nw[e]);
     if (writer && p.normed_out) st_pair(p.normed_out, tid, v);
@@ -369,8 +414,10 @@ CH_DEV void cta_combine(const Phase &p, const float *wpart) {
       }
     const float up = __shfl_down_sync(0xffffffffu, sum, 8);
     if (inside) {
-      if (p.out.act) {
-        if (lane < 8) p.out.direct[rt * 8 + lane] = __fmul_rn(gelu_tanh(sum), up);
+      if (p.out.act) {  // act values of lanes 0..7 as B fragments, in pairs
+        const float av = __fmul_rn(gelu_tanh(sum), up);
+        const float an = __shfl_down_sync(0xffffffffu, av, 1);
+        if (lane < 8 && !(lane & 1)) store_frag_pair(reinterpret_cast<uint32_t *>(p.out.direct), rt * 8 + lane, av, an);
       } else if (lane < 16) {
         p.out.direct[rt * 16 + lane] = sum;
       }
@@ -397,10 +444,13 @@ CH_DEV void gemv_tiles(const Phase &p, const MegaArgs &a, uint32_t gw, const Sme
   bool first_seg = true;
   auto flush = [&](uint32_t frt, uint32_t kb, uint32_t ke) {
     const float acc0 = __fadd_rn(a0, b0), acc1 = __fadd_rn(a1, b1);
+    // act mode: lanes t == 0 hold act value g of the row tile; pair g, g+1 (lane + 4)
+    const float av = __fmul_rn(gelu_tanh(acc0), acc1);
+    const float an = __shfl_down_sync(0xffffffffu, av, 4);
     if (t == 0) {
       if (kb == 0 && ke == KT) {
         if (p.out.act) {
-          p.out.direct[frt * 8 + g] = __fmul_rn(gelu_tanh(acc0), acc1);
+          if (!(g & 1)) store_frag_pair(reinterpret_cast<uint32_t *>(p.out.direct), frt * 8 + g, av, an);
         } else {
           p.out.direct[frt * 16 + g] = acc0;
           p.out.direct[frt * 16 + g + 8] = acc1;
@@ -544,18 +594,20 @@ CH_DEV void attn_pre(const Phase &p, const MegaArgs &a, const StepParams &sp, co
   const size_t kv_dim = (size_t)a.nkv * D;
   const uint32_t *wp = L.wphys + p.is_sliding * kWinSlots;
   const uint32_t t = threadIdx.x;
-  if (t < 2 * kWinSlots) {  // one 512-byte row per thread: K rows, then V rows
-    const uint32_t i = t % kWinSlots, which = t / kWinSlots;
-    const uint32_t phys = i < it.n ? wp[i] : 0xFFFFFFFFu;
-    if (phys < a.cache_slots && phys != sp.slot) {
-      const __half *src = (which ? p.v_cache : p.k_cache) + (size_t)phys * kv_dim + (size_t)it.kvh * D;
-      stage_copy(L, sm.kv + (size_t)(which * kWinSlots + i) * D, src, D * 2);
-    }
-  } else if (t == 2 * kWinSlots) {
+  // one 512-byte row per thread (K rows, then V rows); thread 0 registers all their bytes at once
+  const uint32_t i = t % kWinSlots, which = t / kWinSlots;
+  const uint32_t phys = (t < 2 * kWinSlots && i < it.n) ? wp[i] : 0xFFFFFFFFu;
+  const bool copy = phys < a.cache_slots && phys != sp.slot;
+  const uint32_t nrows = __syncthreads_count(copy);
+  if (t == 0) {
+    mbar_expect_tx(L.vbar, nrows * D * 2);
     stage_copy(L, sm.qn_w, p.q_norm_w, D * 4);
     stage_copy(L, sm.kn_w, p.k_norm_w, D * 4);
     stage_copy(L, sm.cs, p.rope_cs, a.rot * 4);  // rot/2 (cos, sin) pairs
   }
+  if (copy)
+    bulk_g2s(sm.kv + (size_t)(which * kWinSlots + i) * D,
+             (which ? p.v_cache : p.k_cache) + (size_t)phys * kv_dim + (size_t)it.kvh * D, D * 2, L.vbar);
   for (uint32_t i = kWinSlots + threadIdx.x; i < it.n; i += MK_THREADS) {
     const uint32_t phys = __ldcg(it.list + it.c0 + i);
     if (phys < a.cache_slots) {
@@ -582,7 +634,7 @@ CH_DEV void attn_post_copies(const Phase &p, const MegaArgs &a, const StepParams
 }
 
 template <int R>
-CH_DEV void attn_phase(const Phase &p, const MegaArgs &a, const StepParams &sp, const SmemLayout &L) {
+CH_DEV void attn_phase(const Phase &p, const MegaArgs &a, const StepParams &sp, const SmemLayout &L, uint32_t pi) {
   constexpr int D = kHeadDim, EPL = 8;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const AttnItem it = attn_item(a, sp, p.is_sliding);
@@ -593,11 +645,21 @@ CH_DEV void attn_phase(const Phase &p, const MegaArgs &a, const StepParams &sp, 
   AttnSmem<R> sm(L.u, chunk_cap, max_splits);
   const uint32_t *wp = L.wphys + p.is_sliding * kWinSlots;
 
-  // 0. straddling rows of the staged heads
-  patch_staged(p.r_in, L.slist, sm.part, kvh * R * D, (kvh + 1) * R * D, sm.q_s);
-  patch_staged(p.r_in, L.slist, sm.part, a.nq * D + kvh * D, a.nq * D + (kvh + 1) * D, sm.k_new);
-  patch_staged(p.r_in, L.slist, sm.part, a.nq * D + (uint32_t)kv_dim + kvh * D,
-               a.nq * D + (uint32_t)kv_dim + (kvh + 1) * D, sm.v_new);
+  // 0. straddling rows of the staged heads (q heads, k, v: three row ranges)
+  {
+    const uint32_t n16 = (gridDim.x - 1) * 16;
+    const uint32_t q0 = kvh * R * D, k0 = a.nq * D + kvh * D, v0 = a.nq * D + (uint32_t)kv_dim + kvh * D;
+    for (uint32_t idx = tid; idx < n16; idx += MK_THREADS) {
+      const uint32_t e = L.slist[idx / 16];
+      if (e == kNoStraddle) continue;
+      const uint32_t row = idx % 16, r = (e & 0xFFFFu) * 16 + row;
+      float *dst = nullptr;
+      if (r >= q0 && r < q0 + R * D) dst = sm.q_s + (r - q0);
+      else if (r >= k0 && r < k0 + D) dst = sm.k_new + (r - k0);
+      else if (r >= v0 && r < v0 + D) dst = sm.v_new + (r - v0);
+      if (dst) *dst = straddle_value(p.r_in, L.slist, L.soff, sm.part, idx / 16, row);
+    }
+  }
   __syncthreads();
   // 1. q heads | k | v of this kv head: warp h norms and ropes head h in registers, in place
   if (warp < R + 2) {
@@ -656,6 +718,7 @@ CH_DEV void attn_phase(const Phase &p, const MegaArgs &a, const StepParams &sp, 
   }
   if (it.split == 0 && sp.slot >= a.cache_slots && tid == 0) atomicOr(a.err, DEV_ERR_BAD_SLOT);
   __syncthreads();
+  PHASE_MARK(pi, 2);
 
   // 2. scores: warp w takes slots w, w+16, ...; lane holds d = lane*8 .. +7
   float qr[R][EPL];
@@ -752,15 +815,17 @@ CH_DEV void attn_phase(const Phase &p, const MegaArgs &a, const StepParams &sp, 
     }
   }
   __syncthreads();
+  uint32_t *out_frag = reinterpret_cast<uint32_t *>(p.attn_out);  // B fragments of the o-projection input
   if (it.nsplit == 1) {  // whole list in this CTA: normalize and write (same arithmetic as a 1-split combine)
-    for (int idx = tid; idx < R * D; idx += MK_THREADS) {
+    for (int idx = tid; idx < R * D; idx += MK_THREADS) {  // R*D is a multiple of 32: whole warps
       const int h = idx / D, d = idx % D;
       float s = 0.f;
 #pragma unroll
       for (int w = 0; w < MK_NW; w++) s = __fadd_rn(s, sm.o_s[(w * R + h) * D + d]);
       const float Lsum = __fmaf_rn(sm.stat[2 * h + 1], 1.0f, 0.f);
-      p.attn_out[(size_t)(kvh * R + h) * D + d] =
-          __fmul_rn(__fmaf_rn(s, 1.0f, 0.f), __fdiv_rn(1.0f, __fadd_rn(Lsum, 1e-9f)));
+      const float o = __fmul_rn(__fmaf_rn(s, 1.0f, 0.f), __fdiv_rn(1.0f, __fadd_rn(Lsum, 1e-9f)));
+      const float on = __shfl_down_sync(0xffffffffu, o, 1);
+      if (!(idx & 1)) store_frag_pair(out_frag, (kvh * R + h) * D + d, o, on);
     }
     return;
   }
@@ -776,52 +841,67 @@ CH_DEV void attn_phase(const Phase &p, const MegaArgs &a, const StepParams &sp, 
     part[tid * (D + 2) + D] = sm.stat[2 * tid];
     part[tid * (D + 2) + D + 1] = sm.stat[2 * tid + 1];
   }
+  PHASE_MARK(pi, 3);
+  // 5. publish, wait for every split of this kv head (all CTAs of the cooperative grid
+  //    are resident), then each split combines its own slice of the R*D outputs
   __threadfence();
   __syncthreads();
-  __shared__ uint32_t last_flag;
-  if (tid == 0) last_flag = (atomicAdd(&a.attn_counters[kvh], 1u) == it.nsplit - 1) ? 1u : 0u;
-  __syncthreads();
-  if (!last_flag) return;
-  __threadfence();
-  // 5. last CTA of this kv head: log-sum-exp combine of the splits, all loads in flight at once
-  const float *base = a.attn_partial + ((size_t)kvh * max_splits * R) * (D + 2);
   const uint32_t nsplit = it.nsplit;
-  for (int idx0 = 0; idx0 < R * D; idx0 += MK_THREADS) {
-    const int idx = idx0 + tid;
-    const int h = idx / D, d = idx % D;
-    float pv[kMkMaxSplits];
-#pragma unroll
-    for (uint32_t j = 0; j < kMkMaxSplits; j++)
-      pv[j] = (j < nsplit && idx < R * D) ? __ldcg(&base[((size_t)j * R + h) * (D + 2) + d]) : 0.f;
-    if (idx0 == 0) {
-      for (int s = tid; s < R * (int)nsplit; s += MK_THREADS) {
-        const int hh = s / nsplit, j = s % nsplit;
-        const float2 ml = __ldcg(reinterpret_cast<const float2 *>(&base[((size_t)j * R + hh) * (D + 2) + D]));
-        sm.cmb[hh * max_splits + j] = ml.x;
-        sm.cml[hh * max_splits + j] = ml.y;
-      }
-      __syncthreads();
-      if (tid < R) {
-        float M = -INFINITY, Lsum = 0.f;
-        for (uint32_t j = 0; j < nsplit; j++) M = fmaxf(M, sm.cmb[tid * max_splits + j]);
-        for (uint32_t j = 0; j < nsplit; j++) {
-          const float f = expf(__fsub_rn(sm.cmb[tid * max_splits + j], M));
-          Lsum = __fmaf_rn(sm.cml[tid * max_splits + j], f, Lsum);
-          sm.cmb[tid * max_splits + j] = f;
+  if (tid == 0) {
+    atomicAdd(&a.attn_counters[kvh], 1u);
+    uint32_t v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(&a.attn_counters[kvh]) : "memory");
+    if (v < nsplit) {
+      const uint64_t t0 = globaltimer_ns();
+      for (;;) {
+        asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(&a.attn_counters[kvh]) : "memory");
+        if (v >= nsplit) break;
+        if (globaltimer_ns() - t0 > 2000000000ull) {
+          atomicOr(a.err, DEV_ERR_PEER_TIMEOUT);
+          break;
         }
-        sm.stat[2 * tid] = __fdiv_rn(1.0f, __fadd_rn(Lsum, 1e-9f));
       }
-      __syncthreads();
-    }
-    if (idx < R * D) {
-      float O = 0.f;
-#pragma unroll
-      for (uint32_t j = 0; j < kMkMaxSplits; j++)
-        if (j < nsplit) O = __fmaf_rn(pv[j], sm.cmb[h * max_splits + j], O);
-      p.attn_out[(size_t)(kvh * R + h) * D + d] = __fmul_rn(O, sm.stat[2 * h]);
     }
   }
-  if (tid == 0) a.attn_counters[kvh] = 0u;
+  __syncthreads();
+  const float *base = a.attn_partial + ((size_t)kvh * max_splits * R) * (D + 2);
+  const uint32_t per = (((R * D + nsplit - 1) / nsplit) + 1) & ~1u, i0 = it.split * per;  // even: whole pairs
+  const uint32_t i1 = min(i0 + per, (uint32_t)(R * D));
+  const uint32_t idx = i0 + tid;
+  const bool mine = idx < i1;
+  const int h = (int)(idx / D), d = (int)(idx % D);
+  float pv[kMkMaxSplits];
+#pragma unroll
+  for (uint32_t j = 0; j < kMkMaxSplits; j++)
+    pv[j] = (j < nsplit && mine) ? __ldcg(&base[((size_t)j * R + h) * (D + 2) + d]) : 0.f;
+  for (int s2 = tid; s2 < R * (int)nsplit; s2 += MK_THREADS) {
+    const int hh = s2 / nsplit, j = s2 % nsplit;
+    const float2 ml = __ldcg(reinterpret_cast<const float2 *>(&base[((size_t)j * R + hh) * (D + 2) + D]));
+    sm.cmb[hh * max_splits + j] = ml.x;
+    sm.cml[hh * max_splits + j] = ml.y;
+  }
+  __syncthreads();
+  if (tid < R) {
+    float M = -INFINITY, Lsum = 0.f;
+    for (uint32_t j = 0; j < nsplit; j++) M = fmaxf(M, sm.cmb[tid * max_splits + j]);
+    for (uint32_t j = 0; j < nsplit; j++) {
+      const float f = expf(__fsub_rn(sm.cmb[tid * max_splits + j], M));
+      Lsum = __fmaf_rn(sm.cml[tid * max_splits + j], f, Lsum);
+      sm.cmb[tid * max_splits + j] = f;
+    }
+    sm.stat[2 * tid] = __fdiv_rn(1.0f, __fadd_rn(Lsum, 1e-9f));
+  }
+  __syncthreads();
+  float o = 0.f;
+  if (mine) {
+    float O = 0.f;
+#pragma unroll
+    for (uint32_t j = 0; j < kMkMaxSplits; j++)
+      if (j < nsplit) O = __fmaf_rn(pv[j], sm.cmb[h * max_splits + j], O);
+    o = __fmul_rn(O, sm.stat[2 * h]);
+  }
+  const float on = __shfl_down_sync(0xffffffffu, o, 1);
+  if (mine && !(idx & 1)) store_frag_pair(out_frag, (kvh * R + h) * D + d, o, on);
 }
 
 // ---------------------------------------------------------------------------
@@ -863,7 +943,7 @@ CH_DEV void topk_phase(const Phase &p, const MegaArgs &a, const SmemLayout &L) {
   uint32_t lo, hi;
   topk_slice(p, lo, hi);
   const uint32_t lo4 = lo & ~3u;
-  patch_staged(p.r_in, L.slist, sm.part, lo4, (hi + 3u) & ~3u, sm.lg);
+  patch_staged(p.r_in, L.slist, L.soff, sm.part, lo4, (hi + 3u) & ~3u, sm.lg);
   __syncthreads();
   {
     uint64_t k[E1];
@@ -928,7 +1008,7 @@ CH_DEV void pre_phase(const Phase &p, const MegaArgs &a, const StepParams &sp, c
   fence_proxy_async();  // this thread's generic shared-memory writes before the bulk copies that reuse it
   __syncthreads();
   if (p.kind == PH_GEMV) {
-    if (p.pm == PM_ADD_NORM || p.pm == PM_GELU) build_slist(p.r_in, L.slist);
+    if (p.pm == PM_ADD_NORM || p.pm == PM_GELU) build_slist(p.r_in, L.slist, L.soff);
     if ((p.pm == PM_NORM || p.pm == PM_ADD_NORM) && threadIdx.x == 0) {
       GemvStage S(L.u, p.K, p.pm);
       stage_copy(L, S.s1, p.x_in, p.K * 4);  // residual: written at least one barrier ago
@@ -936,10 +1016,10 @@ CH_DEV void pre_phase(const Phase &p, const MegaArgs &a, const StepParams &sp, c
       if (p.post_w) stage_copy(L, S.s2, p.post_w, p.K * 4);
     }
   } else if (p.kind == PH_ATTN) {
-    build_slist(p.r_in, L.slist);
+    build_slist(p.r_in, L.slist, L.soff);
     attn_pre<R>(p, a, sp, L);
   } else {
-    build_slist(p.r_in, L.slist);
+    build_slist(p.r_in, L.slist, L.soff);
   }
   __syncthreads();  // every expect_tx of this phase precedes the arrival
   if (threadIdx.x == 0) mbar_arrive(L.vbar);
@@ -949,6 +1029,8 @@ CH_DEV void pre_phase(const Phase &p, const MegaArgs &a, const StepParams &sp, c
 template <int R>
 CH_DEV void post_copies(const Phase &p, const MegaArgs &a, const StepParams &sp, const SmemLayout &L) {
   if (threadIdx.x != 0) return;
+  if (p.kind == PH_GEMV && p.pm == PM_DIRECT && blockIdx.x == 0)  // the phase after ATTN: reset its counters
+    for (uint32_t k = 0; k < a.nkv; k++) a.attn_counters[k] = 0u;
   fence_proxy_async_global();  // the other CTAs' generic writes, acquired by the barrier, before bulk reads
   if (p.kind == PH_GEMV) {
     GemvStage S(L.u, p.K, p.pm);
@@ -976,7 +1058,8 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(const MegaAr
   L.xzero = reinterpret_cast<uint4 *>(L.vbar + 2);
   L.wpart = reinterpret_cast<float *>(L.xzero + 1);
   L.slist = reinterpret_cast<uint32_t *>(L.wpart + MK_NW * 2 * 16);
-  L.wphys = L.slist + kMaxGrid + 1;
+  L.soff = L.slist + kMaxGrid + 1;
+  L.wphys = L.soff + kMaxGrid + 1;
   L.u = reinterpret_cast<uint8_t *>(L.wphys + 2 * kWinSlots);
   __shared__ float red[32];
   __shared__ Phase ph_s[3];  // phases pi, pi+1 and pi+2 (copied ahead with cp.async)
@@ -1017,32 +1100,34 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(const MegaAr
     post_copies<R>(p, a, sp_s, L);
     if (!mbar_wait_bounded(L.vbar, vpar, a.err)) ok = false;
     vpar ^= 1u;
+    PHASE_MARK(pi, 1);
     if (p.kind == PH_GEMV) {
       gemv_prologue(p, a, L, red);
       __syncthreads();
-      PHASE_MARK(pi, 1);
+      PHASE_MARK(pi, 2);
       const uint4 *xf = reinterpret_cast<const uint4 *>(L.u);
       if (p.fmt == FMT_Q4)
         gemv_tiles<FMT_Q4>(p, a, gw, L, xf, cidx, st, ok, pol);
       else
         gemv_tiles<FMT_Q8>(p, a, gw, L, xf, cidx, st, ok, pol);
       __syncthreads();
-      PHASE_MARK(pi, 2);
+      PHASE_MARK(pi, 3);
       cta_combine(p, L.wpart);
     } else if (p.kind == PH_ATTN) {
-      attn_phase<R>(p, a, sp_s, L);
+      attn_phase<R>(p, a, sp_s, L, pi);
     } else {
       topk_phase(p, a, L);
     }
 #ifdef CH_PHASE_TRACE
     __syncthreads();
 #endif
-    PHASE_MARK(pi, 3);
+    PHASE_MARK(pi, 4);
     if (pi + 1 < a.nphases) {
+      grid_arrive(a.arrive);
       pre_phase<R>(ph_s[(pi + 1) % 3], a, sp_s, L);
-      PHASE_MARK(pi, 4);
-      grid_barrier(a.arrive, base + (unsigned long long)(pi + 1) * gridDim.x, a.err);
       PHASE_MARK(pi, 5);
+      grid_wait(a.arrive, base + (unsigned long long)(pi + 1) * gridDim.x, a.err);
+      PHASE_MARK(pi, 6);
     }
   }
   if (!ok && lane == 0) {
@@ -1057,7 +1142,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(const MegaAr
 size_t mk_smem_bytes(uint32_t max_k, uint32_t hidden, uint32_t ratio, uint32_t max_splits, uint32_t cache_slots,
                      uint32_t grid) {
   const size_t fixed = (size_t)MK_NW * MK_SPW * MK_STAGE + (MK_NW * MK_SPW + 2) * 8 + 16 + MK_NW * 2 * 16 * 4 +
-                      (kMaxGrid + 1) * 4 + 2 * kWinSlots * 4;
+                      2 * (kMaxGrid + 1) * 4 + 2 * kWinSlots * 4;
   const size_t part = (size_t)grid * 32 * 4;  // straddle partials of the previous GEMV
   // GEMV staging: 4 vectors of `hidden` for the norm prologues, one of max_k otherwise
   const size_t gemv = std::max((size_t)4 * hidden * 4, (size_t)max_k * 4) + part;

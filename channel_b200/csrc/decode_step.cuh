@@ -20,11 +20,11 @@ enum PrologueMode : uint32_t {
 // one partial sum per CTA (slot 0: the CTA's first row tile, slot 1: its last)
 // and the consumer phase adds them up while it loads its input.
 struct GemvOut {
-  float *direct;       // [rows]; act mode: [rows/2] = gelu(gate) * up
+  float *direct;       // [rows]; act mode: B fragments (f16 hi|lo) of the rows/2 values gelu(gate) * up
   float *partial;      // [grid][2][16] CTA partial sums of straddling row tiles
   uint32_t KT;         // k tiles of the producing GEMV
   uint32_t q, rem;     // balanced partition of its rows/16*KT tiles over grid*warps
-  uint32_t act;        // 1: interleaved gate|up GEMV; direct holds gelu(gate)*up
+  uint32_t act;        // 1: interleaved gate|up GEMV whose consumer takes B fragments
 };
 
 struct alignas(16) Phase {
@@ -43,7 +43,7 @@ struct alignas(16) Phase {
   const float *q_norm_w, *k_norm_w;
   const float2 *rope_cs;
   __half *k_cache, *v_cache;
-  float *attn_out;
+  float *attn_out;  // ATTN output, written as B fragments of the o-projection's input
 };
 
 // the weight stream of one GEMV phase (phases in order, GEMV phases only)

@@ -3,14 +3,19 @@
 Loads the instrumented library (``python -m channel_b200.build --trace`` builds
 libchannel_b200_trace.so with -DCH_PHASE_TRACE), decodes a few greedy tokens of
 the 12B-shape model on synthetic weights and prints, per phase kind, where the
-time of one token goes.  Each CTA's thread 0 records %globaltimer at six points
-of every phase:
+time of one token goes.  Each CTA's thread 0 records %globaltimer at seven
+points of every phase:
 
-  0 phase start (after the barrier)   1 input prologue done   2 weight tiles done
-  3 phase done                        4 next phase's pre-loads issued   5 barrier passed
+  0 phase start (grid barrier passed)    1 staged inputs landed (bulk copies)
+  2 GEMV: B fragments built / ATTN: heads normed and roped
+  3 GEMV: weight tiles done / ATTN: split partial written
+  4 phase done (GEMV: CTA combine; ATTN: split combine)
+  5 arrived at the next barrier and issued the next phase's early copies
+  6 next barrier passed
 
 A phase's cost is taken from the slowest CTA at each point (the grid waits for
-it).  Usage (one GPU):
+it); the per-CTA table shows median / max of each interval for layer 1.
+Usage (one GPU):
 
   python -m channel_b200.phase_trace [--layers 48] [--steps 4] [--clock 599] [--lib PATH]
 """
@@ -19,10 +24,12 @@ from __future__ import annotations
 import argparse
 import collections
 import ctypes as C
+from pathlib import Path
 
 import numpy as np
 
-TRACE_CTAS, TRACE_PHASES, TRACE_MARKS = 256, 512, 6
+TRACE_CTAS, TRACE_PHASES, TRACE_MARKS = 256, 512, 8
+COLS = ["staging", "prologue", "tiles/core", "combine", "arrive+pre", "barrier"]
 
 
 def main() -> None:
@@ -33,8 +40,6 @@ def main() -> None:
     ap.add_argument("--lib", default=None, help="an already built instrumented library (default: build it)")
     args = ap.parse_args()
 
-    from pathlib import Path
-
     from channel_b200 import _lib as L
     from channel_b200 import build
 
@@ -42,6 +47,8 @@ def main() -> None:
     lib = L.load()
     lib.ch_phase_trace_copy.restype = C.c_int
     lib.ch_phase_trace_copy.argtypes = [C.c_void_p, C.c_size_t]
+
+    import torch
 
     from channel_b200 import DynamicRingBuffer, GpuContext, GpuModelContext, config_12b
     from channel_b200.engine import gpu_dispatch_forward_token
@@ -60,49 +67,46 @@ def main() -> None:
     ctx.synchronize()
     buf = np.zeros(TRACE_CTAS * TRACE_PHASES * TRACE_MARKS, np.uint64)
     L.check(lib.ch_phase_trace_copy(buf.ctypes.data, buf.size))
-    grid = min(TRACE_CTAS, gm_grid())
+    grid = min(TRACE_CTAS, torch.cuda.get_device_properties(0).multi_processor_count)
     nph = 5 * cfg.num_hidden_layers + 2
-    tr = buf.reshape(TRACE_CTAS, TRACE_PHASES, TRACE_MARKS)[:grid, :nph, :].astype(np.int64)
+    tr = buf.reshape(TRACE_CTAS, TRACE_PHASES, TRACE_MARKS)[:grid, :nph, :7].astype(np.int64)
     kinds = ["qkv", "attn", "o", "gateup", "down"]
-    cols = ["prologue", "tiles", "combine/attn", "pre-loads", "barrier"]
-    agg = collections.defaultdict(lambda: np.zeros(5))
+
+    def fill(t, pi):
+        """marks a phase kind (or CTA) does not record take the previous mark's time"""
+        t = t.copy()
+        last = pi == nph - 1
+        for k in range(1, 7):
+            if last and k >= 5:
+                t[..., k] = t[..., 4]
+            else:
+                t[..., k] = np.where(t[..., k] == 0, t[..., k - 1], t[..., k])
+        return t
+
+    agg = collections.defaultdict(lambda: np.zeros(6))
     cnt = collections.Counter()
     for pi in range(nph):
         kind = kinds[pi % 5] if pi < 5 * cfg.num_hidden_layers else ("lm" if pi == nph - 2 else "topk")
-        st = tr[:, pi, :].max(axis=0)  # slowest CTA at each mark
-        if kind in ("attn", "topk"):
-            st[1] = st[2] = st[0]
-        if pi == nph - 1:
-            st[4] = st[5] = st[3]
-        agg[kind] += np.diff(st)
+        st = fill(tr[:, pi, :], pi)
+        agg[kind] += np.diff(st.max(axis=0))  # slowest CTA at each mark
         cnt[kind] += 1
-    span = tr[:, nph - 1, 3].max() - tr[:, 0, 0].min()
+    span = tr[:, nph - 1, 4].max() - tr[:, 0, 0].min()
     print(f"decode step span {span / 1e3:.1f} us ({cfg.num_hidden_layers} layers, clock {args.clock}, "
           f"{len(act)} active / {len(sli)} sliding slots)")
-    print("phase   n    " + "  ".join(f"{c:>12s}" for c in cols) + "   (us per phase, slowest CTA)")
+    print("phase   n   " + "".join(f"{c:>12s}" for c in COLS) + "   (us per phase, slowest CTA)")
     for k in ["qkv", "attn", "o", "gateup", "down", "lm", "topk"]:
         a = agg[k] / max(cnt[k], 1) / 1e3
-        print(f"{k:7s} {cnt[k]:3d}  " + "  ".join(f"{v:12.2f}" for v in a))
+        print(f"{k:7s} {cnt[k]:3d} " + "".join(f"{v:12.2f}" for v in a))
     per_layer = sum(agg[k].sum() for k in kinds) / cfg.num_hidden_layers / 1e3
     print(f"per layer {per_layer:.2f} us")
-    # per-CTA spread of layer 1's phases: median / max over CTAs of each interval
     print("layer 1, per CTA (median / max us):")
     for j, k in enumerate(kinds):
         pi = 5 + j
-        d = np.diff(tr[:, pi, :], axis=1) / 1e3
-        if k == "attn":
-            d[:, 0] = d[:, 1] = 0.0
-            d[:, 2] = (tr[:, pi, 3] - tr[:, pi, 0]) / 1e3
+        d = np.diff(fill(tr[:, pi, :], pi), axis=1) / 1e3
         med, mx = np.median(d, axis=0), d.max(axis=0)
-        print(f"  {k:7s} " + "  ".join(f"{a:6.2f}/{b:6.2f}" for a, b in zip(med, mx)) +
-              f"   slowest prologue CTA {int(d[:, 0].argmax())}, slowest tiles CTA {int(d[:, 1].argmax())}")
+        print(f"  {k:7s} " + "  ".join(f"{a:5.2f}/{b:5.2f}" for a, b in zip(med, mx)))
     gm.deinit()
     ctx.deinit()
-
-
-def gm_grid() -> int:
-    import torch
-    return torch.cuda.get_device_properties(0).multi_processor_count
 
 
 if __name__ == "__main__":
