@@ -82,8 +82,29 @@ CH_DEV uint32_t part_warp_of(uint32_t t, uint32_t q, uint32_t rem) {
   const uint32_t big = rem * (q + 1);
   return t < big ? t / (q + 1) : rem + (t - big) / q;
 }
-// CTA-level view of the same partition: CTA c owns tiles [cta_begin(c), cta_begin(c+1))
-CH_DEV uint32_t cta_begin(const GemvOut &o, uint32_t c) { return part_begin(c * MK_NW, o.q, o.rem); }
+// CTA c owns tiles [cta_begin(c), cta_begin(c+1)) (stream-K or whole row tiles)
+CH_DEV uint32_t cta_begin(const Partition &pt, uint32_t c) {
+  return pt.aligned ? (c * pt.rq + min(c, pt.rrem)) * pt.KT : part_begin(c * MK_NW, pt.q, pt.rem);
+}
+CH_DEV uint32_t cta_begin(const GemvOut &o, uint32_t c) { return cta_begin(o.pt, c); }
+// first tile of warp w (0..MK_NW) of CTA c
+CH_DEV uint32_t warp_begin(const Partition &pt, uint32_t c, uint32_t w) {
+  if (!pt.aligned) return part_begin(c * MK_NW + w, pt.q, pt.rem);
+  const uint32_t b = cta_begin(pt, c), T = cta_begin(pt, c + 1) - b;
+  return b + part_begin(w, T / MK_NW, T % MK_NW);
+}
+// warp of CTA c (0..MK_NW-1) whose range holds tile t of that CTA
+CH_DEV uint32_t warp_of(const Partition &pt, uint32_t c, uint32_t t) {
+  if (!pt.aligned) return part_warp_of(t, pt.q, pt.rem) - c * MK_NW;
+  const uint32_t b = cta_begin(pt, c), T = cta_begin(pt, c + 1) - b;
+  return part_warp_of(t - b, T / MK_NW, T % MK_NW);
+}
+
+// tensor parallel: the same buffer in rank r's exchange arena
+template <typename T>
+CH_DEV T *on_rank(const MegaArgs &a, T *local, uint32_t r) {
+  return reinterpret_cast<T *>(a.arena[r] + (reinterpret_cast<const uint8_t *>(local) - a.arena[a.rank]));
+}
 
 // ---------------------------------------------------------------------------
 // Straddle list of a GEMV output: entry k = c-1 describes the CTA boundary in front
@@ -94,7 +115,7 @@ CH_DEV uint32_t cta_begin(const GemvOut &o, uint32_t c) { return part_begin(c * 
 // CTAs).  slist[k] = kNoStraddle for boundaries between row tiles.  One thread
 // per entry.
 CH_DEV void build_slist(const GemvOut &o, uint32_t *slist, uint32_t *soff) {
-  const uint32_t G = gridDim.x, KT = o.KT;
+  const uint32_t G = gridDim.x, KT = o.pt.KT;
   for (uint32_t c = 1 + threadIdx.x; c < G; c += blockDim.x) {
     const uint32_t B = cta_begin(o, c);  // first tile of CTA c
     const uint32_t rt = B / KT;
@@ -116,7 +137,7 @@ CH_DEV float straddle_value(const GemvOut &o, const uint32_t *slist, const uint3
                             uint32_t k, uint32_t row) {
   const uint32_t off = soff[k];
   if (off != kNoStraddle) return __fadd_rn(__fadd_rn(0.f, P[(off & 0xFFFFu) + row]), P[(off >> 16) + row]);
-  const uint32_t t_lo = slist[k] * o.KT, t_hi = t_lo + o.KT - 1;
+  const uint32_t t_lo = slist[k] * o.pt.KT, t_hi = t_lo + o.pt.KT - 1;
   float v = 0.f;
   for (uint32_t cc = k; cc < gridDim.x && cta_begin(o, cc) <= t_hi; cc++) {
     const uint32_t b = cta_begin(o, cc);
@@ -140,24 +161,36 @@ CH_DEV void patch_staged(const GemvOut &o, const uint32_t *slist, const uint32_t
 // Grid barrier on a monotonically increasing arrival counter, in two halves so a
 // CTA can do work that does not depend on the other CTAs between its arrival
 // and its wait.  The wait is bounded.
-CH_DEV void grid_arrive(unsigned long long *arrive) {
+CH_DEV void grid_arrive(const MegaArgs &a) {
   __syncthreads();
   if (threadIdx.x == 0) {
-    __threadfence();
-    asm volatile("red.relaxed.gpu.global.add.u64 [%0], 1;" ::"l"(arrive) : "memory");
+    if (a.world > 1) {  // every CTA of every rank arrives on every rank's counter
+      __threadfence_system();
+      for (uint32_t r = 0; r < a.world; r++)
+        asm volatile("red.relaxed.sys.global.add.u64 [%0], 1;" ::"l"(on_rank(a, a.arrive, r)) : "memory");
+    } else {
+      __threadfence();
+      asm volatile("red.relaxed.gpu.global.add.u64 [%0], 1;" ::"l"(a.arrive) : "memory");
+    }
   }
 }
-CH_DEV void grid_wait(unsigned long long *arrive, unsigned long long target, uint32_t *err) {
+CH_DEV unsigned long long load_acquire_u64(const unsigned long long *p, bool sys) {
+  unsigned long long v;
+  if (sys)
+    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  else
+    asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+CH_DEV void grid_wait(const MegaArgs &a, unsigned long long target) {
   if (threadIdx.x == 0) {
-    unsigned long long v;
-    asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(arrive) : "memory");
-    if (v < target) {
+    const bool sys = a.world > 1;
+    if (load_acquire_u64(a.arrive, sys) < target) {
       const uint64_t t0 = globaltimer_ns();
       for (;;) {
-        asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(arrive) : "memory");
-        if (v >= target) break;
+        if (load_acquire_u64(a.arrive, sys) >= target) break;
         if (globaltimer_ns() - t0 > 2000000000ull) {
-          atomicOr(err, DEV_ERR_PEER_TIMEOUT);
+          atomicOr(a.err, DEV_ERR_PEER_TIMEOUT);
           break;
         }
       }
@@ -210,6 +243,23 @@ CH_DEV void store_frag_pair(uint32_t *frag, uint32_t j, float v0, float v1) {
   frag[frag_word(j, 0)] = pack_half2(h0, h1);
   frag[frag_word(j, 1)] = pack_half2(l0, l1);
 }
+// one finished output row (local index) of a GEMV: local buffer, or every rank's copy
+CH_DEV void out_row(const MegaArgs &a, const GemvOut &o, uint32_t row, float v) {
+  if (!o.push) {
+    o.direct[row] = v;
+    return;
+  }
+  for (uint32_t r = 0; r < a.world; r++) on_rank(a, o.direct, r)[o.row0 + row] = v;
+}
+// act values (j, j+1) (local index, j even) of a gate|up GEMV as B fragments
+CH_DEV void out_act_pair(const MegaArgs &a, const GemvOut &o, uint32_t j, float v0, float v1) {
+  uint32_t *f = reinterpret_cast<uint32_t *>(o.direct);
+  if (!o.push) {
+    store_frag_pair(f, j, v0, v1);
+    return;
+  }
+  for (uint32_t r = 0; r < a.world; r++) store_frag_pair(on_rank(a, f, r), o.row0 + j, v0, v1);
+}
 // Patch the act values of straddling gate|up row tiles (8 per row tile, act index
 // rt*8 + i = gelu(gate row i) * up row i+8) into a staged B-fragment array
 CH_DEV void patch_act_frag(const GemvOut &o, const uint32_t *slist, const uint32_t *soff, const float *P, uint32_t K,
@@ -256,30 +306,39 @@ CH_DEV void ld_pair_rot(const float *src, uint32_t p, float (&v)[8]) {
 struct Stream {
   uint32_t g, ck, nck, tb, te;  // GEMV stream index, next chunk, chunks of this warp's share, its tiles
   const uint8_t *tiles;
-  uint4 nxt;                    // raw StreamDesc of stream g + 1
+  uint4 nxt0, nxt1;             // raw StreamDesc of stream g + 1
 };
-CH_DEV uint4 load_desc(const MegaArgs &a, uint32_t g) {
-  return g < a.nstreams ? __ldg(reinterpret_cast<const uint4 *>(a.streams + g)) : make_uint4(0u, 0u, 0u, 0u);
+CH_DEV void load_desc(const MegaArgs &a, uint32_t g, uint4 &d0, uint4 &d1) {
+  if (g < a.nstreams) {
+    d0 = __ldg(reinterpret_cast<const uint4 *>(a.streams + g));
+    d1 = __ldg(reinterpret_cast<const uint4 *>(a.streams + g) + 1);
+  } else {
+    d0 = d1 = make_uint4(0u, 0u, 0u, 0u);
+  }
 }
-CH_DEV void stream_enter(uint32_t gw, Stream &s, const uint4 &d) {
-  s.tiles = reinterpret_cast<const uint8_t *>((uint64_t)d.x | ((uint64_t)d.y << 32));
-  s.tb = part_begin(gw, d.z, d.w);
-  s.te = part_begin(gw + 1, d.z, d.w);
+// StreamDesc {tiles, Partition{KT, q, rem, aligned, rq, rrem}} from its two 16-byte halves
+CH_DEV void stream_enter(uint32_t gw, Stream &s, const uint4 &d0, const uint4 &d1) {
+  s.tiles = reinterpret_cast<const uint8_t *>((uint64_t)d0.x | ((uint64_t)d0.y << 32));
+  const Partition pt{d0.z, d0.w, d1.x, d1.y, d1.z, d1.w};
+  s.tb = warp_begin(pt, gw / MK_NW, gw % MK_NW);
+  s.te = warp_begin(pt, gw / MK_NW, gw % MK_NW + 1);
   s.nck = (s.te - s.tb + MK_CT - 1) / MK_CT;
   s.ck = 0;
 }
 CH_DEV void stream_init(const MegaArgs &a, uint32_t gw, Stream &s) {
   s.g = 0;
-  stream_enter(gw, s, load_desc(a, 0));
-  s.nxt = load_desc(a, 1);
+  uint4 d0, d1;
+  load_desc(a, 0, d0, d1);
+  stream_enter(gw, s, d0, d1);
+  load_desc(a, 1, s.nxt0, s.nxt1);
 }
 // advance to the next chunk to issue; false when the step's stream is done
 CH_DEV bool stream_next(const MegaArgs &a, uint32_t gw, Stream &s) {
   while (s.ck >= s.nck) {
     if (s.g + 1 >= a.nstreams) return false;
     s.g++;
-    stream_enter(gw, s, s.nxt);
-    s.nxt = load_desc(a, s.g + 1);
+    stream_enter(gw, s, s.nxt0, s.nxt1);
+    load_desc(a, s.g + 1, s.nxt0, s.nxt1);
   }
   return true;
 }
@@ -394,32 +453,33 @@ CH_DEV void gemv_prologue(const Phase &p, const MegaArgs &a, const SmemLayout &L
 
 // After every warp of the CTA finished its tiles: fold the warps' partial segments.
 // Row tiles inside the CTA's range go to `direct`, straddling ones to the CTA's slot.
-CH_DEV void cta_combine(const Phase &p, const float *wpart) {
+CH_DEV void cta_combine(const Phase &p, const MegaArgs &a, const float *wpart) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const uint32_t c = blockIdx.x, KT = p.k_tiles;
-  const uint32_t cb = cta_begin(p.out, c), ce = cta_begin(p.out, c + 1);
+  const Partition &pt = p.out.pt;
+  const uint32_t cb = cta_begin(pt, c), ce = cta_begin(pt, c + 1);
   if (ce == cb) return;
   const uint32_t rt0 = cb / KT, rt1 = (ce - 1) / KT;
   for (uint32_t rt = rt0 + warp; rt <= rt1; rt += MK_NW) {
     const uint32_t t_lo = rt * KT, t_hi = t_lo + KT - 1;
     const uint32_t a_lo = max(t_lo, cb), a_hi = min(t_hi, ce - 1);
-    const uint32_t w0 = part_warp_of(a_lo, p.q, p.rem), w1 = part_warp_of(a_hi, p.q, p.rem);
+    const uint32_t w0 = warp_of(pt, c, a_lo), w1 = warp_of(pt, c, a_hi);
     const bool inside = cb <= t_lo && t_hi < ce;
-    if (w0 == w1 && inside) continue;  // one warp covered the whole row tile: already direct
+    if (w0 == w1 && inside) continue;  // one warp covered the whole row tile: already stored
     float sum = 0.f;
     if (lane < 16)
       for (uint32_t w = w0; w <= w1; w++) {
-        const uint32_t slot = part_begin(w, p.q, p.rem) < t_lo ? 1u : 0u;
-        sum = __fadd_rn(sum, wpart[((w - c * MK_NW) * 2 + slot) * 16 + lane]);
+        const uint32_t slot = warp_begin(pt, c, w) < t_lo ? 1u : 0u;
+        sum = __fadd_rn(sum, wpart[(w * 2 + slot) * 16 + lane]);
       }
     const float up = __shfl_down_sync(0xffffffffu, sum, 8);
     if (inside) {
       if (p.out.act) {  // act values of lanes 0..7 as B fragments, in pairs
         const float av = __fmul_rn(gelu_tanh(sum), up);
         const float an = __shfl_down_sync(0xffffffffu, av, 1);
-        if (lane < 8 && !(lane & 1)) store_frag_pair(reinterpret_cast<uint32_t *>(p.out.direct), rt * 8 + lane, av, an);
+        if (lane < 8 && !(lane & 1)) out_act_pair(a, p.out, rt * 8 + lane, av, an);
       } else if (lane < 16) {
-        p.out.direct[rt * 16 + lane] = sum;
+        out_row(a, p.out, rt * 16 + lane, sum);
       }
     } else if (lane < 16) {  // straddling row tile: this CTA's share, added up by the consumer
       p.out.partial[((size_t)c * 2 + (cb < t_lo ? 1u : 0u)) * 16 + lane] = sum;
@@ -435,7 +495,7 @@ CH_DEV void gemv_tiles(const Phase &p, const MegaArgs &a, uint32_t gw, const Sme
   uint8_t *my_stages = L.stages + (size_t)warp * MK_SPW * MK_STAGE;
   uint64_t *my_bars = L.bars + warp * MK_SPW;
   const uint32_t KT = p.k_tiles;
-  const uint32_t tb = part_begin(gw, p.q, p.rem), te = part_begin(gw + 1, p.q, p.rem);
+  const uint32_t tb = warp_begin(p.out.pt, blockIdx.x, warp), te = warp_begin(p.out.pt, blockIdx.x, warp + 1);
   const uint32_t nchunks = (te - tb + MK_CT - 1) / MK_CT;
   const uint4 *xb = (g < 2) ? xf + t * 2 + g : L.xzero;
   const uint32_t xs = (g < 2) ? 8u : 0u;
@@ -450,10 +510,10 @@ CH_DEV void gemv_tiles(const Phase &p, const MegaArgs &a, uint32_t gw, const Sme
     if (t == 0) {
       if (kb == 0 && ke == KT) {
         if (p.out.act) {
-          if (!(g & 1)) store_frag_pair(reinterpret_cast<uint32_t *>(p.out.direct), frt * 8 + g, av, an);
+          if (!(g & 1)) out_act_pair(a, p.out, frt * 8 + g, av, an);
         } else {
-          p.out.direct[frt * 16 + g] = acc0;
-          p.out.direct[frt * 16 + g + 8] = acc1;
+          out_row(a, p.out, frt * 16 + g, acc0);
+          out_row(a, p.out, frt * 16 + g + 8, acc1);
         }
       } else {
         const uint32_t slot = first_seg ? 0u : 1u;
@@ -533,6 +593,17 @@ CH_DEV AttnItem attn_item(const MegaArgs &a, const StepParams &sp, uint32_t is_s
   const uint32_t c1 = min(it.S, it.c0 + it.chunk);
   it.n = c1 > it.c0 ? c1 - it.c0 : 0;
   return it;
+}
+
+// attention output elements (j, j+1) of this rank's heads as B fragments of the
+// o-projection input: local buffer, or (tensor parallel) every rank's copy at the
+// rank's global head offset
+CH_DEV void attn_out_pair(const MegaArgs &a, uint32_t *frag, uint32_t j, float v0, float v1) {
+  if (a.world <= 1) {
+    store_frag_pair(frag, j, v0, v1);
+    return;
+  }
+  for (uint32_t r = 0; r < a.world; r++) store_frag_pair(on_rank(a, frag, r), a.attn_q0 * kHeadDim + j, v0, v1);
 }
 
 // Shared-memory layout of the ATTN phase (inside the union region).
@@ -825,7 +896,7 @@ CH_DEV void attn_phase(const Phase &p, const MegaArgs &a, const StepParams &sp, 
       const float Lsum = __fmaf_rn(sm.stat[2 * h + 1], 1.0f, 0.f);
       const float o = __fmul_rn(__fmaf_rn(s, 1.0f, 0.f), __fdiv_rn(1.0f, __fadd_rn(Lsum, 1e-9f)));
       const float on = __shfl_down_sync(0xffffffffu, o, 1);
-      if (!(idx & 1)) store_frag_pair(out_frag, (kvh * R + h) * D + d, o, on);
+      if (!(idx & 1)) attn_out_pair(a, out_frag, (kvh * R + h) * D + d, o, on);
     }
     return;
   }
@@ -901,7 +972,7 @@ CH_DEV void attn_phase(const Phase &p, const MegaArgs &a, const StepParams &sp, 
     o = __fmul_rn(O, sm.stat[2 * h]);
   }
   const float on = __shfl_down_sync(0xffffffffu, o, 1);
-  if (mine && !(idx & 1)) store_frag_pair(out_frag, (kvh * R + h) * D + d, o, on);
+  if (mine && !(idx & 1)) attn_out_pair(a, out_frag, (kvh * R + h) * D + d, o, on);
 }
 
 // ---------------------------------------------------------------------------
@@ -934,6 +1005,28 @@ CH_DEV void topk_post_copies(const Phase &p, const SmemLayout &L) {
   if (hi4 > lo4) stage_copy(L, sm.lg, p.r_in.direct + lo4, (hi4 - lo4) * 4);
   stage_copy(L, sm.part, p.r_in.partial, gridDim.x * 32 * 4);
 }
+// the final 64 (sorted keys) -> ids / vals / greedy token / device-loop step
+CH_DEV void topk_finish(const MegaArgs &a, const uint64_t *sorted) {
+  const int tid = threadIdx.x;
+  if (tid < 64) {
+    const uint64_t key = sorted[tid];
+    uint32_t id = 0;
+    float val = -1e30f;
+    if (key != 0) {
+      id = 0xFFFFFFFFu - (uint32_t)(key & 0xFFFFFFFFu);
+      val = unsortable((uint32_t)(key >> 32));
+    }
+    a.ids[tid] = id;
+    a.vals[tid] = val;
+    if (tid == 0) {
+      if (a.token_out) *a.token_out = id;
+      if (a.sp_rw) {
+        const uint32_t step = a.sp_rw->step;
+        if (a.token_hist && step < a.hist_cap) a.token_hist[step] = id;
+      }
+    }
+  }
+}
 CH_DEV void topk_phase(const Phase &p, const MegaArgs &a, const SmemLayout &L) {
   constexpr int E1 = 8, E2 = 20;  // per-thread keys: slice <= 4096, candidates <= 10240
   TopkSmem sm(L.u);
@@ -952,7 +1045,7 @@ CH_DEV void topk_phase(const Phase &p, const MegaArgs &a, const SmemLayout &L) {
       const uint32_t idx = lo + e * MK_THREADS + tid;
       if (idx < hi) {
         const float v = softcap(sm.lg[idx - lo4]);
-        k[e] = ((uint64_t)sortable(v) << 32) | (uint64_t)(0xFFFFFFFFu - idx);
+        k[e] = ((uint64_t)sortable(v) << 32) | (uint64_t)(0xFFFFFFFFu - (p.vocab0 + idx));  // global id
       } else {
         k[e] = 0;
       }
@@ -976,26 +1069,27 @@ CH_DEV void topk_phase(const Phase &p, const MegaArgs &a, const SmemLayout &L) {
   }
   const uint64_t thr = block_kth_largest<E2>(k, 64, sm.hist, sm.sh);
   collect_sorted64<E2>(k, thr, sm.buf, sm.cnt, sm.sorted);
-  if (tid < 64) {
-    const uint64_t key = sm.sorted[tid];
-    uint32_t id = 0;
-    float val = -1e30f;
-    if (key != 0) {
-      id = 0xFFFFFFFFu - (uint32_t)(key & 0xFFFFFFFFu);
-      val = unsortable((uint32_t)(key >> 32));
-    }
-    a.ids[tid] = id;
-    a.vals[tid] = val;
-    if (tid == 0) {
-      if (a.token_out) *a.token_out = id;
-      if (a.sp_rw) {
-        const uint32_t step = a.sp_rw->step;
-        if (a.token_hist && step < a.hist_cap) a.token_hist[step] = id;
-        a.sp_rw->step = step + 1;
-      }
-    }
-  }
   if (tid == 0) *a.topk_counter = 0u;
+  if (a.world <= 1) {
+    topk_finish(a, sm.sorted);
+    return;
+  }
+  // tensor parallel: this rank's 64 go to slot `rank` of every rank's candidate table
+  if (tid < 64)
+    for (uint32_t r = 0; r < a.world; r++) on_rank(a, a.xcand, r)[a.rank * 64 + tid] = sm.sorted[tid];
+}
+
+// MERGE phase (tensor parallel): every rank's CTA 0 merges the world x 64 staged
+// candidates into the same final 64 and token
+CH_DEV void merge_phase(const MegaArgs &a, const SmemLayout &L) {
+  if (blockIdx.x != 0) return;
+  TopkSmem sm(L.u);
+  const uint64_t *staged = reinterpret_cast<const uint64_t *>(sm.lg);
+  uint64_t k[1];
+  k[0] = threadIdx.x < a.world * 64 ? staged[threadIdx.x] : 0ull;
+  const uint64_t thr = block_kth_largest<1>(k, 64, sm.hist, sm.sh);
+  collect_sorted64<1>(k, thr, sm.buf, sm.cnt, sm.sorted);
+  topk_finish(a, sm.sorted);
 }
 
 // ---------------------------------------------------------------------------
@@ -1018,7 +1112,7 @@ CH_DEV void pre_phase(const Phase &p, const MegaArgs &a, const StepParams &sp, c
   } else if (p.kind == PH_ATTN) {
     build_slist(p.r_in, L.slist, L.soff);
     attn_pre<R>(p, a, sp, L);
-  } else {
+  } else if (p.kind == PH_TOPK) {
     build_slist(p.r_in, L.slist, L.soff);
   }
   __syncthreads();  // every expect_tx of this phase precedes the arrival
@@ -1041,8 +1135,11 @@ CH_DEV void post_copies(const Phase &p, const MegaArgs &a, const StepParams &sp,
     }
   } else if (p.kind == PH_ATTN) {
     attn_post_copies<R>(p, a, sp, L);
-  } else {
+  } else if (p.kind == PH_TOPK) {
     topk_post_copies(p, L);
+  } else if (blockIdx.x == 0) {  // PH_MERGE: every rank's candidates, written by the peers before the barrier
+    TopkSmem sm(L.u);
+    stage_copy(L, sm.lg, a.xcand, a.world * 64 * 8);
   }
   mbar_arrive(L.vbar);
 }
@@ -1089,8 +1186,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(const MegaAr
   attn_lists_init(a, sp_s, L.wphys);
   pre_phase<R>(ph_s[0], a, sp_s, L);
 
-  const unsigned long long epoch = *a.epoch;
-  const unsigned long long base = epoch * (unsigned long long)(a.nphases - 1) * gridDim.x;
+  const unsigned long long base = *a.base;  // arrivals before this launch
   uint32_t cidx = 0, vpar = 0;
   bool ok = true;
   for (uint32_t pi = 0; pi < a.nphases; pi++) {
@@ -1112,21 +1208,23 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(const MegaAr
         gemv_tiles<FMT_Q8>(p, a, gw, L, xf, cidx, st, ok, pol);
       __syncthreads();
       PHASE_MARK(pi, 3);
-      cta_combine(p, L.wpart);
+      cta_combine(p, a, L.wpart);
     } else if (p.kind == PH_ATTN) {
       attn_phase<R>(p, a, sp_s, L, pi);
-    } else {
+    } else if (p.kind == PH_TOPK) {
       topk_phase(p, a, L);
+    } else {
+      merge_phase(a, L);
     }
 #ifdef CH_PHASE_TRACE
     __syncthreads();
 #endif
     PHASE_MARK(pi, 4);
     if (pi + 1 < a.nphases) {
-      grid_arrive(a.arrive);
+      grid_arrive(a);
       pre_phase<R>(ph_s[(pi + 1) % 3], a, sp_s, L);
       PHASE_MARK(pi, 5);
-      grid_wait(a.arrive, base + (unsigned long long)(pi + 1) * gridDim.x, a.err);
+      grid_wait(a, base + (unsigned long long)(pi + 1) * gridDim.x * a.world);
       PHASE_MARK(pi, 6);
     }
   }
@@ -1136,7 +1234,9 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(const MegaAr
     for (uint32_t j = cidx >= MK_SPW ? cidx - MK_SPW : 0; j < cidx; j++)
       mbar_wait_bounded(&my_bars[j % MK_SPW], (j / MK_SPW) & 1, nullptr, 100000000ull);
   }
-  if (blockIdx.x == 0 && threadIdx.x == 0) *a.epoch = (uint32_t)(epoch + 1);
+  // every CTA has passed the last barrier, so all have read `base`: advance it for the next launch
+  if (blockIdx.x == 0 && threadIdx.x == 0)
+    *a.base = base + (unsigned long long)(a.nphases - 1) * gridDim.x * a.world;
 }
 
 size_t mk_smem_bytes(uint32_t max_k, uint32_t hidden, uint32_t ratio, uint32_t max_splits, uint32_t cache_slots,

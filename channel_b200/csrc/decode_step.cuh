@@ -6,7 +6,7 @@
 
 namespace ch {
 
-enum PhaseKind : uint32_t { PH_GEMV = 0, PH_ATTN = 1, PH_TOPK = 2 };
+enum PhaseKind : uint32_t { PH_GEMV = 0, PH_ATTN = 1, PH_TOPK = 2, PH_MERGE = 3 };
 // how a GEMV phase builds its input vector
 enum PrologueMode : uint32_t {
   PM_DIRECT = 0,    // x_in as is (attention output)
@@ -15,23 +15,38 @@ enum PrologueMode : uint32_t {
   PM_GELU = 3,      // gelu_tanh(gate) * up from an interleaved gate|up GEMV output
 };
 
+constexpr uint32_t kMaxWorld = 8;  // ranks of a tensor-parallel decode
+
+// How a GEMV phase's tiles (row tiles x KT k tiles, row-tile major) are split over
+// the grid's warps.  Stream-K: one balanced split over all grid*warps warps (row
+// tiles may straddle CTAs).  Aligned: whole row tiles per CTA (rq or rq+1), then a
+// balanced split over the CTA's warps -- no row tile crosses a CTA, so every
+// output row is finished inside one CTA (used when outputs go to other GPUs).
+struct Partition {
+  uint32_t KT;        // k tiles per row tile
+  uint32_t q, rem;    // stream-K: tiles per warp (q or q+1)
+  uint32_t aligned;   // 1: whole row tiles per CTA
+  uint32_t rq, rrem;  // aligned: row tiles per CTA (rq or rq+1)
+};
+
 // Output of a GEMV phase.  A row tile whose k tiles all fall in one CTA's share
 // is finished by that CTA in `direct`; a row tile that straddles CTAs is left as
 // one partial sum per CTA (slot 0: the CTA's first row tile, slot 1: its last)
 // and the consumer phase adds them up while it loads its input.
 struct GemvOut {
-  float *direct;       // [rows]; act mode: B fragments (f16 hi|lo) of the rows/2 values gelu(gate) * up
-  float *partial;      // [grid][2][16] CTA partial sums of straddling row tiles
-  uint32_t KT;         // k tiles of the producing GEMV
-  uint32_t q, rem;     // balanced partition of its rows/16*KT tiles over grid*warps
-  uint32_t act;        // 1: interleaved gate|up GEMV whose consumer takes B fragments
+  float *direct;   // [rows]; act mode: B fragments (f16 hi|lo) of the rows/2 values gelu(gate) * up
+  float *partial;  // [grid][2][16] CTA partial sums of straddling row tiles
+  Partition pt;    // the producing GEMV's split
+  uint32_t act;    // 1: interleaved gate|up GEMV whose consumer takes B fragments
+  uint32_t row0;   // tensor parallel: index of this rank's first row (act value) in the gathered vector
+  uint32_t push;   // 1: rows go to every rank's copy of `direct` (peer stores), 0: local only
 };
 
 struct alignas(16) Phase {
   uint32_t kind, fmt, pm, is_sliding;
   // GEMV
   const uint8_t *tiles;
-  uint32_t row_tiles, k_tiles, K, q, rem, vocab;
+  uint32_t row_tiles, k_tiles, K, vocab, vocab0;
   GemvOut out;
   // GEMV prologue inputs / ATTN and TOPK inputs
   const float *x_in;
@@ -49,7 +64,7 @@ struct alignas(16) Phase {
 // the weight stream of one GEMV phase (phases in order, GEMV phases only)
 struct alignas(16) StreamDesc {
   const uint8_t *tiles;
-  uint32_t q, rem;  // balanced partition of the phase's tiles over grid * warps
+  Partition pt;
 };
 
 struct MegaArgs {
@@ -58,11 +73,11 @@ struct MegaArgs {
   uint32_t nstreams;
   uint32_t nphases, grid;
   unsigned long long *arrive;  // grid-barrier arrivals (monotonic across launches)
-  uint32_t *epoch;    // completed launches
+  unsigned long long *base;    // arrivals at the start of this launch (advanced by the launch)
   uint32_t *err;
   const StepParams *sp;
-  StepParams *sp_rw;  // device loop: step counter advanced by the top-k phase (else null)
-  uint32_t nq, nkv, rot, attn_max_splits, cache_slots;
+  StepParams *sp_rw;  // device loop: the top-k phase records the token at history slot sp->step (else null)
+  uint32_t nq, nkv, rot, attn_max_splits, cache_slots;  // nq / nkv: this rank's heads
   float eps;
   float *attn_partial;
   uint32_t *attn_counters;
@@ -72,6 +87,11 @@ struct MegaArgs {
   float *vals;
   uint32_t *token_out, *token_hist;
   uint32_t hist_cap;
+  // tensor parallel (world > 1): every rank's exchange arena, mapped into this process
+  uint32_t world, rank;
+  uint32_t attn_q0;            // global index of this rank's first q head
+  uint8_t *arena[kMaxWorld];   // arena[rank] is this rank's own
+  uint64_t *xcand;             // this rank's [world][64] top-64 candidates of every rank (in its arena)
 };
 
 int mk_warps();

@@ -74,7 +74,10 @@ struct StepParams {
   uint32_t clock, slot, n_active, n_sliding;
   const uint32_t *active;   // device list of physical slots (full-attention layers)
   const uint32_t *sliding;  // device list (sliding layers)
-  uint32_t step, pad;
+  uint32_t step;            // index of this step in the plan (token history slot)
+  uint32_t next;            // device loop: plan index of the next step (advanced by step_begin)
+  uint32_t force;           // plan entry: token + 1 to embed instead of the fed-back token (0: fed back)
+  uint32_t pad;
 };
 
 struct AttnArgs {

@@ -150,6 +150,16 @@ struct ch_model {
   ch_ctx *ctx = nullptr;
   ch_model_config cfg{};
   uint32_t H = 0, I = 0, V = 0, D = 0, nq = 0, nkv = 0, qd = 0, kvd = 0, L = 0;
+  // tensor parallel: this process holds shard `rank` of `world` (1 = the whole model).
+  // Local sizes: q / kv heads, o and down output rows, gate and up rows, vocab rows.
+  uint32_t rank = 0, world = 1;
+  uint32_t nq_l = 0, nkv_l = 0, qd_l = 0, kvd_l = 0, Ho = 0, Il = 0, Vl = 0;
+  uint8_t *arena = nullptr;                // exchange arena (CUDA IPC shared): gathered vectors + arrivals
+  uint8_t *peer_arena[kMaxWorld] = {};     // every rank's arena mapped here (peer_arena[rank] = arena)
+  bool peers_ready = false;
+  size_t off_arrive = 0, off_o = 0, off_down = 0, off_act = 0, off_attn = 0, off_cand = 0, arena_bytes = 0;
+  StepParams *pplan = nullptr;             // tensor-parallel prefill: forced-token plan
+  uint32_t *pplan_lists = nullptr;
   std::vector<DevLayer> layers;
   uint8_t *lm = nullptr;
   float *final_norm = nullptr;
@@ -196,7 +206,7 @@ struct ch_model {
   float *gdir[5] = {nullptr, nullptr, nullptr, nullptr, nullptr};
   float *gpart[5] = {nullptr, nullptr, nullptr, nullptr, nullptr};
   unsigned long long *mk_arrive = nullptr;
-  uint32_t *mk_epoch = nullptr;
+  unsigned long long *mk_base = nullptr;  // barrier arrivals before the next launch
   size_t mk_smem = 0;
   int mk_grid = 0;
   bool use_ops = false;  // kernel-per-op decode (CH_DECODE_OPS=1), kept for A/B measurement
@@ -239,7 +249,12 @@ static void free_model(ch_model *m) {
   cudaFree(m->d_streams);
   cudaFree(m->d_streams_nl);
   cudaFree(m->mk_arrive);
-  cudaFree(m->mk_epoch);
+  cudaFree(m->mk_base);
+  cudaFree(m->pplan);
+  cudaFree(m->pplan_lists);
+  for (uint32_t r = 0; r < m->world && r < kMaxWorld; r++)
+    if (r != m->rank && m->peer_arena[r]) cudaIpcCloseMemHandle(m->peer_arena[r]);
+  cudaFree(m->arena);
   void *host[] = {m->h_x, m->h_sp, m->h_lists, m->h_ids, m->h_vals, m->h_run, m->h_rope};
   for (void *p : host) cudaFreeHost(p);
   if (m->g_host_logits) cudaGraphExecDestroy(m->g_host_logits);
@@ -287,24 +302,32 @@ static int alloc_model_buffers(ch_model *m) {
   m->qd = m->nq * m->D;
   m->kvd = m->nkv * m->D;
   m->L = c.num_hidden_layers;
+  const uint32_t P = m->world;
+  m->nq_l = m->nq / P;
+  m->nkv_l = m->nkv / P;
+  m->qd_l = m->nq_l * m->D;
+  m->kvd_l = m->nkv_l * m->D;
+  m->Ho = m->H / P;
+  m->Il = m->I / P;
+  m->Vl = m->V / P;
   m->layers.resize(m->L);
   for (uint32_t l = 0; l < m->L; l++) {
     DevLayer &dl = m->layers[l];
     dl.full = c.layer_types[l] != 0;
-    CH_TRY(dmalloc(&dl.qkv, q4_tile_bytes(m->qd + 2 * m->kvd, m->H)));
-    CH_TRY(dmalloc(&dl.o, q4_tile_bytes(m->H, m->qd)));
-    CH_TRY(dmalloc(&dl.gateup, q4_tile_bytes(2 * m->I, m->H)));
-    CH_TRY(dmalloc(&dl.down, q4_tile_bytes(m->H, m->I)));
+    CH_TRY(dmalloc(&dl.qkv, q4_tile_bytes(m->qd_l + 2 * m->kvd_l, m->H)));
+    CH_TRY(dmalloc(&dl.o, q4_tile_bytes(m->Ho, m->qd)));
+    CH_TRY(dmalloc(&dl.gateup, q4_tile_bytes(2 * m->Il, m->H)));
+    CH_TRY(dmalloc(&dl.down, q4_tile_bytes(m->Ho, m->I)));
     CH_TRY(dmalloc(&dl.input_norm, m->H));
     CH_TRY(dmalloc(&dl.q_norm, m->D));
     CH_TRY(dmalloc(&dl.k_norm, m->D));
     CH_TRY(dmalloc(&dl.pre_ffn, m->H));
-    CH_TRY(dmalloc(&dl.kc, (size_t)kSlots * m->kvd));
-    CH_TRY(dmalloc(&dl.vc, (size_t)kSlots * m->kvd));
-    CH_CUDA(cudaMemsetAsync(dl.kc, 0, (size_t)kSlots * m->kvd * 2, m->ctx->stream));
-    CH_CUDA(cudaMemsetAsync(dl.vc, 0, (size_t)kSlots * m->kvd * 2, m->ctx->stream));
+    CH_TRY(dmalloc(&dl.kc, (size_t)kSlots * m->kvd_l));
+    CH_TRY(dmalloc(&dl.vc, (size_t)kSlots * m->kvd_l));
+    CH_CUDA(cudaMemsetAsync(dl.kc, 0, (size_t)kSlots * m->kvd_l * 2, m->ctx->stream));
+    CH_CUDA(cudaMemsetAsync(dl.vc, 0, (size_t)kSlots * m->kvd_l * 2, m->ctx->stream));
   }
-  CH_TRY(dmalloc(&m->lm, q8_tile_bytes(m->V, m->H)));
+  CH_TRY(dmalloc(&m->lm, q8_tile_bytes(m->Vl, m->H)));
   CH_TRY(dmalloc(&m->final_norm, m->H));
   CH_TRY(dmalloc(&m->inv_freq_s, c.rotary_dim / 2));
   CH_TRY(dmalloc(&m->inv_freq_f, c.rotary_dim / 2));
@@ -369,13 +392,32 @@ enum GemvKind { GK_QKV = 0, GK_O = 1, GK_GU = 2, GK_DOWN = 3, GK_LM = 4 };
 
 static int build_phases(ch_model *m, bool with_logits, Phase **d_out, uint32_t *n_out, StreamDesc **d_str,
                         uint32_t *n_str) {
-  const uint32_t GW = (uint32_t)m->mk_grid * mk_warps();
-  const uint32_t rows[5] = {m->qd + 2 * m->kvd, m->H, 2 * m->I, m->H, m->V};
+  const uint32_t G = (uint32_t)m->mk_grid, GW = G * mk_warps();
+  const bool tp = m->world > 1;
+  // local output rows of each GEMV, its k tiles, and whether its outputs are gathered
+  // from every rank (tensor parallel: o, gate|up and down outputs)
+  const uint32_t rows[5] = {m->qd_l + 2 * m->kvd_l, m->Ho, 2 * m->Il, m->Ho, m->Vl};
   const uint32_t KT[5] = {m->H / 64, m->qd / 64, m->H / 64, m->I / 64, m->H / 32};
+  const bool gathered[5] = {false, tp, tp, tp, false};
+  float *dst[5] = {m->gdir[GK_QKV], m->gdir[GK_O], m->gdir[GK_GU], m->gdir[GK_DOWN], m->gdir[GK_LM]};
+  uint32_t row0[5] = {0, 0, 0, 0, 0};
+  if (tp) {
+    dst[GK_O] = reinterpret_cast<float *>(m->arena + m->off_o);
+    dst[GK_GU] = reinterpret_cast<float *>(m->arena + m->off_act);
+    dst[GK_DOWN] = reinterpret_cast<float *>(m->arena + m->off_down);
+    row0[GK_O] = row0[GK_DOWN] = m->rank * m->Ho;
+    row0[GK_GU] = m->rank * m->Il;  // act values
+  }
   GemvOut outs[5];
   for (int k = 0; k < 5; k++) {
     const uint64_t T = (uint64_t)(rows[k] / 16) * KT[k];
-    outs[k] = GemvOut{m->gdir[k], m->gpart[k], KT[k], (uint32_t)(T / GW), (uint32_t)(T % GW), k == GK_GU ? 1u : 0u};
+    Partition pt{KT[k], (uint32_t)(T / GW), (uint32_t)(T % GW), 0u, 0u, 0u};
+    if (gathered[k]) {  // whole row tiles per CTA: every row finished inside one CTA, then sent to all ranks
+      pt.aligned = 1;
+      pt.rq = (rows[k] / 16) / G;
+      pt.rrem = (rows[k] / 16) % G;
+    }
+    outs[k] = GemvOut{dst[k], m->gpart[k], pt, k == GK_GU ? 1u : 0u, row0[k], gathered[k] ? 1u : 0u};
   }
   auto gemv = [&](int kind, const uint8_t *tiles, int fmt, uint32_t K) {
     Phase p{};
@@ -385,12 +427,11 @@ static int build_phases(ch_model *m, bool with_logits, Phase **d_out, uint32_t *
     p.row_tiles = rows[kind] / 16;
     p.k_tiles = KT[kind];
     p.K = K;
-    p.q = outs[kind].q;
-    p.rem = outs[kind].rem;
     p.out = outs[kind];
     p.scalar = 1.0f;
     return p;
   };
+  float *attn_frag = tp ? reinterpret_cast<float *>(m->arena + m->off_attn) : m->attn;
   std::vector<Phase> ph;
   const uint32_t rh = m->cfg.rotary_dim / 2;
   for (uint32_t l = 0; l < m->L; l++) {
@@ -421,11 +462,11 @@ static int build_phases(ch_model *m, bool with_logits, Phase **d_out, uint32_t *
     at.v_cache = dl.vc;
     at.is_sliding = dl.full ? 0 : 1;
     at.attn_scale = 1.0f;  // Gemma-style: q/k norms replace 1/sqrt(d) (forward.zig:85)
-    at.attn_out = m->attn;
+    at.attn_out = attn_frag;
     ph.push_back(at);
     Phase o = gemv(GK_O, dl.o, FMT_Q4, m->qd);
     o.pm = PM_DIRECT;
-    o.x_in = m->attn;
+    o.x_in = attn_frag;
     ph.push_back(o);
     Phase gu = gemv(GK_GU, dl.gateup, FMT_Q4, m->H);
     gu.pm = PM_ADD_NORM;
@@ -453,22 +494,28 @@ static int build_phases(ch_model *m, bool with_logits, Phase **d_out, uint32_t *
   lm.normed_out = m->normed;
   if (!with_logits) {  // prologue only: fold the last residual add + final norm
     lm.row_tiles = 0;
-    lm.q = lm.rem = 0;
+    lm.out.pt.q = lm.out.pt.rem = 0;
   }
   ph.push_back(lm);
   if (with_logits) {
     Phase tk{};
     tk.kind = PH_TOPK;
     tk.r_in = outs[GK_LM];
-    tk.vocab = m->V;
+    tk.vocab = m->Vl;
+    tk.vocab0 = m->rank * m->Vl;
     ph.push_back(tk);
+    if (tp) {
+      Phase mg{};
+      mg.kind = PH_MERGE;
+      ph.push_back(mg);
+    }
   }
   CH_TRY(dmalloc(d_out, ph.size()));
   CH_CUDA(cudaMemcpy(*d_out, ph.data(), ph.size() * sizeof(Phase), cudaMemcpyHostToDevice));
   *n_out = (uint32_t)ph.size();
   std::vector<StreamDesc> st;
   for (const Phase &p : ph)
-    if (p.kind == PH_GEMV) st.push_back(StreamDesc{p.tiles, p.q, p.rem});
+    if (p.kind == PH_GEMV) st.push_back(StreamDesc{p.tiles, p.out.pt});
   CH_TRY(dmalloc(d_str, st.size()));
   CH_CUDA(cudaMemcpy(*d_str, st.data(), st.size() * sizeof(StreamDesc), cudaMemcpyHostToDevice));
   *n_str = (uint32_t)st.size();
@@ -478,35 +525,58 @@ static int build_phases(ch_model *m, bool with_logits, Phase **d_out, uint32_t *
 // attention splits per kv head in the decode-step kernel: at most one CTA per
 // (kv head, split) and no more than its combine keeps in registers
 static uint32_t mk_attn_splits(const ch_model *m) {
-  return (uint32_t)std::min({m->mk_grid / (int)m->nkv, m->attn_splits, (int)kMkMaxSplits});
+  return (uint32_t)std::min({m->mk_grid / (int)m->nkv_l, m->attn_splits, (int)kMkMaxSplits});
 }
 
 // The decode step runs as one persistent kernel (decode_step.cu) when the shape
 // fits it; otherwise -- or with CH_DECODE_OPS=1, for A/B measurement -- as the
 // captured graph of per-op kernels.  Both are GPU paths with the same results.
+// A tensor-parallel shard always uses the persistent kernel (the per-op graph
+// has no exchange step).
 static int init_decode_step(ch_model *m) {
   m->mk_grid = std::min(num_sms(), 255);  // straddle lists hold CTA ids in 8 bits
+  const bool tp = m->world > 1;
   const char *env = getenv("CH_DECODE_OPS");
-  m->use_ops = env && env[0] == '1';
+  m->use_ops = !tp && env && env[0] == '1';
   const uint32_t ratio = m->nq / m->nkv;
   const uint32_t max_k = std::max({m->H, m->qd, m->I});
   m->mk_smem = mk_smem_bytes(max_k, m->H, ratio, mk_attn_splits(m), kSlots, (uint32_t)m->mk_grid);
   int co = 0;
   CH_CUDA(cudaDeviceGetAttribute(&co, cudaDevAttrCooperativeLaunch, m->ctx->device));
   const bool fits = co && m->H <= 4096 && m->D == 256 && (ratio == 1 || ratio == 2 || ratio == 4) &&
-                    (m->V + m->mk_grid - 1) / m->mk_grid <= 4096 && m->mk_smem <= 226 * 1024;
-  if (!fits) m->use_ops = true;
+                    (m->Vl + m->mk_grid - 1) / m->mk_grid <= 4096 && m->mk_smem <= 226 * 1024;
+  if (!fits) {
+    if (tp) return fail(CH_EINVAL, "tensor-parallel decode needs the persistent decode kernel; shape does not fit it");
+    m->use_ops = true;
+  }
   if (m->use_ops) return CH_OK;
   const size_t part = (size_t)m->mk_grid * mk_warps() * 2 * 16;
-  const uint32_t rows[5] = {m->qd + 2 * m->kvd, m->H, 2 * m->I, m->H, m->V};
+  const uint32_t rows[5] = {m->qd_l + 2 * m->kvd_l, m->H, 2 * m->I, m->H, m->Vl};
   for (int k = 0; k < 5; k++) {
     CH_TRY(dmalloc(&m->gdir[k], rows[k]));
     CH_TRY(dmalloc(&m->gpart[k], part));
   }
   CH_TRY(dmalloc(&m->mk_arrive, 1));
-  CH_TRY(dmalloc(&m->mk_epoch, 1));
+  CH_TRY(dmalloc(&m->mk_base, 1));
   CH_CUDA(cudaMemset(m->mk_arrive, 0, 8));
-  CH_CUDA(cudaMemset(m->mk_epoch, 0, 4));
+  CH_CUDA(cudaMemset(m->mk_base, 0, 8));
+  if (tp) {
+    // exchange arena: arrival counter, gathered o / down outputs, act and attention
+    // B fragments, every rank's top-64 -- same offsets on every rank
+    auto take = [&](size_t bytes) {
+      const size_t o = m->arena_bytes;
+      m->arena_bytes += (bytes + 255) & ~(size_t)255;
+      return o;
+    };
+    m->off_arrive = take(8);
+    m->off_o = take((size_t)m->H * 4);
+    m->off_down = take((size_t)m->H * 4);
+    m->off_act = take((size_t)m->I * 4);
+    m->off_attn = take((size_t)m->qd * 4);
+    m->off_cand = take((size_t)m->world * 64 * 8);
+    CH_TRY(dmalloc(&m->arena, m->arena_bytes));
+    CH_CUDA(cudaMemset(m->arena, 0, m->arena_bytes));
+  }
   CH_TRY(build_phases(m, true, &m->d_phases, &m->n_phases, &m->d_streams, &m->n_streams));
   CH_TRY(build_phases(m, false, &m->d_phases_nl, &m->n_phases_nl, &m->d_streams_nl, &m->n_streams_nl));
   return CH_OK;
@@ -519,13 +589,18 @@ static MegaArgs mega_args(ch_model *m, bool logits, bool device_loop) {
   a.streams = logits ? m->d_streams : m->d_streams_nl;
   a.nstreams = logits ? m->n_streams : m->n_streams_nl;
   a.grid = (uint32_t)m->mk_grid;
-  a.arrive = m->mk_arrive;
-  a.epoch = m->mk_epoch;
+  a.arrive = m->world > 1 ? reinterpret_cast<unsigned long long *>(m->arena + m->off_arrive) : m->mk_arrive;
+  a.base = m->mk_base;
   a.err = m->ctx->err;
   a.sp = m->sp;
   a.sp_rw = device_loop ? m->sp : nullptr;
-  a.nq = m->nq;
-  a.nkv = m->nkv;
+  a.nq = m->nq_l;
+  a.nkv = m->nkv_l;
+  a.world = m->world;
+  a.rank = m->rank;
+  a.attn_q0 = m->rank * m->nq_l;
+  for (uint32_t r = 0; r < m->world && r < kMaxWorld; r++) a.arena[r] = m->peer_arena[r];
+  a.xcand = m->arena ? reinterpret_cast<uint64_t *>(m->arena + m->off_cand) : nullptr;
   a.rot = m->cfg.rotary_dim;
   a.attn_max_splits = mk_attn_splits(m);
   a.cache_slots = kSlots;
@@ -772,14 +847,15 @@ extern "C" int ch_model_zero_state(ch_model *m) {
   if (!m) return fail(CH_EINVAL, "model is NULL");
   cudaStream_t s = m->ctx->stream;
   for (auto &l : m->layers) {
-    CH_CUDA(cudaMemsetAsync(l.kc, 0, (size_t)kSlots * m->kvd * 2, s));
-    CH_CUDA(cudaMemsetAsync(l.vc, 0, (size_t)kSlots * m->kvd * 2, s));
+    CH_CUDA(cudaMemsetAsync(l.kc, 0, (size_t)kSlots * m->kvd_l * 2, s));
+    CH_CUDA(cudaMemsetAsync(l.vc, 0, (size_t)kSlots * m->kvd_l * 2, s));
   }
   CH_CUDA(cudaMemsetAsync(m->X[0], 0, m->H * 4, s));
   CH_CUDA(cudaMemsetAsync(m->X[1], 0, m->H * 4, s));
   CH_CUDA(cudaMemsetAsync(m->normed, 0, m->H * 4, s));
   if (m->mk_arrive) CH_CUDA(cudaMemsetAsync(m->mk_arrive, 0, 8, s));
-  if (m->mk_epoch) CH_CUDA(cudaMemsetAsync(m->mk_epoch, 0, 4, s));
+  if (m->mk_base) CH_CUDA(cudaMemsetAsync(m->mk_base, 0, 8, s));
+  if (m->arena) CH_CUDA(cudaMemsetAsync(m->arena + m->off_arrive, 0, 8, s));
   CH_CUDA(cudaStreamSynchronize(s));
   return CH_OK;
 }
@@ -997,6 +1073,9 @@ extern "C" int ch_forward_token(ch_model *m, const float *x, uint32_t clock, uin
   m->h_sp->active = m->active;
   m->h_sp->sliding = m->sliding;
   m->h_sp->step = 0;
+  m->h_sp->next = 0;
+  m->h_sp->force = 0;
+  m->h_sp->pad = 0;
   if (n_active) memcpy(m->h_lists, active, n_active * 4);
   if (n_sliding) memcpy(m->h_lists + kSlots, sliding, n_sliding * 4);
   const uint32_t rh = m->cfg.rotary_dim / 2;
@@ -1057,6 +1136,8 @@ extern "C" int ch_decode_plan(ch_model *m, const ch_step_desc *steps, uint32_t n
     hp[i].sliding = m->plan_lists + off;
     off += steps[i].n_sliding;
     hp[i].step = i;
+    hp[i].next = 0;
+    hp[i].force = 0;
     hp[i].pad = 0;
   }
   if (n_steps) CH_CUDA(cudaMemcpy(m->plan, hp.data(), n_steps * sizeof(StepParams), cudaMemcpyHostToDevice));
@@ -1105,7 +1186,7 @@ extern "C" int ch_decode_run(ch_model *m, uint32_t first_token, uint32_t n_steps
   CH_CUDA(cudaStreamSynchronize(s));  // previous run may still read the staging words
   m->h_run[0] = 0;
   m->h_run[1] = first_token;
-  CH_CUDA(cudaMemcpyAsync(&m->sp->step, &m->h_run[0], 4, cudaMemcpyHostToDevice, s));
+  CH_CUDA(cudaMemcpyAsync(&m->sp->next, &m->h_run[0], 4, cudaMemcpyHostToDevice, s));
   CH_CUDA(cudaMemcpyAsync(m->token, &m->h_run[1], 4, cudaMemcpyHostToDevice, s));
   CH_TRY(launch_loop_steps(m, n_steps));
   m->loop_pos = n_steps;

@@ -84,7 +84,6 @@ __global__ void __launch_bounds__(kTkThreads) topk64_kernel(const TopkArgs a) {
       if (a.sp) {
         const uint32_t step = a.sp->step;
         if (a.token_hist && step < a.hist_cap) a.token_hist[step] = id;
-        a.sp->step = step + 1;
       }
     }
   }
@@ -115,13 +114,14 @@ __global__ void step_begin_kernel(const StepBeginArgs a) {
   grid_dep_wait();
   __shared__ StepParams cur;
   if (threadIdx.x == 0) {
-    uint32_t step = a.sp->step;
+    uint32_t step = a.sp->next;
     if (step >= a.n_plan) {  // replayed past the uploaded plan: keep the last entry, flag it
       atomicOr(a.err, DEV_ERR_BAD_LIST);
       step = a.n_plan - 1;
     }
     cur = a.plan[step];
     cur.step = step;
+    cur.next = step + 1;
   }
   __syncthreads();
   if (blockIdx.x == 0 && threadIdx.x == 0) *a.sp = cur;
@@ -134,7 +134,7 @@ __global__ void step_begin_kernel(const StepBeginArgs a) {
     sincos((double)ang, &sd, &cd);
     a.rope_cs[i] = make_float2((float)cd, (float)sd);
   }
-  const uint32_t tok = *a.token;
+  const uint32_t tok = cur.force ? cur.force - 1 : *a.token;  // a forced (prompt) token, or the fed-back one
   const uint16_t *row = a.embed + (size_t)tok * a.H;
   for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < a.H; i += gridDim.x * blockDim.x)
     a.x[i] = __fmul_rn(bf16_to_f32(row[i]), a.embed_scale);
