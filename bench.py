@@ -15,8 +15,12 @@ stream is 7.2 GB (> 126 MB L2), so no L2 flush is needed between steps.
   --impl reference : the reference CPU path = the oracle restatement (Zig cannot
           be built here), all host threads, one bounded sample per step.
 
-Multi-GPU (torchrun): replicas -- each rank decodes its own stream on its own GPU
-(weak scaling); row-sharded tensor parallel decode is not in this build yet.
+Multi-GPU (torchrun): row-sharded tensor parallel -- all ranks decode the same
+token stream, each with 1/N of the weights (q|k|v and KV by heads, o / down by
+output rows, gate|up by intermediate rows, LM head by vocab rows); the persistent
+decode kernel writes each phase's outputs straight into every rank's memory over
+NVLink and the ranks meet at one arrival counter per phase (strong scaling).
+The prefill runs token by token through the same kernel.
 """
 from __future__ import annotations
 
@@ -220,16 +224,23 @@ def ours(args):
     cfg = config_12b(layers=args.layers)
     ctx = GpuContext.init(local)
     t0 = time.time()
-    gm = GpuModelContext.synthetic(ctx, cfg, SEED)
+    if world > 1:  # row-sharded tensor parallel: one token stream over all GPUs
+        from channel_b200.engine import attach_tensor_parallel
+        gm = GpuModelContext.synthetic_sharded(ctx, cfg, SEED, rank, world)
+        attach_tensor_parallel(gm)
+    else:
+        gm = GpuModelContext.synthetic(ctx, cfg, SEED)
     build_s = time.time() - t0
     stream = torch.cuda.ExternalStream(ctx.stream)
 
-    rng = np.random.default_rng(SEED + rank)
+    rng = np.random.default_rng(SEED)  # the same prompt on every rank
     prompt = rng.integers(0, cfg.vocab_size, PROMPT).astype(np.uint32)
     n_total = args.warmup + args.steps
 
     def fresh_prefill():
         gm.zero_state()
+        if dist:
+            dist.barrier()  # every rank's arrival counter is reset before any rank launches
         ring = DynamicRingBuffer(cfg.num_hidden_layers, 0)
         ring.setNumAnchors(min(PROMPT, 512))  # stream_handler.zig:67
         prev = ring.getPrefillPrevSlots(0, 0, PROMPT)
@@ -283,7 +294,7 @@ def ours(args):
         ms = float(t.item())
         dist.barrier()
     ms_per_step = ms / args.steps
-    value = world * args.steps / (ms / 1000.0)
+    value = args.steps / (ms / 1000.0)  # one token stream, whatever the number of GPUs
 
     # ---- roofline: the dominant kernel is the persistent decode-step kernel (one launch
     # per token, >98% of the timed region; the tiny step_begin kernel is included)
@@ -293,19 +304,20 @@ def ours(args):
     step_bytes = (cfg.num_hidden_layers * ((cfg.q_dim + 2 * cfg.kv_dim) * H + H * cfg.q_dim + 3 * I * H) * 18 // 32
                   + cfg.vocab_size * H * 36 // 32)
     kv_bytes = cfg.num_hidden_layers * 2 * 2 * cfg.kv_dim * (PROMPT + args.warmup + args.steps / 2)
-    step_alg = step_bytes + kv_bytes
+    step_alg = (step_bytes + kv_bytes) / world  # this rank's shard of the weights and KV
     step_gbs = step_alg / (ms_per_step / 1000.0) / 1e9
     traffic = None
     tp = ROOT / "profiles" / "decode_step_traffic.json"
     if tp.exists():  # ncu DRAM bytes of one launch on a smaller case, scaled by algorithmic bytes
         t = json.loads(tp.read_text())
         traffic = t["dram_bytes"] * step_alg / t["algorithmic_bytes"]
-    rl = {"bound": "hbm", "kernel": "decode_step_kernel (one greedy token: 48 layers, Q8 LM head, top-64)",
+    rl = {"bound": "hbm", "kernel": "decode_step_kernel (one greedy token: 48 layers, Q8 LM head, top-64)"
+          + (f"; rank 0 of {world}, bytes = its shard" if world > 1 else ""),
           "achieved": step_gbs, "peak": peak, "unit": "GB/s", "frac": step_gbs / peak, "traffic": traffic,
           "bytes_per_launch": step_alg, "us_per_launch": ms_per_step * 1000, "launches_timed": args.steps,
           "peak_kind": peak_kind + " hbm_gbs (copy bandwidth); kernel timed inside the device loop"}
     # the Q4 GEMV on its own (metric's second part): fused gate/up, op-level kernel, rotating layers
-    gemv_rl = gateup_roofline(ctx, gm, cfg, stream, reps=3)
+    gemv_rl = gateup_roofline(ctx, gm, cfg, stream, reps=3) if world == 1 else None
 
     # ---- e2e: reference-facing call with host buffers ---------------------------------
     e2e = None
@@ -349,7 +361,7 @@ def ours(args):
             t = torch.tensor([e_ms], device="cuda")
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
             e_ms = float(t.item())
-        e2e = {"value": world * args.steps / (e_ms / 1000.0), "unit": "tok/s",
+        e2e = {"value": args.steps / (e_ms / 1000.0), "unit": "tok/s",
                "h2d_bytes_per_step": h2d // args.steps, "d2h_bytes_per_step": d2h // args.steps,
                "ms_per_step": e_ms / args.steps,
                "tokens_match_device_loop": bool(list(e_tokens) == [int(t) for t in tokens])}
@@ -364,12 +376,12 @@ def ours(args):
         line = {
             "metric": "decode tok/s (12B-shape Q4) at 1/2/4/8 GPU; Q4 GEMV HBM GB/s vs peak",
             "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": "q4/f16-mma/f32-acc", "data": "synthetic",
             "config": {"workload": "config4: 12B-shape Q4 greedy decode ({} layers, H 3840, I 15360, 16q/8kv heads, "
                                    "D 256, V 262144 Q8 head) after a 512-token prefill, seed 3".format(cfg.num_hidden_layers),
-                       "global_batch": world, "seq_len": PROMPT + n_total,
-                       "parallelism": "replicas" if world > 1 else "single",
+                       "global_batch": 1, "seq_len": PROMPT + n_total,
+                       "parallelism": f"tp{world} (row-sharded, in-kernel NVLink exchange)" if world > 1 else "single",
                        "l2": "per-step weight stream 7.2 GB > 126 MB L2 (no flush needed)"},
             "roofline": rl,
             "gemv_roofline": gemv_rl,
@@ -381,6 +393,8 @@ def ours(args):
             "tokens_head": [int(t) for t in tokens[:8]],
         }
         print(json.dumps(line), flush=True)
+    if dist:
+        dist.barrier()  # no rank frees its arena while another may still run a kernel on it
     gm.deinit()
     ctx.deinit()
     if dist:

@@ -13,6 +13,7 @@ u8, u16, u32, u64, f32 = C.c_uint8, C.c_uint16, C.c_uint32, C.c_uint64, C.c_floa
 vp, sz, i32 = C.c_void_p, C.c_size_t, C.c_int
 P = C.POINTER
 
+CH_IPC_HANDLE_BYTES = 64
 CH_OK, CH_EINVAL, CH_ENOMEM, CH_ECUDA, CH_ETIMEOUT, CH_EBATCH, CH_ESTATE, CH_EDEVICE, CH_ECOMM = 0, -1, -2, -3, -4, -5, -6, -7, -8
 STATUS_NAMES = {0: "CH_OK", -1: "CH_EINVAL", -2: "CH_ENOMEM", -3: "CH_ECUDA", -4: "CH_ETIMEOUT", -5: "CH_EBATCH",
                 -6: "CH_ESTATE", -7: "CH_EDEVICE", -8: "CH_ECOMM"}
@@ -58,6 +59,9 @@ SIGNATURES = {
     "ch_ctx_device_status": (i32, [vp, P(u32)]),
     "ch_model_create": (i32, [vp, P(ChModelConfig), P(ChLayerWeights), P(u32), P(f32), P(u16), P(vp)]),
     "ch_model_create_synthetic": (i32, [vp, P(ChModelConfig), u64, P(vp)]),
+    "ch_model_create_synthetic_sharded": (i32, [vp, P(ChModelConfig), u64, u32, u32, P(vp)]),
+    "ch_model_exchange_handle": (i32, [vp, vp]),
+    "ch_model_attach_peers": (i32, [vp, vp]),
     "ch_model_destroy": (None, [vp]),
     "ch_model_zero_state": (i32, [vp]),
     "ch_model_weight_tiles": (i32, [vp, u32, i32, P(vp), P(u32), P(u32)]),

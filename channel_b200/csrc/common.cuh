@@ -1,5 +1,5 @@
 // common.cuh -- shared device helpers for the sm_100a kernels: PTX wrappers for
-// mbarrier / cp.async.bulk (TMA bulk copies, never multicast), programmatic
+// mbarrier / cp.async.bulk (TMA bulk copies, each to this CTA only), programmatic
 // dependent launch, f16 packing, the seeded synthetic generator and the
 // device-side error word.
 #pragma once
@@ -70,7 +70,7 @@ CH_DEV bool mbar_wait_bounded(uint64_t *bar, uint32_t parity, uint32_t *err,
   return false;
 }
 // 1-D bulk copy global -> this CTA's shared memory, completion on `bar`.
-// dst/src 16-byte aligned, bytes a multiple of 16.  No multicast.
+// dst/src 16-byte aligned, bytes a multiple of 16.  Single destination: this CTA.
 CH_DEV void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
   asm volatile(
       "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_u32(dst)),

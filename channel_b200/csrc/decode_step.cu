@@ -161,16 +161,24 @@ CH_DEV void patch_staged(const GemvOut &o, const uint32_t *slist, const uint32_t
 // Grid barrier on a monotonically increasing arrival counter, in two halves so a
 // CTA can do work that does not depend on the other CTAs between its arrival
 // and its wait.  The wait is bounded.
-CH_DEV void grid_arrive(const MegaArgs &a) {
+// Arrival at the barrier after a phase.  Every CTA releases its writes at GPU
+// scope (its stores to other GPUs' memory included) and arrives on this GPU's
+// counter; for a cross-rank barrier the last local arrival, which has acquired
+// all of them through that counter, releases at system scope with one signal per
+// rank -- a single system-scope release per rank and phase.
+CH_DEV void grid_arrive(const MegaArgs &a, bool cross, unsigned long long local_target) {
   __syncthreads();
   if (threadIdx.x == 0) {
-    if (a.world > 1) {  // every CTA of every rank arrives on every rank's counter
-      __threadfence_system();
-      for (uint32_t r = 0; r < a.world; r++)
-        asm volatile("red.relaxed.sys.global.add.u64 [%0], 1;" ::"l"(on_rank(a, a.arrive, r)) : "memory");
-    } else {
-      __threadfence();
+    if (!cross) {
+      asm volatile("fence.acq_rel.gpu;" ::: "memory");
       asm volatile("red.relaxed.gpu.global.add.u64 [%0], 1;" ::"l"(a.arrive) : "memory");
+    } else {
+      asm volatile("fence.acq_rel.gpu;" ::: "memory");
+      unsigned long long old;
+      asm volatile("atom.acq_rel.gpu.global.add.u64 %0, [%1], 1;" : "=l"(old) : "l"(a.arrive) : "memory");
+      if (old + 1 == local_target)  // this GPU is done: one signal per rank
+        for (uint32_t r = 0; r < a.world; r++)
+          asm volatile("red.release.sys.global.add.u64 [%0], 1;" ::"l"(on_rank(a, a.garrive, r)) : "memory");
     }
   }
 }
@@ -182,15 +190,19 @@ CH_DEV unsigned long long load_acquire_u64(const unsigned long long *p, bool sys
     asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
   return v;
 }
-CH_DEV void grid_wait(const MegaArgs &a, unsigned long long target) {
-  if (threadIdx.x == 0) {
-    const bool sys = a.world > 1;
-    if (load_acquire_u64(a.arrive, sys) < target) {
+// `abort` (shared): set once a wait of this launch gave up, or when the launch
+// started with a peer timeout already recorded -- later waits then return at
+// once, so a lost rank costs one bounded wait, not one per phase.
+CH_DEV void grid_wait(const unsigned long long *ctr, bool sys, unsigned long long target, uint32_t *err,
+                      volatile uint32_t *abort) {
+  if (threadIdx.x == 0 && !*abort) {
+    if (load_acquire_u64(ctr, sys) < target) {
       const uint64_t t0 = globaltimer_ns();
       for (;;) {
-        if (load_acquire_u64(a.arrive, sys) >= target) break;
+        if (load_acquire_u64(ctr, sys) >= target) break;
         if (globaltimer_ns() - t0 > 2000000000ull) {
-          atomicOr(a.err, DEV_ERR_PEER_TIMEOUT);
+          atomicOr(err, DEV_ERR_PEER_TIMEOUT);
+          *abort = 1u;
           break;
         }
       }
@@ -922,7 +934,7 @@ CH_DEV void attn_phase(const Phase &p, const MegaArgs &a, const StepParams &sp, 
     atomicAdd(&a.attn_counters[kvh], 1u);
     uint32_t v;
     asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(&a.attn_counters[kvh]) : "memory");
-    if (v < nsplit) {
+    if (v < nsplit && !(*(volatile uint32_t *)a.err & DEV_ERR_PEER_TIMEOUT)) {
       const uint64_t t0 = globaltimer_ns();
       for (;;) {
         asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(&a.attn_counters[kvh]) : "memory");
@@ -1161,6 +1173,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(const MegaAr
   __shared__ float red[32];
   __shared__ Phase ph_s[3];  // phases pi, pi+1 and pi+2 (copied ahead with cp.async)
   __shared__ StepParams sp_s;
+  __shared__ uint32_t s_abort;
 
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const uint32_t gw = blockIdx.x * MK_NW + warp;
@@ -1179,6 +1192,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(const MegaAr
   if (threadIdx.x == 0) {
     *L.xzero = make_uint4(0u, 0u, 0u, 0u);
     sp_s = *a.sp;
+    s_abort = (*(volatile uint32_t *)a.err & DEV_ERR_PEER_TIMEOUT) ? 1u : 0u;
   }
   for (uint32_t i = 0; i < 2 && i < a.nphases; i++) copy_phase(a.phases + i, &ph_s[i]);
   cp_async_wait_all();
@@ -1186,7 +1200,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(const MegaAr
   attn_lists_init(a, sp_s, L.wphys);
   pre_phase<R>(ph_s[0], a, sp_s, L);
 
-  const unsigned long long base = *a.base;  // arrivals before this launch
+  const unsigned long long base = a.base[0], gbase = a.base[1];  // arrivals before this launch
   uint32_t cidx = 0, vpar = 0;
   bool ok = true;
   for (uint32_t pi = 0; pi < a.nphases; pi++) {
@@ -1221,10 +1235,15 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(const MegaAr
 #endif
     PHASE_MARK(pi, 4);
     if (pi + 1 < a.nphases) {
-      grid_arrive(a);
+      const bool cross = p.cross != 0;
+      const unsigned long long ltarget = base + (unsigned long long)(pi + 1) * gridDim.x;
+      grid_arrive(a, cross, ltarget);
       pre_phase<R>(ph_s[(pi + 1) % 3], a, sp_s, L);
       PHASE_MARK(pi, 5);
-      grid_wait(a, base + (unsigned long long)(pi + 1) * gridDim.x * a.world);
+      if (cross)
+        grid_wait(a.garrive, true, gbase + (unsigned long long)p.gidx * a.world, a.err, &s_abort);
+      else
+        grid_wait(a.arrive, false, ltarget, a.err, &s_abort);
       PHASE_MARK(pi, 6);
     }
   }
@@ -1235,8 +1254,10 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(const MegaAr
       mbar_wait_bounded(&my_bars[j % MK_SPW], (j / MK_SPW) & 1, nullptr, 100000000ull);
   }
   // every CTA has passed the last barrier, so all have read `base`: advance it for the next launch
-  if (blockIdx.x == 0 && threadIdx.x == 0)
-    *a.base = base + (unsigned long long)(a.nphases - 1) * gridDim.x * a.world;
+  if (blockIdx.x == 0 && threadIdx.x == 0) {
+    a.base[0] = base + (unsigned long long)(a.nphases - 1) * gridDim.x;
+    a.base[1] = gbase + (unsigned long long)a.ncross * a.world;
+  }
 }
 
 size_t mk_smem_bytes(uint32_t max_k, uint32_t hidden, uint32_t ratio, uint32_t max_splits, uint32_t cache_slots,

@@ -44,6 +44,9 @@ struct GemvOut {
 
 struct alignas(16) Phase {
   uint32_t kind, fmt, pm, is_sliding;
+  // barrier after this phase: cross = 1 when other ranks read its outputs (tensor
+  // parallel); gidx = number of cross-rank barriers up to and including this one
+  uint32_t cross, gidx;
   // GEMV
   const uint8_t *tiles;
   uint32_t row_tiles, k_tiles, K, vocab, vocab0;
@@ -72,8 +75,10 @@ struct MegaArgs {
   const StreamDesc *streams;
   uint32_t nstreams;
   uint32_t nphases, grid;
-  unsigned long long *arrive;  // grid-barrier arrivals (monotonic across launches)
-  unsigned long long *base;    // arrivals at the start of this launch (advanced by the launch)
+  unsigned long long *arrive;  // this GPU's grid-barrier arrivals (monotonic across launches)
+  unsigned long long *base;    // [2] arrivals (local, cross-rank) before this launch (advanced by the launch)
+  unsigned long long *garrive; // tensor parallel: rank arrivals of cross-rank barriers (in the arena)
+  uint32_t ncross;             // cross-rank barriers per launch
   uint32_t *err;
   const StepParams *sp;
   StepParams *sp_rw;  // device loop: the top-k phase records the token at history slot sp->step (else null)

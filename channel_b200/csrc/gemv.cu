@@ -437,15 +437,17 @@ cudaError_t launch_repack_q8(const uint32_t *src, uint32_t rows, uint32_t cols, 
 
 // ---------------------------------------------------------------------------
 // seeded synthetic tensors (same spec as the oracle's or_gen_*)
-__global__ void gen_q4_kernel(uint32_t *dst, uint64_t nblocks, uint64_t tseed, float scale_std) {
-  for (uint64_t blk = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; blk < nblocks;
-       blk += (uint64_t)gridDim.x * blockDim.x) {
+// blocks [blk0, blk0 + nblocks) of a tensor's block stream (a row range of the matrix)
+__global__ void gen_q4_kernel(uint32_t *dst, uint64_t blk0, uint64_t nblocks, uint64_t tseed, float scale_std) {
+  for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < nblocks;
+       i += (uint64_t)gridDim.x * blockDim.x) {
+    const uint64_t blk = blk0 + i;
     uint64_t ha = hash3(tseed, 0, blk * 2), hb = hash3(tseed, 0, blk * 2 + 1);
     float z = gen_normal(tseed, 1, blk);
     float d = __fmul_rn(fabsf(z), scale_std);
     __half d16 = __float2half_rn(d);
     __half m16 = __float2half_rn(__fmul_rn(-8.0f, __half2float(d16)));
-    uint32_t *o = dst + blk * 5;
+    uint32_t *o = dst + i * 5;
     o[0] = (uint32_t)__half_as_ushort(d16) | ((uint32_t)__half_as_ushort(m16) << 16);
     o[1] = (uint32_t)ha;
     o[2] = (uint32_t)(ha >> 32);
@@ -514,8 +516,12 @@ __global__ void quantize_q4_kernel(const uint16_t *src, uint64_t nblocks, uint32
 
 cudaError_t launch_gen_q4_blocks(uint32_t *dst, uint32_t rows, uint32_t cols, uint64_t tseed, float scale_std,
                                  cudaStream_t s) {
-  uint64_t nb = (uint64_t)rows * (cols / 32);
-  gen_q4_kernel<<<grid_for(nb, 256), 256, 0, s>>>(dst, nb, tseed, scale_std);
+  return launch_gen_q4_rows(dst, 0, rows, cols, tseed, scale_std, s);
+}
+cudaError_t launch_gen_q4_rows(uint32_t *dst, uint32_t row0, uint32_t rows, uint32_t cols, uint64_t tseed,
+                               float scale_std, cudaStream_t s) {
+  const uint64_t nb = (uint64_t)rows * (cols / 32), b0 = (uint64_t)row0 * (cols / 32);
+  gen_q4_kernel<<<grid_for(nb, 256), 256, 0, s>>>(dst, b0, nb, tseed, scale_std);
   return cudaGetLastError();
 }
 cudaError_t launch_gen_bf16(uint16_t *dst, size_t n, uint64_t tseed, float mean, float std, cudaStream_t s) {

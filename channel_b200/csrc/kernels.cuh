@@ -60,6 +60,9 @@ cudaError_t launch_repack_q4(const uint32_t *src_blocks, const uint32_t *src_blo
 cudaError_t launch_repack_q8(const uint32_t *src_blocks, uint32_t rows, uint32_t cols, uint8_t *dst, cudaStream_t s);
 cudaError_t launch_gen_q4_blocks(uint32_t *dst, uint32_t rows, uint32_t cols, uint64_t tseed, float scale_std,
                                  cudaStream_t s);
+// rows [row0, row0 + rows) of the same generated matrix (a tensor-parallel shard)
+cudaError_t launch_gen_q4_rows(uint32_t *dst, uint32_t row0, uint32_t rows, uint32_t cols, uint64_t tseed,
+                               float scale_std, cudaStream_t s);
 cudaError_t launch_gen_bf16(uint16_t *dst, size_t n, uint64_t tseed, float mean, float std, cudaStream_t s);
 cudaError_t launch_gen_f32(float *dst, size_t n, uint64_t tseed, float mean, float std, cudaStream_t s);
 cudaError_t launch_bf16_to_f32(const uint16_t *src, float *dst, size_t n, cudaStream_t s);

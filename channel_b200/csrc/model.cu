@@ -206,7 +206,8 @@ struct ch_model {
   float *gdir[5] = {nullptr, nullptr, nullptr, nullptr, nullptr};
   float *gpart[5] = {nullptr, nullptr, nullptr, nullptr, nullptr};
   unsigned long long *mk_arrive = nullptr;
-  unsigned long long *mk_base = nullptr;  // barrier arrivals before the next launch
+  unsigned long long *mk_base = nullptr;  // [2] barrier arrivals (local, cross-rank) before the next launch
+  uint32_t n_cross = 0, n_cross_nl = 0;    // cross-rank barriers per launch (logits / no-logits tables)
   size_t mk_smem = 0;
   int mk_grid = 0;
   bool use_ops = false;  // kernel-per-op decode (CH_DECODE_OPS=1), kept for A/B measurement
@@ -391,7 +392,7 @@ static int alloc_model_buffers(ch_model *m) {
 enum GemvKind { GK_QKV = 0, GK_O = 1, GK_GU = 2, GK_DOWN = 3, GK_LM = 4 };
 
 static int build_phases(ch_model *m, bool with_logits, Phase **d_out, uint32_t *n_out, StreamDesc **d_str,
-                        uint32_t *n_str) {
+                        uint32_t *n_str, uint32_t *n_cross) {
   const uint32_t G = (uint32_t)m->mk_grid, GW = G * mk_warps();
   const bool tp = m->world > 1;
   // local output rows of each GEMV, its k tiles, and whether its outputs are gathered
@@ -510,6 +511,17 @@ static int build_phases(ch_model *m, bool with_logits, Phase **d_out, uint32_t *
       ph.push_back(mg);
     }
   }
+  // barriers other ranks take part in: after a phase whose outputs go to every rank
+  // (attention, o, gate|up, down, top-64); the others stay on this GPU
+  uint32_t ncross = 0;
+  for (size_t i = 0; i + 1 < ph.size(); i++) {
+    Phase &p = ph[i];
+    const bool pushes = (p.kind == PH_GEMV && p.out.push) || p.kind == PH_ATTN || p.kind == PH_TOPK;
+    p.cross = tp && pushes ? 1u : 0u;
+    if (p.cross) ncross++;
+    p.gidx = ncross;
+  }
+  *n_cross = ncross;
   CH_TRY(dmalloc(d_out, ph.size()));
   CH_CUDA(cudaMemcpy(*d_out, ph.data(), ph.size() * sizeof(Phase), cudaMemcpyHostToDevice));
   *n_out = (uint32_t)ph.size();
@@ -557,9 +569,9 @@ static int init_decode_step(ch_model *m) {
     CH_TRY(dmalloc(&m->gpart[k], part));
   }
   CH_TRY(dmalloc(&m->mk_arrive, 1));
-  CH_TRY(dmalloc(&m->mk_base, 1));
+  CH_TRY(dmalloc(&m->mk_base, 2));
   CH_CUDA(cudaMemset(m->mk_arrive, 0, 8));
-  CH_CUDA(cudaMemset(m->mk_base, 0, 8));
+  CH_CUDA(cudaMemset(m->mk_base, 0, 16));
   if (tp) {
     // exchange arena: arrival counter, gathered o / down outputs, act and attention
     // B fragments, every rank's top-64 -- same offsets on every rank
@@ -577,8 +589,9 @@ static int init_decode_step(ch_model *m) {
     CH_TRY(dmalloc(&m->arena, m->arena_bytes));
     CH_CUDA(cudaMemset(m->arena, 0, m->arena_bytes));
   }
-  CH_TRY(build_phases(m, true, &m->d_phases, &m->n_phases, &m->d_streams, &m->n_streams));
-  CH_TRY(build_phases(m, false, &m->d_phases_nl, &m->n_phases_nl, &m->d_streams_nl, &m->n_streams_nl));
+  CH_TRY(build_phases(m, true, &m->d_phases, &m->n_phases, &m->d_streams, &m->n_streams, &m->n_cross));
+  CH_TRY(build_phases(m, false, &m->d_phases_nl, &m->n_phases_nl, &m->d_streams_nl, &m->n_streams_nl,
+                      &m->n_cross_nl));
   return CH_OK;
 }
 
@@ -589,8 +602,10 @@ static MegaArgs mega_args(ch_model *m, bool logits, bool device_loop) {
   a.streams = logits ? m->d_streams : m->d_streams_nl;
   a.nstreams = logits ? m->n_streams : m->n_streams_nl;
   a.grid = (uint32_t)m->mk_grid;
-  a.arrive = m->world > 1 ? reinterpret_cast<unsigned long long *>(m->arena + m->off_arrive) : m->mk_arrive;
+  a.arrive = m->mk_arrive;
   a.base = m->mk_base;
+  a.garrive = m->arena ? reinterpret_cast<unsigned long long *>(m->arena + m->off_arrive) : nullptr;
+  a.ncross = logits ? m->n_cross : m->n_cross_nl;
   a.err = m->ctx->err;
   a.sp = m->sp;
   a.sp_rw = device_loop ? m->sp : nullptr;
@@ -746,13 +761,23 @@ static int gen_norm(ch_model *m, float **dst, uint32_t n, uint64_t tseed, uint16
   return CH_OK;
 }
 
-extern "C" int ch_model_create_synthetic(ch_ctx *ctx, const ch_model_config *cfg, uint64_t seed, ch_model **out) {
+// Synthetic weights of shard `rank` of `world`: every tensor is generated as rows
+// [row0, row0 + rows) of the whole-model tensor, so the shards of a tensor-parallel
+// model are exactly the rows of ch_model_create_synthetic's weights.
+static int create_synthetic(ch_ctx *ctx, const ch_model_config *cfg, uint64_t seed, uint32_t rank, uint32_t world,
+                            ch_model **out) {
   if (!ctx || !out) return fail(CH_EINVAL, "NULL argument");
   CH_TRY(check_cfg(cfg));
+  if (world == 0 || world > kMaxWorld || rank >= world) return fail(CH_EINVAL, "rank must be < world <= 8");
+  if (world > 1 && (cfg->num_key_value_heads % world || cfg->hidden_size % (16 * world) ||
+                    cfg->intermediate_size % (16 * world) || cfg->vocab_size % (16 * world)))
+    return fail(CH_EINVAL, "tensor parallel: kv heads, hidden/16, intermediate/16 and vocab/16 must divide by world");
   CH_CUDA(cudaSetDevice(ctx->device));
   ch_model *m = new ch_model();
   m->ctx = ctx;
   m->cfg = *cfg;
+  m->rank = rank;
+  m->world = world;
   int r = alloc_model_buffers(m);
   if (r != CH_OK) {
     free_model(m);
@@ -773,20 +798,24 @@ extern "C" int ch_model_create_synthetic(ch_ctx *ctx, const ch_model_config *cfg
   if (dmalloc(&tA, max_words) != CH_OK || dmalloc(&tB, max_words) != CH_OK || dmalloc(&tn, std::max(m->H, m->D)) != CH_OK)
     return bail(CH_ENOMEM);
   const float wstd = 0.02f;
-  const size_t qw = (size_t)m->qd * (m->H / 32) * 5, kw = (size_t)m->kvd * (m->H / 32) * 5;
+  const size_t qw = (size_t)m->qd_l * (m->H / 32) * 5, kw = (size_t)m->kvd_l * (m->H / 32) * 5;
+  const uint32_t rk = m->rank;
   for (uint32_t l = 0; l < m->L; l++) {
     DevLayer &dl = m->layers[l];
-    bool ok = launch_gen_q4_blocks(tA, m->qd, m->H, ch_tensor_seed(seed, l, T_Q), wstd, s) == cudaSuccess &&
-              launch_gen_q4_blocks(tA + qw, m->kvd, m->H, ch_tensor_seed(seed, l, T_K), wstd, s) == cudaSuccess &&
-              launch_gen_q4_blocks(tA + qw + kw, m->kvd, m->H, ch_tensor_seed(seed, l, T_V), wstd, s) == cudaSuccess &&
-              launch_repack_q4(tA, nullptr, m->qd + 2 * m->kvd, m->H, MAP_PLAIN, dl.qkv, s) == cudaSuccess &&
-              launch_gen_q4_blocks(tB, m->H, m->qd, ch_tensor_seed(seed, l, T_O), wstd, s) == cudaSuccess &&
-              launch_repack_q4(tB, nullptr, m->H, m->qd, MAP_PLAIN, dl.o, s) == cudaSuccess &&
-              launch_gen_q4_blocks(tA, m->I, m->H, ch_tensor_seed(seed, l, T_GATE), wstd, s) == cudaSuccess &&
-              launch_gen_q4_blocks(tB, m->I, m->H, ch_tensor_seed(seed, l, T_UP), wstd, s) == cudaSuccess &&
-              launch_repack_q4(tA, tB, 2 * m->I, m->H, MAP_GATEUP, dl.gateup, s) == cudaSuccess &&
-              launch_gen_q4_blocks(tA, m->H, m->I, ch_tensor_seed(seed, l, T_DOWN), wstd, s) == cudaSuccess &&
-              launch_repack_q4(tA, nullptr, m->H, m->I, MAP_PLAIN, dl.down, s) == cudaSuccess;
+    // q | k | v rows of this rank's heads, o / down rows, gate / up rows
+    bool ok =
+        launch_gen_q4_rows(tA, rk * m->qd_l, m->qd_l, m->H, ch_tensor_seed(seed, l, T_Q), wstd, s) == cudaSuccess &&
+        launch_gen_q4_rows(tA + qw, rk * m->kvd_l, m->kvd_l, m->H, ch_tensor_seed(seed, l, T_K), wstd, s) == cudaSuccess &&
+        launch_gen_q4_rows(tA + qw + kw, rk * m->kvd_l, m->kvd_l, m->H, ch_tensor_seed(seed, l, T_V), wstd, s) ==
+            cudaSuccess &&
+        launch_repack_q4(tA, nullptr, m->qd_l + 2 * m->kvd_l, m->H, MAP_PLAIN, dl.qkv, s) == cudaSuccess &&
+        launch_gen_q4_rows(tB, rk * m->Ho, m->Ho, m->qd, ch_tensor_seed(seed, l, T_O), wstd, s) == cudaSuccess &&
+        launch_repack_q4(tB, nullptr, m->Ho, m->qd, MAP_PLAIN, dl.o, s) == cudaSuccess &&
+        launch_gen_q4_rows(tA, rk * m->Il, m->Il, m->H, ch_tensor_seed(seed, l, T_GATE), wstd, s) == cudaSuccess &&
+        launch_gen_q4_rows(tB, rk * m->Il, m->Il, m->H, ch_tensor_seed(seed, l, T_UP), wstd, s) == cudaSuccess &&
+        launch_repack_q4(tA, tB, 2 * m->Il, m->H, MAP_GATEUP, dl.gateup, s) == cudaSuccess &&
+        launch_gen_q4_rows(tA, rk * m->Ho, m->Ho, m->I, ch_tensor_seed(seed, l, T_DOWN), wstd, s) == cudaSuccess &&
+        launch_repack_q4(tA, nullptr, m->Ho, m->I, MAP_PLAIN, dl.down, s) == cudaSuccess;
     if (!ok) return bail(fail(CH_ECUDA, "synthetic layer generation"));
     if (gen_norm(m, &dl.input_norm, m->H, ch_tensor_seed(seed, l, T_IN_NORM), tn) ||
         gen_norm(m, &dl.q_norm, m->D, ch_tensor_seed(seed, l, T_Q_NORM), tn) ||
@@ -809,9 +838,9 @@ extern "C" int ch_model_create_synthetic(ch_ctx *ctx, const ch_model_config *cfg
     const uint32_t chunk_rows = 16384;
     uint32_t *tq = nullptr;
     if (dmalloc(&tq, (size_t)chunk_rows * (m->H / 32) * 9) != CH_OK) return bail(CH_ENOMEM);
-    for (uint32_t r0 = 0; r0 < m->V; r0 += chunk_rows) {
-      uint32_t nr = std::min(chunk_rows, m->V - r0);
-      launch_quantize_q8_rows(m->embed + (size_t)r0 * m->H, nr, m->H, tq, s);
+    for (uint32_t r0 = 0; r0 < m->Vl; r0 += chunk_rows) {  // this rank's vocab rows of the tied embedding
+      uint32_t nr = std::min(chunk_rows, m->Vl - r0);
+      launch_quantize_q8_rows(m->embed + (size_t)(rk * m->Vl + r0) * m->H, nr, m->H, tq, s);
       launch_repack_q8(tq, nr, m->H, m->lm + q8_tile_bytes(r0, m->H), s);
     }
     cudaStreamSynchronize(s);
@@ -826,6 +855,50 @@ extern "C" int ch_model_create_synthetic(ch_ctx *ctx, const ch_model_config *cfg
   return CH_OK;
 }
 
+extern "C" int ch_model_create_synthetic(ch_ctx *ctx, const ch_model_config *cfg, uint64_t seed, ch_model **out) {
+  return create_synthetic(ctx, cfg, seed, 0, 1, out);
+}
+extern "C" int ch_model_create_synthetic_sharded(ch_ctx *ctx, const ch_model_config *cfg, uint64_t seed, uint32_t rank,
+                                                 uint32_t world, ch_model **out) {
+  return create_synthetic(ctx, cfg, seed, rank, world, out);
+}
+
+// ---------------------------------------------------------------------------
+// tensor parallel: the exchange arena is shared between the ranks' processes
+// with CUDA IPC; every rank maps every other rank's arena.
+extern "C" int ch_model_exchange_handle(ch_model *m, void *handle) {
+  if (!m || !handle) return fail(CH_EINVAL, "NULL argument");
+  if (m->world <= 1 || !m->arena) return fail(CH_ESTATE, "not a tensor-parallel model");
+  CH_CUDA(cudaSetDevice(m->ctx->device));
+  cudaIpcMemHandle_t h;
+  CH_CUDA(cudaIpcGetMemHandle(&h, m->arena));
+  static_assert(sizeof(cudaIpcMemHandle_t) == CH_IPC_HANDLE_BYTES, "IPC handle size");
+  memcpy(handle, &h, sizeof(h));
+  return CH_OK;
+}
+extern "C" int ch_model_attach_peers(ch_model *m, const void *handles) {
+  if (!m || !handles) return fail(CH_EINVAL, "NULL argument");
+  if (m->world <= 1 || !m->arena) return fail(CH_ESTATE, "not a tensor-parallel model");
+  if (m->peers_ready) return fail(CH_ESTATE, "peers already attached");
+  CH_CUDA(cudaSetDevice(m->ctx->device));
+  const uint8_t *hb = static_cast<const uint8_t *>(handles);
+  for (uint32_t r = 0; r < m->world; r++) {
+    if (r == m->rank) {
+      m->peer_arena[r] = m->arena;
+      continue;
+    }
+    cudaIpcMemHandle_t h;
+    memcpy(&h, hb + (size_t)r * sizeof(h), sizeof(h));
+    void *p = nullptr;
+    cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess)
+      return fail(CH_ECOMM, "cudaIpcOpenMemHandle(rank " + std::to_string(r) + "): " + cudaGetErrorString(e));
+    m->peer_arena[r] = static_cast<uint8_t *>(p);
+  }
+  m->peers_ready = true;
+  return CH_OK;
+}
+
 extern "C" void ch_model_destroy(ch_model *m) { free_model(m); }
 
 extern "C" int ch_model_weight_tiles(ch_model *m, uint32_t layer, int which, void **tiles, uint32_t *rows,
@@ -833,11 +906,11 @@ extern "C" int ch_model_weight_tiles(ch_model *m, uint32_t layer, int which, voi
   if (!m || !tiles || !rows || !cols || layer >= m->L) return fail(CH_EINVAL, "bad argument");
   const DevLayer &l = m->layers[layer];
   switch (which) {
-    case 0: *tiles = l.qkv, *rows = m->qd + 2 * m->kvd, *cols = m->H; break;
-    case 1: *tiles = l.o, *rows = m->H, *cols = m->qd; break;
-    case 2: *tiles = l.gateup, *rows = 2 * m->I, *cols = m->H; break;
-    case 3: *tiles = l.down, *rows = m->H, *cols = m->I; break;
-    case 4: *tiles = m->lm, *rows = m->V, *cols = m->H; break;
+    case 0: *tiles = l.qkv, *rows = m->qd_l + 2 * m->kvd_l, *cols = m->H; break;  // this rank's shard
+    case 1: *tiles = l.o, *rows = m->Ho, *cols = m->qd; break;
+    case 2: *tiles = l.gateup, *rows = 2 * m->Il, *cols = m->H; break;
+    case 3: *tiles = l.down, *rows = m->Ho, *cols = m->I; break;
+    case 4: *tiles = m->lm, *rows = m->Vl, *cols = m->H; break;
     default: return fail(CH_EINVAL, "which must be 0..4");
   }
   return CH_OK;
@@ -854,7 +927,7 @@ extern "C" int ch_model_zero_state(ch_model *m) {
   CH_CUDA(cudaMemsetAsync(m->X[1], 0, m->H * 4, s));
   CH_CUDA(cudaMemsetAsync(m->normed, 0, m->H * 4, s));
   if (m->mk_arrive) CH_CUDA(cudaMemsetAsync(m->mk_arrive, 0, 8, s));
-  if (m->mk_base) CH_CUDA(cudaMemsetAsync(m->mk_base, 0, 8, s));
+  if (m->mk_base) CH_CUDA(cudaMemsetAsync(m->mk_base, 0, 16, s));
   if (m->arena) CH_CUDA(cudaMemsetAsync(m->arena + m->off_arrive, 0, 8, s));
   CH_CUDA(cudaStreamSynchronize(s));
   return CH_OK;
@@ -1060,6 +1133,7 @@ extern "C" int ch_forward_token(ch_model *m, const float *x, uint32_t clock, uin
   if (slot >= kSlots) return fail(CH_EINVAL, "slot >= 4096");
   CH_TRY(check_lists(active, n_active));
   CH_TRY(check_lists(sliding, n_sliding));
+  if (m->world > 1 && !m->peers_ready) return fail(CH_ESTATE, "tensor parallel: ch_model_attach_peers first");
   CH_CUDA(cudaSetDevice(m->ctx->device));
   const bool logits = topk_out || token_out;
   cudaGraphExec_t *g = logits ? &m->g_host_logits : &m->g_host_nologits;
@@ -1180,6 +1254,7 @@ static int launch_loop_steps(ch_model *m, uint32_t n_steps) {
 extern "C" int ch_decode_run(ch_model *m, uint32_t first_token, uint32_t n_steps) {
   if (!m) return fail(CH_EINVAL, "model is NULL");
   if (!m->loop_ready || n_steps > m->plan_steps) return fail(CH_ESTATE, "ch_decode_plan must cover n_steps first");
+  if (m->world > 1 && !m->peers_ready) return fail(CH_ESTATE, "tensor parallel: ch_model_attach_peers first");
   if (first_token >= m->V) return fail(CH_EINVAL, "first_token >= vocab");
   CH_CUDA(cudaSetDevice(m->ctx->device));
   cudaStream_t s = m->ctx->stream;
@@ -1228,6 +1303,7 @@ extern "C" int ch_read_normed_x(ch_model *m, float *x) {
   return CH_OK;
 }
 extern "C" int ch_kv_read(ch_model *m, uint32_t layer, uint32_t slot, float *k, float *v) {
+  if (m && m->world > 1) return fail(CH_ESTATE, "tensor parallel: each rank holds only its kv heads");
   if (!m || layer >= m->L || slot >= kSlots) return fail(CH_EINVAL, "bad layer / slot");
   CH_CUDA(cudaStreamSynchronize(m->ctx->stream));
   std::vector<__half> hk(m->kvd), hv(m->kvd);
@@ -1240,6 +1316,7 @@ extern "C" int ch_kv_read(ch_model *m, uint32_t layer, uint32_t slot, float *k, 
   return CH_OK;
 }
 extern "C" int ch_kv_write(ch_model *m, uint32_t layer, uint32_t slot, const float *k, const float *v) {
+  if (m && m->world > 1) return fail(CH_ESTATE, "tensor parallel: each rank holds only its kv heads");
   if (!m || layer >= m->L || slot >= kSlots || !k || !v) return fail(CH_EINVAL, "bad argument");
   std::vector<__half> hk(m->kvd), hv(m->kvd);
   for (uint32_t i = 0; i < m->kvd; i++) {
@@ -1270,6 +1347,53 @@ static int ensure_prefill(ch_model *m) {
   return CH_OK;
 }
 
+// Tensor-parallel prefill: the prompt runs through the persistent decode kernel one
+// token at a time (plan entries with forced tokens; the LM head only for the last),
+// every rank in lock step.  Token t attends to slots[0 .. num_prev + t] (its sliding
+// list is the last 1024 of them, batch_causal_attn.wgsl:53), like the batched path.
+static int prefill_tp(ch_model *m, const uint32_t *tokens, uint32_t n, const uint32_t *slots, uint32_t start_clock,
+                      uint32_t num_prev, ch_topk *topk_out, ch_progress_fn progress_fn, void *progress_ctx) {
+  if (!m->peers_ready) return fail(CH_ESTATE, "tensor parallel: ch_model_attach_peers first");
+  if (!m->embed) return fail(CH_ESTATE, "tensor-parallel prefill embeds on the device: no device embedding table");
+  cudaStream_t s = m->ctx->stream;
+  CH_CUDA(cudaStreamSynchronize(s));
+  cudaFree(m->pplan);
+  cudaFree(m->pplan_lists);
+  m->pplan = nullptr;
+  m->pplan_lists = nullptr;
+  CH_TRY(dmalloc(&m->pplan, n));
+  CH_TRY(dmalloc(&m->pplan_lists, num_prev + n));
+  CH_CUDA(cudaMemcpy(m->pplan_lists, slots, (size_t)(num_prev + n) * 4, cudaMemcpyHostToDevice));
+  std::vector<StepParams> hp(n);
+  for (uint32_t t = 0; t < n; t++) {
+    const uint32_t na = num_prev + t + 1, ns = std::min<uint32_t>(na, 1024);
+    hp[t] = StepParams{start_clock + t, slots[num_prev + t], na, ns, m->pplan_lists, m->pplan_lists + (na - ns),
+                       t, 0, tokens[t] + 1, 0};
+  }
+  CH_CUDA(cudaMemcpy(m->pplan, hp.data(), n * sizeof(StepParams), cudaMemcpyHostToDevice));
+  m->h_run[0] = 0;
+  CH_CUDA(cudaMemcpyAsync(&m->sp->next, &m->h_run[0], 4, cudaMemcpyHostToDevice, s));
+  StepBeginArgs sb{m->embed,      m->H,       sqrtf((float)m->H), m->token,    m->X[0],
+                   m->sp,         m->pplan,   n,                  m->ctx->err, m->inv_freq_s,
+                   m->inv_freq_f, m->rope_cs, m->cfg.rotary_dim / 2};
+  const MegaArgs a_nl = mega_args(m, false, false), a_lg = mega_args(m, true, false);
+  for (uint32_t t = 0; t < n; t++) {
+    CH_CUDA(launch_step_begin(sb, s, false));
+    CH_CUDA(launch_decode_step(t + 1 < n ? a_nl : a_lg, m->mk_smem, s));
+  }
+  if (topk_out) {
+    CH_CUDA(cudaMemcpyAsync(m->h_ids, m->ids, 256, cudaMemcpyDeviceToHost, s));
+    CH_CUDA(cudaMemcpyAsync(m->h_vals, m->vals, 256, cudaMemcpyDeviceToHost, s));
+  }
+  CH_CUDA(cudaStreamSynchronize(s));
+  if (topk_out)
+    for (int i = 0; i < 64; i++) topk_out[i] = ch_topk{m->h_ids[i], m->h_vals[i]};
+  if (progress_fn) progress_fn(m->L, m->L, progress_ctx);
+  uint32_t f = 0;
+  CH_TRY(ch_ctx_device_status(m->ctx, &f));
+  return status_from_flags(f);
+}
+
 extern "C" int ch_prefill(ch_model *m, const uint32_t *tokens, uint32_t n, const uint16_t *embed_bf16,
                           const uint32_t *slots, uint32_t start_clock, uint32_t num_prev, ch_topk *topk_out,
                           ch_progress_fn progress_fn, void *progress_ctx) {
@@ -1282,6 +1406,7 @@ extern "C" int ch_prefill(ch_model *m, const uint32_t *tokens, uint32_t n, const
     if (tokens[i] >= m->V) return fail(CH_EINVAL, "token id >= vocab");
   if (!embed_bf16 && !m->embed) return fail(CH_ESTATE, "no embedding table (host or device)");
   CH_CUDA(cudaSetDevice(m->ctx->device));
+  if (m->world > 1) return prefill_tp(m, tokens, n, slots, start_clock, num_prev, topk_out, progress_fn, progress_ctx);
   CH_TRY(ensure_prefill(m));
   cudaStream_t s = m->ctx->stream;
   const float scale = sqrtf((float)m->H);

@@ -188,6 +188,32 @@ class GpuModelContext:
         L.check(lib.ch_model_create_synthetic(ctx.handle, C.byref(cfg), seed, C.byref(h)))
         return cls(ctx, h.value, config)
 
+    @classmethod
+    def synthetic_sharded(cls, ctx: GpuContext, config: ModelConfig, seed: int, rank: int,
+                          world: int) -> "GpuModelContext":
+        """Shard `rank` of a `world`-GPU tensor-parallel model with the same synthetic
+        weights as synthetic(); call attach_peers before decoding."""
+        lib = L.load()
+        cfg = config.to_c()
+        h = C.c_void_p()
+        L.check(lib.ch_model_create_synthetic_sharded(ctx.handle, C.byref(cfg), seed, rank, world, C.byref(h)))
+        m = cls(ctx, h.value, config)
+        m.rank, m.world = rank, world
+        return m
+
+    def exchange_handle(self) -> bytes:
+        """CUDA IPC handle of this rank's exchange arena (CH_IPC_HANDLE_BYTES bytes)."""
+        buf = (C.c_uint8 * L.CH_IPC_HANDLE_BYTES)()
+        L.check(L.load().ch_model_exchange_handle(self.handle, buf))
+        return bytes(buf)
+
+    def attach_peers(self, handles: Sequence[bytes]) -> None:
+        """Map every rank's arena; `handles` in rank order (this rank's included)."""
+        blob = b"".join(handles)
+        assert len(blob) == L.CH_IPC_HANDLE_BYTES * len(handles)
+        buf = (C.c_uint8 * len(blob)).from_buffer_copy(blob)
+        L.check(L.load().ch_model_attach_peers(self.handle, buf))
+
     def deinit(self) -> None:
         if self.handle:
             L.load().ch_model_destroy(self.handle)
@@ -360,3 +386,20 @@ class DynamicRingBuffer:
         out = np.empty(TOTAL_SLOTS, np.uint32)
         n = self._lib.ch_ring_prefill_prev_slots(self.h, layer, start_clock, chunk_len, _ptr(out, C.c_uint32))
         return out[:n].copy()
+
+
+def attach_tensor_parallel(gm: "GpuModelContext", group=None) -> None:
+    """All-gather the ranks' arena handles over torch.distributed (any backend:
+    gloo on the host or NCCL) and attach them -- the only host-side exchange a
+    tensor-parallel model needs."""
+    import torch
+    import torch.distributed as dist
+
+    mine = torch.tensor(list(gm.exchange_handle()), dtype=torch.uint8)
+    backend = dist.get_backend(group)
+    if backend == "nccl":
+        mine = mine.cuda()
+    world = dist.get_world_size(group)
+    parts = [torch.empty_like(mine) for _ in range(world)]
+    dist.all_gather(parts, mine, group=group)
+    gm.attach_peers([bytes(p.cpu().tolist()) for p in parts])

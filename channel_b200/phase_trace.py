@@ -18,6 +18,7 @@ it); the per-CTA table shows median / max of each interval for layer 1.
 Usage (one GPU):
 
   python -m channel_b200.phase_trace [--layers 48] [--steps 4] [--clock 599] [--lib PATH]
+  torchrun --nproc-per-node N -m channel_b200.phase_trace   # tensor parallel, rank 0 prints
 """
 from __future__ import annotations
 
@@ -53,9 +54,22 @@ def main() -> None:
     from channel_b200 import DynamicRingBuffer, GpuContext, GpuModelContext, config_12b
     from channel_b200.engine import gpu_dispatch_forward_token
 
-    ctx = GpuContext.init(0)
+    import os
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    torch.cuda.set_device(rank)
+    ctx = GpuContext.init(rank)
     cfg = config_12b(layers=args.layers)
-    gm = GpuModelContext.synthetic(ctx, cfg, 3)
+    if world > 1:  # tensor parallel under torchrun: every rank traces, rank 0 prints
+        import torch.distributed as dist
+
+        from channel_b200.engine import attach_tensor_parallel
+        dist.init_process_group("gloo")
+        gm = GpuModelContext.synthetic_sharded(ctx, cfg, 3, rank, world)
+        attach_tensor_parallel(gm)
+        dist.barrier()
+    else:
+        gm = GpuModelContext.synthetic(ctx, cfg, 3)
     ring = DynamicRingBuffer(cfg.num_hidden_layers, 0)
     x = np.random.default_rng(0).standard_normal(cfg.hidden_size).astype(np.float32)
     for c in range(args.clock + 1):
@@ -67,8 +81,14 @@ def main() -> None:
     ctx.synchronize()
     buf = np.zeros(TRACE_CTAS * TRACE_PHASES * TRACE_MARKS, np.uint64)
     L.check(lib.ch_phase_trace_copy(buf.ctypes.data, buf.size))
-    grid = min(TRACE_CTAS, torch.cuda.get_device_properties(0).multi_processor_count)
-    nph = 5 * cfg.num_hidden_layers + 2
+    grid = min(TRACE_CTAS, torch.cuda.get_device_properties(rank).multi_processor_count)
+    nph = 5 * cfg.num_hidden_layers + (3 if world > 1 else 2)
+    if rank != 0:
+        if world > 1:
+            dist.barrier()
+        gm.deinit()
+        ctx.deinit()
+        return
     tr = buf.reshape(TRACE_CTAS, TRACE_PHASES, TRACE_MARKS)[:grid, :nph, :7].astype(np.int64)
     kinds = ["qkv", "attn", "o", "gateup", "down"]
 
@@ -86,7 +106,8 @@ def main() -> None:
     agg = collections.defaultdict(lambda: np.zeros(6))
     cnt = collections.Counter()
     for pi in range(nph):
-        kind = kinds[pi % 5] if pi < 5 * cfg.num_hidden_layers else ("lm" if pi == nph - 2 else "topk")
+        tail = ["lm", "topk", "merge"]
+        kind = kinds[pi % 5] if pi < 5 * cfg.num_hidden_layers else tail[pi - 5 * cfg.num_hidden_layers]
         st = fill(tr[:, pi, :], pi)
         agg[kind] += np.diff(st.max(axis=0))  # slowest CTA at each mark
         cnt[kind] += 1
@@ -94,7 +115,7 @@ def main() -> None:
     print(f"decode step span {span / 1e3:.1f} us ({cfg.num_hidden_layers} layers, clock {args.clock}, "
           f"{len(act)} active / {len(sli)} sliding slots)")
     print("phase   n   " + "".join(f"{c:>12s}" for c in COLS) + "   (us per phase, slowest CTA)")
-    for k in ["qkv", "attn", "o", "gateup", "down", "lm", "topk"]:
+    for k in ["qkv", "attn", "o", "gateup", "down", "lm", "topk"] + (["merge"] if world > 1 else []):
         a = agg[k] / max(cnt[k], 1) / 1e3
         print(f"{k:7s} {cnt[k]:3d} " + "".join(f"{v:12.2f}" for v in a))
     per_layer = sum(agg[k].sum() for k in kinds) / cfg.num_hidden_layers / 1e3
@@ -105,6 +126,8 @@ def main() -> None:
         d = np.diff(fill(tr[:, pi, :], pi), axis=1) / 1e3
         med, mx = np.median(d, axis=0), d.max(axis=0)
         print(f"  {k:7s} " + "  ".join(f"{a:5.2f}/{b:5.2f}" for a, b in zip(med, mx)))
+    if world > 1:
+        dist.barrier()
     gm.deinit()
     ctx.deinit()
 

@@ -91,6 +91,25 @@ int ch_model_create(ch_ctx *ctx, const ch_model_config *cfg, const ch_layer_weig
  * uniform in [-8,7], scales |N(0,0.02)| as f16, embedding bf16 N(0,0.02), LM head
  * = Q8_0 of the embedding, norms 1+N(0,0.02)); generator shared with the oracle. */
 int ch_model_create_synthetic(ch_ctx *ctx, const ch_model_config *cfg, uint64_t seed, ch_model **out);
+
+/* Tensor-parallel decode (no counterpart in the reference, which runs one GPU):
+ * shard `rank` of `world` (<= 8, one process per GPU) of the same synthetic model.
+ * q|k|v and the KV cache are split by heads, o_proj / down_proj by output rows,
+ * gate/up by intermediate rows, the LM head by vocab rows; norms and the embedding
+ * are replicated.  Each rank's persistent decode kernel writes its output rows
+ * straight into every rank's copy of the next phase's input (NVLink peer stores
+ * through CUDA IPC) and all ranks meet at one arrival counter per phase, so the
+ * ranks compute identical tokens.  Before decoding, every rank gets its handle
+ * with ch_model_exchange_handle, the caller all-gathers the world handles in rank
+ * order and every rank passes them to ch_model_attach_peers.  All ranks must then
+ * make the same sequence of decode / prefill calls (prefill runs token by token
+ * through the decode kernel); after ch_model_zero_state the caller synchronizes
+ * the ranks before the next call.  KV read/write is not available on a shard. */
+#define CH_IPC_HANDLE_BYTES 64
+int ch_model_create_synthetic_sharded(ch_ctx *ctx, const ch_model_config *cfg, uint64_t seed, uint32_t rank,
+                                      uint32_t world, ch_model **out);
+int ch_model_exchange_handle(ch_model *m, void *handle /* CH_IPC_HANDLE_BYTES */);
+int ch_model_attach_peers(ch_model *m, const void *handles /* world x CH_IPC_HANDLE_BYTES, rank order */);
 void ch_model_destroy(ch_model *m);
 /* Zero KV caches and decode state (src/server.zig:76-82). */
 int ch_model_zero_state(ch_model *m);
