@@ -90,6 +90,8 @@ SIGNATURES = {
     "ch_topk64": (i32, [vp, vp, u32, vp, vp]),
     "ch_batch_gemm_q4": (i32, [vp, vp, u32, u32, vp, u32, vp]),
     "ch_batch_fused_mlp_q4": (i32, [vp, vp, u32, u32, vp, u32, vp]),
+    "ch_batch_gemm_q4_mma": (i32, [vp, vp, u32, u32, vp, u32, vp]),
+    "ch_batch_fused_mlp_q4_mma": (i32, [vp, vp, u32, u32, vp, u32, vp]),
     "ch_gen_q4_blocks": (i32, [vp, vp, u32, u32, u64, f32]),
     "ch_gen_bf16": (i32, [vp, vp, sz, u64, f32, f32]),
     "ch_quantize_q8_rows": (i32, [vp, vp, u32, u32, vp]),

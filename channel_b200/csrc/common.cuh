@@ -19,6 +19,7 @@ enum DevError : uint32_t {
   DEV_ERR_BAD_SLOT = 1u << 1,
   DEV_ERR_BAD_LIST = 1u << 2,
   DEV_ERR_PEER_TIMEOUT = 1u << 3,
+  DEV_ERR_SCALE_RANGE = 1u << 4,  // a Q4 block scale outside the tensor-core GEMM's exact range
 };
 
 

@@ -175,4 +175,23 @@ struct BatchGemmArgs {
 };
 cudaError_t launch_batch_gemm_q4(const BatchGemmArgs &a, cudaStream_t s);
 
+// tcgen05 prefill GEMM (prefill_tc.cu).  One scratch buffer per call site:
+// [16 KB split-K tile counters, zero between launches][split activation][split-K
+// partials]; tc_gemm_scratch_bytes(N, M, K) bytes, 256-byte aligned, the first
+// 16 KB zeroed once when it is allocated.
+struct TcGemmArgs {
+  const uint8_t *tiles;  // Q4 tiles [M/16][K/64]
+  const uint8_t *xs;     // split activation, 16-byte aligned
+  float *Y;              // EPI_STORE: [N][M]; EPI_GELU_MUL: [N][M/2]
+  uint32_t M, K, N;
+  int epi;
+  uint32_t *err;  // device error word (bounded waits, scale range)
+};
+size_t tc_split_x_bytes(uint32_t N, uint32_t K);
+size_t tc_gemm_scratch_bytes(uint32_t N, uint32_t M, uint32_t K);
+cudaError_t launch_tc_split_x(const float *X, uint32_t N, uint32_t K, uint8_t *xs, cudaStream_t s);
+cudaError_t launch_batch_gemm_tc(const TcGemmArgs &a, uint8_t *scratch, cudaStream_t s);
+// split + GEMM: the prefill's Q4 GEMM
+cudaError_t launch_batch_gemm_q4_tc(const BatchGemmArgs &g, uint8_t *scratch, uint32_t *err, cudaStream_t s);
+
 }  // namespace ch

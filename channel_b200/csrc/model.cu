@@ -65,6 +65,8 @@ struct ch_ctx {
   float2 *attn_rope = nullptr;
   size_t attn_rope_n = 0;
   StepParams *op_sp = nullptr;
+  uint8_t *xs = nullptr;  // scratch of the tcgen05 GEMM (counters | split activation | partials)
+  size_t xs_n = 0;
 };
 
 static int ctx_ensure_gemv(ch_ctx *c, uint32_t row_tiles) {
@@ -75,6 +77,18 @@ static int ctx_ensure_gemv(ch_ctx *c, uint32_t row_tiles) {
     CH_CUDA(cudaMalloc(&c->gemv_counters, row_tiles * sizeof(uint32_t)));
     CH_CUDA(cudaMemsetAsync(c->gemv_counters, 0, row_tiles * sizeof(uint32_t), c->stream));
   }
+  return CH_OK;
+}
+
+static int ctx_ensure_xs(ch_ctx *c, size_t bytes) {
+  if (c->xs_n >= bytes) return CH_OK;
+  CH_CUDA(cudaStreamSynchronize(c->stream));
+  if (c->xs) CH_CUDA(cudaFree(c->xs));
+  c->xs = nullptr;
+  c->xs_n = 0;
+  CH_CUDA(cudaMalloc(&c->xs, bytes));
+  CH_CUDA(cudaMemsetAsync(c->xs, 0, 16384, c->stream));  // split-K tile counters start at zero
+  c->xs_n = bytes;
   return CH_OK;
 }
 
@@ -110,6 +124,7 @@ extern "C" void ch_ctx_destroy(ch_ctx *c) {
   cudaFree(c->topk_counter);
   cudaFree(c->attn_rope);
   cudaFree(c->op_sp);
+  cudaFree(c->xs);
   cudaStreamDestroy(c->stream);
   delete c;
 }
@@ -215,6 +230,7 @@ struct ch_model {
   uint32_t pf_cap = 0;
   float *pX = nullptr, *pNX = nullptr, *pQKV = nullptr, *pQO = nullptr, *pA = nullptr, *pMO = nullptr, *pACT = nullptr;
   uint32_t *pSlots = nullptr, *pTok = nullptr;
+  uint8_t *pXS = nullptr;  // scratch of the tcgen05 GEMM (counters | split activation | partials)
 };
 
 static void free_model(ch_model *m) {
@@ -239,7 +255,7 @@ static void free_model(ch_model *m) {
                  m->attn, m->o_out, m->act, m->down_out, m->logits, m->vals, m->ids, m->token, m->token_hist, m->sp,
                  m->active, m->sliding, m->gemv_partial, m->gemv_counters, m->attn_partial, m->attn_counters,
                  m->topk_cand, m->topk_counter, m->plan, m->plan_lists, m->pX, m->pNX, m->pQKV, m->pQO, m->pA, m->pMO,
-                 m->pACT, m->pSlots, m->pTok};
+                 m->pACT, m->pSlots, m->pTok, m->pXS};
   for (void *p : dev) cudaFree(p);
   for (int k = 0; k < 5; k++) {
     cudaFree(m->gdir[k]);
@@ -1343,6 +1359,15 @@ static int ensure_prefill(ch_model *m) {
   CH_TRY(dmalloc(&m->pACT, (size_t)N * m->I));
   CH_TRY(dmalloc(&m->pSlots, (size_t)N + kSlots));
   CH_TRY(dmalloc(&m->pTok, (size_t)N));
+  {
+    const uint32_t qkvd = m->qd + 2 * m->kvd;
+    size_t need = tc_gemm_scratch_bytes(N, qkvd, m->H);
+    need = std::max(need, tc_gemm_scratch_bytes(N, m->H, m->qd));
+    need = std::max(need, tc_gemm_scratch_bytes(N, 2 * m->I, m->H));
+    need = std::max(need, tc_gemm_scratch_bytes(N, m->H, m->I));
+    CH_TRY(dmalloc(&m->pXS, need));
+    CH_CUDA(cudaMemset(m->pXS, 0, 16384));  // split-K tile counters start at zero
+  }
   m->pf_cap = N;
   return CH_OK;
 }
@@ -1431,10 +1456,11 @@ extern "C" int ch_prefill(ch_model *m, const uint32_t *tokens, uint32_t n, const
   CH_CUDA(cudaMemcpyAsync(m->pSlots, slots, (num_prev + n) * 4, cudaMemcpyHostToDevice, s));
   const float eps = m->cfg.rms_norm_eps;
   const uint32_t qkvd = m->qd + 2 * m->kvd;
+  uint32_t *err = m->ctx->err;
   for (uint32_t l = 0; l < m->L; l++) {
     DevLayer &dl = m->layers[l];
     if (l == 0) CH_CUDA(launch_rmsnorm_rows(m->pX, dl.input_norm, m->pNX, n, m->H, eps, s));
-    CH_CUDA(launch_batch_gemm_q4(BatchGemmArgs{dl.qkv, qkvd, m->H, n, m->pNX, m->pQKV, EPI_STORE}, s));
+    CH_CUDA(launch_batch_gemm_q4_tc(BatchGemmArgs{dl.qkv, qkvd, m->H, n, m->pNX, m->pQKV, EPI_STORE}, m->pXS, err, s));
     BatchQkvRopeArgs r{};
     r.q = m->pQKV;
     r.k = m->pQKV + m->qd;
@@ -1460,11 +1486,12 @@ extern "C" int ch_prefill(ch_model *m, const uint32_t *tokens, uint32_t n, const
     CH_CUDA(launch_batch_qkv_rope(r, s));
     BatchAttnArgs at{m->pQO, dl.kc, dl.vc, m->pSlots, n, num_prev, m->nq, m->nkv, m->D, 1.0f, dl.full ? 0 : 1, m->pA};
     CH_CUDA(launch_batch_causal_attn(at, s));
-    CH_CUDA(launch_batch_gemm_q4(BatchGemmArgs{dl.o, m->H, m->qd, n, m->pA, m->pMO, EPI_STORE}, s));
+    CH_CUDA(launch_batch_gemm_q4_tc(BatchGemmArgs{dl.o, m->H, m->qd, n, m->pA, m->pMO, EPI_STORE}, m->pXS, err, s));
     if (dl.post_attn) CH_CUDA(launch_rmsnorm_rows(m->pMO, dl.post_attn, m->pMO, n, m->H, eps, s));
     CH_CUDA(launch_add_rmsnorm_rows(m->pX, m->pMO, dl.pre_ffn, m->pNX, n, m->H, eps, 1.0f, s));
-    CH_CUDA(launch_batch_gemm_q4(BatchGemmArgs{dl.gateup, 2 * m->I, m->H, n, m->pNX, m->pACT, EPI_GELU_MUL}, s));
-    CH_CUDA(launch_batch_gemm_q4(BatchGemmArgs{dl.down, m->H, m->I, n, m->pACT, m->pMO, EPI_STORE}, s));
+    CH_CUDA(launch_batch_gemm_q4_tc(BatchGemmArgs{dl.gateup, 2 * m->I, m->H, n, m->pNX, m->pACT, EPI_GELU_MUL}, m->pXS,
+                                    err, s));
+    CH_CUDA(launch_batch_gemm_q4_tc(BatchGemmArgs{dl.down, m->H, m->I, n, m->pACT, m->pMO, EPI_STORE}, m->pXS, err, s));
     if (dl.post_ffn) CH_CUDA(launch_rmsnorm_rows(m->pMO, dl.post_ffn, m->pMO, n, m->H, eps, s));
     const float *next = (l + 1 < m->L) ? m->layers[l + 1].input_norm : m->final_norm;
     CH_CUDA(launch_add_rmsnorm_rows(m->pX, m->pMO, next, m->pNX, n, m->H, eps, dl.scalar, s));
@@ -1655,11 +1682,30 @@ extern "C" int ch_topk64(ch_ctx *c, const float *logits, uint32_t V, uint32_t *i
 extern "C" int ch_batch_gemm_q4(ch_ctx *c, const void *tiles, uint32_t rows, uint32_t cols, const float *x, uint32_t n,
                                 float *y) {
   if (!c || !tiles || !x || !y || rows % 16 || cols % 64) return fail(CH_EINVAL, "batch_gemm_q4 arguments");
-  CH_CUDA(launch_batch_gemm_q4(BatchGemmArgs{(const uint8_t *)tiles, rows, cols, n, x, y, EPI_STORE}, c->stream));
+  if (n == 0) return CH_OK;
+  CH_TRY(ctx_ensure_xs(c, tc_gemm_scratch_bytes(n, rows, cols)));
+  CH_CUDA(launch_batch_gemm_q4_tc(BatchGemmArgs{(const uint8_t *)tiles, rows, cols, n, x, y, EPI_STORE}, c->xs, c->err,
+                                  c->stream));
   return CH_OK;
 }
 extern "C" int ch_batch_fused_mlp_q4(ch_ctx *c, const void *tiles, uint32_t rows, uint32_t cols, const float *x,
                                      uint32_t n, float *act) {
+  if (!c || !tiles || !x || !act || rows % 8 || cols % 64) return fail(CH_EINVAL, "batch_fused_mlp_q4 arguments");
+  if (n == 0) return CH_OK;
+  CH_TRY(ctx_ensure_xs(c, tc_gemm_scratch_bytes(n, 2 * rows, cols)));
+  CH_CUDA(launch_batch_gemm_q4_tc(BatchGemmArgs{(const uint8_t *)tiles, 2 * rows, cols, n, x, act, EPI_GELU_MUL}, c->xs,
+                                  c->err, c->stream));
+  return CH_OK;
+}
+// the same two GEMMs on the legacy mma.sync tensor path, kept as the measured baseline
+extern "C" int ch_batch_gemm_q4_mma(ch_ctx *c, const void *tiles, uint32_t rows, uint32_t cols, const float *x,
+                                    uint32_t n, float *y) {
+  if (!c || !tiles || !x || !y || rows % 16 || cols % 64) return fail(CH_EINVAL, "batch_gemm_q4 arguments");
+  CH_CUDA(launch_batch_gemm_q4(BatchGemmArgs{(const uint8_t *)tiles, rows, cols, n, x, y, EPI_STORE}, c->stream));
+  return CH_OK;
+}
+extern "C" int ch_batch_fused_mlp_q4_mma(ch_ctx *c, const void *tiles, uint32_t rows, uint32_t cols, const float *x,
+                                         uint32_t n, float *act) {
   if (!c || !tiles || !x || !act || rows % 8 || cols % 64) return fail(CH_EINVAL, "batch_fused_mlp_q4 arguments");
   CH_CUDA(launch_batch_gemm_q4(BatchGemmArgs{(const uint8_t *)tiles, 2 * rows, cols, n, x, act, EPI_GELU_MUL}, c->stream));
   return CH_OK;

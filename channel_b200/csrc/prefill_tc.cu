@@ -1,0 +1,627 @@
+// prefill_tc.cu -- the batched prefill GEMM on the 5th-generation tensor cores.
+//
+// Restated reference shaders:
+//   batch_gemm_q4.wgsl:26-160       Y[t*M + r] = sum_b d_rb sum_i (q_rbi - 8) X[t][32b+i]
+//   batch_fused_mlp_q4.wgsl:33-196  Y[t*M/2 + r] = gelu_tanh(gate_r . x_t) * (up_r . x_t)
+//
+// A pair of CTAs (a cluster of 2 on two SMs) computes a tile of 256 weight rows x
+// 256 tokens with tcgen05.mma.cta_group::2 (kind::f16, M=256, N=256, f32
+// accumulators in tensor memory): each CTA holds 128 rows of the weight operand and
+// 128 tokens of the activation operand and receives the 128 x 256 accumulators of
+// its own rows.  M=256 x N=256 is the largest tcgen05 shape: an MMA instruction
+// takes about the same time at any smaller shape.
+//
+// Numerics (fp32-faithful; the shaders' up to the order of the additions):
+//   * the weight w = (q-8) d of a 32-block enters as two exact f16 operands:
+//     d = d_hi + d_lo with d_hi = d's top 8 significant bits and d_lo the rest
+//     (at most 3 bits), A_hi = (q-8) d_hi 2^8 and A_lo = (q-8) d_lo 2^16 -- both
+//     products fit an f16 significand, so the dequantised weights are exact;
+//   * the activation enters as an f16 pair hi + lo (x = hi + lo to 2^-22), the lo
+//     part stored as lo 2^8;
+//   * per 16-wide k step three MMAs: D1 += A_hi X_hi (scale 2^-8) and the two
+//     correction terms D2 += A_hi (X_lo 2^8), D2 += A_lo X_hi (scale 2^-16), so
+//     that the small terms are summed among themselves and not rounded away
+//     against the main sum; Y = 2^-8 D1 + 2^-16 D2.  The one term left out,
+//     A_lo X_lo, is below 2^-18 of each product.
+//   Scales are assumed |d| < 16 (checked; the device error word flags others).
+//
+// Per 64-wide k tile each CTA takes two copy requests -- one 3-D TMA box of its 8
+// Q4 tiles (576 B each, at a stride of K/64 tiles in the row-tile-major layout)
+// and one 32 KB bulk copy of its activation share, pre-split and pre-swizzled by
+// tc_split_x_kernel -- because the copy engine takes tens of cycles per request.
+//
+// Warp roles (22 warps per CTA):
+//   0-15  epilogue: after the k loop, warp w reads TMEM lanes 32*(w%4).. (a warp
+//         may touch only its quarter of the lanes) and token columns
+//         64*(w/4)..+63 of both accumulators, and stores Y (or a split-K partial)
+//   16-19 dequant: Q4 nibbles and scales (staged by TMA) -> A_hi, A_lo tiles
+//   20    producer: TMEM allocation (whole warp, both CTAs); the copies (lane 0)
+//   21    MMA issuer (lane 0 of the pair's leader CTA, rank 0)
+// Barriers: a 3-deep stage ring (full: copy bytes, per CTA; aready: one arrival
+// per dequant warp of both CTAs, at the leader; empty: tcgen05.commit multicast to
+// both) and dfull (commit multicast after the last k tile).  Arrivals at the
+// leader's barriers are release.cluster and its waits on them acquire.cluster.
+// Every wait is bounded: a wait that gives up sets the device error word and the
+// CTA's abort flag; the roles then leave their loops, the MMAs in flight are
+// waited for (bounded), both CTAs meet at a cluster barrier and TMEM is released.
+//
+// Split-K (when the rows give too few tile pairs for the SMs): the k tiles are
+// divided among SK pairs per output tile; each writes its partial to a workspace
+// and the last to finish (an atomic counter per tile) adds the SK partials in split
+// order -- the same order on every run -- and applies the epilogue.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+
+#include "common.cuh"
+#include "kernels.cuh"
+
+namespace ch {
+namespace {
+constexpr int kTcBM = 128, kTcBN = 256, kTcBK = 64;      // per CTA: 128 rows; per pair: 256 tokens
+constexpr int kTcHalfN = kTcBN / 2;                       // tokens of the activation operand per CTA
+constexpr int kTcStages = 3;
+constexpr uint32_t kTcABytes = kTcBM * kTcBK * 2;        // 16 KB: 128 rows x 128 B (one of A_hi, A_lo)
+constexpr uint32_t kTcPlane = kTcHalfN * kTcBK * 2;      // 16 KB: one f16 plane of 128 tokens
+constexpr uint32_t kTcXBytes = 2 * kTcPlane;             // this CTA's share: hi plane, lo plane
+constexpr uint32_t kTcRawBytes = 8 * kTileBytes;         // 8 whole Q4 tiles (nibbles + scales): one TMA box
+constexpr uint32_t kTcStageBytes = 2 * kTcABytes + kTcXBytes;  // 64 KB: A_hi | A_lo | X_hi | X_lo
+constexpr int kEpiWarps = 16, kDqWarps = 4;
+constexpr int kDqWarp0 = kEpiWarps, kProdWarp = kEpiWarps + kDqWarps, kMmaWarp = kProdWarp + 1;
+constexpr int kTcThreads = (kMmaWarp + 1) * 32;
+constexpr int kEpiThreads = kEpiWarps * 32;
+constexpr uint32_t kTmemCols = 512;  // D1: columns 0-255, D2: 256-511
+constexpr uint32_t kCounterBytes = 16384;
+constexpr uint32_t kMaxCounters = kCounterBytes / 4;
+
+// shared-memory map, offsets from a 1024-byte aligned base (the swizzle atoms of
+// the A and X tiles start on 1024-byte boundaries); identical in both CTAs
+constexpr uint32_t kOffRaw = kTcStages * kTcStageBytes;
+constexpr uint32_t kOffBars = kOffRaw + kTcStages * kTcRawBytes;
+constexpr uint32_t kNumBars = 3 * kTcStages + 1;
+constexpr uint32_t kOffMisc = kOffBars + kNumBars * 8;
+constexpr uint32_t kTcSmemUsed = kOffMisc + 16;
+static_assert(kTcStageBytes % 1024 == 0, "stage alignment");
+static_assert(kTcRawBytes % 128 == 0, "TMA destination alignment");
+}  // namespace
+constexpr size_t kTcSmemBytes = kTcSmemUsed + 1024;  // + alignment slack
+static_assert(kTcSmemBytes <= 232448, "shared memory per CTA");
+
+// Optional pipeline timeline (trace build, -DCH_PHASE_TRACE): one role thread of the
+// leader CTA of pair 1 (token tile 0, split 0) records clock64 at each event:
+// 0 producer issued k tile, 1 dequant saw its copies land, 2 dequant published the
+// A tiles, 3 MMA started the k tile, 4 MMA issued the k tile, 5 epilogue saw the
+// accumulators complete, 6 epilogue done (warp 0).
+#ifdef CH_PHASE_TRACE
+constexpr int kTcTraceKinds = 8, kTcTraceLen = 1024;
+__device__ long long g_tc_trace[kTcTraceKinds * kTcTraceLen];
+#define TC_MARK(kind, idx)                                                                     \
+  do {                                                                                         \
+    if (blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 1 && (idx) < (uint32_t)kTcTraceLen) \
+      g_tc_trace[(kind) * kTcTraceLen + (idx)] = clock64();                                    \
+  } while (0)
+#else
+#define TC_MARK(kind, idx) \
+  do {                     \
+  } while (0)
+#endif
+
+// ---------------------------------------------------------------------------
+// tcgen05 / TMEM / cluster primitives (PTX ISA 8.7, sm_100a)
+
+// Shared-memory matrix descriptor of a K-major tile in the 128-byte swizzle: rows of
+// 128 B, 8-row atoms of 1024 B (stride byte offset), leading byte offset unused (1),
+// descriptor version 1, layout type 2 = SWIZZLE_128B.
+CH_DEV uint64_t umma_desc_sw128(uint32_t saddr) {
+  return (uint64_t)((saddr & 0x3FFFFu) >> 4) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+         ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+// Instruction descriptor, kind::f16: D f32 (bits 4-5 = 1), A and B f16 (0), both
+// K-major (bits 15, 16 = 0), N >> 3 at bits 17-22, M >> 4 at bits 24-28; M = 256
+// across the CTA pair.
+constexpr uint32_t kTcIdesc = (1u << 4) | ((uint32_t)(kTcBN >> 3) << 17) | ((uint32_t)((2 * kTcBM) >> 4) << 24);
+
+// D[tmem] (+)= A[adesc] * B[bdesc]^T over the CTA pair (issued by the leader)
+CH_DEV void tc_mma(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(kTcIdesc), "r"(accumulate)
+      : "memory");
+}
+// arrive on `bar` (same offset) in both CTAs of the pair once every tcgen05
+// operation this thread issued so far is complete
+CH_DEV void tc_commit_pair(uint64_t *bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+          smem_u32(bar)),
+      "h"((unsigned short)3)
+      : "memory");
+}
+CH_DEV void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+CH_DEV void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+CH_DEV void tc_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+// 32 consecutive f32 columns of this thread's TMEM lane
+CH_DEV void tc_ld32(uint32_t taddr, uint32_t (&v)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),
+        "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]), "=r"(v[16]),
+        "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]),
+        "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+      : "r"(taddr)
+      : "memory");
+}
+// 3-D tiled TMA load (no multicast) of the box at (x, y, z) into this CTA's shared memory
+CH_DEV void tma_load_3d(void *dst, const CUtensorMap *map, int x, int y, int z, uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
+      "[%5];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
+      : "memory");
+}
+CH_DEV void st_shared_u32(uint32_t addr, uint32_t v) {
+  asm volatile("st.shared.b32 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
+}
+CH_DEV uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// address of this CTA's shared variable `local` in CTA `rank` of the cluster
+CH_DEV uint32_t map_shared(uint32_t local, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local), "r"(rank));
+  return r;
+}
+CH_DEV void mbar_arrive_cluster(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+CH_DEV bool mbar_try_wait_cluster(uint64_t *bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n"
+      " selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+CH_DEV void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// the epilogue warps' own barrier (named barrier 1, 512 threads)
+CH_DEV void epi_sync() { asm volatile("bar.sync 1, %0;" ::"r"(kEpiThreads) : "memory"); }
+
+// Bounded mbarrier wait (cluster: acquire at cluster scope, for barriers the other
+// CTA arrives at).  With `abort` it also gives up as soon as another role has
+// aborted; a wait that runs out of time raises the abort flag and the error.
+CH_DEV bool tc_wait(uint64_t *bar, uint32_t parity, volatile uint32_t *abort, uint32_t *err, bool cluster = false) {
+  auto poll = [&]() { return cluster ? mbar_try_wait_cluster(bar, parity) : mbar_try_wait(bar, parity); };
+  if (poll()) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (;;) {
+    for (int i = 0; i < 32; i++)
+      if (poll()) return true;
+    if (abort && *abort) return false;
+    if (globaltimer_ns() - t0 > 2000000000ull) break;
+  }
+  if (abort) *abort = 1u;
+  if (err) atomicOr(err, DEV_ERR_TMA_TIMEOUT);
+  return false;
+}
+
+// gelu_tanh(g) * u with the operation order of batch_fused_mlp_q4.wgsl's epilogue
+CH_DEV float gelu_mul(float g, float u) {
+  const float x3 = __fmul_rn(__fmul_rn(__fmul_rn(0.044715f, g), g), g);
+  const float inner = __fmul_rn(0.7978845608f, __fadd_rn(g, x3));
+  return __fmul_rn(__fmul_rn(__fmul_rn(0.5f, g), __fadd_rn(1.0f, tanhf(inner))), u);
+}
+
+// f16 block scale d -> the f16x2 multipliers (d_hi 2^8, d_hi 2^8) and (d_lo 2^16,
+// d_lo 2^16); both exact.  Returns false for |d| >= 16 (outside the exact range).
+CH_DEV bool split_scale(uint32_t dbits, uint32_t &hs, uint32_t &ls) {
+  const uint32_t hb = dbits & 0xFFF8u;  // top 8 significant bits (sign kept)
+  const float d = __half2float(__ushort_as_half((unsigned short)dbits));
+  const float dh = __half2float(__ushort_as_half((unsigned short)hb));
+  const float dl = __fsub_rn(d, dh);  // exact: at most 3 significant bits
+  const unsigned short h16 = __half_as_ushort(__float2half_rn(__fmul_rn(dh, 256.f)));
+  const unsigned short l16 = __half_as_ushort(__float2half_rn(__fmul_rn(dl, 65536.f)));
+  hs = (uint32_t)h16 | ((uint32_t)h16 << 16);
+  ls = (uint32_t)l16 | ((uint32_t)l16 << 16);
+  return fabsf(d) < 16.f;
+}
+CH_DEV uint32_t hmul2_u32(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+
+// ---------------------------------------------------------------------------
+// X [N][K] f32 -> per (256-token tile, k tile) block of 64 KB made of two 32 KB
+// halves (tokens 0-127, 128-255: the share of CTA rank 0 and 1), each the f16 hi
+// plane then the (lo 2^8) plane of 128 token rows x 64 k in the 128-byte swizzle (16-byte
+// chunk c of row r stored at chunk c ^ (r % 8)).  Token rows >= N are zero.
+__global__ void tc_split_x_kernel(const float *X, uint32_t N, uint32_t K, uint32_t ntok, uint8_t *xs) {
+  const uint32_t KT = K / 64, c8n = K / 8;
+  const uint64_t total = (uint64_t)ntok * c8n;
+  for (uint64_t idx = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; idx < total;
+       idx += (uint64_t)gridDim.x * blockDim.x) {
+    const uint32_t n = (uint32_t)(idx / c8n), c8 = (uint32_t)(idx % c8n);
+    const uint32_t kt = c8 >> 3, c = c8 & 7, nt = n >> 8, h = (n >> 7) & 1, r = n & 127;
+    float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    if (n < N) {
+      const float4 *src = reinterpret_cast<const float4 *>(X + (size_t)n * K + (size_t)c8 * 8);
+      const float4 x0 = src[0], x1 = src[1];
+      v[0] = x0.x, v[1] = x0.y, v[2] = x0.z, v[3] = x0.w, v[4] = x1.x, v[5] = x1.y, v[6] = x1.z, v[7] = x1.w;
+    }
+    uint32_t hi[4], lo[4];
+#pragma unroll
+    for (int e = 0; e < 4; e++) {
+      const __half h0 = __float2half_rn(v[2 * e]), h1 = __float2half_rn(v[2 * e + 1]);
+      const __half l0 = __float2half_rn(__fmul_rn(__fsub_rn(v[2 * e], __half2float(h0)), 256.f));
+      const __half l1 = __float2half_rn(__fmul_rn(__fsub_rn(v[2 * e + 1], __half2float(h1)), 256.f));
+      hi[e] = pack_half2(h0, h1);
+      lo[e] = pack_half2(l0, l1);
+    }
+    uint8_t *blk = xs + (((size_t)nt * KT + kt) * 2 + h) * kTcXBytes;
+    const uint32_t off = (r >> 3) * 1024 + (r & 7) * 128 + ((c ^ (r & 7)) << 4);
+    *reinterpret_cast<uint4 *>(blk + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+    *reinterpret_cast<uint4 *>(blk + kTcPlane + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+  }
+}
+
+// ---------------------------------------------------------------------------
+struct TcLaunch {
+  uint32_t sk;         // split-K factor (k tiles per split = KT / sk)
+  uint32_t nt_tiles;   // 256-token tiles
+  uint32_t *counters;  // split-K: one per CTA tile, zero between launches
+  float *ws;           // split-K partials [sk][nt_tiles*256][M]
+};
+
+// grid (2, token tiles, row pairs x splits), clusters of 2 along x: blockIdx.x = rank
+template <int EPI>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
+    batch_gemm_tc_kernel(const TcGemmArgs a, const TcLaunch L, const __grid_constant__ CUtensorMap wmap) {
+  extern __shared__ uint8_t smem_dyn[];
+  const uint32_t dyn = smem_u32(smem_dyn);
+  uint8_t *sm = smem_dyn + (((dyn + 1023u) & ~1023u) - dyn);
+  const uint32_t sbase = smem_u32(sm);
+  uint64_t *bars = reinterpret_cast<uint64_t *>(sm + kOffBars);
+  uint64_t *full = bars, *aready = bars + kTcStages, *empty = bars + 2 * kTcStages, *dfull = bars + 3 * kTcStages;
+  uint32_t *misc = reinterpret_cast<uint32_t *>(sm + kOffMisc);
+  uint32_t *tmem_slot = misc;
+  volatile uint32_t *abort = misc + 1;
+  volatile uint32_t *is_last = misc + 2;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_rank();
+  const bool leader = rank == 0;
+  const uint32_t KT = a.K / kTcBK, KTS = KT / L.sk;
+  const uint32_t nt = blockIdx.y, mp = blockIdx.z / L.sk, sk = blockIdx.z % L.sk;
+  const uint32_t kt0 = sk * KTS;
+  const uint32_t rt0 = (mp * 2 + rank) * 8;
+  const uint32_t row_tiles = a.M / 16;
+  const uint32_t ntiles = rt0 < row_tiles ? min(8u, row_tiles - rt0) : 0u;  // Q4 row tiles of this CTA
+  const uint32_t ready_l = map_shared(smem_u32(aready), 0);  // the leader's aready, as a cluster address
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kTcStages; s++) {
+      mbar_init(&full[s], 1);
+      mbar_init(&aready[s], 2 * kDqWarps);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(dfull, 1);
+    *abort = 0u;
+    fence_mbar_init();
+  }
+  if (warp == kProdWarp) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  cluster_sync_all();  // barriers initialised and TMEM allocated in both CTAs
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == kProdWarp) {
+    if (lane == 0) {
+      const uint8_t *xs = a.xs + ((size_t)nt * KT * 2 + rank) * kTcXBytes;  // + kt * 2 * kTcXBytes
+      uint32_t i = 0;
+      for (; i < KTS; i++) {
+        const uint32_t kt = kt0 + i;
+        const int s = i % kTcStages;
+        if (i >= (uint32_t)kTcStages && !tc_wait(&empty[s], ((i / kTcStages) - 1) & 1, abort, a.err)) break;
+        // the TMA box always lands whole (rows past M read as zeros)
+        mbar_arrive_expect_tx(&full[s], kTcRawBytes + kTcXBytes);
+        tma_load_3d(sm + kOffRaw + s * kTcRawBytes, &wmap, 0, (int)kt, (int)rt0, &full[s]);
+        bulk_g2s(sm + s * kTcStageBytes + 2 * kTcABytes, xs + (size_t)kt * 2 * kTcXBytes, kTcXBytes, &full[s]);
+        TC_MARK(0, i);
+      }
+      // the copies of the last issues land before the CTA may leave (normally long done)
+      for (uint32_t j = i > (uint32_t)kTcStages ? i - kTcStages : 0; j < i; j++)
+        tc_wait(&full[j % kTcStages], (j / kTcStages) & 1, nullptr, a.err);
+    }
+  } else if (warp == kMmaWarp) {
+    if (leader && lane == 0) {
+      bool issued = false;
+      for (uint32_t i = 0; i < KTS; i++) {
+        const int s = i % kTcStages;
+        if (!tc_wait(&full[s], (i / kTcStages) & 1, abort, a.err)) break;         // own activation share landed
+        if (!tc_wait(&aready[s], (i / kTcStages) & 1, abort, a.err, true)) break;  // both CTAs' A tiles written
+        tc_fence_after();
+        TC_MARK(3, i);
+        const uint32_t st = sbase + s * kTcStageBytes;
+        const uint64_t ah = umma_desc_sw128(st), al = umma_desc_sw128(st + kTcABytes);
+        const uint64_t xh = umma_desc_sw128(st + 2 * kTcABytes), xl = umma_desc_sw128(st + 2 * kTcABytes + kTcPlane);
+#pragma unroll
+        for (int ks = 0; ks < 4; ks++) {
+          const uint64_t ko = (uint64_t)(ks * 2);  // 32 B per 16-wide k step, in 16-byte units
+          const uint32_t acc = (i | ks) != 0;
+          tc_mma(tmem, ah + ko, xh + ko, acc);          // D1 += A_hi X_hi
+          tc_mma(tmem + kTcBN, ah + ko, xl + ko, acc);  // D2 += A_hi (X_lo 2^8)
+          tc_mma(tmem + kTcBN, al + ko, xh + ko, 1u);   // D2 += A_lo X_hi
+        }
+        issued = true;
+        tc_commit_pair(&empty[s]);
+        TC_MARK(4, i);
+      }
+      // the accumulators are complete (or, after an abort, every MMA issued is)
+      if (issued) tc_commit_pair(dfull);
+    }
+  } else if (warp >= kDqWarp0) {
+    // dequant: thread dt handles Q4 tile j (16 threads per tile), two lanes of it,
+    // ordered so that a warp's 4-byte stores hit 32 distinct banks
+    const uint32_t dt = threadIdx.x - kDqWarp0 * 32;
+    const uint32_t j = dt >> 4, p = j & 1;
+    for (uint32_t i = 0; i < KTS; i++) {
+      const int s = i % kTcStages;
+      if (!__all_sync(0xFFFFFFFFu, tc_wait(&full[s], (i / kTcStages) & 1, abort, a.err))) break;  // warp-uniform
+      if (dt == 0) TC_MARK(1, i);
+      const uint8_t *raw = sm + kOffRaw + s * kTcRawBytes + j * kTileBytes;
+      const uint32_t Ah = sbase + s * kTcStageBytes, Al = Ah + kTcABytes;
+      if (j < ntiles) {
+#pragma unroll
+        for (uint32_t q = 0; q < 2; q++) {
+          const uint32_t ln = (dt & 15) + 16 * (q ^ p);
+          const uint32_t g = ln >> 2, t4 = ln & 3;
+          const uint4 w = *reinterpret_cast<const uint4 *>(raw + ln * 16);
+          const uint2 sc = *reinterpret_cast<const uint2 *>(raw + 512 + g * 8);  // rows g, g+8: (blk0 | blk1 << 16)
+          uint32_t hs[2][2], ls[2][2];                                            // [row g / g+8][blk]
+          bool ok = split_scale(sc.x & 0xFFFFu, hs[0][0], ls[0][0]);
+          ok &= split_scale(sc.x >> 16, hs[0][1], ls[0][1]);
+          ok &= split_scale(sc.y & 0xFFFFu, hs[1][0], ls[1][0]);
+          ok &= split_scale(sc.y >> 16, hs[1][1], ls[1][1]);
+          if (!ok) atomicOr(a.err, DEV_ERR_SCALE_RANGE);
+          const uint32_t m0 = j * 16 + g;  // rows m0 (tile row g) and m0 + 8; both have m % 8 == g
+          const uint32_t o_r0 = (m0 >> 3) * 1024 + g * 128 + 4 * t4, o_r1 = o_r0 + 1024;
+          const uint32_t ws[4] = {w.x, w.y, w.z, w.w};  // (blk, ch) = (0,0) (0,1) (1,0) (1,1)
+#pragma unroll
+          for (int wi = 0; wi < 4; wi++) {
+            const int blk = wi >> 1;
+            uint32_t f[4];
+            dequant_q4_word(ws[wi], f);  // exact q-8 pairs: (g, k) (g+8, k) (g, k+8) (g+8, k+8), k = kb + 2 t4
+            const uint32_t c = blk * 4 + (wi & 1) * 2;  // 16-byte chunk of k = kb .. kb+7
+            const uint32_t o0 = (c ^ g) << 4, o1 = ((c + 1) ^ g) << 4;
+            st_shared_u32(Ah + o_r0 + o0, hmul2_u32(f[0], hs[0][blk]));
+            st_shared_u32(Ah + o_r1 + o0, hmul2_u32(f[1], hs[1][blk]));
+            st_shared_u32(Ah + o_r0 + o1, hmul2_u32(f[2], hs[0][blk]));
+            st_shared_u32(Ah + o_r1 + o1, hmul2_u32(f[3], hs[1][blk]));
+            st_shared_u32(Al + o_r0 + o0, hmul2_u32(f[0], ls[0][blk]));
+            st_shared_u32(Al + o_r1 + o0, hmul2_u32(f[1], ls[1][blk]));
+            st_shared_u32(Al + o_r0 + o1, hmul2_u32(f[2], ls[0][blk]));
+            st_shared_u32(Al + o_r1 + o1, hmul2_u32(f[3], ls[1][blk]));
+          }
+        }
+      }
+      fence_proxy_async();  // generic-proxy stores -> visible to the tensor core
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(ready_l + s * 8);  // one arrival per warp, at the leader
+      if (dt == 0) TC_MARK(2, i);
+    }
+  } else {
+    // epilogue: waits for the accumulators, then 2 chunks of 32 token columns
+    const uint32_t quad = warp & 3, cg = warp >> 2;
+    const uint32_t m = quad * 32 + lane;  // row within the CTA's tile = TMEM lane
+    const uint32_t jt = m >> 4, i16 = m & 15;
+    bool ok = __all_sync(0xFFFFFFFFu, tc_wait(dfull, 0, abort, a.err));
+    tc_fence_after();
+    if (threadIdx.x == 0) TC_MARK(5, 0);
+    ok = __all_sync(0xFFFFFFFFu, ok && !*abort);
+    const uint32_t row = rt0 * 16 + m;
+    const bool row_ok = jt < ntiles;
+    const uint32_t tok0 = nt * kTcBN + cg * 64;
+    const size_t Mr = a.M, ntok = (size_t)L.nt_tiles * kTcBN;
+    // Y (or the act of the gate|up epilogue) for 32 tokens from tok; whole warp
+    auto store_out = [&](const float (&y)[32], uint32_t tok) {
+      if (EPI == EPI_STORE) {
+        if (row_ok) {
+#pragma unroll
+          for (int i = 0; i < 32; i++)
+            if (tok + i < a.N) a.Y[(size_t)(tok + i) * Mr + row] = y[i];
+        }
+      } else {
+        // interleaved gate|up tiles: tile row i16 < 8 is gate row (rt0+jt)*8 + i16, its
+        // up partner sits 8 lanes higher in the same warp
+        const bool gate = i16 < 8 && row_ok;
+        const uint32_t Mo = a.M / 2, r = (rt0 + jt) * 8 + (i16 & 7);
+#pragma unroll
+        for (int i = 0; i < 32; i++) {
+          const float u = __shfl_xor_sync(0xFFFFFFFFu, y[i], 8);
+          if (gate && tok + i < a.N) a.Y[(size_t)(tok + i) * Mo + r] = gelu_mul(y[i], u);
+        }
+      }
+    };
+    if (ok) {
+#pragma unroll 1
+      for (int ch = 0; ch < 2; ch++) {
+        const uint32_t taddr = tmem + ((quad * 32u) << 16) + cg * 64 + ch * 32;
+        uint32_t v1[32], v2[32];
+        tc_ld32(taddr, v1);
+        tc_ld32(taddr + kTcBN, v2);
+        tc_wait_ld();
+        float y[32];
+#pragma unroll
+        for (int i = 0; i < 32; i++)
+          y[i] = __fmaf_rn(__uint_as_float(v2[i]), 1.0f / 65536.f, __fmul_rn(__uint_as_float(v1[i]), 1.0f / 256.f));
+        if (L.sk == 1) {
+          store_out(y, tok0 + ch * 32);
+        } else if (row_ok) {  // partial -> workspace [sk][token][row]
+          float *wsk = L.ws + (size_t)sk * ntok * Mr;
+#pragma unroll
+          for (int i = 0; i < 32; i++) wsk[(size_t)(tok0 + ch * 32 + i) * Mr + row] = y[i];
+        }
+      }
+    }
+    if (L.sk > 1) {
+      // the last split of this tile to finish adds all partials in split order
+      __threadfence();
+      epi_sync();
+      if (threadIdx.x == 0) {
+        const uint32_t tile = (mp * 2 + rank) * L.nt_tiles + nt;
+        const uint32_t prev = atomicAdd(&L.counters[tile], 1u);
+        *is_last = prev == L.sk - 1;
+        if (prev == L.sk - 1) L.counters[tile] = 0u;  // ready for the next launch
+      }
+      epi_sync();
+      if (ok && *is_last) {
+        __threadfence();
+#pragma unroll 1
+        for (int ch = 0; ch < 2; ch++) {
+          float y[32];
+#pragma unroll
+          for (int i = 0; i < 32; i++) {
+            const size_t o = (size_t)(tok0 + ch * 32 + i) * Mr + row;
+            float acc = row_ok ? L.ws[o] : 0.f;
+            for (uint32_t s2 = 1; s2 < L.sk; s2++)
+              if (row_ok) acc = __fadd_rn(acc, L.ws[(size_t)s2 * ntok * Mr + o]);
+            y[i] = acc;
+          }
+          store_out(y, tok0 + ch * 32);
+        }
+      }
+    }
+    if (threadIdx.x == 0) TC_MARK(6, 0);
+  }
+
+  __syncwarp();
+  tc_fence_before();
+  cluster_sync_all();  // both CTAs done with TMEM and with each other's shared memory
+  if (warp == kProdWarp) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
+  }
+}
+
+// ---------------------------------------------------------------------------
+// The Q4 tile array [M/16][K/64][576 B] as a 3-D tensor of u64: x = 72 words of a
+// tile, y = k tile (stride 576 B), z = row tile (stride K/64 * 576 B); box 72 x 1 x 8.
+static cudaError_t encode_tile_map(CUtensorMap *map, const uint8_t *tiles, uint32_t M, uint32_t K) {
+  static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
+  if (!encode) {
+    void *fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
+    if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || !fn) return e != cudaSuccess ? e : cudaErrorNotSupported;
+    encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  }
+  const cuuint64_t dims[3] = {kTileBytes / 8, K / kTcBK, M / 16};
+  const cuuint64_t strides[2] = {kTileBytes, (cuuint64_t)(K / kTcBK) * kTileBytes};
+  const cuuint32_t box[3] = {kTileBytes / 8, 1, 8}, estr[3] = {1, 1, 1};
+  CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT64, 3, const_cast<uint8_t *>(tiles), dims, strides, box, estr,
+                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
+// split-K factor: more CTA pairs when the rows alone leave SM pairs idle, choosing
+// the factor with the fewest waves x k tiles per split; each split keeps >= 8 k tiles
+static uint32_t choose_split(uint32_t pairs, uint32_t KT) {
+  const uint32_t sm_pairs = (uint32_t)num_sms() / 2;
+  if (pairs * 4 >= sm_pairs * 3) return 1;
+  uint32_t best = 1;
+  uint64_t best_cost = (uint64_t)((pairs + sm_pairs - 1) / sm_pairs) * KT;
+  for (uint32_t sk = 2; sk <= 8; sk++) {
+    if (KT % sk || KT / sk < 8) continue;
+    const uint64_t cost = (uint64_t)((pairs * sk + sm_pairs - 1) / sm_pairs) * (KT / sk);
+    if (cost < best_cost) best = sk, best_cost = cost;
+  }
+  return best;
+}
+static uint32_t gemm_split(uint32_t N, uint32_t M, uint32_t K) {
+  const uint32_t nt = (N + kTcBN - 1) / kTcBN, mp = (M / 16 + 15) / 16;
+  const uint32_t sk = choose_split(nt * mp, K / kTcBK);
+  return (sk > 1 && mp * 2 * nt > kMaxCounters) ? 1 : sk;
+}
+static size_t xs_region(uint32_t N, uint32_t K) { return (tc_split_x_bytes(N, K) + 255) & ~(size_t)255; }
+
+size_t tc_split_x_bytes(uint32_t N, uint32_t K) {
+  return (size_t)((N + kTcBN - 1) / kTcBN) * (K / kTcBK) * 2 * kTcXBytes;
+}
+// enough for any token count up to N (fewer tokens can choose a larger split)
+size_t tc_gemm_scratch_bytes(uint32_t N, uint32_t M, uint32_t K) {
+  size_t ws = 0;
+  for (uint32_t nt = 1; nt <= (N + kTcBN - 1) / kTcBN; nt++) {
+    const uint32_t sk = gemm_split(nt * kTcBN, M, K);
+    if (sk > 1) ws = std::max(ws, (size_t)sk * nt * kTcBN * M * sizeof(float));
+  }
+  return kCounterBytes + xs_region(N, K) + ws;
+}
+
+cudaError_t launch_tc_split_x(const float *X, uint32_t N, uint32_t K, uint8_t *xs, cudaStream_t s) {
+  if (K % 64 || N == 0) return N == 0 ? cudaSuccess : cudaErrorInvalidValue;
+  const uint32_t ntok = (N + kTcBN - 1) / kTcBN * kTcBN;
+  const uint64_t total = (uint64_t)ntok * (K / 8);
+  const uint64_t cap = (uint64_t)num_sms() * 8;
+  const uint64_t blocks = (total + 255) / 256;
+  tc_split_x_kernel<<<(unsigned)(blocks < cap ? blocks : cap), 256, 0, s>>>(X, N, K, ntok, xs);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_batch_gemm_tc(const TcGemmArgs &a, uint8_t *scratch, cudaStream_t s) {
+  if (a.M % 16 || a.K % kTcBK || a.N == 0) return a.N == 0 ? cudaSuccess : cudaErrorInvalidValue;
+  if (((uintptr_t)a.xs & 15) || ((uintptr_t)a.tiles & 15) || ((uintptr_t)scratch & 255))
+    return cudaErrorInvalidValue;  // copy alignment
+  alignas(64) CUtensorMap wmap;
+  cudaError_t me = encode_tile_map(&wmap, a.tiles, a.M, a.K);
+  if (me != cudaSuccess) return me;
+  const uint32_t nt = (a.N + kTcBN - 1) / kTcBN, mp = (a.M / 16 + 15) / 16;
+  TcLaunch L{};
+  L.sk = gemm_split(a.N, a.M, a.K);
+  L.nt_tiles = nt;
+  L.counters = reinterpret_cast<uint32_t *>(scratch);
+  L.ws = reinterpret_cast<float *>(scratch + kCounterBytes + xs_region(a.N, a.K));
+  const dim3 grid(2, nt, mp * L.sk);  // clusters of 2: 256 rows x 256 tokens, per split
+  if (a.epi == EPI_STORE) {
+    cudaError_t e = cudaFuncSetAttribute(batch_gemm_tc_kernel<EPI_STORE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)kTcSmemBytes);
+    if (e != cudaSuccess) return e;
+    batch_gemm_tc_kernel<EPI_STORE><<<grid, kTcThreads, kTcSmemBytes, s>>>(a, L, wmap);
+  } else {
+    cudaError_t e = cudaFuncSetAttribute(batch_gemm_tc_kernel<EPI_GELU_MUL>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kTcSmemBytes);
+    if (e != cudaSuccess) return e;
+    batch_gemm_tc_kernel<EPI_GELU_MUL><<<grid, kTcThreads, kTcSmemBytes, s>>>(a, L, wmap);
+  }
+  return cudaGetLastError();
+}
+
+cudaError_t launch_batch_gemm_q4_tc(const BatchGemmArgs &g, uint8_t *scratch, uint32_t *err, cudaStream_t s) {
+  uint8_t *xs = scratch + kCounterBytes;
+  cudaError_t e = launch_tc_split_x(g.X, g.N, g.K, xs, s);
+  if (e != cudaSuccess) return e;
+  return launch_batch_gemm_tc(TcGemmArgs{g.tiles, xs, g.Y, g.M, g.K, g.N, g.epi, err}, scratch, s);
+}
+
+}  // namespace ch
+
+#ifdef CH_PHASE_TRACE
+extern "C" int ch_tc_trace_copy(long long *host, size_t count) {
+  if (count > sizeof(ch::g_tc_trace) / 8) count = sizeof(ch::g_tc_trace) / 8;
+  return cudaMemcpyFromSymbol(host, ch::g_tc_trace, count * 8) == cudaSuccess ? 0 : -3;
+}
+#endif

@@ -56,7 +56,8 @@ void ch_ctx_destroy(ch_ctx *ctx);
 int ch_ctx_synchronize(ch_ctx *ctx);
 void *ch_ctx_stream(ch_ctx *ctx); /* cudaStream_t */
 /* Reads and clears the device status word (bit 0 bulk-copy wait timeout,
- * bit 1 bad slot, bit 2 bad slot-list entry, bit 3 peer wait timeout). */
+ * bit 1 bad slot, bit 2 bad slot-list entry, bit 3 peer wait timeout, bit 4 a Q4
+ * block scale with |d| >= 16, outside the tensor-core GEMM's exact range). */
 int ch_ctx_device_status(ch_ctx *ctx, uint32_t *flags);
 
 /* ------------------------------------------------------------------------
@@ -215,11 +216,22 @@ int ch_decode_attention(ch_ctx *ctx, const float *qkv_dev, const float *q_norm_d
                         float eps, float scale, float *out_dev);
 /* topk_pass1/2.wgsl: softcap + top-64, value desc then lowest index */
 int ch_topk64(ch_ctx *ctx, const float *logits_dev, uint32_t vocab, uint32_t *ids_dev, float *vals_dev);
-/* batch_gemm_q4.wgsl (Y[t*rows + r]) and batch_fused_mlp_q4.wgsl on tiles */
+/* batch_gemm_q4.wgsl (Y[t*rows + r]) and batch_fused_mlp_q4.wgsl on tiles, on the
+ * tcgen05 tensor cores: each weight (q-8)*d enters exactly as two f16 operands
+ * (d split into its top 8 significant bits and the rest), the activation as an
+ * f16 hi + lo pair, f32 accumulation.  The context keeps a scratch buffer (the
+ * split activation, about 4 * n * cols bytes, plus split-K partials for short row
+ * counts), grown on first use of a larger shape. */
 int ch_batch_gemm_q4(ch_ctx *ctx, const void *tiles_dev, uint32_t rows, uint32_t cols, const float *x_dev,
                      uint32_t n_tokens, float *y_dev);
 int ch_batch_fused_mlp_q4(ch_ctx *ctx, const void *gateup_tiles_dev, uint32_t rows, uint32_t cols, const float *x_dev,
                           uint32_t n_tokens, float *act_dev);
+/* The same two GEMMs on the legacy mma.sync tensor path (no counterpart in the
+ * reference): kept as the measured baseline of the tcgen05 kernels. */
+int ch_batch_gemm_q4_mma(ch_ctx *ctx, const void *tiles_dev, uint32_t rows, uint32_t cols, const float *x_dev,
+                         uint32_t n_tokens, float *y_dev);
+int ch_batch_fused_mlp_q4_mma(ch_ctx *ctx, const void *gateup_tiles_dev, uint32_t rows, uint32_t cols,
+                              const float *x_dev, uint32_t n_tokens, float *act_dev);
 /* seeded generators (same spec as the oracle) */
 int ch_gen_q4_blocks(ch_ctx *ctx, uint32_t *blocks_dev, uint32_t rows, uint32_t cols, uint64_t tensor_seed,
                      float scale_std);
