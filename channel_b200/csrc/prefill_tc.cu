@@ -30,20 +30,30 @@
 // and one 32 KB bulk copy of its activation share, pre-split and pre-swizzled by
 // tc_split_x_kernel -- because the copy engine takes tens of cycles per request.
 //
-// Warp roles (22 warps per CTA):
-//   0-15  epilogue: after the k loop, warp w reads TMEM lanes 32*(w%4).. (a warp
-//         may touch only its quarter of the lanes) and token columns
-//         64*(w/4)..+63 of both accumulators, and stores Y (or a split-K partial)
-//   16-19 dequant: Q4 nibbles and scales (staged by TMA) -> A_hi, A_lo tiles
-//   20    producer: TMEM allocation (whole warp, both CTAs); the copies (lane 0)
-//   21    MMA issuer (lane 0 of the pair's leader CTA, rank 0)
-// Barriers: a 3-deep stage ring (full: copy bytes, per CTA; aready: one arrival
-// per dequant warp of both CTAs, at the leader; empty: tcgen05.commit multicast to
-// both) and dfull (commit multicast after the last k tile).  Arrivals at the
-// leader's barriers are release.cluster and its waits on them acquire.cluster.
-// Every wait is bounded: a wait that gives up sets the device error word and the
-// CTA's abort flag; the roles then leave their loops, the MMAs in flight are
-// waited for (bounded), both CTAs meet at a cluster barrier and TMEM is released.
+// Warp roles (19 warps per CTA):
+//   0-15  during the k loop, dequant: warp w expands Q4 tile w % 8 of the even
+//         (w < 8) or odd k tiles -- nibbles and scales (staged by TMA) -> A_hi,
+//         A_lo, stored by stmatrix straight from the mma fragment layout of the Q4
+//         tiles; two k tiles are dequantised at a time.  After the k loop, the
+//         epilogue: warp w reads TMEM lanes 32*(w%4).. (a warp may touch only its
+//         quarter of the lanes) and token columns 64*(w/4)..+63 of both
+//         accumulators, and stores Y (or a split-K partial)
+//   16    producer: TMEM allocation (whole warp, both CTAs); the activation copies
+//         (lane 0)
+//   17    MMA issuer (lane 0 of the pair's leader CTA, rank 0)
+//   18    weight producer: the Q4 tile boxes (lane 0)
+// Barriers: a 3-deep stage ring of A_hi | A_lo | X (xfull: activation copy bytes,
+// per CTA; aready: one arrival per dequant warp of the k tile in both CTAs, at the
+// leader, once its A tile is written and its CTA's activation share has landed;
+// empty: tcgen05.commit multicast to both), a 5-deep ring of Q4 tile boxes (rfull:
+// copy bytes; rempty: one arrival per dequant warp of the k tile once read), and
+// dfull (commit multicast after the last k tile).  The weight boxes run ahead of
+// the stages, so the dequant of a k tile overlaps the copy of its activation share.
+// Arrivals at the leader's barriers are release.cluster and its waits on them
+// acquire.cluster.  Every wait is bounded: a wait that gives up sets the device
+// error word and the CTA's abort flag; the roles then leave their loops, the MMAs
+// in flight are waited for (bounded), both CTAs meet at a cluster barrier and TMEM
+// is released.
 //
 // Split-K (when the rows give too few tile pairs for the SMs): the k tiles are
 // divided among SK pairs per output tile; each writes its partial to a workspace
@@ -61,15 +71,17 @@ namespace ch {
 namespace {
 constexpr int kTcBM = 128, kTcBN = 256, kTcBK = 64;      // per CTA: 128 rows; per pair: 256 tokens
 constexpr int kTcHalfN = kTcBN / 2;                       // tokens of the activation operand per CTA
-constexpr int kTcStages = 3;
+constexpr int kTcStages = 3;  // A_hi | A_lo | X stages (what the MMAs read)
+constexpr int kTcRaw = 5;     // Q4 tile boxes (what the dequant reads), a deeper ring
 constexpr uint32_t kTcABytes = kTcBM * kTcBK * 2;        // 16 KB: 128 rows x 128 B (one of A_hi, A_lo)
 constexpr uint32_t kTcPlane = kTcHalfN * kTcBK * 2;      // 16 KB: one f16 plane of 128 tokens
 constexpr uint32_t kTcXBytes = 2 * kTcPlane;             // this CTA's share: hi plane, lo plane
 constexpr uint32_t kTcRawBytes = 8 * kTileBytes;         // 8 whole Q4 tiles (nibbles + scales): one TMA box
 constexpr uint32_t kTcStageBytes = 2 * kTcABytes + kTcXBytes;  // 64 KB: A_hi | A_lo | X_hi | X_lo
-constexpr int kEpiWarps = 16, kDqWarps = 4;
-constexpr int kDqWarp0 = kEpiWarps, kProdWarp = kEpiWarps + kDqWarps, kMmaWarp = kProdWarp + 1;
-constexpr int kTcThreads = (kMmaWarp + 1) * 32;
+constexpr int kEpiWarps = 16;              // dequant during the k loop, epilogue after it
+constexpr int kDqPerTile = kEpiWarps / 2;  // warps per k tile: one Q4 tile each; even/odd k tiles alternate
+constexpr int kProdWarp = kEpiWarps, kMmaWarp = kProdWarp + 1, kRawWarp = kMmaWarp + 1;
+constexpr int kTcThreads = (kRawWarp + 1) * 32;
 constexpr int kEpiThreads = kEpiWarps * 32;
 constexpr uint32_t kTmemCols = 512;  // D1: columns 0-255, D2: 256-511
 constexpr uint32_t kCounterBytes = 16384;
@@ -78,8 +90,8 @@ constexpr uint32_t kMaxCounters = kCounterBytes / 4;
 // shared-memory map, offsets from a 1024-byte aligned base (the swizzle atoms of
 // the A and X tiles start on 1024-byte boundaries); identical in both CTAs
 constexpr uint32_t kOffRaw = kTcStages * kTcStageBytes;
-constexpr uint32_t kOffBars = kOffRaw + kTcStages * kTcRawBytes;
-constexpr uint32_t kNumBars = 3 * kTcStages + 1;
+constexpr uint32_t kOffBars = kOffRaw + kTcRaw * kTcRawBytes;
+constexpr uint32_t kNumBars = 3 * kTcStages + 1 + 2 * kTcRaw;
 constexpr uint32_t kOffMisc = kOffBars + kNumBars * 8;
 constexpr uint32_t kTcSmemUsed = kOffMisc + 16;
 static_assert(kTcStageBytes % 1024 == 0, "stage alignment");
@@ -90,11 +102,12 @@ static_assert(kTcSmemBytes <= 232448, "shared memory per CTA");
 
 // Optional pipeline timeline (trace build, -DCH_PHASE_TRACE): one role thread of the
 // leader CTA of pair 1 (token tile 0, split 0) records clock64 at each event:
-// 0 producer issued k tile, 1 dequant saw its copies land, 2 dequant published the
-// A tiles, 3 MMA started the k tile, 4 MMA issued the k tile, 5 epilogue saw the
-// accumulators complete, 6 epilogue done (warp 0).
+// 0 activation copy issued, 1 dequant began the k tile (box landed, A slot free),
+// 2 dequant published the A tiles, 3 MMA started the k tile, 4 MMA issued the k
+// tile, 5 epilogue saw the accumulators complete, 6 epilogue done (warp 0),
+// 7 dequant loaded its words and scales, 8 dequant stores issued, 9 box issued.
 #ifdef CH_PHASE_TRACE
-constexpr int kTcTraceKinds = 8, kTcTraceLen = 1024;
+constexpr int kTcTraceKinds = 10, kTcTraceLen = 1024;
 __device__ long long g_tc_trace[kTcTraceKinds * kTcTraceLen];
 #define TC_MARK(kind, idx)                                                                     \
   do {                                                                                         \
@@ -162,8 +175,11 @@ CH_DEV void tma_load_3d(void *dst, const CUtensorMap *map, int x, int y, int z, 
       "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
       : "memory");
 }
-CH_DEV void st_shared_u32(uint32_t addr, uint32_t v) {
-  asm volatile("st.shared.b32 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
+// four 8x8 b16 blocks from mma fragments; lane l gives the address of row l % 8 of block l / 8
+CH_DEV void stmatrix_x4(uint32_t addr, uint32_t r0, uint32_t r1, uint32_t r2, uint32_t r3) {
+  asm volatile("stmatrix.sync.aligned.m8n8.x4.shared.b16 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(r0), "r"(r1),
+               "r"(r2), "r"(r3)
+               : "memory");
 }
 CH_DEV uint32_t cluster_rank() {
   uint32_t r;
@@ -290,7 +306,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
   uint8_t *sm = smem_dyn + (((dyn + 1023u) & ~1023u) - dyn);
   const uint32_t sbase = smem_u32(sm);
   uint64_t *bars = reinterpret_cast<uint64_t *>(sm + kOffBars);
-  uint64_t *full = bars, *aready = bars + kTcStages, *empty = bars + 2 * kTcStages, *dfull = bars + 3 * kTcStages;
+  uint64_t *xfull = bars, *aready = bars + kTcStages, *empty = bars + 2 * kTcStages, *dfull = bars + 3 * kTcStages;
+  uint64_t *rfull = dfull + 1, *rempty = rfull + kTcRaw;
   uint32_t *misc = reinterpret_cast<uint32_t *>(sm + kOffMisc);
   uint32_t *tmem_slot = misc;
   volatile uint32_t *abort = misc + 1;
@@ -309,9 +326,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kTcStages; s++) {
-      mbar_init(&full[s], 1);
-      mbar_init(&aready[s], 2 * kDqWarps);
+      mbar_init(&xfull[s], 1);
+      mbar_init(&aready[s], 2 * kDqPerTile);
       mbar_init(&empty[s], 1);
+    }
+    for (int r = 0; r < kTcRaw; r++) {
+      mbar_init(&rfull[r], 1);
+      mbar_init(&rempty[r], kDqPerTile);
     }
     mbar_init(dfull, 1);
     *abort = 0u;
@@ -333,26 +354,37 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
       const uint8_t *xs = a.xs + ((size_t)nt * KT * 2 + rank) * kTcXBytes;  // + kt * 2 * kTcXBytes
       uint32_t i = 0;
       for (; i < KTS; i++) {
-        const uint32_t kt = kt0 + i;
         const int s = i % kTcStages;
         if (i >= (uint32_t)kTcStages && !tc_wait(&empty[s], ((i / kTcStages) - 1) & 1, abort, a.err)) break;
-        // the TMA box always lands whole (rows past M read as zeros)
-        mbar_arrive_expect_tx(&full[s], kTcRawBytes + kTcXBytes);
-        tma_load_3d(sm + kOffRaw + s * kTcRawBytes, &wmap, 0, (int)kt, (int)rt0, &full[s]);
-        bulk_g2s(sm + s * kTcStageBytes + 2 * kTcABytes, xs + (size_t)kt * 2 * kTcXBytes, kTcXBytes, &full[s]);
+        mbar_arrive_expect_tx(&xfull[s], kTcXBytes);
+        bulk_g2s(sm + s * kTcStageBytes + 2 * kTcABytes, xs + (size_t)(kt0 + i) * 2 * kTcXBytes, kTcXBytes, &xfull[s]);
         TC_MARK(0, i);
       }
       // the copies of the last issues land before the CTA may leave (normally long done)
       for (uint32_t j = i > (uint32_t)kTcStages ? i - kTcStages : 0; j < i; j++)
-        tc_wait(&full[j % kTcStages], (j / kTcStages) & 1, nullptr, a.err);
+        tc_wait(&xfull[j % kTcStages], (j / kTcStages) & 1, nullptr, a.err);
+    }
+  } else if (warp == kRawWarp) {
+    if (lane == 0) {
+      uint32_t i = 0;
+      for (; i < KTS; i++) {
+        const int r = i % kTcRaw;
+        if (i >= (uint32_t)kTcRaw && !tc_wait(&rempty[r], ((i / kTcRaw) - 1) & 1, abort, a.err)) break;
+        // the TMA box always lands whole (rows past M read as zeros)
+        mbar_arrive_expect_tx(&rfull[r], kTcRawBytes);
+        tma_load_3d(sm + kOffRaw + r * kTcRawBytes, &wmap, 0, (int)(kt0 + i), (int)rt0, &rfull[r]);
+        TC_MARK(9, i);
+      }
+      for (uint32_t j = i > (uint32_t)kTcRaw ? i - kTcRaw : 0; j < i; j++)
+        tc_wait(&rfull[j % kTcRaw], (j / kTcRaw) & 1, nullptr, a.err);
     }
   } else if (warp == kMmaWarp) {
     if (leader && lane == 0) {
       bool issued = false;
       for (uint32_t i = 0; i < KTS; i++) {
         const int s = i % kTcStages;
-        if (!tc_wait(&full[s], (i / kTcStages) & 1, abort, a.err)) break;         // own activation share landed
-        if (!tc_wait(&aready[s], (i / kTcStages) & 1, abort, a.err, true)) break;  // both CTAs' A tiles written
+        // both CTAs' A tiles written and activation shares landed
+        if (!tc_wait(&aready[s], (i / kTcStages) & 1, abort, a.err, true)) break;
         tc_fence_after();
         TC_MARK(3, i);
         const uint32_t st = sbase + s * kTcStageBytes;
@@ -373,57 +405,59 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
       // the accumulators are complete (or, after an abort, every MMA issued is)
       if (issued) tc_commit_pair(dfull);
     }
-  } else if (warp >= kDqWarp0) {
-    // dequant: thread dt handles Q4 tile j (16 threads per tile), two lanes of it,
-    // ordered so that a warp's 4-byte stores hit 32 distinct banks
-    const uint32_t dt = threadIdx.x - kDqWarp0 * 32;
-    const uint32_t j = dt >> 4, p = j & 1;
-    for (uint32_t i = 0; i < KTS; i++) {
-      const int s = i % kTcStages;
-      if (!__all_sync(0xFFFFFFFFu, tc_wait(&full[s], (i / kTcStages) & 1, abort, a.err))) break;  // warp-uniform
-      if (dt == 0) TC_MARK(1, i);
-      const uint8_t *raw = sm + kOffRaw + s * kTcRawBytes + j * kTileBytes;
+  } else if (warp < kEpiWarps) {
+    // dequant.  A Q4 tile's 32 lanes hold an mma fragment -- lane (g, t4) has rows
+    // g, g+8 at k = 2 t4, 2 t4 + 1 (+8) of each 16-wide k chunk -- so each
+    // dequantised word is one stmatrix.x4 (four 8x8 f16 blocks) per operand, with
+    // the row addresses in the 128-byte swizzle.
+    const uint32_t j = warp % kDqPerTile, par = warp / kDqPerTile;
+    const uint32_t g = lane >> 2, mi = lane >> 3, rr = lane & 7;
+    const bool mark = j == 0 && lane == 0;
+    for (uint32_t i = par; i < KTS; i += 2) {
+      const int s = i % kTcStages, r = i % kTcRaw;
+      // warp-uniform waits: the Q4 box landed, and the A slot's previous MMAs are done
+      if (!__all_sync(0xFFFFFFFFu, tc_wait(&rfull[r], (i / kTcRaw) & 1, abort, a.err))) break;
+      if (i >= (uint32_t)kTcStages &&
+          !__all_sync(0xFFFFFFFFu, tc_wait(&empty[s], ((i / kTcStages) - 1) & 1, abort, a.err)))
+        break;
+      if (mark) TC_MARK(1, i);
       const uint32_t Ah = sbase + s * kTcStageBytes, Al = Ah + kTcABytes;
       if (j < ntiles) {
+        const uint8_t *raw = sm + kOffRaw + r * kTcRawBytes + j * kTileBytes;
+        const uint4 w = *reinterpret_cast<const uint4 *>(raw + lane * 16);
+        const uint2 sc = *reinterpret_cast<const uint2 *>(raw + 512 + g * 8);  // rows g, g+8: (blk0 | blk1 << 16)
+        if (mark && (w.x | sc.x) != 0xFFFFFFFFu) TC_MARK(7, i);
+        uint32_t hs[2][2], ls[2][2];  // [row g / g+8][blk]
+        bool ok = split_scale(sc.x & 0xFFFFu, hs[0][0], ls[0][0]);
+        ok &= split_scale(sc.x >> 16, hs[0][1], ls[0][1]);
+        ok &= split_scale(sc.y & 0xFFFFu, hs[1][0], ls[1][0]);
+        ok &= split_scale(sc.y >> 16, hs[1][1], ls[1][1]);
+        if (!ok) atomicOr(a.err, DEV_ERR_SCALE_RANGE);
+        // this lane's stmatrix row address: block mi (rows +8 if mi & 1, k +8 if mi & 2), row rr
+        const uint32_t rbase = (2 * j + (mi & 1)) * 1024 + rr * 128;
+        const uint32_t ws[4] = {w.x, w.y, w.z, w.w};  // (blk, ch) = (0,0) (0,1) (1,0) (1,1)
 #pragma unroll
-        for (uint32_t q = 0; q < 2; q++) {
-          const uint32_t ln = (dt & 15) + 16 * (q ^ p);
-          const uint32_t g = ln >> 2, t4 = ln & 3;
-          const uint4 w = *reinterpret_cast<const uint4 *>(raw + ln * 16);
-          const uint2 sc = *reinterpret_cast<const uint2 *>(raw + 512 + g * 8);  // rows g, g+8: (blk0 | blk1 << 16)
-          uint32_t hs[2][2], ls[2][2];                                            // [row g / g+8][blk]
-          bool ok = split_scale(sc.x & 0xFFFFu, hs[0][0], ls[0][0]);
-          ok &= split_scale(sc.x >> 16, hs[0][1], ls[0][1]);
-          ok &= split_scale(sc.y & 0xFFFFu, hs[1][0], ls[1][0]);
-          ok &= split_scale(sc.y >> 16, hs[1][1], ls[1][1]);
-          if (!ok) atomicOr(a.err, DEV_ERR_SCALE_RANGE);
-          const uint32_t m0 = j * 16 + g;  // rows m0 (tile row g) and m0 + 8; both have m % 8 == g
-          const uint32_t o_r0 = (m0 >> 3) * 1024 + g * 128 + 4 * t4, o_r1 = o_r0 + 1024;
-          const uint32_t ws[4] = {w.x, w.y, w.z, w.w};  // (blk, ch) = (0,0) (0,1) (1,0) (1,1)
-#pragma unroll
-          for (int wi = 0; wi < 4; wi++) {
-            const int blk = wi >> 1;
-            uint32_t f[4];
-            dequant_q4_word(ws[wi], f);  // exact q-8 pairs: (g, k) (g+8, k) (g, k+8) (g+8, k+8), k = kb + 2 t4
-            const uint32_t c = blk * 4 + (wi & 1) * 2;  // 16-byte chunk of k = kb .. kb+7
-            const uint32_t o0 = (c ^ g) << 4, o1 = ((c + 1) ^ g) << 4;
-            st_shared_u32(Ah + o_r0 + o0, hmul2_u32(f[0], hs[0][blk]));
-            st_shared_u32(Ah + o_r1 + o0, hmul2_u32(f[1], hs[1][blk]));
-            st_shared_u32(Ah + o_r0 + o1, hmul2_u32(f[2], hs[0][blk]));
-            st_shared_u32(Ah + o_r1 + o1, hmul2_u32(f[3], hs[1][blk]));
-            st_shared_u32(Al + o_r0 + o0, hmul2_u32(f[0], ls[0][blk]));
-            st_shared_u32(Al + o_r1 + o0, hmul2_u32(f[1], ls[1][blk]));
-            st_shared_u32(Al + o_r0 + o1, hmul2_u32(f[2], ls[0][blk]));
-            st_shared_u32(Al + o_r1 + o1, hmul2_u32(f[3], ls[1][blk]));
-          }
+        for (int wi = 0; wi < 4; wi++) {
+          const int blk = wi >> 1;
+          uint32_t f[4];
+          dequant_q4_word(ws[wi], f);  // exact q-8 pairs: (g, k) (g+8, k) (g, k+8) (g+8, k+8), k = kb + 2 t4
+          const uint32_t chunk = blk * 4 + (wi & 1) * 2 + (mi >> 1);  // 16-byte chunk of this lane's row
+          const uint32_t off = rbase + ((chunk ^ rr) << 4);
+          stmatrix_x4(Ah + off, hmul2_u32(f[0], hs[0][blk]), hmul2_u32(f[1], hs[1][blk]), hmul2_u32(f[2], hs[0][blk]),
+                      hmul2_u32(f[3], hs[1][blk]));
+          stmatrix_x4(Al + off, hmul2_u32(f[0], ls[0][blk]), hmul2_u32(f[1], ls[1][blk]), hmul2_u32(f[2], ls[0][blk]),
+                      hmul2_u32(f[3], ls[1][blk]));
         }
       }
-      fence_proxy_async();  // generic-proxy stores -> visible to the tensor core
       __syncwarp();
+      if (lane == 0) mbar_arrive(&rempty[r]);  // the box is read
+      if (mark) TC_MARK(8, i);
+      fence_proxy_async();  // generic-proxy stores -> visible to the tensor core
+      if (!__all_sync(0xFFFFFFFFu, tc_wait(&xfull[s], (i / kTcStages) & 1, abort, a.err))) break;
       if (lane == 0) mbar_arrive_cluster(ready_l + s * 8);  // one arrival per warp, at the leader
-      if (dt == 0) TC_MARK(2, i);
+      if (mark) TC_MARK(2, i);
     }
-  } else {
+
     // epilogue: waits for the accumulators, then 2 chunks of 32 token columns
     const uint32_t quad = warp & 3, cg = warp >> 2;
     const uint32_t m = quad * 32 + lane;  // row within the CTA's tile = TMEM lane
@@ -446,13 +480,27 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
         }
       } else {
         // interleaved gate|up tiles: tile row i16 < 8 is gate row (rt0+jt)*8 + i16, its
-        // up partner sits 8 lanes higher in the same warp
-        const bool gate = i16 < 8 && row_ok;
+        // up partner sits 8 lanes higher in the same warp.  Each pair of lanes shares
+        // the 32 tokens: the gate lane takes the first 16, the up lane the last 16.
+        const bool is_gate = i16 < 8;
         const uint32_t Mo = a.M / 2, r = (rt0 + jt) * 8 + (i16 & 7);
+        float gv[16] = {}, uv[16] = {};
 #pragma unroll
         for (int i = 0; i < 32; i++) {
-          const float u = __shfl_xor_sync(0xFFFFFFFFu, y[i], 8);
-          if (gate && tok + i < a.N) a.Y[(size_t)(tok + i) * Mo + r] = gelu_mul(y[i], u);
+          const float other = __shfl_xor_sync(0xFFFFFFFFu, y[i], 8);
+          if (i < 16) {
+            gv[i] = is_gate ? y[i] : gv[i];
+            uv[i] = is_gate ? other : uv[i];
+          } else {
+            gv[i - 16] = is_gate ? gv[i - 16] : other;
+            uv[i - 16] = is_gate ? uv[i - 16] : y[i];
+          }
+        }
+        const uint32_t t1 = tok + (is_gate ? 0u : 16u);
+        if (row_ok) {
+#pragma unroll
+          for (int i = 0; i < 16; i++)
+            if (t1 + i < a.N) a.Y[(size_t)(t1 + i) * Mo + r] = gelu_mul(gv[i], uv[i]);
         }
       }
     };
