@@ -38,6 +38,28 @@ CH_DEV void block_to_fragments(const float (&v)[32], uint4 *xf_blk) {
     xf_blk[t * 2 + 1] = make_uint4(lw[0], lw[1], lw[2], lw[3]);
   }
 }
+// The same fragments built by all threads of the block: one (32-block b, lane
+// quad t) item per thread -- the 8 values of v[b*32 ..] a lane with t needs, hi and
+// lo -- instead of one whole 32-block per thread.  v may be global or shared.
+CH_DEV void build_fragments(const float *v, uint4 *xf, uint32_t K) {
+  for (uint32_t idx = threadIdx.x; idx < K / 32 * 4; idx += blockDim.x) {
+    const uint32_t b = idx >> 2, t = idx & 3;
+    const float *p = v + b * 32 + 2 * t;
+    const float2 e0 = *reinterpret_cast<const float2 *>(p), e1 = *reinterpret_cast<const float2 *>(p + 8);
+    const float2 e2 = *reinterpret_cast<const float2 *>(p + 16), e3 = *reinterpret_cast<const float2 *>(p + 24);
+    const float e[8] = {e0.x, e0.y, e1.x, e1.y, e2.x, e2.y, e3.x, e3.y};
+    uint32_t hw[4], lw[4];
+#pragma unroll
+    for (int q = 0; q < 4; q++) {
+      const __half h0 = __float2half_rn(e[2 * q]), h1 = __float2half_rn(e[2 * q + 1]);
+      hw[q] = pack_half2(h0, h1);
+      lw[q] = pack_half2(__float2half_rn(__fsub_rn(e[2 * q], __half2float(h0))),
+                         __float2half_rn(__fsub_rn(e[2 * q + 1], __half2float(h1))));
+    }
+    xf[b * 8 + t * 2 + 0] = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+    xf[b * 8 + t * 2 + 1] = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+  }
+}
 CH_DEV void load32(const float *p, float (&v)[32]) {
   const float4 *q = reinterpret_cast<const float4 *>(p);
 #pragma unroll

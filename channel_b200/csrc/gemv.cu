@@ -18,6 +18,8 @@
 // (fixed order) by the last-arriving warp.  The input prologue fuses the
 // reference's rmsnorm / add_rmsnorm passes (add_rmsnorm.wgsl:15-51) so no
 // separate norm kernel runs on the decode path.
+#include <cmath>
+
 #include "common.cuh"
 #include "core.cuh"
 #include "kernels.cuh"
@@ -25,9 +27,16 @@
 namespace ch {
 
 namespace {
-constexpr int NW = 16;   // consumer warps per CTA (each self-feeds its own stages)
-constexpr int SPW = 2;   // stages per warp
-constexpr int CT = 8;    // tiles per stage (4608 B per bulk copy)
+#ifndef CH_GEMV_SPW
+#define CH_GEMV_SPW 2
+#endif
+#ifndef CH_GEMV_CT
+#define CH_GEMV_CT 8
+#endif
+constexpr int NW = 16;           // consumer warps per CTA (each self-feeds its own stages)
+constexpr int SPW = CH_GEMV_SPW;  // stages per warp
+constexpr int CT = CH_GEMV_CT;    // tiles per stage (8: 4608 B per bulk copy)
+static_assert(CT % 2 == 0, "the unrolled stage loop consumes tiles in pairs");
 constexpr int kStageBytes = CT * kTileBytes;
 }  // namespace
 
@@ -66,11 +75,7 @@ template <int PRO>
 CH_DEV void prologue(const GemvArgs &a, float *vec, uint4 *xf, float *red) {
   const uint32_t K = a.K, nb = K / 32;
   if (PRO == PRO_NONE) {
-    for (uint32_t b = threadIdx.x; b < nb; b += blockDim.x) {
-      float v[32];
-      load32(a.x + b * 32, v);
-      block_to_fragments(v, xf + b * 8);
-    }
+    build_fragments(a.x, xf, K);
     return;
   }
   const bool writer = (blockIdx.x == 0);
@@ -113,15 +118,13 @@ CH_DEV void prologue(const GemvArgs &a, float *vec, uint4 *xf, float *red) {
   }
   ss = block_sum(ss, red);
   const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)K), a.eps)));
-  for (uint32_t b = threadIdx.x; b < nb; b += blockDim.x) {
-    float v[32], w[32];
-    load32(vec + b * 32, v);
-    load32(a.norm_w + b * 32, w);
-#pragma unroll
-    for (int e = 0; e < 32; e++) v[e] = __fmul_rn(__fmul_rn(v[e], inv), w[e]);
-    if (writer && a.normed_out) store32(a.normed_out + b * 32, v);
-    block_to_fragments(v, xf + b * 8);
+  for (uint32_t i = threadIdx.x; i < K; i += blockDim.x) {
+    const float v = __fmul_rn(__fmul_rn(vec[i], inv), a.norm_w[i]);
+    vec[i] = v;
+    if (writer && a.normed_out) a.normed_out[i] = v;
   }
+  __syncthreads();
+  build_fragments(vec, xf, K);
 }
 
 template <int FMT, int EPI, int PRO>
@@ -133,6 +136,7 @@ __global__ void __launch_bounds__(NW * 32, 1) gemv_kernel(const GemvArgs a) {
   uint4 *xf = xzero + 1;
   float *vec = reinterpret_cast<float *>(xf + (a.K / 32) * 8);
   __shared__ float red[32];
+  __shared__ float cpart[NW][2][16];  // CTA-local mode: partial row-tile sums, [warp][first/last segment][row]
 
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int g = lane >> 2, t = lane & 3;
@@ -140,7 +144,16 @@ __global__ void __launch_bounds__(NW * 32, 1) gemv_kernel(const GemvArgs a) {
   const uint64_t gw = (uint64_t)blockIdx.x * NW + warp;
   const uint64_t KT = a.k_tiles;
   const uint64_t T = (uint64_t)a.row_tiles * KT;
-  const uint64_t tb = range_begin(T, gw, GW), te = range_begin(T, gw + 1, GW);
+  // Global stream-K: an even split of all tiles over every warp of the grid (a warp's
+  // range may cut row tiles, whose partial sums the last contributor adds through
+  // global memory).  CTA-local (a.cta_rows): each CTA takes whole row tiles and
+  // splits their tiles evenly over its warps; cut row tiles are added up in shared
+  // memory after one CTA barrier.
+  const bool local = a.cta_rows != 0;
+  const uint64_t cr0 = range_begin(a.row_tiles, blockIdx.x, gridDim.x) * KT;  // this CTA's tiles (local)
+  const uint64_t CTn = range_begin(a.row_tiles, blockIdx.x + 1, gridDim.x) * KT - cr0;
+  const uint64_t tb = local ? cr0 + range_begin(CTn, warp, NW) : range_begin(T, gw, GW);
+  const uint64_t te = local ? cr0 + range_begin(CTn, warp + 1, NW) : range_begin(T, gw + 1, GW);
   const uint32_t nchunks = (uint32_t)((te - tb + CT - 1) / CT);
   uint8_t *my_stages = stages + (size_t)warp * SPW * kStageBytes;
   uint64_t *my_bars = bars + warp * SPW;
@@ -180,6 +193,11 @@ __global__ void __launch_bounds__(NW * 32, 1) gemv_kernel(const GemvArgs a) {
     const bool full = (kb == 0 && ke == (uint32_t)KT);
     if (full) {
       if (t == 0) epilogue<EPI>(a.y, (uint32_t)frt, g, acc0, acc1);
+    } else if (local) {
+      if (t == 0) {
+        cpart[warp][first_seg ? 0 : 1][g] = acc0;
+        cpart[warp][first_seg ? 0 : 1][g + 8] = acc1;
+      }
     } else {
       const int slot = first_seg ? 0 : 1;
       if (t == 0) {
@@ -273,12 +291,29 @@ __global__ void __launch_bounds__(NW * 32, 1) gemv_kernel(const GemvArgs a) {
     // drain the copies this warp still has in flight (chunks failed_at .. +SPW-1), bounded
     for (uint32_t j = failed_at + 1; j < nchunks && j < failed_at + SPW; j++)
       mbar_wait_bounded(&my_bars[j % SPW], (j / SPW) & 1, nullptr, 100000000ull);
-    return;
-  }
-  if (cur_rt != ~0ull) {
+  } else if (cur_rt != ~0ull) {
     const uint32_t ke = (uint32_t)(te - cur_rt * KT);
     flush(cur_rt, kt_begin, ke);
   }
+  if (!local) return;
+  __syncthreads();
+  if (!__all_sync(0xffffffffu, ok)) return;  // the device error word already records the failure
+  // The warp whose range holds the last tile of a cut row tile adds the partials of
+  // every warp that touched it, in warp order (slot 0 = that warp's first segment,
+  // slot 1 = its last).  Only a warp's first segment can start inside a row tile, so
+  // the combiner is the warp whose range starts inside row tile r and reaches its end.
+  if (te == tb || tb % KT == 0 || te < (tb / KT + 1) * KT) return;
+  const uint64_t frt = tb / KT, lo = frt * KT - cr0;
+  const uint32_t w_first = (uint32_t)warp_of(lo, CTn, NW);
+  float v0 = 0.f, v1 = 0.f;
+  for (uint32_t w = w_first; w <= (uint32_t)warp; w++) {
+    const uint64_t b = range_begin(CTn, w, NW);
+    if (range_begin(CTn, w + 1, NW) == b) continue;
+    const int sl = (b >= lo) ? 0 : 1;
+    v0 = __fadd_rn(v0, cpart[w][sl][g]);
+    v1 = __fadd_rn(v1, cpart[w][sl][g + 8]);
+  }
+  if (t == 0) epilogue<EPI>(a.y, (uint32_t)frt, g, v0, v1);
 }
 
 template <int FMT, int EPI, int PRO>
@@ -305,10 +340,16 @@ static cudaError_t launch_gemv_t(const GemvArgs &a, int grid, cudaStream_t s, bo
   return cudaLaunchKernelEx(&cfg, gemv_kernel<FMT, EPI, PRO>, a);
 }
 
-cudaError_t launch_gemv(const GemvPlan &p, const GemvArgs &a, cudaStream_t s, bool pdl) {
-  if (a.K % 64 != 0 && p.fmt == FMT_Q4) return cudaErrorInvalidValue;
-  if (a.K % 32 != 0) return cudaErrorInvalidValue;
+cudaError_t launch_gemv(const GemvPlan &p, const GemvArgs &a0, cudaStream_t s, bool pdl) {
+  if (a0.K % 64 != 0 && p.fmt == FMT_Q4) return cudaErrorInvalidValue;
+  if (a0.K % 32 != 0) return cudaErrorInvalidValue;
   int grid = p.grid > 0 ? p.grid : gemv_default_grid();
+  // Whole row tiles per CTA (stream-K over its warps, cut rows added in shared memory)
+  // when that keeps the CTAs within 10% of an even share -- e.g. the 1920 row tiles
+  // of the 12B gate|up matrix on 148 CTAs; otherwise the grid-wide stream-K split.
+  GemvArgs a = a0;
+  const double per_cta = (double)a.row_tiles / grid;
+  a.cta_rows = per_cta >= 1.0 && std::ceil(per_cta) <= 1.1 * per_cta;
 #define CH_GEMV_CASE(F, E, P) \
   if (p.fmt == F && p.epi == E && p.pro == P) return launch_gemv_t<F, E, P>(a, grid, s, pdl);
   CH_GEMV_CASE(FMT_Q4, EPI_STORE, PRO_NONE)

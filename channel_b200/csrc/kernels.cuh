@@ -41,6 +41,7 @@ struct GemvArgs {
   float *partial = nullptr;     // stream-K partials [grid*warps][2][16]
   uint32_t *counters = nullptr; // per row tile, zero between launches
   uint32_t *err = nullptr;
+  uint32_t cta_rows = 0;         // set by launch_gemv: CTAs take whole row tiles (shared-memory combine)
 };
 
 struct GemvPlan {

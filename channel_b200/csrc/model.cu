@@ -1574,7 +1574,9 @@ static int op_gemv(ch_ctx *c, int fmt, int epi, const void *tiles, uint32_t rows
   a.partial = c->gemv_partial;
   a.counters = c->gemv_counters;
   a.err = c->err;
-  CH_CUDA(launch_gemv(p, a, c->stream, false));
+  // programmatic dependent launch: the weight stream starts while the previous
+  // kernel on the stream finishes; x and the scratch are read after it completes
+  CH_CUDA(launch_gemv(p, a, c->stream, true));
   return CH_OK;
 }
 extern "C" int ch_gemv_q4(ch_ctx *c, const void *tiles, uint32_t rows, uint32_t cols, const float *x, float *y) {
