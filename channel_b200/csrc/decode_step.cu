@@ -427,7 +427,21 @@ CH_DEV void gemv_prologue(const Phase &p, const MegaArgs &a, const SmemLayout &L
 #pragma unroll
     for (int e = 0; e < 8; e++) r[e] = 0.f;
     if (on) {
-      ld_pair_rot(S.s0, tid, r);
+      if (p.nsum > 1) {
+        // row-parallel producer: every rank's partial vector, added in rank order (the
+        // same sums on every rank); through L2, since this CTA's L1 may hold last step's
+        const float *q = p.r_in.direct + (tid >> 2) * 32 + (tid & 3u) * 2;
+        for (uint32_t rk = 0; rk < p.nsum; rk++, q += K) {
+#pragma unroll
+          for (int g = 0; g < 4; g++) {
+            const float2 v = __ldcg(reinterpret_cast<const float2 *>(q + 8 * g));
+            r[2 * g] = rk ? __fadd_rn(r[2 * g], v.x) : v.x;
+            r[2 * g + 1] = rk ? __fadd_rn(r[2 * g + 1], v.y) : v.y;
+          }
+        }
+      } else {
+        ld_pair_rot(S.s0, tid, r);
+      }
       ld_pair_rot(S.s1, tid, x);
       if (p.post_w) ld_pair_rot(S.s2, tid, w);
     }
@@ -608,10 +622,11 @@ CH_DEV AttnItem attn_item(const MegaArgs &a, const StepParams &sp, uint32_t is_s
 }
 
 // attention output elements (j, j+1) of this rank's heads as B fragments of the
-// o-projection input: local buffer, or (tensor parallel) every rank's copy at the
-// rank's global head offset
+// o-projection input: local buffer (one GPU, or tensor parallel with a row-parallel o
+// projection reading this rank's heads only), or every rank's copy at the rank's
+// global head offset
 CH_DEV void attn_out_pair(const MegaArgs &a, uint32_t *frag, uint32_t j, float v0, float v1) {
-  if (a.world <= 1) {
+  if (a.world <= 1 || a.attn_local) {
     store_frag_pair(frag, j, v0, v1);
     return;
   }
@@ -1142,7 +1157,7 @@ CH_DEV void post_copies(const Phase &p, const MegaArgs &a, const StepParams &sp,
     GemvStage S(L.u, p.K, p.pm);
     if (p.pm == PM_DIRECT) stage_copy(L, S.s0, p.x_in, p.K * 4);
     if (p.pm == PM_ADD_NORM || p.pm == PM_GELU) {
-      stage_copy(L, S.s0, p.r_in.direct, p.K * 4);  // act mode: K act values
+      if (p.nsum <= 1) stage_copy(L, S.s0, p.r_in.direct, p.K * 4);  // act mode: K act values
       stage_copy(L, S.part, p.r_in.partial, gridDim.x * 32 * 4);
     }
   } else if (p.kind == PH_ATTN) {

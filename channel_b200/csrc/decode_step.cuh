@@ -47,6 +47,9 @@ struct alignas(16) Phase {
   // barrier after this phase: cross = 1 when other ranks read its outputs (tensor
   // parallel); gidx = number of cross-rank barriers up to and including this one
   uint32_t cross, gidx;
+  // PM_ADD_NORM input: nsum > 1 = r_in.direct holds nsum partial vectors of K floats
+  // (one per rank, row-parallel GEMV), added in rank order by the prologue
+  uint32_t nsum;
   // GEMV
   const uint8_t *tiles;
   uint32_t row_tiles, k_tiles, K, vocab, vocab0;
@@ -95,6 +98,7 @@ struct MegaArgs {
   // tensor parallel (world > 1): every rank's exchange arena, mapped into this process
   uint32_t world, rank;
   uint32_t attn_q0;            // global index of this rank's first q head
+  uint32_t attn_local;         // tensor parallel: the attention output stays on this rank (row-parallel o)
   uint8_t *arena[kMaxWorld];   // arena[rank] is this rank's own
   uint64_t *xcand;             // this rank's [world][64] top-64 candidates of every rank (in its arena)
 };

@@ -479,10 +479,13 @@ cudaError_t launch_repack_q8(const uint32_t *src, uint32_t rows, uint32_t cols, 
 // ---------------------------------------------------------------------------
 // seeded synthetic tensors (same spec as the oracle's or_gen_*)
 // blocks [blk0, blk0 + nblocks) of a tensor's block stream (a row range of the matrix)
-__global__ void gen_q4_kernel(uint32_t *dst, uint64_t blk0, uint64_t nblocks, uint64_t tseed, float scale_std) {
+// block i of the output is global block blk0 + i, or with a column range (nbl > 0)
+// global block (i / nbl) * nbf + cb0 + i % nbl: blocks cb0 .. cb0+nbl of rows of nbf
+__global__ void gen_q4_kernel(uint32_t *dst, uint64_t blk0, uint64_t nblocks, uint64_t tseed, float scale_std,
+                              uint64_t nbf = 0, uint64_t cb0 = 0, uint64_t nbl = 0) {
   for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < nblocks;
        i += (uint64_t)gridDim.x * blockDim.x) {
-    const uint64_t blk = blk0 + i;
+    const uint64_t blk = nbl ? (i / nbl) * nbf + cb0 + i % nbl : blk0 + i;
     uint64_t ha = hash3(tseed, 0, blk * 2), hb = hash3(tseed, 0, blk * 2 + 1);
     float z = gen_normal(tseed, 1, blk);
     float d = __fmul_rn(fabsf(z), scale_std);
@@ -563,6 +566,13 @@ cudaError_t launch_gen_q4_rows(uint32_t *dst, uint32_t row0, uint32_t rows, uint
                                float scale_std, cudaStream_t s) {
   const uint64_t nb = (uint64_t)rows * (cols / 32), b0 = (uint64_t)row0 * (cols / 32);
   gen_q4_kernel<<<grid_for(nb, 256), 256, 0, s>>>(dst, b0, nb, tseed, scale_std);
+  return cudaGetLastError();
+}
+cudaError_t launch_gen_q4_cols(uint32_t *dst, uint32_t rows, uint32_t cols, uint32_t col0, uint32_t ncols,
+                               uint64_t tseed, float scale_std, cudaStream_t s) {
+  if (col0 % 32 || ncols % 32 || col0 + ncols > cols) return cudaErrorInvalidValue;
+  const uint64_t nbl = ncols / 32, nb = (uint64_t)rows * nbl;
+  gen_q4_kernel<<<grid_for(nb, 256), 256, 0, s>>>(dst, 0, nb, tseed, scale_std, cols / 32, col0 / 32, nbl);
   return cudaGetLastError();
 }
 cudaError_t launch_gen_bf16(uint16_t *dst, size_t n, uint64_t tseed, float mean, float std, cudaStream_t s) {

@@ -64,6 +64,9 @@ cudaError_t launch_gen_q4_blocks(uint32_t *dst, uint32_t rows, uint32_t cols, ui
 // rows [row0, row0 + rows) of the same generated matrix (a tensor-parallel shard)
 cudaError_t launch_gen_q4_rows(uint32_t *dst, uint32_t row0, uint32_t rows, uint32_t cols, uint64_t tseed,
                                float scale_std, cudaStream_t s);
+// columns [col0, col0 + ncols) of all rows of the same seeded matrix (row-parallel shards)
+cudaError_t launch_gen_q4_cols(uint32_t *dst, uint32_t rows, uint32_t cols, uint32_t col0, uint32_t ncols,
+                               uint64_t tseed, float scale_std, cudaStream_t s);
 cudaError_t launch_gen_bf16(uint16_t *dst, size_t n, uint64_t tseed, float mean, float std, cudaStream_t s);
 cudaError_t launch_gen_f32(float *dst, size_t n, uint64_t tseed, float mean, float std, cudaStream_t s);
 cudaError_t launch_bf16_to_f32(const uint16_t *src, float *dst, size_t n, cudaStream_t s);

@@ -168,11 +168,11 @@ struct ch_model {
   // tensor parallel: this process holds shard `rank` of `world` (1 = the whole model).
   // Local sizes: q / kv heads, o and down output rows, gate and up rows, vocab rows.
   uint32_t rank = 0, world = 1;
-  uint32_t nq_l = 0, nkv_l = 0, qd_l = 0, kvd_l = 0, Ho = 0, Il = 0, Vl = 0;
+  uint32_t nq_l = 0, nkv_l = 0, qd_l = 0, kvd_l = 0, Il = 0, Vl = 0;
   uint8_t *arena = nullptr;                // exchange arena (CUDA IPC shared): gathered vectors + arrivals
   uint8_t *peer_arena[kMaxWorld] = {};     // every rank's arena mapped here (peer_arena[rank] = arena)
   bool peers_ready = false;
-  size_t off_arrive = 0, off_o = 0, off_down = 0, off_act = 0, off_attn = 0, off_cand = 0, arena_bytes = 0;
+  size_t off_arrive = 0, off_o = 0, off_down = 0, off_cand = 0, arena_bytes = 0;
   StepParams *pplan = nullptr;             // tensor-parallel prefill: forced-token plan
   uint32_t *pplan_lists = nullptr;
   std::vector<DevLayer> layers;
@@ -324,7 +324,6 @@ static int alloc_model_buffers(ch_model *m) {
   m->nkv_l = m->nkv / P;
   m->qd_l = m->nq_l * m->D;
   m->kvd_l = m->nkv_l * m->D;
-  m->Ho = m->H / P;
   m->Il = m->I / P;
   m->Vl = m->V / P;
   m->layers.resize(m->L);
@@ -332,9 +331,9 @@ static int alloc_model_buffers(ch_model *m) {
     DevLayer &dl = m->layers[l];
     dl.full = c.layer_types[l] != 0;
     CH_TRY(dmalloc(&dl.qkv, q4_tile_bytes(m->qd_l + 2 * m->kvd_l, m->H)));
-    CH_TRY(dmalloc(&dl.o, q4_tile_bytes(m->Ho, m->qd)));
+    CH_TRY(dmalloc(&dl.o, q4_tile_bytes(m->H, m->qd_l)));  // row-parallel shards: all rows, this rank's columns
     CH_TRY(dmalloc(&dl.gateup, q4_tile_bytes(2 * m->Il, m->H)));
-    CH_TRY(dmalloc(&dl.down, q4_tile_bytes(m->Ho, m->I)));
+    CH_TRY(dmalloc(&dl.down, q4_tile_bytes(m->H, m->Il)));
     CH_TRY(dmalloc(&dl.input_norm, m->H));
     CH_TRY(dmalloc(&dl.q_norm, m->D));
     CH_TRY(dmalloc(&dl.k_norm, m->D));
@@ -411,19 +410,21 @@ static int build_phases(ch_model *m, bool with_logits, Phase **d_out, uint32_t *
                         uint32_t *n_str, uint32_t *n_cross) {
   const uint32_t G = (uint32_t)m->mk_grid, GW = G * mk_warps();
   const bool tp = m->world > 1;
-  // local output rows of each GEMV, its k tiles, and whether its outputs are gathered
-  // from every rank (tensor parallel: o, gate|up and down outputs)
-  const uint32_t rows[5] = {m->qd_l + 2 * m->kvd_l, m->Ho, 2 * m->Il, m->Ho, m->Vl};
-  const uint32_t KT[5] = {m->H / 64, m->qd / 64, m->H / 64, m->I / 64, m->H / 32};
-  const bool gathered[5] = {false, tp, tp, tp, false};
+  // Local output rows of each GEMV and its k tiles.  Tensor parallel (Megatron
+  // layout): q|k|v and gate|up are column-parallel (this rank's heads / act rows, full
+  // K), o and down row-parallel (all H rows over this rank's K columns); each rank
+  // sends its o / down partial vector to slot `rank` of every rank's arena and the
+  // next add+norm prologue adds the world partials -- two exchanges per layer.
+  const uint32_t rows[5] = {m->qd_l + 2 * m->kvd_l, m->H, 2 * m->Il, m->H, m->Vl};
+  const uint32_t KT[5] = {m->H / 64, m->qd_l / 64, m->H / 64, m->Il / 64, m->H / 32};
+  const bool gathered[5] = {false, tp, false, tp, false};
   float *dst[5] = {m->gdir[GK_QKV], m->gdir[GK_O], m->gdir[GK_GU], m->gdir[GK_DOWN], m->gdir[GK_LM]};
   uint32_t row0[5] = {0, 0, 0, 0, 0};
+  const uint32_t nsum = tp ? m->world : 1u;
   if (tp) {
     dst[GK_O] = reinterpret_cast<float *>(m->arena + m->off_o);
-    dst[GK_GU] = reinterpret_cast<float *>(m->arena + m->off_act);
     dst[GK_DOWN] = reinterpret_cast<float *>(m->arena + m->off_down);
-    row0[GK_O] = row0[GK_DOWN] = m->rank * m->Ho;
-    row0[GK_GU] = m->rank * m->Il;  // act values
+    row0[GK_O] = row0[GK_DOWN] = m->rank * m->H;  // this rank's partial-vector slot
   }
   GemvOut outs[5];
   for (int k = 0; k < 5; k++) {
@@ -448,7 +449,7 @@ static int build_phases(ch_model *m, bool with_logits, Phase **d_out, uint32_t *
     p.scalar = 1.0f;
     return p;
   };
-  float *attn_frag = tp ? reinterpret_cast<float *>(m->arena + m->off_attn) : m->attn;
+  float *attn_frag = m->attn;  // this rank's heads only (row-parallel o)
   std::vector<Phase> ph;
   const uint32_t rh = m->cfg.rotary_dim / 2;
   for (uint32_t l = 0; l < m->L; l++) {
@@ -464,6 +465,7 @@ static int build_phases(ch_model *m, bool with_logits, Phase **d_out, uint32_t *
       q.pm = PM_ADD_NORM;
       q.x_in = m->X[1];
       q.r_in = outs[GK_DOWN];
+      q.nsum = nsum;
       q.post_w = pl.post_ffn;
       q.scalar = pl.scalar;
       q.x_out = m->X[0];
@@ -481,7 +483,7 @@ static int build_phases(ch_model *m, bool with_logits, Phase **d_out, uint32_t *
     at.attn_scale = 1.0f;  // Gemma-style: q/k norms replace 1/sqrt(d) (forward.zig:85)
     at.attn_out = attn_frag;
     ph.push_back(at);
-    Phase o = gemv(GK_O, dl.o, FMT_Q4, m->qd);
+    Phase o = gemv(GK_O, dl.o, FMT_Q4, m->qd_l);
     o.pm = PM_DIRECT;
     o.x_in = attn_frag;
     ph.push_back(o);
@@ -489,12 +491,13 @@ static int build_phases(ch_model *m, bool with_logits, Phase **d_out, uint32_t *
     gu.pm = PM_ADD_NORM;
     gu.x_in = m->X[0];
     gu.r_in = outs[GK_O];
+    gu.nsum = nsum;
     gu.post_w = dl.post_attn;
     gu.norm_w = dl.pre_ffn;
     gu.x_out = m->X[1];
     gu.normed_out = m->normed;
     ph.push_back(gu);
-    Phase dn = gemv(GK_DOWN, dl.down, FMT_Q4, m->I);
+    Phase dn = gemv(GK_DOWN, dl.down, FMT_Q4, m->Il);
     dn.pm = PM_GELU;
     dn.r_in = outs[GK_GU];
     ph.push_back(dn);
@@ -504,6 +507,7 @@ static int build_phases(ch_model *m, bool with_logits, Phase **d_out, uint32_t *
   lm.pm = PM_ADD_NORM;
   lm.x_in = m->X[1];
   lm.r_in = outs[GK_DOWN];
+  lm.nsum = nsum;
   lm.post_w = last.post_ffn;
   lm.scalar = last.scalar;
   lm.norm_w = m->final_norm;
@@ -528,11 +532,11 @@ static int build_phases(ch_model *m, bool with_logits, Phase **d_out, uint32_t *
     }
   }
   // barriers other ranks take part in: after a phase whose outputs go to every rank
-  // (attention, o, gate|up, down, top-64); the others stay on this GPU
+  // (the o and down partials, top-64); the others stay on this GPU
   uint32_t ncross = 0;
   for (size_t i = 0; i + 1 < ph.size(); i++) {
     Phase &p = ph[i];
-    const bool pushes = (p.kind == PH_GEMV && p.out.push) || p.kind == PH_ATTN || p.kind == PH_TOPK;
+    const bool pushes = (p.kind == PH_GEMV && p.out.push) || p.kind == PH_TOPK;
     p.cross = tp && pushes ? 1u : 0u;
     if (p.cross) ncross++;
     p.gidx = ncross;
@@ -589,18 +593,16 @@ static int init_decode_step(ch_model *m) {
   CH_CUDA(cudaMemset(m->mk_arrive, 0, 8));
   CH_CUDA(cudaMemset(m->mk_base, 0, 16));
   if (tp) {
-    // exchange arena: arrival counter, gathered o / down outputs, act and attention
-    // B fragments, every rank's top-64 -- same offsets on every rank
+    // exchange arena: arrival counter, every rank's o and down partial vectors,
+    // every rank's top-64 -- same offsets on every rank
     auto take = [&](size_t bytes) {
       const size_t o = m->arena_bytes;
       m->arena_bytes += (bytes + 255) & ~(size_t)255;
       return o;
     };
     m->off_arrive = take(8);
-    m->off_o = take((size_t)m->H * 4);
-    m->off_down = take((size_t)m->H * 4);
-    m->off_act = take((size_t)m->I * 4);
-    m->off_attn = take((size_t)m->qd * 4);
+    m->off_o = take((size_t)m->world * m->H * 4);
+    m->off_down = take((size_t)m->world * m->H * 4);
     m->off_cand = take((size_t)m->world * 64 * 8);
     CH_TRY(dmalloc(&m->arena, m->arena_bytes));
     CH_CUDA(cudaMemset(m->arena, 0, m->arena_bytes));
@@ -630,6 +632,7 @@ static MegaArgs mega_args(ch_model *m, bool logits, bool device_loop) {
   a.world = m->world;
   a.rank = m->rank;
   a.attn_q0 = m->rank * m->nq_l;
+  a.attn_local = 1;
   for (uint32_t r = 0; r < m->world && r < kMaxWorld; r++) a.arena[r] = m->peer_arena[r];
   a.xcand = m->arena ? reinterpret_cast<uint64_t *>(m->arena + m->off_cand) : nullptr;
   a.rot = m->cfg.rotary_dim;
@@ -785,9 +788,9 @@ static int create_synthetic(ch_ctx *ctx, const ch_model_config *cfg, uint64_t se
   if (!ctx || !out) return fail(CH_EINVAL, "NULL argument");
   CH_TRY(check_cfg(cfg));
   if (world == 0 || world > kMaxWorld || rank >= world) return fail(CH_EINVAL, "rank must be < world <= 8");
-  if (world > 1 && (cfg->num_key_value_heads % world || cfg->hidden_size % (16 * world) ||
-                    cfg->intermediate_size % (16 * world) || cfg->vocab_size % (16 * world)))
-    return fail(CH_EINVAL, "tensor parallel: kv heads, hidden/16, intermediate/16 and vocab/16 must divide by world");
+  if (world > 1 && (cfg->num_key_value_heads % world || cfg->intermediate_size % (64 * world) ||
+                    cfg->vocab_size % (16 * world) || (cfg->num_attention_heads / world * cfg->head_dim) % 64))
+    return fail(CH_EINVAL, "tensor parallel: kv heads, intermediate/64, vocab/16 and the per-rank q width/64 must divide by world");
   CH_CUDA(cudaSetDevice(ctx->device));
   ch_model *m = new ch_model();
   m->ctx = ctx;
@@ -825,13 +828,15 @@ static int create_synthetic(ch_ctx *ctx, const ch_model_config *cfg, uint64_t se
         launch_gen_q4_rows(tA + qw + kw, rk * m->kvd_l, m->kvd_l, m->H, ch_tensor_seed(seed, l, T_V), wstd, s) ==
             cudaSuccess &&
         launch_repack_q4(tA, nullptr, m->qd_l + 2 * m->kvd_l, m->H, MAP_PLAIN, dl.qkv, s) == cudaSuccess &&
-        launch_gen_q4_rows(tB, rk * m->Ho, m->Ho, m->qd, ch_tensor_seed(seed, l, T_O), wstd, s) == cudaSuccess &&
-        launch_repack_q4(tB, nullptr, m->Ho, m->qd, MAP_PLAIN, dl.o, s) == cudaSuccess &&
+        launch_gen_q4_cols(tB, m->H, m->qd, rk * m->qd_l, m->qd_l, ch_tensor_seed(seed, l, T_O), wstd, s) ==
+            cudaSuccess &&
+        launch_repack_q4(tB, nullptr, m->H, m->qd_l, MAP_PLAIN, dl.o, s) == cudaSuccess &&
         launch_gen_q4_rows(tA, rk * m->Il, m->Il, m->H, ch_tensor_seed(seed, l, T_GATE), wstd, s) == cudaSuccess &&
         launch_gen_q4_rows(tB, rk * m->Il, m->Il, m->H, ch_tensor_seed(seed, l, T_UP), wstd, s) == cudaSuccess &&
         launch_repack_q4(tA, tB, 2 * m->Il, m->H, MAP_GATEUP, dl.gateup, s) == cudaSuccess &&
-        launch_gen_q4_rows(tA, rk * m->Ho, m->Ho, m->I, ch_tensor_seed(seed, l, T_DOWN), wstd, s) == cudaSuccess &&
-        launch_repack_q4(tA, nullptr, m->Ho, m->I, MAP_PLAIN, dl.down, s) == cudaSuccess;
+        launch_gen_q4_cols(tA, m->H, m->I, rk * m->Il, m->Il, ch_tensor_seed(seed, l, T_DOWN), wstd, s) ==
+            cudaSuccess &&
+        launch_repack_q4(tA, nullptr, m->H, m->Il, MAP_PLAIN, dl.down, s) == cudaSuccess;
     if (!ok) return bail(fail(CH_ECUDA, "synthetic layer generation"));
     if (gen_norm(m, &dl.input_norm, m->H, ch_tensor_seed(seed, l, T_IN_NORM), tn) ||
         gen_norm(m, &dl.q_norm, m->D, ch_tensor_seed(seed, l, T_Q_NORM), tn) ||
@@ -923,9 +928,9 @@ extern "C" int ch_model_weight_tiles(ch_model *m, uint32_t layer, int which, voi
   const DevLayer &l = m->layers[layer];
   switch (which) {
     case 0: *tiles = l.qkv, *rows = m->qd_l + 2 * m->kvd_l, *cols = m->H; break;  // this rank's shard
-    case 1: *tiles = l.o, *rows = m->Ho, *cols = m->qd; break;
+    case 1: *tiles = l.o, *rows = m->H, *cols = m->qd_l; break;  // this rank's columns
     case 2: *tiles = l.gateup, *rows = 2 * m->Il, *cols = m->H; break;
-    case 3: *tiles = l.down, *rows = m->Ho, *cols = m->I; break;
+    case 3: *tiles = l.down, *rows = m->H, *cols = m->Il; break;
     case 4: *tiles = m->lm, *rows = m->Vl, *cols = m->H; break;
     default: return fail(CH_EINVAL, "which must be 0..4");
   }
