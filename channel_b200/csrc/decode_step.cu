@@ -255,10 +255,32 @@ CH_DEV void store_frag_pair(uint32_t *frag, uint32_t j, float v0, float v1) {
   frag[frag_word(j, 0)] = pack_half2(h0, h1);
   frag[frag_word(j, 1)] = pack_half2(l0, l1);
 }
+// epochs of the low-latency exchanges of this launch start after this value
+__shared__ unsigned long long s_xep;
+// set when a wait on another rank gave up: later cross-rank waits of the launch return at once
+__shared__ uint32_t s_abort;
+// an exchange word: the value in the low half, its epoch in the high half -- written
+// and read as one 8-byte access, so a reader that sees the epoch sees the value
+CH_DEV void st_x64_sys(unsigned long long *p, unsigned long long v) {
+  asm volatile("st.relaxed.sys.global.b64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+CH_DEV unsigned long long ld_x64_sys(const unsigned long long *p) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.sys.global.b64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
 // one finished output row (local index) of a GEMV: local buffer, or every rank's copy
 CH_DEV void out_row(const MegaArgs &a, const GemvOut &o, uint32_t row, float v) {
   if (!o.push) {
     o.direct[row] = v;
+    return;
+  }
+  if (o.push == 2) {  // word [epoch parity][this rank][row] of every rank's exchange array
+    const unsigned long long ep = s_xep + o.xidx + 1;
+    const unsigned long long w = (ep << 32) | __float_as_uint(v);
+    const size_t slot = ((size_t)(ep & 1) * a.world + a.rank) * o.row0 + row;
+    for (uint32_t r = 0; r < a.world; r++)
+      st_x64_sys(reinterpret_cast<unsigned long long *>(on_rank(a, o.direct, r)) + slot, w);
     return;
   }
   for (uint32_t r = 0; r < a.world; r++) on_rank(a, o.direct, r)[o.row0 + row] = v;
@@ -429,14 +451,27 @@ CH_DEV void gemv_prologue(const Phase &p, const MegaArgs &a, const SmemLayout &L
     if (on) {
       if (p.nsum > 1) {
         // row-parallel producer: every rank's partial vector, added in rank order (the
-        // same sums on every rank); through L2, since this CTA's L1 may hold last step's
-        const float *q = p.r_in.direct + (tid >> 2) * 32 + (tid & 3u) * 2;
+        // same sums on every rank), from the exchange words of this step's epoch --
+        // polled until they arrive (bounded), no barrier before this phase
+        const unsigned long long ep = s_xep + p.r_in.xidx + 1;
+        const unsigned long long *q = reinterpret_cast<const unsigned long long *>(p.r_in.direct) +
+                                      (size_t)(ep & 1) * p.nsum * K + (tid >> 2) * 32 + (tid & 3u) * 2;
+        const uint64_t t0 = globaltimer_ns();
+        bool live = !*(volatile uint32_t *)&s_abort;
         for (uint32_t rk = 0; rk < p.nsum; rk++, q += K) {
 #pragma unroll
-          for (int g = 0; g < 4; g++) {
-            const float2 v = __ldcg(reinterpret_cast<const float2 *>(q + 8 * g));
-            r[2 * g] = rk ? __fadd_rn(r[2 * g], v.x) : v.x;
-            r[2 * g + 1] = rk ? __fadd_rn(r[2 * g + 1], v.y) : v.y;
+          for (int e = 0; e < 8; e++) {
+            unsigned long long w = ld_x64_sys(q + 8 * (e >> 1) + (e & 1));
+            while ((uint32_t)(w >> 32) != (uint32_t)ep && live) {
+              if (globaltimer_ns() - t0 > 2000000000ull) {
+                atomicOr(a.err, DEV_ERR_PEER_TIMEOUT);
+                s_abort = 1u;
+                live = false;
+              }
+              w = ld_x64_sys(q + 8 * (e >> 1) + (e & 1));
+            }
+            const float v = __uint_as_float((uint32_t)w);
+            r[e] = rk ? __fadd_rn(r[e], v) : v;
           }
         }
       } else {
@@ -1188,7 +1223,6 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(const MegaAr
   __shared__ float red[32];
   __shared__ Phase ph_s[3];  // phases pi, pi+1 and pi+2 (copied ahead with cp.async)
   __shared__ StepParams sp_s;
-  __shared__ uint32_t s_abort;
 
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const uint32_t gw = blockIdx.x * MK_NW + warp;
@@ -1208,6 +1242,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(const MegaAr
     *L.xzero = make_uint4(0u, 0u, 0u, 0u);
     sp_s = *a.sp;
     s_abort = (*(volatile uint32_t *)a.err & DEV_ERR_PEER_TIMEOUT) ? 1u : 0u;
+    s_xep = a.base[2];
   }
   for (uint32_t i = 0; i < 2 && i < a.nphases; i++) copy_phase(a.phases + i, &ph_s[i]);
   cp_async_wait_all();
@@ -1251,14 +1286,20 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(const MegaAr
     PHASE_MARK(pi, 4);
     if (pi + 1 < a.nphases) {
       const bool cross = p.cross != 0;
-      const unsigned long long ltarget = base + (unsigned long long)(pi + 1) * gridDim.x;
-      grid_arrive(a, cross, ltarget);
-      pre_phase<R>(ph_s[(pi + 1) % 3], a, sp_s, L);
-      PHASE_MARK(pi, 5);
-      if (cross)
-        grid_wait(a.garrive, true, gbase + (unsigned long long)p.gidx * a.world, a.err, &s_abort);
-      else
-        grid_wait(a.arrive, false, ltarget, a.err, &s_abort);
+      const unsigned long long ltarget = base + (unsigned long long)p.lidx * gridDim.x;
+      if (p.nobar) {  // the consumers poll this phase's exchange words: no barrier
+        __syncthreads();  // the CTA's stores are issued before its next phase reuses shared memory
+        pre_phase<R>(ph_s[(pi + 1) % 3], a, sp_s, L);
+        PHASE_MARK(pi, 5);
+      } else {
+        grid_arrive(a, cross, ltarget);
+        pre_phase<R>(ph_s[(pi + 1) % 3], a, sp_s, L);
+        PHASE_MARK(pi, 5);
+        if (cross)
+          grid_wait(a.garrive, true, gbase + (unsigned long long)p.gidx * a.world, a.err, &s_abort);
+        else
+          grid_wait(a.arrive, false, ltarget, a.err, &s_abort);
+      }
       PHASE_MARK(pi, 6);
     }
   }
@@ -1270,8 +1311,9 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(const MegaAr
   }
   // every CTA has passed the last barrier, so all have read `base`: advance it for the next launch
   if (blockIdx.x == 0 && threadIdx.x == 0) {
-    a.base[0] = base + (unsigned long long)(a.nphases - 1) * gridDim.x;
+    a.base[0] = base + (unsigned long long)a.nlocal * gridDim.x;
     a.base[1] = gbase + (unsigned long long)a.ncross * a.world;
+    a.base[2] = s_xep + a.nx;
   }
 }
 

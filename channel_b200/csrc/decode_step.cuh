@@ -38,8 +38,12 @@ struct GemvOut {
   float *partial;  // [grid][2][16] CTA partial sums of straddling row tiles
   Partition pt;    // the producing GEMV's split
   uint32_t act;    // 1: interleaved gate|up GEMV whose consumer takes B fragments
-  uint32_t row0;   // tensor parallel: index of this rank's first row (act value) in the gathered vector
-  uint32_t push;   // 1: rows go to every rank's copy of `direct` (peer stores), 0: local only
+  uint32_t row0;   // push 1: index of this rank's first row (act value) in the gathered vector;
+                   // push 2: length of the exchanged vector
+  uint32_t push;   // 1: rows go to every rank's copy of `direct` (peer stores), 0: local only,
+                   // 2: low-latency exchange -- `direct` is a [2 parities][world][row0] array of
+                   // 8-byte {value, epoch} words, one plain store per row and rank, no fence
+  uint32_t xidx;   // push 2: index of this exchange within the launch (epoch = base[2] + xidx + 1)
 };
 
 struct alignas(16) Phase {
@@ -47,6 +51,9 @@ struct alignas(16) Phase {
   // barrier after this phase: cross = 1 when other ranks read its outputs (tensor
   // parallel); gidx = number of cross-rank barriers up to and including this one
   uint32_t cross, gidx;
+  // nobar = 1: no barrier after this phase (its outputs are exchange words that the
+  // consumers poll); lidx = grid barriers up to and including this one
+  uint32_t nobar, lidx;
   // PM_ADD_NORM input: nsum > 1 = r_in.direct holds nsum partial vectors of K floats
   // (one per rank, row-parallel GEMV), added in rank order by the prologue
   uint32_t nsum;
@@ -79,9 +86,12 @@ struct MegaArgs {
   uint32_t nstreams;
   uint32_t nphases, grid;
   unsigned long long *arrive;  // this GPU's grid-barrier arrivals (monotonic across launches)
-  unsigned long long *base;    // [2] arrivals (local, cross-rank) before this launch (advanced by the launch)
+  unsigned long long *base;    // [3] arrivals (local, cross-rank) and exchange epochs before this
+                               // launch (advanced by the launch)
   unsigned long long *garrive; // tensor parallel: rank arrivals of cross-rank barriers (in the arena)
   uint32_t ncross;             // cross-rank barriers per launch
+  uint32_t nlocal;             // grid barriers per launch (transitions with nobar = 0)
+  uint32_t nx;                 // low-latency exchanges per launch
   uint32_t *err;
   const StepParams *sp;
   StepParams *sp_rw;  // device loop: the top-k phase records the token at history slot sp->step (else null)

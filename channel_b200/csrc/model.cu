@@ -221,8 +221,10 @@ struct ch_model {
   float *gdir[5] = {nullptr, nullptr, nullptr, nullptr, nullptr};
   float *gpart[5] = {nullptr, nullptr, nullptr, nullptr, nullptr};
   unsigned long long *mk_arrive = nullptr;
-  unsigned long long *mk_base = nullptr;  // [2] barrier arrivals (local, cross-rank) before the next launch
+  unsigned long long *mk_base = nullptr;  // [3] barrier arrivals (local, cross-rank), exchange epochs
   uint32_t n_cross = 0, n_cross_nl = 0;    // cross-rank barriers per launch (logits / no-logits tables)
+  uint32_t n_local = 0, n_local_nl = 0;    // grid barriers per launch
+  uint32_t n_x = 0, n_x_nl = 0;            // low-latency exchanges per launch
   size_t mk_smem = 0;
   int mk_grid = 0;
   bool use_ops = false;  // kernel-per-op decode (CH_DECODE_OPS=1), kept for A/B measurement
@@ -407,7 +409,7 @@ static int alloc_model_buffers(ch_model *m) {
 enum GemvKind { GK_QKV = 0, GK_O = 1, GK_GU = 2, GK_DOWN = 3, GK_LM = 4 };
 
 static int build_phases(ch_model *m, bool with_logits, Phase **d_out, uint32_t *n_out, StreamDesc **d_str,
-                        uint32_t *n_str, uint32_t *n_cross) {
+                        uint32_t *n_str, uint32_t *n_cross, uint32_t *n_local, uint32_t *n_x) {
   const uint32_t G = (uint32_t)m->mk_grid, GW = G * mk_warps();
   const bool tp = m->world > 1;
   // Local output rows of each GEMV and its k tiles.  Tensor parallel (Megatron
@@ -421,10 +423,10 @@ static int build_phases(ch_model *m, bool with_logits, Phase **d_out, uint32_t *
   float *dst[5] = {m->gdir[GK_QKV], m->gdir[GK_O], m->gdir[GK_GU], m->gdir[GK_DOWN], m->gdir[GK_LM]};
   uint32_t row0[5] = {0, 0, 0, 0, 0};
   const uint32_t nsum = tp ? m->world : 1u;
-  if (tp) {
+  if (tp) {  // low-latency exchange arrays [2 parities][world][H] of {value, epoch} words
     dst[GK_O] = reinterpret_cast<float *>(m->arena + m->off_o);
     dst[GK_DOWN] = reinterpret_cast<float *>(m->arena + m->off_down);
-    row0[GK_O] = row0[GK_DOWN] = m->rank * m->H;  // this rank's partial-vector slot
+    row0[GK_O] = row0[GK_DOWN] = m->H;
   }
   GemvOut outs[5];
   for (int k = 0; k < 5; k++) {
@@ -435,7 +437,7 @@ static int build_phases(ch_model *m, bool with_logits, Phase **d_out, uint32_t *
       pt.rq = (rows[k] / 16) / G;
       pt.rrem = (rows[k] / 16) % G;
     }
-    outs[k] = GemvOut{dst[k], m->gpart[k], pt, k == GK_GU ? 1u : 0u, row0[k], gathered[k] ? 1u : 0u};
+    outs[k] = GemvOut{dst[k], m->gpart[k], pt, k == GK_GU ? 1u : 0u, row0[k], gathered[k] ? 2u : 0u, 0u};
   }
   auto gemv = [&](int kind, const uint8_t *tiles, int fmt, uint32_t K) {
     Phase p{};
@@ -452,6 +454,8 @@ static int build_phases(ch_model *m, bool with_logits, Phase **d_out, uint32_t *
   float *attn_frag = m->attn;  // this rank's heads only (row-parallel o)
   std::vector<Phase> ph;
   const uint32_t rh = m->cfg.rotary_dim / 2;
+  uint32_t nx = 0;          // exchanges numbered in phase order: o of layer l = 2l, down = 2l + 1
+  GemvOut prev_down{};      // the previous layer's down output (its exchange index)
   for (uint32_t l = 0; l < m->L; l++) {
     const DevLayer &dl = m->layers[l];
     Phase q = gemv(GK_QKV, dl.qkv, FMT_Q4, m->H);
@@ -464,7 +468,7 @@ static int build_phases(ch_model *m, bool with_logits, Phase **d_out, uint32_t *
       const DevLayer &pl = m->layers[l - 1];
       q.pm = PM_ADD_NORM;
       q.x_in = m->X[1];
-      q.r_in = outs[GK_DOWN];
+      q.r_in = prev_down;
       q.nsum = nsum;
       q.post_w = pl.post_ffn;
       q.scalar = pl.scalar;
@@ -484,13 +488,14 @@ static int build_phases(ch_model *m, bool with_logits, Phase **d_out, uint32_t *
     at.attn_out = attn_frag;
     ph.push_back(at);
     Phase o = gemv(GK_O, dl.o, FMT_Q4, m->qd_l);
+    if (o.out.push == 2) o.out.xidx = nx++;
     o.pm = PM_DIRECT;
     o.x_in = attn_frag;
     ph.push_back(o);
     Phase gu = gemv(GK_GU, dl.gateup, FMT_Q4, m->H);
     gu.pm = PM_ADD_NORM;
     gu.x_in = m->X[0];
-    gu.r_in = outs[GK_O];
+    gu.r_in = o.out;
     gu.nsum = nsum;
     gu.post_w = dl.post_attn;
     gu.norm_w = dl.pre_ffn;
@@ -498,6 +503,8 @@ static int build_phases(ch_model *m, bool with_logits, Phase **d_out, uint32_t *
     gu.normed_out = m->normed;
     ph.push_back(gu);
     Phase dn = gemv(GK_DOWN, dl.down, FMT_Q4, m->Il);
+    if (dn.out.push == 2) dn.out.xidx = nx++;
+    prev_down = dn.out;
     dn.pm = PM_GELU;
     dn.r_in = outs[GK_GU];
     ph.push_back(dn);
@@ -506,7 +513,7 @@ static int build_phases(ch_model *m, bool with_logits, Phase **d_out, uint32_t *
   Phase lm = gemv(GK_LM, m->lm, FMT_Q8, m->H);
   lm.pm = PM_ADD_NORM;
   lm.x_in = m->X[1];
-  lm.r_in = outs[GK_DOWN];
+  lm.r_in = prev_down;
   lm.nsum = nsum;
   lm.post_w = last.post_ffn;
   lm.scalar = last.scalar;
@@ -531,17 +538,22 @@ static int build_phases(ch_model *m, bool with_logits, Phase **d_out, uint32_t *
       ph.push_back(mg);
     }
   }
-  // barriers other ranks take part in: after a phase whose outputs go to every rank
-  // (the o and down partials, top-64); the others stay on this GPU
-  uint32_t ncross = 0;
+  // After a phase whose outputs are exchange words (tensor parallel o and down
+  // partials) there is no barrier: the next phase's prologue polls the words.  After
+  // the top-64 phase a cross-rank barrier; after every other phase a grid barrier.
+  uint32_t ncross = 0, nlocal = 0;
   for (size_t i = 0; i + 1 < ph.size(); i++) {
     Phase &p = ph[i];
-    const bool pushes = (p.kind == PH_GEMV && p.out.push) || p.kind == PH_TOPK;
-    p.cross = tp && pushes ? 1u : 0u;
+    p.nobar = (p.kind == PH_GEMV && p.out.push == 2) ? 1u : 0u;
+    p.cross = (tp && p.kind == PH_TOPK) ? 1u : 0u;
     if (p.cross) ncross++;
+    if (!p.nobar) nlocal++;
     p.gidx = ncross;
+    p.lidx = nlocal;
   }
   *n_cross = ncross;
+  *n_local = nlocal;
+  *n_x = nx;
   CH_TRY(dmalloc(d_out, ph.size()));
   CH_CUDA(cudaMemcpy(*d_out, ph.data(), ph.size() * sizeof(Phase), cudaMemcpyHostToDevice));
   *n_out = (uint32_t)ph.size();
@@ -589,27 +601,29 @@ static int init_decode_step(ch_model *m) {
     CH_TRY(dmalloc(&m->gpart[k], part));
   }
   CH_TRY(dmalloc(&m->mk_arrive, 1));
-  CH_TRY(dmalloc(&m->mk_base, 2));
+  CH_TRY(dmalloc(&m->mk_base, 3));
   CH_CUDA(cudaMemset(m->mk_arrive, 0, 8));
-  CH_CUDA(cudaMemset(m->mk_base, 0, 16));
+  CH_CUDA(cudaMemset(m->mk_base, 0, 24));
   if (tp) {
-    // exchange arena: arrival counter, every rank's o and down partial vectors,
-    // every rank's top-64 -- same offsets on every rank
+    // exchange arena: arrival counter, the o and down exchange arrays
+    // ([2 parities][world][H] {value, epoch} words), every rank's top-64 -- same
+    // offsets on every rank
     auto take = [&](size_t bytes) {
       const size_t o = m->arena_bytes;
       m->arena_bytes += (bytes + 255) & ~(size_t)255;
       return o;
     };
     m->off_arrive = take(8);
-    m->off_o = take((size_t)m->world * m->H * 4);
-    m->off_down = take((size_t)m->world * m->H * 4);
+    m->off_o = take((size_t)2 * m->world * m->H * 8);
+    m->off_down = take((size_t)2 * m->world * m->H * 8);
     m->off_cand = take((size_t)m->world * 64 * 8);
     CH_TRY(dmalloc(&m->arena, m->arena_bytes));
     CH_CUDA(cudaMemset(m->arena, 0, m->arena_bytes));
   }
-  CH_TRY(build_phases(m, true, &m->d_phases, &m->n_phases, &m->d_streams, &m->n_streams, &m->n_cross));
+  CH_TRY(build_phases(m, true, &m->d_phases, &m->n_phases, &m->d_streams, &m->n_streams, &m->n_cross,
+                      &m->n_local, &m->n_x));
   CH_TRY(build_phases(m, false, &m->d_phases_nl, &m->n_phases_nl, &m->d_streams_nl, &m->n_streams_nl,
-                      &m->n_cross_nl));
+                      &m->n_cross_nl, &m->n_local_nl, &m->n_x_nl));
   return CH_OK;
 }
 
@@ -624,6 +638,8 @@ static MegaArgs mega_args(ch_model *m, bool logits, bool device_loop) {
   a.base = m->mk_base;
   a.garrive = m->arena ? reinterpret_cast<unsigned long long *>(m->arena + m->off_arrive) : nullptr;
   a.ncross = logits ? m->n_cross : m->n_cross_nl;
+  a.nlocal = logits ? m->n_local : m->n_local_nl;
+  a.nx = logits ? m->n_x : m->n_x_nl;
   a.err = m->ctx->err;
   a.sp = m->sp;
   a.sp_rw = device_loop ? m->sp : nullptr;
@@ -948,8 +964,13 @@ extern "C" int ch_model_zero_state(ch_model *m) {
   CH_CUDA(cudaMemsetAsync(m->X[1], 0, m->H * 4, s));
   CH_CUDA(cudaMemsetAsync(m->normed, 0, m->H * 4, s));
   if (m->mk_arrive) CH_CUDA(cudaMemsetAsync(m->mk_arrive, 0, 8, s));
-  if (m->mk_base) CH_CUDA(cudaMemsetAsync(m->mk_base, 0, 16, s));
-  if (m->arena) CH_CUDA(cudaMemsetAsync(m->arena + m->off_arrive, 0, 8, s));
+  if (m->mk_base) CH_CUDA(cudaMemsetAsync(m->mk_base, 0, 24, s));
+  if (m->arena) {
+    CH_CUDA(cudaMemsetAsync(m->arena + m->off_arrive, 0, 8, s));
+    // exchange words restart at epoch 1: no word of an earlier run may carry it
+    CH_CUDA(cudaMemsetAsync(m->arena + m->off_o, 0, (size_t)2 * m->world * m->H * 8, s));
+    CH_CUDA(cudaMemsetAsync(m->arena + m->off_down, 0, (size_t)2 * m->world * m->H * 8, s));
+  }
   CH_CUDA(cudaStreamSynchronize(s));
   return CH_OK;
 }
