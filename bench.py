@@ -167,6 +167,25 @@ def reference_arm(args):
 
 
 # ----------------------------------------------------------------------------------------
+def time_launches(ctx, stream, call, n):
+    """Device time per launch of n back-to-back calls (call(i) enqueues launch i on the
+    library stream).  The stream first waits behind a short device sleep on torch's
+    stream, so every launch is queued before the first runs: the events then time the
+    kernels, not the host's call rate."""
+    import torch
+    ctx.synchronize()
+    torch.cuda.synchronize()
+    torch.cuda._sleep(int(4e6))  # a few ms of device time (clock cycles)
+    stream.wait_stream(torch.cuda.current_stream())
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(n):
+        call(i)
+    e1.record(stream)
+    e1.synchronize()
+    return e0.elapsed_time(e1) / n
+
+
 def gateup_roofline(ctx, gm, cfg, stream, reps=3):
     """Dominant decode kernel (fused gate/up Q4 GEMV + GELU*up, 53% of the weight bytes)
     timed alone through ch_fused_mlp_q4 with CUDA events on the library stream, rotating
@@ -179,17 +198,13 @@ def gateup_roofline(ctx, gm, cfg, stream, reps=3):
     ybuf = torch.empty(I, device="cuda", dtype=torch.float32)
     tiles = [gm.weight_tiles(l, 2)[0] for l in range(cfg.num_hidden_layers)]
     torch.cuda.synchronize()
-    for l in range(len(tiles)):
-        L.check(lib.ch_fused_mlp_q4(ctx.handle, tiles[l], I, H, xbuf.data_ptr(), ybuf.data_ptr()))
-    n = reps * len(tiles)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    ctx.synchronize()
-    e0.record(stream)
-    for i in range(n):
+
+    def call(i):
         L.check(lib.ch_fused_mlp_q4(ctx.handle, tiles[i % len(tiles)], I, H, xbuf.data_ptr(), ybuf.data_ptr()))
-    e1.record(stream)
-    e1.synchronize()
-    k_ms = e0.elapsed_time(e1) / n
+    for i in range(len(tiles)):
+        call(i)
+    n = reps * len(tiles)
+    k_ms = time_launches(ctx, stream, call, n)
     nbytes = 2 * I * H * 18 // 32 + H * 4 + I * 4
     peak, peak_kind = peaks()
     achieved = nbytes / (k_ms / 1000.0) / 1e9
@@ -201,6 +216,40 @@ def gateup_roofline(ctx, gm, cfg, stream, reps=3):
             "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak, "traffic": traffic,
             "bytes_per_launch": nbytes, "us_per_launch": k_ms * 1000, "launches_timed": n,
             "peak_kind": peak_kind + " hbm_gbs (burst; kernel timed alone over {} rotating layers)".format(len(tiles))}
+
+
+def gemv_config1(ctx, stream, reps=8, copies=24):
+    """BASELINE config 1 through the C-ABI: one 8192 x 2048 Q4 GEMV (synthetic Q4
+    weights and N(0,1) x), timed back to back over `copies` packed copies
+    of the matrix (226 MB, so no launch finds its 9.4 MB in L2)."""
+    import torch
+    from channel_b200 import _lib as L
+    lib = L.load()
+    M, K = 8192, 2048
+    blocks = torch.empty(M * (K // 32) * 5, dtype=torch.int32, device="cuda")
+    tb = lib.ch_q4_tile_bytes(M, K)
+    tiles = torch.empty(copies * tb, dtype=torch.uint8, device="cuda")
+    x = torch.randn(K, dtype=torch.float32, device="cuda", generator=torch.Generator("cuda").manual_seed(0))
+    y = torch.empty(M, dtype=torch.float32, device="cuda")
+    torch.cuda.synchronize()
+    L.check(lib.ch_gen_q4_blocks(ctx.handle, blocks.data_ptr(), M, K, 1, 0.02))
+    for c in range(copies):
+        L.check(lib.ch_q4_pack(ctx.handle, blocks.data_ptr(), M, K, tiles.data_ptr() + c * tb))
+
+    def call(i):
+        L.check(lib.ch_gemv_q4(ctx.handle, tiles.data_ptr() + (i % copies) * tb, M, K, x.data_ptr(), y.data_ptr()))
+    for i in range(copies):
+        call(i)
+    n = reps * copies
+    k_ms = time_launches(ctx, stream, call, n)
+    nbytes = M * K * 18 // 32 + K * 4 + M * 4
+    peak, peak_kind = peaks()
+    achieved = nbytes / (k_ms / 1000.0) / 1e9
+    ctx.synchronize()
+    del blocks, tiles, x, y
+    return {"kernel": "gemv_kernel<Q4, STORE> (config 1: 8192 x 2048)", "achieved": achieved, "peak": peak,
+            "unit": "GB/s", "frac": achieved / peak, "bytes_per_launch": nbytes, "us_per_launch": k_ms * 1000,
+            "launches_timed": n, "peak_kind": peak_kind + " hbm_gbs (burst)"}
 
 
 def prefill_roofline(ctx, gm, cfg, stream, n_tok, layers=8, reps=2):
@@ -315,6 +364,7 @@ def ours(args):
     if args.kernel_only:
         r = gateup_roofline(ctx, gm, cfg, stream, reps=3)
         print(json.dumps({"kernel": "fused gate/up GEMV", **r}), flush=True)
+        print(json.dumps(gemv_config1(ctx, stream)), flush=True)
         gm.deinit()
         ctx.deinit()
         return
@@ -371,6 +421,7 @@ def ours(args):
           "peak_kind": peak_kind + " hbm_gbs (copy bandwidth); kernel timed inside the device loop"}
     # the Q4 GEMV on its own (metric's second part): fused gate/up, op-level kernel, rotating layers
     gemv_rl = gateup_roofline(ctx, gm, cfg, stream, reps=3) if world == 1 else None
+    gemv_c1 = gemv_config1(ctx, stream) if world == 1 else None
     # the batched prefill (one GPU): whole 512-token prompt, and its tensor-core GEMMs alone
     prefill_rl = None
     if world == 1:
@@ -445,6 +496,7 @@ def ours(args):
                        "l2": "per-step weight stream 7.2 GB > 126 MB L2 (no flush needed)"},
             "roofline": rl,
             "gemv_roofline": gemv_rl,
+            "gemv_config1": gemv_c1,
             "prefill_roofline": prefill_rl,
             "cpu_baseline": cpu,
             "e2e": e2e,

@@ -139,6 +139,18 @@ CH_DEV void mma_16816(float *d, const uint32_t *a, uint32_t b0, uint32_t b1) {
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
+// D(16x8 s32) = A(16x32 s8, row) * B(32x8 s8, col) + c (c in every accumulator)
+CH_DEV void imma_16832(int (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1, int c) {
+  asm("mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};"
+      : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "r"(c));
+}
+CH_DEV uint32_t lop3_and_xor(uint32_t a, uint32_t b, uint32_t c) {  // (a & b) ^ c
+  uint32_t d;
+  asm("lop3.b32 %0, %1, %2, %3, 0x6A;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+
 // Q4 word (8 nibbles in the repacked order) -> A fragment {a0,a1,a2,a3}, values q-8 exact in f16.
 //   bits 0-3 / 16-19  -> a0 ; bits 4-7 / 20-23 -> a1 ; bits 8-11 / 24-27 -> a2 ; bits 12-15 / 28-31 -> a3
 CH_DEV void dequant_q4_word(uint32_t w, uint32_t *a) {

@@ -116,6 +116,139 @@ CH_DEV void tile_mma(const uint8_t *tile, uint32_t kt, const uint4 *xb, uint32_t
   }
 }
 
+// ---------------------------------------------------------------------------
+// Integer tensor-core tiles (standalone GEMV).  The weights enter mma.sync
+// m16n8k32 as s8 without a float dequant: a Q4 nibble q becomes the byte
+// 16 * (q - 8) by one mask-and-xor, a Q8 byte (stored q ^ 0x80) becomes q by one
+// xor.  The input enters as four s8 limbs per value against a power-of-two scale
+// per 32-block, x = sx * (l0 + l1 / 2^7 + l2 / 2^14 + l3 / 2^21) with every
+// |limb| <= 64, so each block dot product is an exact int32 and x is kept to
+// 2^-27 of the block's largest magnitude.  Limb c is B column c (lanes g >= 4
+// repeat columns 0..3; those results are not used).  The accumulators start at
+// 1.5 * 2^23 in integer form, so a result's float view minus 1.5 * 2^23 is the
+// exact dot product (|dot| < 2^22) with no integer-to-float conversion.
+//
+// k order inside a register: splitting the nibbles of a repacked Q4 word (low
+// nibble: row g, high nibble: row g+8) gives bytes for k0 + {2t, 2t+8, 2t+1,
+// 2t+9} (k0 = the 16-chunk base); Q8 words are regrouped by byte_perm into the
+// same order and the limb bytes are built in it.  A and B agree on the order,
+// which is all the MMA needs.
+constexpr float kLimbMagicF = 12582912.0f;  // 1.5 * 2^23
+constexpr int kLimbMagicI = 0x4B400000;     // its bit pattern
+
+// x (K floats, global or shared) -> xq[b*16 + t*4 + c] = limb c of the 8 values
+// of block b that lane quad t multiplies (k = {2t, 2t+8, 2t+1, 2t+9} and +16),
+// sxs[b] = 2^(e-6) where max|x_b| < 2^e.  One (block b, quad t) item per thread;
+// a block's 4 items sit on 4 aligned lanes of one warp (blockDim.x % 32 == 0).
+CH_DEV void build_limbs(const float *v, uint2 *xq, float *sxs, uint32_t K) {
+  for (uint32_t idx = threadIdx.x; idx < K / 32 * 4; idx += blockDim.x) {
+    const uint32_t b = idx >> 2, t = idx & 3;
+    const float *p = v + b * 32 + 2 * t;
+    const float2 e0 = *reinterpret_cast<const float2 *>(p), e1 = *reinterpret_cast<const float2 *>(p + 8);
+    const float2 e2 = *reinterpret_cast<const float2 *>(p + 16), e3 = *reinterpret_cast<const float2 *>(p + 24);
+    const float e[8] = {e0.x, e1.x, e0.y, e1.y, e2.x, e3.x, e2.y, e3.y};
+    float m = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; j++) m = fmaxf(m, fabsf(e[j]));
+    const uint32_t quad = 0xFu << (threadIdx.x & 28u);
+    m = fmaxf(m, __shfl_xor_sync(quad, m, 1));
+    m = fmaxf(m, __shfl_xor_sync(quad, m, 2));
+    // biased exponent E: m < 2^(E-126); scale 2^(132-E) puts |x| below 64
+    const uint32_t E = max((__float_as_uint(m) >> 23) & 0xFFu, 6u);
+    const float scale = __uint_as_float((259u - E) << 23);
+    uint32_t by[4][8];  // limb c of value j in the low byte (float view of 1.5 * 2^23 + limb)
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+      float u = __fmul_rn(e[j], scale);
+#pragma unroll
+      for (int c = 0; c < 4; c++) {
+        const float r = __fadd_rn(u, kLimbMagicF);  // round to nearest integer
+        by[c][j] = __float_as_uint(r);
+        if (c < 3) u = __fmul_rn(__fsub_rn(u, __fsub_rn(r, kLimbMagicF)), 128.0f);  // exact remainder
+      }
+    }
+    uint32_t wd[4][2];
+#pragma unroll
+    for (int c = 0; c < 4; c++)
+#pragma unroll
+      for (int h = 0; h < 2; h++)
+        wd[c][h] = __byte_perm(__byte_perm(by[c][4 * h], by[c][4 * h + 1], 0x0040u),
+                               __byte_perm(by[c][4 * h + 2], by[c][4 * h + 3], 0x0040u), 0x5410u);
+    uint4 *o = reinterpret_cast<uint4 *>(xq + b * 16 + t * 4);
+    o[0] = make_uint4(wd[0][0], wd[0][1], wd[1][0], wd[1][1]);
+    o[1] = make_uint4(wd[2][0], wd[2][1], wd[3][0], wd[3][1]);
+    if (t == 0) sxs[b] = __uint_as_float((E - 5u) << 23);
+  }
+}
+
+CH_DEV float limb_dot(int d) { return __fsub_rn(__int_as_float(d), kLimbMagicF); }
+
+// one 576-byte tile on the integer path; acc[0..1] = row g, columns 2t / 2t+1,
+// acc[2..3] = row g+8.  xql = xq + t*4 + (g & 3).
+template <int FMT>
+CH_DEV void tile_i8(const uint8_t *tile, uint32_t kt, const uint2 *xql, const float *sxs, int lane, float (&acc)[4]) {
+  const int g = lane >> 2;
+  const uint4 w = *reinterpret_cast<const uint4 *>(tile + lane * 16);
+  uint32_t a[4];
+  int d[4];
+  if (FMT == FMT_Q4) {
+    const uint2 sc = *reinterpret_cast<const uint2 *>(tile + 512 + g * 8);  // f16 (row g | g+8: blk0, blk1)
+    const uint2 bA = xql[kt * 32], bB = xql[kt * 32 + 16];
+    const float2 sxv = *reinterpret_cast<const float2 *>(sxs + kt * 2);
+    const uint32_t M = 0xF0F0F0F0u, X = 0x80808080u;
+    a[0] = lop3_and_xor(w.x << 4, M, X);
+    a[1] = lop3_and_xor(w.x, M, X);
+    a[2] = lop3_and_xor(w.y << 4, M, X);
+    a[3] = lop3_and_xor(w.y, M, X);
+    imma_16832(d, a, bA.x, bA.y, kLimbMagicI);
+    const float2 fg = __half22float2(*reinterpret_cast<const __half2 *>(&sc.x));
+    const float2 fg8 = __half22float2(*reinterpret_cast<const __half2 *>(&sc.y));
+    float s0 = __fmul_rn(fg.x, sxv.x), s8 = __fmul_rn(fg8.x, sxv.x);
+    acc[0] = __fmaf_rn(s0, limb_dot(d[0]), acc[0]);
+    acc[1] = __fmaf_rn(s0, limb_dot(d[1]), acc[1]);
+    acc[2] = __fmaf_rn(s8, limb_dot(d[2]), acc[2]);
+    acc[3] = __fmaf_rn(s8, limb_dot(d[3]), acc[3]);
+    a[0] = lop3_and_xor(w.z << 4, M, X);
+    a[1] = lop3_and_xor(w.z, M, X);
+    a[2] = lop3_and_xor(w.w << 4, M, X);
+    a[3] = lop3_and_xor(w.w, M, X);
+    imma_16832(d, a, bB.x, bB.y, kLimbMagicI);
+    s0 = __fmul_rn(fg.y, sxv.y);
+    s8 = __fmul_rn(fg8.y, sxv.y);
+    acc[0] = __fmaf_rn(s0, limb_dot(d[0]), acc[0]);
+    acc[1] = __fmaf_rn(s0, limb_dot(d[1]), acc[1]);
+    acc[2] = __fmaf_rn(s8, limb_dot(d[2]), acc[2]);
+    acc[3] = __fmaf_rn(s8, limb_dot(d[3]), acc[3]);
+  } else {
+    const float2 sc = *reinterpret_cast<const float2 *>(tile + 512 + g * 8);  // f32 (row g, row g+8)
+    const uint2 b = xql[kt * 16];
+    const float sx = sxs[kt];
+    a[0] = __byte_perm(w.x, w.y, 0x5140u) ^ 0x80808080u;
+    a[1] = __byte_perm(w.x, w.y, 0x7362u) ^ 0x80808080u;
+    a[2] = __byte_perm(w.z, w.w, 0x5140u) ^ 0x80808080u;
+    a[3] = __byte_perm(w.z, w.w, 0x7362u) ^ 0x80808080u;
+    imma_16832(d, a, b.x, b.y, kLimbMagicI);
+    const float s0 = __fmul_rn(sc.x, sx), s8 = __fmul_rn(sc.y, sx);
+    acc[0] = __fmaf_rn(s0, limb_dot(d[0]), acc[0]);
+    acc[1] = __fmaf_rn(s0, limb_dot(d[1]), acc[1]);
+    acc[2] = __fmaf_rn(s8, limb_dot(d[2]), acc[2]);
+    acc[3] = __fmaf_rn(s8, limb_dot(d[3]), acc[3]);
+  }
+}
+
+// rows g / g+8 of two accumulator sets (valid on lanes t == 0): limb c weighs
+// 2^-7c, and Q4 bytes carry a factor 16.  Whole warp.
+template <int FMT>
+CH_DEV void limb_rows(const float (&acc)[4], const float (&accb)[4], int t, float &v0, float &v1) {
+  constexpr float f = FMT == FMT_Q4 ? 0.0625f : 1.0f;
+  const float w0 = t == 0 ? f : (t == 1 ? f * 0x1p-14f : 0.f);
+  const float w1 = t == 0 ? f * 0x1p-7f : (t == 1 ? f * 0x1p-21f : 0.f);
+  v0 = __fadd_rn(__fmul_rn(__fadd_rn(acc[0], accb[0]), w0), __fmul_rn(__fadd_rn(acc[1], accb[1]), w1));
+  v1 = __fadd_rn(__fmul_rn(__fadd_rn(acc[2], accb[2]), w0), __fmul_rn(__fadd_rn(acc[3], accb[3]), w1));
+  v0 = __fadd_rn(v0, __shfl_down_sync(0xffffffffu, v0, 1));
+  v1 = __fadd_rn(v1, __shfl_down_sync(0xffffffffu, v1, 1));
+}
+
 // One warp normalizes one head held in shared memory (in -> out, may alias):
 // rope: out = rope(rmsnorm(in) * w) with the (cos, sin) table; else unit rmsnorm.
 CH_DEV void head_norm_rope_s(const float *in, const float *w, float *out, uint32_t D, uint32_t rot, const float2 *cs,

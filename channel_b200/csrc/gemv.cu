@@ -9,13 +9,15 @@
 // B200 design: each warp streams a contiguous range of 576-byte tiles with
 // 1-D bulk copies (cp.async.bulk, mbarrier completion, SPW stages per warp) --
 // the ranges are an even "stream-K" split of all tiles over every warp of a
-// persistent grid, so any matrix shape keeps every SM streaming.  Dequant is
-// in registers (LOP3/PRMT magic-number tricks giving exact q-8 / q in f16) and
-// the 16x16 weight fragments feed mma.sync as the A operand against x split
-// into f16 hi + lo columns (B), so each 32-weight block dot product is fp32
-// accurate; the block scale is applied in f32 exactly like the shader.
-// Partial row tiles at warp-range boundaries are combined deterministically
-// (fixed order) by the last-arriving warp.  The input prologue fuses the
+// persistent grid.  With at least as many row tiles as CTAs, each CTA takes
+// whole row tiles and splits their tiles evenly over its warps (cut row tiles
+// are added in shared memory); otherwise the split is grid-wide and cut row
+// tiles are combined through global memory by the last-arriving warp.  Both
+// combines add in a fixed order.  The weights feed integer mma.sync (m16n8k32,
+// s8): a Q4 nibble becomes 16 (q - 8) by one mask-and-xor and a Q8 byte q by one
+// xor, against x as four s8 limbs per value under a power-of-two scale per
+// 32-block (core.cuh: build_limbs / tile_i8), so every block dot product is an
+// exact integer; the block scales are applied in f32.  The input prologue fuses the
 // reference's rmsnorm / add_rmsnorm passes (add_rmsnorm.wgsl:15-51) so no
 // separate norm kernel runs on the decode path.
 #include <cmath>
@@ -72,10 +74,10 @@ CH_DEV void epilogue(float *y, uint32_t rt, int g, float v0, float v1) {
 }
 
 template <int PRO>
-CH_DEV void prologue(const GemvArgs &a, float *vec, uint4 *xf, float *red) {
+CH_DEV void prologue(const GemvArgs &a, float *vec, uint2 *xq, float *sxs, float *red) {
   const uint32_t K = a.K, nb = K / 32;
   if (PRO == PRO_NONE) {
-    build_fragments(a.x, xf, K);
+    build_limbs(a.x, xq, sxs, K);
     return;
   }
   const bool writer = (blockIdx.x == 0);
@@ -124,7 +126,7 @@ CH_DEV void prologue(const GemvArgs &a, float *vec, uint4 *xf, float *red) {
     if (writer && a.normed_out) a.normed_out[i] = v;
   }
   __syncthreads();
-  build_fragments(vec, xf, K);
+  build_limbs(vec, xq, sxs, K);
 }
 
 template <int FMT, int EPI, int PRO>
@@ -132,9 +134,9 @@ __global__ void __launch_bounds__(NW * 32, 1) gemv_kernel(const GemvArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
   uint8_t *stages = smem;
   uint64_t *bars = reinterpret_cast<uint64_t *>(smem + NW * SPW * kStageBytes);
-  uint4 *xzero = reinterpret_cast<uint4 *>(smem + NW * SPW * kStageBytes + NW * SPW * 8);
-  uint4 *xf = xzero + 1;
-  float *vec = reinterpret_cast<float *>(xf + (a.K / 32) * 8);
+  float *vec = reinterpret_cast<float *>(smem + NW * SPW * kStageBytes + NW * SPW * 8);  // norm prologues: K floats
+  uint2 *xq = reinterpret_cast<uint2 *>(vec + (PRO == PRO_NONE ? 0u : a.K));              // input limbs
+  float *sxs = reinterpret_cast<float *>(xq + (a.K / 32) * 16);                           // their block scales
   __shared__ float red[32];
   __shared__ float cpart[NW][2][16];  // CTA-local mode: partial row-tile sums, [warp][first/last segment][row]
 
@@ -169,19 +171,17 @@ __global__ void __launch_bounds__(NW * 32, 1) gemv_kernel(const GemvArgs a) {
       bulk_g2s(my_stages + (size_t)j * kStageBytes, a.tiles + t0 * kTileBytes, bytes, &my_bars[j]);
     }
   }
-  if (threadIdx.x == 0) *xzero = make_uint4(0u, 0u, 0u, 0u);
   __syncwarp();
 
   grid_dep_wait();
-  prologue<PRO>(a, vec, xf, red);
+  prologue<PRO>(a, vec, xq, sxs, red);
   __syncthreads();
   grid_dep_launch();
 
-  const uint4 *xb = (g < 2) ? xf + t * 2 + g : xzero;
-  const uint32_t xs = (g < 2) ? 8u : 0u;
+  const uint2 *xql = xq + t * 4 + (g & 3);
   uint64_t cur_rt = ~0ull, rt = 0;
   uint32_t kt_begin = 0, kt = 0;
-  float a0 = 0.f, a1 = 0.f, b0 = 0.f, b1 = 0.f;  // two accumulator chains (even / odd tiles)
+  float acc[4] = {0.f, 0.f, 0.f, 0.f}, accb[4] = {0.f, 0.f, 0.f, 0.f};  // two chains (even / odd tiles)
   bool first_seg = true;
   if (nchunks > 0) {
     rt = tb / KT;
@@ -189,7 +189,8 @@ __global__ void __launch_bounds__(NW * 32, 1) gemv_kernel(const GemvArgs a) {
   }
 
   auto flush = [&](uint64_t frt, uint32_t kb, uint32_t ke) {
-    const float acc0 = __fadd_rn(a0, b0), acc1 = __fadd_rn(a1, b1);
+    float acc0, acc1;
+    limb_rows<FMT>(acc, accb, t, acc0, acc1);
     const bool full = (kb == 0 && ke == (uint32_t)KT);
     if (full) {
       if (t == 0) epilogue<EPI>(a.y, (uint32_t)frt, g, acc0, acc1);
@@ -248,7 +249,8 @@ __global__ void __launch_bounds__(NW * 32, 1) gemv_kernel(const GemvArgs a) {
         if (cur_rt != ~0ull) flush(cur_rt, kt_begin, (uint32_t)KT);
         cur_rt = rt;
         kt_begin = kt;
-        a0 = a1 = b0 = b1 = 0.f;
+#pragma unroll
+        for (int c = 0; c < 4; c++) acc[c] = accb[c] = 0.f;
       }
       // a run of tiles inside one row tile: no per-tile boundary checks
       const uint32_t run = min(nt - i, (uint32_t)KT - kt);
@@ -257,17 +259,17 @@ __global__ void __launch_bounds__(NW * 32, 1) gemv_kernel(const GemvArgs a) {
       if (run == CT) {
 #pragma unroll
         for (int q = 0; q < CT; q += 2) {
-          tile_mma<FMT>(p + q * kTileBytes, kt + q, xb, xs, lane, a0, a1);
-          tile_mma<FMT>(p + (q + 1) * kTileBytes, kt + q + 1, xb, xs, lane, b0, b1);
+          tile_i8<FMT>(p + q * kTileBytes, kt + q, xql, sxs, lane, acc);
+          tile_i8<FMT>(p + (q + 1) * kTileBytes, kt + q + 1, xql, sxs, lane, accb);
         }
         r = CT;
       } else {
         for (; r + 2 <= run; r += 2) {
-          tile_mma<FMT>(p + r * kTileBytes, kt + r, xb, xs, lane, a0, a1);
-          tile_mma<FMT>(p + (r + 1) * kTileBytes, kt + r + 1, xb, xs, lane, b0, b1);
+          tile_i8<FMT>(p + r * kTileBytes, kt + r, xql, sxs, lane, acc);
+          tile_i8<FMT>(p + (r + 1) * kTileBytes, kt + r + 1, xql, sxs, lane, accb);
         }
         if (r < run) {
-          tile_mma<FMT>(p + r * kTileBytes, kt + r, xb, xs, lane, a0, a1);
+          tile_i8<FMT>(p + r * kTileBytes, kt + r, xql, sxs, lane, acc);
           r++;
         }
       }
@@ -318,7 +320,7 @@ __global__ void __launch_bounds__(NW * 32, 1) gemv_kernel(const GemvArgs a) {
 
 template <int FMT, int EPI, int PRO>
 static cudaError_t launch_gemv_t(const GemvArgs &a, int grid, cudaStream_t s, bool pdl) {
-  size_t smem = (size_t)NW * SPW * kStageBytes + NW * SPW * 8 + 16 + (size_t)(a.K / 32) * 128;
+  size_t smem = (size_t)NW * SPW * kStageBytes + NW * SPW * 8 + (size_t)(a.K / 32) * (128 + 4);
   if (PRO != PRO_NONE) smem += (size_t)a.K * 4;
   static size_t attr_bytes = 0;  // dynamic smem opt-in granted so far (static smem counts against 227 KB)
   if (smem > 48 * 1024 && smem > attr_bytes) {
@@ -345,11 +347,11 @@ cudaError_t launch_gemv(const GemvPlan &p, const GemvArgs &a0, cudaStream_t s, b
   if (a0.K % 32 != 0) return cudaErrorInvalidValue;
   int grid = p.grid > 0 ? p.grid : gemv_default_grid();
   // Whole row tiles per CTA (stream-K over its warps, cut rows added in shared memory)
-  // when that keeps the CTAs within 10% of an even share -- e.g. the 1920 row tiles
-  // of the 12B gate|up matrix on 148 CTAs; otherwise the grid-wide stream-K split.
+  // whenever every CTA gets at least one: even an uneven share (240 row tiles on 148
+  // CTAs) beats the grid-wide split, whose cross-CTA combine (fences, counters, a
+  // second pass over global partials) costs several microseconds per launch.
   GemvArgs a = a0;
-  const double per_cta = (double)a.row_tiles / grid;
-  a.cta_rows = per_cta >= 1.0 && std::ceil(per_cta) <= 1.1 * per_cta;
+  a.cta_rows = a.row_tiles >= (uint32_t)grid;
 #define CH_GEMV_CASE(F, E, P) \
   if (p.fmt == F && p.epi == E && p.pro == P) return launch_gemv_t<F, E, P>(a, grid, s, pdl);
   CH_GEMV_CASE(FMT_Q4, EPI_STORE, PRO_NONE)
