@@ -57,6 +57,28 @@ CH_DEV uint64_t globaltimer_ns() {
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
   return t;
 }
+CH_DEV bool mbar_test_wait(uint64_t *bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// bounded wait that polls without suspending (for waits the whole CTA takes at once,
+// where a suspended warp's wake-up would delay the CTA's next barrier)
+CH_DEV bool mbar_spin_bounded(uint64_t *bar, uint32_t parity, uint32_t *err, uint64_t limit_ns = 2000000000ull) {
+  if (mbar_test_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (;;) {
+    for (int i = 0; i < 64; i++)
+      if (mbar_test_wait(bar, parity)) return true;
+    if (globaltimer_ns() - t0 > limit_ns) break;
+  }
+  if (err) atomicOr(err, DEV_ERR_TMA_TIMEOUT);
+  return false;
+}
 // bounded wait (wall-clock limit); returns false and records the error when it gives up
 CH_DEV bool mbar_wait_bounded(uint64_t *bar, uint32_t parity, uint32_t *err,
                               uint64_t limit_ns = 2000000000ull) {

@@ -146,15 +146,30 @@ CH_DEV float straddle_value(const GemvOut &o, const uint32_t *slist, const uint3
   }
   return v;
 }
-// Patch the straddling rows of staged (non-act) output rows [r0, r1), dst[i] = row r0 + i
+// rows q .. q+3 (q % 4 == 0) of straddle entry k: 16-byte loads of the two CTAs'
+// partial slots when exactly two CTAs share the row tile
+CH_DEV float4 straddle_quad(const GemvOut &o, const uint32_t *slist, const uint32_t *soff, const float *P, uint32_t k,
+                            uint32_t q) {
+  const uint32_t off = soff[k];
+  if (off != kNoStraddle) {
+    const float4 x = *reinterpret_cast<const float4 *>(P + (off & 0xFFFFu) + q);
+    const float4 y = *reinterpret_cast<const float4 *>(P + (off >> 16) + q);
+    return make_float4(__fadd_rn(__fadd_rn(0.f, x.x), y.x), __fadd_rn(__fadd_rn(0.f, x.y), y.y),
+                       __fadd_rn(__fadd_rn(0.f, x.z), y.z), __fadd_rn(__fadd_rn(0.f, x.w), y.w));
+  }
+  return make_float4(straddle_value(o, slist, soff, P, k, q), straddle_value(o, slist, soff, P, k, q + 1),
+                     straddle_value(o, slist, soff, P, k, q + 2), straddle_value(o, slist, soff, P, k, q + 3));
+}
+// Patch the straddling rows of staged (non-act) output rows [r0, r1) (both multiples
+// of 4; dst 16-byte aligned), dst[i] = row r0 + i; four rows per thread
 CH_DEV void patch_staged(const GemvOut &o, const uint32_t *slist, const uint32_t *soff, const float *P, uint32_t r0,
                          uint32_t r1, float *dst) {
-  const uint32_t n = (gridDim.x - 1) * 16;
-  for (uint32_t idx = threadIdx.x; idx < n; idx += blockDim.x) {
-    const uint32_t k = idx >> 4, rt = slist[k];
+  const uint32_t items = (gridDim.x - 1) * 4;
+  for (uint32_t idx = threadIdx.x; idx < items; idx += blockDim.x) {
+    const uint32_t k = idx >> 2, rt = slist[k];
     if (rt == kNoStraddle) continue;
-    const uint32_t row = idx & 15u, r = rt * 16 + row;
-    if (r >= r0 && r < r1) dst[r - r0] = straddle_value(o, slist, soff, P, k, row);
+    const uint32_t q = (idx & 3u) * 4, r = rt * 16 + q;
+    if (r >= r0 && r + 4 <= r1) *reinterpret_cast<float4 *>(dst + (r - r0)) = straddle_quad(o, slist, soff, P, k, q);
   }
 }
 
@@ -298,15 +313,15 @@ CH_DEV void out_act_pair(const MegaArgs &a, const GemvOut &o, uint32_t j, float 
 // rt*8 + i = gelu(gate row i) * up row i+8) into a staged B-fragment array
 CH_DEV void patch_act_frag(const GemvOut &o, const uint32_t *slist, const uint32_t *soff, const float *P, uint32_t K,
                            uint32_t *frag) {
-  const uint32_t n = (gridDim.x - 1) * 4;
-  for (uint32_t idx = threadIdx.x; idx < n; idx += blockDim.x) {
-    const uint32_t k = idx >> 2, rt = slist[k];
+  const uint32_t n = (gridDim.x - 1) * 2;
+  for (uint32_t idx = threadIdx.x; idx < n; idx += blockDim.x) {  // act values rt*8 + i .. +3, i = 0 / 4
+    const uint32_t k = idx >> 1, rt = slist[k];
     if (rt == kNoStraddle) continue;
-    const uint32_t i = (idx & 3u) * 2, j = rt * 8 + i;
-    if (j >= K) continue;
-    const float g0 = straddle_value(o, slist, soff, P, k, i), g1 = straddle_value(o, slist, soff, P, k, i + 1);
-    const float u0 = straddle_value(o, slist, soff, P, k, i + 8), u1 = straddle_value(o, slist, soff, P, k, i + 9);
-    store_frag_pair(frag, j, __fmul_rn(gelu_tanh(g0), u0), __fmul_rn(gelu_tanh(g1), u1));
+    const uint32_t i = (idx & 1u) * 4, j = rt * 8 + i;
+    if (j + 4 > K) continue;
+    const float4 gv = straddle_quad(o, slist, soff, P, k, i), uv = straddle_quad(o, slist, soff, P, k, i + 8);
+    store_frag_pair(frag, j, __fmul_rn(gelu_tanh(gv.x), uv.x), __fmul_rn(gelu_tanh(gv.y), uv.y));
+    store_frag_pair(frag, j + 2, __fmul_rn(gelu_tanh(gv.z), uv.z), __fmul_rn(gelu_tanh(gv.w), uv.w));
   }
 }
 // ld_pair without shared-memory bank conflicts: the pairs of one half-warp cover
@@ -427,7 +442,7 @@ struct GemvStage {
 };
 
 // GEMV input: B fragments of the phase's input vector, in place over S0
-CH_DEV void gemv_prologue(const Phase &p, const MegaArgs &a, const SmemLayout &L, float *red) {
+CH_DEV void gemv_prologue(const Phase &p, const MegaArgs &a, const SmemLayout &L, float *red, uint32_t pi) {
   const uint32_t K = p.K, npairs = K / 8, tid = threadIdx.x;
   GemvStage S(L.u, K, p.pm);
   uint4 *xf = reinterpret_cast<uint4 *>(S.s0);
@@ -445,6 +460,7 @@ CH_DEV void gemv_prologue(const Phase &p, const MegaArgs &a, const SmemLayout &L
   if (p.pm == PM_ADD_NORM) {  // x = (x_in + [rmsnorm(r) * post_w]) * scalar     (add_rmsnorm.wgsl:15-51)
     patch_staged(p.r_in, L.slist, L.soff, S.part, 0, K, S.s0);
     __syncthreads();
+    PHASE_MARK(pi, 7);
     float r[8];
 #pragma unroll
     for (int e = 0; e < 8; e++) r[e] = 0.f;
@@ -778,22 +794,24 @@ CH_DEV void attn_phase(const Phase &p, const MegaArgs &a, const StepParams &sp, 
   AttnSmem<R> sm(L.u, chunk_cap, max_splits);
   const uint32_t *wp = L.wphys + p.is_sliding * kWinSlots;
 
-  // 0. straddling rows of the staged heads (q heads, k, v: three row ranges)
+  // 0. straddling rows of the staged heads (q heads, k, v: three row ranges, each a
+  //    multiple of 4 rows, so a quad of rows never crosses one)
   {
-    const uint32_t n16 = (gridDim.x - 1) * 16;
+    const uint32_t n4 = (gridDim.x - 1) * 4;
     const uint32_t q0 = kvh * R * D, k0 = a.nq * D + kvh * D, v0 = a.nq * D + (uint32_t)kv_dim + kvh * D;
-    for (uint32_t idx = tid; idx < n16; idx += MK_THREADS) {
-      const uint32_t e = L.slist[idx / 16];
+    for (uint32_t idx = tid; idx < n4; idx += MK_THREADS) {
+      const uint32_t e = L.slist[idx / 4];
       if (e == kNoStraddle) continue;
-      const uint32_t row = idx % 16, r = (e & 0xFFFFu) * 16 + row;
+      const uint32_t q = (idx % 4) * 4, r = (e & 0xFFFFu) * 16 + q;
       float *dst = nullptr;
       if (r >= q0 && r < q0 + R * D) dst = sm.q_s + (r - q0);
       else if (r >= k0 && r < k0 + D) dst = sm.k_new + (r - k0);
       else if (r >= v0 && r < v0 + D) dst = sm.v_new + (r - v0);
-      if (dst) *dst = straddle_value(p.r_in, L.slist, L.soff, sm.part, idx / 16, row);
+      if (dst) *reinterpret_cast<float4 *>(dst) = straddle_quad(p.r_in, L.slist, L.soff, sm.part, idx / 4, q);
     }
   }
   __syncthreads();
+  PHASE_MARK(pi, 7);
   // 1. q heads | k | v of this kv head: warp h norms and ropes head h in registers, in place
   if (warp < R + 2) {
     float *hd = warp < R ? sm.q_s + warp * D : (warp == R ? sm.k_new : sm.v_new);
@@ -1258,11 +1276,11 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(const MegaAr
     PHASE_MARK(pi, 0);
     if (pi + 2 < a.nphases) copy_phase(a.phases + pi + 2, &ph_s[(pi + 2) % 3]);
     post_copies<R>(p, a, sp_s, L);
-    if (!mbar_wait_bounded(L.vbar, vpar, a.err)) ok = false;
+    if (!mbar_spin_bounded(L.vbar, vpar, a.err)) ok = false;
     vpar ^= 1u;
     PHASE_MARK(pi, 1);
     if (p.kind == PH_GEMV) {
-      gemv_prologue(p, a, L, red);
+      gemv_prologue(p, a, L, red, pi);
       __syncthreads();
       PHASE_MARK(pi, 2);
       const uint4 *xf = reinterpret_cast<const uint4 *>(L.u);

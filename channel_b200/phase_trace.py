@@ -12,6 +12,7 @@ points of every phase:
   4 phase done (GEMV: CTA combine; ATTN: split combine)
   5 arrived at the next barrier and issued the next phase's early copies
   6 next barrier passed
+  7 (inside the prologue) GEMV add+norm: straddling rows patched / ATTN: q|k|v rows patched
 
 A phase's cost is taken from the slowest CTA at each point (the grid waits for
 it); the per-CTA table shows median / max of each interval for layer 1.
@@ -39,6 +40,7 @@ def main() -> None:
     ap.add_argument("--steps", type=int, default=4)
     ap.add_argument("--clock", type=int, default=599, help="decode position (active slots = clock + 1)")
     ap.add_argument("--lib", default=None, help="an already built instrumented library (default: build it)")
+    ap.add_argument("--dump", default=None, help="also save the raw [cta][phase][8 marks] ns array (.npy)")
     args = ap.parse_args()
 
     from channel_b200 import _lib as L
@@ -89,6 +91,8 @@ def main() -> None:
         gm.deinit()
         ctx.deinit()
         return
+    if args.dump:
+        np.save(args.dump, buf.reshape(TRACE_CTAS, TRACE_PHASES, TRACE_MARKS)[:grid, :nph])
     tr = buf.reshape(TRACE_CTAS, TRACE_PHASES, TRACE_MARKS)[:grid, :nph, :7].astype(np.int64)
     kinds = ["qkv", "attn", "o", "gateup", "down"]
 
