@@ -2,9 +2,9 @@
 must produce the oracle's greedy tokens, like the single-GPU model.
 
 CPU tests cover the shard checks of the C-ABI and the handle exchange over a
-gloo process group of two ranks; the GPU test runs two ranks on two GPUs (it is
-skipped on a box with fewer) with bounded device waits, so a rank that fails
-makes the other return an error instead of hanging."""
+gloo process group of two ranks; the GPU test runs 2, 4 and 8 ranks, one per GPU
+(each skipped on a box with fewer GPUs), with bounded device waits, so a rank that
+fails makes the others return an error instead of hanging."""
 import ctypes as C
 import os
 import socket
@@ -83,6 +83,11 @@ def test_handle_exchange_gloo_two_ranks():
 SEED = 5
 
 
+def _tp_config(world):
+    """the small test model; 4 and 8 ranks need 8 kv heads (one or two per rank)"""
+    return small_config() if world <= 2 else small_config(num_attention_heads=16, num_key_value_heads=8)
+
+
 def _tp_worker(rank, world, port, xs, plan, prompt, slots, n_prev, q):
     try:
         import torch.distributed as dist
@@ -92,7 +97,7 @@ def _tp_worker(rank, world, port, xs, plan, prompt, slots, n_prev, q):
         torch.cuda.set_device(rank)
         dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
         ctx = GpuContext.init(rank)
-        cfg = small_config()
+        cfg = _tp_config(world)
         gm = GpuModelContext.synthetic_sharded(ctx, cfg, SEED, rank, world)
         attach_tensor_parallel(gm)
         gm.zero_state()
@@ -128,11 +133,12 @@ def _tp_worker(rank, world, port, xs, plan, prompt, slots, n_prev, q):
 
 
 @pytest.mark.gpu
-def test_tp2_decode_matches_oracle(oracle):
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs 2 GPUs")
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_tp_decode_matches_oracle(oracle, world):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     from channel_b200 import DynamicRingBuffer
-    cfg = small_config()
+    cfg = _tp_config(world)
     w = oracle.SyntheticWeights(cfg, SEED)
     om = oracle.Model(cfg, w)
     ring = DynamicRingBuffer(cfg.num_hidden_layers, 0)
@@ -167,16 +173,17 @@ def test_tp2_decode_matches_oracle(oracle):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    ps = [ctx.Process(target=_tp_worker, args=(r, 2, port, xs, plan, prompt, slots, len(prev), q)) for r in range(2)]
+    ps = [ctx.Process(target=_tp_worker, args=(r, world, port, xs, plan, prompt, slots, len(prev), q))
+          for r in range(world)]
     for p in ps:
         p.start()
     res = {}
-    for _ in range(2):
+    for _ in range(world):
         rank, host, first, loop, err = q.get(timeout=600)
         res[rank] = (host, first, loop, err)
     for p in ps:
         p.join(timeout=120)
-    for rank in range(2):
+    for rank in range(world):
         host, first, loop, err = res[rank]
         assert err is None, f"rank {rank}: {err}"
         for step, ((gtok, gids, gvals), (rtok, rid, rvals)) in enumerate(zip(host, ref)):
@@ -184,4 +191,5 @@ def test_tp2_decode_matches_oracle(oracle):
             assert np.allclose(gvals, rvals[:8], rtol=1e-3, atol=1e-3)
         assert first == int(ptok), f"rank {rank}: prefill token"
         assert loop == loop_ref, f"rank {rank}: device-loop tokens after prefill"
-    assert res[0][0] == res[1][0]
+    for rank in range(1, world):
+        assert res[rank][0] == res[0][0]
