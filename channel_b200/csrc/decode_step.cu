@@ -50,7 +50,7 @@ constexpr int MK_SPW = CH_MK_SPW;  // bulk-copy stages per warp
 constexpr int MK_CT = CH_MK_CT;    // tiles per stage
 constexpr int MK_STAGE = MK_CT * kTileBytes;
 constexpr int MK_THREADS = MK_NW * 32;
-constexpr uint32_t kMinChunk = 64;
+constexpr uint32_t kMinChunk = 32;  // slots per attention work item before splitting further stops paying
 constexpr uint32_t kWinSlots = 64;  // attention slots per work item staged in shared memory before the barrier
 constexpr uint32_t kNoStraddle = 0xFFFFFFFFu;
 constexpr int kHeadDim = 256;
@@ -732,8 +732,10 @@ CH_DEV void attn_lists_init(const MegaArgs &a, const StepParams &sp, uint32_t *w
   }
 }
 
-// before the barrier: bulk copies of the window's K/V rows, the head norm weights
-// and the RoPE table into shared memory; the rest of the chunk toward L2
+// before the barrier: the window's K/V rows as 16-byte cp.async pieces (each thread
+// waits for its own in attn_phase; one bulk copy per 512-byte row measured slower),
+// bulk copies of the head norm weights and the RoPE table, and the chunk's slots
+// beyond the window toward L2
 template <int R>
 CH_DEV void attn_pre(const Phase &p, const MegaArgs &a, const StepParams &sp, const SmemLayout &L) {
   constexpr int D = kHeadDim;
@@ -743,20 +745,21 @@ CH_DEV void attn_pre(const Phase &p, const MegaArgs &a, const StepParams &sp, co
   const size_t kv_dim = (size_t)a.nkv * D;
   const uint32_t *wp = L.wphys + p.is_sliding * kWinSlots;
   const uint32_t t = threadIdx.x;
-  // one 512-byte row per thread (K rows, then V rows); thread 0 registers all their bytes at once
-  const uint32_t i = t % kWinSlots, which = t / kWinSlots;
-  const uint32_t phys = (t < 2 * kWinSlots && i < it.n) ? wp[i] : 0xFFFFFFFFu;
-  const bool copy = phys < a.cache_slots && phys != sp.slot;
-  const uint32_t nrows = __syncthreads_count(copy);
   if (t == 0) {
-    mbar_expect_tx(L.vbar, nrows * D * 2);
     stage_copy(L, sm.qn_w, p.q_norm_w, D * 4);
     stage_copy(L, sm.kn_w, p.k_norm_w, D * 4);
     stage_copy(L, sm.cs, p.rope_cs, a.rot * 4);  // rot/2 (cos, sin) pairs
   }
-  if (copy)
-    bulk_g2s(sm.kv + (size_t)(which * kWinSlots + i) * D,
-             (which ? p.v_cache : p.k_cache) + (size_t)phys * kv_dim + (size_t)it.kvh * D, D * 2, L.vbar);
+  constexpr uint32_t kPieces = D * 2 / 16;  // 16-byte pieces per row
+  for (uint32_t piece = t; piece < 2 * kWinSlots * kPieces; piece += MK_THREADS) {
+    const uint32_t row = piece / kPieces, sub = piece % kPieces;
+    const uint32_t which = row / kWinSlots, i = row % kWinSlots;  // K rows, then V rows
+    if (i >= it.n) continue;
+    const uint32_t phys = wp[i];
+    if (phys >= a.cache_slots || phys == sp.slot) continue;
+    cp_async16(sm.kv + (size_t)row * D + sub * 8,
+               (which ? p.v_cache : p.k_cache) + (size_t)phys * kv_dim + (size_t)it.kvh * D + sub * 8);
+  }
   for (uint32_t i = kWinSlots + threadIdx.x; i < it.n; i += MK_THREADS) {
     const uint32_t phys = __ldcg(it.list + it.c0 + i);
     if (phys < a.cache_slots) {
@@ -868,6 +871,7 @@ CH_DEV void attn_phase(const Phase &p, const MegaArgs &a, const StepParams &sp, 
     *reinterpret_cast<float4 *>(hd + lane * 8 + 4) = make_float4(out[4], out[5], out[6], out[7]);
   }
   if (it.split == 0 && sp.slot >= a.cache_slots && tid == 0) atomicOr(a.err, DEV_ERR_BAD_SLOT);
+  cp_async_wait_all();  // this thread's pieces of the K/V window (attn_pre)
   __syncthreads();
   PHASE_MARK(pi, 2);
 
