@@ -121,9 +121,10 @@ CH_DEV void tile_mma(const uint8_t *tile, uint32_t kt, const uint4 *xb, uint32_t
 // m16n8k32 as s8 without a float dequant: a Q4 nibble q becomes the byte
 // 16 * (q - 8) by one mask-and-xor, a Q8 byte (stored q ^ 0x80) becomes q by one
 // xor.  The input enters as four s8 limbs per value against a power-of-two scale
-// per 32-block, x = sx * (l0 + l1 / 2^7 + l2 / 2^14 + l3 / 2^21) with every
-// |limb| <= 64, so each block dot product is an exact int32 and x is kept to
-// 2^-27 of the block's largest magnitude.  Limb c is B column c (lanes g >= 4
+// per 32-block, x = sx * (l0 + l1 / 2^7 + l2 / 2^14 + l3 / 2^21): X = rint(x /
+// sx * 2^21) is a 27-bit integer, l0 = X >> 21 in [-64, 63] and l1..l3 its 7-bit
+// fields in [0, 127], so each block dot product is an exact int32 and x is kept
+// to 2^-27 of the block's largest magnitude.  Limb c is B column c (lanes g >= 4
 // repeat columns 0..3; those results are not used).  The accumulators start at
 // 1.5 * 2^23 in integer form, so a result's float view minus 1.5 * 2^23 is the
 // exact dot product (|dot| < 2^22) with no integer-to-float conversion.
@@ -136,10 +137,46 @@ CH_DEV void tile_mma(const uint8_t *tile, uint32_t kt, const uint4 *xb, uint32_t
 constexpr float kLimbMagicF = 12582912.0f;  // 1.5 * 2^23
 constexpr int kLimbMagicI = 0x4B400000;     // its bit pattern
 
-// x (K floats, global or shared) -> xq[b*16 + t*4 + c] = limb c of the 8 values
-// of block b that lane quad t multiplies (k = {2t, 2t+8, 2t+1, 2t+9} and +16),
-// sxs[b] = 2^(e-6) where max|x_b| < 2^e.  One (block b, quad t) item per thread;
-// a block's 4 items sit on 4 aligned lanes of one warp (blockDim.x % 32 == 0).
+// One (32-block b, lane quad t) item: e = the 8 values of block b that quad t
+// multiplies, in register byte order (k = 2t, 2t+8, 2t+1, 2t+9, then +16) ->
+// xq[b*16 + t*4 + c] = their limb c, sxs[b] = 2^(e-6) where max|x_b| < 2^e.  The 4
+// items of a block run on the 4 lanes of an aligned quad at the same time; their
+// shuffles for the block maximum come after every read of the inputs and before any
+// write, so the limbs may overwrite the block's own inputs in place.
+CH_DEV void limb_item(const float (&e)[8], uint32_t b, uint32_t t, uint2 *xq, float *sxs) {
+  float m = 0.f;
+#pragma unroll
+  for (int j = 0; j < 8; j++) m = fmaxf(m, fabsf(e[j]));
+  const uint32_t quad = 0xFu << (threadIdx.x & 28u);
+  m = fmaxf(m, __shfl_xor_sync(quad, m, 1));
+  m = fmaxf(m, __shfl_xor_sync(quad, m, 2));
+  // biased exponent E: m < 2^(E-126); X = rint(x * 2^(153-E)) has |X| < 2^27
+  const uint32_t E = max((__float_as_uint(m) >> 23) & 0xFFu, 26u);
+  const float scale = __uint_as_float((280u - E) << 23);
+  int X[8];
+#pragma unroll
+  for (int j = 0; j < 8; j++) X[j] = __float2int_rn(__fmul_rn(e[j], scale));
+  uint32_t wd[4][2];  // limb c of values 4h .. 4h+3, one byte each
+#pragma unroll
+  for (int h = 0; h < 2; h++) {
+    const int *x = X + 4 * h;
+    wd[0][h] = __byte_perm(__byte_perm(x[0] >> 21, x[1] >> 21, 0x0040u), __byte_perm(x[2] >> 21, x[3] >> 21, 0x0040u),
+                           0x5410u);
+#pragma unroll
+    for (int c = 1; c < 4; c++) {
+      const int sh = 21 - 7 * c;
+      wd[c][h] = __byte_perm(__byte_perm(x[0] >> sh, x[1] >> sh, 0x0040u), __byte_perm(x[2] >> sh, x[3] >> sh, 0x0040u),
+                             0x5410u) &
+                 0x7F7F7F7Fu;
+    }
+  }
+  uint4 *o = reinterpret_cast<uint4 *>(xq + b * 16 + t * 4);
+  o[0] = make_uint4(wd[0][0], wd[0][1], wd[1][0], wd[1][1]);
+  o[1] = make_uint4(wd[2][0], wd[2][1], wd[3][0], wd[3][1]);
+  if (t == 0) sxs[b] = __uint_as_float((E - 5u) << 23);
+}
+// x (K floats, global or shared) -> the limbs of every block; one item per thread
+// (blockDim.x % 32 == 0).  In place (v == xq) is allowed.
 CH_DEV void build_limbs(const float *v, uint2 *xq, float *sxs, uint32_t K) {
   for (uint32_t idx = threadIdx.x; idx < K / 32 * 4; idx += blockDim.x) {
     const uint32_t b = idx >> 2, t = idx & 3;
@@ -147,37 +184,7 @@ CH_DEV void build_limbs(const float *v, uint2 *xq, float *sxs, uint32_t K) {
     const float2 e0 = *reinterpret_cast<const float2 *>(p), e1 = *reinterpret_cast<const float2 *>(p + 8);
     const float2 e2 = *reinterpret_cast<const float2 *>(p + 16), e3 = *reinterpret_cast<const float2 *>(p + 24);
     const float e[8] = {e0.x, e1.x, e0.y, e1.y, e2.x, e3.x, e2.y, e3.y};
-    float m = 0.f;
-#pragma unroll
-    for (int j = 0; j < 8; j++) m = fmaxf(m, fabsf(e[j]));
-    const uint32_t quad = 0xFu << (threadIdx.x & 28u);
-    m = fmaxf(m, __shfl_xor_sync(quad, m, 1));
-    m = fmaxf(m, __shfl_xor_sync(quad, m, 2));
-    // biased exponent E: m < 2^(E-126); scale 2^(132-E) puts |x| below 64
-    const uint32_t E = max((__float_as_uint(m) >> 23) & 0xFFu, 6u);
-    const float scale = __uint_as_float((259u - E) << 23);
-    uint32_t by[4][8];  // limb c of value j in the low byte (float view of 1.5 * 2^23 + limb)
-#pragma unroll
-    for (int j = 0; j < 8; j++) {
-      float u = __fmul_rn(e[j], scale);
-#pragma unroll
-      for (int c = 0; c < 4; c++) {
-        const float r = __fadd_rn(u, kLimbMagicF);  // round to nearest integer
-        by[c][j] = __float_as_uint(r);
-        if (c < 3) u = __fmul_rn(__fsub_rn(u, __fsub_rn(r, kLimbMagicF)), 128.0f);  // exact remainder
-      }
-    }
-    uint32_t wd[4][2];
-#pragma unroll
-    for (int c = 0; c < 4; c++)
-#pragma unroll
-      for (int h = 0; h < 2; h++)
-        wd[c][h] = __byte_perm(__byte_perm(by[c][4 * h], by[c][4 * h + 1], 0x0040u),
-                               __byte_perm(by[c][4 * h + 2], by[c][4 * h + 3], 0x0040u), 0x5410u);
-    uint4 *o = reinterpret_cast<uint4 *>(xq + b * 16 + t * 4);
-    o[0] = make_uint4(wd[0][0], wd[0][1], wd[1][0], wd[1][1]);
-    o[1] = make_uint4(wd[2][0], wd[2][1], wd[3][0], wd[3][1]);
-    if (t == 0) sxs[b] = __uint_as_float((E - 5u) << 23);
+    limb_item(e, b, t, xq, sxs);
   }
 }
 

@@ -228,7 +228,8 @@ CH_DEV void grid_wait(const unsigned long long *ctr, bool sys, unsigned long lon
 
 // ---------------------------------------------------------------------------
 // input pairs: pair p = (32-block b = p/4, t = p%4) holds the 8 values at
-// k = 32b + 2t + {0,1, 8,9, 16,17, 24,25} -- exactly one lane's B fragments
+// k = 32b + 2t + {0,1, 8,9, 16,17, 24,25} -- exactly one lane quad's share of the
+// 32-block in the GEMV tiles' B operand
 CH_DEV void ld_pair(const float *src, uint32_t p, float (&v)[8]) {
   const float *q = src + (p >> 2) * 32 + (p & 3u) * 2;
 #pragma unroll
@@ -242,33 +243,13 @@ CH_DEV void st_pair(float *dst, uint32_t p, const float (&v)[8]) {
 #pragma unroll
   for (int i = 0; i < 4; i++) *reinterpret_cast<float2 *>(q + 8 * i) = make_float2(v[2 * i], v[2 * i + 1]);
 }
-// f16 hi/lo B fragments of a pair: xf[p*2] = hi, xf[p*2+1] = lo (layout of block_to_fragments).
-// xf[p*2 .. p*2+1] occupies the bytes of floats [8p, 8p+8) of the same 32-block, so a
-// staged vector can be converted in place once every pair of the block has been read.
-CH_DEV void pair_to_fragments(const float (&v)[8], uint4 *xf_pair) {
-  __half h[8], l[8];
-#pragma unroll
-  for (int e = 0; e < 8; e++) {
-    h[e] = __float2half_rn(v[e]);
-    l[e] = __float2half_rn(__fsub_rn(v[e], __half2float(h[e])));
-  }
-  xf_pair[0] = make_uint4(pack_half2(h[0], h[1]), pack_half2(h[2], h[3]), pack_half2(h[4], h[5]), pack_half2(h[6], h[7]));
-  xf_pair[1] = make_uint4(pack_half2(l[0], l[1]), pack_half2(l[2], l[3]), pack_half2(l[4], l[5]), pack_half2(l[6], l[7]));
-}
-
-// u32 word of a B-fragment array (layout of pair_to_fragments) that holds
-// elements (j, j+1), j even, of the K-vector: hi half (hl = 0) or lo half (hl = 1)
-CH_DEV uint32_t frag_word(uint32_t j, uint32_t hl) {
-  const uint32_t b = j >> 5, k = j & 31u;
-  return ((b * 4 + ((k & 7u) >> 1)) * 2 + hl) * 4 + (k >> 3);
-}
-// f16 hi/lo split of elements (j, j+1) into a B-fragment array (shared or global)
-CH_DEV void store_frag_pair(uint32_t *frag, uint32_t j, float v0, float v1) {
-  const __half h0 = __float2half_rn(v0), h1 = __float2half_rn(v1);
-  const __half l0 = __float2half_rn(__fsub_rn(v0, __half2float(h0)));
-  const __half l1 = __float2half_rn(__fsub_rn(v1, __half2float(h1)));
-  frag[frag_word(j, 0)] = pack_half2(h0, h1);
-  frag[frag_word(j, 1)] = pack_half2(l0, l1);
+// Input limbs of pair p (values v in ld_pair order) -- the GEMV tiles' B operand
+// (core.cuh: limb_item / tile_i8).  A pair's limb words take the bytes of floats
+// [8p, 8p+8) of its own 32-block, and the block's 4 pairs run on one aligned lane
+// quad, so a staged vector converts in place.  sxs = the block scales (K/32 floats).
+CH_DEV void pair_to_limbs(const float (&v)[8], uint32_t p, uint2 *xq, float *sxs) {
+  const float e[8] = {v[0], v[2], v[1], v[3], v[4], v[6], v[5], v[7]};
+  limb_item(e, p >> 2, p & 3u, xq, sxs);
 }
 // epochs of the low-latency exchanges of this launch start after this value
 __shared__ unsigned long long s_xep;
@@ -300,19 +281,19 @@ CH_DEV void out_row(const MegaArgs &a, const GemvOut &o, uint32_t row, float v) 
   }
   for (uint32_t r = 0; r < a.world; r++) on_rank(a, o.direct, r)[o.row0 + row] = v;
 }
-// act values (j, j+1) (local index, j even) of a gate|up GEMV as B fragments
+// act values (j, j+1) (local index, j even) of a gate|up GEMV
 CH_DEV void out_act_pair(const MegaArgs &a, const GemvOut &o, uint32_t j, float v0, float v1) {
-  uint32_t *f = reinterpret_cast<uint32_t *>(o.direct);
   if (!o.push) {
-    store_frag_pair(f, j, v0, v1);
+    *reinterpret_cast<float2 *>(o.direct + j) = make_float2(v0, v1);
     return;
   }
-  for (uint32_t r = 0; r < a.world; r++) store_frag_pair(on_rank(a, f, r), o.row0 + j, v0, v1);
+  for (uint32_t r = 0; r < a.world; r++)
+    *reinterpret_cast<float2 *>(on_rank(a, o.direct, r) + o.row0 + j) = make_float2(v0, v1);
 }
 // Patch the act values of straddling gate|up row tiles (8 per row tile, act index
-// rt*8 + i = gelu(gate row i) * up row i+8) into a staged B-fragment array
-CH_DEV void patch_act_frag(const GemvOut &o, const uint32_t *slist, const uint32_t *soff, const float *P, uint32_t K,
-                           uint32_t *frag) {
+// rt*8 + i = gelu(gate row i) * up row i+8) into the staged act vector
+CH_DEV void patch_act(const GemvOut &o, const uint32_t *slist, const uint32_t *soff, const float *P, uint32_t K,
+                      float *act) {
   const uint32_t n = (gridDim.x - 1) * 2;
   for (uint32_t idx = threadIdx.x; idx < n; idx += blockDim.x) {  // act values rt*8 + i .. +3, i = 0 / 4
     const uint32_t k = idx >> 1, rt = slist[k];
@@ -320,8 +301,9 @@ CH_DEV void patch_act_frag(const GemvOut &o, const uint32_t *slist, const uint32
     const uint32_t i = (idx & 1u) * 4, j = rt * 8 + i;
     if (j + 4 > K) continue;
     const float4 gv = straddle_quad(o, slist, soff, P, k, i), uv = straddle_quad(o, slist, soff, P, k, i + 8);
-    store_frag_pair(frag, j, __fmul_rn(gelu_tanh(gv.x), uv.x), __fmul_rn(gelu_tanh(gv.y), uv.y));
-    store_frag_pair(frag, j + 2, __fmul_rn(gelu_tanh(gv.z), uv.z), __fmul_rn(gelu_tanh(gv.w), uv.w));
+    *reinterpret_cast<float4 *>(act + j) =
+        make_float4(__fmul_rn(gelu_tanh(gv.x), uv.x), __fmul_rn(gelu_tanh(gv.y), uv.y),
+                    __fmul_rn(gelu_tanh(gv.z), uv.z), __fmul_rn(gelu_tanh(gv.w), uv.w));
   }
 }
 // ld_pair without shared-memory bank conflicts: the pairs of one half-warp cover
@@ -413,7 +395,6 @@ struct SmemLayout {
   uint8_t *stages;
   uint64_t *bars;
   uint64_t *vbar;   // staged activations: two arrivals per phase (before and after the grid barrier)
-  uint4 *xzero;
   float *wpart;     // [warps][2][16] partial segments of the current GEMV phase
   uint32_t *slist;  // [kMaxGrid] straddle list of the current phase's input
   uint32_t *soff;   // [kMaxGrid] its partial-slot offsets
@@ -426,9 +407,10 @@ CH_DEV void stage_copy(const SmemLayout &L, void *dst, const void *src, uint32_t
   bulk_g2s(dst, src, bytes, L.vbar);
 }
 
-// GEMV staging in the union region (K floats each): S0 = previous output (then the
-// B fragments, in place); for the norm prologues S1 = residual, S2 = post-norm
-// weight, S3 = norm weight; then the straddle partials of the previous GEMV.
+// GEMV staging in the union region (K floats each): S0 = previous output (then its
+// limbs, in place, with their block scales over the start of what follows); for the
+// norm prologues S1 = residual, S2 = post-norm weight, S3 = norm weight; then the
+// straddle partials of the previous GEMV.
 CH_DEV uint32_t gemv_stage_vectors(uint32_t pm) { return (pm == PM_NORM || pm == PM_ADD_NORM) ? 4u : 1u; }
 struct GemvStage {
   float *s0, *s1, *s2, *s3, *part;
@@ -441,15 +423,24 @@ struct GemvStage {
   }
 };
 
-// GEMV input: B fragments of the phase's input vector, in place over S0
+// GEMV input: the limbs of the phase's input vector, in place over S0, and their
+// block scales over the first K/32 floats after it
 CH_DEV void gemv_prologue(const Phase &p, const MegaArgs &a, const SmemLayout &L, float *red, uint32_t pi) {
   const uint32_t K = p.K, npairs = K / 8, tid = threadIdx.x;
   GemvStage S(L.u, K, p.pm);
-  uint4 *xf = reinterpret_cast<uint4 *>(S.s0);
+  uint2 *xq = reinterpret_cast<uint2 *>(S.s0);
+  float *sxs = S.s0 + K;
   const bool writer = (blockIdx.x == 0);
-  if (p.pm == PM_DIRECT) return;  // S0 holds the producer's B fragments
-  if (p.pm == PM_GELU) {           // S0 holds the B fragments of gelu(gate) * up; add the straddling ones
-    patch_act_frag(p.r_in, L.slist, L.soff, S.part, K, reinterpret_cast<uint32_t *>(S.s0));
+  if (p.pm == PM_DIRECT || p.pm == PM_GELU) {  // S0 holds the producer's f32 vector (attention out / act)
+    if (p.pm == PM_GELU) {                     // add the straddling act values (from the partials after S0)
+      patch_act(p.r_in, L.slist, L.soff, S.part, K, S.s0);
+      __syncthreads();
+    }
+    for (uint32_t q = tid; q < npairs; q += MK_THREADS) {  // a block's 4 pairs: one aligned quad, one pass
+      float v[8];
+      ld_pair_rot(S.s0, q, v);
+      pair_to_limbs(v, q, xq, sxs);
+    }
     return;
   }
   // PM_NORM / PM_ADD_NORM: one pair per thread (K <= 8 * threads)
@@ -516,7 +507,7 @@ CH_DEV void gemv_prologue(const Phase &p, const MegaArgs &a, const SmemLayout &L
   float ss = 0.f;
 #pragma unroll
   for (int e = 0; e < 8; e++) ss = __fmaf_rn(x[e], x[e], ss);
-  ss = block_sum(ss, red);  // also orders every read of S0 before the in-place fragment writes
+  ss = block_sum(ss, red);  // also orders every read of S0 / S1 before the in-place limb writes
   const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)K), a.eps)));
   if (on) {
     float nw[8], v[8];
@@ -524,7 +515,7 @@ CH_DEV void gemv_prologue(const Phase &p, const MegaArgs &a, const SmemLayout &L
 #pragma unroll
     for (int e = 0; e < 8; e++) v[e] = __fmul_rn(__fmul_rn(x[e], inv), nw[e]);
     if (writer && p.normed_out) st_pair(p.normed_out, tid, v);
-    pair_to_fragments(v, xf + tid * 2);
+    pair_to_limbs(v, tid, xq, sxs);
   }
 }
 
@@ -551,7 +542,7 @@ CH_DEV void cta_combine(const Phase &p, const MegaArgs &a, const float *wpart) {
       }
     const float up = __shfl_down_sync(0xffffffffu, sum, 8);
     if (inside) {
-      if (p.out.act) {  // act values of lanes 0..7 as B fragments, in pairs
+      if (p.out.act) {  // act values of lanes 0..7, in pairs
         const float av = __fmul_rn(gelu_tanh(sum), up);
         const float an = __shfl_down_sync(0xffffffffu, av, 1);
         if (lane < 8 && !(lane & 1)) out_act_pair(a, p.out, rt * 8 + lane, av, an);
@@ -565,8 +556,8 @@ CH_DEV void cta_combine(const Phase &p, const MegaArgs &a, const float *wpart) {
 }
 
 template <int FMT>
-CH_DEV void gemv_tiles(const Phase &p, const MegaArgs &a, uint32_t gw, const SmemLayout &L, const uint4 *xf,
-                       uint32_t &cidx, Stream &st, bool &ok, uint64_t pol) {
+CH_DEV void gemv_tiles(const Phase &p, const MegaArgs &a, uint32_t gw, const SmemLayout &L, const uint2 *xq,
+                       const float *sxs, uint32_t &cidx, Stream &st, bool &ok, uint64_t pol) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int g = lane >> 2, t = lane & 3;
   uint8_t *my_stages = L.stages + (size_t)warp * MK_SPW * MK_STAGE;
@@ -574,13 +565,13 @@ CH_DEV void gemv_tiles(const Phase &p, const MegaArgs &a, uint32_t gw, const Sme
   const uint32_t KT = p.k_tiles;
   const uint32_t tb = warp_begin(p.out.pt, blockIdx.x, warp), te = warp_begin(p.out.pt, blockIdx.x, warp + 1);
   const uint32_t nchunks = (te - tb + MK_CT - 1) / MK_CT;
-  const uint4 *xb = (g < 2) ? xf + t * 2 + g : L.xzero;
-  const uint32_t xs = (g < 2) ? 8u : 0u;
+  const uint2 *xql = xq + t * 4 + (g & 3);
   uint32_t rt = tb / KT, kt = tb - (tb / KT) * KT, cur_rt = 0xFFFFFFFFu, kt_begin = 0;
-  float a0 = 0.f, a1 = 0.f, b0 = 0.f, b1 = 0.f;
+  float acc[4] = {0.f, 0.f, 0.f, 0.f}, accb[4] = {0.f, 0.f, 0.f, 0.f};  // two chains (even / odd tiles)
   bool first_seg = true;
   auto flush = [&](uint32_t frt, uint32_t kb, uint32_t ke) {
-    const float acc0 = __fadd_rn(a0, b0), acc1 = __fadd_rn(a1, b1);
+    float acc0, acc1;
+    limb_rows<FMT>(acc, accb, t, acc0, acc1);
     // act mode: lanes t == 0 hold act value g of the row tile; pair g, g+1 (lane + 4)
     const float av = __fmul_rn(gelu_tanh(acc0), acc1);
     const float an = __shfl_down_sync(0xffffffffu, av, 4);
@@ -612,7 +603,8 @@ CH_DEV void gemv_tiles(const Phase &p, const MegaArgs &a, uint32_t gw, const Sme
         if (cur_rt != 0xFFFFFFFFu) flush(cur_rt, kt_begin, KT);
         cur_rt = rt;
         kt_begin = kt;
-        a0 = a1 = b0 = b1 = 0.f;
+#pragma unroll
+        for (int c = 0; c < 4; c++) acc[c] = accb[c] = 0.f;
       }
       const uint32_t run = min(nt - i, KT - kt);
       const uint8_t *pp = stg + (size_t)i * kTileBytes;
@@ -620,16 +612,16 @@ CH_DEV void gemv_tiles(const Phase &p, const MegaArgs &a, uint32_t gw, const Sme
       if (run == MK_CT) {
 #pragma unroll
         for (int q = 0; q < MK_CT; q += 2) {
-          tile_mma<FMT>(pp + q * kTileBytes, kt + q, xb, xs, lane, a0, a1);
-          tile_mma<FMT>(pp + (q + 1) * kTileBytes, kt + q + 1, xb, xs, lane, b0, b1);
+          tile_i8<FMT>(pp + q * kTileBytes, kt + q, xql, sxs, lane, acc);
+          tile_i8<FMT>(pp + (q + 1) * kTileBytes, kt + q + 1, xql, sxs, lane, accb);
         }
         r = MK_CT;
       } else {
         for (; r + 2 <= run; r += 2) {
-          tile_mma<FMT>(pp + r * kTileBytes, kt + r, xb, xs, lane, a0, a1);
-          tile_mma<FMT>(pp + (r + 1) * kTileBytes, kt + r + 1, xb, xs, lane, b0, b1);
+          tile_i8<FMT>(pp + r * kTileBytes, kt + r, xql, sxs, lane, acc);
+          tile_i8<FMT>(pp + (r + 1) * kTileBytes, kt + r + 1, xql, sxs, lane, accb);
         }
-        if (r < run) tile_mma<FMT>(pp + r * kTileBytes, kt + r, xb, xs, lane, a0, a1);
+        if (r < run) tile_i8<FMT>(pp + r * kTileBytes, kt + r, xql, sxs, lane, acc);
       }
       i += run;
       kt += run;
@@ -672,16 +664,16 @@ CH_DEV AttnItem attn_item(const MegaArgs &a, const StepParams &sp, uint32_t is_s
   return it;
 }
 
-// attention output elements (j, j+1) of this rank's heads as B fragments of the
-// o-projection input: local buffer (one GPU, or tensor parallel with a row-parallel o
-// projection reading this rank's heads only), or every rank's copy at the rank's
-// global head offset
-CH_DEV void attn_out_pair(const MegaArgs &a, uint32_t *frag, uint32_t j, float v0, float v1) {
+// attention output elements (j, j+1), j even, of this rank's heads (the o-projection
+// input): local buffer (one GPU, or tensor parallel with a row-parallel o projection
+// reading this rank's heads only), or every rank's copy at the rank's global head offset
+CH_DEV void attn_out_pair(const MegaArgs &a, float *out, uint32_t j, float v0, float v1) {
   if (a.world <= 1 || a.attn_local) {
-    store_frag_pair(frag, j, v0, v1);
+    *reinterpret_cast<float2 *>(out + j) = make_float2(v0, v1);
     return;
   }
-  for (uint32_t r = 0; r < a.world; r++) store_frag_pair(on_rank(a, frag, r), a.attn_q0 * kHeadDim + j, v0, v1);
+  for (uint32_t r = 0; r < a.world; r++)
+    *reinterpret_cast<float2 *>(on_rank(a, out, r) + a.attn_q0 * kHeadDim + j) = make_float2(v0, v1);
 }
 
 // Shared-memory layout of the ATTN phase (inside the union region).
@@ -970,7 +962,7 @@ CH_DEV void attn_phase(const Phase &p, const MegaArgs &a, const StepParams &sp, 
     }
   }
   __syncthreads();
-  uint32_t *out_frag = reinterpret_cast<uint32_t *>(p.attn_out);  // B fragments of the o-projection input
+  float *attn_o = p.attn_out;  // the o-projection input
   if (it.nsplit == 1) {  // whole list in this CTA: normalize and write (same arithmetic as a 1-split combine)
     for (int idx = tid; idx < R * D; idx += MK_THREADS) {  // R*D is a multiple of 32: whole warps
       const int h = idx / D, d = idx % D;
@@ -980,7 +972,7 @@ CH_DEV void attn_phase(const Phase &p, const MegaArgs &a, const StepParams &sp, 
       const float Lsum = __fmaf_rn(sm.stat[2 * h + 1], 1.0f, 0.f);
       const float o = __fmul_rn(__fmaf_rn(s, 1.0f, 0.f), __fdiv_rn(1.0f, __fadd_rn(Lsum, 1e-9f)));
       const float on = __shfl_down_sync(0xffffffffu, o, 1);
-      if (!(idx & 1)) attn_out_pair(a, out_frag, (kvh * R + h) * D + d, o, on);
+      if (!(idx & 1)) attn_out_pair(a, attn_o, (kvh * R + h) * D + d, o, on);
     }
     return;
   }
@@ -1056,7 +1048,7 @@ CH_DEV void attn_phase(const Phase &p, const MegaArgs &a, const StepParams &sp, 
     o = __fmul_rn(O, sm.stat[2 * h]);
   }
   const float on = __shfl_down_sync(0xffffffffu, o, 1);
-  if (mine && !(idx & 1)) attn_out_pair(a, out_frag, (kvh * R + h) * D + d, o, on);
+  if (mine && !(idx & 1)) attn_out_pair(a, attn_o, (kvh * R + h) * D + d, o, on);
 }
 
 // ---------------------------------------------------------------------------
@@ -1236,8 +1228,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(const MegaAr
   L.stages = smem;
   L.bars = reinterpret_cast<uint64_t *>(smem + MK_NW * MK_SPW * MK_STAGE);
   L.vbar = L.bars + MK_NW * MK_SPW;
-  L.xzero = reinterpret_cast<uint4 *>(L.vbar + 2);
-  L.wpart = reinterpret_cast<float *>(L.xzero + 1);
+  L.wpart = reinterpret_cast<float *>(L.vbar + 2);
   L.slist = reinterpret_cast<uint32_t *>(L.wpart + MK_NW * 2 * 16);
   L.soff = L.slist + kMaxGrid + 1;
   L.wphys = L.soff + kMaxGrid + 1;
@@ -1261,7 +1252,6 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(const MegaAr
       if (stream_next(a, gw, st)) stream_issue(st, my_stages + (size_t)s * MK_STAGE, &my_bars[s], pol);
   }
   if (threadIdx.x == 0) {
-    *L.xzero = make_uint4(0u, 0u, 0u, 0u);
     sp_s = *a.sp;
     s_abort = (*(volatile uint32_t *)a.err & DEV_ERR_PEER_TIMEOUT) ? 1u : 0u;
     s_xep = a.base[2];
@@ -1287,11 +1277,12 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(const MegaAr
       gemv_prologue(p, a, L, red, pi);
       __syncthreads();
       PHASE_MARK(pi, 2);
-      const uint4 *xf = reinterpret_cast<const uint4 *>(L.u);
+      const uint2 *xq = reinterpret_cast<const uint2 *>(L.u);
+      const float *sxs = reinterpret_cast<const float *>(L.u) + p.K;
       if (p.fmt == FMT_Q4)
-        gemv_tiles<FMT_Q4>(p, a, gw, L, xf, cidx, st, ok, pol);
+        gemv_tiles<FMT_Q4>(p, a, gw, L, xq, sxs, cidx, st, ok, pol);
       else
-        gemv_tiles<FMT_Q8>(p, a, gw, L, xf, cidx, st, ok, pol);
+        gemv_tiles<FMT_Q8>(p, a, gw, L, xq, sxs, cidx, st, ok, pol);
       __syncthreads();
       PHASE_MARK(pi, 3);
       cta_combine(p, a, L.wpart);
@@ -1341,7 +1332,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(const MegaAr
 
 size_t mk_smem_bytes(uint32_t max_k, uint32_t hidden, uint32_t ratio, uint32_t max_splits, uint32_t cache_slots,
                      uint32_t grid) {
-  const size_t fixed = (size_t)MK_NW * MK_SPW * MK_STAGE + (MK_NW * MK_SPW + 2) * 8 + 16 + MK_NW * 2 * 16 * 4 +
+  const size_t fixed = (size_t)MK_NW * MK_SPW * MK_STAGE + (MK_NW * MK_SPW + 2) * 8 + MK_NW * 2 * 16 * 4 +
                       2 * (kMaxGrid + 1) * 4 + 2 * kWinSlots * 4;
   const size_t part = (size_t)grid * 32 * 4;  // straddle partials of the previous GEMV
   // GEMV staging: 4 vectors of `hidden` for the norm prologues, one of max_k otherwise

@@ -451,7 +451,7 @@ static int build_phases(ch_model *m, bool with_logits, Phase **d_out, uint32_t *
     p.scalar = 1.0f;
     return p;
   };
-  float *attn_frag = m->attn;  // this rank's heads only (row-parallel o)
+  float *attn_in = m->attn;  // this rank's heads only (row-parallel o)
   std::vector<Phase> ph;
   const uint32_t rh = m->cfg.rotary_dim / 2;
   uint32_t nx = 0;          // exchanges numbered in phase order: o of layer l = 2l, down = 2l + 1
@@ -485,12 +485,12 @@ static int build_phases(ch_model *m, bool with_logits, Phase **d_out, uint32_t *
     at.v_cache = dl.vc;
     at.is_sliding = dl.full ? 0 : 1;
     at.attn_scale = 1.0f;  // Gemma-style: q/k norms replace 1/sqrt(d) (forward.zig:85)
-    at.attn_out = attn_frag;
+    at.attn_out = attn_in;
     ph.push_back(at);
     Phase o = gemv(GK_O, dl.o, FMT_Q4, m->qd_l);
     if (o.out.push == 2) o.out.xidx = nx++;
     o.pm = PM_DIRECT;
-    o.x_in = attn_frag;
+    o.x_in = attn_in;
     ph.push_back(o);
     Phase gu = gemv(GK_GU, dl.gateup, FMT_Q4, m->H);
     gu.pm = PM_ADD_NORM;

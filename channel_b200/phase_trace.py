@@ -7,7 +7,7 @@ time of one token goes.  Each CTA's thread 0 records %globaltimer at seven
 points of every phase:
 
   0 phase start (grid barrier passed)    1 staged inputs landed (bulk copies)
-  2 GEMV: B fragments built / ATTN: heads normed and roped
+  2 GEMV: input limbs built / ATTN: heads normed and roped
   3 GEMV: weight tiles done / ATTN: split partial written
   4 phase done (GEMV: CTA combine; ATTN: split combine)
   5 arrived at the next barrier and issued the next phase's early copies
