@@ -251,6 +251,22 @@ CH_DEV void pair_to_limbs(const float (&v)[8], uint32_t p, uint2 *xq, float *sxs
   const float e[8] = {v[0], v[2], v[1], v[3], v[4], v[6], v[5], v[7]};
   limb_item(e, p >> 2, p & 3u, xq, sxs);
 }
+
+// u32 word of a B-fragment array (f16 hi/lo B fragments of tile_mma: [32-block][t][hi | lo] uint4) that holds
+// elements (j, j+1), j even, of the K-vector: hi half (hl = 0) or lo half (hl = 1)
+CH_DEV uint32_t frag_word(uint32_t j, uint32_t hl) {
+  const uint32_t b = j >> 5, k = j & 31u;
+  return ((b * 4 + ((k & 7u) >> 1)) * 2 + hl) * 4 + (k >> 3);
+}
+// f16 hi/lo split of elements (j, j+1) into a B-fragment array (shared or global)
+CH_DEV void store_frag_pair(uint32_t *frag, uint32_t j, float v0, float v1) {
+  const __half h0 = __float2half_rn(v0), h1 = __float2half_rn(v1);
+  const __half l0 = __float2half_rn(__fsub_rn(v0, __half2float(h0)));
+  const __half l1 = __float2half_rn(__fsub_rn(v1, __half2float(h1)));
+  frag[frag_word(j, 0)] = pack_half2(h0, h1);
+  frag[frag_word(j, 1)] = pack_half2(l0, l1);
+}
+
 // epochs of the low-latency exchanges of this launch start after this value
 __shared__ unsigned long long s_xep;
 // set when a wait on another rank gave up: later cross-rank waits of the launch return at once
@@ -281,19 +297,19 @@ CH_DEV void out_row(const MegaArgs &a, const GemvOut &o, uint32_t row, float v) 
   }
   for (uint32_t r = 0; r < a.world; r++) on_rank(a, o.direct, r)[o.row0 + row] = v;
 }
-// act values (j, j+1) (local index, j even) of a gate|up GEMV
+// act values (j, j+1) (local index, j even) of a gate|up GEMV as B fragments
 CH_DEV void out_act_pair(const MegaArgs &a, const GemvOut &o, uint32_t j, float v0, float v1) {
+  uint32_t *f = reinterpret_cast<uint32_t *>(o.direct);
   if (!o.push) {
-    *reinterpret_cast<float2 *>(o.direct + j) = make_float2(v0, v1);
+    store_frag_pair(f, j, v0, v1);
     return;
   }
-  for (uint32_t r = 0; r < a.world; r++)
-    *reinterpret_cast<float2 *>(on_rank(a, o.direct, r) + o.row0 + j) = make_float2(v0, v1);
+  for (uint32_t r = 0; r < a.world; r++) store_frag_pair(on_rank(a, f, r), o.row0 + j, v0, v1);
 }
 // Patch the act values of straddling gate|up row tiles (8 per row tile, act index
-// rt*8 + i = gelu(gate row i) * up row i+8) into the staged act vector
-CH_DEV void patch_act(const GemvOut &o, const uint32_t *slist, const uint32_t *soff, const float *P, uint32_t K,
-                      float *act) {
+// rt*8 + i = gelu(gate row i) * up row i+8) into a staged B-fragment array
+CH_DEV void patch_act_frag(const GemvOut &o, const uint32_t *slist, const uint32_t *soff, const float *P, uint32_t K,
+                           uint32_t *frag) {
   const uint32_t n = (gridDim.x - 1) * 2;
   for (uint32_t idx = threadIdx.x; idx < n; idx += blockDim.x) {  // act values rt*8 + i .. +3, i = 0 / 4
     const uint32_t k = idx >> 1, rt = slist[k];
@@ -301,9 +317,8 @@ CH_DEV void patch_act(const GemvOut &o, const uint32_t *slist, const uint32_t *s
     const uint32_t i = (idx & 1u) * 4, j = rt * 8 + i;
     if (j + 4 > K) continue;
     const float4 gv = straddle_quad(o, slist, soff, P, k, i), uv = straddle_quad(o, slist, soff, P, k, i + 8);
-    *reinterpret_cast<float4 *>(act + j) =
-        make_float4(__fmul_rn(gelu_tanh(gv.x), uv.x), __fmul_rn(gelu_tanh(gv.y), uv.y),
-                    __fmul_rn(gelu_tanh(gv.z), uv.z), __fmul_rn(gelu_tanh(gv.w), uv.w));
+    store_frag_pair(frag, j, __fmul_rn(gelu_tanh(gv.x), uv.x), __fmul_rn(gelu_tanh(gv.y), uv.y));
+    store_frag_pair(frag, j + 2, __fmul_rn(gelu_tanh(gv.z), uv.z), __fmul_rn(gelu_tanh(gv.w), uv.w));
   }
 }
 // ld_pair without shared-memory bank conflicts: the pairs of one half-warp cover
@@ -395,6 +410,7 @@ struct SmemLayout {
   uint8_t *stages;
   uint64_t *bars;
   uint64_t *vbar;   // staged activations: two arrivals per phase (before and after the grid barrier)
+  uint4 *xzero;     // a zero B fragment (f16 tiles: the lanes without an x column)
   float *wpart;     // [warps][2][16] partial segments of the current GEMV phase
   uint32_t *slist;  // [kMaxGrid] straddle list of the current phase's input
   uint32_t *soff;   // [kMaxGrid] its partial-slot offsets
@@ -407,10 +423,11 @@ CH_DEV void stage_copy(const SmemLayout &L, void *dst, const void *src, uint32_t
   bulk_g2s(dst, src, bytes, L.vbar);
 }
 
-// GEMV staging in the union region (K floats each): S0 = previous output (then its
-// limbs, in place, with their block scales over the start of what follows); for the
-// norm prologues S1 = residual, S2 = post-norm weight, S3 = norm weight; then the
-// straddle partials of the previous GEMV.
+// GEMV staging in the union region (K floats each): S0 = previous output (norm
+// prologues: then its limbs, in place, with their block scales over the start of
+// S1; o / down: the producer's B fragments); for the norm prologues S1 = residual,
+// S2 = post-norm weight, S3 = norm weight; then the straddle partials of the
+// previous GEMV.
 CH_DEV uint32_t gemv_stage_vectors(uint32_t pm) { return (pm == PM_NORM || pm == PM_ADD_NORM) ? 4u : 1u; }
 struct GemvStage {
   float *s0, *s1, *s2, *s3, *part;
@@ -423,24 +440,21 @@ struct GemvStage {
   }
 };
 
-// GEMV input: the limbs of the phase's input vector, in place over S0, and their
-// block scales over the first K/32 floats after it
+// GEMV input.  Norm prologues (q|k|v, gate|up, LM head): the limbs of the normed
+// vector, in place over S0, and their block scales over the first K/32 floats after
+// it -- integer tiles.  PM_DIRECT / PM_GELU (o, down): S0 already holds the
+// producer's f16 hi/lo B fragments (attention out / GELU*up), patched for the
+// straddling act values -- f16 tiles; building limbs of those long vectors in every
+// CTA (one item per 8 values) cost more than the integer tiles save.
 CH_DEV void gemv_prologue(const Phase &p, const MegaArgs &a, const SmemLayout &L, float *red, uint32_t pi) {
   const uint32_t K = p.K, npairs = K / 8, tid = threadIdx.x;
   GemvStage S(L.u, K, p.pm);
   uint2 *xq = reinterpret_cast<uint2 *>(S.s0);
   float *sxs = S.s0 + K;
   const bool writer = (blockIdx.x == 0);
-  if (p.pm == PM_DIRECT || p.pm == PM_GELU) {  // S0 holds the producer's f32 vector (attention out / act)
-    if (p.pm == PM_GELU) {                     // add the straddling act values (from the partials after S0)
-      patch_act(p.r_in, L.slist, L.soff, S.part, K, S.s0);
-      __syncthreads();
-    }
-    for (uint32_t q = tid; q < npairs; q += MK_THREADS) {  // a block's 4 pairs: one aligned quad, one pass
-      float v[8];
-      ld_pair_rot(S.s0, q, v);
-      pair_to_limbs(v, q, xq, sxs);
-    }
+  if (p.pm == PM_DIRECT) return;
+  if (p.pm == PM_GELU) {
+    patch_act_frag(p.r_in, L.slist, L.soff, S.part, K, reinterpret_cast<uint32_t *>(S.s0));
     return;
   }
   // PM_NORM / PM_ADD_NORM: one pair per thread (K <= 8 * threads)
@@ -542,7 +556,7 @@ CH_DEV void cta_combine(const Phase &p, const MegaArgs &a, const float *wpart) {
       }
     const float up = __shfl_down_sync(0xffffffffu, sum, 8);
     if (inside) {
-      if (p.out.act) {  // act values of lanes 0..7, in pairs
+      if (p.out.act) {  // act values of lanes 0..7 as B fragments, in pairs
         const float av = __fmul_rn(gelu_tanh(sum), up);
         const float an = __shfl_down_sync(0xffffffffu, av, 1);
         if (lane < 8 && !(lane & 1)) out_act_pair(a, p.out, rt * 8 + lane, av, an);
@@ -555,7 +569,9 @@ CH_DEV void cta_combine(const Phase &p, const MegaArgs &a, const float *wpart) {
   }
 }
 
-template <int FMT>
+// LIMBS: integer tiles against the input limbs (xq, sxs); else f16 tiles against the
+// f16 hi/lo B fragments at xq (sxs unused)
+template <int FMT, bool LIMBS>
 CH_DEV void gemv_tiles(const Phase &p, const MegaArgs &a, uint32_t gw, const SmemLayout &L, const uint2 *xq,
                        const float *sxs, uint32_t &cidx, Stream &st, bool &ok, uint64_t pol) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -566,12 +582,26 @@ CH_DEV void gemv_tiles(const Phase &p, const MegaArgs &a, uint32_t gw, const Sme
   const uint32_t tb = warp_begin(p.out.pt, blockIdx.x, warp), te = warp_begin(p.out.pt, blockIdx.x, warp + 1);
   const uint32_t nchunks = (te - tb + MK_CT - 1) / MK_CT;
   const uint2 *xql = xq + t * 4 + (g & 3);
+  // f16 path: lanes g < 2 read the hi / lo column, the others a zero page
+  const uint4 *xb = (g < 2) ? reinterpret_cast<const uint4 *>(xq) + t * 2 + g : L.xzero;
+  const uint32_t xs = (g < 2) ? 8u : 0u;
   uint32_t rt = tb / KT, kt = tb - (tb / KT) * KT, cur_rt = 0xFFFFFFFFu, kt_begin = 0;
   float acc[4] = {0.f, 0.f, 0.f, 0.f}, accb[4] = {0.f, 0.f, 0.f, 0.f};  // two chains (even / odd tiles)
   bool first_seg = true;
+  auto tile = [&](const uint8_t *tp, uint32_t k, float(&ac)[4]) {
+    if constexpr (LIMBS)
+      tile_i8<FMT>(tp, k, xql, sxs, lane, ac);
+    else
+      tile_mma<FMT>(tp, k, xb, xs, lane, ac[0], ac[1]);
+  };
   auto flush = [&](uint32_t frt, uint32_t kb, uint32_t ke) {
     float acc0, acc1;
-    limb_rows<FMT>(acc, accb, t, acc0, acc1);
+    if constexpr (LIMBS) {
+      limb_rows<FMT>(acc, accb, t, acc0, acc1);
+    } else {
+      acc0 = __fadd_rn(acc[0], accb[0]);
+      acc1 = __fadd_rn(acc[1], accb[1]);
+    }
     // act mode: lanes t == 0 hold act value g of the row tile; pair g, g+1 (lane + 4)
     const float av = __fmul_rn(gelu_tanh(acc0), acc1);
     const float an = __shfl_down_sync(0xffffffffu, av, 4);
@@ -612,16 +642,16 @@ CH_DEV void gemv_tiles(const Phase &p, const MegaArgs &a, uint32_t gw, const Sme
       if (run == MK_CT) {
 #pragma unroll
         for (int q = 0; q < MK_CT; q += 2) {
-          tile_i8<FMT>(pp + q * kTileBytes, kt + q, xql, sxs, lane, acc);
-          tile_i8<FMT>(pp + (q + 1) * kTileBytes, kt + q + 1, xql, sxs, lane, accb);
+          tile(pp + q * kTileBytes, kt + q, acc);
+          tile(pp + (q + 1) * kTileBytes, kt + q + 1, accb);
         }
         r = MK_CT;
       } else {
         for (; r + 2 <= run; r += 2) {
-          tile_i8<FMT>(pp + r * kTileBytes, kt + r, xql, sxs, lane, acc);
-          tile_i8<FMT>(pp + (r + 1) * kTileBytes, kt + r + 1, xql, sxs, lane, accb);
+          tile(pp + r * kTileBytes, kt + r, acc);
+          tile(pp + (r + 1) * kTileBytes, kt + r + 1, accb);
         }
-        if (r < run) tile_i8<FMT>(pp + r * kTileBytes, kt + r, xql, sxs, lane, acc);
+        if (r < run) tile(pp + r * kTileBytes, kt + r, acc);
       }
       i += run;
       kt += run;
@@ -664,16 +694,16 @@ CH_DEV AttnItem attn_item(const MegaArgs &a, const StepParams &sp, uint32_t is_s
   return it;
 }
 
-// attention output elements (j, j+1), j even, of this rank's heads (the o-projection
-// input): local buffer (one GPU, or tensor parallel with a row-parallel o projection
-// reading this rank's heads only), or every rank's copy at the rank's global head offset
-CH_DEV void attn_out_pair(const MegaArgs &a, float *out, uint32_t j, float v0, float v1) {
+// attention output elements (j, j+1) of this rank's heads as B fragments of the
+// o-projection input: local buffer (one GPU, or tensor parallel with a row-parallel o
+// projection reading this rank's heads only), or every rank's copy at the rank's
+// global head offset
+CH_DEV void attn_out_pair(const MegaArgs &a, uint32_t *frag, uint32_t j, float v0, float v1) {
   if (a.world <= 1 || a.attn_local) {
-    *reinterpret_cast<float2 *>(out + j) = make_float2(v0, v1);
+    store_frag_pair(frag, j, v0, v1);
     return;
   }
-  for (uint32_t r = 0; r < a.world; r++)
-    *reinterpret_cast<float2 *>(on_rank(a, out, r) + a.attn_q0 * kHeadDim + j) = make_float2(v0, v1);
+  for (uint32_t r = 0; r < a.world; r++) store_frag_pair(on_rank(a, frag, r), a.attn_q0 * kHeadDim + j, v0, v1);
 }
 
 // Shared-memory layout of the ATTN phase (inside the union region).
@@ -962,7 +992,7 @@ CH_DEV void attn_phase(const Phase &p, const MegaArgs &a, const StepParams &sp, 
     }
   }
   __syncthreads();
-  float *attn_o = p.attn_out;  // the o-projection input
+  uint32_t *attn_o = reinterpret_cast<uint32_t *>(p.attn_out);  // B fragments of the o-projection input
   if (it.nsplit == 1) {  // whole list in this CTA: normalize and write (same arithmetic as a 1-split combine)
     for (int idx = tid; idx < R * D; idx += MK_THREADS) {  // R*D is a multiple of 32: whole warps
       const int h = idx / D, d = idx % D;
@@ -1228,7 +1258,8 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(const MegaAr
   L.stages = smem;
   L.bars = reinterpret_cast<uint64_t *>(smem + MK_NW * MK_SPW * MK_STAGE);
   L.vbar = L.bars + MK_NW * MK_SPW;
-  L.wpart = reinterpret_cast<float *>(L.vbar + 2);
+  L.xzero = reinterpret_cast<uint4 *>(L.vbar + 2);
+  L.wpart = reinterpret_cast<float *>(L.xzero + 1);
   L.slist = reinterpret_cast<uint32_t *>(L.wpart + MK_NW * 2 * 16);
   L.soff = L.slist + kMaxGrid + 1;
   L.wphys = L.soff + kMaxGrid + 1;
@@ -1252,6 +1283,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(const MegaAr
       if (stream_next(a, gw, st)) stream_issue(st, my_stages + (size_t)s * MK_STAGE, &my_bars[s], pol);
   }
   if (threadIdx.x == 0) {
+    *L.xzero = make_uint4(0u, 0u, 0u, 0u);
     sp_s = *a.sp;
     s_abort = (*(volatile uint32_t *)a.err & DEV_ERR_PEER_TIMEOUT) ? 1u : 0u;
     s_xep = a.base[2];
@@ -1279,10 +1311,12 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(const MegaAr
       PHASE_MARK(pi, 2);
       const uint2 *xq = reinterpret_cast<const uint2 *>(L.u);
       const float *sxs = reinterpret_cast<const float *>(L.u) + p.K;
-      if (p.fmt == FMT_Q4)
-        gemv_tiles<FMT_Q4>(p, a, gw, L, xq, sxs, cidx, st, ok, pol);
+      if (p.pm == PM_DIRECT || p.pm == PM_GELU)  // Q4 o / down: f16 fragments
+        gemv_tiles<FMT_Q4, false>(p, a, gw, L, xq, sxs, cidx, st, ok, pol);
+      else if (p.fmt == FMT_Q4)
+        gemv_tiles<FMT_Q4, true>(p, a, gw, L, xq, sxs, cidx, st, ok, pol);
       else
-        gemv_tiles<FMT_Q8>(p, a, gw, L, xq, sxs, cidx, st, ok, pol);
+        gemv_tiles<FMT_Q8, true>(p, a, gw, L, xq, sxs, cidx, st, ok, pol);
       __syncthreads();
       PHASE_MARK(pi, 3);
       cta_combine(p, a, L.wpart);
@@ -1332,7 +1366,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(const MegaAr
 
 size_t mk_smem_bytes(uint32_t max_k, uint32_t hidden, uint32_t ratio, uint32_t max_splits, uint32_t cache_slots,
                      uint32_t grid) {
-  const size_t fixed = (size_t)MK_NW * MK_SPW * MK_STAGE + (MK_NW * MK_SPW + 2) * 8 + MK_NW * 2 * 16 * 4 +
+  const size_t fixed = (size_t)MK_NW * MK_SPW * MK_STAGE + (MK_NW * MK_SPW + 2) * 8 + 16 + MK_NW * 2 * 16 * 4 +
                       2 * (kMaxGrid + 1) * 4 + 2 * kWinSlots * 4;
   const size_t part = (size_t)grid * 32 * 4;  // straddle partials of the previous GEMV
   // GEMV staging: 4 vectors of `hidden` for the norm prologues, one of max_k otherwise

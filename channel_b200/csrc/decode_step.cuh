@@ -34,10 +34,10 @@ struct Partition {
 // one partial sum per CTA (slot 0: the CTA's first row tile, slot 1: its last)
 // and the consumer phase adds them up while it loads its input.
 struct GemvOut {
-  float *direct;   // [rows]; act mode: the rows/2 values gelu(gate) * up
+  float *direct;   // [rows]; act mode: B fragments (f16 hi|lo) of the rows/2 values gelu(gate) * up
   float *partial;  // [grid][2][16] CTA partial sums of straddling row tiles
   Partition pt;    // the producing GEMV's split
-  uint32_t act;    // 1: interleaved gate|up GEMV whose output is gelu(gate) * up
+  uint32_t act;    // 1: interleaved gate|up GEMV whose consumer takes B fragments of gelu(gate) * up
   uint32_t row0;   // push 1: index of this rank's first row (act value) in the gathered vector;
                    // push 2: length of the exchanged vector
   uint32_t push;   // 1: rows go to every rank's copy of `direct` (peer stores), 0: local only,
@@ -71,7 +71,7 @@ struct alignas(16) Phase {
   const float *q_norm_w, *k_norm_w;
   const float2 *rope_cs;
   __half *k_cache, *v_cache;
-  float *attn_out;  // ATTN output (f32), the o-projection's input
+  float *attn_out;  // ATTN output, written as B fragments (f16 hi|lo) of the o-projection's input
 };
 
 // the weight stream of one GEMV phase (phases in order, GEMV phases only)
