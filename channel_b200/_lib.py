@@ -46,6 +46,11 @@ class ChStepDesc(C.Structure):
                 ("active", P(u32)), ("sliding", P(u32))]
 
 
+class ChStreamStep(C.Structure):
+    _fields_ = [("stream", u32), ("token", u32), ("clock", u32), ("slot", u32),
+                ("active", P(u32)), ("sliding", P(u32)), ("n_active", u32), ("n_sliding", u32)]
+
+
 PROGRESS_FN = C.CFUNCTYPE(None, sz, sz, vp)
 
 # name -> (restype, argtypes); every symbol declared in include/channel_cuda.h
@@ -72,6 +77,9 @@ SIGNATURES = {
     "ch_kv_read": (i32, [vp, u32, u32, P(f32), P(f32)]),
     "ch_kv_write": (i32, [vp, u32, u32, P(f32), P(f32)]),
     "ch_decode_plan": (i32, [vp, P(ChStepDesc), u32]),
+    "ch_streams_init": (i32, [vp, u32, u32]),
+    "ch_stream_prefill": (i32, [vp, u32, P(u32), u32, P(u32), u32, u32, P(u32)]),
+    "ch_streams_decode": (i32, [vp, P(ChStreamStep), u32, P(u32)]),
     "ch_decode_run": (i32, [vp, u32, u32]),
     "ch_decode_continue": (i32, [vp, u32]),
     "ch_decode_tokens": (i32, [vp, P(u32), u32]),

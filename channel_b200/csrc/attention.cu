@@ -60,11 +60,19 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attn_kernel(const AttnArg
   __shared__ uint32_t last_flag;
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const uint32_t kvh = blockIdx.x, split = blockIdx.y;
+  const uint32_t kvh = blockIdx.x, split = blockIdx.y, b = blockIdx.z;
   const size_t kv_dim = (size_t)a.nkv * D;
+  // this token's views (batched decode: one token per stream)
+  const float *qkv = a.qkv + (size_t)b * a.qkv_stride;
+  const float2 *rope_cs = a.rope_cs + (size_t)b * a.rope_stride;
+  const size_t coff = a.stream ? (size_t)a.stream[b] * a.cache_stride : 0;
+  __half *k_cache = a.k_cache + coff, *v_cache = a.v_cache + coff;
+  float *out = a.out + (size_t)b * a.out_stride;
+  float *partial = a.partial + (size_t)b * a.nkv * max_splits * R * (D + 2);
+  uint32_t *counters = a.counters + (size_t)b * a.nkv;
 
   // step state was written before the previous kernel started (see model.cu)
-  const StepParams sp = *a.sp;
+  const StepParams sp = a.sp[b];
   const uint32_t S = a.is_sliding ? sp.n_sliding : sp.n_active;
   const uint32_t *list = a.is_sliding ? sp.sliding : sp.active;
   // adaptive split: at least kMinChunk slots per CTA, at most max_splits CTAs per kv head
@@ -78,8 +86,8 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attn_kernel(const AttnArg
   for (uint32_t i = c0 + tid; i < c1; i += kAttnThreads) {
     const uint32_t phys = list[i];
     if (phys < a.cache_slots) {
-      const __half *kr = a.k_cache + (size_t)phys * kv_dim + (size_t)kvh * D;
-      const __half *vr = a.v_cache + (size_t)phys * kv_dim + (size_t)kvh * D;
+      const __half *kr = k_cache + (size_t)phys * kv_dim + (size_t)kvh * D;
+      const __half *vr = v_cache + (size_t)phys * kv_dim + (size_t)kvh * D;
       asm volatile("prefetch.global.L2 [%0];" ::"l"(kr));
       asm volatile("prefetch.global.L2 [%0];" ::"l"(kr + 128));
       asm volatile("prefetch.global.L2 [%0];" ::"l"(vr));
@@ -89,23 +97,23 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attn_kernel(const AttnArg
   grid_dep_wait();
 
   // ---- stage q heads | k | v of this kv head (one round trip), then norm + rope ----
-  const float *kraw = a.qkv + (size_t)a.nq * D;
+  const float *kraw = qkv + (size_t)a.nq * D;
   for (int idx = tid; idx < (R + 2) * (D / 4); idx += kAttnThreads) {
     const int h = idx / (D / 4), f = idx % (D / 4);
-    const float *src = h < R ? a.qkv + (size_t)(kvh * R + h) * D : (h == R ? kraw : kraw + kv_dim) + (size_t)kvh * D;
+    const float *src = h < R ? qkv + (size_t)(kvh * R + h) * D : (h == R ? kraw : kraw + kv_dim) + (size_t)kvh * D;
     reinterpret_cast<float4 *>(raw + h * D)[f] = reinterpret_cast<const float4 *>(src)[f];
   }
   __syncthreads();
   for (int h = warp; h < R + 2; h += kAttnWarps) {
     float *hd = raw + h * D;
     if (h <= R) {
-      head_norm_rope_s(hd, h < R ? a.q_norm_w : a.k_norm_w, hd, D, a.rot, a.rope_cs, a.eps, true, lane);
+      head_norm_rope_s(hd, h < R ? a.q_norm_w : a.k_norm_w, hd, D, a.rot, rope_cs, a.eps, true, lane);
     } else {
       head_norm_rope_s(hd, nullptr, hd, D, a.rot, nullptr, a.eps, false, lane);
     }
     __syncwarp();
     if (h >= R) {  // round the new K / V to the cache's f16 and write them (split 0 only)
-      __half *dst = (h == R ? a.k_cache : a.v_cache) + (size_t)sp.slot * kv_dim + (size_t)kvh * D;
+      __half *dst = (h == R ? k_cache : v_cache) + (size_t)sp.slot * kv_dim + (size_t)kvh * D;
       for (uint32_t d = lane; d < D; d += 32) {
         const __half hv = __float2half_rn(hd[d]);
         hd[d] = __half2float(hv);
@@ -132,7 +140,7 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attn_kernel(const AttnArg
 #pragma unroll
       for (int e = 0; e < EPL; e++) kv[e] = k_new[lane * EPL + e];
     } else if (phys < a.cache_slots) {
-      const uint4 rw = *reinterpret_cast<const uint4 *>(a.k_cache + (size_t)phys * kv_dim + (size_t)kvh * D + lane * EPL);
+      const uint4 rw = *reinterpret_cast<const uint4 *>(k_cache + (size_t)phys * kv_dim + (size_t)kvh * D + lane * EPL);
       const __half2 *hp = reinterpret_cast<const __half2 *>(&rw);
 #pragma unroll
       for (int e = 0; e < EPL / 2; e++) {
@@ -189,7 +197,7 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attn_kernel(const AttnArg
 #pragma unroll
       for (int e = 0; e < EPL; e++) vv[e] = v_new[lane * EPL + e];
     } else if (phys < a.cache_slots) {
-      const uint4 rw = *reinterpret_cast<const uint4 *>(a.v_cache + (size_t)phys * kv_dim + (size_t)kvh * D + lane * EPL);
+      const uint4 rw = *reinterpret_cast<const uint4 *>(v_cache + (size_t)phys * kv_dim + (size_t)kvh * D + lane * EPL);
       const __half2 *hp = reinterpret_cast<const __half2 *>(&rw);
 #pragma unroll
       for (int e = 0; e < EPL / 2; e++) {
@@ -215,7 +223,7 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attn_kernel(const AttnArg
   __syncthreads();
 
   // ---- partial out: [kvh][split][h] = {o[D], m, l} ----
-  float *part = a.partial + ((size_t)(kvh * max_splits + split) * R) * (D + 2);
+  float *part = partial + ((size_t)(kvh * max_splits + split) * R) * (D + 2);
   for (int idx = tid; idx < R * D; idx += kAttnThreads) {
     const int h = idx / D, d = idx % D;
     float s = 0.f;
@@ -230,7 +238,7 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attn_kernel(const AttnArg
   __threadfence();
   __syncthreads();
   if (tid == 0) {
-    const uint32_t old = atomicAdd(&a.counters[kvh], 1u);
+    const uint32_t old = atomicAdd(&counters[kvh], 1u);
     last_flag = (old == nsplit - 1) ? 1u : 0u;
   }
   __syncthreads();
@@ -238,7 +246,7 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attn_kernel(const AttnArg
   __threadfence();
 
   // ---- combine (fixed split order): factors first, then one pipelined pass ----
-  const float *base = a.partial + ((size_t)kvh * max_splits * R) * (D + 2);
+  const float *base = partial + ((size_t)kvh * max_splits * R) * (D + 2);
   for (int idx = tid; idx < R * (int)nsplit; idx += kAttnThreads) {
     const int h = idx / nsplit, j = idx % nsplit;
     cmb[h * max_splits + j] = __ldcg(&base[((size_t)j * R + h) * (D + 2) + D]);
@@ -270,9 +278,9 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attn_kernel(const AttnArg
       O = __fmaf_rn(p3, cmb[h * max_splits + j + 3], O);
     }
     for (; j < nsplit; j++) O = __fmaf_rn(__ldcg(&base[((size_t)j * R + h) * (D + 2) + d]), cmb[h * max_splits + j], O);
-    a.out[(size_t)(kvh * R + h) * D + d] = __fmul_rn(O, stat[2 * h]);
+    out[(size_t)(kvh * R + h) * D + d] = __fmul_rn(O, stat[2 * h]);
   }
-  if (tid == 0) a.counters[kvh] = 0u;
+  if (tid == 0) counters[kvh] = 0u;
 }
 
 template <int R>
@@ -287,7 +295,7 @@ static cudaError_t launch_attn_t(const AttnArgs &a, int splits, cudaStream_t s, 
     attr_bytes = smem;
   }
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(a.nkv, splits);
+  cfg.gridDim = dim3(a.nkv, splits, a.n_tok);
   cfg.blockDim = dim3(kAttnThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = s;

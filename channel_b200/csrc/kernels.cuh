@@ -101,6 +101,14 @@ struct AttnArgs {
   uint32_t *counters;   // [nkv]
   uint32_t *err;
   uint32_t cache_slots; // 4096
+  // Batched decode, one token per stream: token b = grid z uses sp[b], rope_cs + b *
+  // rope_stride, qkv + b * qkv_stride, out + b * out_stride, the caches of stream
+  // stream[b] (cache_stride elements apart) and its own partial / counter slices.
+  // One token with zero strides is the single-stream case.
+  uint32_t n_tok = 1;
+  const uint32_t *stream = nullptr;  // [n_tok] (nullptr: every token uses the caches as given)
+  size_t cache_stride = 0;
+  uint32_t qkv_stride = 0, out_stride = 0, rope_stride = 0;
 };
 int attn_default_splits(uint32_t nkv);
 size_t attn_partial_floats(uint32_t nkv, uint32_t ratio, uint32_t D, int splits);
@@ -121,6 +129,8 @@ struct TopkArgs {
 };
 int topk_blocks(uint32_t V);
 cudaError_t launch_topk64(const TopkArgs &a, cudaStream_t s, bool pdl);
+// greedy (top-1 of the softcapped keys) of each of n rows of V logits
+cudaError_t launch_argmax_rows(const float *logits, uint32_t n, uint32_t V, uint32_t *ids, cudaStream_t s);
 
 // embedding + step advance for the device-resident decode loop
 struct StepBeginArgs {

@@ -233,8 +233,21 @@ struct ch_model {
   float *pX = nullptr, *pNX = nullptr, *pQKV = nullptr, *pQO = nullptr, *pA = nullptr, *pMO = nullptr, *pACT = nullptr;
   uint32_t *pSlots = nullptr, *pTok = nullptr;
   uint8_t *pXS = nullptr;  // scratch of the tcgen05 GEMM (counters | split activation | partials)
+  // multi-stream decode: per-stream KV caches and the buffers of one batched step
+  uint32_t ms_n = 0, ms_cap = 0;   // decode streams and the largest step
+  std::vector<__half *> skc, svc;  // per layer: [ms_n][4096][kv_dim]
+  float *ms_logits = nullptr;      // [ms_cap][V]
+  uint32_t *ms_tok = nullptr, *ms_stream = nullptr, *ms_ids = nullptr, *ms_lists = nullptr;
+  StepParams *ms_sp = nullptr;     // [ms_cap]
+  float2 *ms_rope = nullptr;       // [2][ms_cap][rot/2]: sliding theta, then full theta
+  float *ms_partial = nullptr;     // attention split partials, [ms_cap] slices
+  uint32_t *ms_counters = nullptr; // [ms_cap][n_kv]
+  uint32_t *h_ms_u32 = nullptr;    // pinned: tokens | streams | lists | ids
+  StepParams *h_ms_sp = nullptr;
+  float2 *h_ms_rope = nullptr;
 };
 
+static void free_streams(ch_model *m);
 static void free_model(ch_model *m) {
   if (!m) return;
   cudaSetDevice(m->ctx->device);
@@ -253,6 +266,7 @@ static void free_model(ch_model *m) {
     cudaFree(l.kc);
     cudaFree(l.vc);
   }
+  free_streams(m);
   void *dev[] = {m->lm, m->final_norm, m->embed, m->inv_freq_s, m->inv_freq_f, m->rope_cs, m->X[0], m->X[1], m->normed, m->qkv,
                  m->attn, m->o_out, m->act, m->down_out, m->logits, m->vals, m->ids, m->token, m->token_hist, m->sp,
                  m->active, m->sliding, m->gemv_partial, m->gemv_counters, m->attn_partial, m->attn_counters,
@@ -1445,9 +1459,10 @@ static int prefill_tp(ch_model *m, const uint32_t *tokens, uint32_t n, const uin
   return status_from_flags(f);
 }
 
-extern "C" int ch_prefill(ch_model *m, const uint32_t *tokens, uint32_t n, const uint16_t *embed_bf16,
-                          const uint32_t *slots, uint32_t start_clock, uint32_t num_prev, ch_topk *topk_out,
-                          ch_progress_fn progress_fn, void *progress_ctx) {
+// stream < 0: the model's own KV cache; else that stream's (ch_streams_init)
+static int prefill_impl(ch_model *m, const uint32_t *tokens, uint32_t n, const uint16_t *embed_bf16,
+                        const uint32_t *slots, uint32_t start_clock, uint32_t num_prev, ch_topk *topk_out,
+                        ch_progress_fn progress_fn, void *progress_ctx, int stream) {
   if (!m || !tokens || !slots) return fail(CH_EINVAL, "NULL argument");
   const uint32_t cap = m->cfg.max_prefill_tokens ? m->cfg.max_prefill_tokens : 1024;
   if (n == 0 || n > cap) return fail(CH_EBATCH, "BatchTooLarge: n_tokens must be 1..max_prefill_tokens");
@@ -1459,6 +1474,9 @@ extern "C" int ch_prefill(ch_model *m, const uint32_t *tokens, uint32_t n, const
   CH_CUDA(cudaSetDevice(m->ctx->device));
   if (m->world > 1) return prefill_tp(m, tokens, n, slots, start_clock, num_prev, topk_out, progress_fn, progress_ctx);
   CH_TRY(ensure_prefill(m));
+  const size_t soff = stream < 0 ? 0 : (size_t)stream * kSlots * m->kvd;  // the stream's cache within the layer's
+  auto kc_of = [&](uint32_t l) { return stream < 0 ? m->layers[l].kc : m->skc[l] + soff; };
+  auto vc_of = [&](uint32_t l) { return stream < 0 ? m->layers[l].vc : m->svc[l] + soff; };
   cudaStream_t s = m->ctx->stream;
   const float scale = sqrtf((float)m->H);
   if (embed_bf16) {
@@ -1497,8 +1515,8 @@ extern "C" int ch_prefill(ch_model *m, const uint32_t *tokens, uint32_t n, const
     r.k_norm_w = dl.k_norm;
     r.inv_freq = dl.full ? m->inv_freq_f : m->inv_freq_s;
     r.q_out = m->pQO;
-    r.k_cache = dl.kc;
-    r.v_cache = dl.vc;
+    r.k_cache = kc_of(l);
+    r.v_cache = vc_of(l);
     r.slots = m->pSlots;
     r.slot_offset = num_prev;
     r.start_clock = start_clock;
@@ -1510,7 +1528,7 @@ extern "C" int ch_prefill(ch_model *m, const uint32_t *tokens, uint32_t n, const
     r.eps = eps;
     r.k_eq_v = 0;
     CH_CUDA(launch_batch_qkv_rope(r, s));
-    BatchAttnArgs at{m->pQO, dl.kc, dl.vc, m->pSlots, n, num_prev, m->nq, m->nkv, m->D, 1.0f, dl.full ? 0 : 1, m->pA};
+    BatchAttnArgs at{m->pQO, kc_of(l), vc_of(l), m->pSlots, n, num_prev, m->nq, m->nkv, m->D, 1.0f, dl.full ? 0 : 1, m->pA};
     CH_CUDA(launch_batch_causal_attn(at, s));
     CH_CUDA(launch_batch_gemm_q4_tc(BatchGemmArgs{dl.o, m->H, m->qd, n, m->pA, m->pMO, EPI_STORE}, m->pXS, err, s));
     if (dl.post_attn) CH_CUDA(launch_rmsnorm_rows(m->pMO, dl.post_attn, m->pMO, n, m->H, eps, s));
@@ -1559,6 +1577,208 @@ extern "C" int ch_prefill(ch_model *m, const uint32_t *tokens, uint32_t n, const
   CH_CUDA(cudaStreamSynchronize(s));
   if (topk_out)
     for (int i = 0; i < 64; i++) topk_out[i] = ch_topk{m->h_ids[i], m->h_vals[i]};
+  uint32_t f = 0;
+  CH_TRY(ch_ctx_device_status(m->ctx, &f));
+  return status_from_flags(f);
+}
+
+extern "C" int ch_prefill(ch_model *m, const uint32_t *tokens, uint32_t n, const uint16_t *embed_bf16,
+                          const uint32_t *slots, uint32_t start_clock, uint32_t num_prev, ch_topk *topk_out,
+                          ch_progress_fn progress_fn, void *progress_ctx) {
+  return prefill_impl(m, tokens, n, embed_bf16, slots, start_clock, num_prev, topk_out, progress_fn, progress_ctx, -1);
+}
+
+// ---------------------------------------------------------------------------
+// Multi-stream greedy decode.  Every stream has its own
+// 4,096-slot KV cache per layer.  One step takes one token from each of up to
+// ms_cap streams and runs the layers as a batch: the row norms and tcgen05 Q4 GEMMs
+// of the prefill path on B tokens, then decode attention with one token per stream
+// -- each against its own stream's cache and slot lists, at its own clock (RoPE) --
+// and the Q8 LM head and greedy argmax per token.  The weights are read once per
+// step for all B streams.  The reference serves one stream (server_queue.zig:9-145,
+// server.zig:259-281); this batching is new.
+static void free_streams(ch_model *m) {
+  for (auto *p : m->skc) cudaFree(p);
+  for (auto *p : m->svc) cudaFree(p);
+  m->skc.clear();
+  m->svc.clear();
+  void *dev[] = {m->ms_logits, m->ms_tok, m->ms_stream, m->ms_ids, m->ms_lists, m->ms_sp, m->ms_rope,
+                 m->ms_partial, m->ms_counters};
+  for (void *p : dev) cudaFree(p);
+  void *host[] = {m->h_ms_u32, m->h_ms_sp, m->h_ms_rope};
+  for (void *p : host) cudaFreeHost(p);
+  m->ms_logits = nullptr, m->ms_tok = m->ms_stream = m->ms_ids = m->ms_lists = nullptr, m->ms_sp = nullptr;
+  m->ms_rope = nullptr, m->ms_partial = nullptr, m->ms_counters = nullptr;
+  m->h_ms_u32 = nullptr, m->h_ms_sp = nullptr, m->h_ms_rope = nullptr;
+  m->ms_n = m->ms_cap = 0;
+}
+
+static int init_streams(ch_model *m, uint32_t n_streams, uint32_t max_batch) {
+  CH_TRY(ensure_prefill(m));
+  const size_t per = (size_t)n_streams * kSlots * m->kvd;
+  m->skc.assign(m->L, nullptr);
+  m->svc.assign(m->L, nullptr);
+  for (uint32_t l = 0; l < m->L; l++) {
+    CH_TRY(dmalloc(&m->skc[l], per));
+    CH_TRY(dmalloc(&m->svc[l], per));
+    CH_CUDA(cudaMemset(m->skc[l], 0, per * sizeof(__half)));
+    CH_CUDA(cudaMemset(m->svc[l], 0, per * sizeof(__half)));
+  }
+  const uint32_t rh = m->cfg.rotary_dim / 2, R = m->nq / m->nkv;
+  CH_TRY(dmalloc(&m->ms_logits, (size_t)max_batch * m->V));
+  CH_TRY(dmalloc(&m->ms_tok, max_batch));
+  CH_TRY(dmalloc(&m->ms_stream, max_batch));
+  CH_TRY(dmalloc(&m->ms_ids, max_batch));
+  CH_TRY(dmalloc(&m->ms_lists, (size_t)max_batch * 2 * kSlots));
+  CH_TRY(dmalloc(&m->ms_sp, max_batch));
+  CH_TRY(dmalloc(&m->ms_rope, (size_t)2 * max_batch * rh));
+  CH_TRY(dmalloc(&m->ms_partial, (size_t)max_batch * attn_partial_floats(m->nkv, R, m->D, m->attn_splits)));
+  CH_TRY(dmalloc(&m->ms_counters, (size_t)max_batch * m->nkv));
+  CH_CUDA(cudaMemset(m->ms_counters, 0, (size_t)max_batch * m->nkv * 4));
+  CH_CUDA(cudaMallocHost(&m->h_ms_u32, ((size_t)3 * max_batch + (size_t)max_batch * 2 * kSlots) * 4));
+  CH_CUDA(cudaMallocHost(&m->h_ms_sp, max_batch * sizeof(StepParams)));
+  CH_CUDA(cudaMallocHost(&m->h_ms_rope, (size_t)2 * max_batch * rh * sizeof(float2)));
+  m->ms_n = n_streams;
+  m->ms_cap = max_batch;
+  return CH_OK;
+}
+
+extern "C" int ch_streams_init(ch_model *m, uint32_t n_streams, uint32_t max_batch) {
+  if (!m) return fail(CH_EINVAL, "NULL model");
+  if (m->world > 1)
+    return fail(CH_ESTATE, "multi-stream decode runs on one GPU (across GPUs: one replica per GPU)");
+  if (!m->embed) return fail(CH_ESTATE, "multi-stream decode embeds on the device: the model needs its embedding");
+  if (m->ms_n) return fail(CH_ESTATE, "streams already initialised");
+  const uint32_t cap = m->cfg.max_prefill_tokens ? m->cfg.max_prefill_tokens : 1024;
+  if (n_streams == 0 || max_batch == 0 || max_batch > n_streams || max_batch > cap)
+    return fail(CH_EINVAL, "streams: 1 <= max_batch <= n_streams, max_batch <= max_prefill_tokens");
+  CH_CUDA(cudaSetDevice(m->ctx->device));
+  const int rc = init_streams(m, n_streams, max_batch);
+  if (rc != CH_OK) {
+    const std::string msg = g_err;
+    free_streams(m);
+    return fail(rc, msg);
+  }
+  return CH_OK;
+}
+
+extern "C" int ch_stream_prefill(ch_model *m, uint32_t stream, const uint32_t *tokens, uint32_t n,
+                                 const uint32_t *slots, uint32_t start_clock, uint32_t num_prev, uint32_t *token_out) {
+  if (!m) return fail(CH_EINVAL, "NULL model");
+  if (stream >= m->ms_n) return fail(CH_EINVAL, "stream index >= the streams initialised");
+  ch_topk top[64];
+  CH_TRY(prefill_impl(m, tokens, n, nullptr, slots, start_clock, num_prev, token_out ? top : nullptr, nullptr, nullptr,
+                      (int)stream));
+  if (token_out) *token_out = top[0].id;
+  return CH_OK;
+}
+
+extern "C" int ch_streams_decode(ch_model *m, const ch_stream_step *steps, uint32_t n, uint32_t *tokens_out) {
+  if (!m || !steps || !tokens_out) return fail(CH_EINVAL, "NULL argument");
+  if (!m->ms_n) return fail(CH_ESTATE, "ch_streams_init first");
+  if (n == 0 || n > m->ms_cap) return fail(CH_EBATCH, "BatchTooLarge: 1..max_batch tokens per step");
+  std::vector<uint8_t> seen(m->ms_n, 0);
+  for (uint32_t b = 0; b < n; b++) {
+    const ch_stream_step &st = steps[b];
+    if (st.stream >= m->ms_n) return fail(CH_EINVAL, "stream index >= the streams initialised");
+    if (seen[st.stream]++) return fail(CH_EINVAL, "a stream appears twice in one step");
+    if (st.token >= m->V) return fail(CH_EINVAL, "token id >= vocab");
+    if (st.slot >= kSlots) return fail(CH_EINVAL, "slot >= 4096");
+    CH_TRY(check_lists(st.active, st.n_active));
+    CH_TRY(check_lists(st.sliding, st.n_sliding));
+  }
+  CH_CUDA(cudaSetDevice(m->ctx->device));
+  cudaStream_t s = m->ctx->stream;
+  const uint32_t cap = m->ms_cap, rh = m->cfg.rotary_dim / 2, qkvd = m->qd + 2 * m->kvd;
+  uint32_t *h_tok = m->h_ms_u32, *h_str = h_tok + cap, *h_ids = h_str + cap, *h_lists = h_ids + cap;
+  for (uint32_t b = 0; b < n; b++) {
+    const ch_stream_step &st = steps[b];
+    h_tok[b] = st.token;
+    h_str[b] = st.stream;
+    uint32_t *la = h_lists + (size_t)b * 2 * kSlots;
+    if (st.n_active) memcpy(la, st.active, st.n_active * 4);
+    if (st.n_sliding) memcpy(la + kSlots, st.sliding, st.n_sliding * 4);
+    StepParams &sp = m->h_ms_sp[b];
+    sp = StepParams{};
+    sp.clock = st.clock;
+    sp.slot = st.slot;
+    sp.n_active = st.n_active;
+    sp.n_sliding = st.n_sliding;
+    sp.active = m->ms_lists + (size_t)b * 2 * kSlots;
+    sp.sliding = m->ms_lists + (size_t)b * 2 * kSlots + kSlots;
+    rope_table(m->h_inv_s, st.clock, m->h_ms_rope + (size_t)b * rh);
+    rope_table(m->h_inv_f, st.clock, m->h_ms_rope + ((size_t)cap + b) * rh);
+  }
+  CH_CUDA(cudaMemcpyAsync(m->ms_tok, h_tok, n * 4, cudaMemcpyHostToDevice, s));
+  CH_CUDA(cudaMemcpyAsync(m->ms_stream, h_str, n * 4, cudaMemcpyHostToDevice, s));
+  CH_CUDA(cudaMemcpyAsync(m->ms_lists, h_lists, (size_t)n * 2 * kSlots * 4, cudaMemcpyHostToDevice, s));
+  CH_CUDA(cudaMemcpyAsync(m->ms_sp, m->h_ms_sp, n * sizeof(StepParams), cudaMemcpyHostToDevice, s));
+  CH_CUDA(cudaMemcpyAsync(m->ms_rope, m->h_ms_rope, (size_t)n * rh * sizeof(float2), cudaMemcpyHostToDevice, s));
+  CH_CUDA(cudaMemcpyAsync(m->ms_rope + (size_t)cap * rh, m->h_ms_rope + (size_t)cap * rh, (size_t)n * rh * sizeof(float2),
+                          cudaMemcpyHostToDevice, s));
+  CH_CUDA(launch_embed_rows(m->embed, m->ms_tok, n, m->H, sqrtf((float)m->H), m->pX, s));
+  const float eps = m->cfg.rms_norm_eps;
+  uint32_t *err = m->ctx->err;
+  for (uint32_t l = 0; l < m->L; l++) {
+    DevLayer &dl = m->layers[l];
+    if (l == 0) CH_CUDA(launch_rmsnorm_rows(m->pX, dl.input_norm, m->pNX, n, m->H, eps, s));
+    CH_CUDA(launch_batch_gemm_q4_tc(BatchGemmArgs{dl.qkv, qkvd, m->H, n, m->pNX, m->pQKV, EPI_STORE}, m->pXS, err, s));
+    AttnArgs a{};
+    a.qkv = m->pQKV;
+    a.qkv_stride = qkvd;
+    a.q_norm_w = dl.q_norm;
+    a.k_norm_w = dl.k_norm;
+    a.rope_cs = m->ms_rope + (dl.full ? (size_t)cap * rh : 0);
+    a.rope_stride = rh;
+    a.k_cache = m->skc[l];
+    a.v_cache = m->svc[l];
+    a.stream = m->ms_stream;
+    a.cache_stride = (size_t)kSlots * m->kvd;
+    a.sp = m->ms_sp;
+    a.is_sliding = dl.full ? 0 : 1;
+    a.nq = m->nq;
+    a.nkv = m->nkv;
+    a.D = m->D;
+    a.rot = m->cfg.rotary_dim;
+    a.eps = eps;
+    a.scale = 1.0f;  // Gemma-style: q/k norms replace 1/sqrt(d) (forward.zig:85)
+    a.out = m->pA;
+    a.out_stride = m->qd;
+    a.partial = m->ms_partial;
+    a.counters = m->ms_counters;
+    a.err = err;
+    a.cache_slots = kSlots;
+    a.n_tok = n;
+    CH_CUDA(launch_decode_attn(a, m->attn_splits, s, false));
+    CH_CUDA(launch_batch_gemm_q4_tc(BatchGemmArgs{dl.o, m->H, m->qd, n, m->pA, m->pMO, EPI_STORE}, m->pXS, err, s));
+    if (dl.post_attn) CH_CUDA(launch_rmsnorm_rows(m->pMO, dl.post_attn, m->pMO, n, m->H, eps, s));
+    CH_CUDA(launch_add_rmsnorm_rows(m->pX, m->pMO, dl.pre_ffn, m->pNX, n, m->H, eps, 1.0f, s));
+    CH_CUDA(launch_batch_gemm_q4_tc(BatchGemmArgs{dl.gateup, 2 * m->I, m->H, n, m->pNX, m->pACT, EPI_GELU_MUL}, m->pXS,
+                                    err, s));
+    CH_CUDA(launch_batch_gemm_q4_tc(BatchGemmArgs{dl.down, m->H, m->I, n, m->pACT, m->pMO, EPI_STORE}, m->pXS, err, s));
+    if (dl.post_ffn) CH_CUDA(launch_rmsnorm_rows(m->pMO, dl.post_ffn, m->pMO, n, m->H, eps, s));
+    const float *next = (l + 1 < m->L) ? m->layers[l + 1].input_norm : m->final_norm;
+    CH_CUDA(launch_add_rmsnorm_rows(m->pX, m->pMO, next, m->pNX, n, m->H, eps, dl.scalar, s));
+  }
+  for (uint32_t b = 0; b < n; b++) {  // Q8 LM head of each token's final-normed state
+    GemvArgs a;
+    GemvPlan p;
+    p.fmt = FMT_Q8;
+    a.tiles = m->lm;
+    a.row_tiles = m->V / 16;
+    a.k_tiles = m->H / 32;
+    a.K = m->H;
+    a.x = m->pNX + (size_t)b * m->H;
+    a.y = m->ms_logits + (size_t)b * m->V;
+    a.partial = m->gemv_partial;
+    a.counters = m->gemv_counters;
+    a.err = err;
+    CH_CUDA(launch_gemv(p, a, s, b > 0));
+  }
+  CH_CUDA(launch_argmax_rows(m->ms_logits, n, m->V, m->ms_ids, s));
+  CH_CUDA(cudaMemcpyAsync(h_ids, m->ms_ids, n * 4, cudaMemcpyDeviceToHost, s));
+  CH_CUDA(cudaStreamSynchronize(s));
+  memcpy(tokens_out, h_ids, n * 4);
   uint32_t f = 0;
   CH_TRY(ch_ctx_device_status(m->ctx, &f));
   return status_from_flags(f);

@@ -140,6 +140,35 @@ __global__ void step_begin_kernel(const StepBeginArgs a) {
     a.x[i] = __fmul_rn(bf16_to_f32(row[i]), a.embed_scale);
   grid_dep_launch();
 }
+// Greedy token of each of n logit rows: the largest key (sortable softcap bits << 32 |
+// ~index) -- the top-1 of topk64_kernel, value first, then the lowest index.  One CTA
+// per row.
+__global__ void __launch_bounds__(kTkThreads) argmax_rows_kernel(const float *logits, uint32_t V, uint32_t *ids) {
+  __shared__ uint64_t wbest[kTkThreads / 32];
+  const float *row = logits + (size_t)blockIdx.x * V;
+  uint64_t best = 0;
+  for (uint32_t idx = threadIdx.x; idx < V; idx += kTkThreads) {
+    const uint64_t k = ((uint64_t)sortable(softcap(row[idx])) << 32) | (uint64_t)(0xFFFFFFFFu - idx);
+    best = k > best ? k : best;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const uint64_t other = __shfl_xor_sync(0xffffffffu, best, o);
+    best = other > best ? other : best;
+  }
+  if ((threadIdx.x & 31) == 0) wbest[threadIdx.x >> 5] = best;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < kTkThreads / 32; w++) best = wbest[w] > best ? wbest[w] : best;
+    ids[blockIdx.x] = 0xFFFFFFFFu - (uint32_t)(best & 0xFFFFFFFFu);
+  }
+}
+cudaError_t launch_argmax_rows(const float *logits, uint32_t n, uint32_t V, uint32_t *ids, cudaStream_t s) {
+  if (n == 0) return cudaSuccess;
+  argmax_rows_kernel<<<n, kTkThreads, 0, s>>>(logits, V, ids);
+  return cudaGetLastError();
+}
+
 cudaError_t launch_step_begin(const StepBeginArgs &a, cudaStream_t s, bool pdl) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(1);

@@ -257,6 +257,36 @@ class GpuModelContext:
             arr[i].active, arr[i].sliding = _ptr(a, C.c_uint32), _ptr(s, C.c_uint32)
         L.check(lib.ch_decode_plan(self.handle, arr, len(steps)))
 
+    # ---- multi-stream greedy decode ----
+    def streams_init(self, n_streams: int, max_batch: int) -> None:
+        """Per-stream 4,096-slot KV caches for n_streams; steps of up to max_batch streams."""
+        L.check(L.load().ch_streams_init(self.handle, n_streams, max_batch))
+
+    def stream_prefill(self, stream: int, tokens, slots, start_clock: int, num_prev: int) -> int:
+        """Batched prefill of one stream's prompt into its own cache; returns the greedy next token."""
+        t = np.ascontiguousarray(tokens, np.uint32)
+        sl = np.ascontiguousarray(slots, np.uint32)
+        out = C.c_uint32()
+        L.check(L.load().ch_stream_prefill(self.handle, stream, _ptr(t, C.c_uint32), len(t), _ptr(sl, C.c_uint32),
+                                           start_clock, num_prev, C.byref(out)))
+        return int(out.value)
+
+    def streams_decode(self, steps: Sequence[tuple]) -> np.ndarray:
+        """One batched step; steps: (stream, token, clock, slot, active_list, sliding_list).
+        Returns each stream's greedy next token (step order)."""
+        arr = (L.ChStreamStep * len(steps))()
+        keep = []
+        for i, (stream, token, clock, slot, act, sli) in enumerate(steps):
+            a = np.ascontiguousarray(act, np.uint32)
+            s = np.ascontiguousarray(sli, np.uint32)
+            keep += [a, s]
+            arr[i].stream, arr[i].token, arr[i].clock, arr[i].slot = stream, token, clock, slot
+            arr[i].active, arr[i].sliding = _ptr(a, C.c_uint32), _ptr(s, C.c_uint32)
+            arr[i].n_active, arr[i].n_sliding = len(a), len(s)
+        out = np.zeros(len(steps), np.uint32)
+        L.check(L.load().ch_streams_decode(self.handle, arr, len(steps), _ptr(out, C.c_uint32)))
+        return out
+
     def decode_run(self, first_token: int, n_steps: int) -> None:
         L.check(L.load().ch_decode_run(self.handle, first_token, n_steps))
 

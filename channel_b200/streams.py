@@ -1,0 +1,78 @@
+"""Ragged multi-stream greedy decode over one model.
+
+Each stream has its own ring (host bookkeeping, ``DynamicRingBuffer``) and its own
+4,096-slot KV cache per layer on the device.  Prompts of any length are prefilled
+stream by stream (batched tcgen05 GEMMs + causal attention into that stream's
+cache); then every step packs one token from each unfinished stream -- up to
+``max_batch`` per launch -- into ``ch_streams_decode``: the weights are read once
+per step for the whole batch, and each token attends to its own stream's cache at
+its own position.  The per-stream host work per step is the same as the
+single-stream engine's (``src/model/forward.zig:42-45``: activate the clock's slot,
+read the active and sliding lists); the reference itself serves one stream
+(``src/server_queue.zig:9-145``), so the packing is new.
+"""
+from __future__ import annotations
+
+from typing import List, Sequence
+
+import numpy as np
+
+from .engine import DynamicRingBuffer
+
+
+class MultiStreamDecoder:
+    def __init__(self, gm, config, n_streams: int, max_batch: int):
+        self.gm, self.cfg = gm, config
+        self.n, self.max_batch = n_streams, max_batch
+        gm.streams_init(n_streams, max_batch)
+        self.rings = [DynamicRingBuffer(config.num_hidden_layers, 0) for _ in range(n_streams)]
+        self.clock = [0] * n_streams
+        self.next_token = [0] * n_streams
+        self.tokens: List[List[int]] = [[] for _ in range(n_streams)]
+        self.steps = 0  # batched decode launches so far
+
+    def prefill(self, stream: int, prompt: Sequence[int]) -> int:
+        """Prefill the stream's prompt from clock 0; returns (and records) its first greedy token."""
+        ring, n = self.rings[stream], len(prompt)
+        prev = list(ring.getPrefillPrevSlots(0, 0, n))
+        slots = prev + [ring.getSlotIndex(c) for c in range(n)]
+        for c in range(n):
+            for layer in range(self.cfg.num_hidden_layers):
+                ring.activateSlot(layer, c)
+        tok = self.gm.stream_prefill(stream, np.asarray(prompt, np.uint32), np.asarray(slots, np.uint32), 0, len(prev))
+        self.clock[stream], self.next_token[stream], self.tokens[stream] = n, tok, [tok]
+        return tok
+
+    def _step_lists(self, stream: int):
+        ring, clock, w = self.rings[stream], self.clock[stream], self.cfg.sliding_window
+        ring.activateSlot(0, clock)
+        return (ring.getSlotIndex(clock), ring.getActiveSlotsLayer(0, clock, False, w),
+                ring.getActiveSlotsLayer(0, clock, True, w))
+
+    def step(self, streams: Sequence[int]) -> np.ndarray:
+        """One batched greedy step over distinct streams (<= max_batch); returns their next tokens."""
+        batch = []
+        for s in streams:
+            slot, act, sli = self._step_lists(s)
+            batch.append((s, self.next_token[s], self.clock[s], slot, act, sli))
+        out = self.gm.streams_decode(batch)
+        for s, t in zip(streams, out):
+            self.next_token[s] = int(t)
+            self.tokens[s].append(int(t))
+            self.clock[s] += 1
+        self.steps += 1
+        return out
+
+    def run(self, prompts: Sequence[Sequence[int]], n_tokens: int) -> List[List[int]]:
+        """Prefill every stream, then decode until each has n_tokens greedy tokens
+        (the prefill's token counts as the first).  Streams are packed up to
+        max_batch per step, in stream order."""
+        for s, p in enumerate(prompts):
+            self.prefill(s, p)
+        while True:
+            live = [s for s in range(len(prompts)) if len(self.tokens[s]) < n_tokens]
+            if not live:
+                break
+            for i in range(0, len(live), self.max_batch):
+                self.step(live[i:i + self.max_batch])
+        return [t[:n_tokens] for t in self.tokens[:len(prompts)]]

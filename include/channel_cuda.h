@@ -166,6 +166,26 @@ int ch_decode_continue(ch_model *m, uint32_t n_steps);                      /* a
 int ch_decode_tokens(ch_model *m, uint32_t *tokens, uint32_t n);            /* syncs, copies step tokens */
 
 /* ------------------------------------------------------------------------
+ * Multi-stream greedy decode (no reference counterpart: the
+ * reference serves one stream, src/server_queue.zig:9-145, src/server.zig:259-281).
+ * Each stream owns a 4,096-slot KV cache per layer; its ring bookkeeping stays on
+ * the host (ch_ring_*), one ring per stream.  A step takes one token from each of
+ * up to max_batch distinct streams and returns each stream's greedy next token; the
+ * weights are read once per step for the whole batch.  One GPU (no tensor parallel);
+ * needs the device embedding.
+ * ---------------------------------------------------------------------- */
+typedef struct {
+  uint32_t stream, token, clock, slot; /* token: the stream's current input token */
+  const uint32_t *active, *sliding;    /* host lists, like ch_forward_token */
+  uint32_t n_active, n_sliding;
+} ch_stream_step;
+int ch_streams_init(ch_model *m, uint32_t n_streams, uint32_t max_batch);
+/* ch_prefill into the stream's cache; *token_out = greedy token after the prompt */
+int ch_stream_prefill(ch_model *m, uint32_t stream, const uint32_t *tokens, uint32_t n_tokens, const uint32_t *slots,
+                      uint32_t start_clock, uint32_t num_prev_slots, uint32_t *token_out);
+int ch_streams_decode(ch_model *m, const ch_stream_step *steps, uint32_t n, uint32_t *tokens_out);
+
+/* ------------------------------------------------------------------------
  * Op-level entry points (device pointers, async on the context stream).
  * Weight tiles: 16 rows x 64 k (Q4) / 16 x 32 (Q8), 576 bytes each.
  * ---------------------------------------------------------------------- */

@@ -1,0 +1,78 @@
+"""Multi-stream greedy decode (BASELINE config 5's path) against the oracle.
+
+Four streams with ragged prompts share one model; each has its own ring and KV
+cache.  Steps pack up to three streams per launch (so a round of four streams
+takes two launches) and every stream must reproduce, token for token, the greedy
+stream the oracle produces for it alone (prefill, then forward_token per step)."""
+import numpy as np
+import pytest
+
+from channel_b200 import _lib as L
+from tests.model_util import ring_step_lists, small_config
+
+pytestmark = pytest.mark.gpu
+
+SEED = 7
+PROMPT_LENS = [5, 11, 3, 17]
+N_TOKENS = 6
+
+
+def _oracle_stream(oracle, cfg, w, prompt, n_tokens):
+    from channel_b200 import DynamicRingBuffer
+    om = oracle.Model(cfg, w)
+    ring = DynamicRingBuffer(cfg.num_hidden_layers, 0)
+    n = len(prompt)
+    prev = ring.getPrefillPrevSlots(0, 0, n)
+    slots = np.concatenate([prev, [ring.getSlotIndex(c) for c in range(n)]]).astype(np.uint32)
+    for c in range(n):
+        for layer in range(cfg.num_hidden_layers):
+            ring.activateSlot(layer, c)
+    t, _, _ = om.prefill(oracle.embed(w.embed, prompt, cfg.hidden_size), slots, 0, len(prev))
+    out = [int(t)]
+    for i in range(n_tokens - 1):
+        clock = n + i
+        slot, act, sli = ring_step_lists(ring, cfg, clock)
+        t, _, _ = om.forward_token(oracle.embed(w.embed, [int(t)], cfg.hidden_size)[0], clock, slot, act, sli)
+        out.append(int(t))
+    return out
+
+
+def test_streams_match_oracle(ctx, oracle):
+    from channel_b200 import GpuModelContext
+    from channel_b200.streams import MultiStreamDecoder
+    cfg = small_config()
+    rng = np.random.default_rng(11)
+    prompts = [rng.integers(0, cfg.vocab_size, n).astype(np.uint32) for n in PROMPT_LENS]
+    w = oracle.SyntheticWeights(cfg, SEED)
+    refs = [_oracle_stream(oracle, cfg, w, p, N_TOKENS) for p in prompts]
+    gm = GpuModelContext.synthetic(ctx, cfg, SEED)
+    dec = MultiStreamDecoder(gm, cfg, n_streams=len(prompts), max_batch=3)
+    got = dec.run(prompts, N_TOKENS)
+    for s, (g, r) in enumerate(zip(got, refs)):
+        assert g == r, f"stream {s}: {g} != oracle {r}"
+    assert dec.steps == 2 * (N_TOKENS - 1)  # four streams at three per launch
+    assert ctx.device_status() == 0
+    gm.deinit()
+
+
+def test_streams_reject_bad_steps(ctx):
+    from channel_b200 import GpuModelContext
+    cfg = small_config()
+    gm = GpuModelContext.synthetic(ctx, cfg, SEED)
+    gm.streams_init(2, 2)
+    lib = L.load()
+    with pytest.raises(L.ChannelError):
+        gm.streams_init(2, 2)  # twice
+    dup = [(0, 1, 0, 0, [0], [0]), (0, 2, 0, 0, [0], [0])]
+    with pytest.raises(L.ChannelError) as e:
+        gm.streams_decode(dup)
+    assert e.value.status == L.CH_EINVAL
+    three = [(i % 2, 1, 0, 0, [0], [0]) for i in range(3)]
+    with pytest.raises(L.ChannelError) as e:
+        gm.streams_decode(three)
+    assert e.value.status == L.CH_EBATCH
+    with pytest.raises(L.ChannelError) as e:
+        gm.streams_decode([(2, 1, 0, 0, [0], [0])])
+    assert e.value.status == L.CH_EINVAL
+    assert b"stream" in lib.ch_last_error()
+    gm.deinit()
