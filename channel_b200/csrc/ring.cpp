@@ -62,6 +62,12 @@ extern "C" size_t ch_ring_activate_slot(ch_ring *r, size_t layer, size_t clock) 
   if (layer == 0 && clock >= r->ingested) r->ingested = clock + 1;
   return slot;
 }
+extern "C" void ch_ring_activate_range(ch_ring *r, size_t clock0, size_t n, uint32_t *slots_out) {
+  for (size_t c = clock0; c < clock0 + n; c++) {
+    for (size_t l = 0; l < r->layers; l++) ch_ring_activate_slot(r, l, c);
+    if (slots_out) slots_out[c - clock0] = (uint32_t)ch_ring_get_slot_index(r, 0, c);
+  }
+}
 extern "C" void ch_ring_deactivate_slot(ch_ring *r, size_t layer, size_t clock) {
   const size_t i = layer * kTotal + ch_ring_get_slot_index(r, layer, clock);
   if (r->clocks[i] == clock) {

@@ -378,6 +378,12 @@ class DynamicRingBuffer:
     def activateSlot(self, layer: int, clock: int) -> int:
         return self._lib.ch_ring_activate_slot(self.h, layer, clock)
 
+    def activateRange(self, clock0: int, n: int) -> np.ndarray:
+        """activateSlot of clocks [clock0, clock0 + n) in every layer; returns their slots."""
+        out = np.empty(n, np.uint32)
+        self._lib.ch_ring_activate_range(self.h, clock0, n, _ptr(out, C.c_uint32))
+        return out
+
     def deactivateSlot(self, layer: int, clock: int):
         self._lib.ch_ring_deactivate_slot(self.h, layer, clock)
 

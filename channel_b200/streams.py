@@ -32,14 +32,18 @@ class MultiStreamDecoder:
         self.steps = 0  # batched decode launches so far
 
     def prefill(self, stream: int, prompt: Sequence[int]) -> int:
-        """Prefill the stream's prompt from clock 0; returns (and records) its first greedy token."""
+        """Prefill the stream's prompt from clock 0, in chunks of at most the model's
+        max_prefill_tokens (each chunk attends to the earlier ones through the ring's
+        previous slots); returns (and records) its first greedy token."""
         ring, n = self.rings[stream], len(prompt)
-        prev = list(ring.getPrefillPrevSlots(0, 0, n))
-        slots = prev + [ring.getSlotIndex(c) for c in range(n)]
-        for c in range(n):
-            for layer in range(self.cfg.num_hidden_layers):
-                ring.activateSlot(layer, c)
-        tok = self.gm.stream_prefill(stream, np.asarray(prompt, np.uint32), np.asarray(slots, np.uint32), 0, len(prev))
+        cap = self.cfg.max_prefill_tokens
+        prompt = np.asarray(prompt, np.uint32)
+        tok = 0
+        for c0 in range(0, n, cap):
+            m = min(cap, n - c0)
+            prev = ring.getPrefillPrevSlots(0, c0, m)
+            slots = np.concatenate([prev, ring.activateRange(c0, m)]).astype(np.uint32)
+            tok = self.gm.stream_prefill(stream, prompt[c0:c0 + m], slots, c0, len(prev))
         self.clock[stream], self.next_token[stream], self.tokens[stream] = n, tok, [tok]
         return tok
 

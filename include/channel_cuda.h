@@ -170,7 +170,7 @@ int ch_decode_tokens(ch_model *m, uint32_t *tokens, uint32_t n);            /* s
  * reference serves one stream, src/server_queue.zig:9-145, src/server.zig:259-281).
  * Each stream owns a 4,096-slot KV cache per layer; its ring bookkeeping stays on
  * the host (ch_ring_*), one ring per stream.  A step takes one token from each of
- * up to max_batch distinct streams and returns each stream's greedy next token; the
+ * up to max_batch (<= 64) distinct streams and returns each stream's greedy next token; the
  * weights are read once per step for the whole batch.  One GPU (no tensor parallel);
  * needs the device embedding.
  * ---------------------------------------------------------------------- */
@@ -273,6 +273,10 @@ size_t ch_ring_total_ingested(const ch_ring *r);
 size_t ch_ring_window_size(const ch_ring *r, size_t layer);
 size_t ch_ring_get_slot_index(const ch_ring *r, size_t layer, size_t clock);
 size_t ch_ring_activate_slot(ch_ring *r, size_t layer, size_t clock);
+/* no reference counterpart: ch_ring_activate_slot of clocks [clock0, clock0 + n) in every
+ * layer, in clock order, with each clock's layer-0 slot in slots_out (may be NULL) -- the
+ * host bookkeeping of a prompt chunk in one call */
+void ch_ring_activate_range(ch_ring *r, size_t clock0, size_t n, uint32_t *slots_out);
 void ch_ring_deactivate_slot(ch_ring *r, size_t layer, size_t clock);
 void ch_ring_rollback_clock(ch_ring *r, size_t target_clock);
 void ch_ring_write_kv_meta(ch_ring *r, size_t layer, size_t clock);
