@@ -52,6 +52,8 @@ def parse():
     ap.add_argument("--layers", type=int, default=48)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-config5", action="store_true", help="skip the multi-stream (config 5) measurement")
+    ap.add_argument("--config5-streams", type=int, default=64)
     ap.add_argument("--kernel-only", action="store_true",
                     help="only time the dominant kernel (fused gate/up GEMV) over rotating layers; for ncu captures")
     return ap.parse_args()
@@ -252,6 +254,62 @@ def gemv_config1(ctx, stream, reps=8, copies=24):
             "launches_timed": n, "peak_kind": peak_kind + " hbm_gbs (burst)"}
 
 
+def config5(ctx, gm, cfg, stream, n_streams=64, n_tokens=128, lo=16, hi=2048, seed=4):
+    """BASELINE config 5 on the config-4 model: n_streams greedy streams, prompt lengths
+    uniform in [lo, hi] and uniform token ids (seeded), n_tokens tokens each (the
+    prefill's greedy token is the first), every stream with its own 4,096-slot ring KV.
+    Prompts are prefilled stream by stream; then each decode step packs every stream
+    (up to 64) into one ch_streams_decode call.  decode_tok_s = generated decode tokens
+    / decode time (CUDA events on the library stream around all steps, the host ring
+    bookkeeping between steps included); bytes_per_step = Q4 + Q8 weights once + every
+    stream's K/V rows read."""
+    import torch
+    from channel_b200.streams import MultiStreamDecoder
+    rng = np.random.default_rng(seed)
+    lens = rng.integers(lo, hi + 1, n_streams)
+    prompts = [rng.integers(0, cfg.vocab_size, int(n)).astype(np.uint32) for n in lens]
+    dec = MultiStreamDecoder(gm, cfg, n_streams, min(n_streams, 64))
+    ctx.synchronize()
+    t0 = time.time()
+    for s, p in enumerate(prompts):
+        dec.prefill(s, p)
+    ctx.synchronize()
+    prefill_s = time.time() - t0
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    kv_rows = 0  # K/V rows (all kv heads of one slot, per layer) the decode steps read
+    n_full = sum(1 for full in cfg.layer_types[:cfg.num_hidden_layers] if full)
+    e0.record(stream)
+    while True:
+        live = [s for s in range(n_streams) if len(dec.tokens[s]) < n_tokens]
+        if not live:
+            break
+        for i in range(0, len(live), dec.max_batch):
+            batch = live[i:i + dec.max_batch]
+            for s in batch:
+                c = dec.clock[s] + 1  # slots the step attends to
+                kv_rows += n_full * min(c, 4096) + (cfg.num_hidden_layers - n_full) * min(c, cfg.sliding_window)
+            dec.step(batch)
+    e1.record(stream)
+    e1.synchronize()
+    decode_s = e0.elapsed_time(e1) / 1000.0
+    steps = dec.steps
+    tokens = n_streams * (n_tokens - 1)
+    weight_bytes = (cfg.num_hidden_layers * (cfg.hidden_size * (cfg.q_dim + 2 * cfg.kv_dim) + cfg.q_dim * cfg.hidden_size
+                                             + 3 * cfg.hidden_size * cfg.intermediate_size) * 18 // 32
+                    + cfg.vocab_size * cfg.hidden_size * 36 // 32)
+    kv_bytes = kv_rows * 2 * cfg.kv_dim * 2
+    step_bytes = weight_bytes + kv_bytes / steps
+    peak, peak_kind = peaks()
+    gbs = step_bytes / (decode_s / steps) / 1e9
+    return {"workload": f"config5: {n_streams} streams, prompts U[{lo},{hi}] (seed {seed}), {n_tokens} greedy tokens each, "
+                        "own 4096-slot ring KV per stream, one batched step for all streams",
+            "prompt_tokens": int(lens.sum()), "prefill_s": prefill_s, "prefill_tok_s": float(lens.sum()) / prefill_s,
+            "decode_steps": steps, "decode_s": decode_s, "decode_tok_s": tokens / decode_s,
+            "ms_per_step": decode_s / steps * 1000, "bytes_per_step": step_bytes,
+            "achieved_gbs": gbs, "peak_gbs": peak, "frac": gbs / peak, "peak_kind": peak_kind + " hbm_gbs",
+            "tokens_head": [dec.tokens[s][:4] for s in range(2)]}
+
+
 def prefill_roofline(ctx, gm, cfg, stream, n_tok, layers=8, reps=2):
     """The prefill's Q4 GEMMs (tcgen05 kernel, CTA-pair M256xN256) on a 512-token
     batch: QKV, O, fused gate|up (+GELU*up) and down of `layers` consecutive layers,
@@ -422,6 +480,9 @@ def ours(args):
     # the Q4 GEMV on its own (metric's second part): fused gate/up, op-level kernel, rotating layers
     gemv_rl = gateup_roofline(ctx, gm, cfg, stream, reps=3) if world == 1 else None
     gemv_c1 = gemv_config1(ctx, stream) if world == 1 else None
+    c5 = None
+    if world == 1 and not args.no_config5 and cfg.num_hidden_layers == 48:
+        c5 = config5(ctx, gm, cfg, stream, n_streams=args.config5_streams)
     # the batched prefill (one GPU): whole 512-token prompt, and its tensor-core GEMMs alone
     prefill_rl = None
     if world == 1:
@@ -497,6 +558,7 @@ def ours(args):
             "roofline": rl,
             "gemv_roofline": gemv_rl,
             "gemv_config1": gemv_c1,
+            "config5": c5,
             "prefill_roofline": prefill_rl,
             "cpu_baseline": cpu,
             "e2e": e2e,

@@ -129,6 +129,16 @@ struct TopkArgs {
 };
 int topk_blocks(uint32_t V);
 cudaError_t launch_topk64(const TopkArgs &a, cudaStream_t s, bool pdl);
+// Q8 LM head for B <= 64 hidden states at once (lmhead.cu)
+struct LmHeadArgs {
+  const uint8_t *tiles;  // Q8 tiles of the head, [V/16 row tiles][K/32]
+  uint32_t row_tiles, K, V, B;
+  const uint4 *xf;       // set by launch_lmhead_q8 (the token fragments)
+  float *logits;         // [B][V]
+  uint32_t *err;
+};
+size_t lmhead_frag_words(uint32_t B, uint32_t K);
+cudaError_t launch_lmhead_q8(const float *x, uint32_t ldx, LmHeadArgs a, uint32_t *xf, cudaStream_t s);
 // greedy (top-1 of the softcapped keys) of each of n rows of V logits
 cudaError_t launch_argmax_rows(const float *logits, uint32_t n, uint32_t V, uint32_t *ids, cudaStream_t s);
 

@@ -242,6 +242,7 @@ struct ch_model {
   float2 *ms_rope = nullptr;       // [2][ms_cap][rot/2]: sliding theta, then full theta
   float *ms_partial = nullptr;     // attention split partials, [ms_cap] slices
   uint32_t *ms_counters = nullptr; // [ms_cap][n_kv]
+  uint32_t *ms_xf = nullptr;       // the LM head's token fragments
   uint32_t *h_ms_u32 = nullptr;    // pinned: tokens | streams | lists | ids
   StepParams *h_ms_sp = nullptr;
   float2 *h_ms_rope = nullptr;
@@ -1603,12 +1604,12 @@ static void free_streams(ch_model *m) {
   m->skc.clear();
   m->svc.clear();
   void *dev[] = {m->ms_logits, m->ms_tok, m->ms_stream, m->ms_ids, m->ms_lists, m->ms_sp, m->ms_rope,
-                 m->ms_partial, m->ms_counters};
+                 m->ms_partial, m->ms_counters, m->ms_xf};
   for (void *p : dev) cudaFree(p);
   void *host[] = {m->h_ms_u32, m->h_ms_sp, m->h_ms_rope};
   for (void *p : host) cudaFreeHost(p);
   m->ms_logits = nullptr, m->ms_tok = m->ms_stream = m->ms_ids = m->ms_lists = nullptr, m->ms_sp = nullptr;
-  m->ms_rope = nullptr, m->ms_partial = nullptr, m->ms_counters = nullptr;
+  m->ms_rope = nullptr, m->ms_partial = nullptr, m->ms_counters = nullptr, m->ms_xf = nullptr;
   m->h_ms_u32 = nullptr, m->h_ms_sp = nullptr, m->h_ms_rope = nullptr;
   m->ms_n = m->ms_cap = 0;
 }
@@ -1635,6 +1636,7 @@ static int init_streams(ch_model *m, uint32_t n_streams, uint32_t max_batch) {
   CH_TRY(dmalloc(&m->ms_partial, (size_t)max_batch * attn_partial_floats(m->nkv, R, m->D, m->attn_splits)));
   CH_TRY(dmalloc(&m->ms_counters, (size_t)max_batch * m->nkv));
   CH_CUDA(cudaMemset(m->ms_counters, 0, (size_t)max_batch * m->nkv * 4));
+  CH_TRY(dmalloc(&m->ms_xf, lmhead_frag_words(max_batch, m->H)));
   CH_CUDA(cudaMallocHost(&m->h_ms_u32, ((size_t)3 * max_batch + (size_t)max_batch * 2 * kSlots) * 4));
   CH_CUDA(cudaMallocHost(&m->h_ms_sp, max_batch * sizeof(StepParams)));
   CH_CUDA(cudaMallocHost(&m->h_ms_rope, (size_t)2 * max_batch * rh * sizeof(float2)));
@@ -1650,8 +1652,8 @@ extern "C" int ch_streams_init(ch_model *m, uint32_t n_streams, uint32_t max_bat
   if (!m->embed) return fail(CH_ESTATE, "multi-stream decode embeds on the device: the model needs its embedding");
   if (m->ms_n) return fail(CH_ESTATE, "streams already initialised");
   const uint32_t cap = m->cfg.max_prefill_tokens ? m->cfg.max_prefill_tokens : 1024;
-  if (n_streams == 0 || max_batch == 0 || max_batch > n_streams || max_batch > cap)
-    return fail(CH_EINVAL, "streams: 1 <= max_batch <= n_streams, max_batch <= max_prefill_tokens");
+  if (n_streams == 0 || max_batch == 0 || max_batch > n_streams || max_batch > cap || max_batch > 64)
+    return fail(CH_EINVAL, "streams: 1 <= max_batch <= n_streams, max_batch <= 64 and <= max_prefill_tokens");
   CH_CUDA(cudaSetDevice(m->ctx->device));
   const int rc = init_streams(m, n_streams, max_batch);
   if (rc != CH_OK) {
@@ -1760,20 +1762,16 @@ extern "C" int ch_streams_decode(ch_model *m, const ch_stream_step *steps, uint3
     const float *next = (l + 1 < m->L) ? m->layers[l + 1].input_norm : m->final_norm;
     CH_CUDA(launch_add_rmsnorm_rows(m->pX, m->pMO, next, m->pNX, n, m->H, eps, dl.scalar, s));
   }
-  for (uint32_t b = 0; b < n; b++) {  // Q8 LM head of each token's final-normed state
-    GemvArgs a;
-    GemvPlan p;
-    p.fmt = FMT_Q8;
-    a.tiles = m->lm;
-    a.row_tiles = m->V / 16;
-    a.k_tiles = m->H / 32;
-    a.K = m->H;
-    a.x = m->pNX + (size_t)b * m->H;
-    a.y = m->ms_logits + (size_t)b * m->V;
-    a.partial = m->gemv_partial;
-    a.counters = m->gemv_counters;
-    a.err = err;
-    CH_CUDA(launch_gemv(p, a, s, b > 0));
+  {  // Q8 LM head of every token's final-normed state, the head read once for the batch
+    LmHeadArgs h{};
+    h.tiles = m->lm;
+    h.row_tiles = m->V / 16;
+    h.K = m->H;
+    h.V = m->V;
+    h.B = n;
+    h.logits = m->ms_logits;
+    h.err = err;
+    CH_CUDA(launch_lmhead_q8(m->pNX, m->H, h, m->ms_xf, s));
   }
   CH_CUDA(launch_argmax_rows(m->ms_logits, n, m->V, m->ms_ids, s));
   CH_CUDA(cudaMemcpyAsync(h_ids, m->ms_ids, n * 4, cudaMemcpyDeviceToHost, s));

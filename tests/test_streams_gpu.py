@@ -1,9 +1,10 @@
 """Multi-stream greedy decode (BASELINE config 5's path) against the oracle.
 
-Four streams with ragged prompts share one model; each has its own ring and KV
-cache.  Steps pack up to three streams per launch (so a round of four streams
-takes two launches) and every stream must reproduce, token for token, the greedy
-stream the oracle produces for it alone (prefill, then forward_token per step)."""
+Streams with ragged prompts share one model; each has its own ring and KV cache.
+Steps pack up to max_batch streams per launch (four streams at three per launch
+take two launches a round; 9 and 17 streams in one launch run the batched LM head
+with padded token groups) and every stream must reproduce, token for token, the
+greedy stream the oracle produces for it alone (prefill, then forward_token)."""
 import numpy as np
 import pytest
 
@@ -13,7 +14,6 @@ from tests.model_util import ring_step_lists, small_config
 pytestmark = pytest.mark.gpu
 
 SEED = 7
-PROMPT_LENS = [5, 11, 3, 17]
 N_TOKENS = 6
 
 
@@ -37,20 +37,22 @@ def _oracle_stream(oracle, cfg, w, prompt, n_tokens):
     return out
 
 
-def test_streams_match_oracle(ctx, oracle):
+@pytest.mark.parametrize("n_streams,max_batch", [(4, 3), (9, 9), (17, 17)])
+def test_streams_match_oracle(ctx, oracle, n_streams, max_batch):
     from channel_b200 import GpuModelContext
     from channel_b200.streams import MultiStreamDecoder
     cfg = small_config()
-    rng = np.random.default_rng(11)
-    prompts = [rng.integers(0, cfg.vocab_size, n).astype(np.uint32) for n in PROMPT_LENS]
+    rng = np.random.default_rng(11 + n_streams)
+    lens = rng.integers(1, 20, n_streams)
+    prompts = [rng.integers(0, cfg.vocab_size, n).astype(np.uint32) for n in lens]
     w = oracle.SyntheticWeights(cfg, SEED)
     refs = [_oracle_stream(oracle, cfg, w, p, N_TOKENS) for p in prompts]
     gm = GpuModelContext.synthetic(ctx, cfg, SEED)
-    dec = MultiStreamDecoder(gm, cfg, n_streams=len(prompts), max_batch=3)
+    dec = MultiStreamDecoder(gm, cfg, n_streams=n_streams, max_batch=max_batch)
     got = dec.run(prompts, N_TOKENS)
     for s, (g, r) in enumerate(zip(got, refs)):
         assert g == r, f"stream {s}: {g} != oracle {r}"
-    assert dec.steps == 2 * (N_TOKENS - 1)  # four streams at three per launch
+    assert dec.steps == -(-n_streams // max_batch) * (N_TOKENS - 1)
     assert ctx.device_status() == 0
     gm.deinit()
 
