@@ -132,36 +132,58 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attn_kernel(const AttnArg
 #pragma unroll
     for (int e = 0; e < EPL; e++) qr[h][e] = q_s[h * D + lane * EPL + e];
 
-  for (uint32_t i = warp; i < n; i += kAttnWarps) {
+  // rows of this chunk, kU slots per warp iteration with every load issued before any is
+  // used (one slot per iteration left each warp waiting a full memory round trip per
+  // slot); the per-slot arithmetic and the per-warp slot order are unchanged.
+  // kind: 0 = cache row in rw, 1 = the new row (shared memory), 2 = invalid slot, 3 = past n
+  constexpr int kU = 4;
+  auto fetch = [&](const __half *cache, uint32_t i, uint4 &rw) -> int {
+    if (i >= n) return 3;
     const uint32_t phys = list[c0 + i];
-    float kv[EPL];
-    bool valid = true;
-    if (phys == sp.slot) {
+    if (phys == sp.slot) return 1;
+    if (phys >= a.cache_slots) return 2;
+    rw = *reinterpret_cast<const uint4 *>(cache + (size_t)phys * kv_dim + (size_t)kvh * D + lane * EPL);
+    return 0;
+  };
+  auto unpack = [&](int kind, const uint4 &rw, const float *fresh, float (&f)[EPL]) {
+    if (kind == 1) {
 #pragma unroll
-      for (int e = 0; e < EPL; e++) kv[e] = k_new[lane * EPL + e];
-    } else if (phys < a.cache_slots) {
-      const uint4 rw = *reinterpret_cast<const uint4 *>(k_cache + (size_t)phys * kv_dim + (size_t)kvh * D + lane * EPL);
+      for (int e = 0; e < EPL; e++) f[e] = fresh[lane * EPL + e];
+    } else if (kind == 0) {
       const __half2 *hp = reinterpret_cast<const __half2 *>(&rw);
 #pragma unroll
       for (int e = 0; e < EPL / 2; e++) {
-        float2 f = __half22float2(hp[e]);
-        kv[2 * e] = f.x;
-        kv[2 * e + 1] = f.y;
+        const float2 v = __half22float2(hp[e]);
+        f[2 * e] = v.x;
+        f[2 * e + 1] = v.y;
       }
     } else {
-      valid = false;
 #pragma unroll
-      for (int e = 0; e < EPL; e++) kv[e] = 0.f;
+      for (int e = 0; e < EPL; e++) f[e] = 0.f;
     }
+  };
+  for (uint32_t i0 = warp; i0 < n; i0 += kU * kAttnWarps) {
+    uint4 rw[kU];
+    int kind[kU];
 #pragma unroll
-    for (int h = 0; h < R; h++) {
-      float dot = 0.f;
+    for (int u = 0; u < kU; u++) kind[u] = fetch(k_cache, i0 + u * kAttnWarps, rw[u]);
 #pragma unroll
-      for (int e = 0; e < EPL; e++) dot = __fmaf_rn(qr[h][e], kv[e], dot);
-      dot = warp_sum(dot);
-      if (lane == 0) sc[h * chunk_cap + i] = valid ? __fmul_rn(dot, a.scale) : -INFINITY;
+    for (int u = 0; u < kU; u++) {
+      if (kind[u] == 3) continue;
+      const uint32_t i = i0 + u * kAttnWarps;
+      float kv[EPL];
+      unpack(kind[u], rw[u], k_new, kv);
+      const bool valid = kind[u] != 2;
+#pragma unroll
+      for (int h = 0; h < R; h++) {
+        float dot = 0.f;
+#pragma unroll
+        for (int e = 0; e < EPL; e++) dot = __fmaf_rn(qr[h][e], kv[e], dot);
+        dot = warp_sum(dot);
+        if (lane == 0) sc[h * chunk_cap + i] = valid ? __fmul_rn(dot, a.scale) : -INFINITY;
+      }
+      if (!valid && lane == 0) atomicOr(a.err, DEV_ERR_BAD_LIST);
     }
-    if (!valid && lane == 0) atomicOr(a.err, DEV_ERR_BAD_LIST);
   }
   __syncthreads();
 
@@ -190,30 +212,23 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attn_kernel(const AttnArg
   for (int h = 0; h < R; h++)
 #pragma unroll
     for (int e = 0; e < EPL; e++) acc[h][e] = 0.f;
-  for (uint32_t i = warp; i < n; i += kAttnWarps) {
-    const uint32_t phys = list[c0 + i];
-    float vv[EPL];
-    if (phys == sp.slot) {
+  for (uint32_t i0 = warp; i0 < n; i0 += kU * kAttnWarps) {
+    uint4 rw[kU];
+    int kind[kU];
 #pragma unroll
-      for (int e = 0; e < EPL; e++) vv[e] = v_new[lane * EPL + e];
-    } else if (phys < a.cache_slots) {
-      const uint4 rw = *reinterpret_cast<const uint4 *>(v_cache + (size_t)phys * kv_dim + (size_t)kvh * D + lane * EPL);
-      const __half2 *hp = reinterpret_cast<const __half2 *>(&rw);
+    for (int u = 0; u < kU; u++) kind[u] = fetch(v_cache, i0 + u * kAttnWarps, rw[u]);
 #pragma unroll
-      for (int e = 0; e < EPL / 2; e++) {
-        float2 f = __half22float2(hp[e]);
-        vv[2 * e] = f.x;
-        vv[2 * e + 1] = f.y;
+    for (int u = 0; u < kU; u++) {
+      if (kind[u] == 3) continue;
+      const uint32_t i = i0 + u * kAttnWarps;
+      float vv[EPL];
+      unpack(kind[u], rw[u], v_new, vv);
+#pragma unroll
+      for (int h = 0; h < R; h++) {
+        const float p = sc[h * chunk_cap + i];
+#pragma unroll
+        for (int e = 0; e < EPL; e++) acc[h][e] = __fmaf_rn(p, vv[e], acc[h][e]);
       }
-    } else {
-#pragma unroll
-      for (int e = 0; e < EPL; e++) vv[e] = 0.f;
-    }
-#pragma unroll
-    for (int h = 0; h < R; h++) {
-      const float p = sc[h * chunk_cap + i];
-#pragma unroll
-      for (int e = 0; e < EPL; e++) acc[h][e] = __fmaf_rn(p, vv[e], acc[h][e]);
     }
   }
 #pragma unroll

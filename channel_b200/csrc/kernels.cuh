@@ -138,6 +138,20 @@ struct LmHeadArgs {
   uint32_t *err;
 };
 size_t lmhead_frag_words(uint32_t B, uint32_t K);
+// Q4 projections for B <= 64 hidden states at once (lmhead.cu): split-K partials, then an
+// ordered sum with the epilogue (EPI_STORE or EPI_GELU_MUL on gate|up tiles)
+struct SkinnyArgs {
+  const uint8_t *tiles;  // Q4 tiles, [row_tiles][K/64]
+  uint32_t row_tiles, K, B, splits, kt_per_split;
+  const uint4 *xf;
+  float *partial;        // [splits][B][row_tiles * 16]
+  uint32_t *err;
+};
+uint32_t skinny_splits(uint32_t row_tiles, uint32_t K);
+size_t skinny_partial_floats(uint32_t B, uint32_t row_tiles, uint32_t K);
+cudaError_t launch_skinny_q4(const uint8_t *tiles, uint32_t row_tiles, uint32_t K, const float *x, uint32_t ldx,
+                             uint32_t B, int epi, float *y, uint32_t ldy, uint32_t *xf, float *partial, uint32_t *err,
+                             cudaStream_t s);
 cudaError_t launch_lmhead_q8(const float *x, uint32_t ldx, LmHeadArgs a, uint32_t *xf, cudaStream_t s);
 // greedy (top-1 of the softcapped keys) of each of n rows of V logits
 cudaError_t launch_argmax_rows(const float *logits, uint32_t n, uint32_t V, uint32_t *ids, cudaStream_t s);

@@ -1,4 +1,5 @@
-// lmhead.cu -- the Q8 LM head for a batch of hidden states (multi-stream decode).
+// lmhead.cu -- skinny GEMMs of the multi-stream decode step: the Q8 LM head and the
+// Q4 layer projections for a batch of up to 64 hidden states.
 //
 // logits[b][r] = sum_blk s_{r,blk} * sum_i q_{r,i} * x_{b,i}   (gemv_q8.wgsl, for B vectors)
 //
@@ -11,6 +12,8 @@
 // the two k16 MMAs of a token group are summed (hi + lo) and scaled by the row's f32
 // block scale into the lane's accumulators, like the single-vector tiles (core.cuh:
 // tile_mma<FMT_Q8>), so every logit is fp32-faithful.
+#include <algorithm>
+
 #include "common.cuh"
 #include "core.cuh"
 #include "kernels.cuh"
@@ -157,6 +160,154 @@ __global__ void __launch_bounds__(kLw * 32, 1) lmhead_q8_kernel(const LmHeadArgs
   }
 }
 
+// ---------------------------------------------------------------------------
+// Q4 projections (q|k|v, o, gate|up, down) for the batch: the same scheme on Q4 tiles
+// (16 rows x 64 k, two 32-blocks with f16 scales; tile_mma<FMT_Q4>'s arithmetic per
+// token), with the K dimension split over gridDim.y so that the 240-row-tile o and down
+// matrices still cover the GPU.  Each split writes its partial sums to
+// partial[split][token][row]; skinny_reduce_kernel adds the splits in order (so the
+// result does not depend on scheduling) and applies the epilogue.
+template <int NG>
+__global__ void __launch_bounds__(kLw * 32, 1) skinny_q4_kernel(const SkinnyArgs a) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  constexpr uint32_t kXChunk = 2 * kKc * NG * 32 * 16;  // x fragments of kKc Q4 k-tiles (2 per k-tile)
+  constexpr uint32_t kWChunk = kKc * kTileBytes;
+  uint4 *xs = reinterpret_cast<uint4 *>(smem);  // [2][2 kKc][NG][32]
+  uint8_t *ws = smem + 2 * kXChunk;             // [kLw][2][kWChunk]
+  uint64_t *xbar = reinterpret_cast<uint64_t *>(ws + (size_t)kLw * 2 * kWChunk);
+  uint64_t *wbar = xbar + 2;
+  __shared__ uint32_t bad, fail_ch;
+
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int g = lane >> 2, t = lane & 3;
+  const uint32_t rt = blockIdx.x * kLw + warp;
+  const bool active = rt < a.row_tiles;
+  const uint32_t KT = a.K / 64, k0 = blockIdx.y * a.kt_per_split, k1 = min(KT, k0 + a.kt_per_split);
+  const uint32_t nkt = k1 > k0 ? k1 - k0 : 0, nch = (nkt + kKc - 1) / kKc;
+  auto chunk_tiles = [&](uint32_t ch) { return min((uint32_t)kKc, nkt - ch * kKc); };
+  uint8_t *my_w = ws + (size_t)warp * 2 * kWChunk;
+  auto issue_x = [&](uint32_t ch) {  // x fragments are per 32-block: two per Q4 k-tile
+    const uint32_t bytes = 2 * chunk_tiles(ch) * NG * 32 * 16;
+    mbar_arrive_expect_tx(&xbar[ch & 1], bytes);
+    bulk_g2s(xs + (size_t)(ch & 1) * 2 * kKc * NG * 32, a.xf + (size_t)(2 * (k0 + ch * kKc)) * NG * 32, bytes,
+             &xbar[ch & 1]);
+  };
+  auto issue_w = [&](uint32_t ch) {
+    const uint32_t bytes = chunk_tiles(ch) * kTileBytes;
+    mbar_arrive_expect_tx(&wbar[warp * 2 + (ch & 1)], bytes);
+    bulk_g2s(my_w + (size_t)(ch & 1) * kWChunk, a.tiles + ((size_t)rt * KT + k0 + (size_t)ch * kKc) * kTileBytes,
+             bytes, &wbar[warp * 2 + (ch & 1)]);
+  };
+  if (threadIdx.x == 0) {
+    bad = 0u;
+    fail_ch = nch;
+    mbar_init(&xbar[0], 1);
+    mbar_init(&xbar[1], 1);
+  }
+  if (lane == 0) {
+    mbar_init(&wbar[warp * 2], 1);
+    mbar_init(&wbar[warp * 2 + 1], 1);
+  }
+  fence_mbar_init();
+  __syncthreads();
+  if (threadIdx.x == 0)
+    for (uint32_t ch = 0; ch < 2 && ch < nch; ch++) issue_x(ch);
+  if (active && lane == 0)
+    for (uint32_t ch = 0; ch < 2 && ch < nch; ch++) issue_w(ch);
+
+  float acc[NG][2];
+#pragma unroll
+  for (int j = 0; j < NG; j++) acc[j][0] = acc[j][1] = 0.f;
+  for (uint32_t ch = 0; ch < nch; ch++) {
+    const uint32_t s = ch & 1, par = (ch >> 1) & 1;
+    if (!*(volatile uint32_t *)&bad && !mbar_wait_bounded(&xbar[s], par, a.err)) {
+      bad = 1u;
+      atomicMin(&fail_ch, ch);
+    }
+    if (active && !*(volatile uint32_t *)&bad && !mbar_wait_bounded(&wbar[warp * 2 + s], par, a.err)) {
+      bad = 1u;
+      atomicMin(&fail_ch, ch);
+    }
+    if (active && !*(volatile uint32_t *)&bad) {
+      const uint4 *xc = xs + (size_t)s * 2 * kKc * NG * 32;
+      const uint8_t *wc = my_w + (size_t)s * kWChunk;
+      const uint32_t nk = chunk_tiles(ch);
+      for (uint32_t kk = 0; kk < nk; kk++) {
+        const uint8_t *tile = wc + (size_t)kk * kTileBytes;
+        const uint4 w = *reinterpret_cast<const uint4 *>(tile + lane * 16);
+        const uint2 sc = *reinterpret_cast<const uint2 *>(tile + 512 + g * 8);
+        const float2 fg = __half22float2(*reinterpret_cast<const __half2 *>(&sc.x));   // row g: blk0, blk1
+        const float2 fg8 = __half22float2(*reinterpret_cast<const __half2 *>(&sc.y));  // row g+8
+        uint32_t a0[4], a1[4], a2[4], a3[4];
+        dequant_q4_word(w.x, a0);
+        dequant_q4_word(w.y, a1);
+        dequant_q4_word(w.z, a2);
+        dequant_q4_word(w.w, a3);
+#pragma unroll
+        for (int j = 0; j < NG; j++) {
+          const uint4 b0 = xc[((size_t)(2 * kk) * NG + j) * 32 + lane];
+          const uint4 b1 = xc[((size_t)(2 * kk + 1) * NG + j) * 32 + lane];
+          float d0[4] = {0.f, 0.f, 0.f, 0.f}, d1[4] = {0.f, 0.f, 0.f, 0.f};
+          mma_16816(d0, a0, b0.x, b0.y);
+          mma_16816(d1, a2, b1.x, b1.y);
+          mma_16816(d0, a1, b0.z, b0.w);
+          mma_16816(d1, a3, b1.z, b1.w);
+          acc[j][0] = __fmaf_rn(fg.x, __fadd_rn(d0[0], d0[1]), acc[j][0]);
+          acc[j][1] = __fmaf_rn(fg8.x, __fadd_rn(d0[2], d0[3]), acc[j][1]);
+          acc[j][0] = __fmaf_rn(fg.y, __fadd_rn(d1[0], d1[1]), acc[j][0]);
+          acc[j][1] = __fmaf_rn(fg8.y, __fadd_rn(d1[2], d1[3]), acc[j][1]);
+        }
+      }
+    }
+    __syncthreads();
+    if (ch + 2 < nch && !bad) {
+      fence_proxy_async();
+      if (threadIdx.x == 0) issue_x(ch + 2);
+      if (active && lane == 0) issue_w(ch + 2);
+    }
+  }
+  if (bad) {
+    for (uint32_t ch = fail_ch; ch < fail_ch + 2 && ch < nch; ch++) {
+      if (threadIdx.x == 0) mbar_wait_bounded(&xbar[ch & 1], (ch >> 1) & 1, nullptr, 100000000ull);
+      if (active && lane == 0) mbar_wait_bounded(&wbar[warp * 2 + (ch & 1)], (ch >> 1) & 1, nullptr, 100000000ull);
+    }
+    return;
+  }
+  if (!active) return;
+  const size_t R16 = (size_t)a.row_tiles * 16;
+  const uint32_t r0 = rt * 16 + g;
+#pragma unroll
+  for (int j = 0; j < NG; j++) {
+    const uint32_t tok = 4 * j + t;
+    if (tok < a.B) {
+      float *pr = a.partial + ((size_t)blockIdx.y * a.B + tok) * R16;
+      pr[r0] = acc[j][0];
+      pr[r0 + 8] = acc[j][1];
+    }
+  }
+}
+
+// sum of the splits in order, then the epilogue: y[tok * ldy + row] (EPI_STORE) or, for
+// gate|up tiles (rows 0-7 gate, 8-15 up of each row tile), y[tok * ldy + rt*8 + i] =
+// gelu(gate row i) * up row i
+__global__ void skinny_reduce_kernel(const float *partial, uint32_t splits, uint32_t B, uint32_t row_tiles, int epi,
+                                     float *y, uint32_t ldy) {
+  const size_t R16 = (size_t)row_tiles * 16;
+  const uint32_t per_tok = epi == EPI_GELU_MUL ? row_tiles * 8 : row_tiles * 16;
+  const size_t n = (size_t)B * per_tok;
+  for (size_t idx = blockIdx.x * (size_t)blockDim.x + threadIdx.x; idx < n; idx += (size_t)gridDim.x * blockDim.x) {
+    const uint32_t tok = (uint32_t)(idx / per_tok), o = (uint32_t)(idx % per_tok);
+    const uint32_t row = epi == EPI_GELU_MUL ? (o / 8) * 16 + o % 8 : o;
+    float v = 0.f, u = 0.f;
+    for (uint32_t s = 0; s < splits; s++) {
+      const float *pr = partial + ((size_t)s * B + tok) * R16;
+      v = s ? __fadd_rn(v, pr[row]) : pr[row];
+      if (epi == EPI_GELU_MUL) u = s ? __fadd_rn(u, pr[row + 8]) : pr[row + 8];
+    }
+    y[(size_t)tok * ldy + o] = epi == EPI_GELU_MUL ? __fmul_rn(gelu_tanh(v), u) : v;
+  }
+}
+
 // token groups of 4 the kernel runs for B tokens (instantiated: 1, 2, 4, 8, 16)
 static uint32_t lmhead_groups(uint32_t B) {
   const uint32_t ng = (B + 3) / 4;
@@ -176,6 +327,65 @@ static cudaError_t launch_lmhead_t(const LmHeadArgs &a, cudaStream_t s) {
   const uint32_t grid = (a.row_tiles + kLw - 1) / kLw;
   lmhead_q8_kernel<NG><<<grid, kLw * 32, smem, s>>>(a);
   return cudaGetLastError();
+}
+
+// K splits for a Q4 skinny GEMM of row_tiles x (K/64) tiles: enough CTAs for two waves of
+// the GPU, each split at least kKc k-tiles
+uint32_t skinny_splits(uint32_t row_tiles, uint32_t K) {
+  const uint32_t KT = K / 64, ctas = (row_tiles + kLw - 1) / kLw, want = (2 * (uint32_t)num_sms() + ctas - 1) / ctas;
+  const uint32_t cap = std::max(1u, KT / kKc);
+  return std::max(1u, std::min(want, cap));
+}
+
+template <int NG>
+static cudaError_t launch_skinny_t(const SkinnyArgs &a, cudaStream_t s) {
+  const size_t smem = (size_t)2 * 2 * kKc * NG * 32 * 16 + (size_t)kLw * 2 * kKc * kTileBytes + (2 + 2 * kLw) * 8;
+  static size_t attr = 0;
+  if (smem > attr) {
+    cudaError_t e = cudaFuncSetAttribute(skinny_q4_kernel<NG>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    attr = smem;
+  }
+  skinny_q4_kernel<NG><<<dim3((a.row_tiles + kLw - 1) / kLw, a.splits), kLw * 32, smem, s>>>(a);
+  return cudaGetLastError();
+}
+
+// y = W x for B tokens (x row stride ldx, y row stride ldy); xf and partial are scratch of
+// lmhead_frag_words(B, K) words and skinny_partial_floats(B, row_tiles, K) floats
+cudaError_t launch_skinny_q4(const uint8_t *tiles, uint32_t row_tiles, uint32_t K, const float *x, uint32_t ldx,
+                             uint32_t B, int epi, float *y, uint32_t ldy, uint32_t *xf, float *partial, uint32_t *err,
+                             cudaStream_t s) {
+  if (B == 0 || B > 64 || K % 64 || row_tiles == 0) return cudaErrorInvalidValue;
+  const uint32_t ngp = lmhead_groups(B), n = K / 32 * ngp * 32;
+  lmhead_frag_kernel<<<(n + 255) / 256, 256, 0, s>>>(x, ldx, B, K, ngp, reinterpret_cast<uint4 *>(xf));
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  SkinnyArgs a{};
+  a.tiles = tiles;
+  a.row_tiles = row_tiles;
+  a.K = K;
+  a.B = B;
+  a.splits = skinny_splits(row_tiles, K);
+  a.kt_per_split = (K / 64 + a.splits - 1) / a.splits;
+  a.splits = (K / 64 + a.kt_per_split - 1) / a.kt_per_split;  // no empty split
+  a.xf = reinterpret_cast<const uint4 *>(xf);
+  a.partial = partial;
+  a.err = err;
+  switch (ngp) {
+    case 1: e = launch_skinny_t<1>(a, s); break;
+    case 2: e = launch_skinny_t<2>(a, s); break;
+    case 4: e = launch_skinny_t<4>(a, s); break;
+    case 8: e = launch_skinny_t<8>(a, s); break;
+    default: e = launch_skinny_t<16>(a, s); break;
+  }
+  if (e != cudaSuccess) return e;
+  const size_t outs = (size_t)B * row_tiles * 16;
+  skinny_reduce_kernel<<<(unsigned)std::min<size_t>((outs + 255) / 256, 4096), 256, 0, s>>>(partial, a.splits, B,
+                                                                                          row_tiles, epi, y, ldy);
+  return cudaGetLastError();
+}
+size_t skinny_partial_floats(uint32_t B, uint32_t row_tiles, uint32_t K) {
+  return (size_t)skinny_splits(row_tiles, K) * B * row_tiles * 16;
 }
 
 // x: B hidden states (row stride ldx floats); xf scratch: lmhead_frag_words(B, K) words

@@ -242,7 +242,8 @@ struct ch_model {
   float2 *ms_rope = nullptr;       // [2][ms_cap][rot/2]: sliding theta, then full theta
   float *ms_partial = nullptr;     // attention split partials, [ms_cap] slices
   uint32_t *ms_counters = nullptr; // [ms_cap][n_kv]
-  uint32_t *ms_xf = nullptr;       // the LM head's token fragments
+  uint32_t *ms_xf = nullptr;       // token fragments of the skinny GEMMs (largest K)
+  float *ms_skp = nullptr;         // split-K partials of the skinny Q4 GEMMs
   uint32_t *h_ms_u32 = nullptr;    // pinned: tokens | streams | lists | ids
   StepParams *h_ms_sp = nullptr;
   float2 *h_ms_rope = nullptr;
@@ -1604,12 +1605,12 @@ static void free_streams(ch_model *m) {
   m->skc.clear();
   m->svc.clear();
   void *dev[] = {m->ms_logits, m->ms_tok, m->ms_stream, m->ms_ids, m->ms_lists, m->ms_sp, m->ms_rope,
-                 m->ms_partial, m->ms_counters, m->ms_xf};
+                 m->ms_partial, m->ms_counters, m->ms_xf, m->ms_skp};
   for (void *p : dev) cudaFree(p);
   void *host[] = {m->h_ms_u32, m->h_ms_sp, m->h_ms_rope};
   for (void *p : host) cudaFreeHost(p);
   m->ms_logits = nullptr, m->ms_tok = m->ms_stream = m->ms_ids = m->ms_lists = nullptr, m->ms_sp = nullptr;
-  m->ms_rope = nullptr, m->ms_partial = nullptr, m->ms_counters = nullptr, m->ms_xf = nullptr;
+  m->ms_rope = nullptr, m->ms_partial = nullptr, m->ms_counters = nullptr, m->ms_xf = nullptr, m->ms_skp = nullptr;
   m->h_ms_u32 = nullptr, m->h_ms_sp = nullptr, m->h_ms_rope = nullptr;
   m->ms_n = m->ms_cap = 0;
 }
@@ -1636,7 +1637,15 @@ static int init_streams(ch_model *m, uint32_t n_streams, uint32_t max_batch) {
   CH_TRY(dmalloc(&m->ms_partial, (size_t)max_batch * attn_partial_floats(m->nkv, R, m->D, m->attn_splits)));
   CH_TRY(dmalloc(&m->ms_counters, (size_t)max_batch * m->nkv));
   CH_CUDA(cudaMemset(m->ms_counters, 0, (size_t)max_batch * m->nkv * 4));
-  CH_TRY(dmalloc(&m->ms_xf, lmhead_frag_words(max_batch, m->H)));
+  CH_TRY(dmalloc(&m->ms_xf, lmhead_frag_words(max_batch, std::max({m->H, m->qd, m->I}))));
+  {
+    const uint32_t qkvd = m->qd + 2 * m->kvd;
+    size_t p = skinny_partial_floats(max_batch, qkvd / 16, m->H);
+    p = std::max(p, skinny_partial_floats(max_batch, m->H / 16, m->qd));
+    p = std::max(p, skinny_partial_floats(max_batch, 2 * m->I / 16, m->H));
+    p = std::max(p, skinny_partial_floats(max_batch, m->H / 16, m->I));
+    CH_TRY(dmalloc(&m->ms_skp, p));
+  }
   CH_CUDA(cudaMallocHost(&m->h_ms_u32, ((size_t)3 * max_batch + (size_t)max_batch * 2 * kSlots) * 4));
   CH_CUDA(cudaMallocHost(&m->h_ms_sp, max_batch * sizeof(StepParams)));
   CH_CUDA(cudaMallocHost(&m->h_ms_rope, (size_t)2 * max_batch * rh * sizeof(float2)));
@@ -1724,7 +1733,8 @@ extern "C" int ch_streams_decode(ch_model *m, const ch_stream_step *steps, uint3
   for (uint32_t l = 0; l < m->L; l++) {
     DevLayer &dl = m->layers[l];
     if (l == 0) CH_CUDA(launch_rmsnorm_rows(m->pX, dl.input_norm, m->pNX, n, m->H, eps, s));
-    CH_CUDA(launch_batch_gemm_q4_tc(BatchGemmArgs{dl.qkv, qkvd, m->H, n, m->pNX, m->pQKV, EPI_STORE}, m->pXS, err, s));
+    CH_CUDA(launch_skinny_q4(dl.qkv, qkvd / 16, m->H, m->pNX, m->H, n, EPI_STORE, m->pQKV, qkvd, m->ms_xf, m->ms_skp,
+                             err, s));
     AttnArgs a{};
     a.qkv = m->pQKV;
     a.qkv_stride = qkvd;
@@ -1751,13 +1761,19 @@ extern "C" int ch_streams_decode(ch_model *m, const ch_stream_step *steps, uint3
     a.err = err;
     a.cache_slots = kSlots;
     a.n_tok = n;
-    CH_CUDA(launch_decode_attn(a, m->attn_splits, s, false));
-    CH_CUDA(launch_batch_gemm_q4_tc(BatchGemmArgs{dl.o, m->H, m->qd, n, m->pA, m->pMO, EPI_STORE}, m->pXS, err, s));
+    // splits per (token, kv head): about 8 CTAs per SM over the whole batch (64 streams x 8
+    // kv heads need 3; a single token keeps the model's split count)
+    const uint32_t want = (8u * (uint32_t)num_sms() + n * m->nkv - 1) / (n * m->nkv);
+    const int splits = (int)std::max(1u, std::min((uint32_t)m->attn_splits, want));
+    CH_CUDA(launch_decode_attn(a, splits, s, false));
+    CH_CUDA(launch_skinny_q4(dl.o, m->H / 16, m->qd, m->pA, m->qd, n, EPI_STORE, m->pMO, m->H, m->ms_xf, m->ms_skp,
+                             err, s));
     if (dl.post_attn) CH_CUDA(launch_rmsnorm_rows(m->pMO, dl.post_attn, m->pMO, n, m->H, eps, s));
     CH_CUDA(launch_add_rmsnorm_rows(m->pX, m->pMO, dl.pre_ffn, m->pNX, n, m->H, eps, 1.0f, s));
-    CH_CUDA(launch_batch_gemm_q4_tc(BatchGemmArgs{dl.gateup, 2 * m->I, m->H, n, m->pNX, m->pACT, EPI_GELU_MUL}, m->pXS,
-                                    err, s));
-    CH_CUDA(launch_batch_gemm_q4_tc(BatchGemmArgs{dl.down, m->H, m->I, n, m->pACT, m->pMO, EPI_STORE}, m->pXS, err, s));
+    CH_CUDA(launch_skinny_q4(dl.gateup, 2 * m->I / 16, m->H, m->pNX, m->H, n, EPI_GELU_MUL, m->pACT, m->I, m->ms_xf,
+                             m->ms_skp, err, s));
+    CH_CUDA(launch_skinny_q4(dl.down, m->H / 16, m->I, m->pACT, m->I, n, EPI_STORE, m->pMO, m->H, m->ms_xf,
+                             m->ms_skp, err, s));
     if (dl.post_ffn) CH_CUDA(launch_rmsnorm_rows(m->pMO, dl.post_ffn, m->pMO, n, m->H, eps, s));
     const float *next = (l + 1 < m->L) ? m->layers[l + 1].input_norm : m->final_norm;
     CH_CUDA(launch_add_rmsnorm_rows(m->pX, m->pMO, next, m->pNX, n, m->H, eps, dl.scalar, s));
