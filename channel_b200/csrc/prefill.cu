@@ -143,10 +143,9 @@ __global__ void __launch_bounds__(256) batch_causal_attn_kernel(const BatchAttnA
   float m = -1e9f, l = 0.f, acc[EPL];
 #pragma unroll
   for (int e = 0; e < EPL; e++) acc[e] = 0.f;
-  for (uint32_t i = start; i < S; i++) {
-    const uint32_t phys = a.slots[i];
-    const uint4 kr = *reinterpret_cast<const uint4 *>(a.k_cache + (size_t)phys * kvd + (size_t)kvh * D + lane * EPL);
-    const uint4 vr = *reinterpret_cast<const uint4 *>(a.v_cache + (size_t)phys * kvd + (size_t)kvh * D + lane * EPL);
+  // online softmax in slot order; the rows of four slots are loaded before any is used
+  // (one slot at a time left the warp waiting a memory round trip per slot)
+  auto step = [&](const uint4 &kr, const uint4 &vr) {
     const __half2 *kh = reinterpret_cast<const __half2 *>(&kr);
     const __half2 *vh = reinterpret_cast<const __half2 *>(&vr);
     float dot = 0.f;
@@ -168,6 +167,28 @@ __global__ void __launch_bounds__(256) batch_causal_attn_kernel(const BatchAttnA
       acc[2 * e + 1] = __fmaf_rn(acc[2 * e + 1], corr, __fmul_rn(p, f.y));
     }
     m = mn;
+  };
+  auto row = [&](const __half *cache, uint32_t phys) {
+    return *reinterpret_cast<const uint4 *>(cache + (size_t)phys * kvd + (size_t)kvh * D + lane * EPL);
+  };
+  constexpr int kU = 4;
+  uint32_t i = start;
+  for (; i + kU <= S; i += kU) {
+    uint32_t ph[kU];
+    uint4 kr[kU], vr[kU];
+#pragma unroll
+    for (int u = 0; u < kU; u++) ph[u] = a.slots[i + u];
+#pragma unroll
+    for (int u = 0; u < kU; u++) {
+      kr[u] = row(a.k_cache, ph[u]);
+      vr[u] = row(a.v_cache, ph[u]);
+    }
+#pragma unroll
+    for (int u = 0; u < kU; u++) step(kr[u], vr[u]);
+  }
+  for (; i < S; i++) {
+    const uint32_t phys = a.slots[i];
+    step(row(a.k_cache, phys), row(a.v_cache, phys));
   }
   const float inv = __fdiv_rn(1.0f, __fadd_rn(l, 1e-9f));
   float *op = a.out + t * qd + (size_t)h * D + lane * EPL;
