@@ -153,6 +153,18 @@ cudaError_t launch_skinny_q4(const uint8_t *tiles, uint32_t row_tiles, uint32_t 
                              uint32_t B, int epi, float *y, uint32_t ldy, uint32_t *xf, float *partial, uint32_t *err,
                              cudaStream_t s);
 cudaError_t launch_lmhead_q8(const float *x, uint32_t ldx, LmHeadArgs a, uint32_t *xf, cudaStream_t s);
+// the tcgen05 variant (skinny_tc.cu): partials only.  launch_skinny_q4 picks it for batches of
+// kSkinnyTcMinTokens or more, where its cost (which does not grow with the batch) is below
+// the mma.sync tiles' (which grows with the token groups)
+constexpr uint32_t kSkinnyTcMinTokens = 17;
+uint32_t skinny_tc_splits(uint32_t row_tiles, uint32_t K);
+size_t skinny_tc_x_bytes(uint32_t K);
+size_t skinny_tc_partial_floats(uint32_t B, uint32_t row_tiles, uint32_t K);
+cudaError_t launch_skinny_q4_tc(const uint8_t *tiles, uint32_t row_tiles, uint32_t K, const float *x, uint32_t ldx,
+                                uint32_t B, uint8_t *xs, float *partial, uint32_t *err, uint32_t *splits,
+                                cudaStream_t s);
+// scratch of launch_skinny_q4 and launch_lmhead_q8 for up to B tokens and K columns
+size_t skinny_x_words(uint32_t B, uint32_t K);
 // greedy (top-1 of the softcapped keys) of each of n rows of V logits
 cudaError_t launch_argmax_rows(const float *logits, uint32_t n, uint32_t V, uint32_t *ids, cudaStream_t s);
 

@@ -351,11 +351,21 @@ static cudaError_t launch_skinny_t(const SkinnyArgs &a, cudaStream_t s) {
 }
 
 // y = W x for B tokens (x row stride ldx, y row stride ldy); xf and partial are scratch of
-// lmhead_frag_words(B, K) words and skinny_partial_floats(B, row_tiles, K) floats
+// skinny_x_words(B, K) words and skinny_partial_floats(B, row_tiles, K) floats
 cudaError_t launch_skinny_q4(const uint8_t *tiles, uint32_t row_tiles, uint32_t K, const float *x, uint32_t ldx,
                              uint32_t B, int epi, float *y, uint32_t ldy, uint32_t *xf, float *partial, uint32_t *err,
                              cudaStream_t s) {
   if (B == 0 || B > 64 || K % 64 || row_tiles == 0) return cudaErrorInvalidValue;
+  const size_t outs = (size_t)B * row_tiles * 16;
+  const unsigned rblocks = (unsigned)std::min<size_t>((outs + 255) / 256, 4096);
+  if (B >= kSkinnyTcMinTokens) {
+    uint32_t splits = 0;
+    cudaError_t e = launch_skinny_q4_tc(tiles, row_tiles, K, x, ldx, B, reinterpret_cast<uint8_t *>(xf), partial, err,
+                                        &splits, s);
+    if (e != cudaSuccess) return e;
+    skinny_reduce_kernel<<<rblocks, 256, 0, s>>>(partial, splits, B, row_tiles, epi, y, ldy);
+    return cudaGetLastError();
+  }
   const uint32_t ngp = lmhead_groups(B), n = K / 32 * ngp * 32;
   lmhead_frag_kernel<<<(n + 255) / 256, 256, 0, s>>>(x, ldx, B, K, ngp, reinterpret_cast<uint4 *>(xf));
   cudaError_t e = cudaGetLastError();
@@ -379,13 +389,19 @@ cudaError_t launch_skinny_q4(const uint8_t *tiles, uint32_t row_tiles, uint32_t 
     default: e = launch_skinny_t<16>(a, s); break;
   }
   if (e != cudaSuccess) return e;
-  const size_t outs = (size_t)B * row_tiles * 16;
-  skinny_reduce_kernel<<<(unsigned)std::min<size_t>((outs + 255) / 256, 4096), 256, 0, s>>>(partial, a.splits, B,
-                                                                                          row_tiles, epi, y, ldy);
+  skinny_reduce_kernel<<<rblocks, 256, 0, s>>>(partial, a.splits, B, row_tiles, epi, y, ldy);
   return cudaGetLastError();
 }
+// enough for any batch up to B (the two variants split K differently)
 size_t skinny_partial_floats(uint32_t B, uint32_t row_tiles, uint32_t K) {
-  return (size_t)skinny_splits(row_tiles, K) * B * row_tiles * 16;
+  size_t p = (size_t)skinny_splits(row_tiles, K) * B * row_tiles * 16;
+  if (B >= kSkinnyTcMinTokens) p = std::max(p, skinny_tc_partial_floats(B, row_tiles, K));
+  return p;
+}
+size_t skinny_x_words(uint32_t B, uint32_t K) {
+  size_t w = lmhead_frag_words(B, K);
+  if (B >= kSkinnyTcMinTokens) w = std::max(w, skinny_tc_x_bytes(K) / 4);
+  return w;
 }
 
 // x: B hidden states (row stride ldx floats); xf scratch: lmhead_frag_words(B, K) words

@@ -1637,7 +1637,7 @@ static int init_streams(ch_model *m, uint32_t n_streams, uint32_t max_batch) {
   CH_TRY(dmalloc(&m->ms_partial, (size_t)max_batch * attn_partial_floats(m->nkv, R, m->D, m->attn_splits)));
   CH_TRY(dmalloc(&m->ms_counters, (size_t)max_batch * m->nkv));
   CH_CUDA(cudaMemset(m->ms_counters, 0, (size_t)max_batch * m->nkv * 4));
-  CH_TRY(dmalloc(&m->ms_xf, lmhead_frag_words(max_batch, std::max({m->H, m->qd, m->I}))));
+  CH_TRY(dmalloc(&m->ms_xf, skinny_x_words(max_batch, std::max({m->H, m->qd, m->I}))));
   {
     const uint32_t qkvd = m->qd + 2 * m->kvd;
     size_t p = skinny_partial_floats(max_batch, qkvd / 16, m->H);
@@ -1941,10 +1941,23 @@ extern "C" int ch_topk64(ch_ctx *c, const float *logits, uint32_t V, uint32_t *i
   CH_CUDA(launch_topk64(t, c->stream, false));
   return CH_OK;
 }
+// 17..64 tokens: the skinny tcgen05 GEMM of the multi-stream decode step (skinny_tc.cu),
+// whose cost does not depend on the token count; scratch: after the prefill GEMM's split-K
+// counters (the first 16 KB, which stay zero), its token blocks, then the split-K partials
+static int batch_gemm_skinny(ch_ctx *c, const void *tiles, uint32_t M, uint32_t K, const float *x, uint32_t n, int epi,
+                             float *y, uint32_t ldy) {
+  const size_t x0 = 16384, xw = (skinny_x_words(n, K) * 4 + 255) & ~(size_t)255;
+  CH_TRY(ctx_ensure_xs(c, x0 + xw + skinny_partial_floats(n, M / 16, K) * sizeof(float)));
+  CH_CUDA(launch_skinny_q4((const uint8_t *)tiles, M / 16, K, x, K, n, epi, y, ldy,
+                           reinterpret_cast<uint32_t *>(c->xs + x0), reinterpret_cast<float *>(c->xs + x0 + xw), c->err,
+                           c->stream));
+  return CH_OK;
+}
 extern "C" int ch_batch_gemm_q4(ch_ctx *c, const void *tiles, uint32_t rows, uint32_t cols, const float *x, uint32_t n,
                                 float *y) {
   if (!c || !tiles || !x || !y || rows % 16 || cols % 64) return fail(CH_EINVAL, "batch_gemm_q4 arguments");
   if (n == 0) return CH_OK;
+  if (n >= kSkinnyTcMinTokens && n <= 64) return batch_gemm_skinny(c, tiles, rows, cols, x, n, EPI_STORE, y, rows);
   CH_TRY(ctx_ensure_xs(c, tc_gemm_scratch_bytes(n, rows, cols)));
   CH_CUDA(launch_batch_gemm_q4_tc(BatchGemmArgs{(const uint8_t *)tiles, rows, cols, n, x, y, EPI_STORE}, c->xs, c->err,
                                   c->stream));
@@ -1954,7 +1967,8 @@ extern "C" int ch_batch_fused_mlp_q4(ch_ctx *c, const void *tiles, uint32_t rows
                                      uint32_t n, float *act) {
   if (!c || !tiles || !x || !act || rows % 8 || cols % 64) return fail(CH_EINVAL, "batch_fused_mlp_q4 arguments");
   if (n == 0) return CH_OK;
-  CH_TRY(ctx_ensure_xs(c, tc_gemm_scratch_bytes(n, 2 * rows, cols)));
+  if (n >= kSkinnyTcMinTokens && n <= 64)
+    return batch_gemm_skinny(c, tiles, 2 * rows, cols, x, n, EPI_GELU_MUL, act, rows);
   CH_CUDA(launch_batch_gemm_q4_tc(BatchGemmArgs{(const uint8_t *)tiles, 2 * rows, cols, n, x, act, EPI_GELU_MUL}, c->xs,
                                   c->err, c->stream));
   return CH_OK;

@@ -2,7 +2,10 @@
 batch_fused_mlp_q4.wgsl) against the oracle, on config 3's shapes, ragged token
 counts (partial 128-token tiles), row counts that are not a multiple of 128 and
 the 12B shapes (those against the oracle on a subset of tokens and against the
-legacy mma.sync kernel on all of them)."""
+legacy mma.sync kernel on all of them).  17 to 64 tokens run the skinny tcgen05
+kernel of the multi-stream decode step (tokens on the MMA's M side, 256 weight rows
+per CTA, split K): those shapes include row counts that are not a multiple of 256
+and K loops of one to sixty k tiles per split."""
 import numpy as np
 import pytest
 import torch
@@ -33,7 +36,7 @@ def _pack_gateup(lib, ctx, Wg, Wu, M, K):
 
 # (N tokens, M rows, K): config 3's QKV / O / down, ragged and small shapes
 GEMM_SHAPES = [(512, 2560, 2048), (512, 2048, 2048), (512, 2048, 8192), (1, 16, 64), (24, 48, 192), (130, 272, 2048),
-               (300, 2560, 128), (1024, 128, 64)]
+               (300, 2560, 128), (1024, 128, 64), (17, 272, 2048), (64, 2560, 2048), (40, 4112, 512), (64, 16, 64)]
 
 
 @pytest.mark.parametrize("N,M,K", GEMM_SHAPES)
@@ -54,7 +57,7 @@ def test_batch_gemm_q4_parity(ctx, oracle, N, M, K):
 
 
 # (N, I, K): config 3's gate|up, ragged and small
-MLP_SHAPES = [(512, 8192, 2048), (24, 8, 64), (130, 40, 192), (200, 1920, 3840)]
+MLP_SHAPES = [(512, 8192, 2048), (24, 8, 64), (130, 40, 192), (200, 1920, 3840), (64, 1920, 3840), (33, 40, 192)]
 
 
 @pytest.mark.parametrize("N,M,K", MLP_SHAPES)
@@ -74,13 +77,15 @@ def test_batch_fused_mlp_q4_parity(ctx, oracle, N, M, K):
     assert ctx.device_status() == 0
 
 
+@pytest.mark.parametrize("N", [512, 64, 17])
 @pytest.mark.parametrize("kind,M,K", [("gemm", 8192, 3840), ("gemm", 3840, 4096), ("gemm", 3840, 15360),
                                       ("mlp", 15360, 3840)])
-def test_12b_shapes_against_mma_path_and_oracle(ctx, oracle, kind, M, K):
-    """512 tokens at the 12B shapes: every output against the mma.sync kernel,
+def test_12b_shapes_against_mma_path_and_oracle(ctx, oracle, kind, M, K, N):
+    """512 tokens (the prefill kernel) and 64 / 17 (the skinny kernel of the
+    multi-stream step) at the 12B shapes: every output against the mma.sync kernel,
     the first 16 tokens against the oracle."""
     lib = L.load()
-    N, NO = 512, 16
+    NO = 16
     X = oracle.gen_f32(N * K, 13).reshape(N, K)
     if kind == "gemm":
         W = oracle.gen_q4(M, K, oracle.tensor_seed(3, 0, 1))
