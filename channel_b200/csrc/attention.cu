@@ -56,6 +56,7 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attn_kernel(const AttnArg
   float *o_s = v_new + D;                 // [warps][R][D]
   float *sc = o_s + kAttnWarps * R * D;   // [R][chunk_cap]
   float *cmb = sc + R * chunk_cap;        // [R][max_splits] combine factors
+  uint32_t *slist = reinterpret_cast<uint32_t *>(cmb + R * max_splits);  // [chunk_cap] this chunk's slots
   __shared__ float stat[2 * kMaxRatio];
   __shared__ uint32_t last_flag;
 
@@ -82,10 +83,13 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attn_kernel(const AttnArg
   const uint32_t c0 = split * chunk, c1 = min(S, c0 + chunk);
   const uint32_t n = c1 > c0 ? c1 - c0 : 0;
 
-  // warm L2 with this CTA's K/V rows while the projections finish
-  for (uint32_t i = c0 + tid; i < c1; i += kAttnThreads) {
-    const uint32_t phys = list[i];
-    if (phys < a.cache_slots) {
+  // stage this chunk's slot list (the row loads below then wait for one round trip, not
+  // two); for a single token also warm L2 with the chunk's K/V rows while the
+  // projections finish -- a batch's rows (hundreds of MB per layer) would not stay there
+  for (uint32_t i = tid; i < n; i += kAttnThreads) {
+    const uint32_t phys = list[c0 + i];
+    slist[i] = phys;
+    if (a.n_tok == 1 && phys < a.cache_slots) {
       const __half *kr = k_cache + (size_t)phys * kv_dim + (size_t)kvh * D;
       const __half *vr = v_cache + (size_t)phys * kv_dim + (size_t)kvh * D;
       asm volatile("prefetch.global.L2 [%0];" ::"l"(kr));
@@ -139,7 +143,7 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attn_kernel(const AttnArg
   constexpr int kU = 4;
   auto fetch = [&](const __half *cache, uint32_t i, uint4 &rw) -> int {
     if (i >= n) return 3;
-    const uint32_t phys = list[c0 + i];
+    const uint32_t phys = slist[i];
     if (phys == sp.slot) return 1;
     if (phys >= a.cache_slots) return 2;
     rw = *reinterpret_cast<const uint4 *>(cache + (size_t)phys * kv_dim + (size_t)kvh * D + lane * EPL);
@@ -302,7 +306,8 @@ template <int R>
 static cudaError_t launch_attn_t(const AttnArgs &a, int splits, cudaStream_t s, bool pdl) {
   const int chunk_cap = (int)std::max<uint32_t>(kMinChunk, (a.cache_slots + splits - 1) / splits);
   const size_t smem = sizeof(float) * ((size_t)(R + 2) * 256 + (size_t)kAttnWarps * R * 256 + (size_t)R * chunk_cap +
-                                       (size_t)R * splits);
+                                       (size_t)R * splits) +
+                      sizeof(uint32_t) * (size_t)chunk_cap;
   static size_t attr_bytes = 0;  // dynamic smem opt-in granted so far
   if (smem > 48 * 1024 && smem > attr_bytes) {
     cudaError_t e = cudaFuncSetAttribute(decode_attn_kernel<R>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);

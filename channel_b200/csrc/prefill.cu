@@ -15,7 +15,83 @@
 namespace ch {
 
 // ---------------------------------------------------------------------------
-// norms: one CTA per row
+// norms: one CTA per row.  Rows of H <= 4 * 4 * 256 floats with H % 4 == 0 take the
+// register path: each thread loads its (up to four) float4 of the row at once and keeps
+// them for the second pass; other rows the strided scalar loop.
+constexpr int kNormThreads = 256, kNormVec = 4;
+__global__ void __launch_bounds__(kNormThreads) rmsnorm_rows_vec_kernel(const float *x, const float *w, float *y,
+                                                                       uint32_t H, float eps) {
+  __shared__ float red[32];
+  const float4 *xr = reinterpret_cast<const float4 *>(x + (size_t)blockIdx.x * H);
+  float4 *yr = reinterpret_cast<float4 *>(y + (size_t)blockIdx.x * H);
+  const float4 *w4 = reinterpret_cast<const float4 *>(w);
+  const uint32_t n4 = H / 4;
+  float4 v[kNormVec];
+#pragma unroll
+  for (int k = 0; k < kNormVec; k++) {
+    const uint32_t j = threadIdx.x + k * kNormThreads;
+    v[k] = j < n4 ? xr[j] : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  float ss = 0.f;
+#pragma unroll
+  for (int k = 0; k < kNormVec; k++) {
+    ss = __fmaf_rn(v[k].x, v[k].x, ss);
+    ss = __fmaf_rn(v[k].y, v[k].y, ss);
+    ss = __fmaf_rn(v[k].z, v[k].z, ss);
+    ss = __fmaf_rn(v[k].w, v[k].w, ss);
+  }
+  ss = block_sum(ss, red);
+  const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)H), eps)));
+#pragma unroll
+  for (int k = 0; k < kNormVec; k++) {
+    const uint32_t j = threadIdx.x + k * kNormThreads;
+    if (j < n4) {
+      const float4 g = w4[j];
+      yr[j] = make_float4(__fmul_rn(__fmul_rn(v[k].x, inv), g.x), __fmul_rn(__fmul_rn(v[k].y, inv), g.y),
+                          __fmul_rn(__fmul_rn(v[k].z, inv), g.z), __fmul_rn(__fmul_rn(v[k].w, inv), g.w));
+    }
+  }
+}
+__global__ void __launch_bounds__(kNormThreads) add_rmsnorm_rows_vec_kernel(float *x, const float *r, const float *w,
+                                                                           float *y, uint32_t H, float eps,
+                                                                           float scalar) {
+  __shared__ float red[32];
+  float4 *xr = reinterpret_cast<float4 *>(x + (size_t)blockIdx.x * H);
+  const float4 *rr = reinterpret_cast<const float4 *>(r + (size_t)blockIdx.x * H);
+  float4 *yr = reinterpret_cast<float4 *>(y + (size_t)blockIdx.x * H);
+  const float4 *w4 = reinterpret_cast<const float4 *>(w);
+  const uint32_t n4 = H / 4;
+  float4 v[kNormVec];
+#pragma unroll
+  for (int k = 0; k < kNormVec; k++) {
+    const uint32_t j = threadIdx.x + k * kNormThreads;
+    float4 a = make_float4(0.f, 0.f, 0.f, 0.f), b = a;
+    if (j < n4) a = xr[j], b = rr[j];
+    v[k] = make_float4(__fmul_rn(__fadd_rn(a.x, b.x), scalar), __fmul_rn(__fadd_rn(a.y, b.y), scalar),
+                       __fmul_rn(__fadd_rn(a.z, b.z), scalar), __fmul_rn(__fadd_rn(a.w, b.w), scalar));
+  }
+  float ss = 0.f;
+#pragma unroll
+  for (int k = 0; k < kNormVec; k++) {
+    const uint32_t j = threadIdx.x + k * kNormThreads;
+    if (j < n4) xr[j] = v[k];
+    ss = __fmaf_rn(v[k].x, v[k].x, ss);
+    ss = __fmaf_rn(v[k].y, v[k].y, ss);
+    ss = __fmaf_rn(v[k].z, v[k].z, ss);
+    ss = __fmaf_rn(v[k].w, v[k].w, ss);
+  }
+  ss = block_sum(ss, red);
+  const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)H), eps)));
+#pragma unroll
+  for (int k = 0; k < kNormVec; k++) {
+    const uint32_t j = threadIdx.x + k * kNormThreads;
+    if (j < n4) {
+      const float4 g = w4[j];
+      yr[j] = make_float4(__fmul_rn(__fmul_rn(v[k].x, inv), g.x), __fmul_rn(__fmul_rn(v[k].y, inv), g.y),
+                          __fmul_rn(__fmul_rn(v[k].z, inv), g.z), __fmul_rn(__fmul_rn(v[k].w, inv), g.w));
+    }
+  }
+}
 __global__ void rmsnorm_rows_kernel(const float *x, const float *w, float *y, uint32_t H, float eps) {
   __shared__ float red[32];
   const float *xr = x + (size_t)blockIdx.x * H;
@@ -45,13 +121,22 @@ __global__ void add_rmsnorm_rows_kernel(float *x, const float *r, const float *w
 cudaError_t launch_rmsnorm_rows(const float *x, const float *w, float *y, uint32_t N, uint32_t H, float eps,
                                 cudaStream_t s) {
   if (N == 0) return cudaSuccess;
-  rmsnorm_rows_kernel<<<N, 256, 0, s>>>(x, w, y, H, eps);
+  const bool vec = H % 4 == 0 && H <= 4u * kNormVec * kNormThreads && !(((uintptr_t)x | (uintptr_t)w | (uintptr_t)y) & 15);
+  if (vec)
+    rmsnorm_rows_vec_kernel<<<N, kNormThreads, 0, s>>>(x, w, y, H, eps);
+  else
+    rmsnorm_rows_kernel<<<N, 256, 0, s>>>(x, w, y, H, eps);
   return cudaGetLastError();
 }
 cudaError_t launch_add_rmsnorm_rows(float *x, const float *r, const float *w, float *y, uint32_t N, uint32_t H,
                                     float eps, float scalar, cudaStream_t s) {
   if (N == 0) return cudaSuccess;
-  add_rmsnorm_rows_kernel<<<N, 256, 0, s>>>(x, r, w, y, H, eps, scalar);
+  const bool vec = H % 4 == 0 && H <= 4u * kNormVec * kNormThreads &&
+                   !(((uintptr_t)x | (uintptr_t)r | (uintptr_t)w | (uintptr_t)y) & 15);
+  if (vec)
+    add_rmsnorm_rows_vec_kernel<<<N, kNormThreads, 0, s>>>(x, r, w, y, H, eps, scalar);
+  else
+    add_rmsnorm_rows_kernel<<<N, 256, 0, s>>>(x, r, w, y, H, eps, scalar);
   return cudaGetLastError();
 }
 __global__ void embed_rows_kernel(const uint16_t *embed, const uint32_t *tokens, uint32_t H, float scale, float *x) {
