@@ -1689,11 +1689,8 @@ extern "C" int ch_streams_decode(ch_model *m, const ch_stream_step *steps, uint3
   if (!m->ms_n) return fail(CH_ESTATE, "ch_streams_init first");
   if (n == 0 || n > m->ms_cap) return fail(CH_EBATCH, "BatchTooLarge: 1..max_batch tokens per step");
   std::vector<uint8_t> seen(m->ms_n, 0);
-  uint32_t max_active = 0, max_sliding = 0;  // longest lists of the step: the attention's split count
   for (uint32_t b = 0; b < n; b++) {
     const ch_stream_step &st = steps[b];
-    max_active = std::max(max_active, st.n_active);
-    max_sliding = std::max(max_sliding, st.n_sliding);
     if (st.stream >= m->ms_n) return fail(CH_EINVAL, "stream index >= the streams initialised");
     if (seen[st.stream]++) return fail(CH_EINVAL, "a stream appears twice in one step");
     if (st.token >= m->V) return fail(CH_EINVAL, "token id >= vocab");
@@ -1764,13 +1761,10 @@ extern "C" int ch_streams_decode(ch_model *m, const ch_stream_step *steps, uint3
     a.err = err;
     a.cache_slots = kSlots;
     a.n_tok = n;
-    // splits per (token, kv head): at least about 8 CTAs per SM over the whole batch (a
-    // single token keeps the model's split count), and chunks of about 128 slots for the
-    // longest stream so that long streams do not trail the short ones (the kernel splits
-    // each stream by its own length; CTAs past a stream's last chunk exit at once)
+    // splits per (token, kv head): about 8 CTAs per SM over the whole batch (64 streams x 8
+    // kv heads need 3; a single token keeps the model's split count)
     const uint32_t want = (8u * (uint32_t)num_sms() + n * m->nkv - 1) / (n * m->nkv);
-    const uint32_t longest = dl.full ? max_active : max_sliding;
-    const int splits = (int)std::max(1u, std::min((uint32_t)m->attn_splits, std::max(want, (longest + 127) / 128)));
+    const int splits = (int)std::max(1u, std::min((uint32_t)m->attn_splits, want));
     CH_CUDA(launch_decode_attn(a, splits, s, false));
     CH_CUDA(launch_skinny_q4(dl.o, m->H / 16, m->qd, m->pA, m->qd, n, EPI_STORE, m->pMO, m->H, m->ms_xf, m->ms_skp,
                              err, s));
