@@ -244,6 +244,7 @@ struct ch_model {
   uint32_t *ms_counters = nullptr; // [ms_cap][n_kv]
   uint32_t *ms_xf = nullptr;       // token fragments of the skinny GEMMs (largest K)
   float *ms_skp = nullptr;         // split-K partials of the skinny Q4 GEMMs
+  std::vector<cudaGraphExec_t> ms_exec;  // the batched step per batch size (index n)
   uint32_t *h_ms_u32 = nullptr;    // pinned: tokens | streams | lists | ids
   StepParams *h_ms_sp = nullptr;
   float2 *h_ms_rope = nullptr;
@@ -1600,6 +1601,9 @@ extern "C" int ch_prefill(ch_model *m, const uint32_t *tokens, uint32_t n, const
 // step for all B streams.  The reference serves one stream (server_queue.zig:9-145,
 // server.zig:259-281); this batching is new.
 static void free_streams(ch_model *m) {
+  for (auto g : m->ms_exec)
+    if (g) cudaGraphExecDestroy(g);
+  m->ms_exec.clear();
   for (auto *p : m->skc) cudaFree(p);
   for (auto *p : m->svc) cudaFree(p);
   m->skc.clear();
@@ -1684,56 +1688,23 @@ extern "C" int ch_stream_prefill(ch_model *m, uint32_t stream, const uint32_t *t
   return CH_OK;
 }
 
-extern "C" int ch_streams_decode(ch_model *m, const ch_stream_step *steps, uint32_t n, uint32_t *tokens_out) {
-  if (!m || !steps || !tokens_out) return fail(CH_EINVAL, "NULL argument");
-  if (!m->ms_n) return fail(CH_ESTATE, "ch_streams_init first");
-  if (n == 0 || n > m->ms_cap) return fail(CH_EBATCH, "BatchTooLarge: 1..max_batch tokens per step");
-  std::vector<uint8_t> seen(m->ms_n, 0);
-  for (uint32_t b = 0; b < n; b++) {
-    const ch_stream_step &st = steps[b];
-    if (st.stream >= m->ms_n) return fail(CH_EINVAL, "stream index >= the streams initialised");
-    if (seen[st.stream]++) return fail(CH_EINVAL, "a stream appears twice in one step");
-    if (st.token >= m->V) return fail(CH_EINVAL, "token id >= vocab");
-    if (st.slot >= kSlots) return fail(CH_EINVAL, "slot >= 4096");
-    CH_TRY(check_lists(st.active, st.n_active));
-    CH_TRY(check_lists(st.sliding, st.n_sliding));
-  }
-  CH_CUDA(cudaSetDevice(m->ctx->device));
-  cudaStream_t s = m->ctx->stream;
+// The device work of one batched step once its inputs are staged: embedding, the layers,
+// the LM head and the argmax -- about 17 launches per layer, captured into a CUDA graph
+// per batch size (their arguments depend only on the batch size and the model).
+#define SK_TRY(x)                         \
+  do {                                    \
+    const cudaError_t e_ = (x);           \
+    if (e_ != cudaSuccess) return e_;     \
+  } while (0)
+static cudaError_t enqueue_streams_step(ch_model *m, uint32_t n, cudaStream_t s) {
   const uint32_t cap = m->ms_cap, rh = m->cfg.rotary_dim / 2, qkvd = m->qd + 2 * m->kvd;
-  uint32_t *h_tok = m->h_ms_u32, *h_str = h_tok + cap, *h_ids = h_str + cap, *h_lists = h_ids + cap;
-  for (uint32_t b = 0; b < n; b++) {
-    const ch_stream_step &st = steps[b];
-    h_tok[b] = st.token;
-    h_str[b] = st.stream;
-    uint32_t *la = h_lists + (size_t)b * 2 * kSlots;
-    if (st.n_active) memcpy(la, st.active, st.n_active * 4);
-    if (st.n_sliding) memcpy(la + kSlots, st.sliding, st.n_sliding * 4);
-    StepParams &sp = m->h_ms_sp[b];
-    sp = StepParams{};
-    sp.clock = st.clock;
-    sp.slot = st.slot;
-    sp.n_active = st.n_active;
-    sp.n_sliding = st.n_sliding;
-    sp.active = m->ms_lists + (size_t)b * 2 * kSlots;
-    sp.sliding = m->ms_lists + (size_t)b * 2 * kSlots + kSlots;
-    rope_table(m->h_inv_s, st.clock, m->h_ms_rope + (size_t)b * rh);
-    rope_table(m->h_inv_f, st.clock, m->h_ms_rope + ((size_t)cap + b) * rh);
-  }
-  CH_CUDA(cudaMemcpyAsync(m->ms_tok, h_tok, n * 4, cudaMemcpyHostToDevice, s));
-  CH_CUDA(cudaMemcpyAsync(m->ms_stream, h_str, n * 4, cudaMemcpyHostToDevice, s));
-  CH_CUDA(cudaMemcpyAsync(m->ms_lists, h_lists, (size_t)n * 2 * kSlots * 4, cudaMemcpyHostToDevice, s));
-  CH_CUDA(cudaMemcpyAsync(m->ms_sp, m->h_ms_sp, n * sizeof(StepParams), cudaMemcpyHostToDevice, s));
-  CH_CUDA(cudaMemcpyAsync(m->ms_rope, m->h_ms_rope, (size_t)n * rh * sizeof(float2), cudaMemcpyHostToDevice, s));
-  CH_CUDA(cudaMemcpyAsync(m->ms_rope + (size_t)cap * rh, m->h_ms_rope + (size_t)cap * rh, (size_t)n * rh * sizeof(float2),
-                          cudaMemcpyHostToDevice, s));
-  CH_CUDA(launch_embed_rows(m->embed, m->ms_tok, n, m->H, sqrtf((float)m->H), m->pX, s));
+  SK_TRY(launch_embed_rows(m->embed, m->ms_tok, n, m->H, sqrtf((float)m->H), m->pX, s));
   const float eps = m->cfg.rms_norm_eps;
   uint32_t *err = m->ctx->err;
   for (uint32_t l = 0; l < m->L; l++) {
     DevLayer &dl = m->layers[l];
-    if (l == 0) CH_CUDA(launch_rmsnorm_rows(m->pX, dl.input_norm, m->pNX, n, m->H, eps, s));
-    CH_CUDA(launch_skinny_q4(dl.qkv, qkvd / 16, m->H, m->pNX, m->H, n, EPI_STORE, m->pQKV, qkvd, m->ms_xf, m->ms_skp,
+    if (l == 0) SK_TRY(launch_rmsnorm_rows(m->pX, dl.input_norm, m->pNX, n, m->H, eps, s));
+    SK_TRY(launch_skinny_q4(dl.qkv, qkvd / 16, m->H, m->pNX, m->H, n, EPI_STORE, m->pQKV, qkvd, m->ms_xf, m->ms_skp,
                              err, s));
     AttnArgs a{};
     a.qkv = m->pQKV;
@@ -1765,18 +1736,18 @@ extern "C" int ch_streams_decode(ch_model *m, const ch_stream_step *steps, uint3
     // kv heads need 3; a single token keeps the model's split count)
     const uint32_t want = (8u * (uint32_t)num_sms() + n * m->nkv - 1) / (n * m->nkv);
     const int splits = (int)std::max(1u, std::min((uint32_t)m->attn_splits, want));
-    CH_CUDA(launch_decode_attn(a, splits, s, false));
-    CH_CUDA(launch_skinny_q4(dl.o, m->H / 16, m->qd, m->pA, m->qd, n, EPI_STORE, m->pMO, m->H, m->ms_xf, m->ms_skp,
+    SK_TRY(launch_decode_attn(a, splits, s, false));
+    SK_TRY(launch_skinny_q4(dl.o, m->H / 16, m->qd, m->pA, m->qd, n, EPI_STORE, m->pMO, m->H, m->ms_xf, m->ms_skp,
                              err, s));
-    if (dl.post_attn) CH_CUDA(launch_rmsnorm_rows(m->pMO, dl.post_attn, m->pMO, n, m->H, eps, s));
-    CH_CUDA(launch_add_rmsnorm_rows(m->pX, m->pMO, dl.pre_ffn, m->pNX, n, m->H, eps, 1.0f, s));
-    CH_CUDA(launch_skinny_q4(dl.gateup, 2 * m->I / 16, m->H, m->pNX, m->H, n, EPI_GELU_MUL, m->pACT, m->I, m->ms_xf,
+    if (dl.post_attn) SK_TRY(launch_rmsnorm_rows(m->pMO, dl.post_attn, m->pMO, n, m->H, eps, s));
+    SK_TRY(launch_add_rmsnorm_rows(m->pX, m->pMO, dl.pre_ffn, m->pNX, n, m->H, eps, 1.0f, s));
+    SK_TRY(launch_skinny_q4(dl.gateup, 2 * m->I / 16, m->H, m->pNX, m->H, n, EPI_GELU_MUL, m->pACT, m->I, m->ms_xf,
                              m->ms_skp, err, s));
-    CH_CUDA(launch_skinny_q4(dl.down, m->H / 16, m->I, m->pACT, m->I, n, EPI_STORE, m->pMO, m->H, m->ms_xf,
+    SK_TRY(launch_skinny_q4(dl.down, m->H / 16, m->I, m->pACT, m->I, n, EPI_STORE, m->pMO, m->H, m->ms_xf,
                              m->ms_skp, err, s));
-    if (dl.post_ffn) CH_CUDA(launch_rmsnorm_rows(m->pMO, dl.post_ffn, m->pMO, n, m->H, eps, s));
+    if (dl.post_ffn) SK_TRY(launch_rmsnorm_rows(m->pMO, dl.post_ffn, m->pMO, n, m->H, eps, s));
     const float *next = (l + 1 < m->L) ? m->layers[l + 1].input_norm : m->final_norm;
-    CH_CUDA(launch_add_rmsnorm_rows(m->pX, m->pMO, next, m->pNX, n, m->H, eps, dl.scalar, s));
+    SK_TRY(launch_add_rmsnorm_rows(m->pX, m->pMO, next, m->pNX, n, m->H, eps, dl.scalar, s));
   }
   {  // Q8 LM head of every token's final-normed state, the head read once for the batch
     LmHeadArgs h{};
@@ -1787,9 +1758,72 @@ extern "C" int ch_streams_decode(ch_model *m, const ch_stream_step *steps, uint3
     h.B = n;
     h.logits = m->ms_logits;
     h.err = err;
-    CH_CUDA(launch_lmhead_q8(m->pNX, m->H, h, m->ms_xf, s));
+    SK_TRY(launch_lmhead_q8(m->pNX, m->H, h, m->ms_xf, s));
   }
-  CH_CUDA(launch_argmax_rows(m->ms_logits, n, m->V, m->ms_ids, s));
+  SK_TRY(launch_argmax_rows(m->ms_logits, n, m->V, m->ms_ids, s));
+  return cudaSuccess;
+}
+#undef SK_TRY
+
+extern "C" int ch_streams_decode(ch_model *m, const ch_stream_step *steps, uint32_t n, uint32_t *tokens_out) {
+  if (!m || !steps || !tokens_out) return fail(CH_EINVAL, "NULL argument");
+  if (!m->ms_n) return fail(CH_ESTATE, "ch_streams_init first");
+  if (n == 0 || n > m->ms_cap) return fail(CH_EBATCH, "BatchTooLarge: 1..max_batch tokens per step");
+  std::vector<uint8_t> seen(m->ms_n, 0);
+  for (uint32_t b = 0; b < n; b++) {
+    const ch_stream_step &st = steps[b];
+    if (st.stream >= m->ms_n) return fail(CH_EINVAL, "stream index >= the streams initialised");
+    if (seen[st.stream]++) return fail(CH_EINVAL, "a stream appears twice in one step");
+    if (st.token >= m->V) return fail(CH_EINVAL, "token id >= vocab");
+    if (st.slot >= kSlots) return fail(CH_EINVAL, "slot >= 4096");
+    CH_TRY(check_lists(st.active, st.n_active));
+    CH_TRY(check_lists(st.sliding, st.n_sliding));
+  }
+  CH_CUDA(cudaSetDevice(m->ctx->device));
+  cudaStream_t s = m->ctx->stream;
+  const uint32_t cap = m->ms_cap, rh = m->cfg.rotary_dim / 2;
+  uint32_t *h_tok = m->h_ms_u32, *h_str = h_tok + cap, *h_ids = h_str + cap, *h_lists = h_ids + cap;
+  for (uint32_t b = 0; b < n; b++) {
+    const ch_stream_step &st = steps[b];
+    h_tok[b] = st.token;
+    h_str[b] = st.stream;
+    uint32_t *la = h_lists + (size_t)b * 2 * kSlots;
+    if (st.n_active) memcpy(la, st.active, st.n_active * 4);
+    if (st.n_sliding) memcpy(la + kSlots, st.sliding, st.n_sliding * 4);
+    StepParams &sp = m->h_ms_sp[b];
+    sp = StepParams{};
+    sp.clock = st.clock;
+    sp.slot = st.slot;
+    sp.n_active = st.n_active;
+    sp.n_sliding = st.n_sliding;
+    sp.active = m->ms_lists + (size_t)b * 2 * kSlots;
+    sp.sliding = m->ms_lists + (size_t)b * 2 * kSlots + kSlots;
+    rope_table(m->h_inv_s, st.clock, m->h_ms_rope + (size_t)b * rh);
+    rope_table(m->h_inv_f, st.clock, m->h_ms_rope + ((size_t)cap + b) * rh);
+  }
+  CH_CUDA(cudaMemcpyAsync(m->ms_tok, h_tok, n * 4, cudaMemcpyHostToDevice, s));
+  CH_CUDA(cudaMemcpyAsync(m->ms_stream, h_str, n * 4, cudaMemcpyHostToDevice, s));
+  CH_CUDA(cudaMemcpyAsync(m->ms_lists, h_lists, (size_t)n * 2 * kSlots * 4, cudaMemcpyHostToDevice, s));
+  CH_CUDA(cudaMemcpyAsync(m->ms_sp, m->h_ms_sp, n * sizeof(StepParams), cudaMemcpyHostToDevice, s));
+  CH_CUDA(cudaMemcpyAsync(m->ms_rope, m->h_ms_rope, (size_t)n * rh * sizeof(float2), cudaMemcpyHostToDevice, s));
+  CH_CUDA(cudaMemcpyAsync(m->ms_rope + (size_t)cap * rh, m->h_ms_rope + (size_t)cap * rh, (size_t)n * rh * sizeof(float2),
+                          cudaMemcpyHostToDevice, s));
+  if (m->ms_exec.size() <= n) m->ms_exec.resize(n + 1, nullptr);
+  if (!m->ms_exec[n]) {
+    cudaGraph_t g = nullptr;
+    CH_CUDA(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
+    cudaError_t e = enqueue_streams_step(m, n, s);
+    const cudaError_t e2 = cudaStreamEndCapture(s, &g);
+    if (e == cudaSuccess) e = e2;
+    if (e == cudaSuccess) e = cudaGraphInstantiate(&m->ms_exec[n], g, 0);
+    if (g) cudaGraphDestroy(g);
+    if (e != cudaSuccess) {
+      m->ms_exec[n] = nullptr;
+      cudaGetLastError();
+      return fail(CH_ECUDA, std::string("streams step capture: ") + cudaGetErrorString(e));
+    }
+  }
+  CH_CUDA(cudaGraphLaunch(m->ms_exec[n], s));
   CH_CUDA(cudaMemcpyAsync(h_ids, m->ms_ids, n * 4, cudaMemcpyDeviceToHost, s));
   CH_CUDA(cudaStreamSynchronize(s));
   memcpy(tokens_out, h_ids, n * 4);
