@@ -209,49 +209,68 @@ cudaError_t launch_batch_qkv_rope(const BatchQkvRopeArgs &a, cudaStream_t s) {
 }
 
 // ---------------------------------------------------------------------------
-// batch causal attention: one warp per (q head, token), online softmax over the
-// gathered slots (K/V rows shared through L1/L2 by the 8 tokens of a CTA).
-__global__ void __launch_bounds__(256) batch_causal_attn_kernel(const BatchAttnArgs a) {
+// batch causal attention: one warp per (token, pair of q heads of one kv head) -- one warp
+// per (q head, token) when the group size is odd -- online softmax over the gathered
+// slots (K/V rows shared through L1/L2 by the 8 tokens of a CTA, and by the two heads
+// within the warp).
+template <int HW>  // q heads per warp: HW heads of one kv head share every K/V row load
+__global__ void __launch_bounds__(256, 3) batch_causal_attn_kernel(const BatchAttnArgs a) {
   constexpr int D = 256, EPL = 8;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const uint32_t h = blockIdx.y;
+  const uint32_t h0 = blockIdx.y * HW;
   const uint32_t t = blockIdx.x * 8 + warp;
   if (t >= a.N) return;
-  const uint32_t ratio = a.nq / a.nkv, kvh = h / ratio;
+  const uint32_t ratio = a.nq / a.nkv, kvh = h0 / ratio;  // HW divides ratio: one kv head for all HW
   const size_t qd = (size_t)a.nq * D, kvd = (size_t)a.nkv * D;
-  const float *qp = a.q + t * qd + (size_t)h * D + lane * EPL;
-  float q[EPL];
+  float q[HW][EPL];
 #pragma unroll
-  for (int e = 0; e < EPL; e++) q[e] = qp[e];
+  for (int hh = 0; hh < HW; hh++) {
+    const float *qp = a.q + t * qd + (size_t)(h0 + hh) * D + lane * EPL;
+#pragma unroll
+    for (int e = 0; e < EPL; e++) q[hh][e] = qp[e];
+  }
   const uint32_t S = a.num_prev + t + 1;
   const uint32_t start = (a.is_sliding && S > 1024) ? S - 1024 : 0;
-  float m = -1e9f, l = 0.f, acc[EPL];
+  float m[HW], l[HW], acc[HW][EPL];
 #pragma unroll
-  for (int e = 0; e < EPL; e++) acc[e] = 0.f;
-  // online softmax in slot order; the rows of four slots are loaded before any is used
-  // (one slot at a time left the warp waiting a memory round trip per slot)
+  for (int hh = 0; hh < HW; hh++) {
+    m[hh] = -1e9f;
+    l[hh] = 0.f;
+#pragma unroll
+    for (int e = 0; e < EPL; e++) acc[hh][e] = 0.f;
+  }
+  // online softmax in slot order, per head the same operations as one head per warp; the
+  // rows of four slots are loaded before any is used (one slot at a time left the warp
+  // waiting a memory round trip per slot)
   auto step = [&](const uint4 &kr, const uint4 &vr) {
     const __half2 *kh = reinterpret_cast<const __half2 *>(&kr);
     const __half2 *vh = reinterpret_cast<const __half2 *>(&vr);
-    float dot = 0.f;
+    float kf[EPL], vf[EPL];
 #pragma unroll
     for (int e = 0; e < EPL / 2; e++) {
-      const float2 f = __half22float2(kh[e]);
-      dot = __fmaf_rn(q[2 * e], f.x, dot);
-      dot = __fmaf_rn(q[2 * e + 1], f.y, dot);
+      const float2 fk = __half22float2(kh[e]), fv = __half22float2(vh[e]);
+      kf[2 * e] = fk.x, kf[2 * e + 1] = fk.y, vf[2 * e] = fv.x, vf[2 * e + 1] = fv.y;
     }
-    dot = __fmul_rn(warp_sum(dot), a.scale);
-    const float mn = fmaxf(m, dot);
-    const float corr = expf(__fsub_rn(m, mn));
-    const float p = expf(__fsub_rn(dot, mn));
-    l = __fmaf_rn(l, corr, p);
+    float dot[HW];
 #pragma unroll
-    for (int e = 0; e < EPL / 2; e++) {
-      const float2 f = __half22float2(vh[e]);
-      acc[2 * e] = __fmaf_rn(acc[2 * e], corr, __fmul_rn(p, f.x));
-      acc[2 * e + 1] = __fmaf_rn(acc[2 * e + 1], corr, __fmul_rn(p, f.y));
+    for (int hh = 0; hh < HW; hh++) {
+      float d = 0.f;
+#pragma unroll
+      for (int e = 0; e < EPL; e++) d = __fmaf_rn(q[hh][e], kf[e], d);
+      dot[hh] = d;
     }
-    m = mn;
+#pragma unroll
+    for (int hh = 0; hh < HW; hh++) dot[hh] = __fmul_rn(warp_sum(dot[hh]), a.scale);
+#pragma unroll
+    for (int hh = 0; hh < HW; hh++) {
+      const float mn = fmaxf(m[hh], dot[hh]);
+      const float corr = expf(__fsub_rn(m[hh], mn));
+      const float p = expf(__fsub_rn(dot[hh], mn));
+      l[hh] = __fmaf_rn(l[hh], corr, p);
+#pragma unroll
+      for (int e = 0; e < EPL; e++) acc[hh][e] = __fmaf_rn(acc[hh][e], corr, __fmul_rn(p, vf[e]));
+      m[hh] = mn;
+    }
   };
   auto row = [&](const __half *cache, uint32_t phys) {
     return *reinterpret_cast<const uint4 *>(cache + (size_t)phys * kvd + (size_t)kvh * D + lane * EPL);
@@ -275,15 +294,22 @@ __global__ void __launch_bounds__(256) batch_causal_attn_kernel(const BatchAttnA
     const uint32_t phys = a.slots[i];
     step(row(a.k_cache, phys), row(a.v_cache, phys));
   }
-  const float inv = __fdiv_rn(1.0f, __fadd_rn(l, 1e-9f));
-  float *op = a.out + t * qd + (size_t)h * D + lane * EPL;
 #pragma unroll
-  for (int e = 0; e < EPL; e++) op[e] = __fmul_rn(acc[e], inv);
+  for (int hh = 0; hh < HW; hh++) {
+    const float inv = __fdiv_rn(1.0f, __fadd_rn(l[hh], 1e-9f));
+    float *op = a.out + t * qd + (size_t)(h0 + hh) * D + lane * EPL;
+#pragma unroll
+    for (int e = 0; e < EPL; e++) op[e] = __fmul_rn(acc[hh][e], inv);
+  }
 }
 cudaError_t launch_batch_causal_attn(const BatchAttnArgs &a, cudaStream_t s) {
   if (a.D != 256 || a.N == 0) return a.N == 0 ? cudaSuccess : cudaErrorInvalidValue;
-  dim3 grid((a.N + 7) / 8, a.nq);
-  batch_causal_attn_kernel<<<grid, 256, 0, s>>>(a);
+  if (a.nkv == 0 || a.nq % a.nkv) return cudaErrorInvalidValue;
+  if ((a.nq / a.nkv) % 2 == 0) {  // pairs of q heads of one kv head per warp
+    batch_causal_attn_kernel<2><<<dim3((a.N + 7) / 8, a.nq / 2), 256, 0, s>>>(a);
+  } else {
+    batch_causal_attn_kernel<1><<<dim3((a.N + 7) / 8, a.nq), 256, 0, s>>>(a);
+  }
   return cudaGetLastError();
 }
 
