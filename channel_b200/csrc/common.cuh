@@ -122,6 +122,11 @@ CH_DEV void cp_async16(void *dst, const void *src) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
 }
 CH_DEV void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+CH_DEV void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+CH_DEV void cp_async_wait_group() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
 
 // programmatic dependent launch
 CH_DEV void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }

@@ -213,24 +213,33 @@ cudaError_t launch_batch_qkv_rope(const BatchQkvRopeArgs &a, cudaStream_t s) {
 // per (q head, token) when the group size is odd -- online softmax over the gathered
 // slots (K/V rows shared through L1/L2 by the 8 tokens of a CTA, and by the two heads
 // within the warp).
-template <int HW>  // q heads per warp: HW heads of one kv head share every K/V row load
+constexpr int kCaBlk = 32;  // slots per staged block
+constexpr size_t kCaSmem = 2 * 2 * kCaBlk * 32 * sizeof(uint4);  // [2 buffers][K, V][32 slots][512 B]
+
+template <int HW>  // q heads per warp: HW heads of one kv head share every K/V row
 __global__ void __launch_bounds__(256, 3) batch_causal_attn_kernel(const BatchAttnArgs a) {
   constexpr int D = 256, EPL = 8;
+  extern __shared__ uint4 kv_s[];  // [buf][0 K, 1 V][slot][lane]
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const uint32_t h0 = blockIdx.y * HW;
-  const uint32_t t = blockIdx.x * 8 + warp;
-  if (t >= a.N) return;
+  // the last tokens attend to the most slots: their CTAs are issued first
+  const uint32_t tb = (gridDim.x - 1 - blockIdx.x) * 8;  // this CTA's first token (< N)
+  const uint32_t t = tb + warp;
+  const bool live = t < a.N;
   const uint32_t ratio = a.nq / a.nkv, kvh = h0 / ratio;  // HW divides ratio: one kv head for all HW
   const size_t qd = (size_t)a.nq * D, kvd = (size_t)a.nkv * D;
   float q[HW][EPL];
 #pragma unroll
   for (int hh = 0; hh < HW; hh++) {
-    const float *qp = a.q + t * qd + (size_t)(h0 + hh) * D + lane * EPL;
+    const float *qp = a.q + (size_t)min(t, a.N - 1) * qd + (size_t)(h0 + hh) * D + lane * EPL;
 #pragma unroll
     for (int e = 0; e < EPL; e++) q[hh][e] = qp[e];
   }
-  const uint32_t S = a.num_prev + t + 1;
-  const uint32_t start = (a.is_sliding && S > 1024) ? S - 1024 : 0;
+  auto first_slot = [&](uint32_t S) { return (a.is_sliding && S > 1024) ? S - 1024 : 0u; };
+  const uint32_t S = a.num_prev + t + 1, start = first_slot(S);
+  // the CTA's slots: from its first token's window start to its last token
+  const uint32_t u0 = first_slot(a.num_prev + tb + 1), u1 = a.num_prev + min(tb + 7, a.N - 1) + 1;
+  const uint32_t nblk = (u1 - u0 + kCaBlk - 1) / kCaBlk;
   float m[HW], l[HW], acc[HW][EPL];
 #pragma unroll
   for (int hh = 0; hh < HW; hh++) {
@@ -239,9 +248,7 @@ __global__ void __launch_bounds__(256, 3) batch_causal_attn_kernel(const BatchAt
 #pragma unroll
     for (int e = 0; e < EPL; e++) acc[hh][e] = 0.f;
   }
-  // online softmax in slot order, per head the same operations as one head per warp; the
-  // rows of four slots are loaded before any is used (one slot at a time left the warp
-  // waiting a memory round trip per slot)
+  // online softmax in slot order, per head the same operations as one head per warp
   auto step = [&](const uint4 &kr, const uint4 &vr) {
     const __half2 *kh = reinterpret_cast<const __half2 *>(&kr);
     const __half2 *vh = reinterpret_cast<const __half2 *>(&vr);
@@ -263,37 +270,65 @@ __global__ void __launch_bounds__(256, 3) batch_causal_attn_kernel(const BatchAt
     for (int hh = 0; hh < HW; hh++) dot[hh] = __fmul_rn(warp_sum(dot[hh]), a.scale);
 #pragma unroll
     for (int hh = 0; hh < HW; hh++) {
-      const float mn = fmaxf(m[hh], dot[hh]);
-      const float corr = expf(__fsub_rn(m[hh], mn));
-      const float p = expf(__fsub_rn(dot[hh], mn));
-      l[hh] = __fmaf_rn(l[hh], corr, p);
+      // dot is the same in every lane (warp_sum), so the branch is uniform.  A slot that
+      // does not raise the max has corr = expf(+0) = 1 exactly, and fma(x, 1, y) is x + y
+      // rounded once: the short path gives the same bits without the second expf.
+      if (dot[hh] <= m[hh]) {
+        const float p = expf(__fsub_rn(dot[hh], m[hh]));
+        l[hh] = __fadd_rn(l[hh], p);
 #pragma unroll
-      for (int e = 0; e < EPL; e++) acc[hh][e] = __fmaf_rn(acc[hh][e], corr, __fmul_rn(p, vf[e]));
-      m[hh] = mn;
+        for (int e = 0; e < EPL; e++) acc[hh][e] = __fadd_rn(acc[hh][e], __fmul_rn(p, vf[e]));
+      } else {
+        const float mn = dot[hh];
+        const float corr = expf(__fsub_rn(m[hh], mn));
+        const float p = expf(__fsub_rn(dot[hh], mn));
+        l[hh] = __fmaf_rn(l[hh], corr, p);
+#pragma unroll
+        for (int e = 0; e < EPL; e++) acc[hh][e] = __fmaf_rn(acc[hh][e], corr, __fmul_rn(p, vf[e]));
+        m[hh] = mn;
+      }
     }
   };
-  auto row = [&](const __half *cache, uint32_t phys) {
-    return *reinterpret_cast<const uint4 *>(cache + (size_t)phys * kvd + (size_t)kvh * D + lane * EPL);
-  };
-  constexpr int kU = 4;
-  uint32_t i = start;
-  for (; i + kU <= S; i += kU) {
-    uint32_t ph[kU];
-    uint4 kr[kU], vr[kU];
+  // blocks of 32 slots' K and V rows (32 KB) staged by the whole CTA with cp.async, two
+  // buffers: the copy of block b + 1 runs while the warps consume block b.  Thread
+  // tid copies 64 bytes of the K and of the V row of slot tid / 8.
+  auto stage = [&](uint32_t blk, int buf) {
+    const uint32_t j = threadIdx.x >> 3, part = (threadIdx.x & 7) * 4;
+    const uint32_t i = u0 + blk * kCaBlk + j;
+    if (i < u1) {
+      const size_t off = (size_t)a.slots[i] * kvd + (size_t)kvh * D;
+      const uint4 *kg = reinterpret_cast<const uint4 *>(a.k_cache + off) + part;
+      const uint4 *vg = reinterpret_cast<const uint4 *>(a.v_cache + off) + part;
+      uint4 *kd = kv_s + ((size_t)(buf * 2) * kCaBlk + j) * 32 + part;
+      uint4 *vd = kv_s + ((size_t)(buf * 2 + 1) * kCaBlk + j) * 32 + part;
 #pragma unroll
-    for (int u = 0; u < kU; u++) ph[u] = a.slots[i + u];
-#pragma unroll
-    for (int u = 0; u < kU; u++) {
-      kr[u] = row(a.k_cache, ph[u]);
-      vr[u] = row(a.v_cache, ph[u]);
+      for (int c = 0; c < 4; c++) {
+        cp_async16(kd + c, kg + c);
+        cp_async16(vd + c, vg + c);
+      }
     }
-#pragma unroll
-    for (int u = 0; u < kU; u++) step(kr[u], vr[u]);
+    cp_async_commit();  // one group per block in every thread (empty past the last slot)
+  };
+  stage(0, 0);
+  for (uint32_t blk = 0; blk < nblk; blk++) {
+    if (blk + 1 < nblk)
+      stage(blk + 1, (blk + 1) & 1);
+    else
+      cp_async_commit();
+    cp_async_wait_group<1>();  // this thread's copies of block blk have landed
+    __syncthreads();           // ... and everyone's
+    const int buf = blk & 1;
+    const uint32_t i0 = u0 + blk * kCaBlk;
+    if (live) {
+      const uint32_t lo = max(i0, start), hi = min(i0 + kCaBlk, S);
+      for (uint32_t i = lo; i < hi; i++) {
+        const uint32_t j = i - i0;
+        step(kv_s[((size_t)(buf * 2) * kCaBlk + j) * 32 + lane], kv_s[((size_t)(buf * 2 + 1) * kCaBlk + j) * 32 + lane]);
+      }
+    }
+    __syncthreads();  // block blk consumed before its buffer takes block blk + 2
   }
-  for (; i < S; i++) {
-    const uint32_t phys = a.slots[i];
-    step(row(a.k_cache, phys), row(a.v_cache, phys));
-  }
+  if (!live) return;
 #pragma unroll
   for (int hh = 0; hh < HW; hh++) {
     const float inv = __fdiv_rn(1.0f, __fadd_rn(l[hh], 1e-9f));
@@ -305,10 +340,17 @@ __global__ void __launch_bounds__(256, 3) batch_causal_attn_kernel(const BatchAt
 cudaError_t launch_batch_causal_attn(const BatchAttnArgs &a, cudaStream_t s) {
   if (a.D != 256 || a.N == 0) return a.N == 0 ? cudaSuccess : cudaErrorInvalidValue;
   if (a.nkv == 0 || a.nq % a.nkv) return cudaErrorInvalidValue;
+  const dim3 blocks((a.N + 7) / 8, 1);
   if ((a.nq / a.nkv) % 2 == 0) {  // pairs of q heads of one kv head per warp
-    batch_causal_attn_kernel<2><<<dim3((a.N + 7) / 8, a.nq / 2), 256, 0, s>>>(a);
+    cudaError_t e = cudaFuncSetAttribute(batch_causal_attn_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)kCaSmem);
+    if (e != cudaSuccess) return e;
+    batch_causal_attn_kernel<2><<<dim3(blocks.x, a.nq / 2), 256, kCaSmem, s>>>(a);
   } else {
-    batch_causal_attn_kernel<1><<<dim3((a.N + 7) / 8, a.nq), 256, 0, s>>>(a);
+    cudaError_t e = cudaFuncSetAttribute(batch_causal_attn_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)kCaSmem);
+    if (e != cudaSuccess) return e;
+    batch_causal_attn_kernel<1><<<dim3(blocks.x, a.nq), 256, kCaSmem, s>>>(a);
   }
   return cudaGetLastError();
 }
