@@ -149,9 +149,10 @@ struct SkinnyArgs {
 };
 uint32_t skinny_splits(uint32_t row_tiles, uint32_t K);
 size_t skinny_partial_floats(uint32_t B, uint32_t row_tiles, uint32_t K);
+// x_ready (B >= kSkinnyTcMinTokens only): xf already holds x's blocks (skinny_tail_kernel)
 cudaError_t launch_skinny_q4(const uint8_t *tiles, uint32_t row_tiles, uint32_t K, const float *x, uint32_t ldx,
                              uint32_t B, int epi, float *y, uint32_t ldy, uint32_t *xf, float *partial, uint32_t *err,
-                             cudaStream_t s);
+                             cudaStream_t s, bool x_ready = false);
 cudaError_t launch_lmhead_q8(const float *x, uint32_t ldx, LmHeadArgs a, uint32_t *xf, cudaStream_t s);
 // the tcgen05 variant (skinny_tc.cu): partials only.  launch_skinny_q4 picks it for batches of
 // kSkinnyTcMinTokens or more, where its cost (which does not grow with the batch) is below
@@ -162,7 +163,12 @@ size_t skinny_tc_x_bytes(uint32_t K);
 size_t skinny_tc_partial_floats(uint32_t B, uint32_t row_tiles, uint32_t K);
 cudaError_t launch_skinny_q4_tc(const uint8_t *tiles, uint32_t row_tiles, uint32_t K, const float *x, uint32_t ldx,
                                 uint32_t B, uint8_t *xs, float *partial, uint32_t *err, uint32_t *splits,
-                                cudaStream_t s);
+                                cudaStream_t s, bool x_ready = false);
+// split sum + (post norm) + residual add + norm + the next GEMM's activation blocks, one
+// token row per CTA (skinny_tc.cu); the batched step's o and down epilogues for 17-64 tokens
+cudaError_t launch_skinny_tail(const float *partial, uint32_t splits, uint32_t B, uint32_t H, const float *post_w,
+                               float *x, const float *next_w, float *y, float eps, float scalar, uint8_t *xs,
+                               cudaStream_t s);
 // scratch of launch_skinny_q4 and launch_lmhead_q8 for up to B tokens and K columns
 size_t skinny_x_words(uint32_t B, uint32_t K);
 // greedy (top-1 of the softcapped keys) of each of n rows of V logits

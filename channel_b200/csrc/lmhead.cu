@@ -354,14 +354,15 @@ static cudaError_t launch_skinny_t(const SkinnyArgs &a, cudaStream_t s) {
 // skinny_x_words(B, K) words and skinny_partial_floats(B, row_tiles, K) floats
 cudaError_t launch_skinny_q4(const uint8_t *tiles, uint32_t row_tiles, uint32_t K, const float *x, uint32_t ldx,
                              uint32_t B, int epi, float *y, uint32_t ldy, uint32_t *xf, float *partial, uint32_t *err,
-                             cudaStream_t s) {
+                             cudaStream_t s, bool x_ready) {
   if (B == 0 || B > 64 || K % 64 || row_tiles == 0) return cudaErrorInvalidValue;
+  if (x_ready && B < kSkinnyTcMinTokens) return cudaErrorInvalidValue;  // only the tcgen05 blocks are prepared
   const size_t outs = (size_t)B * row_tiles * 16;
   const unsigned rblocks = (unsigned)std::min<size_t>((outs + 255) / 256, 4096);
   if (B >= kSkinnyTcMinTokens) {
     uint32_t splits = 0;
     cudaError_t e = launch_skinny_q4_tc(tiles, row_tiles, K, x, ldx, B, reinterpret_cast<uint8_t *>(xf), partial, err,
-                                        &splits, s);
+                                        &splits, s, x_ready);
     if (e != cudaSuccess) return e;
     skinny_reduce_kernel<<<rblocks, 256, 0, s>>>(partial, splits, B, row_tiles, epi, y, ldy);
     return cudaGetLastError();

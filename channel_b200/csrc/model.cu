@@ -1701,11 +1701,13 @@ static cudaError_t enqueue_streams_step(ch_model *m, uint32_t n, cudaStream_t s)
   SK_TRY(launch_embed_rows(m->embed, m->ms_tok, n, m->H, sqrtf((float)m->H), m->pX, s));
   const float eps = m->cfg.rms_norm_eps;
   uint32_t *err = m->ctx->err;
+  // 17-64 tokens (the tcgen05 skinny GEMMs): the o and down epilogues run fused
+  const bool fuse = n >= kSkinnyTcMinTokens && m->H % 64 == 0 && m->H <= 4096;
   for (uint32_t l = 0; l < m->L; l++) {
     DevLayer &dl = m->layers[l];
     if (l == 0) SK_TRY(launch_rmsnorm_rows(m->pX, dl.input_norm, m->pNX, n, m->H, eps, s));
     SK_TRY(launch_skinny_q4(dl.qkv, qkvd / 16, m->H, m->pNX, m->H, n, EPI_STORE, m->pQKV, qkvd, m->ms_xf, m->ms_skp,
-                             err, s));
+                            err, s, fuse && l > 0));
     AttnArgs a{};
     a.qkv = m->pQKV;
     a.qkv_stride = qkvd;
@@ -1737,6 +1739,21 @@ static cudaError_t enqueue_streams_step(ch_model *m, uint32_t n, cudaStream_t s)
     const uint32_t want = (8u * (uint32_t)num_sms() + n * m->nkv - 1) / (n * m->nkv);
     const int splits = (int)std::max(1u, std::min((uint32_t)m->attn_splits, want));
     SK_TRY(launch_decode_attn(a, splits, s, false));
+    const float *next = (l + 1 < m->L) ? m->layers[l + 1].input_norm : m->final_norm;
+    if (fuse) {
+      // o and down end in one kernel each: split sum, post norm, residual add, the next
+      // norm and the next GEMM's activation blocks (same operations, same order)
+      uint8_t *xs = reinterpret_cast<uint8_t *>(m->ms_xf);
+      uint32_t sk = 0;
+      SK_TRY(launch_skinny_q4_tc(dl.o, m->H / 16, m->qd, m->pA, m->qd, n, xs, m->ms_skp, err, &sk, s));
+      SK_TRY(launch_skinny_tail(m->ms_skp, sk, n, m->H, dl.post_attn, m->pX, dl.pre_ffn, m->pNX, eps, 1.0f, xs, s));
+      SK_TRY(launch_skinny_q4(dl.gateup, 2 * m->I / 16, m->H, m->pNX, m->H, n, EPI_GELU_MUL, m->pACT, m->I, m->ms_xf,
+                              m->ms_skp, err, s, true));
+      SK_TRY(launch_skinny_q4_tc(dl.down, m->H / 16, m->I, m->pACT, m->I, n, xs, m->ms_skp, err, &sk, s));
+      SK_TRY(launch_skinny_tail(m->ms_skp, sk, n, m->H, dl.post_ffn, m->pX, next, m->pNX, eps, dl.scalar,
+                                l + 1 < m->L ? xs : nullptr, s));
+      continue;
+    }
     SK_TRY(launch_skinny_q4(dl.o, m->H / 16, m->qd, m->pA, m->qd, n, EPI_STORE, m->pMO, m->H, m->ms_xf, m->ms_skp,
                              err, s));
     if (dl.post_attn) SK_TRY(launch_rmsnorm_rows(m->pMO, dl.post_attn, m->pMO, n, m->H, eps, s));
@@ -1746,7 +1763,6 @@ static cudaError_t enqueue_streams_step(ch_model *m, uint32_t n, cudaStream_t s)
     SK_TRY(launch_skinny_q4(dl.down, m->H / 16, m->I, m->pACT, m->I, n, EPI_STORE, m->pMO, m->H, m->ms_xf,
                              m->ms_skp, err, s));
     if (dl.post_ffn) SK_TRY(launch_rmsnorm_rows(m->pMO, dl.post_ffn, m->pMO, n, m->H, eps, s));
-    const float *next = (l + 1 < m->L) ? m->layers[l + 1].input_norm : m->final_norm;
     SK_TRY(launch_add_rmsnorm_rows(m->pX, m->pMO, next, m->pNX, n, m->H, eps, dl.scalar, s));
   }
   {  // Q8 LM head of every token's final-normed state, the head read once for the batch

@@ -321,6 +321,115 @@ __global__ void __launch_bounds__(kSkThreads, 1)
 }
 
 // ---------------------------------------------------------------------------
+// The end of a row-parallel projection (o, down) of the multi-stream step, one token per
+// CTA: v = the K splits' partials added in split order (as skinny_reduce_kernel), then
+// with the operations and order of rmsnorm_rows_vec_kernel and add_rmsnorm_rows_vec_kernel
+// (prefill.cu): v = rmsnorm(v) * post_w (when given), x = (x + v) * scalar,
+// y = rmsnorm(x) * next_w; and, when xs is given, y's hi / lo blocks for the next skinny
+// GEMM (as skinny_tc_x_kernel).  Rows of H <= 4096 floats, H % 64 == 0.
+constexpr int kTailThreads = 256, kTailVec = 4;
+__global__ void __launch_bounds__(kTailThreads)
+    skinny_tail_kernel(const float *partial, uint32_t splits, uint32_t B, uint32_t H, const float *post_w, float *x,
+                       const float *next_w, float *y, float eps, float scalar, uint8_t *xs) {
+  __shared__ float red[32];
+  const uint32_t t = blockIdx.x, n4 = H / 4, tid = threadIdx.x;
+  float4 v[kTailVec];
+#pragma unroll
+  for (int k = 0; k < kTailVec; k++) {
+    const uint32_t j = tid + k * kTailThreads;
+    v[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (j < n4) {
+      const float4 *p0 = reinterpret_cast<const float4 *>(partial + (size_t)t * H) + j;
+      float4 a = p0[0];
+      for (uint32_t sp = 1; sp < splits; sp++) {
+        const float4 b = *(reinterpret_cast<const float4 *>(partial + ((size_t)sp * B + t) * H) + j);
+        a = make_float4(__fadd_rn(a.x, b.x), __fadd_rn(a.y, b.y), __fadd_rn(a.z, b.z), __fadd_rn(a.w, b.w));
+      }
+      v[k] = a;
+    }
+  }
+  auto sumsq = [&](const float4 (&u)[kTailVec]) {
+    float ss = 0.f;
+#pragma unroll
+    for (int k = 0; k < kTailVec; k++) {
+      ss = __fmaf_rn(u[k].x, u[k].x, ss);
+      ss = __fmaf_rn(u[k].y, u[k].y, ss);
+      ss = __fmaf_rn(u[k].z, u[k].z, ss);
+      ss = __fmaf_rn(u[k].w, u[k].w, ss);
+    }
+    const float tot = block_sum(ss, red);
+    return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)H), eps)));
+  };
+  if (post_w) {
+    const float inv = sumsq(v);
+#pragma unroll
+    for (int k = 0; k < kTailVec; k++) {
+      const uint32_t j = tid + k * kTailThreads;
+      if (j < n4) {
+        const float4 g = reinterpret_cast<const float4 *>(post_w)[j];
+        v[k] = make_float4(__fmul_rn(__fmul_rn(v[k].x, inv), g.x), __fmul_rn(__fmul_rn(v[k].y, inv), g.y),
+                           __fmul_rn(__fmul_rn(v[k].z, inv), g.z), __fmul_rn(__fmul_rn(v[k].w, inv), g.w));
+      }
+    }
+  }
+  float4 *xr = reinterpret_cast<float4 *>(x + (size_t)t * H);
+#pragma unroll
+  for (int k = 0; k < kTailVec; k++) {
+    const uint32_t j = tid + k * kTailThreads;
+    float4 a = make_float4(0.f, 0.f, 0.f, 0.f), b = a;
+    if (j < n4) a = xr[j], b = v[k];
+    v[k] = make_float4(__fmul_rn(__fadd_rn(a.x, b.x), scalar), __fmul_rn(__fadd_rn(a.y, b.y), scalar),
+                       __fmul_rn(__fadd_rn(a.z, b.z), scalar), __fmul_rn(__fadd_rn(a.w, b.w), scalar));
+    if (j < n4) xr[j] = v[k];
+  }
+  const float inv = sumsq(v);
+  float4 *yr = reinterpret_cast<float4 *>(y + (size_t)t * H);
+#pragma unroll
+  for (int k = 0; k < kTailVec; k++) {
+    const uint32_t j = tid + k * kTailThreads;
+    float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (j < n4) {
+      const float4 g = reinterpret_cast<const float4 *>(next_w)[j];
+      o = make_float4(__fmul_rn(__fmul_rn(v[k].x, inv), g.x), __fmul_rn(__fmul_rn(v[k].y, inv), g.y),
+                      __fmul_rn(__fmul_rn(v[k].z, inv), g.z), __fmul_rn(__fmul_rn(v[k].w, inv), g.w));
+      yr[j] = o;
+    }
+    if (xs) {  // even thread: its float4 and its neighbour's are one 8-wide chunk (n4 is even)
+      const float4 nb = make_float4(__shfl_down_sync(0xFFFFFFFFu, o.x, 1), __shfl_down_sync(0xFFFFFFFFu, o.y, 1),
+                                    __shfl_down_sync(0xFFFFFFFFu, o.z, 1), __shfl_down_sync(0xFFFFFFFFu, o.w, 1));
+      if (!(tid & 1) && j < n4) {
+        const float e8[8] = {o.x, o.y, o.z, o.w, nb.x, nb.y, nb.z, nb.w};
+        uint32_t hi[4], lo[4];
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+          const __half h0 = __float2half_rn(e8[2 * e]), h1 = __float2half_rn(e8[2 * e + 1]);
+          const __half l0 = __float2half_rn(__fmul_rn(__fsub_rn(e8[2 * e], __half2float(h0)), 256.f));
+          const __half l1 = __float2half_rn(__fmul_rn(__fsub_rn(e8[2 * e + 1], __half2float(h1)), 256.f));
+          hi[e] = pack_half2(h0, h1);
+          lo[e] = pack_half2(l0, l1);
+        }
+        const uint32_t c8 = j >> 1, kt = c8 >> 3, c = c8 & 7;
+        uint8_t *blk = xs + (size_t)kt * kSkXBytes;
+        const uint32_t rh = t, rl = kSkTok + t, sw = (c ^ (t & 7)) << 4;
+        *reinterpret_cast<uint4 *>(blk + (rh >> 3) * 1024 + (rh & 7) * 128 + sw) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+        *reinterpret_cast<uint4 *>(blk + (rl >> 3) * 1024 + (rl & 7) * 128 + sw) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+      }
+    }
+  }
+}
+
+cudaError_t launch_skinny_tail(const float *partial, uint32_t splits, uint32_t B, uint32_t H, const float *post_w,
+                               float *x, const float *next_w, float *y, float eps, float scalar, uint8_t *xs,
+                               cudaStream_t s) {
+  if (B == 0 || B > (uint32_t)kSkTok || splits == 0 || H % 64 || H > 4u * kTailVec * kTailThreads)
+    return cudaErrorInvalidValue;
+  if (((uintptr_t)partial | (uintptr_t)x | (uintptr_t)next_w | (uintptr_t)y | (uintptr_t)post_w | (uintptr_t)xs) & 15)
+    return cudaErrorInvalidValue;
+  skinny_tail_kernel<<<B, kTailThreads, 0, s>>>(partial, splits, B, H, post_w, x, next_w, y, eps, scalar, xs);
+  return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
 // K splits: as many CTAs as fit the SMs in one wave (the rows alone give too few for
 // o and down), at most one per k tile
 uint32_t skinny_tc_splits(uint32_t row_tiles, uint32_t K) {
@@ -363,18 +472,22 @@ static cudaError_t tile_map_cached(const uint8_t *tiles, uint32_t M, uint32_t K,
 }
 
 // partial[split][B][row_tiles * 16] = the K split's share of W x for B <= 64 tokens;
-// xs scratch: skinny_tc_x_bytes(K), 16-byte aligned
+// xs scratch: skinny_tc_x_bytes(K), 16-byte aligned.  x_ready: xs already holds x's
+// blocks (written by skinny_tail_kernel), x is not read.
 cudaError_t launch_skinny_q4_tc(const uint8_t *tiles, uint32_t row_tiles, uint32_t K, const float *x, uint32_t ldx,
                                 uint32_t B, uint8_t *xs, float *partial, uint32_t *err, uint32_t *splits,
-                                cudaStream_t s) {
-  if (B == 0 || B > (uint32_t)kSkTok || K % 64 || row_tiles == 0 || ldx % 4 || ((uintptr_t)x & 15) ||
-      ((uintptr_t)xs & 15) || ((uintptr_t)tiles & 15))
+                                cudaStream_t s, bool x_ready) {
+  if (B == 0 || B > (uint32_t)kSkTok || K % 64 || row_tiles == 0 || ((uintptr_t)xs & 15) || ((uintptr_t)tiles & 15))
     return cudaErrorInvalidValue;
-  const uint32_t total = kSkTok * (K / 8);
-  skinny_tc_x_kernel<<<std::min<uint32_t>((total + 255) / 256, (uint32_t)num_sms() * 8), 256, 0, s>>>(x, ldx, B, K,
-                                                                                                        xs);
-  cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return e;
+  cudaError_t e = cudaSuccess;
+  if (!x_ready) {
+    if (ldx % 4 || ((uintptr_t)x & 15)) return cudaErrorInvalidValue;
+    const uint32_t total = kSkTok * (K / 8);
+    skinny_tc_x_kernel<<<std::min<uint32_t>((total + 255) / 256, (uint32_t)num_sms() * 8), 256, 0, s>>>(x, ldx, B,
+                                                                                                          K, xs);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+  }
   alignas(64) CUtensorMap wmap;
   e = tile_map_cached(tiles, row_tiles * 16, K, &wmap);
   if (e != cudaSuccess) return e;
