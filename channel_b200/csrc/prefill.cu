@@ -337,20 +337,215 @@ __global__ void __launch_bounds__(256, 3) batch_causal_attn_kernel(const BatchAt
     for (int e = 0; e < EPL; e++) op[e] = __fmul_rn(acc[hh][e], inv);
   }
 }
+// ---------------------------------------------------------------------------
+// batch causal attention on the tensor cores (mma.sync.m16n8k16, f32 accumulate) for
+// grouped heads: a CTA is 32 tokens x the two q heads of one kv head (4 warps, 16 rows
+// each), the K / V rows of 32 slots at a time staged in shared memory for all of them.
+//   S = (Q_hi + Q_lo) K^T: q as an exact f16 pair (two MMAs per step), K exact f16;
+//   online softmax per block of 32 slots (row max over the block, one correction of the
+//   running sums per block; masked slots -inf: past the token, or before its window);
+//   O += P V with P rounded to f16 (relative error 2^-12 per weight; the sum l is
+//   taken from the f32 p), V exact; out = O / (l + 1e-9) as batch_causal_attn.wgsl.
+constexpr int kFaTok = 32, kFaSlots = 32, kFaPitch = 264;  // 256 halves + 8: conflict-free rows
+constexpr size_t kFaSmem = (size_t)(2 * 2 * kFaTok + 2 * kFaSlots) * kFaPitch * sizeof(__half);
+
+CH_DEV void ldsm_x4_trans(uint32_t addr, uint32_t &r0, uint32_t &r1, uint32_t &r2, uint32_t &r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+
+__global__ void __launch_bounds__(128, 2) batch_causal_attn_mma_kernel(const BatchAttnArgs a) {
+  constexpr int D = 256;
+  extern __shared__ __align__(16) __half fa_s[];
+  __half *qh = fa_s, *ql = qh + 2 * kFaTok * kFaPitch;  // [head pair row: hh*32 + token][d]
+  __half *ks = ql + 2 * kFaTok * kFaPitch, *vs = ks + kFaSlots * kFaPitch;  // [slot][d]
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, g = lane >> 2, tq = lane & 3;
+  const uint32_t h0 = blockIdx.y * 2, ratio = a.nq / a.nkv, kvh = h0 / ratio;
+  // the last tokens attend to the most slots: their CTAs are issued first
+  const uint32_t t0 = (gridDim.x - 1 - blockIdx.x) * kFaTok;  // < N
+  const size_t qd = (size_t)a.nq * D, kvd = (size_t)a.nkv * D;
+
+  // q rows of both heads -> f16 hi / lo planes (tokens past N: zeros)
+  for (int idx = tid; idx < 2 * kFaTok * (D / 8); idx += 128) {
+    const int row = idx / (D / 8), c8 = idx % (D / 8), hh = row / kFaTok, tk = row % kFaTok;
+    float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    if (t0 + tk < a.N) {
+      const float4 *src = reinterpret_cast<const float4 *>(a.q + (size_t)(t0 + tk) * qd + (size_t)(h0 + hh) * D + c8 * 8);
+      const float4 x0 = src[0], x1 = src[1];
+      v[0] = x0.x, v[1] = x0.y, v[2] = x0.z, v[3] = x0.w, v[4] = x1.x, v[5] = x1.y, v[6] = x1.z, v[7] = x1.w;
+    }
+    uint32_t hi[4], lo[4];
+#pragma unroll
+    for (int e = 0; e < 4; e++) {
+      const __half a0 = __float2half_rn(v[2 * e]), a1 = __float2half_rn(v[2 * e + 1]);
+      hi[e] = pack_half2(a0, a1);
+      lo[e] = pack_half2(__float2half_rn(__fsub_rn(v[2 * e], __half2float(a0))),
+                         __float2half_rn(__fsub_rn(v[2 * e + 1], __half2float(a1))));
+    }
+    *reinterpret_cast<uint4 *>(qh + row * kFaPitch + c8 * 8) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+    *reinterpret_cast<uint4 *>(ql + row * kFaPitch + c8 * 8) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+  }
+
+  // this warp: head h0 + (warp >> 1), tokens t0 + 16 (warp & 1) .. + 15; lane rows g, g + 8
+  const int qrow = (warp >> 1) * kFaTok + (warp & 1) * 16;
+  const uint32_t tr[2] = {t0 + (warp & 1) * 16 + g, t0 + (warp & 1) * 16 + g + 8};
+  auto first_slot = [&](uint32_t S) { return (a.is_sliding && S > 1024) ? S - 1024 : 0u; };
+  uint32_t rs[2], re[2];  // each row's slot range [rs, re)
+#pragma unroll
+  for (int r = 0; r < 2; r++) {
+    re[r] = tr[r] < a.N ? a.num_prev + tr[r] + 1 : 0u;
+    rs[r] = tr[r] < a.N ? first_slot(re[r]) : 0u;
+  }
+  const uint32_t tl = min(t0 + kFaTok - 1, a.N - 1);
+  const uint32_t u0 = first_slot(a.num_prev + t0 + 1), u1 = a.num_prev + tl + 1;  // the CTA's slots
+  const uint32_t nblk = (u1 - u0 + kFaSlots - 1) / kFaSlots;
+
+  float o[32][4];  // 16 rows x 256 d: n-tile j = d 8j..8j+7
+#pragma unroll
+  for (int j = 0; j < 32; j++) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
+  float m[2] = {-1e9f, -1e9f}, l[2] = {0.f, 0.f};  // running max (as the shader starts it) and this lane's part of the sum
+
+  const uint32_t ks_base = smem_u32(ks), vs_base = smem_u32(vs);
+  for (uint32_t blk = 0; blk < nblk; blk++) {
+    const uint32_t i0 = u0 + blk * kFaSlots;
+    __syncthreads();  // the previous block's rows are no longer read (and q is staged)
+    {  // K and V rows of slots i0..i0+31: thread -> slot tid / 4, 128 bytes of each row
+      const uint32_t j = tid >> 2, part = (tid & 3) * 64;  // halves
+      const uint32_t i = i0 + j;
+      __half *kd = ks + j * kFaPitch + part, *vd = vs + j * kFaPitch + part;
+      if (i < u1) {
+        const size_t off = (size_t)a.slots[i] * kvd + (size_t)kvh * D + part;
+#pragma unroll
+        for (int c = 0; c < 8; c++) {
+          cp_async16(kd + c * 8, a.k_cache + off + c * 8);
+          cp_async16(vd + c * 8, a.v_cache + off + c * 8);
+        }
+      } else {
+#pragma unroll
+        for (int c = 0; c < 8; c++) {
+          *reinterpret_cast<uint4 *>(kd + c * 8) = make_uint4(0u, 0u, 0u, 0u);
+          *reinterpret_cast<uint4 *>(vd + c * 8) = make_uint4(0u, 0u, 0u, 0u);
+        }
+      }
+      cp_async_wait_all();
+    }
+    __syncthreads();
+
+    // S (16 x 32) = Q K^T, both q halves into the same accumulators
+    float sc[4][4];
+#pragma unroll
+    for (int nt = 0; nt < 4; nt++) sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.f;
+#pragma unroll 4
+    for (int kk = 0; kk < D / 16; kk++) {
+      const int c0 = kk * 16 + 2 * tq;
+      uint32_t ah[4], al[4];
+      ah[0] = *reinterpret_cast<const uint32_t *>(qh + (qrow + g) * kFaPitch + c0);
+      ah[1] = *reinterpret_cast<const uint32_t *>(qh + (qrow + g + 8) * kFaPitch + c0);
+      ah[2] = *reinterpret_cast<const uint32_t *>(qh + (qrow + g) * kFaPitch + c0 + 8);
+      ah[3] = *reinterpret_cast<const uint32_t *>(qh + (qrow + g + 8) * kFaPitch + c0 + 8);
+      al[0] = *reinterpret_cast<const uint32_t *>(ql + (qrow + g) * kFaPitch + c0);
+      al[1] = *reinterpret_cast<const uint32_t *>(ql + (qrow + g + 8) * kFaPitch + c0);
+      al[2] = *reinterpret_cast<const uint32_t *>(ql + (qrow + g) * kFaPitch + c0 + 8);
+      al[3] = *reinterpret_cast<const uint32_t *>(ql + (qrow + g + 8) * kFaPitch + c0 + 8);
+#pragma unroll
+      for (int nt = 0; nt < 4; nt++) {
+        const uint32_t b0 = *reinterpret_cast<const uint32_t *>(ks + (nt * 8 + g) * kFaPitch + c0);
+        const uint32_t b1 = *reinterpret_cast<const uint32_t *>(ks + (nt * 8 + g) * kFaPitch + c0 + 8);
+        mma_16816(sc[nt], ah, b0, b1);
+        mma_16816(sc[nt], al, b0, b1);
+      }
+    }
+
+    // mask, block max per row (the quad of lanes sharing a row), probabilities
+    float bm[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+    for (int nt = 0; nt < 4; nt++)
+#pragma unroll
+      for (int c = 0; c < 4; c++) {
+        const int r = c >> 1;
+        const uint32_t i = i0 + nt * 8 + 2 * tq + (c & 1);
+        const float v = (i >= rs[r] && i < re[r]) ? __fmul_rn(sc[nt][c], a.scale) : -INFINITY;
+        sc[nt][c] = v;
+        bm[r] = fmaxf(bm[r], v);
+      }
+    float corr[2];
+#pragma unroll
+    for (int r = 0; r < 2; r++) {
+      bm[r] = fmaxf(bm[r], __shfl_xor_sync(0xFFFFFFFFu, bm[r], 1));
+      bm[r] = fmaxf(bm[r], __shfl_xor_sync(0xFFFFFFFFu, bm[r], 2));
+      const float mn = fmaxf(m[r], bm[r]);
+      corr[r] = expf(__fsub_rn(m[r], mn));
+      m[r] = mn;
+      l[r] = __fmul_rn(l[r], corr[r]);
+    }
+    uint32_t pa[2][4];  // P as the A operand of two k16 steps (slots 0-15, 16-31)
+#pragma unroll
+    for (int nt = 0; nt < 4; nt++) {
+      float p[4];
+#pragma unroll
+      for (int c = 0; c < 4; c++) {
+        p[c] = expf(__fsub_rn(sc[nt][c], m[c >> 1]));
+        l[c >> 1] = __fadd_rn(l[c >> 1], p[c]);
+      }
+      const int ksx = nt >> 1, hi8 = nt & 1;
+      pa[ksx][hi8 * 2 + 0] = pack_half2(__float2half_rn(p[0]), __float2half_rn(p[1]));
+      pa[ksx][hi8 * 2 + 1] = pack_half2(__float2half_rn(p[2]), __float2half_rn(p[3]));
+    }
+#pragma unroll
+    for (int j = 0; j < 32; j++) {
+      o[j][0] = __fmul_rn(o[j][0], corr[0]);
+      o[j][1] = __fmul_rn(o[j][1], corr[0]);
+      o[j][2] = __fmul_rn(o[j][2], corr[1]);
+      o[j][3] = __fmul_rn(o[j][3], corr[1]);
+    }
+    // O += P V: V as B operand by ldmatrix.trans, two n-tiles (16 d) per load
+#pragma unroll
+    for (int ksx = 0; ksx < 2; ksx++) {
+      const uint32_t vrow = ksx * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+#pragma unroll
+      for (int nd = 0; nd < 16; nd++) {
+        const uint32_t col = nd * 16 + (lane >> 4) * 8;
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4_trans(vs_base + (vrow * kFaPitch + col) * 2, b0, b1, b2, b3);
+        mma_16816(o[2 * nd], pa[ksx], b0, b1);
+        mma_16816(o[2 * nd + 1], pa[ksx], b2, b3);
+      }
+    }
+  }
+  (void)ks_base;
+
+  // rows' sums over the quad, then out = O / (l + 1e-9)
+#pragma unroll
+  for (int r = 0; r < 2; r++) {
+    l[r] = __fadd_rn(l[r], __shfl_xor_sync(0xFFFFFFFFu, l[r], 1));
+    l[r] = __fadd_rn(l[r], __shfl_xor_sync(0xFFFFFFFFu, l[r], 2));
+  }
+  const uint32_t h = h0 + (warp >> 1);
+#pragma unroll
+  for (int r = 0; r < 2; r++) {
+    if (tr[r] >= a.N) continue;
+    const float inv = __fdiv_rn(1.0f, __fadd_rn(l[r], 1e-9f));
+    float *op = a.out + (size_t)tr[r] * qd + (size_t)h * D + 2 * tq;
+#pragma unroll
+    for (int j = 0; j < 32; j++)
+      *reinterpret_cast<float2 *>(op + j * 8) = make_float2(__fmul_rn(o[j][2 * r], inv), __fmul_rn(o[j][2 * r + 1], inv));
+  }
+}
+
 cudaError_t launch_batch_causal_attn(const BatchAttnArgs &a, cudaStream_t s) {
   if (a.D != 256 || a.N == 0) return a.N == 0 ? cudaSuccess : cudaErrorInvalidValue;
   if (a.nkv == 0 || a.nq % a.nkv) return cudaErrorInvalidValue;
-  const dim3 blocks((a.N + 7) / 8, 1);
-  if ((a.nq / a.nkv) % 2 == 0) {  // pairs of q heads of one kv head per warp
-    cudaError_t e = cudaFuncSetAttribute(batch_causal_attn_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)kCaSmem);
+  if ((a.nq / a.nkv) % 2 == 0) {  // pairs of q heads of one kv head: the tensor-core kernel
+    cudaError_t e = cudaFuncSetAttribute(batch_causal_attn_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)kFaSmem);
     if (e != cudaSuccess) return e;
-    batch_causal_attn_kernel<2><<<dim3(blocks.x, a.nq / 2), 256, kCaSmem, s>>>(a);
+    batch_causal_attn_mma_kernel<<<dim3((a.N + kFaTok - 1) / kFaTok, a.nq / 2), 128, kFaSmem, s>>>(a);
   } else {
     cudaError_t e = cudaFuncSetAttribute(batch_causal_attn_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)kCaSmem);
     if (e != cudaSuccess) return e;
-    batch_causal_attn_kernel<1><<<dim3(blocks.x, a.nq), 256, kCaSmem, s>>>(a);
+    batch_causal_attn_kernel<1><<<dim3((a.N + 7) / 8, a.nq), 256, kCaSmem, s>>>(a);
   }
   return cudaGetLastError();
 }
