@@ -341,11 +341,14 @@ __global__ void __launch_bounds__(256, 3) batch_causal_attn_kernel(const BatchAt
 // batch causal attention on the tensor cores (mma.sync.m16n8k16, f32 accumulate) for
 // grouped heads: a CTA is 32 tokens x the two q heads of one kv head (4 warps, 16 rows
 // each), the K / V rows of 32 slots at a time staged in shared memory for all of them.
-//   S = (Q_hi + Q_lo) K^T: q as an exact f16 pair (two MMAs per step), K exact f16;
+//   S = (Q_hi + Q_lo) K^T: q 2^8 as an f16 pair (two MMAs per step; the scale keeps
+//   q_lo = q - q_hi, ~2^-12 q, a normal f16 for |q| >= 2^-10), K exact f16, S 2^-8;
 //   online softmax per block of 32 slots (row max over the block, one correction of the
 //   running sums per block; masked slots -inf: past the token, or before its window);
-//   O += P V with P rounded to f16 (relative error 2^-12 per weight; the sum l is
-//   taken from the f32 p), V exact; out = O / (l + 1e-9) as batch_causal_attn.wgsl.
+//   O += (P_hi + P_lo) V with p 2^14 as an f16 pair too (two MMAs per step into the same
+//   accumulators; p_lo stays a normal f16 for p >= 2^-16), V exact; the sum l from the
+//   f32 p; out = (O 2^-14) / (l + 1e-9) as batch_causal_attn.wgsl.  The power-of-two
+//   scales are exact.
 constexpr int kFaTok = 32, kFaSlots = 32, kFaPitch = 264;  // 256 halves + 8: conflict-free rows
 constexpr size_t kFaSmem = (size_t)(2 * 2 * kFaTok + 2 * kFaSlots) * kFaPitch * sizeof(__half);
 
@@ -375,6 +378,8 @@ __global__ void __launch_bounds__(128, 2) batch_causal_attn_mma_kernel(const Bat
       const float4 x0 = src[0], x1 = src[1];
       v[0] = x0.x, v[1] = x0.y, v[2] = x0.z, v[3] = x0.w, v[4] = x1.x, v[5] = x1.y, v[6] = x1.z, v[7] = x1.w;
     }
+#pragma unroll
+    for (int e = 0; e < 8; e++) v[e] = __fmul_rn(v[e], 256.f);  // q 2^8 (exact)
     uint32_t hi[4], lo[4];
 #pragma unroll
     for (int e = 0; e < 4; e++) {
@@ -465,7 +470,7 @@ __global__ void __launch_bounds__(128, 2) batch_causal_attn_mma_kernel(const Bat
       for (int c = 0; c < 4; c++) {
         const int r = c >> 1;
         const uint32_t i = i0 + nt * 8 + 2 * tq + (c & 1);
-        const float v = (i >= rs[r] && i < re[r]) ? __fmul_rn(sc[nt][c], a.scale) : -INFINITY;
+        const float v = (i >= rs[r] && i < re[r]) ? __fmul_rn(__fmul_rn(sc[nt][c], 1.0f / 256.f), a.scale) : -INFINITY;
         sc[nt][c] = v;
         bm[r] = fmaxf(bm[r], v);
       }
@@ -479,18 +484,24 @@ __global__ void __launch_bounds__(128, 2) batch_causal_attn_mma_kernel(const Bat
       m[r] = mn;
       l[r] = __fmul_rn(l[r], corr[r]);
     }
-    uint32_t pa[2][4];  // P as the A operand of two k16 steps (slots 0-15, 16-31)
+    uint32_t pa[2][4], pl[2][4];  // P (hi, lo) as the A operand of two k16 steps (slots 0-15, 16-31)
 #pragma unroll
     for (int nt = 0; nt < 4; nt++) {
       float p[4];
+      __half ph[4], plo[4];
 #pragma unroll
       for (int c = 0; c < 4; c++) {
         p[c] = expf(__fsub_rn(sc[nt][c], m[c >> 1]));
         l[c >> 1] = __fadd_rn(l[c >> 1], p[c]);
+        const float ps = __fmul_rn(p[c], 16384.f);  // p 2^14 (exact)
+        ph[c] = __float2half_rn(ps);
+        plo[c] = __float2half_rn(__fsub_rn(ps, __half2float(ph[c])));
       }
       const int ksx = nt >> 1, hi8 = nt & 1;
-      pa[ksx][hi8 * 2 + 0] = pack_half2(__float2half_rn(p[0]), __float2half_rn(p[1]));
-      pa[ksx][hi8 * 2 + 1] = pack_half2(__float2half_rn(p[2]), __float2half_rn(p[3]));
+      pa[ksx][hi8 * 2 + 0] = pack_half2(ph[0], ph[1]);
+      pa[ksx][hi8 * 2 + 1] = pack_half2(ph[2], ph[3]);
+      pl[ksx][hi8 * 2 + 0] = pack_half2(plo[0], plo[1]);
+      pl[ksx][hi8 * 2 + 1] = pack_half2(plo[2], plo[3]);
     }
 #pragma unroll
     for (int j = 0; j < 32; j++) {
@@ -509,7 +520,9 @@ __global__ void __launch_bounds__(128, 2) batch_causal_attn_mma_kernel(const Bat
         uint32_t b0, b1, b2, b3;
         ldsm_x4_trans(vs_base + (vrow * kFaPitch + col) * 2, b0, b1, b2, b3);
         mma_16816(o[2 * nd], pa[ksx], b0, b1);
+        mma_16816(o[2 * nd], pl[ksx], b0, b1);
         mma_16816(o[2 * nd + 1], pa[ksx], b2, b3);
+        mma_16816(o[2 * nd + 1], pl[ksx], b2, b3);
       }
     }
   }
@@ -527,9 +540,11 @@ __global__ void __launch_bounds__(128, 2) batch_causal_attn_mma_kernel(const Bat
     if (tr[r] >= a.N) continue;
     const float inv = __fdiv_rn(1.0f, __fadd_rn(l[r], 1e-9f));
     float *op = a.out + (size_t)tr[r] * qd + (size_t)h * D + 2 * tq;
+    constexpr float kUnscale = 1.0f / 16384.f;
 #pragma unroll
     for (int j = 0; j < 32; j++)
-      *reinterpret_cast<float2 *>(op + j * 8) = make_float2(__fmul_rn(o[j][2 * r], inv), __fmul_rn(o[j][2 * r + 1], inv));
+      *reinterpret_cast<float2 *>(op + j * 8) = make_float2(__fmul_rn(__fmul_rn(o[j][2 * r], kUnscale), inv),
+                                                            __fmul_rn(__fmul_rn(o[j][2 * r + 1], kUnscale), inv));
   }
 }
 

@@ -31,7 +31,9 @@ def ring_step_lists(ring, cfg, clock):
 
 def topk_ids_agree(ids, rid, rvals, tol=1e-4):
     """ids must match exactly wherever the oracle's neighbouring values are separated
-    by more than the numeric tolerance (closer pairs may legitimately swap)."""
+    by more than the numeric tolerance (closer pairs may legitimately swap).  The last
+    entry's lower neighbour (the 65th value) is not in the list, so it is never clear:
+    a near-tie there can swap in a candidate from below."""
     ids, rid, rvals = np.asarray(ids), np.asarray(rid), np.asarray(rvals, np.float64)
     if ids[0] != rid[0] and abs(rvals[0] - rvals[1]) > tol * max(1.0, abs(rvals[0])):
         return False
@@ -39,4 +41,5 @@ def topk_ids_agree(ids, rid, rvals, tol=1e-4):
     clear = np.ones(len(ids), bool)
     clear[:-1] &= gaps > tol * np.maximum(1.0, np.abs(rvals[:-1]))
     clear[1:] &= gaps > tol * np.maximum(1.0, np.abs(rvals[1:]))
+    clear[-1] = False
     return bool(np.all(ids[clear] == rid[clear])) and set(ids[:-4]) <= set(rid)

@@ -85,6 +85,35 @@ def test_prefill_then_decode_matches_oracle(small, oracle):
         tok = int(gtok)
 
 
+@pytest.mark.parametrize("N,chunk", [(1300, 1024), (700, 256)])
+def test_long_prefill_in_chunks_matches_oracle(small, oracle, N, chunk):
+    """Prompts past the 1,024-slot window of the sliding layers, prefilled in chunks that
+    attend to the earlier ones through the ring's previous slots (the tensor-core causal
+    attention: block edges, window starts and the causal diagonal inside one block).
+    The tensor cores' f32 sums are not rounded like the shader's per-slot recurrence: the
+    hidden state agrees to ~2e-4 relative after 700 tokens (measured on B200), inside the
+    1e-3 float bar, so the top-64 ids are held exact away from near-ties at that bar."""
+    cfg, gm, w = small
+    gm.zero_state()
+    om = oracle.Model(cfg, w)
+    prompt = np.random.default_rng(N).integers(0, cfg.vocab_size, N).astype(np.uint32)
+    X = oracle.embed(w.embed, prompt, cfg.hidden_size)
+    ring = DynamicRingBuffer(cfg.num_hidden_layers, 0)
+    for c0 in range(0, N, chunk):
+        m = min(chunk, N - c0)
+        prev = ring.getPrefillPrevSlots(0, c0, m)
+        slots = np.concatenate([prev, ring.activateRange(c0, m)]).astype(np.uint32)
+        cands = gpu_dispatch_prefill_batch(gm, prompt[c0:c0 + m], None, slots, c0, len(prev))
+        rtok, rid, rvals = om.prefill(X[c0:c0 + m], slots, c0, len(prev))
+        ids = np.array([c.id for c in cands])
+        vals = np.array([c.val for c in cands])
+        assert_close(gm.read_normed_x(), om.normed_x(), what=f"normed x after the chunk at {c0}")
+        assert_close(gm.read_x(), om.x(), what=f"residual after the chunk at {c0}")
+        assert ids[0] == rtok, f"greedy token of the chunk at {c0}"
+        diff = [(i, int(ids[i]), float(vals[i]), int(rid[i]), float(rvals[i])) for i in range(len(ids)) if ids[i] != rid[i]]
+        assert topk_ids_agree(ids, rid, rvals, tol=1e-3), f"top-64 ids of the chunk at {c0}: (pos, id, val, oracle id, val) {diff}"
+
+
 def test_prefill_host_embed_equals_device_embed(small, oracle):
     cfg, gm, w = small
     prompt = [5, 6, 7, 4095, 0]
