@@ -411,7 +411,7 @@ __global__ void __launch_bounds__(128, 2) batch_causal_attn_mma_kernel(const Bat
   for (int j = 0; j < 32; j++) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
   float m[2] = {-1e9f, -1e9f}, l[2] = {0.f, 0.f};  // running max (as the shader starts it) and this lane's part of the sum
 
-  const uint32_t ks_base = smem_u32(ks), vs_base = smem_u32(vs);
+  const uint32_t vs_base = smem_u32(vs);
   for (uint32_t blk = 0; blk < nblk; blk++) {
     const uint32_t i0 = u0 + blk * kFaSlots;
     __syncthreads();  // the previous block's rows are no longer read (and q is staged)
@@ -526,7 +526,6 @@ __global__ void __launch_bounds__(128, 2) batch_causal_attn_mma_kernel(const Bat
       }
     }
   }
-  (void)ks_base;
 
   // rows' sums over the quad, then out = O / (l + 1e-9)
 #pragma unroll
