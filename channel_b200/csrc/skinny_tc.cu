@@ -334,19 +334,23 @@ __global__ void __launch_bounds__(kTailThreads)
   __shared__ float red[32];
   const uint32_t t = blockIdx.x, n4 = H / 4, tid = threadIdx.x;
   float4 v[kTailVec];
-#pragma unroll
-  for (int k = 0; k < kTailVec; k++) {
+  auto part = [&](uint32_t sp, int k) {  // split sp's float4 k of this thread (zeros past the row)
     const uint32_t j = tid + k * kTailThreads;
-    v[k] = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (j < n4) {
-      const float4 *p0 = reinterpret_cast<const float4 *>(partial + (size_t)t * H) + j;
-      float4 a = p0[0];
-      for (uint32_t sp = 1; sp < splits; sp++) {
-        const float4 b = *(reinterpret_cast<const float4 *>(partial + ((size_t)sp * B + t) * H) + j);
-        a = make_float4(__fadd_rn(a.x, b.x), __fadd_rn(a.y, b.y), __fadd_rn(a.z, b.z), __fadd_rn(a.w, b.w));
-      }
-      v[k] = a;
-    }
+    return j < n4 ? *(reinterpret_cast<const float4 *>(partial + ((size_t)sp * B + t) * H) + j)
+                  : make_float4(0.f, 0.f, 0.f, 0.f);
+  };
+#pragma unroll
+  for (int k = 0; k < kTailVec; k++) v[k] = part(0, k);
+  // splits in order; the loads of several splits are in flight before their additions
+#pragma unroll 3
+  for (uint32_t sp = 1; sp < splits; sp++) {
+    float4 b[kTailVec];
+#pragma unroll
+    for (int k = 0; k < kTailVec; k++) b[k] = part(sp, k);
+#pragma unroll
+    for (int k = 0; k < kTailVec; k++)
+      v[k] = make_float4(__fadd_rn(v[k].x, b[k].x), __fadd_rn(v[k].y, b[k].y), __fadd_rn(v[k].z, b[k].z),
+                         __fadd_rn(v[k].w, b[k].w));
   }
   auto sumsq = [&](const float4 (&u)[kTailVec]) {
     float ss = 0.f;
