@@ -116,6 +116,7 @@ SIGNATURES = {
     "ch_ring_activate_slot": (sz, [vp, sz, sz]),
     "ch_ring_deactivate_slot": (None, [vp, sz, sz]),
     "ch_ring_activate_range": (None, [vp, sz, sz, P(u32)]),
+    "ch_rings_fill_steps": (None, [P(vp), P(u32), P(u32), P(u32), u32, sz, P(ChStreamStep), P(u32)]),
     "ch_ring_rollback_clock": (None, [vp, sz]),
     "ch_ring_write_kv_meta": (None, [vp, sz, sz]),
     "ch_ring_write_recall_meta": (None, [vp, sz, sz, sz]),

@@ -68,6 +68,29 @@ extern "C" void ch_ring_activate_range(ch_ring *r, size_t clock0, size_t n, uint
     if (slots_out) slots_out[c - clock0] = (uint32_t)ch_ring_get_slot_index(r, 0, c);
   }
 }
+// One decode step's host work for n streams, each with its own ring: activate the clock's
+// slot in layer 0, then the slot index and the full and sliding lists of layer 0 at that
+// clock (forward.zig:42-45, per stream) straight into the step records and the caller's
+// list storage (lists + b * 8192: active, then sliding).
+extern "C" void ch_rings_fill_steps(ch_ring *const *rings, const uint32_t *streams, const uint32_t *tokens,
+                                    const uint32_t *clocks, uint32_t n, size_t sliding_window, ch_stream_step *steps,
+                                    uint32_t *lists) {
+  for (uint32_t b = 0; b < n; b++) {
+    ch_ring *r = rings[b];
+    const size_t clock = clocks[b];
+    ch_ring_activate_slot(r, 0, clock);
+    uint32_t *act = lists + (size_t)b * 2 * kTotal, *sli = act + kTotal;
+    ch_stream_step &st = steps[b];
+    st.stream = streams[b];
+    st.token = tokens[b];
+    st.clock = (uint32_t)clock;
+    st.slot = (uint32_t)ch_ring_get_slot_index(r, 0, clock);
+    st.active = act;
+    st.n_active = (uint32_t)ch_ring_active_slots(r, 0, clock, 0, sliding_window, act);
+    st.sliding = sli;
+    st.n_sliding = (uint32_t)ch_ring_active_slots(r, 0, clock, 1, sliding_window, sli);
+  }
+}
 extern "C" void ch_ring_deactivate_slot(ch_ring *r, size_t layer, size_t clock) {
   const size_t i = layer * kTotal + ch_ring_get_slot_index(r, layer, clock);
   if (r->clocks[i] == clock) {

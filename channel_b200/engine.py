@@ -287,6 +287,12 @@ class GpuModelContext:
         L.check(L.load().ch_streams_decode(self.handle, arr, len(steps), _ptr(out, C.c_uint32)))
         return out
 
+    def streams_decode_steps(self, steps, n: int) -> np.ndarray:
+        """One batched step from n prepared ChStreamStep records (ch_rings_fill_steps)."""
+        out = np.zeros(n, np.uint32)
+        L.check(L.load().ch_streams_decode(self.handle, steps, n, _ptr(out, C.c_uint32)))
+        return out
+
     def decode_run(self, first_token: int, n_steps: int) -> None:
         L.check(L.load().ch_decode_run(self.handle, first_token, n_steps))
 

@@ -13,11 +13,15 @@ read the active and sliding lists); the reference itself serves one stream
 """
 from __future__ import annotations
 
+import ctypes as C
 from typing import List, Sequence
 
 import numpy as np
 
+from . import _lib as L
 from .engine import DynamicRingBuffer
+
+_u32p = C.POINTER(C.c_uint32)
 
 
 class MultiStreamDecoder:
@@ -30,6 +34,9 @@ class MultiStreamDecoder:
         self.next_token = [0] * n_streams
         self.tokens: List[List[int]] = [[] for _ in range(n_streams)]
         self.steps = 0  # batched decode launches so far
+        # step records and list storage reused by every step (ch_rings_fill_steps)
+        self._step_recs = (L.ChStreamStep * max_batch)()
+        self._lists = np.empty(max_batch * 2 * 4096, np.uint32)
 
     def prefill(self, stream: int, prompt: Sequence[int]) -> int:
         """Prefill the stream's prompt from clock 0, in chunks of at most the model's
@@ -54,12 +61,19 @@ class MultiStreamDecoder:
                 ring.getActiveSlotsLayer(0, clock, True, w))
 
     def step(self, streams: Sequence[int]) -> np.ndarray:
-        """One batched greedy step over distinct streams (<= max_batch); returns their next tokens."""
-        batch = []
-        for s in streams:
-            slot, act, sli = self._step_lists(s)
-            batch.append((s, self.next_token[s], self.clock[s], slot, act, sli))
-        out = self.gm.streams_decode(batch)
+        """One batched greedy step over distinct streams (<= max_batch); returns their next
+        tokens.  The per-stream ring work of _step_lists runs in one C call for the batch."""
+        n = len(streams)
+        if n > self.max_batch:
+            raise ValueError("more streams than max_batch in one step")
+        ids = np.asarray(streams, np.uint32)
+        tokens = np.array([self.next_token[s] for s in streams], np.uint32)
+        clocks = np.array([self.clock[s] for s in streams], np.uint32)
+        rings = (C.c_void_p * n)(*[self.rings[s].h for s in streams])
+        L.load().ch_rings_fill_steps(rings, ids.ctypes.data_as(_u32p), tokens.ctypes.data_as(_u32p),
+                                     clocks.ctypes.data_as(_u32p), n, self.cfg.sliding_window, self._step_recs,
+                                     self._lists.ctypes.data_as(_u32p))
+        out = self.gm.streams_decode_steps(self._step_recs, n)
         for s, t in zip(streams, out):
             self.next_token[s] = int(t)
             self.tokens[s].append(int(t))

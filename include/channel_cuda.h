@@ -277,6 +277,13 @@ size_t ch_ring_activate_slot(ch_ring *r, size_t layer, size_t clock);
  * layer, in clock order, with each clock's layer-0 slot in slots_out (may be NULL) -- the
  * host bookkeeping of a prompt chunk in one call */
 void ch_ring_activate_range(ch_ring *r, size_t clock0, size_t n, uint32_t *slots_out);
+/* no reference counterpart: one ch_streams_decode step's host work for n streams, each
+ * with its own ring -- ch_ring_activate_slot(rings[b], 0, clocks[b]), then the slot index
+ * and the full and sliding lists of layer 0 at that clock -- written into steps[b]
+ * (stream, token, clock, slot, lists) with the lists stored at lists + b * 8192 (active,
+ * then sliding; the caller keeps the storage alive for the step) */
+void ch_rings_fill_steps(ch_ring *const *rings, const uint32_t *streams, const uint32_t *tokens, const uint32_t *clocks,
+                         uint32_t n, size_t sliding_window, ch_stream_step *steps, uint32_t *lists);
 void ch_ring_deactivate_slot(ch_ring *r, size_t layer, size_t clock);
 void ch_ring_rollback_clock(ch_ring *r, size_t target_clock);
 void ch_ring_write_kv_meta(ch_ring *r, size_t layer, size_t clock);
