@@ -43,8 +43,8 @@
 namespace ch {
 
 namespace {
-constexpr int kSkRows = 256;                            // weight rows per CTA: the MMA's N
-constexpr int kSkTiles = kSkRows / 16;                  // Q4 row tiles per CTA
+constexpr int kSkRows = 256;                            // weight rows per CTA at most: the MMA's N
+constexpr int kSkTiles = kSkRows / 16;                  // Q4 row tiles per CTA at most
 constexpr int kSkTok = 64;                              // tokens per launch at most (M = 2 x 64)
 constexpr uint32_t kSkXBytes = 2 * kSkTok * 128;        // 16 KB: 128 rows (hi | lo) x 64 k f16
 constexpr uint32_t kSkWBytes = kSkRows * 128;           // 32 KB: one of W_hi, W_lo
@@ -66,15 +66,18 @@ static_assert(kSkSmemBytes <= 232448, "shared memory per CTA");
 // [4 column groups][2 chunks][64 tokens][33] f32 (row pitch 33: no bank conflicts)
 constexpr uint32_t kSkExPitch = 33;
 static_assert(4 * 2 * kSkTok * kSkExPitch * 4 <= kSkWSt * 2 * kSkWBytes, "exchange fits the W stages");
-// instruction descriptor, kind::f16: D f32, A and B f16, both K-major, N = 256, M = 128
-constexpr uint32_t kSkIdesc = (1u << 4) | ((uint32_t)(kSkRows >> 3) << 17) | ((uint32_t)((2 * kSkTok) >> 4) << 24);
+// instruction descriptor, kind::f16: D f32, A and B f16, both K-major, N = the CTA's
+// weight rows (a multiple of 16, at most 256), M = 128
+constexpr uint32_t sk_idesc(uint32_t n_rows) {
+  return (1u << 4) | ((n_rows >> 3) << 17) | ((uint32_t)((2 * kSkTok) >> 4) << 24);
+}
 }  // namespace
 
-CH_DEV void sk_mma(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
+CH_DEV void sk_mma(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
   asm volatile(
       "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
       " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
-      "l"(adesc), "l"(bdesc), "r"(kSkIdesc), "r"(accumulate)
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
 // arrive on `bar` once every tcgen05 operation this thread issued so far is complete
@@ -89,6 +92,8 @@ struct SkTcArgs {
   const uint8_t *xs;  // [K/64][16 KB] activation blocks (skinny_tc_x_kernel)
   float *partial;     // [splits][B][row_tiles * 16]
   uint32_t row_tiles, K, B, splits;
+  uint32_t tpc;       // Q4 row tiles per CTA (the MMA's N / 16, <= 16)
+  uint32_t idesc;     // sk_idesc(16 tpc)
   uint32_t *err;
 };
 
@@ -139,7 +144,7 @@ __global__ void __launch_bounds__(kSkThreads, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t KT = a.K / 64, split = blockIdx.y;
   const uint32_t k0 = split * KT / a.splits, k1 = (split + 1) * KT / a.splits, nk = k1 - k0;
-  const uint32_t rt0 = blockIdx.x * kSkTiles;
+  const uint32_t rt0 = blockIdx.x * a.tpc;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kSkWSt; s++) {
@@ -189,7 +194,7 @@ __global__ void __launch_bounds__(kSkThreads, 1)
         const int r = i % kSkRaw;
         if (i >= (uint32_t)kSkRaw && !tc_wait(&rempty[r], ((i / kSkRaw) - 1) & 1, abort, a.err)) break;
         // the box always lands whole (row tiles past the matrix read as zeros)
-        mbar_arrive_expect_tx(&rfull[r], kSkRawBytes);
+        mbar_arrive_expect_tx(&rfull[r], a.tpc * kTileBytes);
         tma_load_3d(sm + kSkOffRaw + r * kSkRawBytes, &wmap, 0, (int)(k0 + i), (int)rt0, &rfull[r]);
       }
       for (uint32_t j = i > (uint32_t)kSkRaw ? i - kSkRaw : 0; j < i; j++)
@@ -209,8 +214,8 @@ __global__ void __launch_bounds__(kSkThreads, 1)
         for (int ks = 0; ks < 4; ks++) {
           const uint64_t ko = (uint64_t)(ks * 2);  // 32 B per 16-wide k step, in 16-byte units
           const uint32_t acc = (i | ks) != 0;
-          sk_mma(tmem, xd + ko, wh + ko, acc);                 // D1 += X W_hi^T
-          sk_mma(tmem + (uint32_t)kSkRows, xd + ko, wl + ko, acc);  // D2 += X W_lo^T
+          sk_mma(tmem, xd + ko, wh + ko, a.idesc, acc);                 // D1 += X W_hi^T
+          sk_mma(tmem + (uint32_t)kSkRows, xd + ko, wl + ko, a.idesc, acc);  // D2 += X W_lo^T
         }
         sk_commit(&wempty[s]);
         sk_commit(&xempty[xsl]);
@@ -228,28 +233,30 @@ __global__ void __launch_bounds__(kSkThreads, 1)
           !__all_sync(0xFFFFFFFFu, tc_wait(&wempty[s], ((i / kSkWSt) - 1) & 1, abort, a.err)))
         break;
       const uint32_t Wh = sbase + kSkOffW + s * 2 * kSkWBytes, Wl = Wh + kSkWBytes;
-      const uint8_t *raw = sm + kSkOffRaw + r * kSkRawBytes + j * kTileBytes;
-      const uint4 w = *reinterpret_cast<const uint4 *>(raw + lane * 16);
-      const uint2 sc = *reinterpret_cast<const uint2 *>(raw + 512 + g * 8);  // rows g, g+8: (blk0 | blk1 << 16)
-      uint32_t hs[2][2], ls[2][2];                                          // [row g / g+8][blk]
-      bool ok = split_scale(sc.x & 0xFFFFu, hs[0][0], ls[0][0]);
-      ok &= split_scale(sc.x >> 16, hs[0][1], ls[0][1]);
-      ok &= split_scale(sc.y & 0xFFFFu, hs[1][0], ls[1][0]);
-      ok &= split_scale(sc.y >> 16, hs[1][1], ls[1][1]);
-      if (!ok) atomicOr(a.err, DEV_ERR_SCALE_RANGE);
-      const uint32_t rbase = (2 * j + (mi & 1)) * 1024 + rr * 128;
-      const uint32_t ws[4] = {w.x, w.y, w.z, w.w};  // (blk, ch) = (0,0) (0,1) (1,0) (1,1)
+      if (j < a.tpc) {  // warps past the CTA's row tiles only take part in the barriers
+        const uint8_t *raw = sm + kSkOffRaw + r * kSkRawBytes + j * kTileBytes;
+        const uint4 w = *reinterpret_cast<const uint4 *>(raw + lane * 16);
+        const uint2 sc = *reinterpret_cast<const uint2 *>(raw + 512 + g * 8);  // rows g, g+8: (blk0 | blk1 << 16)
+        uint32_t hs[2][2], ls[2][2];                                          // [row g / g+8][blk]
+        bool ok = split_scale(sc.x & 0xFFFFu, hs[0][0], ls[0][0]);
+        ok &= split_scale(sc.x >> 16, hs[0][1], ls[0][1]);
+        ok &= split_scale(sc.y & 0xFFFFu, hs[1][0], ls[1][0]);
+        ok &= split_scale(sc.y >> 16, hs[1][1], ls[1][1]);
+        if (!ok) atomicOr(a.err, DEV_ERR_SCALE_RANGE);
+        const uint32_t rbase = (2 * j + (mi & 1)) * 1024 + rr * 128;
+        const uint32_t ws[4] = {w.x, w.y, w.z, w.w};  // (blk, ch) = (0,0) (0,1) (1,0) (1,1)
 #pragma unroll
-      for (int wi = 0; wi < 4; wi++) {
-        const int blk = wi >> 1;
-        uint32_t f[4];
-        dequant_q4_word(ws[wi], f);
-        const uint32_t chunk = blk * 4 + (wi & 1) * 2 + (mi >> 1);
-        const uint32_t off = rbase + ((chunk ^ rr) << 4);
-        stmatrix_x4(Wh + off, hmul2_u32(f[0], hs[0][blk]), hmul2_u32(f[1], hs[1][blk]), hmul2_u32(f[2], hs[0][blk]),
-                    hmul2_u32(f[3], hs[1][blk]));
-        stmatrix_x4(Wl + off, hmul2_u32(f[0], ls[0][blk]), hmul2_u32(f[1], ls[1][blk]), hmul2_u32(f[2], ls[0][blk]),
-                    hmul2_u32(f[3], ls[1][blk]));
+        for (int wi = 0; wi < 4; wi++) {
+          const int blk = wi >> 1;
+          uint32_t f[4];
+          dequant_q4_word(ws[wi], f);
+          const uint32_t chunk = blk * 4 + (wi & 1) * 2 + (mi >> 1);
+          const uint32_t off = rbase + ((chunk ^ rr) << 4);
+          stmatrix_x4(Wh + off, hmul2_u32(f[0], hs[0][blk]), hmul2_u32(f[1], hs[1][blk]), hmul2_u32(f[2], hs[0][blk]),
+                      hmul2_u32(f[3], hs[1][blk]));
+          stmatrix_x4(Wl + off, hmul2_u32(f[0], ls[0][blk]), hmul2_u32(f[1], ls[1][blk]), hmul2_u32(f[2], ls[0][blk]),
+                      hmul2_u32(f[3], ls[1][blk]));
+        }
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&rempty[r]);  // the box is read
@@ -290,6 +297,7 @@ __global__ void __launch_bounds__(kSkThreads, 1)
         tc_wait_ld();
         const float *row = ex + ((size_t)(cg * 2 + ch) * kSkTok + t) * kSkExPitch;
         const uint32_t r0 = rt0 * 16 + col;
+        const uint32_t rend = min((uint32_t)R16, (rt0 + a.tpc) * 16);  // this CTA's rows
         if (t < a.B) {
           float y[32];
 #pragma unroll
@@ -297,14 +305,14 @@ __global__ void __launch_bounds__(kSkThreads, 1)
             const float corr = __fadd_rn(row[i], __uint_as_float(v2[i]));
             y[i] = __fmaf_rn(corr, 1.0f / 65536.f, __fmul_rn(__uint_as_float(v1[i]), 1.0f / 256.f));
           }
-          if (r0 + 32 <= R16) {  // whole chunk: 16-byte stores (R16 and r0 are multiples of 16)
+          if (r0 + 32 <= rend) {  // whole chunk: 16-byte stores (rend and r0 are multiples of 16)
 #pragma unroll
             for (int i = 0; i < 32; i += 4)
               *reinterpret_cast<float4 *>(pr + r0 + i) = make_float4(y[i], y[i + 1], y[i + 2], y[i + 3]);
           } else {
 #pragma unroll
             for (int i = 0; i < 32; i++)
-              if (r0 + i < R16) pr[r0 + i] = y[i];
+              if (r0 + i < rend) pr[r0 + i] = y[i];
           }
         }
       }
@@ -434,10 +442,17 @@ cudaError_t launch_skinny_tail(const float *partial, uint32_t splits, uint32_t B
 }
 
 // ---------------------------------------------------------------------------
-// K splits: as many CTAs as fit the SMs in one wave (the rows alone give too few for
-// o and down), at most one per k tile
+// Row tiles per CTA: 16 (N = 256), or fewer when 12-15 per SM cover the rows in one wave
+// (an MMA costs about the same at N = 208 as at 256, so the idle SMs of 16-tile groups
+// would be lost: 1,920 row tiles make 148 CTAs of 13 instead of 120 of 16).  K splits:
+// as many CTAs as fit the SMs in one wave (the rows alone give too few for o and down),
+// at most one per k tile.
+static uint32_t skinny_tc_tpc(uint32_t row_tiles) {
+  const uint32_t sms = (uint32_t)num_sms(), per_sm = (row_tiles + sms - 1) / sms;
+  return per_sm >= 12 && per_sm < (uint32_t)kSkTiles ? per_sm : (uint32_t)kSkTiles;
+}
 uint32_t skinny_tc_splits(uint32_t row_tiles, uint32_t K) {
-  const uint32_t ctas = (row_tiles + kSkTiles - 1) / kSkTiles;
+  const uint32_t tpc = skinny_tc_tpc(row_tiles), ctas = (row_tiles + tpc - 1) / tpc;
   return std::max(1u, std::min((uint32_t)num_sms() / std::max(1u, ctas), K / 64));
 }
 size_t skinny_tc_x_bytes(uint32_t K) { return (size_t)(K / 64) * kSkXBytes; }
@@ -445,29 +460,30 @@ size_t skinny_tc_partial_floats(uint32_t B, uint32_t row_tiles, uint32_t K) {
   return (size_t)skinny_tc_splits(row_tiles, K) * B * row_tiles * 16;
 }
 
-// tensor maps of the weight matrices, encoded once per (tiles, rows, K)
-static cudaError_t tile_map_cached(const uint8_t *tiles, uint32_t M, uint32_t K, CUtensorMap *out) {
+// tensor maps of the weight matrices, encoded once per (tiles, rows, K, box rows)
+static cudaError_t tile_map_cached(const uint8_t *tiles, uint32_t M, uint32_t K, uint32_t box, CUtensorMap *out) {
   struct Key {
     const uint8_t *p;
-    uint32_t M, K;
-    bool operator==(const Key &o) const { return p == o.p && M == o.M && K == o.K; }
+    uint32_t M, K, box;
+    bool operator==(const Key &o) const { return p == o.p && M == o.M && K == o.K && box == o.box; }
   };
   struct Hash {
     size_t operator()(const Key &k) const {
-      return std::hash<const void *>()(k.p) ^ ((size_t)k.M * 0x9E3779B97F4A7C15ull) ^ ((size_t)k.K << 1);
+      return std::hash<const void *>()(k.p) ^ ((size_t)k.M * 0x9E3779B97F4A7C15ull) ^ ((size_t)k.K << 1) ^
+             ((size_t)k.box << 40);
     }
   };
   static std::mutex mu;
   static std::unordered_map<Key, CUtensorMap, Hash> cache;
   std::lock_guard<std::mutex> lock(mu);
-  const Key key{tiles, M, K};
+  const Key key{tiles, M, K, box};
   auto it = cache.find(key);
   if (it != cache.end()) {
     std::memcpy(out, &it->second, sizeof(CUtensorMap));
     return cudaSuccess;
   }
   alignas(64) CUtensorMap m;
-  cudaError_t e = encode_tile_map(&m, tiles, M, K, kSkTiles);
+  cudaError_t e = encode_tile_map(&m, tiles, M, K, box);
   if (e != cudaSuccess) return e;
   if (cache.size() > 4096) cache.clear();
   cache.emplace(key, m);
@@ -492,10 +508,13 @@ cudaError_t launch_skinny_q4_tc(const uint8_t *tiles, uint32_t row_tiles, uint32
     e = cudaGetLastError();
     if (e != cudaSuccess) return e;
   }
+  const uint32_t tpc = skinny_tc_tpc(row_tiles);
   alignas(64) CUtensorMap wmap;
-  e = tile_map_cached(tiles, row_tiles * 16, K, &wmap);
+  e = tile_map_cached(tiles, row_tiles * 16, K, tpc, &wmap);
   if (e != cudaSuccess) return e;
   SkTcArgs a{};
+  a.tpc = tpc;
+  a.idesc = sk_idesc(16 * tpc);
   a.xs = xs;
   a.partial = partial;
   a.row_tiles = row_tiles;
@@ -506,7 +525,7 @@ cudaError_t launch_skinny_q4_tc(const uint8_t *tiles, uint32_t row_tiles, uint32
   *splits = a.splits;
   e = cudaFuncSetAttribute(skinny_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSkSmemBytes);
   if (e != cudaSuccess) return e;
-  const dim3 grid((row_tiles + kSkTiles - 1) / kSkTiles, a.splits);
+  const dim3 grid((row_tiles + tpc - 1) / tpc, a.splits);
   skinny_tc_kernel<<<grid, kSkThreads, kSkSmemBytes, s>>>(a, wmap);
   return cudaGetLastError();
 }
