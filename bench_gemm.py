@@ -6,8 +6,8 @@ tcgen05 CTA-pair kernel) against the legacy mma.sync kernels
 shapes, with synthetic Q4 weights from the device generator and CUDA events on
 the library's stream.  TF/s are algorithmic (2 x tokens x weights).
 
-  python -m channel_b200.gemm_bench [--tokens 512]
-  python -m channel_b200.gemm_bench --only gateup12b --launches 3   # e.g. under ncu -k regex:batch_gemm_tc
+  python bench_gemm.py [--tokens 512]
+  python bench_gemm.py --only gateup12b --launches 3   # e.g. under ncu -k regex:batch_gemm_tc
 """
 from __future__ import annotations
 

@@ -18,8 +18,8 @@ A phase's cost is taken from the slowest CTA at each point (the grid waits for
 it); the per-CTA table shows median / max of each interval for layer 1.
 Usage (one GPU):
 
-  python -m channel_b200.phase_trace [--layers 48] [--steps 4] [--clock 599] [--lib PATH]
-  torchrun --nproc-per-node N -m channel_b200.phase_trace   # tensor parallel, rank 0 prints
+  python bench_phases.py [--layers 48] [--steps 4] [--clock 599] [--lib PATH]
+  torchrun --nproc-per-node N bench_phases.py   # tensor parallel, rank 0 prints
 """
 from __future__ import annotations
 

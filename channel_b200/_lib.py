@@ -41,6 +41,21 @@ class ChLayerWeights(C.Structure):
     ]
 
 
+class ChLayerWeightsBf16(C.Structure):
+    _fields_ = [
+        ("q_proj", P(u16)), ("k_proj", P(u16)), ("v_proj", P(u16)), ("o_proj", P(u16)),
+        ("gate_proj", P(u16)), ("up_proj", P(u16)), ("down_proj", P(u16)),
+        ("input_norm", P(u16)), ("q_norm", P(u16)), ("k_norm", P(u16)), ("post_attn_norm", P(u16)),
+        ("pre_ffn_norm", P(u16)), ("post_ffn_norm", P(u16)), ("layer_scalar", f32),
+    ]
+
+
+class ChSamplerParams(C.Structure):
+    _fields_ = [("temp", f32), ("top_p", f32), ("min_p", f32), ("repeat_penalty", f32), ("frequency_penalty", f32),
+                ("presence_penalty", f32), ("top_k", u32), ("suppress_thinking", u8), ("suppress_critique", u8),
+                ("suppress_channel_close", u8), ("reserved", u8)]
+
+
 class ChStepDesc(C.Structure):
     _fields_ = [("clock", u32), ("slot", u32), ("n_active", u32), ("n_sliding", u32),
                 ("active", P(u32)), ("sliding", P(u32))]
@@ -64,6 +79,7 @@ SIGNATURES = {
     "ch_ctx_device_status": (i32, [vp, P(u32)]),
     "ch_model_create": (i32, [vp, P(ChModelConfig), P(ChLayerWeights), P(u32), P(f32), P(u16), P(vp)]),
     "ch_model_create_synthetic": (i32, [vp, P(ChModelConfig), u64, P(vp)]),
+    "ch_model_create_bf16": (i32, [vp, P(ChModelConfig), P(ChLayerWeightsBf16), P(u16), P(u16), P(vp)]),
     "ch_model_create_synthetic_sharded": (i32, [vp, P(ChModelConfig), u64, u32, u32, P(vp)]),
     "ch_model_exchange_handle": (i32, [vp, vp]),
     "ch_model_attach_peers": (i32, [vp, vp]),
@@ -71,7 +87,7 @@ SIGNATURES = {
     "ch_model_zero_state": (i32, [vp]),
     "ch_model_weight_tiles": (i32, [vp, u32, i32, P(vp), P(u32), P(u32)]),
     "ch_forward_token": (i32, [vp, P(f32), u32, u32, P(u32), u32, P(u32), u32, P(ChTopk), P(u32)]),
-    "ch_prefill": (i32, [vp, P(u32), u32, P(u16), P(u32), u32, u32, P(ChTopk), PROGRESS_FN, vp]),
+    "ch_prefill": (i32, [vp, P(u32), u32, P(u16), P(u32), u32, u32, P(ChTopk), P(f32), sz, PROGRESS_FN, vp]),
     "ch_read_x": (i32, [vp, P(f32)]),
     "ch_read_normed_x": (i32, [vp, P(f32)]),
     "ch_kv_read": (i32, [vp, u32, u32, P(f32), P(f32)]),
@@ -80,6 +96,13 @@ SIGNATURES = {
     "ch_streams_init": (i32, [vp, u32, u32]),
     "ch_stream_prefill": (i32, [vp, u32, P(u32), u32, P(u32), u32, u32, P(u32)]),
     "ch_streams_decode": (i32, [vp, P(ChStreamStep), u32, P(u32)]),
+    "ch_streams_read_normed_x": (i32, [vp, u32, P(f32)]),
+    "ch_sampler_create": (i32, [vp, P(ChSamplerParams), u64, u32, P(vp)]),
+    "ch_sampler_destroy": (None, [vp]),
+    "ch_sampler_set_recent": (i32, [vp, P(u32), u32]),
+    "ch_sampler_sample_topk": (i32, [vp, vp, vp, u32, vp, u32, vp]),
+    "ch_model_set_sampler": (i32, [vp, vp]),
+    "ch_streams_read_logits": (i32, [vp, u32, P(f32)]),
     "ch_decode_run": (i32, [vp, u32, u32]),
     "ch_decode_continue": (i32, [vp, u32]),
     "ch_decode_tokens": (i32, [vp, P(u32), u32]),
@@ -126,6 +149,12 @@ SIGNATURES = {
     "ch_ring_slot_clock": (sz, [vp, sz, sz]),
     "ch_ring_active_slots": (sz, [vp, sz, sz, i32, sz, P(u32)]),
     "ch_ring_prefill_prev_slots": (sz, [vp, sz, sz, sz, P(u32)]),
+    "ch_ring_dev_create": (i32, [vp, P(vp)]),
+    "ch_ring_dev_destroy": (None, [vp]),
+    "ch_ring_dev_upload": (i32, [vp, vp]),
+    "ch_ring_dev_lists": (i32, [vp, u32, i32, sz, vp, vp, vp, vp, vp]),
+    "ch_ring_dev_prefill_prev": (i32, [vp, u32, u32, vp, vp]),
+    "ch_decode_run_ring": (i32, [vp, vp, vp, u32, u32, u32]),
 }
 
 _lib = None

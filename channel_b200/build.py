@@ -5,6 +5,7 @@ nothing is installed into site-packages.  Usage: ``python -m channel_b200.build`
 """
 from __future__ import annotations
 
+import concurrent.futures
 import os
 import shutil
 import subprocess
@@ -48,7 +49,7 @@ def build(verbose: bool = False, force: bool = False, trace: bool = False) -> Pa
     obj_dir.mkdir(exist_ok=True)
     headers = list(CSRC.glob("*.cuh")) + [ROOT / "include" / "channel_cuda.h"]
     newest_hdr = max(h.stat().st_mtime for h in headers)
-    objs = []
+    objs, cmds = [], []
     for src in sources():
         obj = obj_dir / (src.name + ".o")
         objs.append(obj)
@@ -57,9 +58,14 @@ def build(verbose: bool = False, force: bool = False, trace: bool = False) -> Pa
         cmd = [nvcc, *NVCC_FLAGS, *extra, "-c", str(src), "-o", str(obj)]
         if src.suffix == ".cpp":
             cmd = [nvcc, "-x", "cu", *cmd[1:]]
-        if verbose:
-            print(" ".join(cmd), flush=True)
-        subprocess.run(cmd, check=True)
+        cmds.append(cmd)
+    # independent translation units: compile them side by side
+    with concurrent.futures.ThreadPoolExecutor(max_workers=max(1, min(len(cmds), os.cpu_count() or 1))) as ex:
+        for cmd in cmds:
+            if verbose:
+                print(" ".join(cmd), flush=True)
+        for f in [ex.submit(subprocess.run, cmd, check=True) for cmd in cmds]:
+            f.result()
     if force or not out.exists() or out.stat().st_mtime < max(o.stat().st_mtime for o in objs):
         cmd = [nvcc, "-shared", "-gencode", "arch=compute_100a,code=sm_100a", *map(str, objs), "-o", str(out),
                "-lcudart"]

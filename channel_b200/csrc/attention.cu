@@ -193,7 +193,7 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attn_kernel(const AttnArg
 
   // ---- chunk max / exp / sum per q head (warp h handles head h) ----
   for (int h = warp; h < R; h += kAttnWarps) {
-    float m = -1e9f;  // decode_attn.wgsl:261
+    float m = -1e9f;  // decode_attn.wgsl:81
     for (uint32_t i = lane; i < n; i += 32) m = fmaxf(m, sc[h * chunk_cap + i]);
     m = warp_max(m);
     float l = 0.f;
@@ -308,11 +308,9 @@ static cudaError_t launch_attn_t(const AttnArgs &a, int splits, cudaStream_t s, 
   const size_t smem = sizeof(float) * ((size_t)(R + 2) * 256 + (size_t)kAttnWarps * R * 256 + (size_t)R * chunk_cap +
                                        (size_t)R * splits) +
                       sizeof(uint32_t) * (size_t)chunk_cap;
-  static size_t attr_bytes = 0;  // dynamic smem opt-in granted so far
-  if (smem > 48 * 1024 && smem > attr_bytes) {
-    cudaError_t e = cudaFuncSetAttribute(decode_attn_kernel<R>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  {
+    const cudaError_t e = ensure_smem_attr((const void *)decode_attn_kernel<R>, smem);
     if (e != cudaSuccess) return e;
-    attr_bytes = smem;
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(a.nkv, splits, a.n_tok);

@@ -1,7 +1,7 @@
 // decode_step.cu -- one greedy decode token as ONE persistent kernel.
 //
 // Replaces the reference's per-token command buffer of ~12 dispatches per layer
-// (src/gpu/model_dispatch.zig:226-342: fused_qkv_q4, qkv_rope, decode_attn,
+// (src/gpu/model_dispatch.zig:10-45,103-126: fused_qkv_q4, qkv_rope, decode_attn,
 // gemv_q4(O), rmsnorm/add_rmsnorm, fused_mlp_q4, gemv_q4(down), ..., gemv_q8 +
 // topk_pass1/2) with a phase list executed by a cooperative grid of one CTA per
 // SM:
@@ -59,7 +59,7 @@ constexpr uint32_t kMaxGrid = 255;  // straddle-list entries hold CTA ids in 8 b
 
 int mk_warps() { return MK_NW; }
 
-// Optional per-phase timeline (build with -DCH_PHASE_TRACE, see channel_b200/phase_trace.py):
+// Optional per-phase timeline (build with -DCH_PHASE_TRACE, see bench_phases.py):
 // thread 0 of every CTA records %globaltimer at seven points of each phase.
 #ifdef CH_PHASE_TRACE
 constexpr int kTraceCtas = 256, kTracePhases = 512, kTraceMarks = 8;
@@ -947,7 +947,7 @@ CH_DEV void attn_phase(const Phase &p, const MegaArgs &a, const StepParams &sp, 
     if (!valid && lane == 0) atomicOr(a.err, DEV_ERR_BAD_LIST);
   }
   __syncthreads();
-  // 3. softmax statistics per head over this chunk (max seeded at -1e9, decode_attn.wgsl:261)
+  // 3. softmax statistics per head over this chunk (max seeded at -1e9, decode_attn.wgsl:81)
   for (int h = warp; h < R; h += MK_NW) {
     float m = -1e9f;
     for (uint32_t i = lane; i < n; i += 32) m = fmaxf(m, sm.sc[h * chunk_cap + i]);
@@ -1381,11 +1381,9 @@ size_t mk_smem_bytes(uint32_t max_k, uint32_t hidden, uint32_t ratio, uint32_t m
 
 template <int R>
 static cudaError_t launch_decode_step_t(const MegaArgs &a, size_t smem, cudaStream_t s) {
-  static size_t attr = 0;
-  if (smem > attr) {
-    cudaError_t e = cudaFuncSetAttribute(decode_step_kernel<R>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  {
+    const cudaError_t e = ensure_smem_attr((const void *)decode_step_kernel<R>, smem);
     if (e != cudaSuccess) return e;
-    attr = smem;
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(a.grid);

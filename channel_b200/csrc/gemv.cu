@@ -22,6 +22,10 @@
 // separate norm kernel runs on the decode path.
 #include <cmath>
 
+#include <atomic>
+#include <map>
+#include <mutex>
+
 #include "common.cuh"
 #include "core.cuh"
 #include "kernels.cuh"
@@ -43,14 +47,29 @@ constexpr int kStageBytes = CT * kTileBytes;
 }  // namespace
 
 int num_sms() {
-  static int n = 0;
-  if (n == 0) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-    if (n <= 0) n = 148;
-  }
+  constexpr int kMaxDev = 64;
+  static std::atomic<int> cache[kMaxDev];  // zero: not looked up yet
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) dev = 0;
+  int n = (dev >= 0 && dev < kMaxDev) ? cache[dev].load(std::memory_order_relaxed) : 0;
+  if (n > 0) return n;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+  if (dev >= 0 && dev < kMaxDev) cache[dev].store(n, std::memory_order_relaxed);
   return n;
+}
+cudaError_t ensure_smem_attr(const void *func, size_t smem) {
+  if (smem <= 48 * 1024) return cudaSuccess;
+  static std::mutex mu;
+  static std::map<std::pair<int, const void *>, size_t> granted;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  std::lock_guard<std::mutex> lock(mu);
+  size_t &g = granted[{dev, func}];
+  if (smem <= g) return cudaSuccess;
+  e = cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e == cudaSuccess) g = smem;
+  return e;
 }
 int gemv_default_grid() { return num_sms(); }
 size_t gemv_partial_floats(int grid) { return (size_t)grid * NW * 2 * 16; }
@@ -322,12 +341,9 @@ template <int FMT, int EPI, int PRO>
 static cudaError_t launch_gemv_t(const GemvArgs &a, int grid, cudaStream_t s, bool pdl) {
   size_t smem = (size_t)NW * SPW * kStageBytes + NW * SPW * 8 + (size_t)(a.K / 32) * (128 + 4);
   if (PRO != PRO_NONE) smem += (size_t)a.K * 4;
-  static size_t attr_bytes = 0;  // dynamic smem opt-in granted so far (static smem counts against 227 KB)
-  if (smem > 48 * 1024 && smem > attr_bytes) {
-    cudaError_t e =
-        cudaFuncSetAttribute(gemv_kernel<FMT, EPI, PRO>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  {
+    const cudaError_t e = ensure_smem_attr((const void *)gemv_kernel<FMT, EPI, PRO>, smem);
     if (e != cudaSuccess) return e;
-    attr_bytes = smem;
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);

@@ -1,6 +1,7 @@
 // kernels.cuh -- host-side launch interface of the device kernels (internal to
 // libchannel_b200; the public boundary is include/channel_cuda.h).
 #pragma once
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stddef.h>
 #include <stdint.h>
@@ -49,7 +50,13 @@ struct GemvPlan {
   int grid = 0;
 };
 
+// SM count of the CURRENT device (cached per device)
 int num_sms();
+// Opt `func` in to `smem` bytes of dynamic shared memory on the CURRENT device.
+// cudaFuncSetAttribute is per device, so the granted size is remembered per
+// (device, kernel) under a lock; a second GPU in the same process gets its own
+// opt-in instead of inheriting the first one's.
+cudaError_t ensure_smem_attr(const void *func, size_t smem);
 // scratch sizes needed by gemv for a given grid
 size_t gemv_partial_floats(int grid);
 int gemv_default_grid();
@@ -175,6 +182,52 @@ size_t skinny_x_words(uint32_t B, uint32_t K);
 cudaError_t launch_argmax_rows(const float *logits, uint32_t n, uint32_t V, uint32_t *ids, cudaStream_t s);
 
 // embedding + step advance for the device-resident decode loop
+// Device copy of one DynamicRingBuffer's layer-0 slot metadata (src/ring_buffer.zig:
+// 21-44): the decode step's slot lists come from layer 0 (forward.zig:44-45).
+constexpr uint32_t kRingSlots = 4096, kRingRecallStart = 4096 - 128, kRingMaxBoundaries = 1024;
+struct RingDevState {
+  uint32_t anchors, window, nb, ingested;  // window = windowSize(0); nb = boundaries marked so far
+  uint32_t next_clock, step, pad0, pad1;   // device loop: clock of its next step, steps taken
+  uint32_t clocks[kRingSlots];
+  uint32_t boundary[kRingMaxBoundaries];   // turn boundaries, slot i % 1024 (markBoundary)
+  uint8_t active[kRingSlots];
+};
+struct RingStepArgs {
+  RingDevState *ring = nullptr;
+  uint32_t clock = 0, sliding_window = 0, chunk_len = 0;
+  int activate = 0;  // activateSlot(0, clock) first
+  int prev = 0;      // getPrefillPrevSlots(0, clock, chunk_len) into active_out instead
+  int loop = 0;      // clock = ring->next_clock, then advance it (device loop)
+  uint32_t *slot_out = nullptr, *active_out = nullptr, *n_active_out = nullptr, *sliding_out = nullptr,
+           *n_sliding_out = nullptr;
+  StepParams *sp = nullptr;  // also write the step's StepParams here (lists = active_out / sliding_out)
+};
+cudaError_t launch_ring_step(const RingStepArgs &a, cudaStream_t s);
+
+// Sampler fields (src/sampler.zig:55-66); same layout as ch_sampler_params
+struct SamplerParams {
+  float temp, top_p, min_p, repeat_penalty, frequency_penalty, presence_penalty;
+  uint32_t top_k;
+  uint8_t suppress_thinking, suppress_critique, suppress_channel_close, reserved;
+};
+struct SampleArgs {
+  const uint32_t *ids = nullptr;  // candidates, value descending (top-64)
+  const float *vals = nullptr;
+  uint32_t n = 0;
+  const uint32_t *recent = nullptr;  // recent tokens (NULL: none)
+  uint32_t n_recent = 0;
+  uint32_t *n_recent_dev = nullptr;  // device loop: the list length lives on the device ...
+  uint32_t *recent_w = nullptr;      // ... and the sampled token is appended here
+  uint32_t recent_cap = 0;
+  SamplerParams p{};
+  uint64_t *prng = nullptr;          // [4] Xoshiro256++ state
+  uint32_t *token_out = nullptr;
+  const StepParams *sp = nullptr;    // device loop: history slot of the step
+  uint32_t *token_hist = nullptr;
+  uint32_t hist_cap = 0;
+};
+cudaError_t launch_sample_topk(const SampleArgs &a, cudaStream_t s);
+
 struct StepBeginArgs {
   const uint16_t *embed;  // bf16 [V][H]
   uint32_t H;

@@ -318,11 +318,9 @@ size_t lmhead_frag_words(uint32_t B, uint32_t K) { return (size_t)K / 32 * lmhea
 template <int NG>
 static cudaError_t launch_lmhead_t(const LmHeadArgs &a, cudaStream_t s) {
   const size_t smem = (size_t)2 * kKc * NG * 32 * 16 + (size_t)kLw * 2 * kKc * kTileBytes + (2 + 2 * kLw) * 8;
-  static size_t attr = 0;
-  if (smem > attr) {
-    cudaError_t e = cudaFuncSetAttribute(lmhead_q8_kernel<NG>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  {
+    const cudaError_t e = ensure_smem_attr((const void *)lmhead_q8_kernel<NG>, smem);
     if (e != cudaSuccess) return e;
-    attr = smem;
   }
   const uint32_t grid = (a.row_tiles + kLw - 1) / kLw;
   lmhead_q8_kernel<NG><<<grid, kLw * 32, smem, s>>>(a);
@@ -340,11 +338,9 @@ uint32_t skinny_splits(uint32_t row_tiles, uint32_t K) {
 template <int NG>
 static cudaError_t launch_skinny_t(const SkinnyArgs &a, cudaStream_t s) {
   const size_t smem = (size_t)2 * 2 * kKc * NG * 32 * 16 + (size_t)kLw * 2 * kKc * kTileBytes + (2 + 2 * kLw) * 8;
-  static size_t attr = 0;
-  if (smem > attr) {
-    cudaError_t e = cudaFuncSetAttribute(skinny_q4_kernel<NG>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  {
+    const cudaError_t e = ensure_smem_attr((const void *)skinny_q4_kernel<NG>, smem);
     if (e != cudaSuccess) return e;
-    attr = smem;
   }
   skinny_q4_kernel<NG><<<dim3((a.row_tiles + kLw - 1) / kLw, a.splits), kLw * 32, smem, s>>>(a);
   return cudaGetLastError();

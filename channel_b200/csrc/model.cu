@@ -6,7 +6,7 @@
 // Reference interfaces replaced (Sullux/channel):
 //   GpuContext.init/deinit            src/gpu/context.zig:17-109
 //   GpuModelContext.init/deinit       src/gpu/model_gpu.zig:68-216
-//   recordForwardGraph / gpuDispatchForwardToken  src/gpu/model_dispatch.zig:226-369
+//   recordForwardGraph / gpuDispatchForwardToken  src/gpu/model_dispatch.zig:103-153
 //   gpuDispatchPrefillBatch           src/gpu/batch_dispatch.zig:27-172
 #include <algorithm>
 #include <cmath>
@@ -209,6 +209,7 @@ struct ch_model {
   cudaGraphExec_t g_host_logits = nullptr, g_host_nologits = nullptr, g_loop = nullptr;
   bool pdl = true;
   // device loop plan
+  ch_sampler *sampler = nullptr;  // device loops sample with it (NULL: greedy)
   StepParams *plan = nullptr;
   uint32_t *plan_lists = nullptr;
   uint32_t plan_steps = 0, hist_cap = 0, loop_pos = 0;
@@ -789,6 +790,124 @@ extern "C" int ch_model_create(ch_ctx *ctx, const ch_model_config *cfg, const ch
   return CH_OK;
 }
 
+// GpuModelContext.init with quantize-on-load (src/gpu/model_gpu.zig:44-55,109-127,157):
+// the caller hands over the bf16 weights it mapped from safetensors; every projection
+// is uploaded and quantized to Q4_0 on the device (quantizeRowQ4_0, quant.zig:58-98 --
+// the same kernel as ch_quantize_q4_rows, bit-exact with quant.zig), then repacked like
+// ch_model_create's blocks; the tied embedding becomes the Q8_0 LM head
+// (model_gpu.zig:157) and stays on the device for the embedding lookup.  Norms are
+// bf16 -> f32 (createNormBuffer, model_gpu.zig:57-66): a NULL input / q / k / pre-FFN /
+// final norm is all ones like a missing tensor there, a NULL post-attention / post-FFN
+// norm means the layer has none (has_post_*_norm, model_dispatch.zig:35,41); a NULL
+// v_proj takes k_proj (attention_k_eq_v, model_gpu.zig:114).
+extern "C" int ch_model_create_bf16(ch_ctx *ctx, const ch_model_config *cfg, const ch_layer_weights_bf16 *lw,
+                                    const uint16_t *embed_bf16, const uint16_t *final_norm_bf16, ch_model **out) {
+  if (!ctx || !out || !lw || !embed_bf16) return fail(CH_EINVAL, "NULL argument (the tied embedding is required)");
+  CH_TRY(check_cfg(cfg));
+  CH_CUDA(cudaSetDevice(ctx->device));
+  ch_model *m = new ch_model();
+  m->ctx = ctx;
+  m->cfg = *cfg;
+  int r = alloc_model_buffers(m);
+  if (r != CH_OK) {
+    free_model(m);
+    return r;
+  }
+  cudaStream_t s = ctx->stream;
+  const size_t max_elems = std::max({(size_t)m->qd * m->H, (size_t)m->kvd * m->H, (size_t)m->I * m->H});
+  size_t max_words = std::max({(size_t)(m->qd + 2 * m->kvd) * (m->H / 32) * 5, (size_t)m->H * (m->qd / 32) * 5,
+                               (size_t)m->I * (m->H / 32) * 5, (size_t)m->H * (m->I / 32) * 5});
+  uint32_t *tA = nullptr, *tB = nullptr;
+  uint16_t *tb = nullptr;
+  auto bail = [&](int code) {
+    cudaFree(tA);
+    cudaFree(tB);
+    cudaFree(tb);
+    free_model(m);
+    return code;
+  };
+  if (dmalloc(&tA, max_words) != CH_OK || dmalloc(&tB, max_words) != CH_OK || dmalloc(&tb, max_elems) != CH_OK)
+    return bail(CH_ENOMEM);
+  // one bf16 matrix (rows x cols, row-major) -> quant.zig Q4 blocks at dst
+  auto quant = [&](const uint16_t *host, uint32_t rows, uint32_t cols, uint32_t *dst) -> int {
+    if (!host) return fail(CH_EINVAL, "NULL weight pointer");
+    CH_CUDA(cudaMemcpyAsync(tb, host, (size_t)rows * cols * 2, cudaMemcpyHostToDevice, s));
+    CH_CUDA(launch_quantize_q4_rows(tb, rows, cols, dst, s));
+    CH_CUDA(cudaStreamSynchronize(s));  // tb is reused by the next matrix
+    return CH_OK;
+  };
+  // bf16 norm -> f32 on the device; NULL: all ones, or (optional) no norm at all
+  auto norm = [&](float **dst, const uint16_t *host, uint32_t n, bool optional) -> int {
+    if (!host && optional) return CH_OK;
+    if (!*dst) CH_TRY(dmalloc(dst, n));
+    if (host) {
+      CH_CUDA(cudaMemcpyAsync(tb, host, (size_t)n * 2, cudaMemcpyHostToDevice, s));
+      CH_CUDA(launch_bf16_to_f32(tb, *dst, n, s));
+    } else {
+      const std::vector<float> ones(n, 1.0f);
+      CH_CUDA(cudaMemcpyAsync(*dst, ones.data(), (size_t)n * 4, cudaMemcpyHostToDevice, s));
+    }
+    CH_CUDA(cudaStreamSynchronize(s));
+    return CH_OK;
+  };
+  const size_t qw = (size_t)m->qd * (m->H / 32) * 5, kw = (size_t)m->kvd * (m->H / 32) * 5;
+  for (uint32_t l = 0; l < m->L; l++) {
+    const ch_layer_weights_bf16 &w = lw[l];
+    DevLayer &dl = m->layers[l];
+    int rc = CH_OK;
+    auto lfail = [&](const char *what) { return bail(fail(rc, "layer " + std::to_string(l) + " " + what + ": " + g_err)); };
+    if ((rc = quant(w.q_proj, m->qd, m->H, tA)) || (rc = quant(w.k_proj, m->kvd, m->H, tA + qw)) ||
+        (rc = quant(w.v_proj ? w.v_proj : w.k_proj, m->kvd, m->H, tA + qw + kw)))
+      return lfail("q|k|v");
+    if (launch_repack_q4(tA, nullptr, m->qd + 2 * m->kvd, m->H, MAP_PLAIN, dl.qkv, s) != cudaSuccess)
+      return bail(fail(CH_ECUDA, "repack qkv"));
+    if ((rc = quant(w.o_proj, m->H, m->qd, tB))) return lfail("o_proj");
+    if (launch_repack_q4(tB, nullptr, m->H, m->qd, MAP_PLAIN, dl.o, s) != cudaSuccess)
+      return bail(fail(CH_ECUDA, "repack o"));
+    CH_CUDA(cudaStreamSynchronize(s));
+    if ((rc = quant(w.gate_proj, m->I, m->H, tA)) || (rc = quant(w.up_proj, m->I, m->H, tB))) return lfail("gate/up");
+    if (launch_repack_q4(tA, tB, 2 * m->I, m->H, MAP_GATEUP, dl.gateup, s) != cudaSuccess)
+      return bail(fail(CH_ECUDA, "repack gate/up"));
+    CH_CUDA(cudaStreamSynchronize(s));
+    if ((rc = quant(w.down_proj, m->H, m->I, tA))) return lfail("down_proj");
+    if (launch_repack_q4(tA, nullptr, m->H, m->I, MAP_PLAIN, dl.down, s) != cudaSuccess)
+      return bail(fail(CH_ECUDA, "repack down"));
+    CH_CUDA(cudaStreamSynchronize(s));
+    if ((rc = norm(&dl.input_norm, w.input_norm, m->H, false)) || (rc = norm(&dl.q_norm, w.q_norm, m->D, false)) ||
+        (rc = norm(&dl.k_norm, w.k_norm, m->D, false)) || (rc = norm(&dl.pre_ffn, w.pre_ffn_norm, m->H, false)) ||
+        (rc = norm(&dl.post_attn, w.post_attn_norm, m->H, true)) ||
+        (rc = norm(&dl.post_ffn, w.post_ffn_norm, m->H, true)))
+      return lfail("norms");
+    dl.scalar = w.layer_scalar;
+  }
+  if (int rc = norm(&m->final_norm, final_norm_bf16, m->H, false)) return bail(rc);
+  cudaFree(tA);
+  cudaFree(tB);
+  cudaFree(tb);
+  tA = tB = nullptr;
+  tb = nullptr;
+  if (dmalloc(&m->embed, (size_t)m->V * m->H) != CH_OK) return bail(CH_ENOMEM);
+  if (cudaMemcpyAsync(m->embed, embed_bf16, (size_t)m->V * m->H * 2, cudaMemcpyHostToDevice, s) != cudaSuccess)
+    return bail(fail(CH_ECUDA, "embed upload"));
+  {
+    const uint32_t chunk_rows = 16384;
+    uint32_t *tq = nullptr;
+    if (dmalloc(&tq, (size_t)chunk_rows * (m->H / 32) * 9) != CH_OK) return bail(CH_ENOMEM);
+    for (uint32_t r0 = 0; r0 < m->V; r0 += chunk_rows) {
+      const uint32_t nr = std::min(chunk_rows, m->V - r0);
+      launch_quantize_q8_rows(m->embed + (size_t)r0 * m->H, nr, m->H, tq, s);
+      launch_repack_q8(tq, nr, m->H, m->lm + q8_tile_bytes(r0, m->H), s);
+    }
+    cudaStreamSynchronize(s);
+    cudaFree(tq);
+  }
+  const cudaError_t e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess) return bail(fail(CH_ECUDA, std::string("bf16 model upload: ") + cudaGetErrorString(e)));
+  if (int r2 = init_decode_step(m)) return bail(r2);
+  *out = m;
+  return CH_OK;
+}
+
 // tensor ids of the synthetic generator (shared with tests/ and the oracle driver)
 enum : uint32_t {
   T_Q = 0, T_K = 1, T_V = 2, T_O = 3, T_GATE = 4, T_UP = 5, T_DOWN = 6,
@@ -993,7 +1112,7 @@ extern "C" int ch_model_zero_state(ch_model *m) {
 }
 
 // ---------------------------------------------------------------------------
-// the decode step (model_dispatch.zig:226-342 order; norms fused into GEMV prologues)
+// the decode step (model_dispatch.zig:10-45 order; norms fused into GEMV prologues)
 static cudaError_t enqueue_decode(ch_model *m, cudaStream_t s, bool logits, bool device_loop) {
   cudaError_t e;
   const bool pdl = m->pdl;
@@ -1293,6 +1412,7 @@ extern "C" int ch_decode_plan(ch_model *m, const ch_step_desc *steps, uint32_t n
   return CH_OK;
 }
 
+static cudaError_t launch_loop_sample(ch_model *m, cudaStream_t s);
 static int launch_loop_steps(ch_model *m, uint32_t n_steps) {
   cudaStream_t s = m->ctx->stream;
   if (m->use_ops) {
@@ -1306,6 +1426,7 @@ static int launch_loop_steps(ch_model *m, uint32_t n_steps) {
   for (uint32_t i = 0; i < n_steps; i++) {
     CH_CUDA(launch_step_begin(sb, s, false));
     CH_CUDA(launch_decode_step(a, m->mk_smem, s));
+    if (m->sampler) CH_CUDA(launch_loop_sample(m, s));
   }
   return CH_OK;
 }
@@ -1337,6 +1458,249 @@ extern "C" int ch_decode_continue(ch_model *m, uint32_t n_steps) {
   return CH_OK;
 }
 
+// ---------------------------------------------------------------------------
+// Device sampler (sampler.cu): Sampler.sampleTopK with its generator state on the device
+struct ch_sampler {
+  ch_ctx *ctx = nullptr;
+  SamplerParams p{};
+  uint64_t *prng = nullptr;      // [4]
+  uint32_t *recent = nullptr;    // [cap]
+  uint32_t *n_recent = nullptr;  // [1]
+  uint32_t cap = 0;
+};
+static_assert(sizeof(SamplerParams) == sizeof(ch_sampler_params), "sampler params layout");
+extern "C" int ch_sampler_create(ch_ctx *ctx, const ch_sampler_params *params, uint64_t seed, uint32_t recent_cap,
+                                 ch_sampler **out) {
+  if (!ctx || !params || !out) return fail(CH_EINVAL, "NULL argument");
+  CH_CUDA(cudaSetDevice(ctx->device));
+  ch_sampler *s = new ch_sampler();
+  s->ctx = ctx;
+  memcpy(&s->p, params, sizeof(SamplerParams));
+  s->cap = recent_cap;
+  if (dmalloc(&s->prng, 4) != CH_OK || dmalloc(&s->recent, std::max(recent_cap, 1u)) != CH_OK ||
+      dmalloc(&s->n_recent, 1) != CH_OK) {
+    cudaFree(s->prng);
+    cudaFree(s->recent);
+    cudaFree(s->n_recent);
+    delete s;
+    return fail(CH_ENOMEM, "sampler allocation");
+  }
+  // Xoshiro256.init(seed): the state words are four SplitMix64 outputs (Zig std/Random/Xoshiro256.zig)
+  uint64_t st[4], z0 = seed;
+  for (int i = 0; i < 4; i++) {
+    z0 += 0x9e3779b97f4a7c15ull;
+    uint64_t z = z0;
+    z = (z ^ (z >> 30)) * 0xbf58476d1ce4e5b9ull;
+    z = (z ^ (z >> 27)) * 0x94d049bb133111ebull;
+    st[i] = z ^ (z >> 31);
+  }
+  const uint32_t zero = 0;
+  if (cudaMemcpy(s->prng, st, sizeof(st), cudaMemcpyHostToDevice) != cudaSuccess ||
+      cudaMemcpy(s->n_recent, &zero, 4, cudaMemcpyHostToDevice) != cudaSuccess) {
+    cudaFree(s->prng);
+    cudaFree(s->recent);
+    cudaFree(s->n_recent);
+    delete s;
+    return fail(CH_ECUDA, "sampler upload");
+  }
+  *out = s;
+  return CH_OK;
+}
+extern "C" void ch_sampler_destroy(ch_sampler *s) {
+  if (!s) return;
+  cudaSetDevice(s->ctx->device);
+  cudaStreamSynchronize(s->ctx->stream);
+  cudaFree(s->prng);
+  cudaFree(s->recent);
+  cudaFree(s->n_recent);
+  delete s;
+}
+extern "C" int ch_sampler_set_recent(ch_sampler *s, const uint32_t *recent, uint32_t n) {
+  if (!s || (!recent && n)) return fail(CH_EINVAL, "NULL argument");
+  if (n > s->cap) return fail(CH_EINVAL, "more recent tokens than the sampler's capacity");
+  CH_CUDA(cudaSetDevice(s->ctx->device));
+  CH_CUDA(cudaStreamSynchronize(s->ctx->stream));
+  if (n) CH_CUDA(cudaMemcpy(s->recent, recent, (size_t)n * 4, cudaMemcpyHostToDevice));
+  CH_CUDA(cudaMemcpy(s->n_recent, &n, 4, cudaMemcpyHostToDevice));
+  return CH_OK;
+}
+extern "C" int ch_sampler_sample_topk(ch_sampler *s, const uint32_t *ids, const float *vals, uint32_t n,
+                                      const uint32_t *recent, uint32_t n_recent, uint32_t *token) {
+  if (!s || !ids || !vals || !token) return fail(CH_EINVAL, "NULL argument");
+  if (n > 64) return fail(CH_EINVAL, "at most 64 candidates");
+  CH_CUDA(cudaSetDevice(s->ctx->device));
+  SampleArgs a;
+  a.ids = ids;
+  a.vals = vals;
+  a.n = n;
+  a.recent = recent;
+  a.n_recent = recent ? n_recent : 0;
+  a.p = s->p;
+  a.prng = s->prng;
+  a.token_out = token;
+  CH_CUDA(launch_sample_topk(a, s->ctx->stream));
+  return CH_OK;
+}
+extern "C" int ch_model_set_sampler(ch_model *m, ch_sampler *s) {
+  if (!m) return fail(CH_EINVAL, "NULL model");
+  if (s && s->ctx->device != m->ctx->device) return fail(CH_EINVAL, "sampler and model on different devices");
+  if (s && m->use_ops) return fail(CH_ESTATE, "the device sampler runs with the persistent decode kernel");
+  m->sampler = s;
+  return CH_OK;
+}
+// the sampling launch of one device-loop step (after the decode step wrote the top-64)
+static cudaError_t launch_loop_sample(ch_model *m, cudaStream_t s) {
+  ch_sampler *sm = m->sampler;
+  SampleArgs a;
+  a.ids = m->ids;
+  a.vals = m->vals;
+  a.n = 64;
+  a.recent = sm->recent;
+  a.n_recent_dev = sm->n_recent;
+  a.recent_w = sm->recent;
+  a.recent_cap = sm->cap;
+  a.p = sm->p;
+  a.prng = sm->prng;
+  a.token_out = m->token;
+  a.sp = m->sp;
+  a.token_hist = m->token_hist;
+  a.hist_cap = m->hist_cap;
+  return launch_sample_topk(a, s);
+}
+
+// ---------------------------------------------------------------------------
+// Device-side ring lists (ring_dev.cu): a device copy of a ring's layer-0 metadata
+// and the decode loop that builds every step's lists from it on the device.
+namespace ch {
+bool ring_export_layer0(const ch_ring *r, RingDevState *out);
+}
+struct ch_ring_dev {
+  ch_ctx *ctx = nullptr;
+  RingDevState *d = nullptr;
+  RingDevState *h = nullptr;  // pinned staging
+};
+extern "C" int ch_ring_dev_create(ch_ctx *ctx, ch_ring_dev **out) {
+  if (!ctx || !out) return fail(CH_EINVAL, "NULL argument");
+  CH_CUDA(cudaSetDevice(ctx->device));
+  ch_ring_dev *r = new ch_ring_dev();
+  r->ctx = ctx;
+  if (cudaMalloc(&r->d, sizeof(RingDevState)) != cudaSuccess ||
+      cudaMallocHost(&r->h, sizeof(RingDevState)) != cudaSuccess) {
+    cudaFree(r->d);
+    cudaFreeHost(r->h);
+    delete r;
+    return fail(CH_ENOMEM, "ring_dev allocation");
+  }
+  memset(r->h, 0, sizeof(RingDevState));
+  CH_CUDA(cudaMemset(r->d, 0, sizeof(RingDevState)));
+  *out = r;
+  return CH_OK;
+}
+extern "C" void ch_ring_dev_destroy(ch_ring_dev *r) {
+  if (!r) return;
+  cudaSetDevice(r->ctx->device);
+  cudaStreamSynchronize(r->ctx->stream);
+  cudaFree(r->d);
+  cudaFreeHost(r->h);
+  delete r;
+}
+extern "C" int ch_ring_dev_upload(ch_ring_dev *r, const ch_ring *host) {
+  if (!r || !host) return fail(CH_EINVAL, "NULL argument");
+  CH_CUDA(cudaSetDevice(r->ctx->device));
+  CH_CUDA(cudaStreamSynchronize(r->ctx->stream));  // the staging copy may still be in flight
+  if (!ring_export_layer0(host, r->h)) return fail(CH_EINVAL, "ring clock does not fit 32 bits");
+  CH_CUDA(cudaMemcpyAsync(r->d, r->h, sizeof(RingDevState), cudaMemcpyHostToDevice, r->ctx->stream));
+  CH_CUDA(cudaStreamSynchronize(r->ctx->stream));
+  return CH_OK;
+}
+extern "C" int ch_ring_dev_lists(ch_ring_dev *r, uint32_t clock, int activate, size_t sliding_window, uint32_t *slot_dev,
+                                 uint32_t *active_dev, uint32_t *n_active_dev, uint32_t *sliding_dev,
+                                 uint32_t *n_sliding_dev) {
+  if (!r || !active_dev || !n_active_dev || !sliding_dev || !n_sliding_dev) return fail(CH_EINVAL, "NULL argument");
+  if (sliding_window > 0xFFFFFFFFull) return fail(CH_EINVAL, "sliding_window does not fit 32 bits");
+  CH_CUDA(cudaSetDevice(r->ctx->device));
+  RingStepArgs a;
+  a.ring = r->d;
+  a.clock = clock;
+  a.sliding_window = (uint32_t)sliding_window;
+  a.activate = activate ? 1 : 0;
+  a.slot_out = slot_dev;
+  a.active_out = active_dev;
+  a.n_active_out = n_active_dev;
+  a.sliding_out = sliding_dev;
+  a.n_sliding_out = n_sliding_dev;
+  CH_CUDA(launch_ring_step(a, r->ctx->stream));
+  return CH_OK;
+}
+extern "C" int ch_ring_dev_prefill_prev(ch_ring_dev *r, uint32_t start_clock, uint32_t chunk_len, uint32_t *out_dev,
+                                        uint32_t *n_dev) {
+  if (!r || !out_dev || !n_dev) return fail(CH_EINVAL, "NULL argument");
+  CH_CUDA(cudaSetDevice(r->ctx->device));
+  if (start_clock == 0 || chunk_len == 0) {  // ring_buffer.zig:344
+    CH_CUDA(cudaMemsetAsync(n_dev, 0, 4, r->ctx->stream));
+    return CH_OK;
+  }
+  RingStepArgs a;
+  a.ring = r->d;
+  a.clock = start_clock;
+  a.chunk_len = chunk_len;
+  a.prev = 1;
+  a.active_out = out_dev;
+  a.n_active_out = n_dev;
+  CH_CUDA(launch_ring_step(a, r->ctx->stream));
+  return CH_OK;
+}
+extern "C" int ch_decode_run_ring(ch_model *m, ch_ring_dev *r, ch_ring *host, uint32_t first_token,
+                                  uint32_t first_clock, uint32_t n_steps) {
+  if (!m || !r) return fail(CH_EINVAL, "NULL argument");
+  if (!m->embed) return fail(CH_ESTATE, "device decode loop needs the device embedding table");
+  if (r->ctx->device != m->ctx->device) return fail(CH_EINVAL, "ring_dev and model on different devices");
+  if (m->world > 1 && !m->peers_ready) return fail(CH_ESTATE, "tensor parallel: ch_model_attach_peers first");
+  if (first_token >= m->V) return fail(CH_EINVAL, "first_token >= vocab");
+  if (n_steps == 0) return fail(CH_EINVAL, "n_steps == 0");
+  if ((uint64_t)first_clock + n_steps > 0xFFFFFFFFull) return fail(CH_EINVAL, "clock overflow");
+  if (m->use_ops) return fail(CH_ESTATE, "device ring loop runs on the persistent decode kernel");
+  CH_CUDA(cudaSetDevice(m->ctx->device));
+  cudaStream_t s = m->ctx->stream;
+  CH_CUDA(cudaStreamSynchronize(r->ctx->stream));
+  CH_CUDA(cudaStreamSynchronize(s));  // a previous run may still read the staging words
+  if (m->hist_cap < n_steps) {
+    cudaFree(m->token_hist);
+    m->token_hist = nullptr;
+    m->hist_cap = 0;
+    CH_TRY(dmalloc(&m->token_hist, n_steps));
+    m->hist_cap = n_steps;
+  }
+  r->h->next_clock = first_clock;
+  r->h->step = 0;
+  m->h_run[1] = first_token;
+  CH_CUDA(cudaMemcpyAsync(&r->d->next_clock, &r->h->next_clock, 8, cudaMemcpyHostToDevice, s));
+  CH_CUDA(cudaMemcpyAsync(m->token, &m->h_run[1], 4, cudaMemcpyHostToDevice, s));
+  RingStepArgs ra;
+  ra.ring = r->d;
+  ra.sliding_window = m->cfg.sliding_window;
+  ra.activate = 1;
+  ra.loop = 1;
+  ra.active_out = m->active;
+  ra.sliding_out = m->sliding;
+  ra.sp = m->sp;
+  StepBeginArgs sb{m->embed,      m->H,       sqrtf((float)m->H), m->token,    m->X[0],
+                   m->sp,         nullptr,    0,                  m->ctx->err, m->inv_freq_s,
+                   m->inv_freq_f, m->rope_cs, m->cfg.rotary_dim / 2};
+  const MegaArgs a = mega_args(m, true, true);
+  for (uint32_t i = 0; i < n_steps; i++) {
+    CH_CUDA(launch_ring_step(ra, s));
+    CH_CUDA(launch_step_begin(sb, s, false));
+    CH_CUDA(launch_decode_step(a, m->mk_smem, s));
+    if (m->sampler) CH_CUDA(launch_loop_sample(m, s));
+  }
+  // the host ring takes the same activations (the caller's ring stays the source of truth)
+  if (host)
+    for (uint32_t i = 0; i < n_steps; i++) ch_ring_activate_slot(host, 0, (size_t)first_clock + i);
+  m->loop_ready = false;  // the plan's step counter no longer matches the device state
+  return CH_OK;
+}
+
 extern "C" int ch_decode_tokens(ch_model *m, uint32_t *tokens, uint32_t n) {
   if (!m || (!tokens && n)) return fail(CH_EINVAL, "NULL argument");
   if (n > m->hist_cap) return fail(CH_EINVAL, "more tokens than planned steps");
@@ -1361,30 +1725,36 @@ extern "C" int ch_read_normed_x(ch_model *m, float *x) {
   CH_CUDA(cudaMemcpy(x, m->normed, m->H * 4, cudaMemcpyDeviceToHost));
   return CH_OK;
 }
+// k / v hold kv_dim = num_key_value_heads * head_dim floats (every kv head).  A
+// tensor-parallel shard holds kv heads [rank * n_kv / world, (rank + 1) * n_kv / world):
+// ch_kv_read fills that range of k / v and leaves the rest as it was, ch_kv_write
+// stores only that range -- the full row is each rank's call over the same row.
 extern "C" int ch_kv_read(ch_model *m, uint32_t layer, uint32_t slot, float *k, float *v) {
-  if (m && m->world > 1) return fail(CH_ESTATE, "tensor parallel: each rank holds only its kv heads");
   if (!m || layer >= m->L || slot >= kSlots) return fail(CH_EINVAL, "bad layer / slot");
+  CH_CUDA(cudaSetDevice(m->ctx->device));
   CH_CUDA(cudaStreamSynchronize(m->ctx->stream));
-  std::vector<__half> hk(m->kvd), hv(m->kvd);
-  CH_CUDA(cudaMemcpy(hk.data(), m->layers[layer].kc + (size_t)slot * m->kvd, m->kvd * 2, cudaMemcpyDeviceToHost));
-  CH_CUDA(cudaMemcpy(hv.data(), m->layers[layer].vc + (size_t)slot * m->kvd, m->kvd * 2, cudaMemcpyDeviceToHost));
-  for (uint32_t i = 0; i < m->kvd; i++) {
-    if (k) k[i] = __half2float(hk[i]);
-    if (v) v[i] = __half2float(hv[i]);
+  const uint32_t w = m->kvd_l, c0 = m->rank * w;
+  std::vector<__half> hk(w), hv(w);
+  CH_CUDA(cudaMemcpy(hk.data(), m->layers[layer].kc + (size_t)slot * w, w * 2, cudaMemcpyDeviceToHost));
+  CH_CUDA(cudaMemcpy(hv.data(), m->layers[layer].vc + (size_t)slot * w, w * 2, cudaMemcpyDeviceToHost));
+  for (uint32_t i = 0; i < w; i++) {
+    if (k) k[c0 + i] = __half2float(hk[i]);
+    if (v) v[c0 + i] = __half2float(hv[i]);
   }
   return CH_OK;
 }
 extern "C" int ch_kv_write(ch_model *m, uint32_t layer, uint32_t slot, const float *k, const float *v) {
-  if (m && m->world > 1) return fail(CH_ESTATE, "tensor parallel: each rank holds only its kv heads");
   if (!m || layer >= m->L || slot >= kSlots || !k || !v) return fail(CH_EINVAL, "bad argument");
-  std::vector<__half> hk(m->kvd), hv(m->kvd);
-  for (uint32_t i = 0; i < m->kvd; i++) {
-    hk[i] = __float2half_rn(k[i]);
-    hv[i] = __float2half_rn(v[i]);
+  CH_CUDA(cudaSetDevice(m->ctx->device));
+  const uint32_t w = m->kvd_l, c0 = m->rank * w;
+  std::vector<__half> hk(w), hv(w);
+  for (uint32_t i = 0; i < w; i++) {
+    hk[i] = __float2half_rn(k[c0 + i]);
+    hv[i] = __float2half_rn(v[c0 + i]);
   }
   CH_CUDA(cudaStreamSynchronize(m->ctx->stream));
-  CH_CUDA(cudaMemcpy(m->layers[layer].kc + (size_t)slot * m->kvd, hk.data(), m->kvd * 2, cudaMemcpyHostToDevice));
-  CH_CUDA(cudaMemcpy(m->layers[layer].vc + (size_t)slot * m->kvd, hv.data(), m->kvd * 2, cudaMemcpyHostToDevice));
+  CH_CUDA(cudaMemcpy(m->layers[layer].kc + (size_t)slot * w, hk.data(), w * 2, cudaMemcpyHostToDevice));
+  CH_CUDA(cudaMemcpy(m->layers[layer].vc + (size_t)slot * w, hv.data(), w * 2, cudaMemcpyHostToDevice));
   return CH_OK;
 }
 
@@ -1465,8 +1835,13 @@ static int prefill_tp(ch_model *m, const uint32_t *tokens, uint32_t n, const uin
 // stream < 0: the model's own KV cache; else that stream's (ch_streams_init)
 static int prefill_impl(ch_model *m, const uint32_t *tokens, uint32_t n, const uint16_t *embed_bf16,
                         const uint32_t *slots, uint32_t start_clock, uint32_t num_prev, ch_topk *topk_out,
-                        ch_progress_fn progress_fn, void *progress_ctx, int stream) {
+                        float *logits_out, size_t logits_len, ch_progress_fn progress_fn, void *progress_ctx,
+                        int stream) {
   if (!m || !tokens || !slots) return fail(CH_EINVAL, "NULL argument");
+  if (logits_out && logits_len > m->V) return fail(CH_EINVAL, "logits_out longer than the vocabulary");
+  if (!logits_out) logits_len = 0;
+  if (logits_len && m->world > 1)
+    return fail(CH_ESTATE, "tensor parallel: each rank holds only its vocab rows' logits");
   const uint32_t cap = m->cfg.max_prefill_tokens ? m->cfg.max_prefill_tokens : 1024;
   if (n == 0 || n > cap) return fail(CH_EBATCH, "BatchTooLarge: n_tokens must be 1..max_prefill_tokens");
   if (num_prev + n > kSlots) return fail(CH_EINVAL, "num_prev_slots + n_tokens > 4096");
@@ -1550,7 +1925,7 @@ static int prefill_impl(ch_model *m, const uint32_t *tokens, uint32_t n, const u
   // decode-visible state = last token's residual / normed hidden
   CH_CUDA(cudaMemcpyAsync(m->X[0], m->pX + (size_t)(n - 1) * m->H, m->H * 4, cudaMemcpyDeviceToDevice, s));
   CH_CUDA(cudaMemcpyAsync(m->normed, m->pNX + (size_t)(n - 1) * m->H, m->H * 4, cudaMemcpyDeviceToDevice, s));
-  if (topk_out) {
+  if (topk_out || logits_len) {  // LM head + top-64 of the last token (batch_dispatch.zig:145-150)
     GemvArgs a;
     GemvPlan p;
     p.fmt = FMT_Q8;
@@ -1577,6 +1952,8 @@ static int prefill_impl(ch_model *m, const uint32_t *tokens, uint32_t n, const u
     CH_CUDA(cudaMemcpyAsync(m->h_ids, m->ids, 256, cudaMemcpyDeviceToHost, s));
     CH_CUDA(cudaMemcpyAsync(m->h_vals, m->vals, 256, cudaMemcpyDeviceToHost, s));
   }
+  // the reference copies the first logits_out.len raw logits (batch_dispatch.zig:168-170)
+  if (logits_len) CH_CUDA(cudaMemcpyAsync(logits_out, m->logits, logits_len * 4, cudaMemcpyDeviceToHost, s));
   CH_CUDA(cudaStreamSynchronize(s));
   if (topk_out)
     for (int i = 0; i < 64; i++) topk_out[i] = ch_topk{m->h_ids[i], m->h_vals[i]};
@@ -1587,8 +1964,9 @@ static int prefill_impl(ch_model *m, const uint32_t *tokens, uint32_t n, const u
 
 extern "C" int ch_prefill(ch_model *m, const uint32_t *tokens, uint32_t n, const uint16_t *embed_bf16,
                           const uint32_t *slots, uint32_t start_clock, uint32_t num_prev, ch_topk *topk_out,
-                          ch_progress_fn progress_fn, void *progress_ctx) {
-  return prefill_impl(m, tokens, n, embed_bf16, slots, start_clock, num_prev, topk_out, progress_fn, progress_ctx, -1);
+                          float *logits_out, size_t logits_len, ch_progress_fn progress_fn, void *progress_ctx) {
+  return prefill_impl(m, tokens, n, embed_bf16, slots, start_clock, num_prev, topk_out, logits_out, logits_len,
+                      progress_fn, progress_ctx, -1);
 }
 
 // ---------------------------------------------------------------------------
@@ -1682,7 +2060,8 @@ extern "C" int ch_stream_prefill(ch_model *m, uint32_t stream, const uint32_t *t
   if (!m) return fail(CH_EINVAL, "NULL model");
   if (stream >= m->ms_n) return fail(CH_EINVAL, "stream index >= the streams initialised");
   ch_topk top[64];
-  CH_TRY(prefill_impl(m, tokens, n, nullptr, slots, start_clock, num_prev, token_out ? top : nullptr, nullptr, nullptr,
+  CH_TRY(prefill_impl(m, tokens, n, nullptr, slots, start_clock, num_prev, token_out ? top : nullptr, nullptr, 0,
+                      nullptr, nullptr,
                       (int)stream));
   if (token_out) *token_out = top[0].id;
   return CH_OK;
@@ -1846,6 +2225,27 @@ extern "C" int ch_streams_decode(ch_model *m, const ch_stream_step *steps, uint3
   uint32_t f = 0;
   CH_TRY(ch_ctx_device_status(m->ctx, &f));
   return status_from_flags(f);
+}
+
+// State of the last ch_streams_decode step, token b = the step's b-th entry: the
+// final-normed hidden state each token's LM head read, and its raw (pre-softcap) logits.
+extern "C" int ch_streams_read_normed_x(ch_model *m, uint32_t n, float *out) {
+  if (!m || !out) return fail(CH_EINVAL, "NULL argument");
+  if (!m->ms_n) return fail(CH_ESTATE, "ch_streams_init first");
+  if (n == 0 || n > m->ms_cap) return fail(CH_EINVAL, "1..max_batch rows");
+  CH_CUDA(cudaSetDevice(m->ctx->device));
+  CH_CUDA(cudaStreamSynchronize(m->ctx->stream));
+  CH_CUDA(cudaMemcpy(out, m->pNX, (size_t)n * m->H * 4, cudaMemcpyDeviceToHost));
+  return CH_OK;
+}
+extern "C" int ch_streams_read_logits(ch_model *m, uint32_t n, float *out) {
+  if (!m || !out) return fail(CH_EINVAL, "NULL argument");
+  if (!m->ms_n) return fail(CH_ESTATE, "ch_streams_init first");
+  if (n == 0 || n > m->ms_cap) return fail(CH_EINVAL, "1..max_batch rows");
+  CH_CUDA(cudaSetDevice(m->ctx->device));
+  CH_CUDA(cudaStreamSynchronize(m->ctx->stream));
+  CH_CUDA(cudaMemcpy(out, m->ms_logits, (size_t)n * m->V * 4, cudaMemcpyDeviceToHost));
+  return CH_OK;
 }
 
 // ---------------------------------------------------------------------------

@@ -11,6 +11,7 @@
 #include <vector>
 
 #include "../../include/channel_cuda.h"
+#include "kernels.cuh"
 
 namespace {
 constexpr size_t kTotal = 4096, kRecall = 128, kMaxBoundaries = 1024;
@@ -178,3 +179,28 @@ extern "C" size_t ch_ring_prefill_prev_slots(const ch_ring *r, size_t layer, siz
     if (r->active[base + s] && r->clocks[base + s] < start_clock) out[n++] = (uint32_t)s;
   return n;
 }
+
+// Layer-0 metadata of a ring in the device layout (RingDevState) for the device-side
+// list builder (ring_dev.cu); fails when a stored clock does not fit 32 bits.
+namespace ch {
+bool ring_export_layer0(const ch_ring *r, RingDevState *out) {
+  out->anchors = (uint32_t)r->anchors;
+  out->window = (uint32_t)ch_ring_window_size(r, 0);
+  if (r->nb > 0xFFFFFFFFull || r->ingested > 0xFFFFFFFFull) return false;
+  out->nb = (uint32_t)r->nb;
+  out->ingested = (uint32_t)r->ingested;
+  out->next_clock = 0;
+  out->step = 0;
+  out->pad0 = out->pad1 = 0;
+  for (size_t s = 0; s < kTotal; s++) {
+    if (r->clocks[s] > 0xFFFFFFFFull) return false;
+    out->clocks[s] = (uint32_t)r->clocks[s];
+    out->active[s] = r->active[s];
+  }
+  for (size_t i = 0; i < kMaxBoundaries; i++) {
+    if (r->boundary[i] > 0xFFFFFFFFull) return false;
+    out->boundary[i] = (uint32_t)r->boundary[i];
+  }
+  return true;
+}
+}  // namespace ch

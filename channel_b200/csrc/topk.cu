@@ -114,17 +114,21 @@ __global__ void step_begin_kernel(const StepBeginArgs a) {
   grid_dep_wait();
   __shared__ StepParams cur;
   if (threadIdx.x == 0) {
-    uint32_t step = a.sp->next;
-    if (step >= a.n_plan) {  // replayed past the uploaded plan: keep the last entry, flag it
-      atomicOr(a.err, DEV_ERR_BAD_LIST);
-      step = a.n_plan - 1;
+    if (a.plan) {
+      uint32_t step = a.sp->next;
+      if (step >= a.n_plan) {  // replayed past the uploaded plan: keep the last entry, flag it
+        atomicOr(a.err, DEV_ERR_BAD_LIST);
+        step = a.n_plan - 1;
+      }
+      cur = a.plan[step];
+      cur.step = step;
+      cur.next = step + 1;
+    } else {
+      cur = *a.sp;  // no plan: the device ring wrote this step's parameters (ring_dev.cu)
     }
-    cur = a.plan[step];
-    cur.step = step;
-    cur.next = step + 1;
   }
   __syncthreads();
-  if (blockIdx.x == 0 && threadIdx.x == 0) *a.sp = cur;
+  if (a.plan && blockIdx.x == 0 && threadIdx.x == 0) *a.sp = cur;
   // RoPE (cos, sin) of this step's clock for both thetas, evaluated once per step
   // in double and rounded once (same values as the host path and the oracle)
   for (uint32_t i = threadIdx.x; i < 2 * a.rot_half; i += blockDim.x) {

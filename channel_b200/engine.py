@@ -5,14 +5,14 @@ tests read like the reference:
 
     GpuContext.init / deinit                 src/gpu/context.zig:17,109
     GpuModelContext.init / deinit            src/gpu/model_gpu.zig:68,203
-    gpu_dispatch_forward_token               src/gpu/model_dispatch.zig:344
+    gpu_dispatch_forward_token               src/gpu/model_dispatch.zig:128
     gpu_dispatch_prefill_batch               src/gpu/batch_dispatch.zig:27
     DynamicRingBuffer                        src/ring_buffer.zig:21
-    ModelConfig / TopKCandidate              src/model/types.zig:210,282
+    ModelConfig / TopKCandidate              src/model/types.zig:43,115
 
 Errors: every failing call raises ChannelError carrying the C status
 (the reference returns token 0 from a failed decode submit,
-model_dispatch.zig:360, and raises BatchTooLarge / GpuError from prefill).
+model_dispatch.zig:144, and raises BatchTooLarge / GpuError from prefill).
 """
 from __future__ import annotations
 
@@ -43,7 +43,7 @@ class TopKCandidate:
 
 @dataclass
 class ModelConfig:
-    """ModelConfig (src/model/types.zig:210-229); layer_types default every 5th full (:276)."""
+    """ModelConfig (src/model/types.zig:43-62); layer_types default every 5th full (:109)."""
     vocab_size: int = 262144
     hidden_size: int = 1536
     intermediate_size: int = 12288
@@ -125,7 +125,7 @@ class GpuContext:
 
 @dataclass
 class LayerWeightsQ4:
-    """LayerWeights (src/model/types.zig:180-208) with projections already in
+    """LayerWeights (src/model/types.zig:13-41) with projections already in
     quantizeRowQ4_0 block form (uint32 [rows, cols/32*5]) and f32 norms."""
     q_proj: np.ndarray
     k_proj: np.ndarray
@@ -178,6 +178,36 @@ class GpuModelContext:
         h = C.c_void_p()
         L.check(lib.ch_model_create(ctx.handle, C.byref(cfg), arr, _ptr(lm, C.c_uint32), _ptr(fn, C.c_float),
                                     _ptr(emb, C.c_uint16), C.byref(h)))
+        return cls(ctx, h.value, config)
+
+    @classmethod
+    def from_bf16(cls, ctx: GpuContext, config: ModelConfig, layers: Sequence[dict], embed_bf16: np.ndarray,
+                  final_norm_bf16: Optional[np.ndarray] = None) -> "GpuModelContext":
+        """GpuModelContext.init with quantize-on-load (src/gpu/model_gpu.zig:44-55,68-127):
+        layers are dicts of bf16 (uint16) arrays named like LayerWeights (q_proj ...
+        down_proj [out, in]; input_norm, q_norm, k_norm, pre_ffn_norm, post_attn_norm,
+        post_ffn_norm; optional layer_scalar).  Missing v_proj = k_proj; missing norms
+        follow ch_model_create_bf16."""
+        lib = L.load()
+        arr = (L.ChLayerWeightsBf16 * len(layers))()
+        keep = []
+        for i, lw in enumerate(layers):
+            w = arr[i]
+            for name in ("q_proj", "k_proj", "v_proj", "o_proj", "gate_proj", "up_proj", "down_proj", "input_norm",
+                         "q_norm", "k_norm", "post_attn_norm", "pre_ffn_norm", "post_ffn_norm"):
+                v = lw.get(name)
+                if v is None:
+                    continue
+                a = np.ascontiguousarray(v, dtype=np.uint16)
+                keep.append(a)
+                setattr(w, name, _ptr(a, C.c_uint16))
+            w.layer_scalar = float(lw.get("layer_scalar", 1.0))
+        emb = np.ascontiguousarray(embed_bf16, dtype=np.uint16)
+        fn = None if final_norm_bf16 is None else np.ascontiguousarray(final_norm_bf16, dtype=np.uint16)
+        cfg = config.to_c()
+        h = C.c_void_p()
+        L.check(lib.ch_model_create_bf16(ctx.handle, C.byref(cfg), arr, _ptr(emb, C.c_uint16), _ptr(fn, C.c_uint16),
+                                         C.byref(h)))
         return cls(ctx, h.value, config)
 
     @classmethod
@@ -287,6 +317,18 @@ class GpuModelContext:
         L.check(L.load().ch_streams_decode(self.handle, arr, len(steps), _ptr(out, C.c_uint32)))
         return out
 
+    def streams_read_normed_x(self, n: int) -> np.ndarray:
+        """final-normed hidden state of each of the last streams step's n tokens"""
+        out = np.empty((n, self.config.hidden_size), np.float32)
+        L.check(L.load().ch_streams_read_normed_x(self.handle, n, _ptr(out, C.c_float)))
+        return out
+
+    def streams_read_logits(self, n: int) -> np.ndarray:
+        """raw (pre-softcap) logits of each of the last streams step's n tokens"""
+        out = np.empty((n, self.config.vocab_size), np.float32)
+        L.check(L.load().ch_streams_read_logits(self.handle, n, _ptr(out, C.c_float)))
+        return out
+
     def streams_decode_steps(self, steps, n: int) -> np.ndarray:
         """One batched step from n prepared ChStreamStep records (ch_rings_fill_steps)."""
         out = np.zeros(n, np.uint32)
@@ -314,7 +356,7 @@ class GpuModelContext:
 def gpu_dispatch_forward_token(gpu: GpuModelContext, x: np.ndarray, clock: int, slot_idx: int,
                                active_slots: Sequence[int], sliding_slots: Sequence[int],
                                topk_out: bool = True) -> tuple[int, Optional[list]]:
-    """gpuDispatchForwardToken (src/gpu/model_dispatch.zig:344-369).
+    """gpuDispatchForwardToken (src/gpu/model_dispatch.zig:128-153).
 
     Returns (greedy token, list of 64 TopKCandidate or None)."""
     lib = L.load()
@@ -331,17 +373,23 @@ def gpu_dispatch_forward_token(gpu: GpuModelContext, x: np.ndarray, clock: int, 
 
 def gpu_dispatch_prefill_batch(gpu: GpuModelContext, tokens: Sequence[int], embed_tokens: Optional[np.ndarray],
                                slots: Sequence[int], start_clock: int, num_prev_slots: int, want_topk: bool = True,
-                               progress_fn: Optional[Callable[[int, int], None]] = None) -> Optional[list]:
+                               progress_fn: Optional[Callable[[int, int], None]] = None,
+                               logits_out: Optional[np.ndarray] = None) -> Optional[list]:
     """gpuDispatchPrefillBatch (src/gpu/batch_dispatch.zig:27-172).  embed_tokens is
-    the bf16 table as uint16 (None = the model's device table)."""
+    the bf16 table as uint16 (None = the model's device table); logits_out, a float32
+    array of at most vocab entries, receives the last token's raw logits
+    (batch_dispatch.zig:168-170)."""
     lib = L.load()
     tok = np.ascontiguousarray(tokens, np.uint32)
     sl = np.ascontiguousarray(slots, np.uint32)
     emb = None if embed_tokens is None else np.ascontiguousarray(embed_tokens, np.uint16)
     tk = (L.ChTopk * 64)() if want_topk else None
     cb = L.PROGRESS_FN(lambda i, n, _c: progress_fn(i, n)) if progress_fn else L.PROGRESS_FN()
+    if logits_out is not None:
+        assert logits_out.dtype == np.float32 and logits_out.flags.c_contiguous
     L.check(lib.ch_prefill(gpu.handle, _ptr(tok, C.c_uint32), len(tok), _ptr(emb, C.c_uint16), _ptr(sl, C.c_uint32),
-                           start_clock, num_prev_slots, tk, cb, None))
+                           start_clock, num_prev_slots, tk, _ptr(logits_out, C.c_float),
+                           0 if logits_out is None else logits_out.size, cb, None))
     return [TopKCandidate(t.id, t.val) for t in tk] if want_topk else None
 
 

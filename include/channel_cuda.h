@@ -21,7 +21,7 @@
 extern "C" {
 #endif
 
-#define CH_API_VERSION 1
+#define CH_API_VERSION 2
 
 typedef enum {
   CH_OK = 0,
@@ -39,7 +39,7 @@ typedef struct ch_ctx ch_ctx;
 typedef struct ch_model ch_model;
 typedef struct ch_ring ch_ring;
 
-/* TopKCandidate (src/model/types.zig:282-285) */
+/* TopKCandidate (src/model/types.zig:115-118) */
 typedef struct {
   uint32_t id;
   float val;
@@ -63,17 +63,17 @@ int ch_ctx_device_status(ch_ctx *ctx, uint32_t *flags);
 /* ------------------------------------------------------------------------
  * Model -- replaces GpuModelContext.init / deinit (src/gpu/model_gpu.zig:68-216)
  * ---------------------------------------------------------------------- */
-/* ModelConfig subset (src/model/types.zig:210-229) */
+/* ModelConfig subset (src/model/types.zig:43-62) */
 typedef struct {
   uint32_t vocab_size, hidden_size, intermediate_size, num_hidden_layers;
   uint32_t num_attention_heads, num_key_value_heads, head_dim, rotary_dim;
   float rms_norm_eps, rope_theta, rope_theta_full;
   uint32_t sliding_window;     /* decode sliding list length used by the caller's ring */
   uint32_t max_prefill_tokens; /* BatchPrefillContext max_tokens (model_gpu.zig:178): 1024 */
-  uint8_t layer_types[64];     /* 0 = sliding_attention, 1 = full_attention (types.zig:174,228) */
+  uint8_t layer_types[64];     /* 0 = sliding_attention, 1 = full_attention (types.zig:61,109) */
 } ch_model_config;
 
-/* LayerWeights (src/model/types.zig:180-208): projections already quantized by
+/* LayerWeights (src/model/types.zig:13-41): projections already quantized by
  * quantizeRowQ4_0 (src/quant.zig:58-98, 5 words per 32 weights), norms as f32
  * (createNormBuffer, model_gpu.zig:57-66).  post_* may be NULL. */
 typedef struct {
@@ -93,6 +93,24 @@ int ch_model_create(ch_ctx *ctx, const ch_model_config *cfg, const ch_layer_weig
  * = Q8_0 of the embedding, norms 1+N(0,0.02)); generator shared with the oracle. */
 int ch_model_create_synthetic(ch_ctx *ctx, const ch_model_config *cfg, uint64_t seed, ch_model **out);
 
+/* LayerWeights as the reference loads them from safetensors (bf16, row-major
+ * [out][in], src/model/types.zig:13-41).  NULL v_proj = k_proj (attention_k_eq_v);
+ * NULL input / q / k / pre-FFN norm = all ones; NULL post_attn / post_ffn norm =
+ * the layer has none. */
+typedef struct {
+  const uint16_t *q_proj, *k_proj, *v_proj, *o_proj, *gate_proj, *up_proj, *down_proj;
+  const uint16_t *input_norm, *q_norm, *k_norm, *post_attn_norm, *pre_ffn_norm, *post_ffn_norm;
+  float layer_scalar;
+} ch_layer_weights_bf16;
+/* GpuModelContext.init with quantize-on-load (src/gpu/model_gpu.zig:44-55,68-127):
+ * uploads every bf16 projection and quantizes it to Q4_0 on the device
+ * (quantizeRowQ4_0, quant.zig:58-98, bit-exact), norms bf16 -> f32
+ * (createNormBuffer, model_gpu.zig:57-66), the tied embedding (vocab x hidden,
+ * required) to the Q8_0 LM head (model_gpu.zig:157) and the device embedding
+ * table.  final_norm_bf16 NULL = all ones.  One GPU. */
+int ch_model_create_bf16(ch_ctx *ctx, const ch_model_config *cfg, const ch_layer_weights_bf16 *layers,
+                         const uint16_t *embed_bf16, const uint16_t *final_norm_bf16, ch_model **out);
+
 /* Tensor-parallel decode (no counterpart in the reference, which runs one GPU):
  * shard `rank` of `world` (<= 8, one process per GPU) of the same synthetic model.
  * q|k|v and the KV cache are split by heads, o_proj / down_proj by output rows,
@@ -105,7 +123,8 @@ int ch_model_create_synthetic(ch_ctx *ctx, const ch_model_config *cfg, uint64_t 
  * order and every rank passes them to ch_model_attach_peers.  All ranks must then
  * make the same sequence of decode / prefill calls (prefill runs token by token
  * through the decode kernel); after ch_model_zero_state the caller synchronizes
- * the ranks before the next call.  KV read/write is not available on a shard. */
+ * the ranks before the next call.  ch_kv_read / ch_kv_write on a shard touch
+ * only the rank's kv heads (see there). */
 #define CH_IPC_HANDLE_BYTES 64
 int ch_model_create_synthetic_sharded(ch_ctx *ctx, const ch_model_config *cfg, uint64_t seed, uint32_t rank,
                                       uint32_t world, ch_model **out);
@@ -120,7 +139,7 @@ int ch_model_zero_state(ch_model *m);
 int ch_model_weight_tiles(ch_model *m, uint32_t layer, int which, void **tiles_dev, uint32_t *rows, uint32_t *cols);
 
 /* ------------------------------------------------------------------------
- * Decode -- replaces gpuDispatchForwardToken (src/gpu/model_dispatch.zig:344-369)
+ * Decode -- replaces gpuDispatchForwardToken (src/gpu/model_dispatch.zig:128-153)
  * x: f32[hidden] (embedding row * sqrt(hidden), forward.zig:33-37).
  * active / sliding: physical slot lists from DynamicRingBuffer.getActiveSlotsLayer
  * (layer 0, used by every layer, forward.zig:42-45).  topk_out: 64 entries or
@@ -135,12 +154,15 @@ int ch_forward_token(ch_model *m, const float *x, uint32_t clock, uint32_t slot,
  * tokens: n_tokens ids (1..max_prefill_tokens, else CH_EBATCH); embed_bf16: host
  * table (NULL -> device table from model creation); slots: num_prev_slots
  * previous slots followed by the n_tokens new slots; topk_out: 64 or NULL.
+ * logits_out / logits_len: the reference's logits_out slice (batch_dispatch.zig:36,
+ * 168-170) -- the first logits_len raw (pre-softcap) logits of the last token,
+ * logits_len <= vocab (NULL or 0: none; one GPU only).
  * progress_fn is called after every 4 layers like the reference.
  * ---------------------------------------------------------------------- */
 typedef void (*ch_progress_fn)(size_t layer_idx, size_t total_layers, void *ctx);
 int ch_prefill(ch_model *m, const uint32_t *tokens, uint32_t n_tokens, const uint16_t *embed_bf16, const uint32_t *slots,
-               uint32_t start_clock, uint32_t num_prev_slots, ch_topk *topk_out, ch_progress_fn progress_fn,
-               void *progress_ctx);
+               uint32_t start_clock, uint32_t num_prev_slots, ch_topk *topk_out, float *logits_out, size_t logits_len,
+               ch_progress_fn progress_fn, void *progress_ctx);
 
 /* ------------------------------------------------------------------------
  * State access -- replaces the mapped UMA buffers the reference reads/writes
@@ -148,6 +170,10 @@ int ch_prefill(ch_model *m, const uint32_t *tokens, uint32_t n_tokens, const uin
  * ---------------------------------------------------------------------- */
 int ch_read_x(ch_model *m, float *x);               /* residual after the last step */
 int ch_read_normed_x(ch_model *m, float *normed_x); /* final-normed hidden state    */
+/* k / v: kv_dim floats (all kv heads of the slot's row).  On a tensor-parallel
+ * shard only the rank's kv heads [rank*n_kv/world, (rank+1)*n_kv/world) are read
+ * (the rest of k / v is left as it was) or written: the full row is every rank's
+ * call over the same row. */
 int ch_kv_read(ch_model *m, uint32_t layer, uint32_t slot, float *k, float *v);
 int ch_kv_write(ch_model *m, uint32_t layer, uint32_t slot, const float *k, const float *v);
 
@@ -164,6 +190,35 @@ int ch_decode_plan(ch_model *m, const ch_step_desc *steps, uint32_t n_steps); /*
 int ch_decode_run(ch_model *m, uint32_t first_token, uint32_t n_steps);     /* async; restarts at plan step 0 */
 int ch_decode_continue(ch_model *m, uint32_t n_steps);                      /* async; next planned steps   */
 int ch_decode_tokens(ch_model *m, uint32_t *tokens, uint32_t n);            /* syncs, copies step tokens */
+
+/* ------------------------------------------------------------------------
+ * Stochastic sampling on the device -- Sampler.sampleTopK (src/sampler.zig:217-317)
+ * over the top-64: suppressed ids dropped, repeat / frequency / presence penalties
+ * of the recent tokens with a stable re-sort, temperature softmax, min-p, top-p and
+ * one draw from Zig's std.Random.DefaultPrng (Xoshiro256++ seeded by SplitMix64,
+ * Random.float(f32)).  Field order and defaults as Sampler (sampler.zig:55-82).
+ * ---------------------------------------------------------------------- */
+typedef struct {
+  float temp, top_p, min_p, repeat_penalty, frequency_penalty, presence_penalty;
+  uint32_t top_k; /* kept for layout; sampleTopK uses the 64 candidates it gets */
+  uint8_t suppress_thinking, suppress_critique, suppress_channel_close, reserved;
+} ch_sampler_params;
+typedef struct ch_sampler ch_sampler;
+/* Sampler.init(seed, ...): the generator state and a device list of recent tokens
+ * (capacity recent_cap) for device loops */
+int ch_sampler_create(ch_ctx *ctx, const ch_sampler_params *params, uint64_t seed, uint32_t recent_cap,
+                      ch_sampler **out);
+void ch_sampler_destroy(ch_sampler *s);
+/* replace the sampler's recent-token list (the response so far, server/decode.zig:40-60);
+ * a device loop then appends every token it samples */
+int ch_sampler_set_recent(ch_sampler *s, const uint32_t *recent, uint32_t n);
+/* sampleTopK of n (<= 64) device candidates -> *token_dev; recent_dev NULL = no recent
+ * tokens; asynchronous on the context stream (one generator draw when it samples) */
+int ch_sampler_sample_topk(ch_sampler *s, const uint32_t *ids_dev, const float *vals_dev, uint32_t n,
+                           const uint32_t *recent_dev, uint32_t n_recent, uint32_t *token_dev);
+/* device loops of m (ch_decode_run / _continue / _run_ring) sample every step's token
+ * with s and its recent list instead of taking the greedy one; NULL = greedy */
+int ch_model_set_sampler(ch_model *m, ch_sampler *s);
 
 /* ------------------------------------------------------------------------
  * Multi-stream greedy decode (no reference counterpart: the
@@ -184,6 +239,12 @@ int ch_streams_init(ch_model *m, uint32_t n_streams, uint32_t max_batch);
 int ch_stream_prefill(ch_model *m, uint32_t stream, const uint32_t *tokens, uint32_t n_tokens, const uint32_t *slots,
                       uint32_t start_clock, uint32_t num_prev_slots, uint32_t *token_out);
 int ch_streams_decode(ch_model *m, const ch_stream_step *steps, uint32_t n, uint32_t *tokens_out);
+/* State of the last ch_streams_decode step (its first n entries, in step order):
+ * the final-normed hidden state each token's LM head read (n x hidden) and the raw
+ * pre-softcap logits (n x vocab) -- the multi-stream counterpart of ch_read_normed_x
+ * and of the reference's buf_logits read (batch_dispatch.zig:168-170). */
+int ch_streams_read_normed_x(ch_model *m, uint32_t n, float *normed_x);
+int ch_streams_read_logits(ch_model *m, uint32_t n, float *logits);
 
 /* ------------------------------------------------------------------------
  * Op-level entry points (device pointers, async on the context stream).
@@ -295,6 +356,37 @@ size_t ch_ring_slot_clock(const ch_ring *r, size_t layer, size_t slot);
 size_t ch_ring_active_slots(const ch_ring *r, size_t layer, size_t clock, int is_sliding, size_t sliding_window,
                             uint32_t *out);
 size_t ch_ring_prefill_prev_slots(const ch_ring *r, size_t layer, size_t start_clock, size_t chunk_len, uint32_t *out);
+
+/* ------------------------------------------------------------------------
+ * Ring lists on the device (no reference counterpart: the reference builds the
+ * lists on the host every token, src/ring_buffer.zig:287-380 via forward.zig:44-45,
+ * and uploads them, model_dispatch.zig:133-135).  A ch_ring_dev is a device copy of
+ * a ring's layer-0 metadata (active flags, slot clocks, anchors, turn boundaries);
+ * its lists are the host ring's, bit for bit, in the same order.
+ * ---------------------------------------------------------------------- */
+typedef struct ch_ring_dev ch_ring_dev;
+int ch_ring_dev_create(ch_ctx *ctx, ch_ring_dev **out);
+void ch_ring_dev_destroy(ch_ring_dev *r);
+/* copy the host ring's layer-0 metadata to the device (synchronous) */
+int ch_ring_dev_upload(ch_ring_dev *r, const ch_ring *host);
+/* [activateSlot(0, clock) if activate, then] slotIndex(clock) -> *slot_dev (may be NULL),
+ * getActiveSlotsLayer(0, clock, false, .) -> active_dev[*n_active_dev] and
+ * getActiveSlotsLayer(0, clock, true, sliding_window) -> sliding_dev[*n_sliding_dev];
+ * lists hold up to 4096 entries; asynchronous on the context stream */
+int ch_ring_dev_lists(ch_ring_dev *r, uint32_t clock, int activate, size_t sliding_window, uint32_t *slot_dev,
+                      uint32_t *active_dev, uint32_t *n_active_dev, uint32_t *sliding_dev, uint32_t *n_sliding_dev);
+/* getPrefillPrevSlots(0, start_clock, chunk_len) -> out_dev[*n_dev]; asynchronous */
+int ch_ring_dev_prefill_prev(ch_ring_dev *r, uint32_t start_clock, uint32_t chunk_len, uint32_t *out_dev,
+                             uint32_t *n_dev);
+/* Device-resident greedy loop like ch_decode_run, but every step activates its slot
+ * in the device ring and builds its own lists there (clocks first_clock ..
+ * first_clock + n_steps - 1): no plan, nothing uploaded per token.  r must hold the
+ * host ring's state (ch_ring_dev_upload); the host ring `host` (may be NULL) gets
+ * the same activations when the call returns.  Asynchronous; ch_decode_tokens
+ * reads the tokens.  Afterwards ch_decode_run / ch_decode_continue need a new
+ * ch_decode_plan. */
+int ch_decode_run_ring(ch_model *m, ch_ring_dev *r, ch_ring *host, uint32_t first_token, uint32_t first_clock,
+                       uint32_t n_steps);
 
 #ifdef __cplusplus
 }

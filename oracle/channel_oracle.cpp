@@ -226,7 +226,7 @@ extern "C" void or_gen_f32(float *dst, size_t n, uint64_t tseed, float mean, flo
 }
 
 // ----------------------------------------------------------------------------
-// Q4 / Q8 matvec -- shaders/gemv_q4.wgsl:15-26,44-72; gemv_q8.wgsl:163-194
+// Q4 / Q8 matvec -- shaders/gemv_q4.wgsl:15-26,44-72; gemv_q8.wgsl:41-63
 static inline float unpack_dot2(uint32_t w, const float *xa) {
   // gemv_q4.wgsl:15-26: (q - 8) * x for 8 nibbles, little nibble first
   float n0 = (float)(w & 0xFu) - 8.0f, n1 = (float)((w >> 4) & 0xFu) - 8.0f;
@@ -484,6 +484,137 @@ extern "C" uint32_t or_sample_topk_greedy(const uint32_t *ids, const float *vals
     std::stable_sort(items.begin(), items.end(), [](const C &a, const C &b) { return a.val > b.val; });
   }
   return items[0].id;
+}
+
+// Zig's std.Random.DefaultPrng (Xoshiro256++ by Blackman & Vigna, 256-bit state filled
+// by SplitMix64 from the seed: std/Random/Xoshiro256.zig init/seed/next) and
+// Random.float(f32) (std/Random.zig: 23 random mantissa bits, the exponent from the
+// leading zeros of the remaining bits of the same 64-bit draw).
+static inline uint64_t or_rotl(uint64_t x, int k) { return (x << k) | (x >> (64 - k)); }
+extern "C" void or_prng_seed(uint64_t *st, uint64_t seed) {
+  uint64_t z0 = seed;
+  for (int i = 0; i < 4; i++) {  // SplitMix64.next
+    z0 += 0x9e3779b97f4a7c15ull;
+    uint64_t z = z0;
+    z = (z ^ (z >> 30)) * 0xbf58476d1ce4e5b9ull;
+    z = (z ^ (z >> 27)) * 0x94d049bb133111ebull;
+    st[i] = z ^ (z >> 31);
+  }
+}
+extern "C" uint64_t or_prng_next(uint64_t *s) {
+  const uint64_t r = or_rotl(s[0] + s[3], 23) + s[0];
+  const uint64_t t = s[1] << 17;
+  s[2] ^= s[0];
+  s[3] ^= s[1];
+  s[1] ^= s[2];
+  s[0] ^= s[3];
+  s[2] ^= t;
+  s[3] = or_rotl(s[3], 45);
+  return r;
+}
+extern "C" float or_prng_float(uint64_t *s) {
+  const uint64_t rnd = or_prng_next(s);
+  uint32_t lz = rnd ? (uint32_t)__builtin_clzll(rnd) : 64u;
+  if (lz >= 41) {
+    const uint64_t r2 = or_prng_next(s);
+    lz = 41 + (r2 ? (uint32_t)__builtin_clzll(r2) : 64u);
+    if (lz == 41 + 64) lz += (uint32_t)__builtin_clz((uint32_t)or_prng_next(s) | 0x7FFu);
+  }
+  const uint32_t bits = ((126u - lz) << 23) | ((uint32_t)rnd & 0x7FFFFFu);
+  float f;
+  memcpy(&f, &bits, 4);
+  return f;
+}
+// Sampler.sampleTopK (src/sampler.zig:217-317): suppression, penalties with a stable
+// re-sort, then temperature softmax, min-p, top-p and one draw.  params: temp, top_p,
+// min_p, repeat, frequency, presence; flags: bit 0 suppress_thinking, bit 1
+// suppress_critique, bit 2 suppress_channel_close.  recent NULL = no recent tokens.
+extern "C" uint32_t or_sample_topk(const uint32_t *ids, const float *vals, size_t n, const uint32_t *recent,
+                                   size_t n_recent, const float *params, int flags, uint64_t *prng) {
+  const float temp = params[0], top_p = params[1], min_p = params[2], rp = params[3], fp = params[4], pp = params[5];
+  const int sup_think = flags & 1, sup_crit = (flags >> 1) & 1, sup_close = (flags >> 2) & 1;
+  if (n == 0) return 0;
+  const bool has_pen = (rp > 1.0f || fp > 0.0f || pp > 0.0f);
+  if (temp <= 0.0f && (!has_pen || recent == nullptr) && !sup_think && !sup_crit && !sup_close) return ids[0];
+  static const uint32_t sup[] = {0, 258882, 258883, 255999, 256000, 256001, 255995, 255996, 255997, 255998};
+  struct C {
+    uint32_t id;
+    float val;
+  };
+  std::vector<C> items;
+  for (size_t i = 0; i < n; i++) {
+    const uint32_t id = ids[i];
+    bool skip = false;
+    for (uint32_t x : sup)
+      if (id == x) skip = true;
+    if (skip || (sup_think && id == 100) || (sup_close && id == 101) || (sup_crit && is_critique(id))) continue;
+    items.push_back({id, vals[i]});
+    if (items.size() == 64) break;
+  }
+  if (items.empty()) return ids[0];
+  if (recent != nullptr && has_pen) {
+    for (size_t i = 0; i < n_recent; i++) {
+      const uint32_t tok = recent[i];
+      bool seen = false;
+      for (size_t j = 0; j < i; j++)
+        if (recent[j] == tok) seen = true;
+      if (seen) continue;
+      size_t count = 0;
+      for (size_t j = 0; j < n_recent; j++)
+        if (recent[j] == tok) count++;
+      for (auto &it : items)
+        if (it.id == tok) {
+          if (rp > 1.0f) it.val = it.val > 0.0f ? it.val / rp : it.val * rp;
+          it.val -= pp + ((float)count * fp);
+        }
+    }
+    std::stable_sort(items.begin(), items.end(), [](const C &a, const C &b) { return a.val > b.val; });
+  }
+  if (temp <= 0.0f) return items[0].id;
+  const size_t K = items.size();
+  float probs[64];
+  float max_scaled = -1e9f;
+  for (size_t i = 0; i < K; i++) {
+    probs[i] = items[i].val / temp;
+    if (probs[i] > max_scaled) max_scaled = probs[i];
+  }
+  float sum = 0.0f;
+  for (size_t i = 0; i < K; i++) {
+    probs[i] = std::exp(probs[i] - max_scaled);
+    sum += probs[i];
+  }
+  for (size_t i = 0; i < K; i++) probs[i] /= sum;
+  const float p_thresh = probs[0] * min_p;
+  size_t valid_k = 0;
+  float valid_sum = 0.0f;
+  for (size_t i = 0; i < K; i++) {
+    if (probs[i] >= p_thresh) {
+      valid_k = i + 1;
+      valid_sum += probs[i];
+    } else {
+      break;
+    }
+  }
+  if (valid_k == 0) valid_k = 1;
+  for (size_t i = 0; i < valid_k; i++) probs[i] /= valid_sum;
+  float cum_p = 0.0f;
+  size_t cutoff = 0;
+  for (size_t i = 0; i < valid_k; i++) {
+    cum_p += probs[i];
+    cutoff = i + 1;
+    if (cum_p >= top_p) break;
+  }
+  const float r = or_prng_float(prng) * cum_p;
+  float acc = 0.0f;
+  uint32_t chosen = items[0].id;
+  for (size_t i = 0; i < cutoff; i++) {
+    acc += probs[i];
+    if (acc >= r) {
+      chosen = items[i].id;
+      break;
+    }
+  }
+  return chosen;
 }
 
 // ----------------------------------------------------------------------------
@@ -874,7 +1005,7 @@ extern "C" uint32_t or_model_forward_token(or_model *m, const float *x_in, uint3
     qkv_rope_token(m->qo.data(), m->kc[li].data(), m->vc[li].data(), m->q.data(), m->k.data(), m->v.data(), L.q_norm,
                    L.k_norm, c.n_q, c.n_kv, (uint32_t)D, c.rot_dim, 0, full ? m->inv_freq_f.data() : m->inv_freq_s.data(),
                    c.eps, clock, slot);
-    // decode uses layer 0's lists for every layer (model_dispatch.zig:349-351)
+    // decode uses layer 0's lists for every layer (model_dispatch.zig:133-135, forward.zig:44-47)
     const uint32_t *sl = full ? active : sliding;
     uint32_t S = full ? n_active : n_sliding;
     or_decode_attn(m->attn.data(), m->qo.data(), m->kc[li].data(), m->vc[li].data(), sl, S, c.n_q, c.n_kv, (uint32_t)D, 1.0f);

@@ -71,6 +71,15 @@ float or_softcap(float v);
 uint32_t or_sample_topk_greedy(const uint32_t *ids, const float *vals, size_t n, const uint32_t *recent, size_t n_recent,
                                float repeat_penalty, float frequency_penalty, float presence_penalty,
                                int suppress_thinking, int suppress_channel_close, int suppress_critique);
+/* Zig std.Random.DefaultPrng (Xoshiro256++ seeded by SplitMix64) and Random.float(f32) */
+void or_prng_seed(uint64_t *state4, uint64_t seed);
+uint64_t or_prng_next(uint64_t *state4);
+float or_prng_float(uint64_t *state4);
+/* Sampler.sampleTopK (src/sampler.zig:217-317); params = {temp, top_p, min_p, repeat,
+ * frequency, presence}; flags bit 0 suppress_thinking, 1 suppress_critique, 2
+ * suppress_channel_close; recent NULL = none; advances prng by one draw when it samples */
+uint32_t or_sample_topk(const uint32_t *ids, const float *vals, size_t n, const uint32_t *recent, size_t n_recent,
+                        const float *params, int flags, uint64_t *prng);
 
 /* ---- batched prefill ops (shaders/batch_*.wgsl) ---- */
 void or_batch_gemm_q4(float *Y, const uint32_t *W, const float *X, size_t N, size_t M, size_t K, int threads);

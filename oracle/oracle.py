@@ -62,6 +62,8 @@ _SIG = {
     "or_decode_attn": (None, [P(f32), P(f32), P(u16), P(u16), P(u32), u32, u32, u32, u32, f32]),
     "or_topk64": (None, [P(u32), P(f32), P(f32), sz]), "or_argmax": (u32, [P(f32), sz]), "or_softcap": (f32, [f32]),
     "or_sample_topk_greedy": (u32, [P(u32), P(f32), sz, P(u32), sz, f32, f32, f32, i32, i32, i32]),
+    "or_prng_seed": (None, [P(u64), u64]), "or_prng_next": (u64, [P(u64)]), "or_prng_float": (f32, [P(u64)]),
+    "or_sample_topk": (u32, [P(u32), P(f32), sz, P(u32), sz, P(f32), i32, P(u64)]),
     "or_batch_gemm_q4": (None, [P(f32), P(u32), P(f32), sz, sz, sz, i32]),
     "or_batch_fused_mlp_q4": (None, [P(f32), P(u32), P(u32), P(f32), sz, sz, sz, i32]),
     "or_batch_rmsnorm": (None, [P(f32), P(f32), P(f32), sz, sz, f32]),
@@ -324,3 +326,27 @@ def embed(table_bf16: np.ndarray, tokens, H: int) -> np.ndarray:
     out = np.empty((tok.size, H), np.float32)
     lib().or_embed(p(out, f32), p(np.ascontiguousarray(table_bf16, np.uint16), u16), p(tok, u32), tok.size, H)
     return out
+
+
+# ---- sampler ----------------------------------------------------------------------
+class Sampler:
+    """Sampler.sampleTopK (src/sampler.zig:217-317) with Zig's DefaultPrng stream."""
+
+    def __init__(self, seed: int, temp: float, top_p: float, min_p: float = 0.05, repeat_penalty: float = 1.1,
+                 frequency_penalty: float = 0.1, presence_penalty: float = 0.1, suppress_thinking: bool = False,
+                 suppress_critique: bool = False, suppress_channel_close: bool = False):
+        self.state = np.zeros(4, np.uint64)
+        lib().or_prng_seed(p(self.state, u64), seed)
+        self.params = np.array([temp, top_p, min_p, repeat_penalty, frequency_penalty, presence_penalty], np.float32)
+        self.flags = int(suppress_thinking) | (int(suppress_critique) << 1) | (int(suppress_channel_close) << 2)
+
+    def sample_topk(self, ids, vals, recent=None) -> int:
+        ids = np.ascontiguousarray(ids, np.uint32)
+        vals = np.ascontiguousarray(vals, np.float32)
+        rec = None if recent is None else np.ascontiguousarray(recent, np.uint32)
+        return int(lib().or_sample_topk(p(ids, u32), p(vals, f32), ids.size, p(rec, u32),
+                                        0 if rec is None else rec.size, p(self.params, f32), self.flags,
+                                        p(self.state, u64)))
+
+    def float32(self) -> float:
+        return float(lib().or_prng_float(p(self.state, u64)))

@@ -29,7 +29,7 @@ def test_ctypes_table_matches_header():
 def test_api_version_and_bad_args():
     from channel_b200 import _lib
     lib = _lib.load()
-    assert lib.ch_api_version() == 1
+    assert lib.ch_api_version() == 2
     # host-only validation paths: no device touched
     assert lib.ch_ctx_create(0, None) == _lib.CH_EINVAL
     assert b"NULL" in lib.ch_last_error()

@@ -96,4 +96,4 @@ def test_attention_softmax_properties(oracle):
     out = oracle.decode_attn(q, kc, vc, np.arange(100, 140), nq, nkv, D, 1 / 16)
     assert np.allclose(out, 1.0, atol=1e-5)  # convex combination of all-ones V
     out0 = oracle.decode_attn(q, kc, vc, np.array([], np.uint32), nq, nkv, D, 1 / 16)
-    assert np.all(out0 == 0)  # empty list: 0 * 1/(0 + 1e-9) (decode_attn.wgsl:297)
+    assert np.all(out0 == 0)  # empty list: 0 * 1/(0 + 1e-9) (decode_attn.wgsl:117)

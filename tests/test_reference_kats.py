@@ -147,3 +147,21 @@ def test_bf16_roundtrip_kat(oracle):
         back = l.or_bf16_to_f32(l.or_bf16_from_f32(v))
         assert abs(back - v) <= tol
     assert l.or_bf16_to_f32(l.or_bf16_from_f32(0.0)) == 0.0
+
+
+@pytest.mark.parametrize("case", KATS["sampler"], ids=lambda c: c["name"][:48])
+def test_sampler_kat_full_sampler_at_temp_zero(oracle, case):
+    """the same known answers through the full sampleTopK restatement (temp 0)"""
+    s = oracle.Sampler(42, 0.0, 0.95, repeat_penalty=case["repeat"], frequency_penalty=case["freq"],
+                       presence_penalty=case["pres"], suppress_thinking=bool(case["think"]),
+                       suppress_critique=bool(case["crit"]), suppress_channel_close=bool(case["close"]))
+    ids = [c[0] for c in case["cands"]]
+    vals = [c[1] for c in case["cands"]]
+    assert s.sample_topk(ids, vals, case["recent"]) == case["expect"]
+
+
+def test_sampler_kat_low_temperature(oracle):
+    """src/sampler.zig:448-452: Sampler.init(42, 0.01, 0.95), repeat_penalty 1.2, recent
+    [4373, 4373] over the three candidates of :437-441 -> 705"""
+    s = oracle.Sampler(42, 0.01, 0.95, repeat_penalty=1.2)
+    assert s.sample_topk([4373, 705, 1980], [18.0, 17.5, 16.0], [4373, 4373]) == 705

@@ -78,3 +78,43 @@ def test_streams_reject_bad_steps(ctx):
     assert e.value.status == L.CH_EINVAL
     assert b"stream" in lib.ch_last_error()
     gm.deinit()
+
+
+def test_config5_12b_streams_match_oracle_golden(ctx):
+    """A seeded 4-stream subset of BASELINE config 5 on the 12B-shape model (48 layers,
+    seed-3 weights): prompts of 16-64 ids, 8 greedy tokens each, all four streams in
+    every batched step.  Against tests/golden/config5_streams.npz (the oracle running
+    each stream alone, tests/golden/make_config5_streams.py): every token, the last
+    step's final-normed hidden state per stream (1e-3 relative) and the top-8 of its
+    softcapped logits (ids exact away from near-ties, values within 1e-3)."""
+    from pathlib import Path
+
+    from channel_b200 import GpuModelContext
+    from channel_b200.engine import config_12b
+    from channel_b200.streams import MultiStreamDecoder
+    from tests.gpu_util import assert_close
+    from tests.model_util import topk_ids_agree
+
+    g = np.load(Path(__file__).with_name("golden") / "config5_streams.npz")
+    cfg = config_12b()
+    rng = np.random.default_rng(int(g["prompt_seed"]))
+    n_streams, n_tokens = g["tokens"].shape
+    lens = rng.integers(int(g["lo"]), int(g["hi"]) + 1, n_streams)
+    prompts = [rng.integers(0, cfg.vocab_size, int(n)).astype(np.uint32) for n in lens]
+    gm = GpuModelContext.synthetic(ctx, cfg, int(g["weight_seed"]))
+    try:
+        dec = MultiStreamDecoder(gm, cfg, n_streams=n_streams, max_batch=n_streams)
+        got = dec.run(prompts, n_tokens)
+        for s in range(n_streams):
+            assert got[s] == [int(t) for t in g["tokens"][s]], f"stream {s}: {got[s]} != {g['tokens'][s].tolist()}"
+        normed = gm.streams_read_normed_x(n_streams)
+        logits = gm.streams_read_logits(n_streams).astype(np.float64)
+        for s in range(n_streams):
+            assert_close(normed[s], g["normed_x"][s], what=f"stream {s}: last step's normed x")
+            capped = 30.0 * np.tanh(logits[s] / 30.0)
+            top = np.lexsort((np.arange(cfg.vocab_size), -capped))[:8]
+            assert topk_ids_agree(top, g["ids"][s][:8], g["vals"][s][:8], tol=1e-3), f"stream {s}: top-8 ids"
+            np.testing.assert_allclose(capped[top], g["vals"][s][:8], rtol=1e-3, atol=1e-3)
+        assert ctx.device_status() == 0
+    finally:
+        gm.deinit()

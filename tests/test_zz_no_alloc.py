@@ -33,9 +33,12 @@ def test_noalloc_rejects_shapes_beyond_its_scratch():
 @pytest.mark.gpu
 def test_noalloc_matches_gemv_q4_on_consecutive_calls(ctx, oracle):
     lib = L.load()
-    # a shape at the row limit, then a model shape, then a ragged one: each
-    # call reuses the counters the previous one left behind
-    for M, K, seed in [(32768, 1024, 1), (3840, 15360, 2), (8192, 3840, 3), (48, 192, 4)]:
+    # a shape at the row limit, model shapes, then shapes with fewer row tiles than
+    # CTAs (64 x 16384: 4 row tiles, 1024 x 8192: 64, 48 x 192: 3), where several CTAs
+    # feed each row tile through the shared counters and partial slots: each call
+    # reuses the counters the previous one left behind
+    for M, K, seed in [(32768, 1024, 1), (3840, 15360, 2), (8192, 3840, 3), (64, 16384, 5), (1024, 8192, 6),
+                       (48, 192, 4)]:
         W = oracle.gen_q4(M, K, oracle.tensor_seed(7, seed, 0))
         Wd = dev(W)
         tiles = empty(lib.ch_q4_tile_bytes(M, K), torch.uint8)
@@ -49,7 +52,8 @@ def test_noalloc_matches_gemv_q4_on_consecutive_calls(ctx, oracle):
             call(lib.ch_gemv_q4_noalloc, tiles.data_ptr(), M, K, xd.data_ptr(), y.data_ptr(), status.data_ptr(),
                  ctx.stream)
             ctx.synchronize()
-            assert_close(host(y), host(y_ref), what=f"noalloc {M}x{K} call {rep}")
+            assert_close(host(y), host(y_ref), what=f"noalloc {M}x{K} call {rep} vs ch_gemv_q4")
+            assert_close(host(y), oracle.gemv_q4(W, x, M, K), what=f"noalloc {M}x{K} call {rep} vs oracle")
         assert int(status.item()) == 0
     # default stream and no status word
     M, K = 256, 2048
