@@ -8,8 +8,9 @@ prefilled with the batched path, then greedy decode at clocks 512.. (config 4
 decodes 256 tokens; warmup + steps default to 8 + 248 = 256).  Per-token weight
 stream is 7.2 GB (> 126 MB L2), so no L2 flush is needed between steps.
 
-  value : device-resident loop (ch_decode_run: ring lists pre-planned in HBM, the
-          greedy token fed back on the device), CUDA events on the library stream.
+  value : device-resident loop (ch_decode_run_ring: each step's ring lists built on the
+          device, the greedy token fed back on the device), CUDA events on the library
+          stream.
   e2e   : the reference-facing call ch_forward_token per token with host buffers
           (x from the host bf16 table, host ring lists, top-64 read back).
   --impl reference : the reference CPU path = the oracle restatement (Zig cannot
@@ -454,27 +455,28 @@ def ours(args):
         return
 
     # ---- value: device-resident loop -------------------------------------------------
+    # Every step builds its own ring lists on the device (ch_decode_run_ring: activate the
+    # clock's slot, full and sliding lists), embeds the fed-back token and decodes: no
+    # host work and no upload per token inside the timed region.
+    from channel_b200 import DeviceRing
     ring, first, prefill_s = fresh_prefill()
-    plan = []
-    for i in range(n_total):
-        clock = PROMPT + i
-        slot, act, sli = step_lists(ring, clock)
-        plan.append((clock, slot, act, sli))
-    gm.decode_plan(plan)
+    dring = DeviceRing(ctx)
+    dring.upload(ring)
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    gm.decode_run(first, args.warmup)
-    ctx.synchronize()
+    gm.decode_run_ring(dring, ring, first, PROMPT, args.warmup)
+    warm_tokens = [int(t) for t in gm.decode_tokens(args.warmup)]
     if dist:
         dist.barrier()
     torch.cuda.synchronize()
     with ClockSampler(local) as clk:
         ev0.record(stream)
-        gm.decode_continue(args.steps)
+        gm.decode_run_ring(dring, ring, warm_tokens[-1], PROMPT + args.warmup, args.steps)
         ev1.record(stream)
         ev1.synchronize()
     ms = ev0.elapsed_time(ev1)
     torch.cuda.synchronize()
-    tokens = gm.decode_tokens(n_total)
+    tokens = warm_tokens + [int(t) for t in gm.decode_tokens(args.steps)]
+    dring.deinit()
     if dist:
         t = torch.tensor([ms], device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -569,7 +571,7 @@ def ours(args):
         cpu = cpu_sample(steps=4, warmup=1)
         cpu = {k: cpu[k] for k in ("value", "unit", "cores", "cpu_model", "kind", "sample", "timed_s")}
 
-    launches_per_step = 2  # step_begin + the decode-step kernel
+    launches_per_step = 3  # device ring lists + step_begin + the decode-step kernel
     if rank == 0:
         line = {
             "metric": "decode tok/s (12B-shape Q4) at 1/2/4/8 GPU; Q4 GEMV HBM GB/s vs peak",

@@ -30,7 +30,7 @@ from pathlib import Path
 
 import numpy as np
 
-TRACE_CTAS, TRACE_PHASES, TRACE_MARKS = 256, 512, 8
+TRACE_CTAS, TRACE_PHASES, TRACE_MARKS = 256, 512, 12
 COLS = ["staging", "prologue", "tiles/core", "combine", "arrive+pre", "barrier"]
 
 

@@ -6,6 +6,8 @@ the engine loads it and raises if it is missing -- there is no CPU fallback.
 """
 from ._lib import ChannelError, load  # noqa: F401
 from .engine import (  # noqa: F401
+    DeviceRing,
+    DeviceSampler,
     DynamicRingBuffer,
     GpuContext,
     GpuModelContext,

@@ -292,7 +292,10 @@ CH_DEV float softcap(float v) {
   return __fmul_rn(30.0f, tanhf(__fmul_rn(v, 1.0f / 30.0f)));
 }
 
-// K-th largest 64-bit key held E-per-thread across the block (keys unique except 0 padding)
+// Threshold of the K largest 64-bit keys held E-per-thread across the block (keys unique
+// except 0 padding): the K-th largest key, or a smaller value that no key outside the K
+// largest reaches -- keys >= the result are exactly the K largest (radix select, 8 bits
+// per pass from the top, stopping once the selected bin holds exactly the keys still needed)
 template <int E>
 CH_DEV uint64_t block_kth_largest(const uint64_t (&k)[E], int K, uint32_t *hist, uint32_t *sh) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -335,7 +338,11 @@ CH_DEV uint64_t block_kth_largest(const uint64_t (&k)[E], int K, uint32_t *hist,
     need = (int)sh[1];
     prefix |= (uint64_t)sel << shift;
     mask |= 0xFFull << shift;
+    // every key of the selected bin is among the K largest: the prefix (lower bits 0)
+    // already separates them from the rest, so later digits change nothing
+    const bool done = hist[sel] == (uint32_t)need;
     __syncthreads();
+    if (done) break;
   }
   return prefix;
 }

@@ -49,6 +49,7 @@ constexpr int MK_NW = 16;          // warps per CTA (all stream + compute)
 constexpr int MK_SPW = CH_MK_SPW;  // bulk-copy stages per warp
 constexpr int MK_CT = CH_MK_CT;    // tiles per stage
 constexpr int MK_STAGE = MK_CT * kTileBytes;
+static_assert(MK_CT % 2 == 0, "the unrolled chunk loop consumes tiles in pairs");
 constexpr int MK_THREADS = MK_NW * 32;
 constexpr uint32_t kMinChunk = 32;  // slots per attention work item before splitting further stops paying
 constexpr uint32_t kWinSlots = 64;  // attention slots per work item staged in shared memory before the barrier
@@ -62,16 +63,25 @@ int mk_warps() { return MK_NW; }
 // Optional per-phase timeline (build with -DCH_PHASE_TRACE, see bench_phases.py):
 // thread 0 of every CTA records %globaltimer at seven points of each phase.
 #ifdef CH_PHASE_TRACE
-constexpr int kTraceCtas = 256, kTracePhases = 512, kTraceMarks = 8;
+constexpr int kTraceCtas = 256, kTracePhases = 512, kTraceMarks = 12;
 __device__ unsigned long long g_phase_trace[kTraceCtas * kTracePhases * kTraceMarks];
 #define PHASE_MARK(pi, k)                                                                               \
   do {                                                                                                  \
     if (threadIdx.x == 0 && blockIdx.x < kTraceCtas && (pi) < kTracePhases)                             \
       g_phase_trace[((size_t)blockIdx.x * kTracePhases + (pi)) * kTraceMarks + (k)] = globaltimer_ns(); \
   } while (0)
+// marks 8..11 from lane 0 of warp w inside the tile loop (w = 0: marks 8, 9; w = 15: 10, 11)
+#define WARP_MARK(pi, k, w)                                                                             \
+  do {                                                                                                  \
+    if (threadIdx.x == (w) * 32 && blockIdx.x < kTraceCtas && (pi) < kTracePhases)                      \
+      g_phase_trace[((size_t)blockIdx.x * kTracePhases + (pi)) * kTraceMarks + (k)] = globaltimer_ns(); \
+  } while (0)
 #else
 #define PHASE_MARK(pi, k) \
   do {                    \
+  } while (0)
+#define WARP_MARK(pi, k, w) \
+  do {                      \
   } while (0)
 #endif
 
@@ -573,7 +583,7 @@ CH_DEV void cta_combine(const Phase &p, const MegaArgs &a, const float *wpart) {
 // f16 hi/lo B fragments at xq (sxs unused)
 template <int FMT, bool LIMBS>
 CH_DEV void gemv_tiles(const Phase &p, const MegaArgs &a, uint32_t gw, const SmemLayout &L, const uint2 *xq,
-                       const float *sxs, uint32_t &cidx, Stream &st, bool &ok, uint64_t pol) {
+                       const float *sxs, uint32_t &cidx, Stream &st, bool &ok, uint64_t pol, uint32_t pi) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int g = lane >> 2, t = lane & 3;
   uint8_t *my_stages = L.stages + (size_t)warp * MK_SPW * MK_STAGE;
@@ -624,6 +634,10 @@ CH_DEV void gemv_tiles(const Phase &p, const MegaArgs &a, uint32_t gw, const Sme
   for (uint32_t j = 0; j < nchunks; j++) {
     const uint32_t s = cidx % MK_SPW;
     if (ok && !mbar_wait_bounded(&my_bars[s], (cidx / MK_SPW) & 1, a.err)) ok = false;
+    if (j == 0) {
+      WARP_MARK(pi, 8, 0);
+      WARP_MARK(pi, 10, MK_NW - 1);
+    }
     const uint8_t *stg = my_stages + (size_t)s * MK_STAGE;
     const uint32_t t0 = tb + j * MK_CT;
     const uint32_t nt = min((uint32_t)MK_CT, te - t0);
@@ -669,6 +683,8 @@ CH_DEV void gemv_tiles(const Phase &p, const MegaArgs &a, uint32_t gw, const Sme
     __syncwarp();
   }
   if (cur_rt != 0xFFFFFFFFu) flush(cur_rt, kt_begin, te - cur_rt * KT);
+  WARP_MARK(pi, 9, 0);
+  WARP_MARK(pi, 11, MK_NW - 1);
 }
 
 // ---------------------------------------------------------------------------
@@ -1312,11 +1328,11 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(const MegaAr
       const uint2 *xq = reinterpret_cast<const uint2 *>(L.u);
       const float *sxs = reinterpret_cast<const float *>(L.u) + p.K;
       if (p.pm == PM_DIRECT || p.pm == PM_GELU)  // Q4 o / down: f16 fragments
-        gemv_tiles<FMT_Q4, false>(p, a, gw, L, xq, sxs, cidx, st, ok, pol);
+        gemv_tiles<FMT_Q4, false>(p, a, gw, L, xq, sxs, cidx, st, ok, pol, pi);
       else if (p.fmt == FMT_Q4)
-        gemv_tiles<FMT_Q4, true>(p, a, gw, L, xq, sxs, cidx, st, ok, pol);
+        gemv_tiles<FMT_Q4, true>(p, a, gw, L, xq, sxs, cidx, st, ok, pol, pi);
       else
-        gemv_tiles<FMT_Q8, true>(p, a, gw, L, xq, sxs, cidx, st, ok, pol);
+        gemv_tiles<FMT_Q8, true>(p, a, gw, L, xq, sxs, cidx, st, ok, pol, pi);
       __syncthreads();
       PHASE_MARK(pi, 3);
       cta_combine(p, a, L.wpart);

@@ -352,6 +352,56 @@ class GpuModelContext:
         L.check(L.load().ch_decode_tokens(self.handle, _ptr(t, C.c_uint32), n))
         return t
 
+    def decode_run_ring(self, ring_dev: "DeviceRing", host_ring: Optional["DynamicRingBuffer"], first_token: int,
+                        first_clock: int, n_steps: int) -> None:
+        """device-resident loop whose ring lists are built on the device (ch_decode_run_ring)"""
+        L.check(L.load().ch_decode_run_ring(self.handle, ring_dev.h, host_ring.h if host_ring else None, first_token,
+                                            first_clock, n_steps))
+
+    def set_sampler(self, sampler: Optional["DeviceSampler"]) -> None:
+        """device loops sample with `sampler` (Sampler.sampleTopK on the device); None = greedy"""
+        L.check(L.load().ch_model_set_sampler(self.handle, sampler.h if sampler else None))
+
+
+class DeviceRing:
+    """device copy of a ring's layer-0 slot metadata (ch_ring_dev_*)"""
+
+    def __init__(self, ctx: GpuContext):
+        h = C.c_void_p()
+        L.check(L.load().ch_ring_dev_create(ctx.handle, C.byref(h)))
+        self.h = h.value
+
+    def upload(self, ring: "DynamicRingBuffer") -> None:
+        L.check(L.load().ch_ring_dev_upload(self.h, ring.h))
+
+    def deinit(self) -> None:
+        if self.h:
+            L.load().ch_ring_dev_destroy(self.h)
+            self.h = None
+
+
+class DeviceSampler:
+    """Sampler (src/sampler.zig:55-82) whose sampleTopK runs on the device (ch_sampler_*)"""
+
+    def __init__(self, ctx: GpuContext, seed: int, temp: float, top_p: float, min_p: float = 0.05,
+                 repeat_penalty: float = 1.1, frequency_penalty: float = 0.1, presence_penalty: float = 0.1,
+                 suppress_thinking: bool = False, suppress_critique: bool = False,
+                 suppress_channel_close: bool = False, recent_cap: int = 8192):
+        p = L.ChSamplerParams(temp, top_p, min_p, repeat_penalty, frequency_penalty, presence_penalty, 64,
+                              int(suppress_thinking), int(suppress_critique), int(suppress_channel_close), 0)
+        h = C.c_void_p()
+        L.check(L.load().ch_sampler_create(ctx.handle, C.byref(p), seed, recent_cap, C.byref(h)))
+        self.h = h.value
+
+    def set_recent(self, tokens: Sequence[int]) -> None:
+        t = np.ascontiguousarray(tokens, np.uint32)
+        L.check(L.load().ch_sampler_set_recent(self.h, _ptr(t, C.c_uint32), t.size))
+
+    def deinit(self) -> None:
+        if self.h:
+            L.load().ch_sampler_destroy(self.h)
+            self.h = None
+
 
 def gpu_dispatch_forward_token(gpu: GpuModelContext, x: np.ndarray, clock: int, slot_idx: int,
                                active_slots: Sequence[int], sliding_slots: Sequence[int],

@@ -43,3 +43,8 @@ def topk_ids_agree(ids, rid, rvals, tol=1e-4):
     clear[1:] &= gaps > tol * np.maximum(1.0, np.abs(rvals[1:]))
     clear[-1] = False
     return bool(np.all(ids[clear] == rid[clear])) and set(ids[:-4]) <= set(rid)
+
+
+def topk_diff(ids, vals, rid, rvals):
+    """(position, id, value, oracle id, oracle value) of every position where the ids differ"""
+    return [(i, int(ids[i]), float(vals[i]), int(rid[i]), float(rvals[i])) for i in range(len(rid)) if ids[i] != rid[i]]

@@ -14,7 +14,7 @@ import pytest
 from channel_b200 import DynamicRingBuffer, GpuModelContext, gpu_dispatch_forward_token, gpu_dispatch_prefill_batch
 from channel_b200 import _lib as L
 from tests.gpu_util import assert_close
-from tests.model_util import ring_step_lists, small_config, topk_ids_agree
+from tests.model_util import ring_step_lists, small_config, topk_diff, topk_ids_agree
 
 pytestmark = pytest.mark.gpu
 SEED = 5
@@ -123,7 +123,12 @@ def test_bf16_model_quantized_on_load_matches_oracle(ctx, oracle):
             gtok, gc = gpu_dispatch_forward_token(gm, x, clock, slot, act, sli)
             r, rid, rvals = om.forward_token(x, clock, slot, act, sli)
             assert gtok == r, f"bf16 model: token at clock {clock}"
-            assert topk_ids_agree([c.id for c in gc], rid, rvals)
+            # the prompt went through the tensor-core prefill (f32 sums not rounded like the
+            # shader's, ~1e-4 relative on the hidden state), and logits of ~1 with cancelling
+            # terms amplify that: ids are held exact away from near-ties at the 1e-3 float bar
+            gi, gv = [c.id for c in gc], [c.val for c in gc]
+            assert topk_ids_agree(gi, rid, rvals, tol=1e-3), f"clock {clock}: {topk_diff(gi, gv, rid, rvals)}"
+            np.testing.assert_allclose(gv, rvals, rtol=1e-3, atol=1e-3)
             assert_close(gm.read_normed_x(), om.normed_x(), what=f"bf16 model: normed x at clock {clock}")
             tok = int(gtok)
     finally:
