@@ -118,6 +118,7 @@ SIGNATURES = {
     "ch_rmsnorm": (i32, [vp, vp, vp, vp, u32, u32, f32]),
     "ch_add_rmsnorm": (i32, [vp, vp, vp, vp, vp, u32, u32, f32, f32]),
     "ch_decode_attention": (i32, [vp, vp, vp, vp, vp, vp, vp, u32, u32, u32, u32, u32, u32, u32, f32, f32, f32, vp]),
+    "ch_batch_causal_attention": (i32, [vp, vp, vp, vp, vp, u32, u32, u32, u32, u32, f32, i32, vp]),
     "ch_topk64": (i32, [vp, vp, u32, vp, vp]),
     "ch_batch_gemm_q4": (i32, [vp, vp, u32, u32, vp, u32, vp]),
     "ch_batch_fused_mlp_q4": (i32, [vp, vp, u32, u32, vp, u32, vp]),

@@ -205,6 +205,7 @@ struct ch_model {
   uint32_t *h_ids = nullptr;
   float *h_vals = nullptr;
   uint32_t *h_run = nullptr;  // [2] staging for ch_decode_run
+  uint32_t *h_status = nullptr;  // the device status word read back with each forward token
   // graphs
   cudaGraphExec_t g_host_logits = nullptr, g_host_nologits = nullptr, g_loop = nullptr;
   bool pdl = true;
@@ -292,7 +293,7 @@ static void free_model(ch_model *m) {
   for (uint32_t r = 0; r < m->world && r < kMaxWorld; r++)
     if (r != m->rank && m->peer_arena[r]) cudaIpcCloseMemHandle(m->peer_arena[r]);
   cudaFree(m->arena);
-  void *host[] = {m->h_x, m->h_sp, m->h_lists, m->h_ids, m->h_vals, m->h_run, m->h_rope};
+  void *host[] = {m->h_x, m->h_sp, m->h_lists, m->h_ids, m->h_vals, m->h_run, m->h_rope, m->h_status};
   for (void *p : host) cudaFreeHost(p);
   if (m->g_host_logits) cudaGraphExecDestroy(m->g_host_logits);
   if (m->g_host_nologits) cudaGraphExecDestroy(m->g_host_nologits);
@@ -404,6 +405,7 @@ static int alloc_model_buffers(ch_model *m) {
   CH_CUDA(cudaMallocHost(&m->h_sp, sizeof(StepParams)));
   CH_CUDA(cudaMallocHost(&m->h_lists, 2 * kSlots * sizeof(uint32_t)));
   CH_CUDA(cudaMallocHost(&m->h_ids, 64 * sizeof(uint32_t)));
+  CH_CUDA(cudaMallocHost(&m->h_status, sizeof(uint32_t)));
   CH_CUDA(cudaMallocHost(&m->h_vals, 64 * sizeof(float)));
   CH_CUDA(cudaMallocHost(&m->h_run, 2 * sizeof(uint32_t)));
   // RoPE inverse frequencies: same formula as the oracle (double pow, one rounding)
@@ -1346,7 +1348,12 @@ extern "C" int ch_forward_token(ch_model *m, const float *x, uint32_t clock, uin
     CH_CUDA(cudaMemcpyAsync(m->h_ids, m->ids, 64 * 4, cudaMemcpyDeviceToHost, s));
     CH_CUDA(cudaMemcpyAsync(m->h_vals, m->vals, 64 * 4, cudaMemcpyDeviceToHost, s));
   }
+  // the step's device status (a bounded wait that gave up, a bad slot) comes back with
+  // the results, and is cleared for the next call
+  CH_CUDA(cudaMemcpyAsync(m->h_status, m->ctx->err, 4, cudaMemcpyDeviceToHost, s));
+  CH_CUDA(cudaMemsetAsync(m->ctx->err, 0, 4, s));
   CH_CUDA(cudaStreamSynchronize(s));
+  if (const int rc = status_from_flags(*m->h_status)) return rc;
   if (topk_out)
     for (int i = 0; i < 64; i++) topk_out[i] = ch_topk{m->h_ids[i], m->h_vals[i]};
   if (token_out) *token_out = m->h_ids[0];
@@ -2310,6 +2317,19 @@ extern "C" int ch_add_rmsnorm(ch_ctx *c, float *x, const float *r, const float *
                               float eps, float scalar) {
   if (!c || !x || !r || !w || !y) return fail(CH_EINVAL, "NULL argument");
   CH_CUDA(launch_add_rmsnorm_rows(x, r, w, y, n, h, eps, scalar, c->stream));
+  return CH_OK;
+}
+// batch_causal_attn.wgsl:25-223 on its own: token t of the batch attends to
+// slots[0 .. num_prev + t + 1) (the last 1,024 of them on a sliding layer)
+extern "C" int ch_batch_causal_attention(ch_ctx *c, const float *q, const void *k_cache, const void *v_cache,
+                                         const uint32_t *slots, uint32_t n_tokens, uint32_t num_prev, uint32_t nq,
+                                         uint32_t nkv, uint32_t head_dim, float scale, int is_sliding, float *out) {
+  if (!c || !q || !k_cache || !v_cache || !slots || !out) return fail(CH_EINVAL, "NULL argument");
+  if (head_dim != 256 || nkv == 0 || nq % nkv || n_tokens == 0 || num_prev + n_tokens > kSlots)
+    return fail(CH_EINVAL, "batch_causal_attention: head_dim 256, nq % nkv == 0, 1 <= num_prev + n <= 4096");
+  BatchAttnArgs a{q, static_cast<const __half *>(k_cache), static_cast<const __half *>(v_cache), slots, n_tokens,
+                  num_prev, nq, nkv, head_dim, scale, is_sliding ? 1 : 0, out};
+  CH_CUDA(launch_batch_causal_attn(a, c->stream));
   return CH_OK;
 }
 extern "C" int ch_decode_attention(ch_ctx *c, const float *qkv, const float *q_norm, const float *k_norm, void *k_cache,

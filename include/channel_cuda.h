@@ -295,6 +295,13 @@ int ch_decode_attention(ch_ctx *ctx, const float *qkv_dev, const float *q_norm_d
                         void *k_cache_dev, void *v_cache_dev, const uint32_t *slots_dev, uint32_t n_slots, uint32_t clock,
                         uint32_t slot, uint32_t nq, uint32_t nkv, uint32_t head_dim, uint32_t rotary_dim, float theta,
                         float eps, float scale, float *out_dev);
+/* batch_causal_attn.wgsl (25-223): q_dev = n_tokens x nq x head_dim (normed and roped),
+ * K/V caches f16 [4096][nkv*head_dim]; token t attends to slots_dev[0 .. num_prev+t+1),
+ * on a sliding layer (is_sliding) to the last 1,024 of them (:53); out_dev like q_dev.
+ * Pairs of q heads per kv head run on the tensor cores (mma.sync, f32 accumulate). */
+int ch_batch_causal_attention(ch_ctx *ctx, const float *q_dev, const void *k_cache_dev, const void *v_cache_dev,
+                              const uint32_t *slots_dev, uint32_t n_tokens, uint32_t num_prev, uint32_t nq,
+                              uint32_t nkv, uint32_t head_dim, float scale, int is_sliding, float *out_dev);
 /* topk_pass1/2.wgsl: softcap + top-64, value desc then lowest index */
 int ch_topk64(ch_ctx *ctx, const float *logits_dev, uint32_t vocab, uint32_t *ids_dev, float *vals_dev);
 /* batch_gemm_q4.wgsl (Y[t*rows + r]) and batch_fused_mlp_q4.wgsl on tiles, on the

@@ -195,6 +195,15 @@ def decode_attn(q, k_cache, v_cache, slots, nq, nkv, D, scale):
     return out
 
 
+def batch_causal_attn(Q, k_cache, v_cache, slots, N, num_prev, nq, nkv, D, scale, is_sliding) -> np.ndarray:
+    """batch_causal_attn.wgsl:25-223: Q [N][nq*D] -> out [N][nq*D]"""
+    out = np.empty((N, nq * D), np.float32)
+    sl = np.ascontiguousarray(slots, np.uint32)
+    lib().or_batch_causal_attn(p(out, f32), p(np.ascontiguousarray(Q, np.float32), f32), p(k_cache, u16),
+                               p(v_cache, u16), p(sl, u32), N, num_prev, nq, nkv, D, scale, int(is_sliding), nthreads())
+    return out
+
+
 def batch_gemm_q4(W, X, N, M, K) -> np.ndarray:
     Y = np.empty((N, M), np.float32)
     lib().or_batch_gemm_q4(p(Y, f32), p(W, u32), p(np.ascontiguousarray(X, np.float32), f32), N, M, K, nthreads())

@@ -193,3 +193,104 @@ def test_tp_decode_matches_oracle(oracle, world):
         assert loop == loop_ref, f"rank {rank}: device-loop tokens after prefill"
     for rank in range(1, world):
         assert res[rank][0] == res[0][0]
+
+
+# ---------------------------------------------------------------------------
+# Failure detection: a rank that leaves between steps.  Rank 1 stops calling (its
+# process and memory stay alive: nothing of it is in flight and its arena stays
+# mapped), the peers learn of it only through the decode kernel's bounded waits:
+# rank 0's next ch_forward_token must come back with CH_ETIMEOUT within the bound
+# (2 s per wait, and a launch that gave up once stops waiting), and rank 0's
+# context must still run work afterwards.  Host signalling is through queues; no
+# NCCL and no multicast memory are involved.
+def _leave_worker(rank, world, port, xs, plan, q_out, q_left, q_done):
+    try:
+        os.environ["NCCL_NVLS_ENABLE"] = "0"
+        import time
+
+        import torch.distributed as dist
+
+        from channel_b200 import GpuContext, GpuModelContext, gpu_dispatch_forward_token
+        from channel_b200.engine import attach_tensor_parallel
+        torch.cuda.set_device(rank)
+        dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
+        ctx = GpuContext.init(rank)
+        cfg = _tp_config(world)
+        gm = GpuModelContext.synthetic_sharded(ctx, cfg, SEED, rank, world)
+        attach_tensor_parallel(gm)
+        gm.zero_state()
+        dist.barrier()
+        toks = []
+        for x, (clock, slot, act, sli) in zip(xs[:3], plan[:3]):  # three steps together
+            toks.append(int(gpu_dispatch_forward_token(gm, x, clock, slot, act, sli)[0]))
+        ctx.synchronize()
+        dist.barrier()  # every rank is between steps: nothing in flight
+        if rank == 1:
+            q_left.put(1)  # leave: no further calls, memory kept until rank 0 is done
+            q_done.get(timeout=300)
+            gm.deinit()
+            ctx.deinit()
+            q_out.put((rank, toks, None, None, None))
+            return
+        q_left.get(timeout=120)
+        x, (clock, slot, act, sli) = xs[3], plan[3]
+        t0 = time.time()
+        status = None
+        try:
+            gpu_dispatch_forward_token(gm, x, clock, slot, act, sli)
+        except L.ChannelError as e:
+            status = e.status
+        elapsed = time.time() - t0
+        # the context still works: a plain single-GPU call on it
+        lib = L.load()
+        flags = C.c_uint32(0)
+        L.check(lib.ch_ctx_device_status(ctx.handle, C.byref(flags)))
+        y = torch.empty(16, dtype=torch.float32, device="cuda")
+        xx = torch.ones(64, dtype=torch.float32, device="cuda")
+        tiles = torch.zeros(lib.ch_q4_tile_bytes(16, 64), dtype=torch.uint8, device="cuda")
+        L.check(lib.ch_gemv_q4(ctx.handle, tiles.data_ptr(), 16, 64, xx.data_ptr(), y.data_ptr()))
+        ctx.synchronize()
+        usable = bool(torch.isfinite(y).all().item())
+        q_done.put(1)
+        q_out.put((rank, toks, status, elapsed, usable))
+        # rank 0's arena was mapped by rank 1: it is freed only after rank 1 let go
+        gm.deinit()
+        ctx.deinit()
+    except Exception as e:  # report instead of hanging the parent
+        q_out.put((rank, None, None, None, repr(e)))
+
+
+@pytest.mark.gpu
+def test_tp_rank_leaving_makes_next_step_time_out(oracle):
+    world = 2
+    if torch.cuda.device_count() < world:
+        pytest.skip("needs 2 GPUs")
+    from channel_b200 import DynamicRingBuffer
+    cfg = _tp_config(world)
+    w = oracle.SyntheticWeights(cfg, SEED)
+    ring = DynamicRingBuffer(cfg.num_hidden_layers, 0)
+    xs, plan = [], []
+    for clock, tok in enumerate([17, 3, 99, 5]):
+        slot, act, sli = ring_step_lists(ring, cfg, clock)
+        xs.append(oracle.embed(w.embed, [tok], cfg.hidden_size)[0])
+        plan.append((clock, slot, act, sli))
+    ctx = mp.get_context("spawn")
+    q_out, q_left, q_done = ctx.Queue(), ctx.Queue(), ctx.Queue()
+    port = _free_port()
+    ps = [ctx.Process(target=_leave_worker, args=(r, world, port, xs, plan, q_out, q_left, q_done))
+          for r in range(world)]
+    for p in ps:
+        p.start()
+    res = {}
+    for _ in range(world):
+        rank, toks, status, elapsed, usable = q_out.get(timeout=600)
+        res[rank] = (toks, status, elapsed, usable)
+    for p in ps:
+        p.join(timeout=120)
+    assert res[0][0] is not None, f"rank 0 failed: {res[0][3]}"
+    assert res[1][0] is not None, f"rank 1 failed: {res[1][3]}"
+    assert res[0][0] == res[1][0], "the steps taken together agree"
+    _, status, elapsed, usable = res[0]
+    assert status == L.CH_ETIMEOUT, f"rank 0 got {status}"
+    assert elapsed < 20.0, f"the bounded waits took {elapsed:.1f} s"
+    assert usable, "rank 0's context must still run work after the timeout"
