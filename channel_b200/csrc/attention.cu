@@ -45,12 +45,7 @@ namespace {
 constexpr uint32_t kMinChunk = 64;  // slots per CTA before splitting further stops paying
 }
 
-// ONEPASS (batches of tokens): one pass over the chunk with an online softmax per warp --
-// each slot's K and V rows are fetched together and the running max, sum and weighted V
-// are rescaled when the max grows -- instead of a scores pass, the softmax statistics
-// and a second pass over V.  A batch step is many CTA waves each bound by memory
-// round trips, and one pass halves them.  Same partial format for the split combine.
-template <int R, bool ONEPASS>
+template <int R>
 __global__ void __launch_bounds__(kAttnThreads) decode_attn_kernel(const AttnArgs a, int max_splits, int chunk_cap) {
   constexpr int D = 256, EPL = D / 32;  // elements per lane
   extern __shared__ __align__(16) float sm[];
@@ -141,111 +136,6 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attn_kernel(const AttnArg
 #pragma unroll
     for (int e = 0; e < EPL; e++) qr[h][e] = q_s[h * D + lane * EPL + e];
 
-  if constexpr (ONEPASS) {
-    constexpr int kU = 4;  // slots per warp iteration, K and V rows of all in flight together
-    float m[R], l[R], acc[R][EPL];
-#pragma unroll
-    for (int h = 0; h < R; h++) {
-      m[h] = -1e9f;  // decode_attn.wgsl:81
-      l[h] = 0.f;
-#pragma unroll
-      for (int e = 0; e < EPL; e++) acc[h][e] = 0.f;
-    }
-    for (uint32_t i0 = warp; i0 < n; i0 += kU * kAttnWarps) {
-      uint4 kw[kU], vw[kU];
-      int kind[kU];
-#pragma unroll
-      for (int u = 0; u < kU; u++) {
-        const uint32_t i = i0 + u * kAttnWarps;
-        kind[u] = 3;
-        if (i < n) {
-          const uint32_t phys = slist[i];
-          if (phys == sp.slot) {
-            kind[u] = 1;
-          } else if (phys >= a.cache_slots) {
-            kind[u] = 2;
-          } else {
-            const size_t off = (size_t)phys * kv_dim + (size_t)kvh * D + lane * EPL;
-            kw[u] = *reinterpret_cast<const uint4 *>(k_cache + off);
-            vw[u] = *reinterpret_cast<const uint4 *>(v_cache + off);
-            kind[u] = 0;
-          }
-        }
-      }
-#pragma unroll
-      for (int u = 0; u < kU; u++) {
-        if (kind[u] == 3) continue;
-        float kv[EPL], vv[EPL];
-        const bool valid = kind[u] != 2;
-        if (kind[u] == 1) {
-#pragma unroll
-          for (int e = 0; e < EPL; e++) kv[e] = k_new[lane * EPL + e], vv[e] = v_new[lane * EPL + e];
-        } else if (kind[u] == 0) {
-          const __half2 *kp = reinterpret_cast<const __half2 *>(&kw[u]);
-          const __half2 *vp = reinterpret_cast<const __half2 *>(&vw[u]);
-#pragma unroll
-          for (int e = 0; e < EPL / 2; e++) {
-            const float2 k2 = __half22float2(kp[e]), v2 = __half22float2(vp[e]);
-            kv[2 * e] = k2.x, kv[2 * e + 1] = k2.y, vv[2 * e] = v2.x, vv[2 * e + 1] = v2.y;
-          }
-        } else {
-#pragma unroll
-          for (int e = 0; e < EPL; e++) kv[e] = vv[e] = 0.f;
-          if (lane == 0) atomicOr(a.err, DEV_ERR_BAD_LIST);
-        }
-#pragma unroll
-        for (int h = 0; h < R; h++) {
-          float dot = 0.f;
-#pragma unroll
-          for (int e = 0; e < EPL; e++) dot = __fmaf_rn(qr[h][e], kv[e], dot);
-          dot = warp_sum(dot);
-          const float sc_ = valid ? __fmul_rn(dot, a.scale) : -INFINITY;
-          if (sc_ > m[h]) {  // the running max grows: rescale what this warp has so far
-            const float c = expf(__fsub_rn(m[h], sc_));
-            l[h] = __fmul_rn(l[h], c);
-#pragma unroll
-            for (int e = 0; e < EPL; e++) acc[h][e] = __fmul_rn(acc[h][e], c);
-            m[h] = sc_;
-          }
-          const float p = expf(__fsub_rn(sc_, m[h]));
-          l[h] = __fadd_rn(l[h], p);
-#pragma unroll
-          for (int e = 0; e < EPL; e++) acc[h][e] = __fmaf_rn(p, vv[e], acc[h][e]);
-        }
-      }
-    }
-    // fold the warps: max over warps, each warp's sums scaled to it, added in warp order
-    float *wm = sc;              // [warps][R] warp maxima, then factors
-    float *wl = sc + kAttnWarps * R;
-    if (lane == 0)
-#pragma unroll
-      for (int h = 0; h < R; h++) wm[warp * R + h] = m[h], wl[warp * R + h] = l[h];
-#pragma unroll
-    for (int h = 0; h < R; h++)
-#pragma unroll
-      for (int e = 0; e < EPL; e++) o_s[(warp * R + h) * D + lane * EPL + e] = acc[h][e];
-    __syncthreads();
-    if (tid < R) {
-      float M = -1e9f, Lsum = 0.f;
-      for (int w = 0; w < kAttnWarps; w++) M = fmaxf(M, wm[w * R + tid]);
-      for (int w = 0; w < kAttnWarps; w++) {
-        const float f = expf(__fsub_rn(wm[w * R + tid], M));
-        Lsum = __fmaf_rn(wl[w * R + tid], f, Lsum);
-        wm[w * R + tid] = f;
-      }
-      stat[2 * tid] = M;
-      stat[2 * tid + 1] = Lsum;
-    }
-    __syncthreads();
-    for (int idx = tid; idx < R * D; idx += kAttnThreads) {
-      const int h = idx / D, d = idx % D;
-      float O = 0.f;
-#pragma unroll
-      for (int w = 0; w < kAttnWarps; w++) O = __fmaf_rn(o_s[(w * R + h) * D + d], wm[w * R + h], O);
-      o_s[h * D + d] = O;  // warp 0's slot: read back below as the CTA's partial
-    }
-    __syncthreads();
-  } else {
   // rows of this chunk, kU slots per warp iteration with every load issued before any is
   // used (one slot per iteration left each warp waiting a full memory round trip per
   // slot); the per-slot arithmetic and the per-warp slot order are unchanged.
@@ -351,18 +241,13 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attn_kernel(const AttnArg
     for (int e = 0; e < EPL; e++) o_s[(warp * R + h) * D + lane * EPL + e] = acc[h][e];
   __syncthreads();
 
-  }
   // ---- partial out: [kvh][split][h] = {o[D], m, l} ----
   float *part = partial + ((size_t)(kvh * max_splits + split) * R) * (D + 2);
   for (int idx = tid; idx < R * D; idx += kAttnThreads) {
     const int h = idx / D, d = idx % D;
     float s = 0.f;
-    if constexpr (ONEPASS) {
-      s = o_s[h * D + d];
-    } else {
 #pragma unroll
-      for (int w = 0; w < kAttnWarps; w++) s = __fadd_rn(s, o_s[(w * R + h) * D + d]);
-    }
+    for (int w = 0; w < kAttnWarps; w++) s = __fadd_rn(s, o_s[(w * R + h) * D + d]);
     part[h * (D + 2) + d] = s;
   }
   if (tid < R) {
@@ -417,14 +302,14 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attn_kernel(const AttnArg
   if (tid == 0) counters[kvh] = 0u;
 }
 
-template <int R, bool ONEPASS>
+template <int R>
 static cudaError_t launch_attn_t(const AttnArgs &a, int splits, cudaStream_t s, bool pdl) {
   const int chunk_cap = (int)std::max<uint32_t>(kMinChunk, (a.cache_slots + splits - 1) / splits);
   const size_t smem = sizeof(float) * ((size_t)(R + 2) * 256 + (size_t)kAttnWarps * R * 256 + (size_t)R * chunk_cap +
                                        (size_t)R * splits) +
                       sizeof(uint32_t) * (size_t)chunk_cap;
   {
-    const cudaError_t e = ensure_smem_attr((const void *)decode_attn_kernel<R, ONEPASS>, smem);
+    const cudaError_t e = ensure_smem_attr((const void *)decode_attn_kernel<R>, smem);
     if (e != cudaSuccess) return e;
   }
   cudaLaunchConfig_t cfg = {};
@@ -437,18 +322,17 @@ static cudaError_t launch_attn_t(const AttnArgs &a, int splits, cudaStream_t s, 
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, decode_attn_kernel<R, ONEPASS>, a, splits, chunk_cap);
+  return cudaLaunchKernelEx(&cfg, decode_attn_kernel<R>, a, splits, chunk_cap);
 }
 
 cudaError_t launch_decode_attn(const AttnArgs &a, int splits, cudaStream_t s, bool pdl) {
   if (a.D != 256 || a.nkv == 0 || a.nq % a.nkv != 0) return cudaErrorInvalidValue;
   const uint32_t R = a.nq / a.nkv;
-  const bool one = a.n_tok > 1;  // batches: one pass with an online softmax
   switch (R) {
-    case 1: return one ? launch_attn_t<1, true>(a, splits, s, pdl) : launch_attn_t<1, false>(a, splits, s, pdl);
-    case 2: return one ? launch_attn_t<2, true>(a, splits, s, pdl) : launch_attn_t<2, false>(a, splits, s, pdl);
-    case 4: return one ? launch_attn_t<4, true>(a, splits, s, pdl) : launch_attn_t<4, false>(a, splits, s, pdl);
-    case 8: return one ? launch_attn_t<8, true>(a, splits, s, pdl) : launch_attn_t<8, false>(a, splits, s, pdl);
+    case 1: return launch_attn_t<1>(a, splits, s, pdl);
+    case 2: return launch_attn_t<2>(a, splits, s, pdl);
+    case 4: return launch_attn_t<4>(a, splits, s, pdl);
+    case 8: return launch_attn_t<8>(a, splits, s, pdl);
     default: return cudaErrorInvalidValue;
   }
 }
