@@ -390,6 +390,53 @@ def prefill_roofline(ctx, gm, cfg, stream, n_tok, layers=8, reps=2):
             "peak_kind": kind + " bf16_tflops (cuBLAS burst); achieved = algorithmic 2*tokens*weights FLOPs"}
 
 
+def nccl_exchange_floor(cfg, world, iters=20):
+    """The collectives a tensor-parallel step would need if its two per-layer exchanges
+    (the o and down partial sums) and the top-64 merge went through NCCL between kernel
+    launches instead of the decode kernel's own NVLink peer stores: 2 x layers all-reduces
+    of H floats and one all-gather of 64 candidates per token, captured in a CUDA graph
+    and timed with events (the max over ranks).  A floor for that design: its kernels
+    would also have to stop and restart around each collective."""
+    import torch
+    import torch.distributed as dist
+    H = cfg.hidden_size
+    bufs = [torch.zeros(H, device="cuda", dtype=torch.float32) for _ in range(2)]
+    cand = torch.zeros(64, device="cuda", dtype=torch.int64)
+    gath = torch.zeros(64 * world, device="cuda", dtype=torch.int64)
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):  # warm NCCL up outside the capture
+        for _ in range(3):
+            dist.all_reduce(bufs[0])
+            dist.all_gather_into_tensor(gath, cand)
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for l in range(cfg.num_hidden_layers):
+            dist.all_reduce(bufs[0])
+            dist.all_reduce(bufs[1])
+        dist.all_gather_into_tensor(gath, cand)
+    g.replay()
+    torch.cuda.synchronize()
+    dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(iters):
+        g.replay()
+    e1.record()
+    e1.synchronize()
+    t = torch.tensor([e0.elapsed_time(e1) / iters], device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    del g  # the graph holds NCCL work: release it before the process group goes away
+    torch.cuda.synchronize()
+    return {"ms_per_token": ms, "collectives_per_token": 2 * cfg.num_hidden_layers + 1,
+            "us_per_collective": ms * 1000 / (2 * cfg.num_hidden_layers + 1),
+            "what": "2 x layers all-reduce of H f32 + 1 all-gather of 64 u64 per token, NCCL in a CUDA graph, "
+                    "no compute: a floor for exchanging between kernel launches"}
+
+
 def ours(args):
     import torch
 
@@ -519,6 +566,8 @@ def ours(args):
         prefill_rl["prompt_s"] = min(prefill_times)
         prefill_rl["prompt_tok_s"] = PROMPT / min(prefill_times)
 
+    nccl_floor = nccl_exchange_floor(cfg, world) if dist else None
+
     # ---- e2e: reference-facing call with host buffers ---------------------------------
     e2e = None
     if not args.no_e2e:
@@ -594,6 +643,7 @@ def ours(args):
             "clocks": clk.summary(),
             "setup_s": {"model_build": build_s, "prefill_512": prefill_s},
             "tokens_head": [int(t) for t in tokens[:8]],
+            "tp_nccl_exchange_floor": nccl_floor,
         }
         print(json.dumps(line), flush=True)
     if dist:

@@ -63,6 +63,7 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <cstdlib>
 
 #include "common.cuh"
 #include "kernels.cuh"
@@ -432,16 +433,27 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
       epi_sync();
       if (ok && *is_last) {
         __threadfence();
+        // the splits' partials of 32 tokens at a time: every load of a split is in flight
+        // before any is added (one dependent L2 round trip per load cost tens of us);
+        // the additions keep the split order
 #pragma unroll 1
         for (int ch = 0; ch < 2; ch++) {
           float y[32];
 #pragma unroll
-          for (int i = 0; i < 32; i++) {
-            const size_t o = (size_t)(tok0 + ch * 32 + i) * Mr + row;
-            float acc = row_ok ? L.ws[o] : 0.f;
-            for (uint32_t s2 = 1; s2 < L.sk; s2++)
-              if (row_ok) acc = __fadd_rn(acc, L.ws[(size_t)s2 * ntok * Mr + o]);
-            y[i] = acc;
+          for (int i = 0; i < 32; i++) y[i] = 0.f;
+          if (row_ok) {
+            const float *w0 = L.ws + (size_t)(tok0 + ch * 32) * Mr + row;
+#pragma unroll
+            for (int i = 0; i < 32; i++) y[i] = __ldcg(w0 + (size_t)i * Mr);
+#pragma unroll 1
+            for (uint32_t s2 = 1; s2 < L.sk; s2++) {
+              const float *wsp = w0 + (size_t)s2 * ntok * Mr;
+              float t[32];
+#pragma unroll
+              for (int i = 0; i < 32; i++) t[i] = __ldcg(wsp + (size_t)i * Mr);
+#pragma unroll
+              for (int i = 0; i < 32; i++) y[i] = __fadd_rn(y[i], t[i]);
+            }
           }
           store_out(y, tok0 + ch * 32);
         }
@@ -496,7 +508,11 @@ static uint32_t choose_split(uint32_t pairs, uint32_t KT) {
 }
 static uint32_t gemm_split(uint32_t N, uint32_t M, uint32_t K) {
   const uint32_t nt = (N + kTcBN - 1) / kTcBN, mp = (M / 16 + 15) / 16;
-  const uint32_t sk = choose_split(nt * mp, K / kTcBK);
+  uint32_t sk = choose_split(nt * mp, K / kTcBK);
+  if (const char *env = getenv("CH_TC_SPLIT")) {  // measurement override of the split factor
+    const uint32_t f = (uint32_t)atoi(env), KT = K / kTcBK;
+    if (f >= 1 && f <= 16 && KT % f == 0 && KT / f >= 8) sk = f;
+  }
   return (sk > 1 && mp * 2 * nt > kMaxCounters) ? 1 : sk;
 }
 static size_t xs_region(uint32_t N, uint32_t K) { return (tc_split_x_bytes(N, K) + 255) & ~(size_t)255; }
