@@ -299,8 +299,10 @@ struct TcGemmArgs {
 size_t tc_split_x_bytes(uint32_t N, uint32_t K);
 size_t tc_gemm_scratch_bytes(uint32_t N, uint32_t M, uint32_t K);
 cudaError_t launch_tc_split_x(const float *X, uint32_t N, uint32_t K, uint8_t *xs, cudaStream_t s);
-cudaError_t launch_batch_gemm_tc(const TcGemmArgs &a, uint8_t *scratch, cudaStream_t s);
+// scratch_bytes: the buffer's size; a null or short buffer is refused
+cudaError_t launch_batch_gemm_tc(const TcGemmArgs &a, uint8_t *scratch, size_t scratch_bytes, cudaStream_t s);
 // split + GEMM: the prefill's Q4 GEMM
-cudaError_t launch_batch_gemm_q4_tc(const BatchGemmArgs &g, uint8_t *scratch, uint32_t *err, cudaStream_t s);
+cudaError_t launch_batch_gemm_q4_tc(const BatchGemmArgs &g, uint8_t *scratch, size_t scratch_bytes, uint32_t *err,
+                                    cudaStream_t s);
 
 }  // namespace ch

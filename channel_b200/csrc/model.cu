@@ -235,6 +235,7 @@ struct ch_model {
   float *pX = nullptr, *pNX = nullptr, *pQKV = nullptr, *pQO = nullptr, *pA = nullptr, *pMO = nullptr, *pACT = nullptr;
   uint32_t *pSlots = nullptr, *pTok = nullptr;
   uint8_t *pXS = nullptr;  // scratch of the tcgen05 GEMM (counters | split activation | partials)
+  size_t pXS_n = 0;
   // multi-stream decode: per-stream KV caches and the buffers of one batched step
   uint32_t ms_n = 0, ms_cap = 0;   // decode streams and the largest step
   std::vector<__half *> skc, svc;  // per layer: [ms_n][4096][kv_dim]
@@ -1786,6 +1787,7 @@ static int ensure_prefill(ch_model *m) {
     need = std::max(need, tc_gemm_scratch_bytes(N, 2 * m->I, m->H));
     need = std::max(need, tc_gemm_scratch_bytes(N, m->H, m->I));
     CH_TRY(dmalloc(&m->pXS, need));
+    m->pXS_n = need;
     CH_CUDA(cudaMemset(m->pXS, 0, 16384));  // split-K tile counters start at zero
   }
   m->pf_cap = N;
@@ -1889,7 +1891,7 @@ static int prefill_impl(ch_model *m, const uint32_t *tokens, uint32_t n, const u
   for (uint32_t l = 0; l < m->L; l++) {
     DevLayer &dl = m->layers[l];
     if (l == 0) CH_CUDA(launch_rmsnorm_rows(m->pX, dl.input_norm, m->pNX, n, m->H, eps, s));
-    CH_CUDA(launch_batch_gemm_q4_tc(BatchGemmArgs{dl.qkv, qkvd, m->H, n, m->pNX, m->pQKV, EPI_STORE}, m->pXS, err, s));
+    CH_CUDA(launch_batch_gemm_q4_tc(BatchGemmArgs{dl.qkv, qkvd, m->H, n, m->pNX, m->pQKV, EPI_STORE}, m->pXS, m->pXS_n, err, s));
     BatchQkvRopeArgs r{};
     r.q = m->pQKV;
     r.k = m->pQKV + m->qd;
@@ -1915,12 +1917,12 @@ static int prefill_impl(ch_model *m, const uint32_t *tokens, uint32_t n, const u
     CH_CUDA(launch_batch_qkv_rope(r, s));
     BatchAttnArgs at{m->pQO, kc_of(l), vc_of(l), m->pSlots, n, num_prev, m->nq, m->nkv, m->D, 1.0f, dl.full ? 0 : 1, m->pA};
     CH_CUDA(launch_batch_causal_attn(at, s));
-    CH_CUDA(launch_batch_gemm_q4_tc(BatchGemmArgs{dl.o, m->H, m->qd, n, m->pA, m->pMO, EPI_STORE}, m->pXS, err, s));
+    CH_CUDA(launch_batch_gemm_q4_tc(BatchGemmArgs{dl.o, m->H, m->qd, n, m->pA, m->pMO, EPI_STORE}, m->pXS, m->pXS_n, err, s));
     if (dl.post_attn) CH_CUDA(launch_rmsnorm_rows(m->pMO, dl.post_attn, m->pMO, n, m->H, eps, s));
     CH_CUDA(launch_add_rmsnorm_rows(m->pX, m->pMO, dl.pre_ffn, m->pNX, n, m->H, eps, 1.0f, s));
     CH_CUDA(launch_batch_gemm_q4_tc(BatchGemmArgs{dl.gateup, 2 * m->I, m->H, n, m->pNX, m->pACT, EPI_GELU_MUL}, m->pXS,
-                                    err, s));
-    CH_CUDA(launch_batch_gemm_q4_tc(BatchGemmArgs{dl.down, m->H, m->I, n, m->pACT, m->pMO, EPI_STORE}, m->pXS, err, s));
+                                    m->pXS_n, err, s));
+    CH_CUDA(launch_batch_gemm_q4_tc(BatchGemmArgs{dl.down, m->H, m->I, n, m->pACT, m->pMO, EPI_STORE}, m->pXS, m->pXS_n, err, s));
     if (dl.post_ffn) CH_CUDA(launch_rmsnorm_rows(m->pMO, dl.post_ffn, m->pMO, n, m->H, eps, s));
     const float *next = (l + 1 < m->L) ? m->layers[l + 1].input_norm : m->final_norm;
     CH_CUDA(launch_add_rmsnorm_rows(m->pX, m->pMO, next, m->pNX, n, m->H, eps, dl.scalar, s));
@@ -2429,7 +2431,7 @@ extern "C" int ch_batch_gemm_q4(ch_ctx *c, const void *tiles, uint32_t rows, uin
   if (n == 0) return CH_OK;
   if (n >= kSkinnyTcMinTokens && n <= 64) return batch_gemm_skinny(c, tiles, rows, cols, x, n, EPI_STORE, y, rows);
   CH_TRY(ctx_ensure_xs(c, tc_gemm_scratch_bytes(n, rows, cols)));
-  CH_CUDA(launch_batch_gemm_q4_tc(BatchGemmArgs{(const uint8_t *)tiles, rows, cols, n, x, y, EPI_STORE}, c->xs, c->err,
+  CH_CUDA(launch_batch_gemm_q4_tc(BatchGemmArgs{(const uint8_t *)tiles, rows, cols, n, x, y, EPI_STORE}, c->xs, c->xs_n, c->err,
                                   c->stream));
   return CH_OK;
 }
@@ -2439,8 +2441,9 @@ extern "C" int ch_batch_fused_mlp_q4(ch_ctx *c, const void *tiles, uint32_t rows
   if (n == 0) return CH_OK;
   if (n >= kSkinnyTcMinTokens && n <= 64)
     return batch_gemm_skinny(c, tiles, 2 * rows, cols, x, n, EPI_GELU_MUL, act, rows);
+  CH_TRY(ctx_ensure_xs(c, tc_gemm_scratch_bytes(n, 2 * rows, cols)));
   CH_CUDA(launch_batch_gemm_q4_tc(BatchGemmArgs{(const uint8_t *)tiles, 2 * rows, cols, n, x, act, EPI_GELU_MUL}, c->xs,
-                                  c->err, c->stream));
+                                  c->xs_n, c->err, c->stream));
   return CH_OK;
 }
 // the same two GEMMs on the legacy mma.sync tensor path, kept as the measured baseline

@@ -63,7 +63,6 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
-#include <cstdlib>
 
 #include "common.cuh"
 #include "kernels.cuh"
@@ -508,11 +507,7 @@ static uint32_t choose_split(uint32_t pairs, uint32_t KT) {
 }
 static uint32_t gemm_split(uint32_t N, uint32_t M, uint32_t K) {
   const uint32_t nt = (N + kTcBN - 1) / kTcBN, mp = (M / 16 + 15) / 16;
-  uint32_t sk = choose_split(nt * mp, K / kTcBK);
-  if (const char *env = getenv("CH_TC_SPLIT")) {  // measurement override of the split factor
-    const uint32_t f = (uint32_t)atoi(env), KT = K / kTcBK;
-    if (f >= 1 && f <= 16 && KT % f == 0 && KT / f >= 8) sk = f;
-  }
+  const uint32_t sk = choose_split(nt * mp, K / kTcBK);
   return (sk > 1 && mp * 2 * nt > kMaxCounters) ? 1 : sk;
 }
 static size_t xs_region(uint32_t N, uint32_t K) { return (tc_split_x_bytes(N, K) + 255) & ~(size_t)255; }
@@ -540,10 +535,19 @@ cudaError_t launch_tc_split_x(const float *X, uint32_t N, uint32_t K, uint8_t *x
   return cudaGetLastError();
 }
 
-cudaError_t launch_batch_gemm_tc(const TcGemmArgs &a, uint8_t *scratch, cudaStream_t s) {
+// bytes of scratch one launch of this shape uses (tc_gemm_scratch_bytes covers every
+// token count up to N)
+static size_t tc_launch_scratch_bytes(uint32_t N, uint32_t M, uint32_t K) {
+  const uint32_t sk = gemm_split(N, M, K);
+  const size_t nt = (N + kTcBN - 1) / kTcBN;
+  return kCounterBytes + xs_region(N, K) + (sk > 1 ? (size_t)sk * nt * kTcBN * M * sizeof(float) : 0);
+}
+
+cudaError_t launch_batch_gemm_tc(const TcGemmArgs &a, uint8_t *scratch, size_t scratch_bytes, cudaStream_t s) {
   if (a.M % 16 || a.K % kTcBK || a.N == 0) return a.N == 0 ? cudaSuccess : cudaErrorInvalidValue;
   if (((uintptr_t)a.xs & 15) || ((uintptr_t)a.tiles & 15) || ((uintptr_t)scratch & 255))
     return cudaErrorInvalidValue;  // copy alignment
+  if (!scratch || scratch_bytes < tc_launch_scratch_bytes(a.N, a.M, a.K)) return cudaErrorInvalidValue;
   alignas(64) CUtensorMap wmap;
   cudaError_t me = encode_tile_map(&wmap, a.tiles, a.M, a.K, 8);
   if (me != cudaSuccess) return me;
@@ -555,24 +559,26 @@ cudaError_t launch_batch_gemm_tc(const TcGemmArgs &a, uint8_t *scratch, cudaStre
   L.ws = reinterpret_cast<float *>(scratch + kCounterBytes + xs_region(a.N, a.K));
   const dim3 grid(2, nt, mp * L.sk);  // clusters of 2: 256 rows x 256 tokens, per split
   if (a.epi == EPI_STORE) {
-    cudaError_t e = cudaFuncSetAttribute(batch_gemm_tc_kernel<EPI_STORE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)kTcSmemBytes);
+    cudaError_t e = ensure_smem_attr((const void *)batch_gemm_tc_kernel<EPI_STORE>, kTcSmemBytes);
     if (e != cudaSuccess) return e;
     batch_gemm_tc_kernel<EPI_STORE><<<grid, kTcThreads, kTcSmemBytes, s>>>(a, L, wmap);
   } else {
-    cudaError_t e = cudaFuncSetAttribute(batch_gemm_tc_kernel<EPI_GELU_MUL>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kTcSmemBytes);
+    cudaError_t e = ensure_smem_attr((const void *)batch_gemm_tc_kernel<EPI_GELU_MUL>, kTcSmemBytes);
     if (e != cudaSuccess) return e;
     batch_gemm_tc_kernel<EPI_GELU_MUL><<<grid, kTcThreads, kTcSmemBytes, s>>>(a, L, wmap);
   }
   return cudaGetLastError();
 }
 
-cudaError_t launch_batch_gemm_q4_tc(const BatchGemmArgs &g, uint8_t *scratch, uint32_t *err, cudaStream_t s) {
+cudaError_t launch_batch_gemm_q4_tc(const BatchGemmArgs &g, uint8_t *scratch, size_t scratch_bytes, uint32_t *err,
+                                    cudaStream_t s) {
+  if (g.N == 0) return cudaSuccess;
+  if (g.M % 16 || g.K % kTcBK) return cudaErrorInvalidValue;
+  if (!scratch || scratch_bytes < tc_launch_scratch_bytes(g.N, g.M, g.K)) return cudaErrorInvalidValue;
   uint8_t *xs = scratch + kCounterBytes;
   cudaError_t e = launch_tc_split_x(g.X, g.N, g.K, xs, s);
   if (e != cudaSuccess) return e;
-  return launch_batch_gemm_tc(TcGemmArgs{g.tiles, xs, g.Y, g.M, g.K, g.N, g.epi, err}, scratch, s);
+  return launch_batch_gemm_tc(TcGemmArgs{g.tiles, xs, g.Y, g.M, g.K, g.N, g.epi, err}, scratch, scratch_bytes, s);
 }
 
 }  // namespace ch

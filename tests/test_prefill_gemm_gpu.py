@@ -77,6 +77,33 @@ def test_batch_fused_mlp_q4_parity(ctx, oracle, N, M, K):
     assert ctx.device_status() == 0
 
 
+def test_batch_fused_mlp_q4_fresh_context(oracle):
+    """The fused gate|up GEMM as the first call on a new context: the entry point
+    sizes the context's scratch itself (the other tests share one context whose
+    scratch earlier GEMMs already grew)."""
+    from channel_b200 import GpuContext
+    lib = L.load()
+    N, M, K = 300, 520, 512
+    Wg = oracle.gen_q4(M, K, oracle.tensor_seed(2, 1, 4))
+    Wu = oracle.gen_q4(M, K, oracle.tensor_seed(2, 1, 5))
+    X = oracle.gen_f32(N * K, 12).reshape(N, K)
+    ref = oracle.batch_fused_mlp_q4(Wg, Wu, X, N, M, K)
+    c = GpuContext.init(0)
+    try:
+        tiles = _pack_gateup(lib, c, Wg, Wu, M, K)
+        xd, yd = dev(X), empty(N * M)
+        yd.fill_(float("nan"))
+        torch.cuda.synchronize()
+        call(lib.ch_batch_fused_mlp_q4, c.handle, tiles.data_ptr(), M, K, xd.data_ptr(), N, yd.data_ptr())
+        c.synchronize()
+        e = assert_close(host(yd).reshape(N, M), ref, what=f"batch_fused_mlp_q4 fresh {N}x{M}x{K}")
+        assert e < FP32_FAITHFUL
+        assert c.device_status() == 0
+    finally:
+        c.synchronize()
+        c.deinit()
+
+
 @pytest.mark.parametrize("N", [512, 64, 17])
 @pytest.mark.parametrize("kind,M,K", [("gemm", 8192, 3840), ("gemm", 3840, 4096), ("gemm", 3840, 15360),
                                       ("mlp", 15360, 3840)])
