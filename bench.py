@@ -271,7 +271,7 @@ def gemv_config1(ctx, stream, reps=8, copies=24):
             "launches_timed": n, "peak_kind": peak_kind + " hbm_gbs (burst)"}
 
 
-def config5(ctx, gm, cfg, stream, n_streams=64, n_tokens=128, lo=16, hi=2048, seed=4):
+def config5(ctx, gm, cfg, stream, n_streams=64, n_tokens=128, lo=16, hi=2048, seed=4, rank=0, world=1):
     """BASELINE config 5 on the config-4 model: n_streams greedy streams, prompt lengths
     uniform in [lo, hi] and uniform token ids (seeded), n_tokens tokens each (the
     prefill's greedy token is the first), every stream with its own 4,096-slot ring KV.
@@ -279,13 +279,21 @@ def config5(ctx, gm, cfg, stream, n_streams=64, n_tokens=128, lo=16, hi=2048, se
     (up to 64) into one ch_streams_decode call.  decode_tok_s = generated decode tokens
     / decode time (CUDA events on the library stream around all steps, the host ring
     bookkeeping between steps included); bytes_per_step = Q4 + Q8 weights once + every
-    stream's K/V rows read."""
+    stream's K/V rows read.
+
+    world > 1: stream-parallel replicas -- rank r holds a full copy of the weights and
+    decodes streams [n r / world, n (r+1) / world) of the same seeded set, with no
+    exchange between ranks; times are the max over ranks, tokens and bytes the sums."""
     import torch
     from channel_b200.streams import MultiStreamDecoder
     rng = np.random.default_rng(seed)
-    lens = rng.integers(lo, hi + 1, n_streams)
-    prompts = [rng.integers(0, cfg.vocab_size, int(n)).astype(np.uint32) for n in lens]
-    dec = MultiStreamDecoder(gm, cfg, n_streams, min(n_streams, 64))
+    all_lens = rng.integers(lo, hi + 1, n_streams)
+    all_prompts = [rng.integers(0, cfg.vocab_size, int(n)).astype(np.uint32) for n in all_lens]
+    mine = range(n_streams * rank // world, n_streams * (rank + 1) // world)
+    lens = all_lens[mine.start:mine.stop]
+    prompts = all_prompts[mine.start:mine.stop]
+    n_mine = len(prompts)
+    dec = MultiStreamDecoder(gm, cfg, n_mine, min(n_mine, 64))
     ctx.synchronize()
     t0 = time.time()
     longest = int(np.argmax(lens))
@@ -300,9 +308,12 @@ def config5(ctx, gm, cfg, stream, n_streams=64, n_tokens=128, lo=16, hi=2048, se
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     kv_rows = 0  # K/V rows (all kv heads of one slot, per layer) the decode steps read
     n_full = sum(1 for full in cfg.layer_types[:cfg.num_hidden_layers] if full)
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
     e0.record(stream)
     while True:
-        live = [s for s in range(n_streams) if len(dec.tokens[s]) < n_tokens]
+        live = [s for s in range(n_mine) if len(dec.tokens[s]) < n_tokens]
         if not live:
             break
         for i in range(0, len(live), dec.max_batch):
@@ -321,20 +332,30 @@ def config5(ctx, gm, cfg, stream, n_streams=64, n_tokens=128, lo=16, hi=2048, se
     decode_s = e0.elapsed_time(e1) / 1000.0
     steps = dec.steps
     tokens = n_streams * (n_tokens - 1)
+    if world > 1:  # the slowest rank's times; every rank's K/V rows
+        t = torch.tensor([decode_s, prefill_s, float(steps)], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        kv = torch.tensor([float(kv_rows)], device="cuda", dtype=torch.float64)
+        dist.all_reduce(kv, op=dist.ReduceOp.SUM)
+        decode_s, prefill_s, steps, kv_rows = float(t[0]), float(t[1]), int(t[2]), int(kv[0])
     weight_bytes = (cfg.num_hidden_layers * (cfg.hidden_size * (cfg.q_dim + 2 * cfg.kv_dim) + cfg.q_dim * cfg.hidden_size
                                              + 3 * cfg.hidden_size * cfg.intermediate_size) * 18 // 32
                     + cfg.vocab_size * cfg.hidden_size * 36 // 32)
     kv_bytes = kv_rows * 2 * cfg.kv_dim * 2
-    step_bytes = weight_bytes + kv_bytes / steps
+    step_bytes = world * weight_bytes + kv_bytes / steps  # every replica streams its weights
     peak, peak_kind = peaks()
     gbs = step_bytes / (decode_s / steps) / 1e9
+    par = "single" if world == 1 else f"replicas{world} ({n_streams // world} streams per GPU, weights replicated, no exchange)"
     return {"workload": f"config5: {n_streams} streams, prompts U[{lo},{hi}] (seed {seed}), {n_tokens} greedy tokens each, "
                         "own 4096-slot ring KV per stream, one batched step for all streams",
-            "prompt_tokens": int(lens.sum()), "prefill_s": prefill_s, "prefill_tok_s": float(lens.sum()) / prefill_s,
+            "parallelism": par,
+            "prompt_tokens": int(all_lens.sum()), "prefill_s": prefill_s,
+            "prefill_tok_s": float(all_lens.sum()) / prefill_s,
             "decode_steps": steps, "decode_s": decode_s, "decode_tok_s": tokens / decode_s,
             "ms_per_step": decode_s / steps * 1000, "bytes_per_step": step_bytes,
-            "achieved_gbs": gbs, "peak_gbs": peak, "frac": gbs / peak, "peak_kind": peak_kind + " hbm_gbs",
-            "tokens_head": [dec.tokens[s][:4] for s in range(2)]}
+            "achieved_gbs": gbs, "peak_gbs": world * peak, "frac": gbs / (world * peak),
+            "peak_kind": peak_kind + " hbm_gbs" + (f" x {world} GPUs" if world > 1 else ""),
+            "tokens_head": [dec.tokens[s][:4] for s in range(min(2, n_mine))]}
 
 
 def prefill_roofline(ctx, gm, cfg, stream, n_tok, layers=8, reps=2):
@@ -558,6 +579,13 @@ def ours(args):
     c5 = None
     if world == 1 and not args.no_config5 and cfg.num_hidden_layers == 48:
         c5 = config5(ctx, gm, cfg, stream, n_streams=args.config5_streams)
+    elif world > 1 and not args.no_config5 and cfg.num_hidden_layers == 48:
+        # stream-parallel replicas: a full copy of the weights on every rank beside its
+        # tensor-parallel shard (which stays alive: its arena is mapped by the peers)
+        gm5 = GpuModelContext.synthetic(ctx, cfg, SEED)
+        c5 = config5(ctx, gm5, cfg, stream, n_streams=args.config5_streams, rank=rank, world=world)
+        ctx.synchronize()
+        gm5.deinit()
     # the batched prefill (one GPU): whole 512-token prompt, and its tensor-core GEMMs alone
     prefill_rl = None
     if world == 1:

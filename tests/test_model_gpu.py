@@ -154,6 +154,13 @@ def test_device_loop_matches_host_loop(small, oracle):
     gm.decode_run(first, steps)
     dev_tokens = gm.decode_tokens(steps)
     assert list(dev_tokens) == host_tokens
+    # and directly against the oracle's greedy stream over the same lists
+    om = oracle.Model(cfg, w)
+    tok, ref_tokens = first, []
+    for clock, slot, act, sli in plan:
+        tok, _, _ = om.forward_token(oracle.embed(w.embed, [tok], cfg.hidden_size)[0], clock, slot, act, sli)
+        ref_tokens.append(tok)
+    assert list(dev_tokens) == ref_tokens
 
 
 def test_config3_prefill_layer(ctx, oracle):
