@@ -56,6 +56,7 @@ constexpr uint32_t kWinSlots = 64;  // attention slots per work item staged in s
 constexpr uint32_t kNoStraddle = 0xFFFFFFFFu;
 constexpr int kHeadDim = 256;
 constexpr uint32_t kMaxGrid = 255;  // straddle-list entries hold CTA ids in 8 bits
+constexpr uint32_t kMaxComb = 24;   // combine items of one CTA and GEMV kind (at most 17 can occur)
 }  // namespace
 
 int mk_warps() { return MK_NW; }
@@ -124,22 +125,22 @@ CH_DEV T *on_rank(const MegaArgs &a, T *local, uint32_t r) {
 // when c1 == c (the common case), else kNoStraddle (the general sum walks the
 // CTAs).  slist[k] = kNoStraddle for boundaries between row tiles.  One thread
 // per entry.
-CH_DEV void build_slist(const GemvOut &o, uint32_t *slist, uint32_t *soff) {
-  const uint32_t G = gridDim.x, KT = o.pt.KT;
-  for (uint32_t c = 1 + threadIdx.x; c < G; c += blockDim.x) {
-    const uint32_t B = cta_begin(o, c);  // first tile of CTA c
-    const uint32_t rt = B / KT;
-    uint32_t e = kNoStraddle, off = kNoStraddle;
-    const uint32_t b0 = cta_begin(o, c - 1);
-    if (B != rt * KT && b0 <= rt * KT) {
-      const uint32_t t_hi = rt * KT + KT - 1;
-      if (c + 1 >= G || cta_begin(o, c + 1) > t_hi)  // exactly CTAs c-1 and c
-        off = ((c - 1) * 2 + (b0 < rt * KT ? 1u : 0u)) * 16 | ((c * 2) * 16) << 16;
-      e = rt;
-    }
-    slist[c - 1] = e;
-    soff[c - 1] = off;
+// Entry c-1 (c = 1 .. grid-1) of the list of partition pt; computed once per launch
+// for every GEMV kind (straddle_lists), since it depends on the partition alone.
+CH_DEV void slist_entry(const Partition &pt, uint32_t c, uint32_t *slist, uint32_t *soff) {
+  const uint32_t G = gridDim.x, KT = pt.KT;
+  const uint32_t B = cta_begin(pt, c);  // first tile of CTA c
+  const uint32_t rt = B / KT;
+  uint32_t e = kNoStraddle, off = kNoStraddle;
+  const uint32_t b0 = cta_begin(pt, c - 1);
+  if (B != rt * KT && b0 <= rt * KT) {
+    const uint32_t t_hi = rt * KT + KT - 1;
+    if (c + 1 >= G || cta_begin(pt, c + 1) > t_hi)  // exactly CTAs c-1 and c
+      off = ((c - 1) * 2 + (b0 < rt * KT ? 1u : 0u)) * 16 | ((c * 2) * 16) << 16;
+    e = rt;
   }
+  slist[c - 1] = e;
+  soff[c - 1] = off;
 }
 // value of row `row` (0..15) of the straddling row tile of entry k from the staged
 // CTA partials P[grid][2][16]: the CTAs' sums in CTA order
@@ -415,6 +416,24 @@ CH_DEV void copy_phase(const Phase *src, Phase *dst) {
                reinterpret_cast<const uint8_t *>(src) + threadIdx.x * 16);
 }
 
+// The row tiles of CTA c that a GEMV of partition pt leaves to the CTA combine (cut
+// between warps of the CTA, or straddling a CTA boundary), one item each:
+// {rt, w0 | w1 << 4 | inside << 8 | CTA slot << 9 | warp slot bits of w0..w1 << 16}.
+// Depends on the partition alone, so it is computed once per launch (comb_items).
+CH_DEV bool comb_item(const Partition &pt, uint32_t c, uint32_t rt, uint2 &item) {
+  const uint32_t KT = pt.KT, cb = cta_begin(pt, c), ce = cta_begin(pt, c + 1);
+  const uint32_t t_lo = rt * KT, t_hi = t_lo + KT - 1;
+  const uint32_t a_lo = max(t_lo, cb), a_hi = min(t_hi, ce - 1);
+  const uint32_t w0 = warp_of(pt, c, a_lo), w1 = warp_of(pt, c, a_hi);
+  const bool inside = cb <= t_lo && t_hi < ce;
+  if (w0 == w1 && inside) return false;  // one warp covered the whole row tile: stored by its flush
+  uint32_t slots = 0;
+  for (uint32_t w = w0; w <= w1; w++)
+    if (warp_begin(pt, c, w) < t_lo) slots |= 1u << w;
+  item = make_uint2(rt, w0 | w1 << 4 | (inside ? 1u : 0u) << 8 | (cb < t_lo ? 1u : 0u) << 9 | slots << 16);
+  return true;
+}
+
 // ---------------------------------------------------------------------------
 struct SmemLayout {
   uint8_t *stages;
@@ -422,11 +441,45 @@ struct SmemLayout {
   uint64_t *vbar;   // staged activations: two arrivals per phase (before and after the grid barrier)
   uint4 *xzero;     // a zero B fragment (f16 tiles: the lanes without an x column)
   float *wpart;     // [warps][2][16] partial segments of the current GEMV phase
-  uint32_t *slist;  // [kMaxGrid] straddle list of the current phase's input
-  uint32_t *soff;   // [kMaxGrid] its partial-slot offsets
+  uint32_t *sl;     // [kKinds][2][g4] straddle lists (entries, partial-slot offsets) of every GEMV kind
+  uint32_t g4;      // entries per list: the grid rounded up to a multiple of 4
+  uint2 *comb;      // [kKinds][kMaxComb] this CTA's combine items of every GEMV kind
+  uint32_t *ncomb;  // [kKinds] their counts
   uint32_t *wphys;  // [2][kWinSlots] attention window slot ids (full, sliding lists)
   uint8_t *u;       // union region (GEMV staging / attention / top-k)
 };
+// straddle list (and its partial-slot offsets) of the outputs of GEMV kind `kind`
+CH_DEV const uint32_t *sl_list(const SmemLayout &L, uint32_t kind) { return L.sl + kind * 2 * L.g4; }
+CH_DEV const uint32_t *sl_off(const SmemLayout &L, uint32_t kind) { return L.sl + kind * 2 * L.g4 + L.g4; }
+// Once per launch, before the first phase: every kind's straddle list (one thread per
+// entry) and this CTA's combine items (one thread per row tile of its range).
+CH_DEV void launch_tables(const MegaArgs &a, const SmemLayout &L) {
+  const uint32_t G = gridDim.x, c = blockIdx.x;
+  if (threadIdx.x < kKinds) L.ncomb[threadIdx.x] = 0u;
+  for (uint32_t e = threadIdx.x; e < kKinds * (G - 1); e += blockDim.x) {
+    const uint32_t k = e / (G - 1), cc = 1 + e % (G - 1);
+    slist_entry(a.kpart[k], cc, L.sl + k * 2 * L.g4, L.sl + k * 2 * L.g4 + L.g4);
+  }
+  __syncthreads();
+  for (uint32_t k = 0; k < kKinds; k++) {
+    const Partition &pt = a.kpart[k];
+    const uint32_t cb = cta_begin(pt, c), ce = cta_begin(pt, c + 1);
+    if (ce == cb) continue;
+    const uint32_t rt0 = cb / pt.KT, nrt = (ce - 1) / pt.KT - rt0 + 1;
+    for (uint32_t i = threadIdx.x; i < nrt; i += blockDim.x) {
+      uint2 item;
+      if (!comb_item(pt, c, rt0 + i, item)) continue;
+      const uint32_t j = atomicAdd(&L.ncomb[k], 1u);
+      if (j < kMaxComb)
+        L.comb[k * kMaxComb + j] = item;
+      else
+        atomicOr(a.err, DEV_ERR_BAD_LIST);  // cannot happen: at most 17 cut row tiles per CTA
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x < kKinds) L.ncomb[threadIdx.x] = min(L.ncomb[threadIdx.x], kMaxComb);
+  __syncthreads();
+}
 // stage `bytes` from global into shared memory on vbar (any thread)
 CH_DEV void stage_copy(const SmemLayout &L, void *dst, const void *src, uint32_t bytes) {
   mbar_expect_tx(L.vbar, bytes);
@@ -464,7 +517,8 @@ CH_DEV void gemv_prologue(const Phase &p, const MegaArgs &a, const SmemLayout &L
   const bool writer = (blockIdx.x == 0);
   if (p.pm == PM_DIRECT) return;
   if (p.pm == PM_GELU) {
-    patch_act_frag(p.r_in, L.slist, L.soff, S.part, K, reinterpret_cast<uint32_t *>(S.s0));
+    patch_act_frag(p.r_in, sl_list(L, p.r_in.kind), sl_off(L, p.r_in.kind), S.part, K,
+                   reinterpret_cast<uint32_t *>(S.s0));
     return;
   }
   // PM_NORM / PM_ADD_NORM: one pair per thread (K <= 8 * threads)
@@ -473,7 +527,7 @@ CH_DEV void gemv_prologue(const Phase &p, const MegaArgs &a, const SmemLayout &L
 #pragma unroll
   for (int e = 0; e < 8; e++) x[e] = 0.f, w[e] = 0.f;
   if (p.pm == PM_ADD_NORM) {  // x = (x_in + [rmsnorm(r) * post_w]) * scalar     (add_rmsnorm.wgsl:15-51)
-    patch_staged(p.r_in, L.slist, L.soff, S.part, 0, K, S.s0);
+    patch_staged(p.r_in, sl_list(L, p.r_in.kind), sl_off(L, p.r_in.kind), S.part, 0, K, S.s0);
     __syncthreads();
     PHASE_MARK(pi, 7);
     float r[8];
@@ -543,26 +597,23 @@ CH_DEV void gemv_prologue(const Phase &p, const MegaArgs &a, const SmemLayout &L
   }
 }
 
-// After every warp of the CTA finished its tiles: fold the warps' partial segments.
-// Row tiles inside the CTA's range go to `direct`, straddling ones to the CTA's slot.
-CH_DEV void cta_combine(const Phase &p, const MegaArgs &a, const float *wpart) {
+// After every warp of the CTA finished its tiles: fold the warps' partial segments of
+// the row tiles listed for this CTA (comb_item), in warp order.  Row tiles inside the
+// CTA's range go to `direct`, straddling ones to the CTA's slot.
+CH_DEV void cta_combine(const Phase &p, const MegaArgs &a, const SmemLayout &L) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const uint32_t c = blockIdx.x, KT = p.k_tiles;
-  const Partition &pt = p.out.pt;
-  const uint32_t cb = cta_begin(pt, c), ce = cta_begin(pt, c + 1);
-  if (ce == cb) return;
-  const uint32_t rt0 = cb / KT, rt1 = (ce - 1) / KT;
-  for (uint32_t rt = rt0 + warp; rt <= rt1; rt += MK_NW) {
-    const uint32_t t_lo = rt * KT, t_hi = t_lo + KT - 1;
-    const uint32_t a_lo = max(t_lo, cb), a_hi = min(t_hi, ce - 1);
-    const uint32_t w0 = warp_of(pt, c, a_lo), w1 = warp_of(pt, c, a_hi);
-    const bool inside = cb <= t_lo && t_hi < ce;
-    if (w0 == w1 && inside) continue;  // one warp covered the whole row tile: already stored
+  const uint32_t c = blockIdx.x, kind = p.out.kind;
+  const uint2 *items = L.comb + kind * kMaxComb;
+  const uint32_t n = L.ncomb[kind];
+  for (uint32_t j = warp; j < n; j += MK_NW) {
+    const uint2 it = items[j];
+    const uint32_t rt = it.x, w0 = it.y & 15u, w1 = (it.y >> 4) & 15u;
+    const bool inside = (it.y >> 8) & 1u;
     float sum = 0.f;
     if (lane < 16)
       for (uint32_t w = w0; w <= w1; w++) {
-        const uint32_t slot = warp_begin(pt, c, w) < t_lo ? 1u : 0u;
-        sum = __fadd_rn(sum, wpart[(w * 2 + slot) * 16 + lane]);
+        const uint32_t slot = (it.y >> (16 + w)) & 1u;
+        sum = __fadd_rn(sum, L.wpart[(w * 2 + slot) * 16 + lane]);
       }
     const float up = __shfl_down_sync(0xffffffffu, sum, 8);
     if (inside) {
@@ -574,7 +625,7 @@ CH_DEV void cta_combine(const Phase &p, const MegaArgs &a, const float *wpart) {
         out_row(a, p.out, rt * 16 + lane, sum);
       }
     } else if (lane < 16) {  // straddling row tile: this CTA's share, added up by the consumer
-      p.out.partial[((size_t)c * 2 + (cb < t_lo ? 1u : 0u)) * 16 + lane] = sum;
+      p.out.partial[((size_t)c * 2 + ((it.y >> 9) & 1u)) * 16 + lane] = sum;
     }
   }
 }
@@ -841,14 +892,16 @@ CH_DEV void attn_phase(const Phase &p, const MegaArgs &a, const StepParams &sp, 
     const uint32_t n4 = (gridDim.x - 1) * 4;
     const uint32_t q0 = kvh * R * D, k0 = a.nq * D + kvh * D, v0 = a.nq * D + (uint32_t)kv_dim + kvh * D;
     for (uint32_t idx = tid; idx < n4; idx += MK_THREADS) {
-      const uint32_t e = L.slist[idx / 4];
+      const uint32_t e = sl_list(L, p.r_in.kind)[idx / 4];
       if (e == kNoStraddle) continue;
       const uint32_t q = (idx % 4) * 4, r = (e & 0xFFFFu) * 16 + q;
       float *dst = nullptr;
       if (r >= q0 && r < q0 + R * D) dst = sm.q_s + (r - q0);
       else if (r >= k0 && r < k0 + D) dst = sm.k_new + (r - k0);
       else if (r >= v0 && r < v0 + D) dst = sm.v_new + (r - v0);
-      if (dst) *reinterpret_cast<float4 *>(dst) = straddle_quad(p.r_in, L.slist, L.soff, sm.part, idx / 4, q);
+      if (dst)
+        *reinterpret_cast<float4 *>(dst) =
+            straddle_quad(p.r_in, sl_list(L, p.r_in.kind), sl_off(L, p.r_in.kind), sm.part, idx / 4, q);
     }
   }
   __syncthreads();
@@ -1158,7 +1211,7 @@ CH_DEV void topk_phase(const Phase &p, const MegaArgs &a, const SmemLayout &L) {
   uint32_t lo, hi;
   topk_slice(p, lo, hi);
   const uint32_t lo4 = lo & ~3u;
-  patch_staged(p.r_in, L.slist, L.soff, sm.part, lo4, (hi + 3u) & ~3u, sm.lg);
+  patch_staged(p.r_in, sl_list(L, p.r_in.kind), sl_off(L, p.r_in.kind), sm.part, lo4, (hi + 3u) & ~3u, sm.lg);
   __syncthreads();
   {
     uint64_t k[E1];
@@ -1224,7 +1277,6 @@ CH_DEV void pre_phase(const Phase &p, const MegaArgs &a, const StepParams &sp, c
   fence_proxy_async();  // this thread's generic shared-memory writes before the bulk copies that reuse it
   __syncthreads();
   if (p.kind == PH_GEMV) {
-    if (p.pm == PM_ADD_NORM || p.pm == PM_GELU) build_slist(p.r_in, L.slist, L.soff);
     if ((p.pm == PM_NORM || p.pm == PM_ADD_NORM) && threadIdx.x == 0) {
       GemvStage S(L.u, p.K, p.pm);
       stage_copy(L, S.s1, p.x_in, p.K * 4);  // residual: written at least one barrier ago
@@ -1232,10 +1284,7 @@ CH_DEV void pre_phase(const Phase &p, const MegaArgs &a, const StepParams &sp, c
       if (p.post_w) stage_copy(L, S.s2, p.post_w, p.K * 4);
     }
   } else if (p.kind == PH_ATTN) {
-    build_slist(p.r_in, L.slist, L.soff);
     attn_pre<R>(p, a, sp, L);
-  } else if (p.kind == PH_TOPK) {
-    build_slist(p.r_in, L.slist, L.soff);
   }
   __syncthreads();  // every expect_tx of this phase precedes the arrival
   if (threadIdx.x == 0) mbar_arrive(L.vbar);
@@ -1276,9 +1325,11 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(const MegaAr
   L.vbar = L.bars + MK_NW * MK_SPW;
   L.xzero = reinterpret_cast<uint4 *>(L.vbar + 2);
   L.wpart = reinterpret_cast<float *>(L.xzero + 1);
-  L.slist = reinterpret_cast<uint32_t *>(L.wpart + MK_NW * 2 * 16);
-  L.soff = L.slist + kMaxGrid + 1;
-  L.wphys = L.soff + kMaxGrid + 1;
+  L.sl = reinterpret_cast<uint32_t *>(L.wpart + MK_NW * 2 * 16);
+  L.g4 = (gridDim.x + 3u) & ~3u;
+  L.comb = reinterpret_cast<uint2 *>(L.sl + kKinds * 2 * L.g4);
+  L.ncomb = reinterpret_cast<uint32_t *>(L.comb + kKinds * kMaxComb);
+  L.wphys = L.ncomb + 8;
   L.u = reinterpret_cast<uint8_t *>(L.wphys + 2 * kWinSlots);
   __shared__ float red[32];
   __shared__ Phase ph_s[3];  // phases pi, pi+1 and pi+2 (copied ahead with cp.async)
@@ -1308,6 +1359,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(const MegaAr
   cp_async_wait_all();
   __syncthreads();
   attn_lists_init(a, sp_s, L.wphys);
+  launch_tables(a, L);
   pre_phase<R>(ph_s[0], a, sp_s, L);
 
   const unsigned long long base = a.base[0], gbase = a.base[1];  // arrivals before this launch
@@ -1335,7 +1387,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(const MegaAr
         gemv_tiles<FMT_Q8, true>(p, a, gw, L, xq, sxs, cidx, st, ok, pol, pi);
       __syncthreads();
       PHASE_MARK(pi, 3);
-      cta_combine(p, a, L.wpart);
+      cta_combine(p, a, L);
     } else if (p.kind == PH_ATTN) {
       attn_phase<R>(p, a, sp_s, L, pi);
     } else if (p.kind == PH_TOPK) {
@@ -1382,8 +1434,9 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(const MegaAr
 
 size_t mk_smem_bytes(uint32_t max_k, uint32_t hidden, uint32_t ratio, uint32_t max_splits, uint32_t cache_slots,
                      uint32_t grid) {
+  const size_t g4 = (grid + 3u) & ~3u;
   const size_t fixed = (size_t)MK_NW * MK_SPW * MK_STAGE + (MK_NW * MK_SPW + 2) * 8 + 16 + MK_NW * 2 * 16 * 4 +
-                      2 * (kMaxGrid + 1) * 4 + 2 * kWinSlots * 4;
+                      kKinds * 2 * g4 * 4 + kKinds * kMaxComb * 8 + 8 * 4 + 2 * kWinSlots * 4;
   const size_t part = (size_t)grid * 32 * 4;  // straddle partials of the previous GEMV
   // GEMV staging: 4 vectors of `hidden` for the norm prologues, one of max_k otherwise
   const size_t gemv = std::max((size_t)4 * hidden * 4, (size_t)max_k * 4) + part;

@@ -44,7 +44,9 @@ struct GemvOut {
                    // 2: low-latency exchange -- `direct` is a [2 parities][world][row0] array of
                    // 8-byte {value, epoch} words, one plain store per row and rank, no fence
   uint32_t xidx;   // push 2: index of this exchange within the launch (epoch = base[2] + xidx + 1)
+  uint32_t kind;   // which of the launch's kKinds partitions (MegaArgs::kpart) produced it
 };
+constexpr uint32_t kKinds = 5;  // GEMV partitions of a launch: q|k|v, o, gate|up, down, LM head
 
 struct alignas(16) Phase {
   uint32_t kind, fmt, pm, is_sliding;
@@ -84,6 +86,7 @@ struct MegaArgs {
   const Phase *phases;
   const StreamDesc *streams;
   uint32_t nstreams;
+  Partition kpart[kKinds];  // the partition of each GEMV kind (GemvOut::kind)
   uint32_t nphases, grid;
   unsigned long long *arrive;  // this GPU's grid-barrier arrivals (monotonic across launches)
   unsigned long long *base;    // [3] arrivals (local, cross-rank) and exchange epochs before this

@@ -217,6 +217,7 @@ struct ch_model {
   bool loop_ready = false;
   // persistent decode-step kernel: phase tables, per-GEMV outputs, barrier counters
   Phase *d_phases = nullptr, *d_phases_nl = nullptr;
+  Partition kpart[2][kKinds] = {};  // GEMV partitions of each phase table (with / without logits)
   uint32_t n_phases = 0, n_phases_nl = 0;
   StreamDesc *d_streams = nullptr, *d_streams_nl = nullptr;  // weight streams of the GEMV phases
   uint32_t n_streams = 0, n_streams_nl = 0;
@@ -430,7 +431,8 @@ static int alloc_model_buffers(ch_model *m) {
 enum GemvKind { GK_QKV = 0, GK_O = 1, GK_GU = 2, GK_DOWN = 3, GK_LM = 4 };
 
 static int build_phases(ch_model *m, bool with_logits, Phase **d_out, uint32_t *n_out, StreamDesc **d_str,
-                        uint32_t *n_str, uint32_t *n_cross, uint32_t *n_local, uint32_t *n_x) {
+                        uint32_t *n_str, uint32_t *n_cross, uint32_t *n_local, uint32_t *n_x, Partition *kpart) {
+  static_assert(GK_LM + 1 == kKinds, "one partition per GEMV kind");
   const uint32_t G = (uint32_t)m->mk_grid, GW = G * mk_warps();
   const bool tp = m->world > 1;
   // Local output rows of each GEMV and its k tiles.  Tensor parallel (Megatron
@@ -458,7 +460,7 @@ static int build_phases(ch_model *m, bool with_logits, Phase **d_out, uint32_t *
       pt.rq = (rows[k] / 16) / G;
       pt.rrem = (rows[k] / 16) % G;
     }
-    outs[k] = GemvOut{dst[k], m->gpart[k], pt, k == GK_GU ? 1u : 0u, row0[k], gathered[k] ? 2u : 0u, 0u};
+    outs[k] = GemvOut{dst[k], m->gpart[k], pt, k == GK_GU ? 1u : 0u, row0[k], gathered[k] ? 2u : 0u, 0u, (uint32_t)k};
   }
   auto gemv = [&](int kind, const uint8_t *tiles, int fmt, uint32_t K) {
     Phase p{};
@@ -545,6 +547,7 @@ static int build_phases(ch_model *m, bool with_logits, Phase **d_out, uint32_t *
     lm.row_tiles = 0;
     lm.out.pt.q = lm.out.pt.rem = 0;
   }
+  for (int k = 0; k < 5; k++) kpart[k] = k == GK_LM ? lm.out.pt : outs[k].pt;
   ph.push_back(lm);
   if (with_logits) {
     Phase tk{};
@@ -642,9 +645,9 @@ static int init_decode_step(ch_model *m) {
     CH_CUDA(cudaMemset(m->arena, 0, m->arena_bytes));
   }
   CH_TRY(build_phases(m, true, &m->d_phases, &m->n_phases, &m->d_streams, &m->n_streams, &m->n_cross,
-                      &m->n_local, &m->n_x));
+                      &m->n_local, &m->n_x, m->kpart[0]));
   CH_TRY(build_phases(m, false, &m->d_phases_nl, &m->n_phases_nl, &m->d_streams_nl, &m->n_streams_nl,
-                      &m->n_cross_nl, &m->n_local_nl, &m->n_x_nl));
+                      &m->n_cross_nl, &m->n_local_nl, &m->n_x_nl, m->kpart[1]));
   return CH_OK;
 }
 
@@ -653,6 +656,7 @@ static MegaArgs mega_args(ch_model *m, bool logits, bool device_loop) {
   a.phases = logits ? m->d_phases : m->d_phases_nl;
   a.nphases = logits ? m->n_phases : m->n_phases_nl;
   a.streams = logits ? m->d_streams : m->d_streams_nl;
+  for (uint32_t k = 0; k < kKinds; k++) a.kpart[k] = m->kpart[logits ? 0 : 1][k];
   a.nstreams = logits ? m->n_streams : m->n_streams_nl;
   a.grid = (uint32_t)m->mk_grid;
   a.arrive = m->mk_arrive;
