@@ -503,6 +503,29 @@ struct GemvStage {
   }
 };
 
+// Sum over the CTA's threads: block_sum's additions in block_sum's order (the warps'
+// sums 0 .. MK_NW-1 added to 0), with the MK_NW partials read by four 16-byte loads
+// issued together instead of one dependent load per warp.  red: 16-byte aligned.
+CH_DEV float cta_sum(float v, float *red) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  v = warp_sum(v);
+  __syncthreads();
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  float4 q[MK_NW / 4];
+#pragma unroll
+  for (int i = 0; i < MK_NW / 4; i++) q[i] = reinterpret_cast<const float4 *>(red)[i];
+  float t = 0.0f;
+#pragma unroll
+  for (int i = 0; i < MK_NW / 4; i++) {
+    t += q[i].x;
+    t += q[i].y;
+    t += q[i].z;
+    t += q[i].w;
+  }
+  return t;
+}
+
 // GEMV input.  Norm prologues (q|k|v, gate|up, LM head): the limbs of the normed
 // vector, in place over S0, and their block scales over the first K/32 floats after
 // it -- integer tiles.  PM_DIRECT / PM_GELU (o, down): S0 already holds the
@@ -570,7 +593,7 @@ CH_DEV void gemv_prologue(const Phase &p, const MegaArgs &a, const SmemLayout &L
       float sr = 0.f;
 #pragma unroll
       for (int e = 0; e < 8; e++) sr = __fmaf_rn(r[e], r[e], sr);
-      sr = block_sum(sr, red);
+      sr = cta_sum(sr, red);
       inv_r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sr, (float)K), a.eps)));
     }
 #pragma unroll
@@ -585,7 +608,7 @@ CH_DEV void gemv_prologue(const Phase &p, const MegaArgs &a, const SmemLayout &L
   float ss = 0.f;
 #pragma unroll
   for (int e = 0; e < 8; e++) ss = __fmaf_rn(x[e], x[e], ss);
-  ss = block_sum(ss, red);  // also orders every read of S0 / S1 before the in-place limb writes
+  ss = cta_sum(ss, red);  // also orders every read of S0 / S1 before the in-place limb writes
   const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)K), a.eps)));
   if (on) {
     float nw[8], v[8];
@@ -609,12 +632,15 @@ CH_DEV void cta_combine(const Phase &p, const MegaArgs &a, const SmemLayout &L) 
     const uint2 it = items[j];
     const uint32_t rt = it.x, w0 = it.y & 15u, w1 = (it.y >> 4) & 15u;
     const bool inside = (it.y >> 8) & 1u;
+    // every warp's segment loaded first (all in range of wpart), then added in warp order
+    float seg[MK_NW];
+#pragma unroll
+    for (int w = 0; w < MK_NW; w++) seg[w] = L.wpart[(w * 2 + ((it.y >> (16 + w)) & 1u)) * 16 + (lane & 15)];
     float sum = 0.f;
-    if (lane < 16)
-      for (uint32_t w = w0; w <= w1; w++) {
-        const uint32_t slot = (it.y >> (16 + w)) & 1u;
-        sum = __fadd_rn(sum, L.wpart[(w * 2 + slot) * 16 + lane]);
-      }
+#pragma unroll
+    for (int w = 0; w < MK_NW; w++)
+      if ((uint32_t)w >= w0 && (uint32_t)w <= w1) sum = __fadd_rn(sum, seg[w]);
+    if (lane >= 16) sum = 0.f;
     const float up = __shfl_down_sync(0xffffffffu, sum, 8);
     if (inside) {
       if (p.out.act) {  // act values of lanes 0..7 as B fragments, in pairs
@@ -1127,15 +1153,21 @@ CH_DEV void attn_phase(const Phase &p, const MegaArgs &a, const StepParams &sp, 
     sm.cml[hh * max_splits + j] = ml.y;
   }
   __syncthreads();
-  if (tid < R) {
-    float M = -INFINITY, Lsum = 0.f;
-    for (uint32_t j = 0; j < nsplit; j++) M = fmaxf(M, sm.cmb[tid * max_splits + j]);
-    for (uint32_t j = 0; j < nsplit; j++) {
-      const float f = expf(__fsub_rn(sm.cmb[tid * max_splits + j], M));
-      Lsum = __fmaf_rn(sm.cml[tid * max_splits + j], f, Lsum);
-      sm.cmb[tid * max_splits + j] = f;
+  if (warp < R) {  // warp h: lane j holds split j's maximum; the factors in parallel, the sum in split order
+    const int hh = warp;
+    const float mj = (uint32_t)lane < nsplit ? sm.cmb[hh * max_splits + lane] : -INFINITY;
+    const float M = warp_max(mj);
+    const float f = (uint32_t)lane < nsplit ? expf(__fsub_rn(mj, M)) : 0.f;
+    const float lj = (uint32_t)lane < nsplit ? sm.cml[hh * max_splits + lane] : 0.f;
+    float Lsum = 0.f;
+#pragma unroll
+    for (uint32_t j = 0; j < kMkMaxSplits; j++) {
+      const float fj = __shfl_sync(0xffffffffu, f, j), lsj = __shfl_sync(0xffffffffu, lj, j);
+      if (j < nsplit) Lsum = __fmaf_rn(lsj, fj, Lsum);
     }
-    sm.stat[2 * tid] = __fdiv_rn(1.0f, __fadd_rn(Lsum, 1e-9f));
+    __syncwarp();
+    if ((uint32_t)lane < nsplit) sm.cmb[hh * max_splits + lane] = f;
+    if (lane == 0) sm.stat[2 * hh] = __fdiv_rn(1.0f, __fadd_rn(Lsum, 1e-9f));
   }
   __syncthreads();
   float o = 0.f;
@@ -1331,7 +1363,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(const MegaAr
   L.ncomb = reinterpret_cast<uint32_t *>(L.comb + kKinds * kMaxComb);
   L.wphys = L.ncomb + 8;
   L.u = reinterpret_cast<uint8_t *>(L.wphys + 2 * kWinSlots);
-  __shared__ float red[32];
+  __shared__ __align__(16) float red[32];
   __shared__ Phase ph_s[3];  // phases pi, pi+1 and pi+2 (copied ahead with cp.async)
   __shared__ StepParams sp_s;
 
