@@ -942,7 +942,9 @@ CH_DEV void attn_phase(const Phase &p, const MegaArgs &a, const StepParams &sp, 
 #pragma unroll
     for (int e = 0; e < 8; e++) ss = __fmaf_rn(v[e], v[e], ss);
     ss = warp_sum(ss);
-    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)D), a.eps)));
+    // ss / D as ss * 2^-8: D = 256 is a power of two, so both round the same exact value
+    static_assert(D == 256, "the head mean below divides by 256");
+    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fmul_rn(ss, 1.0f / 256.0f), a.eps)));
     float out[8];
     if (warp <= R) {  // rmsnorm * w, then RoPE half-split at `clock` (qkv_rope.wgsl; kernels.zig:101-119)
       const float *w = warp < R ? sm.qn_w : sm.kn_w;
@@ -1026,20 +1028,36 @@ CH_DEV void attn_phase(const Phase &p, const MegaArgs &a, const StepParams &sp, 
       for (int e = 0; e < EPL; e++) f[e] = 0.f;
     }
   };
-  for (uint32_t i = warp; i < n; i += MK_NW) {
-    float kv[EPL];
-    uint32_t phys;
+  // two slots (i, i + MK_NW) per iteration: independent chains, each slot's arithmetic unchanged
+  for (uint32_t i = warp; i < n; i += 2 * MK_NW) {
+    const uint32_t i2 = i + MK_NW;
+    const bool two = i2 < n;
+    float kv[EPL], kv2[EPL];
+    uint32_t phys, phys2 = 0u;
     row(i, 0, kv, phys);
-    const bool valid = phys < a.cache_slots;
+    if (two) {
+      row(i2, 0, kv2, phys2);
+    } else {
+#pragma unroll
+      for (int e = 0; e < EPL; e++) kv2[e] = 0.f;
+    }
+    const bool valid = phys < a.cache_slots, valid2 = phys2 < a.cache_slots;
 #pragma unroll
     for (int h = 0; h < R; h++) {
-      float dot = 0.f;
+      float dot = 0.f, dot2 = 0.f;
 #pragma unroll
-      for (int e = 0; e < EPL; e++) dot = __fmaf_rn(qr[h][e], kv[e], dot);
+      for (int e = 0; e < EPL; e++) {
+        dot = __fmaf_rn(qr[h][e], kv[e], dot);
+        dot2 = __fmaf_rn(qr[h][e], kv2[e], dot2);
+      }
       dot = warp_sum(dot);
-      if (lane == 0) sm.sc[h * chunk_cap + i] = valid ? __fmul_rn(dot, p.attn_scale) : -INFINITY;
+      dot2 = warp_sum(dot2);
+      if (lane == 0) {
+        sm.sc[h * chunk_cap + i] = valid ? __fmul_rn(dot, p.attn_scale) : -INFINITY;
+        if (two) sm.sc[h * chunk_cap + i2] = valid2 ? __fmul_rn(dot2, p.attn_scale) : -INFINITY;
+      }
     }
-    if (!valid && lane == 0) atomicOr(a.err, DEV_ERR_BAD_LIST);
+    if (lane == 0 && (!valid || (two && !valid2))) atomicOr(a.err, DEV_ERR_BAD_LIST);
   }
   __syncthreads();
   // 3. softmax statistics per head over this chunk (max seeded at -1e9, decode_attn.wgsl:81)
@@ -1091,9 +1109,12 @@ CH_DEV void attn_phase(const Phase &p, const MegaArgs &a, const StepParams &sp, 
   if (it.nsplit == 1) {  // whole list in this CTA: normalize and write (same arithmetic as a 1-split combine)
     for (int idx = tid; idx < R * D; idx += MK_THREADS) {  // R*D is a multiple of 32: whole warps
       const int h = idx / D, d = idx % D;
+      float ow[MK_NW];
+#pragma unroll
+      for (int w = 0; w < MK_NW; w++) ow[w] = sm.o_s[(w * R + h) * D + d];
       float s = 0.f;
 #pragma unroll
-      for (int w = 0; w < MK_NW; w++) s = __fadd_rn(s, sm.o_s[(w * R + h) * D + d]);
+      for (int w = 0; w < MK_NW; w++) s = __fadd_rn(s, ow[w]);
       const float Lsum = __fmaf_rn(sm.stat[2 * h + 1], 1.0f, 0.f);
       const float o = __fmul_rn(__fmaf_rn(s, 1.0f, 0.f), __fdiv_rn(1.0f, __fadd_rn(Lsum, 1e-9f)));
       const float on = __shfl_down_sync(0xffffffffu, o, 1);
@@ -1104,9 +1125,12 @@ CH_DEV void attn_phase(const Phase &p, const MegaArgs &a, const StepParams &sp, 
   float *part = a.attn_partial + ((size_t)(kvh * max_splits + it.split) * R) * (D + 2);
   for (int idx = tid; idx < R * D; idx += MK_THREADS) {
     const int h = idx / D, d = idx % D;
+    float ow[MK_NW];
+#pragma unroll
+    for (int w = 0; w < MK_NW; w++) ow[w] = sm.o_s[(w * R + h) * D + d];
     float s = 0.f;
 #pragma unroll
-    for (int w = 0; w < MK_NW; w++) s = __fadd_rn(s, sm.o_s[(w * R + h) * D + d]);
+    for (int w = 0; w < MK_NW; w++) s = __fadd_rn(s, ow[w]);
     part[h * (D + 2) + d] = s;
   }
   if (tid < R) {
