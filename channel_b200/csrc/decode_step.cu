@@ -566,20 +566,32 @@ CH_DEV void gemv_prologue(const Phase &p, const MegaArgs &a, const SmemLayout &L
                                       (size_t)(ep & 1) * p.nsum * K + (tid >> 2) * 32 + (tid & 3u) * 2;
         const uint64_t t0 = globaltimer_ns();
         bool live = !*(volatile uint32_t *)&s_abort;
-        for (uint32_t rk = 0; rk < p.nsum; rk++, q += K) {
+        // two ranks' 8 words at a time in flight together (one round trip), then checked
+        // and added in rank order; a word whose epoch is not here yet is polled alone
+        for (uint32_t rk = 0; rk < p.nsum; rk += 2) {
+          const uint32_t nr = min(2u, p.nsum - rk);
+          unsigned long long w[2][8];
 #pragma unroll
-          for (int e = 0; e < 8; e++) {
-            unsigned long long w = ld_x64_sys(q + 8 * (e >> 1) + (e & 1));
-            while ((uint32_t)(w >> 32) != (uint32_t)ep && live) {
-              if (globaltimer_ns() - t0 > 2000000000ull) {
-                atomicOr(a.err, DEV_ERR_PEER_TIMEOUT);
-                s_abort = 1u;
-                live = false;
+          for (uint32_t j = 0; j < 2; j++)
+#pragma unroll
+            for (int e = 0; e < 8; e++)
+              w[j][e] = j < nr ? ld_x64_sys(q + (size_t)(rk + j) * K + 8 * (e >> 1) + (e & 1)) : 0ull;
+#pragma unroll
+          for (uint32_t j = 0; j < 2; j++) {
+            if (j >= nr) break;
+#pragma unroll
+            for (int e = 0; e < 8; e++) {
+              while ((uint32_t)(w[j][e] >> 32) != (uint32_t)ep && live) {
+                if (globaltimer_ns() - t0 > 2000000000ull) {
+                  atomicOr(a.err, DEV_ERR_PEER_TIMEOUT);
+                  s_abort = 1u;
+                  live = false;
+                }
+                w[j][e] = ld_x64_sys(q + (size_t)(rk + j) * K + 8 * (e >> 1) + (e & 1));
               }
-              w = ld_x64_sys(q + 8 * (e >> 1) + (e & 1));
+              const float v = __uint_as_float((uint32_t)w[j][e]);
+              r[e] = (rk + j) ? __fadd_rn(r[e], v) : v;
             }
-            const float v = __uint_as_float((uint32_t)w);
-            r[e] = rk ? __fadd_rn(r[e], v) : v;
           }
         }
       } else {
