@@ -17,6 +17,7 @@ model_dispatch.zig:144, and raises BatchTooLarge / GpuError from prefill).
 from __future__ import annotations
 
 import ctypes as C
+from collections import abc as _abc
 from dataclasses import dataclass, field
 from typing import Callable, Optional, Sequence
 
@@ -28,17 +29,48 @@ TOTAL_SLOTS = 4096
 UPPER_RECALL_SLOTS = 128
 
 
+_PTR_TYPES: dict = {}
+
+
 def _ptr(a: Optional[np.ndarray], ct):
     if a is None:
         return None
     assert a.flags["C_CONTIGUOUS"]
-    return a.ctypes.data_as(C.POINTER(ct))
+    pt = _PTR_TYPES.get(ct)
+    if pt is None:
+        pt = _PTR_TYPES[ct] = C.POINTER(ct)
+    return C.cast(a.ctypes.data, pt)  # cheaper than ndarray.ctypes.data_as per call
 
 
 @dataclass
 class TopKCandidate:
     id: int = 0
     val: float = 0.0
+
+
+class TopKList(_abc.Sequence):
+    """The 64 TopKCandidate of a step, read from the C-ABI result array on access (a
+    decode loop that only wants the token does not pay for 64 Python objects)."""
+
+    __slots__ = ("_tk",)
+
+    def __init__(self, tk):
+        self._tk = tk
+
+    def __len__(self) -> int:
+        return len(self._tk)
+
+    def __getitem__(self, i):
+        if isinstance(i, slice):
+            return [TopKCandidate(t.id, t.val) for t in self._tk[i]]
+        t = self._tk[i]
+        return TopKCandidate(t.id, t.val)
+
+    def __eq__(self, other) -> bool:
+        return list(self) == list(other)
+
+    def __repr__(self) -> str:
+        return repr(list(self))
 
 
 @dataclass
@@ -408,7 +440,7 @@ def gpu_dispatch_forward_token(gpu: GpuModelContext, x: np.ndarray, clock: int, 
                                topk_out: bool = True) -> tuple[int, Optional[list]]:
     """gpuDispatchForwardToken (src/gpu/model_dispatch.zig:128-153).
 
-    Returns (greedy token, list of 64 TopKCandidate or None)."""
+    Returns (greedy token, the 64 TopKCandidate as a sequence, or None)."""
     lib = L.load()
     x = np.ascontiguousarray(x, np.float32)
     act = np.ascontiguousarray(active_slots, np.uint32)
@@ -417,8 +449,7 @@ def gpu_dispatch_forward_token(gpu: GpuModelContext, x: np.ndarray, clock: int, 
     tok = C.c_uint32(0)
     L.check(lib.ch_forward_token(gpu.handle, _ptr(x, C.c_float), clock, slot_idx, _ptr(act, C.c_uint32), len(act),
                                  _ptr(sli, C.c_uint32), len(sli), tk, C.byref(tok) if topk_out else None))
-    cands = [TopKCandidate(t.id, t.val) for t in tk] if topk_out else None
-    return tok.value, cands
+    return tok.value, (TopKList(tk) if topk_out else None)
 
 
 def gpu_dispatch_prefill_batch(gpu: GpuModelContext, tokens: Sequence[int], embed_tokens: Optional[np.ndarray],
@@ -514,10 +545,11 @@ class DynamicRingBuffer:
         return self._lib.ch_ring_slot_clock(self.h, layer, slot)
 
     def getActiveSlotsLayer(self, layer: int, clock: int, is_sliding: bool, sliding_window: int) -> np.ndarray:
-        out = np.empty(TOTAL_SLOTS, np.uint32)
-        n = self._lib.ch_ring_active_slots(self.h, layer, clock, 1 if is_sliding else 0, sliding_window,
-                                           _ptr(out, C.c_uint32))
-        return out[:n].copy()
+        if getattr(self, "_out", None) is None:  # one output buffer per ring, reused by every call
+            self._out = np.empty(TOTAL_SLOTS, np.uint32)
+            self._out_p = _ptr(self._out, C.c_uint32)
+        n = self._lib.ch_ring_active_slots(self.h, layer, clock, 1 if is_sliding else 0, sliding_window, self._out_p)
+        return self._out[:n].copy()
 
     def getActiveSlots(self, layer: int, clock: int) -> np.ndarray:
         return self.getActiveSlotsLayer(layer, clock, False, 1024)
