@@ -550,6 +550,10 @@ CH_DEV void gemv_prologue(const Phase &p, const MegaArgs &a, const SmemLayout &L
 #pragma unroll
   for (int e = 0; e < 8; e++) x[e] = 0.f, w[e] = 0.f;
   if (p.pm == PM_ADD_NORM) {  // x = (x_in + [rmsnorm(r) * post_w]) * scalar     (add_rmsnorm.wgsl:15-51)
+    if (on) {  // residual and post-norm weight (staged before the barrier): read while the patch runs
+      ld_pair_rot(S.s1, tid, x);
+      if (p.post_w) ld_pair_rot(S.s2, tid, w);
+    }
     patch_staged(p.r_in, sl_list(L, p.r_in.kind), sl_off(L, p.r_in.kind), S.part, 0, K, S.s0);
     __syncthreads();
     PHASE_MARK(pi, 7);
@@ -597,8 +601,6 @@ CH_DEV void gemv_prologue(const Phase &p, const MegaArgs &a, const SmemLayout &L
       } else {
         ld_pair_rot(S.s0, tid, r);
       }
-      ld_pair_rot(S.s1, tid, x);
-      if (p.post_w) ld_pair_rot(S.s2, tid, w);
     }
     float inv_r = 1.0f;
     if (p.post_w) {
