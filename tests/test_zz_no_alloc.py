@@ -67,3 +67,39 @@ def test_noalloc_matches_gemv_q4_on_consecutive_calls(ctx, oracle):
     call(lib.ch_gemv_q4_noalloc, tiles.data_ptr(), M, K, xd.data_ptr(), y.data_ptr(), None, None)
     torch.cuda.synchronize()
     assert_close(host(y), oracle.gemv_q4(W, x, M, K), what="noalloc on the default stream vs oracle")
+
+
+@pytest.mark.gpu
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs a second GPU")
+def test_noalloc_and_gemv_on_a_second_device(ctx, oracle):
+    """Both GEMV entry points on device 1 after device 0 has run them (the session
+    context): the dynamic shared-memory attribute (147 KB) and the no-alloc scratch are
+    per device, so the first launch on the second device must set up its own."""
+    from channel_b200 import GpuContext
+    lib = L.load()
+    M, K = 3840, 15360
+    W = oracle.gen_q4(M, K, oracle.tensor_seed(7, 11, 0))
+    with torch.cuda.device(1):
+        c1 = GpuContext.init(1)
+        try:
+            tiles = empty(lib.ch_q4_tile_bytes(M, K), torch.uint8)
+            Wd = dev(W)
+            call(lib.ch_q4_pack, c1.handle, Wd.data_ptr(), M, K, tiles.data_ptr())
+            status = torch.zeros(1, dtype=torch.int32, device="cuda")
+            for rep in range(2):
+                x = oracle.gen_f32(K, oracle.tensor_seed(7, 11, 100 + rep))
+                ref = oracle.gemv_q4(W, x, M, K)
+                xd, y1, y2 = dev(x), empty(M), empty(M)
+                torch.cuda.synchronize()
+                call(lib.ch_gemv_q4, c1.handle, tiles.data_ptr(), M, K, xd.data_ptr(), y1.data_ptr())
+                c1.synchronize()
+                call(lib.ch_gemv_q4_noalloc, tiles.data_ptr(), M, K, xd.data_ptr(), y2.data_ptr(), status.data_ptr(),
+                     c1.stream)
+                c1.synchronize()
+                assert_close(host(y1), ref, what=f"ch_gemv_q4 on device 1, call {rep}")
+                assert_close(host(y2), ref, what=f"noalloc on device 1, call {rep}")
+            assert int(status.item()) == 0
+            assert c1.device_status() == 0
+        finally:
+            c1.synchronize()
+            c1.deinit()
