@@ -853,7 +853,13 @@ CH_DEV uint32_t attn_chunk_cap(const MegaArgs &a) {
 
 // Once per step: the window's slot ids of this CTA's work item for the full and the
 // sliding lists (the lists do not change within a step).
+// The CTA's two work items (full, sliding list) of the step, computed once per launch
+// (attn_lists_init) and read by every attention phase.
+__shared__ AttnItem s_attn_items[2];
+CH_DEV const AttnItem &attn_item_of(uint32_t is_sliding) { return s_attn_items[is_sliding ? 1 : 0]; }
+
 CH_DEV void attn_lists_init(const MegaArgs &a, const StepParams &sp, uint32_t *wphys) {
+  if (threadIdx.x < 2) s_attn_items[threadIdx.x] = attn_item(a, sp, threadIdx.x);
   for (uint32_t v = 0; v < 2; v++) {
     const AttnItem it = attn_item(a, sp, v);
     for (uint32_t i = threadIdx.x; i < kWinSlots; i += MK_THREADS)
@@ -868,7 +874,7 @@ CH_DEV void attn_lists_init(const MegaArgs &a, const StepParams &sp, uint32_t *w
 template <int R>
 CH_DEV void attn_pre(const Phase &p, const MegaArgs &a, const StepParams &sp, const SmemLayout &L) {
   constexpr int D = kHeadDim;
-  const AttnItem it = attn_item(a, sp, p.is_sliding);
+  const AttnItem &it = attn_item_of(p.is_sliding);
   if (!it.active) return;
   AttnSmem<R> sm(L.u, attn_chunk_cap(a), a.attn_max_splits);
   const size_t kv_dim = (size_t)a.nkv * D;
@@ -904,7 +910,7 @@ CH_DEV void attn_pre(const Phase &p, const MegaArgs &a, const StepParams &sp, co
 template <int R>
 CH_DEV void attn_post_copies(const Phase &p, const MegaArgs &a, const StepParams &sp, const SmemLayout &L) {
   constexpr int D = kHeadDim;
-  const AttnItem it = attn_item(a, sp, p.is_sliding);
+  const AttnItem &it = attn_item_of(p.is_sliding);
   if (!it.active) return;
   AttnSmem<R> sm(L.u, attn_chunk_cap(a), a.attn_max_splits);
   const uint32_t kvh = it.kvh, kv_dim = a.nkv * D;
@@ -918,7 +924,7 @@ template <int R>
 CH_DEV void attn_phase(const Phase &p, const MegaArgs &a, const StepParams &sp, const SmemLayout &L, uint32_t pi) {
   constexpr int D = kHeadDim, EPL = 8;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const AttnItem it = attn_item(a, sp, p.is_sliding);
+  const AttnItem &it = attn_item_of(p.is_sliding);
   if (!it.active) return;
   const uint32_t max_splits = a.attn_max_splits, n = it.n, kvh = it.kvh;
   const size_t kv_dim = (size_t)a.nkv * D;
