@@ -445,6 +445,7 @@ struct SmemLayout {
   uint32_t g4;      // entries per list: the grid rounded up to a multiple of 4
   uint2 *comb;      // [kKinds][kMaxComb] this CTA's combine items of every GEMV kind
   uint32_t *ncomb;  // [kKinds] their counts
+  uint4 *wtab;      // [kKinds][MK_NW] each warp's tile range of every GEMV kind: {first, end, row tile, k tile}
   uint32_t *wphys;  // [2][kWinSlots] attention window slot ids (full, sliding lists)
   uint8_t *u;       // union region (GEMV staging / attention / top-k)
 };
@@ -475,6 +476,12 @@ CH_DEV void launch_tables(const MegaArgs &a, const SmemLayout &L) {
       else
         atomicOr(a.err, DEV_ERR_BAD_LIST);  // cannot happen: at most 17 cut row tiles per CTA
     }
+  }
+  if (threadIdx.x < kKinds * MK_NW) {  // every warp's tile range and its first (row tile, k tile)
+    const uint32_t k = threadIdx.x / MK_NW, w = threadIdx.x % MK_NW;
+    const Partition &pt = a.kpart[k];
+    const uint32_t tb = warp_begin(pt, c, w), te = warp_begin(pt, c, w + 1), rt = tb / pt.KT;
+    L.wtab[threadIdx.x] = make_uint4(tb, te, rt, tb - rt * pt.KT);
   }
   __syncthreads();
   if (threadIdx.x < kKinds) L.ncomb[threadIdx.x] = min(L.ncomb[threadIdx.x], kMaxComb);
@@ -680,13 +687,14 @@ CH_DEV void gemv_tiles(const Phase &p, const MegaArgs &a, uint32_t gw, const Sme
   uint8_t *my_stages = L.stages + (size_t)warp * MK_SPW * MK_STAGE;
   uint64_t *my_bars = L.bars + warp * MK_SPW;
   const uint32_t KT = p.k_tiles;
-  const uint32_t tb = warp_begin(p.out.pt, blockIdx.x, warp), te = warp_begin(p.out.pt, blockIdx.x, warp + 1);
+  const uint4 wt = L.wtab[p.out.kind * MK_NW + warp];  // {first tile, end, its row tile, its k tile}
+  const uint32_t tb = wt.x, te = wt.y;
   const uint32_t nchunks = (te - tb + MK_CT - 1) / MK_CT;
   const uint2 *xql = xq + t * 4 + (g & 3);
   // f16 path: lanes g < 2 read the hi / lo column, the others a zero page
   const uint4 *xb = (g < 2) ? reinterpret_cast<const uint4 *>(xq) + t * 2 + g : L.xzero;
   const uint32_t xs = (g < 2) ? 8u : 0u;
-  uint32_t rt = tb / KT, kt = tb - (tb / KT) * KT, cur_rt = 0xFFFFFFFFu, kt_begin = 0;
+  uint32_t rt = wt.z, kt = wt.w, cur_rt = 0xFFFFFFFFu, kt_begin = 0;
   float acc[4] = {0.f, 0.f, 0.f, 0.f}, accb[4] = {0.f, 0.f, 0.f, 0.f};  // two chains (even / odd tiles)
   bool first_seg = true;
   auto tile = [&](const uint8_t *tp, uint32_t k, float(&ac)[4]) {
@@ -1405,7 +1413,8 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(const MegaAr
   L.g4 = (gridDim.x + 3u) & ~3u;
   L.comb = reinterpret_cast<uint2 *>(L.sl + kKinds * 2 * L.g4);
   L.ncomb = reinterpret_cast<uint32_t *>(L.comb + kKinds * kMaxComb);
-  L.wphys = L.ncomb + 8;
+  L.wtab = reinterpret_cast<uint4 *>(L.ncomb + 8);
+  L.wphys = reinterpret_cast<uint32_t *>(L.wtab + kKinds * MK_NW);
   L.u = reinterpret_cast<uint8_t *>(L.wphys + 2 * kWinSlots);
   __shared__ __align__(16) float red[32];
   __shared__ Phase ph_s[3];  // phases pi, pi+1 and pi+2 (copied ahead with cp.async)
@@ -1512,7 +1521,7 @@ size_t mk_smem_bytes(uint32_t max_k, uint32_t hidden, uint32_t ratio, uint32_t m
                      uint32_t grid) {
   const size_t g4 = (grid + 3u) & ~3u;
   const size_t fixed = (size_t)MK_NW * MK_SPW * MK_STAGE + (MK_NW * MK_SPW + 2) * 8 + 16 + MK_NW * 2 * 16 * 4 +
-                      kKinds * 2 * g4 * 4 + kKinds * kMaxComb * 8 + 8 * 4 + 2 * kWinSlots * 4;
+                      kKinds * 2 * g4 * 4 + kKinds * kMaxComb * 8 + 8 * 4 + kKinds * MK_NW * 16 + 2 * kWinSlots * 4;
   const size_t part = (size_t)grid * 32 * 4;  // straddle partials of the previous GEMV
   // GEMV staging: 4 vectors of `hidden` for the norm prologues, one of max_k otherwise
   const size_t gemv = std::max((size_t)4 * hidden * 4, (size_t)max_k * 4) + part;
