@@ -51,7 +51,10 @@ constexpr int MK_CT = CH_MK_CT;    // tiles per stage
 constexpr int MK_STAGE = MK_CT * kTileBytes;
 static_assert(MK_CT % 2 == 0, "the unrolled chunk loop consumes tiles in pairs");
 constexpr int MK_THREADS = MK_NW * 32;
-constexpr uint32_t kMinChunk = 32;  // slots per attention work item before splitting further stops paying
+#ifndef CH_MK_MINCHUNK
+#define CH_MK_MINCHUNK 32
+#endif
+constexpr uint32_t kMinChunk = CH_MK_MINCHUNK;  // slots per attention work item before splitting further stops paying
 constexpr uint32_t kWinSlots = 64;  // attention slots per work item staged in shared memory before the barrier
 constexpr uint32_t kNoStraddle = 0xFFFFFFFFu;
 constexpr int kHeadDim = 256;
