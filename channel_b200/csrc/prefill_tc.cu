@@ -63,6 +63,7 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <atomic>
 
 #include "common.cuh"
 #include "kernels.cuh"
@@ -471,6 +472,366 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
 }
 
 // ---------------------------------------------------------------------------
+// Persistent stream-K form of the same GEMM: one cluster per SM pair for the whole
+// launch.  The k-tile iterations of all T tiles (tile t = row pair t / nt_tiles, token
+// tile t % nt_tiles; KT k tiles each) are split evenly over the C clusters, and a
+// cluster walks its range as segments -- the part of one tile's k range it owns --
+// with its copy rings, dequant and MMA pipeline running on across segments (no
+// per-tile launch, TMEM allocation or pipeline fill).  TMEM holds one tile's
+// accumulators, so a segment's first MMA waits until both CTAs' epilogue warps have
+// read the previous segment's (tmem_empty).  A segment that covers its whole tile
+// stores Y; a tile cut between clusters is written as one partial per contributing
+// cluster (part = its index among them, in k order) and the last contributor (counter
+// per tile and CTA) adds the parts in k order -- the same order on every run -- and
+// applies the epilogue.
+struct SkLaunch {
+  uint32_t C;          // clusters
+  uint32_t T;          // tiles
+  uint32_t nt_tiles;   // 256-token tiles
+  uint32_t max_parts;  // workspace parts per tile
+  uint32_t *counters;  // [T][2], zero between launches
+  float *ws;           // [max_parts][nt_tiles * 256][M] partials of cut tiles
+};
+constexpr uint32_t kNumBarsSk = kNumBars + 1;  // + tmem_empty
+constexpr uint32_t kOffMiscSk = kOffBars + kNumBarsSk * 8;
+constexpr size_t kTcSmemBytesSk = kOffMiscSk + 16 + 1024;
+static_assert(kTcSmemBytesSk <= 232448, "shared memory per CTA");
+
+CH_DEV uint64_t sk_begin(uint64_t W, uint32_t c, uint32_t C) { return W * c / C; }
+// the cluster whose range holds iteration it
+CH_DEV uint32_t sk_owner(uint64_t W, uint64_t it, uint32_t C) {
+  uint32_t c = (uint32_t)((it * C) / W);
+  while (c + 1 < C && sk_begin(W, c + 1, C) <= it) c++;
+  while (c > 0 && sk_begin(W, c, C) > it) c--;
+  return c;
+}
+
+template <int EPI>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
+    batch_gemm_tc_sk_kernel(const TcGemmArgs a, const SkLaunch L, const __grid_constant__ CUtensorMap wmap) {
+  extern __shared__ uint8_t smem_dyn[];
+  const uint32_t dyn = smem_u32(smem_dyn);
+  uint8_t *sm = smem_dyn + (((dyn + 1023u) & ~1023u) - dyn);
+  const uint32_t sbase = smem_u32(sm);
+  uint64_t *bars = reinterpret_cast<uint64_t *>(sm + kOffBars);
+  uint64_t *xfull = bars, *aready = bars + kTcStages, *empty = bars + 2 * kTcStages, *dfull = bars + 3 * kTcStages;
+  uint64_t *rfull = dfull + 1, *rempty = rfull + kTcRaw, *tmem_empty = rempty + kTcRaw;
+  uint32_t *misc = reinterpret_cast<uint32_t *>(sm + kOffMiscSk);
+  uint32_t *tmem_slot = misc;
+  volatile uint32_t *abort = misc + 1;
+  volatile uint32_t *is_last = misc + 2;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_rank();
+  const bool leader = rank == 0;
+  const uint32_t cid = blockIdx.y;
+  const uint32_t KT = a.K / kTcBK, row_tiles = a.M / 16;
+  const uint64_t W = (uint64_t)L.T * KT;
+  const uint64_t it0 = sk_begin(W, cid, L.C), it1 = sk_begin(W, cid + 1, L.C);
+  const uint32_t ready_l = map_shared(smem_u32(aready), 0);  // the leader's aready, as a cluster address
+  const uint32_t empty_l = map_shared(smem_u32(tmem_empty), 0);
+  // segment at iteration it: tile t, k tiles [k0, k1)
+  auto segment = [&](uint64_t it, uint32_t &t, uint32_t &k0, uint32_t &k1) {
+    t = (uint32_t)(it / KT);
+    k0 = (uint32_t)(it - (uint64_t)t * KT);
+    const uint64_t tend = (uint64_t)(t + 1) * KT;
+    k1 = (uint32_t)((it1 < tend ? it1 : tend) - (uint64_t)t * KT);
+  };
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kTcStages; s++) {
+      mbar_init(&xfull[s], 1);
+      mbar_init(&aready[s], 2 * kDqPerTile);
+      mbar_init(&empty[s], 1);
+    }
+    for (int r = 0; r < kTcRaw; r++) {
+      mbar_init(&rfull[r], 1);
+      mbar_init(&rempty[r], kDqPerTile);
+    }
+    mbar_init(dfull, 1);
+    mbar_init(tmem_empty, 2 * kEpiWarps);
+    *abort = 0u;
+    fence_mbar_init();
+  }
+  if (warp == kProdWarp) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  cluster_sync_all();  // barriers initialised and TMEM allocated in both CTAs
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == kProdWarp) {
+    if (lane == 0) {  // this CTA's activation share of every k tile, in the cluster's order
+      uint32_t g = 0;
+      bool live = true;
+      for (uint64_t it = it0; it < it1 && live;) {
+        uint32_t t, k0, k1;
+        segment(it, t, k0, k1);
+        const uint8_t *xs = a.xs + ((size_t)(t % L.nt_tiles) * KT * 2 + rank) * kTcXBytes;
+        for (uint32_t kt = k0; kt < k1; kt++) {
+          const int s = g % kTcStages;
+          if (g >= (uint32_t)kTcStages && !tc_wait(&empty[s], ((g / kTcStages) - 1) & 1, abort, a.err)) {
+            live = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&xfull[s], kTcXBytes);
+          bulk_g2s(sm + s * kTcStageBytes + 2 * kTcABytes, xs + (size_t)kt * 2 * kTcXBytes, kTcXBytes, &xfull[s]);
+          g++;
+        }
+        it = (uint64_t)t * KT + k1;
+      }
+      for (uint32_t j = g > (uint32_t)kTcStages ? g - kTcStages : 0; j < g; j++)
+        tc_wait(&xfull[j % kTcStages], (j / kTcStages) & 1, nullptr, a.err);
+    }
+  } else if (warp == kRawWarp) {
+    if (lane == 0) {  // this CTA's 8 Q4 tiles of every k tile
+      uint32_t g = 0;
+      bool live = true;
+      for (uint64_t it = it0; it < it1 && live;) {
+        uint32_t t, k0, k1;
+        segment(it, t, k0, k1);
+        const uint32_t rt0 = ((t / L.nt_tiles) * 2 + rank) * 8;
+        for (uint32_t kt = k0; kt < k1; kt++) {
+          const int r = g % kTcRaw;
+          if (g >= (uint32_t)kTcRaw && !tc_wait(&rempty[r], ((g / kTcRaw) - 1) & 1, abort, a.err)) {
+            live = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&rfull[r], kTcRawBytes);  // the box always lands whole (rows past M read as zeros)
+          tma_load_3d(sm + kOffRaw + r * kTcRawBytes, &wmap, 0, (int)kt, (int)rt0, &rfull[r]);
+          g++;
+        }
+        it = (uint64_t)t * KT + k1;
+      }
+      for (uint32_t j = g > (uint32_t)kTcRaw ? g - kTcRaw : 0; j < g; j++)
+        tc_wait(&rfull[j % kTcRaw], (j / kTcRaw) & 1, nullptr, a.err);
+    }
+  } else if (warp == kMmaWarp) {
+    if (leader && lane == 0) {
+      uint32_t g = 0, sidx = 0;
+      bool live = true;
+      for (uint64_t it = it0; it < it1 && live; sidx++) {
+        uint32_t t, k0, k1;
+        segment(it, t, k0, k1);
+        // the previous segment's accumulators read out by both CTAs' epilogue warps
+        if (sidx > 0 && !tc_wait(tmem_empty, (sidx - 1) & 1, abort, a.err, true)) break;
+        tc_fence_after();
+        bool issued = false;
+        for (uint32_t kt = k0; kt < k1; kt++) {
+          const int s = g % kTcStages;
+          if (!tc_wait(&aready[s], (g / kTcStages) & 1, abort, a.err, true)) {
+            live = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t st = sbase + s * kTcStageBytes;
+          const uint64_t ah = umma_desc_sw128(st), al = umma_desc_sw128(st + kTcABytes);
+          const uint64_t xh = umma_desc_sw128(st + 2 * kTcABytes), xl = umma_desc_sw128(st + 2 * kTcABytes + kTcPlane);
+#pragma unroll
+          for (int ks = 0; ks < 4; ks++) {
+            const uint64_t ko = (uint64_t)(ks * 2);  // 32 B per 16-wide k step, in 16-byte units
+            const uint32_t acc = (kt != k0 || ks != 0) ? 1u : 0u;
+            tc_mma(tmem, ah + ko, xh + ko, acc);          // D1 += A_hi X_hi
+            tc_mma(tmem + kTcBN, ah + ko, xl + ko, acc);  // D2 += A_hi (X_lo 2^8)
+            tc_mma(tmem + kTcBN, al + ko, xh + ko, 1u);   // D2 += A_lo X_hi
+          }
+          issued = true;
+          tc_commit_pair(&empty[s]);
+          g++;
+        }
+        if (issued) tc_commit_pair(dfull);  // this segment's accumulators (or, after an abort, every MMA issued)
+        it = (uint64_t)t * KT + k1;
+      }
+    }
+  } else if (warp < kEpiWarps) {
+    const uint32_t j = warp % kDqPerTile, par = warp / kDqPerTile;
+    const uint32_t g4 = lane >> 2, mi = lane >> 3, rr = lane & 7;
+    const uint32_t quad = warp & 3, cg = warp >> 2;
+    const uint32_t m = quad * 32 + lane;  // row within the CTA's tile = TMEM lane
+    const uint32_t jt = m >> 4, i16 = m & 15;
+    const size_t Mr = a.M, ntok = (size_t)L.nt_tiles * kTcBN;
+    uint32_t g = 0, sidx = 0;
+    bool ok = true;
+    // every epilogue warp walks every segment and reaches every named barrier, whatever
+    // its own waits returned: `ok` only gates the work
+    for (uint64_t it = it0; it < it1; sidx++) {
+      uint32_t t, k0, k1;
+      segment(it, t, k0, k1);
+      const uint32_t rt0 = ((t / L.nt_tiles) * 2 + rank) * 8;
+      const uint32_t ntiles = rt0 < row_tiles ? min(8u, row_tiles - rt0) : 0u;
+      // dequant of this segment's k tiles of this warp's parity (see batch_gemm_tc_kernel)
+      for (uint32_t kt = k0; kt < k1; kt++, g++) {
+        if ((g & 1u) != par || !ok) continue;
+        const int s = g % kTcStages, r = g % kTcRaw;
+        if (!__all_sync(0xFFFFFFFFu, tc_wait(&rfull[r], (g / kTcRaw) & 1, abort, a.err))) {
+          ok = false;
+          continue;
+        }
+        if (g >= (uint32_t)kTcStages &&
+            !__all_sync(0xFFFFFFFFu, tc_wait(&empty[s], ((g / kTcStages) - 1) & 1, abort, a.err))) {
+          ok = false;
+          continue;
+        }
+        const uint32_t Ah = sbase + s * kTcStageBytes, Al = Ah + kTcABytes;
+        if (j < ntiles) {
+          const uint8_t *raw = sm + kOffRaw + r * kTcRawBytes + j * kTileBytes;
+          const uint4 w = *reinterpret_cast<const uint4 *>(raw + lane * 16);
+          const uint2 sc = *reinterpret_cast<const uint2 *>(raw + 512 + g4 * 8);
+          uint32_t hs[2][2], ls[2][2];
+          bool sok = split_scale(sc.x & 0xFFFFu, hs[0][0], ls[0][0]);
+          sok &= split_scale(sc.x >> 16, hs[0][1], ls[0][1]);
+          sok &= split_scale(sc.y & 0xFFFFu, hs[1][0], ls[1][0]);
+          sok &= split_scale(sc.y >> 16, hs[1][1], ls[1][1]);
+          if (!sok) atomicOr(a.err, DEV_ERR_SCALE_RANGE);
+          const uint32_t rbase = (2 * j + (mi & 1)) * 1024 + rr * 128;
+          const uint32_t ws4[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+          for (int wi = 0; wi < 4; wi++) {
+            const int blk = wi >> 1;
+            uint32_t f[4];
+            dequant_q4_word(ws4[wi], f);
+            const uint32_t chunk = blk * 4 + (wi & 1) * 2 + (mi >> 1);
+            const uint32_t off = rbase + ((chunk ^ rr) << 4);
+            stmatrix_x4(Ah + off, hmul2_u32(f[0], hs[0][blk]), hmul2_u32(f[1], hs[1][blk]), hmul2_u32(f[2], hs[0][blk]),
+                        hmul2_u32(f[3], hs[1][blk]));
+            stmatrix_x4(Al + off, hmul2_u32(f[0], ls[0][blk]), hmul2_u32(f[1], ls[1][blk]), hmul2_u32(f[2], ls[0][blk]),
+                        hmul2_u32(f[3], ls[1][blk]));
+          }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&rempty[r]);
+        fence_proxy_async();
+        if (!__all_sync(0xFFFFFFFFu, tc_wait(&xfull[s], (g / kTcStages) & 1, abort, a.err))) {
+          ok = false;
+          continue;
+        }
+        if (lane == 0) mbar_arrive_cluster(ready_l + s * 8);
+      }
+
+      // epilogue of the segment
+      const uint32_t nt = t % L.nt_tiles;
+      const bool whole = k0 == 0 && k1 == KT;
+      const uint32_t row = rt0 * 16 + m;
+      const bool row_ok = jt < ntiles;
+      const uint32_t tok0 = nt * kTcBN + cg * 64;
+      const bool got = __all_sync(0xFFFFFFFFu, ok && tc_wait(dfull, sidx & 1, abort, a.err));
+      tc_fence_after();
+      const bool live = __all_sync(0xFFFFFFFFu, got && !*abort);
+      // contributors of a cut tile (clusters in k order) and this cluster's part
+      const uint32_t c_first = sk_owner(W, (uint64_t)t * KT, L.C), c_last = sk_owner(W, (uint64_t)(t + 1) * KT - 1, L.C);
+      const uint32_t part = cid - c_first, nparts = c_last - c_first + 1;
+      if (!whole && nparts > L.max_parts && threadIdx.x == 0) atomicOr(a.err, DEV_ERR_BAD_LIST);
+      const bool part_ok = whole || nparts <= L.max_parts;
+      auto store_out = [&](const float (&y)[32], uint32_t tok) {
+        if (EPI == EPI_STORE) {
+          if (row_ok) {
+#pragma unroll
+            for (int i = 0; i < 32; i++)
+              if (tok + i < a.N) a.Y[(size_t)(tok + i) * Mr + row] = y[i];
+          }
+        } else {  // gate|up pairs: as batch_gemm_tc_kernel's epilogue
+          const bool is_gate = i16 < 8;
+          const uint32_t Mo = a.M / 2, r = (rt0 + jt) * 8 + (i16 & 7);
+          float gv[16] = {}, uv[16] = {};
+#pragma unroll
+          for (int i = 0; i < 32; i++) {
+            const float other = __shfl_xor_sync(0xFFFFFFFFu, y[i], 8);
+            if (i < 16) {
+              gv[i] = is_gate ? y[i] : gv[i];
+              uv[i] = is_gate ? other : uv[i];
+            } else {
+              gv[i - 16] = is_gate ? gv[i - 16] : other;
+              uv[i - 16] = is_gate ? uv[i - 16] : y[i];
+            }
+          }
+          const uint32_t t1 = tok + (is_gate ? 0u : 16u);
+          if (row_ok) {
+#pragma unroll
+            for (int i = 0; i < 16; i++)
+              if (t1 + i < a.N) a.Y[(size_t)(t1 + i) * Mo + r] = gelu_mul(gv[i], uv[i]);
+          }
+        }
+      };
+      if (live) {
+#pragma unroll 1
+        for (int ch = 0; ch < 2; ch++) {
+          const uint32_t taddr = tmem + ((quad * 32u) << 16) + cg * 64 + ch * 32;
+          uint32_t v1[32], v2[32];
+          tc_ld32(taddr, v1);
+          tc_ld32(taddr + kTcBN, v2);
+          tc_wait_ld();
+          float y[32];
+#pragma unroll
+          for (int i = 0; i < 32; i++)
+            y[i] = __fmaf_rn(__uint_as_float(v2[i]), 1.0f / 65536.f, __fmul_rn(__uint_as_float(v1[i]), 1.0f / 256.f));
+          if (whole) {
+            store_out(y, tok0 + ch * 32);
+          } else if (row_ok && part_ok) {  // partial -> workspace [part][token][row]
+            float *wsp = L.ws + (size_t)part * ntok * Mr;
+#pragma unroll
+            for (int i = 0; i < 32; i++) wsp[(size_t)(tok0 + ch * 32 + i) * Mr + row] = y[i];
+          }
+        }
+      }
+      // the accumulators are read: the next segment's MMAs may start
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(empty_l);
+      if (!whole) {  // cut tile: the last contributor adds the parts in k order
+        __threadfence();
+        epi_sync();
+        if (threadIdx.x == 0) {
+          const uint32_t slot = t * 2 + rank;
+          const uint32_t prev = atomicAdd(&L.counters[slot], 1u);
+          *is_last = prev == nparts - 1;
+          if (prev == nparts - 1) L.counters[slot] = 0u;  // ready for the next launch
+        }
+        epi_sync();
+        if (live && part_ok && *is_last) {
+          __threadfence();
+#pragma unroll 1
+          for (int ch = 0; ch < 2; ch++) {
+            float y[32];
+#pragma unroll
+            for (int i = 0; i < 32; i++) y[i] = 0.f;
+            if (row_ok) {
+              const float *w0 = L.ws + (size_t)(tok0 + ch * 32) * Mr + row;
+#pragma unroll
+              for (int i = 0; i < 32; i++) y[i] = __ldcg(w0 + (size_t)i * Mr);
+#pragma unroll 1
+              for (uint32_t p2 = 1; p2 < nparts; p2++) {
+                const float *wsp = w0 + (size_t)p2 * ntok * Mr;
+                float tt[32];
+#pragma unroll
+                for (int i = 0; i < 32; i++) tt[i] = __ldcg(wsp + (size_t)i * Mr);
+#pragma unroll
+                for (int i = 0; i < 32; i++) y[i] = __fadd_rn(y[i], tt[i]);
+              }
+            }
+            store_out(y, tok0 + ch * 32);
+          }
+        }
+        epi_sync();  // every warp has read is_last before the next cut tile rewrites it
+      }
+      ok = ok && live;
+      it = (uint64_t)t * KT + k1;
+    }
+  }
+
+  __syncwarp();
+  tc_fence_before();
+  cluster_sync_all();  // both CTAs done with TMEM and with each other's shared memory
+  if (warp == kProdWarp) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
+  }
+}
+
+// ---------------------------------------------------------------------------
 // The Q4 tile array [M/16][K/64][576 B] as a 3-D tensor of u64: x = 72 words of a
 // tile, y = k tile (stride 576 B), z = row tile (stride K/64 * 576 B); box 72 x 1 x box_rows.
 cudaError_t encode_tile_map(CUtensorMap *map, const uint8_t *tiles, uint32_t M, uint32_t K, uint32_t box_rows) {
@@ -515,12 +876,64 @@ static size_t xs_region(uint32_t N, uint32_t K) { return (tc_split_x_bytes(N, K)
 size_t tc_split_x_bytes(uint32_t N, uint32_t K) {
   return (size_t)((N + kTcBN - 1) / kTcBN) * (K / kTcBK) * 2 * kTcXBytes;
 }
+// Clusters of the persistent stream-K kernel that are resident at once on this device
+// (0: the occupancy query failed -- use the per-tile kernel)
+static uint32_t sk_max_clusters() {
+  constexpr int kMaxDev = 64;
+  static std::atomic<int> cache[kMaxDev];  // 0: not asked yet, -1: unavailable
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDev) return 0;
+  int c = cache[dev].load(std::memory_order_relaxed);
+  if (c == 0) {
+    c = -1;
+    if (ensure_smem_attr((const void *)batch_gemm_tc_sk_kernel<EPI_STORE>, kTcSmemBytesSk) == cudaSuccess &&
+        ensure_smem_attr((const void *)batch_gemm_tc_sk_kernel<EPI_GELU_MUL>, kTcSmemBytesSk) == cudaSuccess) {
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(2, (unsigned)(num_sms() / 2));
+      cfg.blockDim = dim3(kTcThreads);
+      cfg.dynamicSmemBytes = kTcSmemBytesSk;
+      int n = 0;
+      if (cudaOccupancyMaxActiveClusters(&n, (const void *)batch_gemm_tc_sk_kernel<EPI_STORE>, &cfg) == cudaSuccess &&
+          n > 0)
+        c = n;
+      else
+        (void)cudaGetLastError();
+    }
+    cache[dev].store(c, std::memory_order_relaxed);
+  }
+  return c > 0 ? (uint32_t)c : 0u;
+}
+struct SkShape {
+  uint32_t C, T, nt, max_parts;
+};
+// the stream-K split of an N x M x K GEMM; C == 0: the per-tile kernel runs instead
+static SkShape sk_shape(uint32_t N, uint32_t M, uint32_t K) {
+  SkShape sh{};
+  const uint32_t cmax = sk_max_clusters();
+  sh.nt = (N + kTcBN - 1) / kTcBN;
+  sh.T = sh.nt * ((M / 16 + 15) / 16);
+  const uint64_t KT = K / kTcBK, W = (uint64_t)sh.T * KT;
+  // TMEM holds one tile's accumulators, so a segment boundary drains the pipeline
+  // (epilogue, then dequant restart): the persistent form pays only where it replaces
+  // more than two waves of per-tile launches (each wave's CTA start-up and fill)
+  if (cmax == 0 || W == 0 || sh.T <= 2 * cmax || (uint64_t)sh.T * 2 > kMaxCounters) return sh;
+  sh.C = (uint32_t)std::min<uint64_t>(cmax, std::max<uint64_t>(1, W / 8));  // >= 8 k tiles per cluster
+  const uint64_t span = W / sh.C;                                           // every range holds >= span
+  sh.max_parts = (uint32_t)((KT + span - 1) / span + 1);
+  return sh;
+}
+static size_t sk_ws_bytes(uint32_t N, uint32_t M, uint32_t K) {
+  const SkShape sh = sk_shape(N, M, K);
+  return sh.C ? (size_t)sh.max_parts * sh.nt * kTcBN * M * sizeof(float) : 0;
+}
+
 // enough for any token count up to N (fewer tokens can choose a larger split)
 size_t tc_gemm_scratch_bytes(uint32_t N, uint32_t M, uint32_t K) {
   size_t ws = 0;
   for (uint32_t nt = 1; nt <= (N + kTcBN - 1) / kTcBN; nt++) {
     const uint32_t sk = gemm_split(nt * kTcBN, M, K);
     if (sk > 1) ws = std::max(ws, (size_t)sk * nt * kTcBN * M * sizeof(float));
+    ws = std::max(ws, sk_ws_bytes(nt * kTcBN, M, K));
   }
   return kCounterBytes + xs_region(N, K) + ws;
 }
@@ -538,6 +951,7 @@ cudaError_t launch_tc_split_x(const float *X, uint32_t N, uint32_t K, uint8_t *x
 // bytes of scratch one launch of this shape uses (tc_gemm_scratch_bytes covers every
 // token count up to N)
 static size_t tc_launch_scratch_bytes(uint32_t N, uint32_t M, uint32_t K) {
+  if (sk_shape(N, M, K).C) return kCounterBytes + xs_region(N, K) + sk_ws_bytes(N, M, K);
   const uint32_t sk = gemm_split(N, M, K);
   const size_t nt = (N + kTcBN - 1) / kTcBN;
   return kCounterBytes + xs_region(N, K) + (sk > 1 ? (size_t)sk * nt * kTcBN * M * sizeof(float) : 0);
@@ -551,6 +965,22 @@ cudaError_t launch_batch_gemm_tc(const TcGemmArgs &a, uint8_t *scratch, size_t s
   alignas(64) CUtensorMap wmap;
   cudaError_t me = encode_tile_map(&wmap, a.tiles, a.M, a.K, 8);
   if (me != cudaSuccess) return me;
+  const SkShape sh = sk_shape(a.N, a.M, a.K);
+  if (sh.C) {  // persistent stream-K: one cluster per SM pair (all resident)
+    SkLaunch S{};
+    S.C = sh.C;
+    S.T = sh.T;
+    S.nt_tiles = sh.nt;
+    S.max_parts = sh.max_parts;
+    S.counters = reinterpret_cast<uint32_t *>(scratch);
+    S.ws = reinterpret_cast<float *>(scratch + kCounterBytes + xs_region(a.N, a.K));
+    const dim3 grid(2, sh.C);
+    if (a.epi == EPI_STORE)
+      batch_gemm_tc_sk_kernel<EPI_STORE><<<grid, kTcThreads, kTcSmemBytesSk, s>>>(a, S, wmap);
+    else
+      batch_gemm_tc_sk_kernel<EPI_GELU_MUL><<<grid, kTcThreads, kTcSmemBytesSk, s>>>(a, S, wmap);
+    return cudaGetLastError();
+  }
   const uint32_t nt = (a.N + kTcBN - 1) / kTcBN, mp = (a.M / 16 + 15) / 16;
   TcLaunch L{};
   L.sk = gemm_split(a.N, a.M, a.K);
