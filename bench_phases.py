@@ -3,8 +3,9 @@
 Loads the instrumented library (``python -m channel_b200.build --trace`` builds
 libchannel_b200_trace.so with -DCH_PHASE_TRACE), decodes a few greedy tokens of
 the 12B-shape model on synthetic weights and prints, per phase kind, where the
-time of one token goes.  Each CTA's thread 0 records %globaltimer at seven
-points of every phase:
+time of one token goes.  Each CTA's thread 0 records %globaltimer at these
+points of every phase (marks 8-11, from warps 0 and 15 inside the tile loop, are
+saved by --dump):
 
   0 phase start (grid barrier passed)    1 staged inputs landed (bulk copies)
   2 GEMV: input limbs built / ATTN: heads normed and roped

@@ -65,7 +65,8 @@ constexpr uint32_t kMaxComb = 24;   // combine items of one CTA and GEMV kind (a
 int mk_warps() { return MK_NW; }
 
 // Optional per-phase timeline (build with -DCH_PHASE_TRACE, see bench_phases.py):
-// thread 0 of every CTA records %globaltimer at seven points of each phase.
+// thread 0 of every CTA records %globaltimer at eight points of each phase (marks 0-7),
+// lane 0 of warps 0 and 15 at the first chunk and the end of their tiles (marks 8-11).
 #ifdef CH_PHASE_TRACE
 constexpr int kTraceCtas = 256, kTracePhases = 512, kTraceMarks = 12;
 __device__ unsigned long long g_phase_trace[kTraceCtas * kTracePhases * kTraceMarks];
