@@ -39,7 +39,7 @@
 #define CH_MK_SPW 2
 #endif
 #ifndef CH_MK_CT
-#define CH_MK_CT 6
+#define CH_MK_CT 7
 #endif
 
 namespace ch {
@@ -47,15 +47,23 @@ namespace ch {
 namespace {
 constexpr int MK_NW = 16;          // warps per CTA (all stream + compute)
 constexpr int MK_SPW = CH_MK_SPW;  // bulk-copy stages per warp
-constexpr int MK_CT = CH_MK_CT;    // tiles per stage
+// tiles per stage.  The 12B GEMV partitions give each warp n or n + 1 tiles with
+// n = 6 (o), 12 (q|k|v), 24 (down), 48 (gate|up) on one GPU and their halves / quarters
+// under tensor parallelism; with 7-tile chunks both counts need the same number of
+// chunks, so no warp waits for one more bulk-copy round trip than the rest of its phase
+// (6-tile chunks: 2.86 ms per token, 7: 2.79 ms).
+constexpr int MK_CT = CH_MK_CT;
 constexpr int MK_STAGE = MK_CT * kTileBytes;
-static_assert(MK_CT % 2 == 0, "the unrolled chunk loop consumes tiles in pairs");
+static_assert(MK_CT >= 2, "a full chunk is consumed in pairs of tiles, plus one when MK_CT is odd");
 constexpr int MK_THREADS = MK_NW * 32;
 #ifndef CH_MK_MINCHUNK
 #define CH_MK_MINCHUNK 32
 #endif
 constexpr uint32_t kMinChunk = CH_MK_MINCHUNK;  // slots per attention work item before splitting further stops paying
-constexpr uint32_t kWinSlots = 64;  // attention slots per work item staged in shared memory before the barrier
+#ifndef CH_MK_WIN
+#define CH_MK_WIN 56
+#endif
+constexpr uint32_t kWinSlots = CH_MK_WIN;  // attention slots per work item staged in shared memory before the barrier
 constexpr uint32_t kNoStraddle = 0xFFFFFFFFu;
 constexpr int kHeadDim = 256;
 constexpr uint32_t kMaxGrid = 255;  // straddle-list entries hold CTA ids in 8 bits
@@ -758,10 +766,11 @@ CH_DEV void gemv_tiles(const Phase &p, const MegaArgs &a, uint32_t gw, const Sme
       uint32_t r = 0;
       if (run == MK_CT) {
 #pragma unroll
-        for (int q = 0; q < MK_CT; q += 2) {
+        for (int q = 0; q + 1 < MK_CT; q += 2) {
           tile(pp + q * kTileBytes, kt + q, acc);
           tile(pp + (q + 1) * kTileBytes, kt + q + 1, accb);
         }
+        if constexpr (MK_CT % 2) tile(pp + (MK_CT - 1) * kTileBytes, kt + MK_CT - 1, acc);
         r = MK_CT;
       } else {
         for (; r + 2 <= run; r += 2) {
