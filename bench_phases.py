@@ -5,7 +5,7 @@ libchannel_b200_trace.so with -DCH_PHASE_TRACE), decodes a few greedy tokens of
 the 12B-shape model on synthetic weights and prints, per phase kind, where the
 time of one token goes.  Each CTA's thread 0 records %globaltimer at these
 points of every phase (marks 8-11, from warps 0 and 15 inside the tile loop, are
-saved by --dump):
+saved by --dump, as is mark 12 of phase 0, the CTA's SM id):
 
   0 phase start (grid barrier passed)    1 staged inputs landed (bulk copies)
   2 GEMV: input limbs built / ATTN: heads normed and roped
@@ -31,7 +31,7 @@ from pathlib import Path
 
 import numpy as np
 
-TRACE_CTAS, TRACE_PHASES, TRACE_MARKS = 256, 512, 12
+TRACE_CTAS, TRACE_PHASES, TRACE_MARKS = 256, 512, 13
 COLS = ["staging", "prologue", "tiles/core", "combine", "arrive+pre", "barrier"]
 
 

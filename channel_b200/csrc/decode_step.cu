@@ -74,9 +74,10 @@ int mk_warps() { return MK_NW; }
 
 // Optional per-phase timeline (build with -DCH_PHASE_TRACE, see bench_phases.py):
 // thread 0 of every CTA records %globaltimer at eight points of each phase (marks 0-7),
-// lane 0 of warps 0 and 15 at the first chunk and the end of their tiles (marks 8-11).
+// lane 0 of warps 0 and 15 at the first chunk and the end of their tiles (marks 8-11),
+// and the CTA's SM id once (mark 12 of phase 0).
 #ifdef CH_PHASE_TRACE
-constexpr int kTraceCtas = 256, kTracePhases = 512, kTraceMarks = 12;
+constexpr int kTraceCtas = 256, kTracePhases = 512, kTraceMarks = 13;  // mark 12: the CTA's SM id
 __device__ unsigned long long g_phase_trace[kTraceCtas * kTracePhases * kTraceMarks];
 #define PHASE_MARK(pi, k)                                                                               \
   do {                                                                                                  \
@@ -89,7 +90,19 @@ __device__ unsigned long long g_phase_trace[kTraceCtas * kTracePhases * kTraceMa
     if (threadIdx.x == (w) * 32 && blockIdx.x < kTraceCtas && (pi) < kTracePhases)                      \
       g_phase_trace[((size_t)blockIdx.x * kTracePhases + (pi)) * kTraceMarks + (k)] = globaltimer_ns(); \
   } while (0)
+// mark 12 of phase 0: the SM the CTA runs on (%smid)
+#define TRACE_SMID()                                                            \
+  do {                                                                          \
+    if (threadIdx.x == 0 && blockIdx.x < kTraceCtas) {                          \
+      uint32_t sm;                                                              \
+      asm volatile("mov.u32 %0, %%smid;" : "=r"(sm));                           \
+      g_phase_trace[(size_t)blockIdx.x * kTracePhases * kTraceMarks + 12] = sm; \
+    }                                                                           \
+  } while (0)
 #else
+#define TRACE_SMID() \
+  do {               \
+  } while (0)
 #define PHASE_MARK(pi, k) \
   do {                    \
   } while (0)
@@ -1461,6 +1474,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(const MegaAr
   pre_phase<R>(ph_s[0], a, sp_s, L);
 
   const unsigned long long base = a.base[0], gbase = a.base[1];  // arrivals before this launch
+  TRACE_SMID();
   uint32_t cidx = 0, vpar = 0;
   bool ok = true;
   for (uint32_t pi = 0; pi < a.nphases; pi++) {
